@@ -1,0 +1,220 @@
+"""numpy restatement of the reference's eager (pure-PyTorch) SSSD and CHAM algorithms.
+
+TEST INFRASTRUCTURE ONLY -- the parity checker for the CUDA path and the timed CPU
+baseline.  The product package never imports it.
+
+Every function follows the reference's *eager* path (the path the reference trains
+with, and the one its tests treat as ground truth), not its Triton kernels:
+
+* SSSD  -- ``verace_v1/modules/sssd_attention.py``
+    projections / L2-normalise / delta gate      :116-126
+    Cayley factor R = solve(I + X, I - X), X=δA/2 :154-166  (``_solve_cayley`` :21-72)
+    prefix product P_t = R_t ... R_1 (newest left):169      (``parallel_prefix_scan`` :185-217)
+    Ψ_t = P_t Ψ_0,  o_t = Ψ_t q_t                  :173-175
+    head RMSNorm + w_out, state = Ψ_s              :177-181
+* CHAM  -- ``verace_v1/modules/cham_memory.py``
+    projections, v = normalize(silu(.)), γ gate    :129-153
+    U = solve(I - iG/2, I + iG/2), G=γ(kvᵀ+vkᵀ)   :211-218  (``_solve_cham_cayley`` :54-96)
+    prefix product P_t = U_t ... U_1               :222     (``parallel_complex_prefix_scan`` :246-293)
+    H_t = P_t H_0 (H_0 on the right)               :229-230
+    per-position Newton-Schulz x3                  :236     (``parallel_newton_schulz_retraction`` :296-315)
+    rec_t = Re(NS(H_t)) q_t, y = RMSNorm(w_out rec):239-241
+    exported state = raw H_s (never retracted)     :243
+* ``newton_schulz_unitary_retraction``             cham_memory.py:21-51
+
+The prefix products are formed sequentially (P_t = R_t P_{t-1}); the reference's
+Blelloch scan forms the same products in a different association order, which only
+changes fp rounding.  Non-finite Cayley factors are replaced by the identity, as the
+reference's ``_solve_cayley`` / ``_solve_cham_cayley`` do (sssd_attention.py:52-71,
+cham_memory.py:76-96).
+
+``dtype`` selects the arithmetic: ``np.float32`` mirrors the reference's fp32 eager
+path (complex64 for CHAM); ``np.float64`` is the fp64 gold in the style of
+``tests/test_triton_kernels.py:35-83`` (``_cham_fp64_reference``).
+"""
+
+from __future__ import annotations
+
+import numpy as np
+
+__all__ = [
+    "l2_normalize", "sigmoid", "silu", "rms_norm",
+    "sssd_cayley_factors", "sssd_scan", "sssd_forward",
+    "cham_cayley_factors", "cham_scan", "cham_forward",
+    "newton_schulz_unitary_retraction", "sssd_projections", "cham_projections",
+]
+
+
+# --------------------------------------------------------------------------------------
+# elementwise helpers (torch semantics)
+# --------------------------------------------------------------------------------------
+def l2_normalize(x, eps=1e-12):
+    """``F.normalize(x, p=2, dim=-1)``: x / max(||x||_2, eps)."""
+    n = np.sqrt(np.sum(x * x, axis=-1, keepdims=True))
+    return x / np.maximum(n, eps)
+
+
+def sigmoid(x):
+    return 1.0 / (1.0 + np.exp(-x))
+
+
+def silu(x):
+    return x * sigmoid(x)
+
+
+def rms_norm(x, weight, eps=None):
+    """``nn.RMSNorm``: eps=None means ``finfo(dtype).eps`` (torch's default)."""
+    if eps is None:
+        eps = np.finfo(x.dtype).eps
+    ms = np.mean(x * x, axis=-1, keepdims=True)
+    return (x / np.sqrt(ms + eps)) * weight
+
+
+def _linear(x, w):
+    return x @ w.T
+
+
+# --------------------------------------------------------------------------------------
+# SSSD
+# --------------------------------------------------------------------------------------
+def sssd_projections(p, x, num_heads, head_dim, active_mask=None):
+    """sssd_attention.py:116-126 -> q, k, v [b,s,h,d], delta [b,s,h]."""
+    b, s, _ = x.shape
+    q = l2_normalize(_linear(x, p["w_q.weight"]).reshape(b, s, num_heads, head_dim))
+    k = l2_normalize(_linear(x, p["w_k.weight"]).reshape(b, s, num_heads, head_dim))
+    v = l2_normalize(_linear(x, p["w_v.weight"]).reshape(b, s, num_heads, head_dim))
+    delta = 0.1 * sigmoid(_linear(x, p["w_delta.weight"]))  # [b,s,h]
+    if active_mask is not None:
+        delta = delta * active_mask[..., None].astype(delta.dtype)
+    return q, k, v, delta
+
+
+def sssd_cayley_factors(k, v, delta):
+    """R = solve(I + δA/2, I - δA/2), A = k vᵀ - v kᵀ  (sssd_attention.py:154-166).
+
+    k, v: [..., d]; delta: [...].  Returns R: [..., d, d]."""
+    d = k.shape[-1]
+    eye = np.eye(d, dtype=k.dtype)
+    A = k[..., :, None] * v[..., None, :] - v[..., :, None] * k[..., None, :]
+    X = 0.5 * delta[..., None, None] * A
+    R = np.linalg.solve(eye + X, eye - X)
+    bad = ~np.isfinite(R).all(axis=(-1, -2))
+    if bad.any():  # _solve_cayley's identity substitution (sssd_attention.py:52-71)
+        R[bad] = eye
+    return R
+
+
+def sssd_scan(q, k, v, delta, initial_state=None, dtype=np.float64):
+    """Launcher-level SSSD scan (the contract of ``launch_sssd_triton_scan``,
+    triton_kernels.py:603-636), computed by the eager algorithm.
+
+    q, k, v: [b,s,h,d]; delta: [b,s,h]; initial_state: [b,h,d,d] or None (identity).
+    Returns (o [b,s,h,d], psi [b,h,d,d])."""
+    q, k, v, delta = (np.asarray(a, dtype=dtype) for a in (q, k, v, delta))
+    b, s, h, d = q.shape
+    if initial_state is None:
+        psi0 = np.broadcast_to(np.eye(d, dtype=dtype), (b, h, d, d)).copy()
+    else:
+        psi0 = np.asarray(initial_state, dtype=dtype)
+    o = np.zeros((b, s, h, d), dtype=dtype)
+    P = np.broadcast_to(np.eye(d, dtype=dtype), (b, h, d, d)).copy()
+    psi = psi0.copy()
+    for t in range(s):
+        R = sssd_cayley_factors(k[:, t], v[:, t], delta[:, t])  # [b,h,d,d]
+        P = R @ P                                              # P_t = R_t P_{t-1}
+        psi = P @ psi0                                         # Ψ_t = P_t Ψ_0
+        o[:, t] = (psi @ q[:, t, :, :, None])[..., 0]
+    return o, psi
+
+
+def sssd_forward(p, x, num_heads, head_dim, initial_state=None, return_state=False,
+                 active_mask=None, dtype=np.float64):
+    """``SSSDAttention.forward`` (sssd_attention.py:103-182), eager path."""
+    x = np.asarray(x, dtype=dtype)
+    p = {n: np.asarray(w, dtype=dtype) for n, w in p.items()}
+    b, s, _ = x.shape
+    q, k, v, delta = sssd_projections(p, x, num_heads, head_dim, active_mask)
+    o, psi = sssd_scan(q, k, v, delta, initial_state, dtype=dtype)
+    o_norm = rms_norm(o, p["head_rmsnorm.weight"]).reshape(b, s, num_heads * head_dim)
+    out = _linear(o_norm, p["w_out.weight"])
+    return out, (psi if return_state else None)
+
+
+# --------------------------------------------------------------------------------------
+# CHAM
+# --------------------------------------------------------------------------------------
+def cham_projections(p, x, active_mask=None):
+    """cham_memory.py:129-153 -> q, k, v [b,s,D], gamma [b,s]."""
+    q = l2_normalize(_linear(x, p["w_q.weight"]))
+    k = l2_normalize(_linear(x, p["w_k.weight"]))
+    v = l2_normalize(silu(_linear(x, p["w_v.weight"])))
+    gamma = 0.1 * sigmoid(_linear(x, p["w_gamma.weight"]))[..., 0]
+    if active_mask is not None:
+        gamma = gamma * active_mask.astype(gamma.dtype)
+    return q, k, v, gamma
+
+
+def _cdtype(dtype):
+    return np.complex128 if np.dtype(dtype) == np.float64 else np.complex64
+
+
+def cham_cayley_factors(k, v, gamma):
+    """U = solve(I - iG/2, I + iG/2), G = γ(k vᵀ + v kᵀ)  (cham_memory.py:211-218)."""
+    D = k.shape[-1]
+    cd = _cdtype(k.dtype)
+    eye = np.eye(D, dtype=cd)
+    G = gamma[..., None, None] * (k[..., :, None] * v[..., None, :] + v[..., :, None] * k[..., None, :])
+    G = G.astype(cd)
+    U = np.linalg.solve(eye - 0.5j * G, eye + 0.5j * G)
+    bad = ~np.isfinite(U).all(axis=(-1, -2))
+    if bad.any():  # _solve_cham_cayley's identity substitution (cham_memory.py:76-96)
+        U[bad] = eye
+    return U
+
+
+def newton_schulz_unitary_retraction(H_real, H_imag, steps=3):
+    """cham_memory.py:21-51: H <- 0.5 H (3I - Hᴴ H), both parts from the same pre-update H."""
+    H = np.asarray(H_real) + 1j * np.asarray(H_imag)
+    D = H.shape[-1]
+    eye = np.eye(D, dtype=H.dtype)
+    for _ in range(steps):
+        HH = np.conj(np.swapaxes(H, -1, -2)) @ H
+        H = 0.5 * (H @ (3.0 * eye - HH))
+    return H.real.copy(), H.imag.copy()
+
+
+def cham_scan(q, k, v, gamma, initial_hologram=None, dtype=np.float64, ns_steps=3):
+    """Launcher-level CHAM scan (contract of ``launch_cham_triton_update``,
+    triton_kernels.py:639-685) computed by the eager algorithm, including the
+    per-position Newton-Schulz retraction of the readout.
+
+    q, k, v: [b,s,D]; gamma: [b,s]; initial_hologram: (Hr, Hi) [b,D,D] or None (I, 0).
+    Returns (rec [b,s,D], (Hr_raw, Hi_raw) [b,D,D])."""
+    q, k, v, gamma = (np.asarray(a, dtype=dtype) for a in (q, k, v, gamma))
+    b, s, D = q.shape
+    cd = _cdtype(dtype)
+    if initial_hologram is None:
+        H0 = np.broadcast_to(np.eye(D, dtype=cd), (b, D, D)).copy()
+    else:
+        H0 = (np.asarray(initial_hologram[0], dtype=dtype)
+              + 1j * np.asarray(initial_hologram[1], dtype=dtype)).astype(cd)
+    P = np.broadcast_to(np.eye(D, dtype=cd), (b, D, D)).copy()
+    Hraw = H0.copy()
+    rec = np.zeros((b, s, D), dtype=dtype)
+    for t in range(s):
+        U = cham_cayley_factors(k[:, t], v[:, t], gamma[:, t])  # [b,D,D]
+        P = U @ P                       # P_t = U_t P_{t-1}
+        Hraw = P @ H0                   # H_t = P_t H_0
+        Hr, _ = newton_schulz_unitary_retraction(Hraw.real, Hraw.imag, ns_steps)
+        rec[:, t] = (Hr @ q[:, t, :, None])[..., 0]
+    return rec, (Hraw.real.astype(dtype), Hraw.imag.astype(dtype))
+
+
+def cham_forward(p, x, initial_hologram=None, active_mask=None, dtype=np.float64):
+    """``ContinuousHolographicMemory.forward`` (cham_memory.py:117-243), eager path."""
+    x = np.asarray(x, dtype=dtype)
+    p = {n: np.asarray(w, dtype=dtype) for n, w in p.items()}
+    q, k, v, gamma = cham_projections(p, x, active_mask)
+    rec, H = cham_scan(q, k, v, gamma, initial_hologram, dtype=dtype)
+    y = rms_norm(_linear(rec, p["w_out.weight"]), p["norm.weight"])
+    return y, H
