@@ -1,0 +1,109 @@
+/*
+ * verace_b200.h -- C ABI of the B200-native (sm_100a) Verace V1 sequence-mixing path.
+ *
+ * Plain pointers and sizes only; no framework types.  All tensor arguments are
+ * DEVICE pointers to dense row-major (C-contiguous) arrays.  Every entry point
+ * enqueues its kernels on `stream` (a cudaStream_t passed as void*; NULL = the
+ * legacy default stream) and returns without synchronising.  Return value: 0 on
+ * success, otherwise one of VERACE_ERR_*, with a message from verace_last_error().
+ * Inputs are never modified; outputs are written, never read.
+ *
+ * Element types: `dtype` selects the type of q/k/v and of the sequence output
+ * (VERACE_F32, VERACE_BF16, VERACE_F16).  Gates (delta, gamma) are fp32, and every
+ * recurrent state (SSSD Psi, CHAM H = Hr + i Hi) is fp32, as in the reference.
+ *
+ * Scratch: the scan entry points take a caller-allocated device `workspace` of at
+ * least the size returned by the matching *_workspace() query (256-byte aligned).
+ *
+ * The reference these entry points replace is Python (Verace-Pvt-Ltd/Verace-V1,
+ * package verace_v1); each declaration cites the reference function it stands in for.
+ */
+#ifndef VERACE_B200_H_
+#define VERACE_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define VERACE_API __attribute__((visibility("default")))
+#else
+#define VERACE_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum {
+  VERACE_OK = 0,
+  VERACE_ERR_INVALID = 1,     /* bad argument (null pointer, negative size, ...) */
+  VERACE_ERR_UNSUPPORTED = 2, /* valid but unsupported shape (e.g. head_dim > 128) */
+  VERACE_ERR_CUDA = 3,        /* a CUDA runtime call or kernel launch failed */
+  VERACE_ERR_WORKSPACE = 4,   /* workspace missing or smaller than required */
+  VERACE_ERR_TIMEOUT = 5      /* a bounded device-side wait gave up */
+};
+
+enum { VERACE_F32 = 0, VERACE_BF16 = 1, VERACE_F16 = 2 };
+
+/* Version of this ABI (major*10000 + minor*100 + patch). */
+VERACE_API int verace_version(void);
+
+/* Message describing the last error returned on the calling host thread. */
+VERACE_API const char* verace_last_error(void);
+
+/* Number of kernels this library has launched in the process so far (all devices,
+ * all host threads).  Lets a caller count the library's own launches in a region. */
+VERACE_API unsigned long long verace_kernel_launches(void);
+
+/* ------------------------------------------------------------------------------
+ * SSSD Cayley-rotation scan.
+ * Replaces launch_sssd_triton_scan (verace_v1/serving/triton_kernels.py:603-636),
+ * the kernel behind SSSDAttention.forward (verace_v1/modules/sssd_attention.py:129-136),
+ * with the eager path's semantics (sssd_attention.py:144-181):
+ *   R_t = (I + d_t A_t / 2)^-1 (I - d_t A_t / 2),  A_t = k_t v_t^T - v_t k_t^T
+ *   Psi_t = R_t Psi_{t-1},  o_t = Psi_t q_t
+ * q, k, v, out : [b, s, h, d] (dtype)       delta : [b, s, h] fp32
+ * psi0         : [b, h, d, d] fp32, or NULL for the identity
+ * psi_out      : [b, h, d, d] fp32 (state after the last token; = psi0 when s == 0)
+ * Supports 1 <= d <= 128.
+ * ---------------------------------------------------------------------------- */
+VERACE_API size_t verace_sssd_scan_workspace(int b, int s, int h, int d);
+VERACE_API int verace_sssd_scan(const void* q, const void* k, const void* v, const float* delta,
+                     const float* psi0, void* out, float* psi_out,
+                     int b, int s, int h, int d, int dtype,
+                     void* workspace, size_t workspace_bytes, void* stream);
+
+/* ------------------------------------------------------------------------------
+ * CHAM holographic-memory scan with Newton-Schulz readout retraction.
+ * Replaces launch_cham_triton_update / launch_cham_triton_tiled
+ * (verace_v1/serving/triton_kernels.py:639-685, :552-597), the kernels behind
+ * ContinuousHolographicMemory.forward (verace_v1/modules/cham_memory.py:164-168),
+ * with the eager path's semantics (cham_memory.py:177-243):
+ *   U_t = (I - i G_t / 2)^-1 (I + i G_t / 2),  G_t = g_t (k_t v_t^T + v_t k_t^T)
+ *   H_t = U_t H_{t-1}  (raw, never retracted; exported)
+ *   rec_t = Re(NS3(H_t)) q_t          (3 Newton-Schulz steps, cham_memory.py:296-315)
+ * q, k, v, out : [b, s, D] (dtype)          gamma : [b, s] fp32
+ * h0_re, h0_im : [b, D, D] fp32, or both NULL for (I, 0)
+ * h_re, h_im   : [b, D, D] fp32 raw state after the last token
+ * ---------------------------------------------------------------------------- */
+VERACE_API size_t verace_cham_scan_workspace(int b, int s, int D, int has_h0);
+VERACE_API int verace_cham_scan(const void* q, const void* k, const void* v, const float* gamma,
+                     const float* h0_re, const float* h0_im, void* out,
+                     float* h_re, float* h_im, int b, int s, int D, int dtype,
+                     void* workspace, size_t workspace_bytes, void* stream);
+
+/* ------------------------------------------------------------------------------
+ * Dense Newton-Schulz unitary retraction, `steps` iterations of H <- H (3I - H^H H) / 2.
+ * Replaces newton_schulz_unitary_retraction (verace_v1/modules/cham_memory.py:21-51).
+ * h_re, h_im, out_re, out_im : [b, D, D] fp32 (out may not alias the input).
+ * ---------------------------------------------------------------------------- */
+VERACE_API size_t verace_cham_retract_workspace(int b, int D);
+VERACE_API int verace_cham_retract(const float* h_re, const float* h_im, float* out_re, float* out_im,
+                        int b, int D, int steps, void* workspace, size_t workspace_bytes,
+                        void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* VERACE_B200_H_ */

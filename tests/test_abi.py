@@ -1,0 +1,62 @@
+"""CPU checks of the C ABI: the library loads without a GPU, exports every function
+include/verace_b200.h declares, sizes its workspaces, and rejects bad arguments with
+a status code and message before touching the device."""
+import ctypes
+
+import pytest
+
+from verace_v1_b200 import _lib
+
+
+def test_library_loads_and_exports_every_header_symbol():
+    L = _lib.lib()
+    declared = _lib.header_symbols()
+    assert len(declared) >= 8
+    for name in declared:
+        assert hasattr(L, name), f"{name} declared in include/verace_b200.h but not exported"
+    assert set(declared) == set(_lib._SIGNATURES), "ctypes signatures out of sync with the header"
+    assert L.verace_version() >= 10000
+
+
+def test_workspace_queries_grow_with_problem_size():
+    L = _lib.lib()
+    a = L.verace_sssd_scan_workspace(2, 512, 8, 128)
+    b = L.verace_sssd_scan_workspace(2, 1024, 8, 128)
+    assert 0 < a < b
+    c0 = L.verace_cham_scan_workspace(2, 512, 1024, 0)
+    c1 = L.verace_cham_scan_workspace(2, 512, 1024, 1)
+    assert 0 < c0 < c1
+    assert L.verace_cham_retract_workspace(2, 1024) >= 4 * 2 * 1024 * 1024 * 4
+
+
+def _err():
+    return _lib.lib().verace_last_error().decode()
+
+
+def test_sssd_rejects_bad_arguments_without_a_device():
+    L = _lib.lib()
+    fake = ctypes.c_void_p(256)
+    rc = L.verace_sssd_scan(fake, fake, fake, fake, None, fake, fake, 1, 4, 2, 256, 0, fake, 1 << 20, None)
+    assert rc == 2 and "head_dim" in _err()
+    rc = L.verace_sssd_scan(fake, fake, fake, fake, None, fake, fake, 1, 4, 2, 64, 7, fake, 1 << 20, None)
+    assert rc == 1 and "dtype" in _err()
+    rc = L.verace_sssd_scan(fake, fake, fake, fake, None, fake, fake, 1, 4, 2, 64, 0, None, 0, None)
+    assert rc == 4 and "workspace" in _err()
+    rc = L.verace_sssd_scan(fake, fake, fake, fake, None, fake, fake, -1, 4, 2, 64, 0, fake, 1 << 20, None)
+    assert rc == 1
+
+
+def test_cham_rejects_bad_arguments_without_a_device():
+    L = _lib.lib()
+    fake = ctypes.c_void_p(256)
+    rc = L.verace_cham_scan(fake, fake, fake, fake, fake, None, fake, fake, fake, 1, 4, 16, 0, fake, 1 << 20, None)
+    assert rc == 1 and "both" in _err()
+    rc = L.verace_cham_scan(fake, fake, fake, fake, None, None, fake, fake, fake, 1, 4, 16, 0, None, 0, None)
+    assert rc == 4
+    rc = L.verace_cham_retract(fake, fake, fake, fake, 1, 16, -1, fake, 1 << 20, None)
+    assert rc == 1
+
+
+def test_status_error_raises_runtime_error():
+    with pytest.raises(RuntimeError, match="status 2"):
+        _lib.check(2, "probe")

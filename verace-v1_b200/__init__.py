@@ -1,1 +1,21 @@
-"""B200-native (sm_100a) SSSD + CHAM sequence-mixing path for Verace V1 (placeholder)."""
+"""B200-native (sm_100a) implementation of Verace V1's recurrent sequence-mixing path:
+the SSSD Cayley-rotation scan and the CHAM holographic-memory update with its
+Newton-Schulz readout retraction.
+
+Public surface (mirrors the reference package verace_v1 for this path):
+    SSSDAttention, ContinuousHolographicMemory, newton_schulz_unitary_retraction
+    launch_sssd_scan / launch_sssd_triton_scan
+    launch_cham_update / launch_cham_triton_update
+The kernels live in libverace_b200.so (C ABI: include/verace_b200.h), built by
+build.py; nothing here falls back to CPU or Python arithmetic.
+"""
+from .kernels import (cham_retract, launch_cham_triton_update, launch_cham_update,
+                      launch_sssd_scan, launch_sssd_triton_scan)
+from .sssd_attention import SSSDAttention
+from .cham_memory import ContinuousHolographicMemory, newton_schulz_unitary_retraction
+
+__all__ = [
+    "SSSDAttention", "ContinuousHolographicMemory", "newton_schulz_unitary_retraction",
+    "launch_sssd_scan", "launch_sssd_triton_scan", "launch_cham_update",
+    "launch_cham_triton_update", "cham_retract",
+]

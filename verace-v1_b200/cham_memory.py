@@ -1,0 +1,60 @@
+"""ContinuousHolographicMemory with the reference's constructor, parameters and
+forward signature (verace_v1/modules/cham_memory.py:99-243), running its scan and
+readout retraction on the sm_100a kernels.
+
+A reference ``state_dict`` loads unchanged (w_q, w_k, w_v, w_gamma, w_out, norm).
+The forward mirrors the reference's fast path (cham_memory.py:127-168):
+q, k = normalize(W x), v = normalize(silu(w_v x)), gamma = 0.1 sigmoid(w_gamma x)
+masked by ``active_mask``, the scan (exact Cayley updates, raw state exported,
+Newton-Schulz retraction on the readout) and ``norm(w_out(rec))``.
+
+``newton_schulz_unitary_retraction`` is the CUDA version of the reference function
+of the same name (cham_memory.py:21-51).
+"""
+from typing import Optional, Tuple
+
+import torch
+import torch.nn as nn
+import torch.nn.functional as F
+
+from .kernels import cham_retract, launch_cham_update
+from .sssd_attention import _require_inference
+
+
+def newton_schulz_unitary_retraction(H_real: torch.Tensor, H_imag: torch.Tensor, steps: int = 3
+                                     ) -> Tuple[torch.Tensor, torch.Tensor]:
+    return cham_retract(H_real, H_imag, steps)
+
+
+class ContinuousHolographicMemory(nn.Module):
+    def __init__(self, hidden_dim: int = 16384, holographic_dim: int = 1024):
+        super().__init__()
+        self.hidden_dim = hidden_dim
+        self.holographic_dim = holographic_dim
+        self.w_q = nn.Linear(hidden_dim, holographic_dim, bias=False)
+        self.w_k = nn.Linear(hidden_dim, holographic_dim, bias=False)
+        self.w_v = nn.Linear(hidden_dim, holographic_dim, bias=False)
+        self.w_gamma = nn.Linear(hidden_dim, 1, bias=False)
+        self.w_out = nn.Linear(holographic_dim, hidden_dim, bias=False)
+        self.norm = nn.RMSNorm(hidden_dim)
+
+    def project(self, x: torch.Tensor, active_mask: Optional[torch.Tensor] = None):
+        """q, k, v [b, s, D] and gamma [b, s] (cham_memory.py:129-153)."""
+        b, s, _ = x.shape
+        q = F.normalize(self.w_q(x), p=2, dim=-1)
+        k = F.normalize(self.w_k(x), p=2, dim=-1)
+        v = F.normalize(F.silu(self.w_v(x)), p=2, dim=-1)
+        gamma = 0.1 * torch.sigmoid(self.w_gamma(x)).view(b, s)
+        if active_mask is not None:
+            gamma = gamma * active_mask.reshape(b, s).to(gamma.dtype)
+        return q, k, v, gamma
+
+    def forward(self, x: torch.Tensor,
+                initial_hologram: Optional[Tuple[torch.Tensor, torch.Tensor]] = None,
+                active_mask: Optional[torch.Tensor] = None
+                ) -> Tuple[torch.Tensor, Tuple[torch.Tensor, torch.Tensor]]:
+        _require_inference(x, "ContinuousHolographicMemory.forward")
+        q, k, v, gamma = self.project(x, active_mask)
+        rec, (h_real, h_imag) = launch_cham_update(q, k, v, gamma, initial_hologram)
+        y = self.norm(self.w_out(rec))
+        return y, (h_real, h_imag)

@@ -1,0 +1,124 @@
+"""Launchers for the sm_100a SSSD / CHAM kernels, with the reference launchers' contracts.
+
+``launch_sssd_scan`` and ``launch_cham_update`` take and return exactly what the
+reference's ``launch_sssd_triton_scan`` / ``launch_cham_triton_update``
+(verace_v1/serving/triton_kernels.py:603-636, :639-685) take and return, so they are
+drop-ins for them; both names are exported as aliases too.  Differences in behaviour:
+
+* the CHAM readout applies the Newton-Schulz retraction of the eager path
+  (cham_memory.py:236-239) for every holographic width (the reference's D > 128
+  Triton fallback loops on the host per token);
+* non-CUDA inputs raise ``AssertionError("This kernel requires CUDA tensors")``, as
+  the reference launchers do (triton_kernels.py:616, 652).
+
+Outputs are freshly allocated; inputs are never modified; states are fp32.  Kernels
+are enqueued on torch's current CUDA stream.
+"""
+from typing import Optional, Tuple
+
+import torch
+
+from ._lib import BF16, F16, F32, check, lib
+
+_DTYPE = {torch.float32: F32, torch.bfloat16: BF16, torch.float16: F16}
+
+
+def _prep(x: torch.Tensor) -> torch.Tensor:
+    if x.dtype not in _DTYPE:
+        x = x.float()
+    return x.contiguous()
+
+
+def _stream(device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def _workspace(nbytes: int, device) -> torch.Tensor:
+    return torch.empty(max(int(nbytes), 1), dtype=torch.uint8, device=device)
+
+
+def _ptr(t: Optional[torch.Tensor]):
+    return None if t is None else t.data_ptr()
+
+
+def launch_sssd_scan(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, delta: torch.Tensor,
+                     initial_state: Optional[torch.Tensor] = None
+                     ) -> Tuple[torch.Tensor, torch.Tensor]:
+    """q, k, v: [b, s, h, d] (L2-normalised); delta: [b, s, h]; initial_state:
+    optional [b, h, d, d] (identity when None).
+    Returns (out [b, s, h, d] in q's dtype, final_state [b, h, d, d] fp32)."""
+    assert q.is_cuda, "This kernel requires CUDA tensors"
+    b, s, h, d = q.shape
+    q_c = _prep(q)
+    dt = q_c.dtype
+    k_c = k.to(dt).contiguous()
+    v_c = v.to(dt).contiguous()
+    delta_c = delta.reshape(b, s, h).float().contiguous()
+    psi0 = None if initial_state is None else initial_state.float().contiguous()
+    out = torch.empty_like(q_c)
+    psi_out = torch.empty(b, h, d, d, device=q.device, dtype=torch.float32)
+    L = lib()
+    nbytes = L.verace_sssd_scan_workspace(b, s, h, d)
+    ws = _workspace(nbytes, q.device)
+    with torch.cuda.device(q.device):
+        rc = L.verace_sssd_scan(q_c.data_ptr(), k_c.data_ptr(), v_c.data_ptr(), delta_c.data_ptr(),
+                                _ptr(psi0), out.data_ptr(), psi_out.data_ptr(), b, s, h, d,
+                                _DTYPE[dt], ws.data_ptr(), ws.numel(), _stream(q.device))
+    check(rc, "verace_sssd_scan")
+    return out, psi_out
+
+
+def launch_cham_update(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, gamma: torch.Tensor,
+                       initial_hologram: Optional[Tuple[torch.Tensor, torch.Tensor]] = None
+                       ) -> Tuple[torch.Tensor, Tuple[torch.Tensor, torch.Tensor]]:
+    """q, k, v: [b, s, D]; gamma: [b, s]; initial_hologram: optional (H_real, H_imag)
+    [b, D, D] ((I, 0) when None).
+    Returns (out [b, s, D] in q's dtype, (H_real, H_imag) [b, D, D] fp32 raw state)."""
+    assert q.is_cuda, "This kernel requires CUDA tensors"
+    b, s, D = q.shape
+    q_c = _prep(q)
+    dt = q_c.dtype
+    k_c = k.to(dt).contiguous()
+    v_c = v.to(dt).contiguous()
+    g_c = gamma.reshape(b, s).float().contiguous()
+    if initial_hologram is None:
+        h0r = h0i = None
+    else:
+        h0r = initial_hologram[0].float().contiguous()
+        h0i = initial_hologram[1].float().contiguous()
+    out = torch.empty(b, s, D, device=q.device, dtype=dt)
+    hr = torch.empty(b, D, D, device=q.device, dtype=torch.float32)
+    hi = torch.empty(b, D, D, device=q.device, dtype=torch.float32)
+    L = lib()
+    nbytes = L.verace_cham_scan_workspace(b, s, D, 0 if h0r is None else 1)
+    ws = _workspace(nbytes, q.device)
+    with torch.cuda.device(q.device):
+        rc = L.verace_cham_scan(q_c.data_ptr(), k_c.data_ptr(), v_c.data_ptr(), g_c.data_ptr(),
+                                _ptr(h0r), _ptr(h0i), out.data_ptr(), hr.data_ptr(), hi.data_ptr(),
+                                b, s, D, _DTYPE[dt], ws.data_ptr(), ws.numel(), _stream(q.device))
+    check(rc, "verace_cham_scan")
+    return out, (hr, hi)
+
+
+def cham_retract(H_real: torch.Tensor, H_imag: torch.Tensor, steps: int = 3
+                 ) -> Tuple[torch.Tensor, torch.Tensor]:
+    """Dense Newton-Schulz retraction on CUDA (the contract of
+    newton_schulz_unitary_retraction, cham_memory.py:21-51).  [b, D, D] fp32."""
+    assert H_real.is_cuda, "This kernel requires CUDA tensors"
+    hr = H_real.float().contiguous()
+    hi = H_imag.float().contiguous()
+    b, D, _ = hr.shape
+    out_r = torch.empty_like(hr)
+    out_i = torch.empty_like(hi)
+    L = lib()
+    ws = _workspace(L.verace_cham_retract_workspace(b, D), hr.device)
+    with torch.cuda.device(hr.device):
+        rc = L.verace_cham_retract(hr.data_ptr(), hi.data_ptr(), out_r.data_ptr(), out_i.data_ptr(),
+                                   b, D, int(steps), ws.data_ptr(), ws.numel(), _stream(hr.device))
+    check(rc, "verace_cham_retract")
+    return out_r, out_i
+
+
+# drop-in aliases with the reference's launcher names
+launch_sssd_triton_scan = launch_sssd_scan
+launch_cham_triton_update = launch_cham_update
