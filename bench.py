@@ -291,6 +291,40 @@ def run_reference(args):
     }), flush=True)
 
 
+def run_only(args):
+    """Kernel-level case used for profiling: one scan entry point on synthetic inputs."""
+    import torch
+    _load_package()
+    from verace_v1_b200.kernels import launch_cham_update, launch_sssd_scan
+    c = CFG
+    dev = torch.device("cuda", 0)
+    b, s = args.batch or c["batch"], args.seq or c["seq"]
+    g = torch.Generator().manual_seed(0)
+    nrm = torch.nn.functional.normalize
+    if args.only == "cham":
+        D = c["holo"]
+        q, k, v = (nrm(torch.randn(b, s, D, generator=g), dim=-1).to(dev, torch.bfloat16) for _ in range(3))
+        gam = (0.1 * torch.sigmoid(torch.randn(b, s, generator=g))).to(dev)
+        fn = lambda: launch_cham_update(q, k, v, gam)
+    else:
+        h, d = c["heads"], c["head_dim"]
+        q, k, v = (nrm(torch.randn(b, s, h, d, generator=g), dim=-1).to(dev, torch.bfloat16) for _ in range(3))
+        dl = (0.1 * torch.sigmoid(torch.randn(b, s, h, generator=g))).to(dev)
+        fn = lambda: launch_sssd_scan(q, k, v, dl)
+    for _ in range(args.warmup):
+        fn()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        fn()
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / args.steps
+    print(json.dumps({"only": args.only, "batch": b, "seq": s, "ms_per_call": ms,
+                      "tokens_per_s": b * s / (ms * 1e-3)}), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -300,8 +334,14 @@ def main():
     ap.add_argument("--cpu-tokens", type=int, default=32)
     ap.add_argument("--ref-tokens", type=int, default=8)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--only", choices=["cham", "sssd"], default=None,
+                    help="time one scan entry point alone (kernel-level case for profiling)")
+    ap.add_argument("--batch", type=int, default=None)
+    ap.add_argument("--seq", type=int, default=None)
     args = ap.parse_args()
-    if args.impl == "reference":
+    if args.only:
+        run_only(args)
+    elif args.impl == "reference":
         run_reference(args)
     else:
         run_ours(args)
