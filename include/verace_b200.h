@@ -74,6 +74,27 @@ VERACE_API int verace_sssd_scan(const void* q, const void* k, const void* v, con
                      void* workspace, size_t workspace_bytes, void* stream);
 
 /* ------------------------------------------------------------------------------
+ * Allocation-free SSSD scan.  No counterpart in the reference: it exists for hosts
+ * that cannot allocate device memory on the path that runs the scan (plugin or FFI
+ * runtimes that own all device memory and pass only inputs and outputs; serving
+ * loops with a fixed memory budget, where an allocation may synchronise the device).
+ * Same arguments and results as verace_sssd_scan without the workspace: the scratch
+ * is a fixed 16 MiB device array inside this library, which every GPU that loads the
+ * library holds until the process exits.  Sizes whose scratch exceeds 16 MiB
+ * (verace_sssd_scan_workspace(b, s, h, d) > 16 MiB) return VERACE_ERR_UNSUPPORTED.
+ * The first call on a device looks the array's device address up (once per device,
+ * with that device current); make that first call before any stream capture.
+ * All calls in a process share the one array per device: calls that overlap on the
+ * GPU (issued on concurrent streams, or from several host threads) race on it and
+ * give undefined results, so serialise them (one stream, or an event between calls).
+ * Each call rewrites the scratch it reads, so nothing in it needs to start at zero.
+ * ---------------------------------------------------------------------------- */
+VERACE_API int verace_sssd_scan_noalloc(const void* q, const void* k, const void* v,
+                                        const float* delta, const float* psi0, void* out,
+                                        float* psi_out, int b, int s, int h, int d, int dtype,
+                                        void* stream);
+
+/* ------------------------------------------------------------------------------
  * CHAM holographic-memory scan with Newton-Schulz readout retraction.
  * Replaces launch_cham_triton_update / launch_cham_triton_tiled
  * (verace_v1/serving/triton_kernels.py:639-685, :552-597), the kernels behind

@@ -16,6 +16,8 @@
 // stays in shared memory for the whole sequence; chunks are processed in order).
 #include "common.cuh"
 
+#include <mutex>
+
 namespace verace {
 namespace {
 
@@ -286,6 +288,79 @@ extern "C" int verace_sssd_scan(const void* q, const void* k, const void* v, con
   float* Tws = (float*)workspace;
   unsigned long long* badws =
       (unsigned long long*)((char*)workspace + align_up(sssd_t_bytes(chains, nch), 256));
+  cudaStream_t st = (cudaStream_t)stream;
+  switch (dtype) {
+    case VERACE_F32: return launch_sssd<float>(q, k, v, delta, psi0, out, psi_out, b, s, h, d, Tws, badws, st);
+    case VERACE_BF16: return launch_sssd<__nv_bfloat16>(q, k, v, delta, psi0, out, psi_out, b, s, h, d, Tws, badws, st);
+    default: return launch_sssd<__half>(q, k, v, delta, psi0, out, psi_out, b, s, h, d, Tws, badws, st);
+  }
+}
+
+// ---------------------------------------------------------------------------------
+// Allocation-free variant.  Some hosts cannot call cudaMalloc on the path that runs
+// this scan: plugin / FFI runtimes that own every byte of device memory and hand the
+// library only its inputs and outputs, and memory-budgeted serving loops where an
+// allocation (which may synchronise the device) is not allowed.  For them the scan's
+// scratch (the per-chunk transforms T and the non-finite-token masks) lives in the
+// fixed device array below, which every GPU that loads this library holds until the
+// process exits.  Host code never uses the array's name as a device address: the
+// address is looked up with cudaGetSymbolAddress once per device (by the first call
+// on that device, with that device current) and passed to the kernels.
+namespace verace {
+namespace {
+
+constexpr size_t SSSD_NOALLOC_SCRATCH_BYTES = size_t(16) << 20;  // 16 MiB
+static __device__ __align__(256) unsigned char g_sssd_noalloc_scratch[SSSD_NOALLOC_SCRATCH_BYTES];
+
+constexpr int MAX_DEVICES = 64;
+std::mutex g_noalloc_mutex;
+void* g_noalloc_ptr[MAX_DEVICES] = {};
+
+int noalloc_scratch(void** out) {
+  int dev = 0;
+  VERACE_CUDA(cudaGetDevice(&dev));
+  VERACE_REQUIRE(dev >= 0 && dev < MAX_DEVICES, VERACE_ERR_UNSUPPORTED,
+                 "verace_sssd_scan_noalloc: device ordinal %d out of range", dev);
+  std::lock_guard<std::mutex> lock(g_noalloc_mutex);
+  if (g_noalloc_ptr[dev] == nullptr) {
+    void* p = nullptr;
+    VERACE_CUDA(cudaGetSymbolAddress(&p, g_sssd_noalloc_scratch));
+    g_noalloc_ptr[dev] = p;
+  }
+  *out = g_noalloc_ptr[dev];
+  return VERACE_OK;
+}
+
+}  // namespace
+}  // namespace verace
+
+extern "C" int verace_sssd_scan_noalloc(const void* q, const void* k, const void* v,
+                                        const float* delta, const float* psi0, void* out,
+                                        float* psi_out, int b, int s, int h, int d, int dtype,
+                                        void* stream) {
+  VERACE_REQUIRE(b >= 0 && s >= 0 && h >= 1 && d >= 1, VERACE_ERR_INVALID,
+                 "verace_sssd_scan_noalloc: invalid sizes b=%d s=%d h=%d d=%d", b, s, h, d);
+  VERACE_REQUIRE(d <= SSSD_MAX_D, VERACE_ERR_UNSUPPORTED,
+                 "verace_sssd_scan_noalloc: head_dim %d > %d is not supported", d, SSSD_MAX_D);
+  VERACE_REQUIRE(dtype == VERACE_F32 || dtype == VERACE_BF16 || dtype == VERACE_F16,
+                 VERACE_ERR_INVALID, "verace_sssd_scan_noalloc: unknown dtype %d", dtype);
+  if (b == 0) return VERACE_OK;
+  VERACE_REQUIRE(psi_out != nullptr, VERACE_ERR_INVALID, "verace_sssd_scan_noalloc: psi_out is NULL");
+  VERACE_REQUIRE(s == 0 || (q && k && v && delta && out), VERACE_ERR_INVALID,
+                 "verace_sssd_scan_noalloc: NULL input/output pointer");
+  const size_t need = s > 0 ? verace_sssd_scan_workspace(b, s, h, d) : 0;
+  VERACE_REQUIRE(need <= SSSD_NOALLOC_SCRATCH_BYTES, VERACE_ERR_UNSUPPORTED,
+                 "verace_sssd_scan_noalloc: this size needs %zu bytes of scratch, more than the "
+                 "fixed %zu-byte device array; use verace_sssd_scan with a workspace",
+                 need, SSSD_NOALLOC_SCRATCH_BYTES);
+  void* scratch = nullptr;
+  const int rc = noalloc_scratch(&scratch);
+  if (rc != VERACE_OK) return rc;
+  const size_t chains = (size_t)b * h;
+  const size_t nch = ((size_t)s + SC - 1) / SC;
+  float* Tws = (float*)scratch;
+  unsigned long long* badws =
+      (unsigned long long*)((char*)scratch + align_up(sssd_t_bytes(chains, nch), 256));
   cudaStream_t st = (cudaStream_t)stream;
   switch (dtype) {
     case VERACE_F32: return launch_sssd<float>(q, k, v, delta, psi0, out, psi_out, b, s, h, d, Tws, badws, st);
