@@ -51,6 +51,12 @@ VERACE_API int verace_version(void);
 /* Message describing the last error returned on the calling host thread. */
 VERACE_API const char* verace_last_error(void);
 
+/* Synchronises `stream`, then reports (and clears) the device-side status of this
+ * library's bounded waits: VERACE_ERR_TIMEOUT if a kernel gave up waiting for a
+ * tensor-core completion since the last call, else 0.  No reference counterpart: the
+ * reference has no device-side waits. */
+VERACE_API int verace_device_status(void* stream);
+
 /* Number of kernels this library has launched in the process so far (all devices,
  * all host threads).  Lets a caller count the library's own launches in a region. */
 VERACE_API unsigned long long verace_kernel_launches(void);

@@ -1,0 +1,84 @@
+"""The tcgen05 CHAM scan (holographic width a multiple of 128, fresh hologram) against
+the fp64 oracle and against the fp32 SIMT kernels, across chunk boundaries (64-token
+chunks), batch sizes, input dtypes and edge cases.
+
+Tolerances: relative Frobenius <= 1e-4 vs the fp64 oracle for fp32 inputs (the
+north-star fp32 bound), <= 2e-2 on bf16 outputs, <= 1e-4 on fp32 states.
+"""
+import os
+
+import numpy as np
+import pytest
+import torch
+
+import oracle
+import verace_v1_b200 as V
+from gpu_util import random_cham_inputs, rel_fro, to_np
+from verace_v1_b200 import _lib
+
+pytestmark = pytest.mark.gpu
+
+
+def _status_ok():
+    _lib.check(_lib.lib().verace_device_status(torch.cuda.current_stream().cuda_stream), "device status")
+
+
+def _simt(q, k, v, g):
+    os.environ["VERACE_CHAM_SIMT"] = "1"
+    try:
+        return V.launch_cham_update(q, k, v, g)
+    finally:
+        del os.environ["VERACE_CHAM_SIMT"]
+
+
+@pytest.mark.parametrize("b,s,D", [(1, 1, 128), (2, 63, 128), (1, 64, 128), (2, 65, 256),
+                                   (1, 130, 128), (3, 7, 256)])
+def test_tc_scan_fp32_matches_fp64_oracle(b, s, D):
+    q, k, v, g = random_cham_inputs(b, s, D, seed=400 + s + D)
+    out, (Hr, Hi) = V.launch_cham_update(q, k, v, g)
+    _status_ok()
+    r_ref, (Hr_ref, Hi_ref) = oracle.cham_scan(to_np(q), to_np(k), to_np(v), to_np(g))
+    assert rel_fro(to_np(out), r_ref) <= 1e-4
+    assert rel_fro(to_np(Hr), Hr_ref) <= 1e-4
+    assert np.abs(to_np(Hi) - Hi_ref).max() <= 1e-4
+
+
+@pytest.mark.parametrize("b,s,D", [(2, 100, 256), (1, 64, 1024)])
+def test_tc_scan_bf16_matches_fp64_oracle(b, s, D):
+    q, k, v, g = random_cham_inputs(b, s, D, seed=500 + s, dtype=torch.bfloat16)
+    out, (Hr, Hi) = V.launch_cham_update(q, k, v, g)
+    _status_ok()
+    assert out.dtype == torch.bfloat16
+    r_ref, (Hr_ref, Hi_ref) = oracle.cham_scan(to_np(q), to_np(k), to_np(v), to_np(g))
+    assert rel_fro(to_np(out), r_ref) <= 2e-2
+    assert rel_fro(to_np(Hr), Hr_ref) <= 1e-4
+    assert np.abs(to_np(Hi) - Hi_ref).max() <= 1e-4
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_tc_scan_matches_simt_kernels_at_production_width(dtype):
+    q, k, v, g = random_cham_inputs(2, 200, 1024, seed=600, dtype=dtype)
+    out, (Hr, Hi) = V.launch_cham_update(q, k, v, g)
+    _status_ok()
+    out_s, (Hr_s, Hi_s) = _simt(q, k, v, g)
+    assert rel_fro(to_np(out), to_np(out_s)) <= (1e-4 if dtype == torch.float32 else 1e-2)
+    assert rel_fro(to_np(Hr), to_np(Hr_s)) <= 1e-5
+    assert rel_fro(to_np(Hi), to_np(Hi_s)) <= 1e-4
+
+
+def test_tc_scan_zero_gamma_and_nonfinite_tokens():
+    q, k, v, g = random_cham_inputs(2, 70, 128, seed=700)
+    out, (Hr, Hi) = V.launch_cham_update(q, k, v, torch.zeros_like(g))
+    _status_ok()
+    torch.testing.assert_close(Hr, torch.eye(128, device="cuda").expand(2, 128, 128), rtol=0, atol=1e-6)
+    assert Hi.abs().max().item() <= 1e-6
+    torch.testing.assert_close(out, q, rtol=1e-5, atol=1e-5)
+    k_bad = k.clone()
+    k_bad[1, 66, 3] = float("nan")
+    out_b, (Hr_b, _) = V.launch_cham_update(q, k_bad, v, g)
+    g_id = g.clone()
+    g_id[1, 66] = 0.0
+    out_i, (Hr_i, _) = V.launch_cham_update(q, k, v, g_id)
+    _status_ok()
+    torch.testing.assert_close(Hr_b, Hr_i)
+    torch.testing.assert_close(out_b, out_i)

@@ -23,6 +23,7 @@ _SIGNATURES = {
     "verace_version": (_i, []),
     "verace_last_error": (ctypes.c_char_p, []),
     "verace_kernel_launches": (ctypes.c_ulonglong, []),
+    "verace_device_status": (_i, [_p]),
     "verace_sssd_scan_workspace": (_c_size, [_i, _i, _i, _i]),
     "verace_sssd_scan": (_i, [_p, _p, _p, _p, _p, _p, _p, _i, _i, _i, _i, _i, _p, _c_size, _p]),
     "verace_sssd_scan_noalloc": (_i, [_p, _p, _p, _p, _p, _p, _p, _i, _i, _i, _i, _i, _p]),

@@ -31,8 +31,24 @@
 #include "common.cuh"
 #include "cgemm.cuh"
 
+#include <stdlib.h>
+
 namespace verace {
+
+// tcgen05 path (cham_tc.cu)
+bool cham_tc_supported(int D, int dtype, bool has_h0);
+size_t cham_tc_workspace(int b, int s, int D);
+int cham_tc_scan(const void* q, const void* k, const void* v, const float* gamma, void* out,
+                 float* hr, float* hi, int b, int s, int D, int dtype, void* workspace, cudaStream_t st);
+int tc_read_status(cudaStream_t st, int* status);
+
 namespace {
+
+// VERACE_CHAM_SIMT=1 forces the fp32 SIMT kernels (used to compare the two paths).
+bool force_simt() {
+  const char* e = getenv("VERACE_CHAM_SIMT");
+  return e && e[0] && e[0] != '0';
+}
 
 constexpr int CC = 32;       // tokens per chunk
 constexpr int CR = 2 * CC;   // rank of a chunk transform
@@ -486,7 +502,12 @@ using namespace verace;
 
 extern "C" size_t verace_cham_scan_workspace(int b, int s, int D, int has_h0) {
   if (b <= 0 || s <= 0 || D <= 0) return 256;
-  return ws_layout(b, s, D, has_h0 ? 1 : 0, nullptr, nullptr);
+  size_t n = ws_layout(b, s, D, has_h0 ? 1 : 0, nullptr, nullptr);
+  if (!has_h0 && D % 128 == 0) {
+    const size_t t = cham_tc_workspace(b, s, D);
+    if (t > n) n = t;
+  }
+  return n;
 }
 
 extern "C" int verace_cham_scan(const void* q, const void* k, const void* v, const float* gamma,
@@ -519,6 +540,8 @@ extern "C" int verace_cham_scan(const void* q, const void* k, const void* v, con
   VERACE_REQUIRE(workspace != nullptr && workspace_bytes >= need, VERACE_ERR_WORKSPACE,
                  "verace_cham_scan: workspace of %zu bytes required, %zu given", need,
                  workspace ? workspace_bytes : (size_t)0);
+  if (cham_tc_supported(D, dtype, has_h0 != 0) && !force_simt())
+    return cham_tc_scan(q, k, v, gamma, out, h_re, h_im, b, s, D, dtype, workspace, st);
   ChamWs w;
   char* base = (char*)align_up((size_t)workspace, 256);
   ws_layout(b, s, D, has_h0, &w, base);
@@ -575,5 +598,14 @@ extern "C" int verace_cham_retract(const float* h_re, const float* h_im, float* 
     cr = nr;
     ci = ni;
   }
+  return VERACE_OK;
+}
+
+extern "C" int verace_device_status(void* stream) {
+  int status = 0;
+  const int rc = tc_read_status((cudaStream_t)stream, &status);
+  if (rc) return rc;
+  VERACE_REQUIRE(status == 0, VERACE_ERR_TIMEOUT,
+                 "a bounded device-side wait gave up (tensor-core completion never arrived)");
   return VERACE_OK;
 }

@@ -1,0 +1,725 @@
+// CHAM scan on the tcgen05 tensor cores (sm_100a), for holographic widths D that are
+// multiples of 128 and a fresh hologram (H_0 = I, so the readout vectors are y_t = q_t).
+//
+// Same chunked compact-WY recurrence as cham_scan.cu (see the derivation there), with
+// chunks of C = 64 tokens so that the chunk rank 2C = 128 is one tensor-core tile:
+//     Z = Wᵀ S,  [P1 | P2] = [Tr | Ti] Z,  Cm = (P1_re - P2_im) + i (P1_im + P2_re)
+//     S_next = S + W Cm,   E = Re(Cm) Y (reduced over column blocks),
+//     rec_t = Re(S y_t) + sum_{tau<=t} U_tau E_tau,t
+// fp32 operands enter the bf16 tensor cores as hi + lo bf16 pairs (x = hi + lo to 16
+// significant bits); products that need it take hi*hi + hi*lo + lo*hi, accumulated in
+// fp32 in tensor memory.  bf16 q/k/v (the model's dtype) are exact in bf16 and need
+// no split; fp32 q/k/v are split too.  The state stays fp32 in global memory.
+//
+// Kernels (per call: one prep launch, then per chunk one colpass + one readout):
+//   cham_tc_prep     T (complex 128x128) for every chunk, written as bf16 hi/lo tiles
+//                    in the tensor-core operand layout; zeroes the chunk's E block.
+//   cham_tc_colpass  one CTA per (item, 32 complex columns): Z, Cm, E partial, and
+//                    that column block of S_next.  TMEM: 320 of 512 columns.
+//   cham_tc_readout  one CTA per (item, 128 rows): Re(S Y) + W mask(E).
+#include "common.cuh"
+#include "tc.cuh"
+
+namespace verace {
+namespace {
+
+constexpr int C2 = 64;          // tokens per chunk
+constexpr int R2 = 128;         // chunk rank (k and v of 64 tokens)
+constexpr int NB2 = 32;         // complex columns per colpass CTA
+constexpr int N2 = 2 * NB2;     // real columns (re | im) per colpass CTA
+constexpr int KT = 128;         // rows of S per K tile
+constexpr int THR = 256;
+constexpr uint32_t MAX_POLLS = 1u << 22;
+constexpr int PREP_DT = 32;
+
+__device__ int g_tc_status = 0;  // non-zero after a bounded wait gave up
+
+// tile sizes in bytes
+constexpr int W_TILE = R2 * KT * 2;        // 32 KB: 128 vectors x 128 elements, bf16
+constexpr int H_TILE = KT * N2 * 2;        // 16 KB: 128 rows x 64 columns, bf16
+constexpr int T_TILE = R2 * R2 * 2;        // 32 KB: 128 x 128 bf16
+constexpr int Z_TILE = R2 * N2 * 2;        // 16 KB: 128 x 64 bf16
+constexpr int CA_TILE = R2 * NB2 * 2;      //  8 KB: 128 x 32 bf16
+constexpr int Y_TILE = C2 * NB2 * 2;       //  4 KB: 64 tokens x 32 columns bf16
+
+struct TcWs {
+  unsigned char* T;          // [b][nch][4][T_TILE]: Tr_hi, Tr_lo, Ti_hi, Ti_lo
+  float* E;                  // [b][nch][R2][C2]
+  unsigned long long* bad;   // [b][nch]
+  float* Hre;
+  float* Him;
+};
+
+size_t tc_ws_layout(int b, int s, int D, TcWs* w, char* base) {
+  const size_t nch = ((size_t)s + C2 - 1) / C2;
+  size_t off = 0;
+  auto take = [&](size_t bytes) { size_t o = off; off += align_up(bytes, 256); return base ? (void*)(base + o) : nullptr; };
+  TcWs t;
+  t.T = (unsigned char*)take((size_t)b * nch * 4 * T_TILE);
+  t.E = (float*)take((size_t)b * nch * R2 * C2 * sizeof(float));
+  t.bad = (unsigned long long*)take((size_t)b * nch * sizeof(unsigned long long));
+  const bool ping = nch >= 2;
+  t.Hre = (float*)take(ping ? (size_t)b * D * D * sizeof(float) : 0);
+  t.Him = (float*)take(ping ? (size_t)b * D * D * sizeof(float) : 0);
+  if (w) *w = t;
+  return off + 256;
+}
+
+__device__ __forceinline__ void record_timeout() { atomicExch(&g_tc_status, 1); }
+
+// byte offset of element (r, k) in a K-major tile with R rows
+__device__ __forceinline__ int kmaj(int r, int k, int R) { return ((k >> 3) * R + r) * 16 + (k & 7) * 2; }
+// byte offset of element (k, n) in a directly built MN-major tile with NG = N/8 groups
+__device__ __forceinline__ int mnmaj(int k, int n, int NG) { return (((k >> 3) * NG + (n >> 3)) * 128) + (k & 7) * 16 + (n & 7) * 2; }
+
+__device__ __forceinline__ void load8(const __nv_bfloat16* p, float* x) {
+  const uint4 u = *reinterpret_cast<const uint4*>(p);
+  const __nv_bfloat16* h = reinterpret_cast<const __nv_bfloat16*>(&u);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) x[i] = __bfloat162float(h[i]);
+}
+__device__ __forceinline__ void load8(const float* p, float* x) {
+  const float4 a = *reinterpret_cast<const float4*>(p);
+  const float4 b = *reinterpret_cast<const float4*>(p + 4);
+  x[0] = a.x; x[1] = a.y; x[2] = a.z; x[3] = a.w; x[4] = b.x; x[5] = b.y; x[6] = b.z; x[7] = b.w;
+}
+
+// Stage 8 consecutive input elements as one 16-byte bf16 chunk (hi) and, for fp32
+// inputs, the matching lo chunk.  Non-finite or padded tokens are staged as zeros.
+template <typename T>
+__device__ __forceinline__ void stage8(const T* src, bool valid, unsigned char* hi, unsigned char* lo) {
+  if (sizeof(T) == 2) {
+    uint4 u = make_uint4(0, 0, 0, 0);
+    if (valid) u = *reinterpret_cast<const uint4*>(src);
+    *reinterpret_cast<uint4*>(hi) = u;
+  } else {
+    float x[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    if (valid) load8(src, x);
+    uint4 h, l;
+    tc::split8(x, h, l);
+    *reinterpret_cast<uint4*>(hi) = h;
+    *reinterpret_cast<uint4*>(lo) = l;
+  }
+}
+
+// Stage the chunk's k/v vectors, elements [i0, i0+KT), as a K-major tile with rows =
+// vector index r (2*tau + {0: k, 1: v}).
+template <typename T>
+__device__ __forceinline__ void stage_w(unsigned char* sw_hi, unsigned char* sw_lo,
+                                        const T* __restrict__ k, const T* __restrict__ v,
+                                        int item, int S, int D, int t0, int nt, unsigned long long bad,
+                                        int i0, int tid) {
+  for (int e = tid; e < R2 * (KT / 8); e += THR) {
+    const int r = e % R2, g = e / R2;  // consecutive threads -> consecutive vectors
+    const int tau = r >> 1;
+    const bool valid = tau < nt && !((bad >> tau) & 1ull);
+    const T* src = ((r & 1) ? v : k) + ((size_t)item * S + t0 + (valid ? tau : 0)) * D + i0 + g * 8;
+    stage8(src, valid, sw_hi + kmaj(r, g * 8, R2), sw_lo + kmaj(r, g * 8, R2));
+  }
+}
+
+// ---------------------------------------------------------------------------------
+// prep: W Gram matrix, N_t, complex T by block forward substitution (fp32 SIMT), then
+// T written as bf16 hi/lo K-major 128x128 tiles.  smem: Wt [DT][R2+1], Gs/Tr/Ti [R2][R2+1]
+template <typename T>
+__global__ void __launch_bounds__(THR)
+cham_tc_prep(const T* __restrict__ k, const T* __restrict__ v, const float* __restrict__ gamma,
+             unsigned char* __restrict__ Tws, float* __restrict__ Ews, unsigned long long* __restrict__ badws,
+             int S, int D, int nch) {
+  extern __shared__ float sm[];
+  constexpr int P = R2 + 1;
+  float* Wt = sm;
+  float* Gs = Wt + PREP_DT * P;
+  float* Tr = Gs + R2 * P;
+  float* Ti = Tr + R2 * P;
+  __shared__ float Ns[C2 * 6];
+  __shared__ unsigned long long bad_bits;
+  const int c = blockIdx.x, item = blockIdx.y, tid = threadIdx.x;
+  const int t0 = c * C2, nt = min(C2, S - t0);
+  if (tid == 0) bad_bits = 0ull;
+  for (int e = tid; e < R2 * P; e += THR) Gs[e] = 0.f;
+  for (int i0 = 0; i0 < D; i0 += PREP_DT) {
+    __syncthreads();
+    for (int e = tid; e < PREP_DT * R2; e += THR) {
+      const int i = e / R2, r = e % R2, tau = r >> 1;
+      float val = 0.f;
+      if (tau < nt && i0 + i < D) {
+        const size_t off = ((size_t)item * S + t0 + tau) * D + i0 + i;
+        val = to_f32((r & 1) ? v[off] : k[off]);
+      }
+      Wt[i * P + r] = val;
+      if (!isfinite(val)) atomicOr(&bad_bits, 1ull << tau);
+    }
+    __syncthreads();
+    if (bad_bits) {
+      for (int e = tid; e < PREP_DT * R2; e += THR)
+        if ((bad_bits >> ((e % R2) >> 1)) & 1ull) Wt[(e / R2) * P + e % R2] = 0.f;
+      __syncthreads();
+    }
+    smem_gemm<4, 4, true>(R2, R2, PREP_DT, Wt, 1, P, Wt, P, 1, Gs, P, 1, tid, THR);
+  }
+  __syncthreads();
+  if (tid < C2 && tid < nt && !isfinite(gamma[(size_t)item * S + t0 + tid])) atomicOr(&bad_bits, 1ull << tid);
+  __syncthreads();
+  if (tid < C2) {
+    const int tau = tid;
+    float n00r = 0.f, n00i = 0.f, n01r = 0.f, n01i = 0.f, n11r = 0.f, n11i = 0.f;
+    bool flagged = (bad_bits >> tau) & 1ull;
+    if (tau < nt && !flagged) {
+      const float kk = Gs[(2 * tau) * P + 2 * tau];
+      const float vv = Gs[(2 * tau + 1) * P + 2 * tau + 1];
+      const float kv = Gs[(2 * tau) * P + 2 * tau + 1];
+      const float g = gamma[(size_t)item * S + t0 + tau];
+      const float cc = 0.5f * g;
+      const float dr = 1.f + cc * cc * (kk * vv - kv * kv);
+      const float di = -2.f * cc * kv;
+      const float m2 = dr * dr + di * di;
+      const float fr = 2.f * cc * dr / m2;
+      const float fi = -2.f * cc * di / m2;
+      n00r = fr * (-cc * vv); n00i = fi * (-cc * vv);
+      n11r = fr * (-cc * kk); n11i = fi * (-cc * kk);
+      n01r = fr * (cc * kv) - fi; n01i = fr + fi * (cc * kv);
+      const bool ok = isfinite(kk) && isfinite(vv) && isfinite(kv) && isfinite(n00r) && isfinite(n00i) &&
+                      isfinite(n01r) && isfinite(n01i) && isfinite(n11r) && isfinite(n11i);
+      if (!ok) {
+        n00r = n00i = n01r = n01i = n11r = n11i = 0.f;
+        atomicOr(&bad_bits, 1ull << tau);
+        flagged = true;
+      }
+    }
+    if (flagged) {
+      for (int r = 0; r < R2; ++r) {
+        Gs[(2 * tau) * P + r] = 0.f; Gs[(2 * tau + 1) * P + r] = 0.f;
+        Gs[r * P + 2 * tau] = 0.f; Gs[r * P + 2 * tau + 1] = 0.f;
+      }
+    }
+    float* n = Ns + tau * 6;
+    n[0] = n00r; n[1] = n00i; n[2] = n01r; n[3] = n01i; n[4] = n11r; n[5] = n11i;
+  }
+  __syncthreads();
+  if (tid < R2) {
+    const int sg = tid, blk = sg >> 1;
+    for (int r = 0; r < 2 * blk; ++r) { Tr[r * P + sg] = 0.f; Ti[r * P + sg] = 0.f; }
+    for (int t = blk; t < C2; ++t) {
+      float x0r = (sg == 2 * t) ? 1.f : 0.f, x0i = 0.f;
+      float x1r = (sg == 2 * t + 1) ? 1.f : 0.f, x1i = 0.f;
+      for (int tp = blk; tp < t; ++tp) {
+        const float a0r = Tr[(2 * tp) * P + sg], a0i = Ti[(2 * tp) * P + sg];
+        const float a1r = Tr[(2 * tp + 1) * P + sg], a1i = Ti[(2 * tp + 1) * P + sg];
+        const float g00 = Gs[(2 * t) * P + 2 * tp], g01 = Gs[(2 * t) * P + 2 * tp + 1];
+        const float g10 = Gs[(2 * t + 1) * P + 2 * tp], g11 = Gs[(2 * t + 1) * P + 2 * tp + 1];
+        x0r += g00 * a0r + g01 * a1r; x0i += g00 * a0i + g01 * a1i;
+        x1r += g10 * a0r + g11 * a1r; x1i += g10 * a0i + g11 * a1i;
+      }
+      const float* n = Ns + t * 6;
+      Tr[(2 * t) * P + sg] = n[0] * x0r - n[1] * x0i + n[2] * x1r - n[3] * x1i;
+      Ti[(2 * t) * P + sg] = n[0] * x0i + n[1] * x0r + n[2] * x1i + n[3] * x1r;
+      Tr[(2 * t + 1) * P + sg] = n[2] * x0r - n[3] * x0i + n[4] * x1r - n[5] * x1i;
+      Ti[(2 * t + 1) * P + sg] = n[2] * x0i + n[3] * x0r + n[4] * x1i + n[5] * x1r;
+    }
+  }
+  __syncthreads();
+  const size_t chunk = (size_t)item * nch + c;
+  unsigned char* To = Tws + chunk * 4 * T_TILE;
+  // K-major tiles: A(m = r, k = r') = T[r][r']
+  for (int e = tid; e < R2 * (R2 / 8); e += THR) {
+    const int r = e % R2, g = e / R2;
+    float xr[8], xi[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) { xr[j] = Tr[r * P + g * 8 + j]; xi[j] = Ti[r * P + g * 8 + j]; }
+    uint4 h, l;
+    const int off = kmaj(r, g * 8, R2);
+    tc::split8(xr, h, l);
+    *reinterpret_cast<uint4*>(To + 0 * T_TILE + off) = h;
+    *reinterpret_cast<uint4*>(To + 1 * T_TILE + off) = l;
+    tc::split8(xi, h, l);
+    *reinterpret_cast<uint4*>(To + 2 * T_TILE + off) = h;
+    *reinterpret_cast<uint4*>(To + 3 * T_TILE + off) = l;
+  }
+  float* Eo = Ews + chunk * R2 * C2;
+  for (int e = tid; e < R2 * C2; e += THR) Eo[e] = 0.f;
+  if (tid == 0) badws[chunk] = bad_bits;
+}
+
+// ---------------------------------------------------------------------------------
+// colpass.  Shared memory (bytes):
+//   U   [0, 128K)     phase A/B: W hi (32K) | H hi (16K) | H lo (16K) | W lo (32K, fp32 inputs)
+//                     phase T:   Tr hi | Tr lo | Ti hi | Ti lo (4 x 32K)
+//   Zs  [128K, 160K)  Z as the B operand of T Z (MN-major, hi 16K | lo 16K)
+//   Cs  [160K, 192K)  Cm as the B operand of W Cm (MN-major, hi 16K | lo 16K)
+//   Ca  [192K, 208K)  Re(Cm) as the A operand of E (K-major, hi 8K | lo 8K)
+//   Ys  [208K, 216K)  Y block as the B operand of E (K-major, hi 4K | lo 4K)
+//   bar, tmem slot
+// TMEM columns: Z [0,64) P1 [64,128) P2 [128,192) E [192,256) dH [256,320)
+constexpr int SM_U = 0, SM_Z = 128 * 1024, SM_C = 160 * 1024, SM_CA = 192 * 1024, SM_Y = 208 * 1024;
+constexpr int SM_BAR = 216 * 1024;
+// 8 KB of slack after the last operand tile keeps every tensor-core read of a tile's
+// descriptor footprint inside the allocation.
+constexpr int SMEM_SLACK = 8 * 1024;
+constexpr int COLPASS_SMEM = SM_BAR + 64 + SMEM_SLACK;
+
+template <typename T>
+__global__ void __launch_bounds__(THR, 1)
+cham_tc_colpass(const T* __restrict__ q, const T* __restrict__ k, const T* __restrict__ v,
+                const unsigned char* __restrict__ Tws, float* __restrict__ Ews,
+                const unsigned long long* __restrict__ badws,
+                const float* __restrict__ src_r, const float* __restrict__ src_i,
+                float* __restrict__ dst_r, float* __restrict__ dst_i, int S, int D, int nch, int c) {
+  extern __shared__ __align__(1024) unsigned char smc[];
+  constexpr bool F32IN = sizeof(T) == 4;
+  unsigned char* sW = smc + SM_U;
+  unsigned char* sHh = smc + SM_U + W_TILE;
+  unsigned char* sHl = sHh + H_TILE;
+  unsigned char* sWl = sHl + H_TILE;
+  unsigned char* sT = smc + SM_U;
+  unsigned char* sZh = smc + SM_Z;
+  unsigned char* sZl = sZh + Z_TILE;
+  unsigned char* sCh = smc + SM_C;
+  unsigned char* sCl = sCh + Z_TILE;
+  unsigned char* sAh = smc + SM_CA;
+  unsigned char* sAl = sAh + CA_TILE;
+  unsigned char* sYh = smc + SM_Y;
+  unsigned char* sYl = sYh + Y_TILE;
+  uint64_t* bar = reinterpret_cast<uint64_t*>(smc + SM_BAR);
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(smc + SM_BAR + 16);
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int item = blockIdx.y, j0 = blockIdx.x * NB2;
+  const int t0 = c * C2, nt = min(C2, S - t0);
+  const size_t chunk = (size_t)item * nch + c;
+  const unsigned long long bad = badws[chunk];
+  const size_t soff = (size_t)item * D * D;
+  const float* sr = src_r ? src_r + soff : nullptr;
+  const float* si = src_i ? src_i + soff : nullptr;
+
+  if (warp == 0) tc::tmem_alloc(tslot, 512);
+  if (tid == 0) { tc::mbar_init(bar, 1); tc::fence_mbar_init(); }
+  tc::fence_before_sync();
+  __syncthreads();
+  tc::fence_after_sync();
+  const uint32_t tbase = *tslot;
+  const uint32_t tZ = tbase, tP1 = tbase + 64, tP2 = tbase + 128, tE = tbase + 192, tDH = tbase + 256;
+  const uint32_t lane_base = (uint32_t)(32 * (warp & 3)) << 16;
+  const int row = 32 * (warp & 3) + lane;   // TMEM lane == accumulator row of this thread
+  const int half = warp >> 2;               // which half of the accumulator columns
+  uint32_t phase = 0;
+  bool failed = false;
+
+  auto wait_mma = [&]() -> bool {
+    const bool ok = tc::mbar_wait(bar, phase, MAX_POLLS);
+    phase ^= 1u;
+    if (__syncthreads_or(!ok)) { if (tid == 0) record_timeout(); return false; }
+    tc::fence_after_sync();
+    return true;
+  };
+
+  // ---------------- phase A: Z = Wᵀ S[:, block]
+  constexpr uint32_t ID_Z = tc::idesc_bf16(128, N2, false, true);
+  for (int i0 = 0; i0 < D && !failed; i0 += KT) {
+    stage_w<T>(sW, sWl, k, v, item, S, D, t0, nt, bad, i0, tid);
+    for (int e = tid; e < KT * (N2 / 8); e += THR) {
+      const int g = e % (N2 / 8), i = e / (N2 / 8);   // 8 consecutive columns of row i
+      const int col = j0 + (g & 3) * 8;             // g < 4: re, g >= 4: im
+      const int gi = i0 + i;
+      float x[8];
+      if (sr) {
+        const float* p = ((g < 4) ? sr : si) + (size_t)gi * D + col;
+        load8(p, x);
+      } else {
+#pragma unroll
+        for (int jj = 0; jj < 8; ++jj) x[jj] = (g < 4 && gi == col + jj) ? 1.f : 0.f;
+      }
+      uint4 h, l;
+      tc::split8(x, h, l);
+      *reinterpret_cast<uint4*>(sHh + mnmaj(i, g * 8, N2 / 8)) = h;
+      *reinterpret_cast<uint4*>(sHl + mnmaj(i, g * 8, N2 / 8)) = l;
+    }
+    tc::fence_proxy_async();
+    __syncthreads();
+    if (tid == 0) {
+      tc::fence_after_sync();
+      const uint32_t aw = tc::smem_addr(sW), awl = tc::smem_addr(sWl);
+      const uint32_t bh = tc::smem_addr(sHh), bl = tc::smem_addr(sHl);
+#pragma unroll 1
+      for (int ks = 0; ks < KT / 16; ++ks) {
+        const uint64_t a = tc::sdesc(aw + ks * 2 * R2 * 16, R2 * 16, 128);
+        const uint64_t b_hi = tc::sdesc(bh + ks * 2 * (N2 / 8) * 128, (N2 / 8) * 128, 128);
+        const uint64_t b_lo = tc::sdesc(bl + ks * 2 * (N2 / 8) * 128, (N2 / 8) * 128, 128);
+        tc::mma_bf16(tZ, a, b_hi, ID_Z, (i0 > 0 || ks > 0) ? 1u : 0u);
+        tc::mma_bf16(tZ, a, b_lo, ID_Z, 1u);
+        if (F32IN) tc::mma_bf16(tZ, tc::sdesc(awl + ks * 2 * R2 * 16, R2 * 16, 128), b_hi, ID_Z, 1u);
+      }
+      tc::commit(bar);
+    }
+    failed = !wait_mma();
+  }
+
+  // ---------------- phase T: P1 = Tr Z, P2 = Ti Z  (Z split hi/lo, T split hi/lo)
+  if (!failed) {
+    float z[32];
+    tc::tmem_ld16(tZ + lane_base + 32 * half, z);
+    tc::tmem_ld16(tZ + lane_base + 32 * half + 16, z + 16);
+#pragma unroll
+    for (int g = 0; g < 4; ++g) {
+      uint4 h, l;
+      tc::split8(z + 8 * g, h, l);
+      const int off = mnmaj(row, 32 * half + 8 * g, N2 / 8);
+      *reinterpret_cast<uint4*>(sZh + off) = h;
+      *reinterpret_cast<uint4*>(sZl + off) = l;
+    }
+    const uint4* Tin = reinterpret_cast<const uint4*>(Tws + chunk * 4 * T_TILE);
+    for (int e = tid; e < 4 * T_TILE / 16; e += THR) reinterpret_cast<uint4*>(sT)[e] = Tin[e];
+    tc::fence_proxy_async();
+    tc::fence_before_sync();
+    __syncthreads();
+    if (tid == 0) {
+      tc::fence_after_sync();
+      constexpr uint32_t ID_T = tc::idesc_bf16(128, N2, false, true);
+      const uint32_t t_base = tc::smem_addr(sT);
+      const uint32_t zh = tc::smem_addr(sZh), zl = tc::smem_addr(sZl);
+#pragma unroll 1
+      for (int part = 0; part < 2; ++part) {       // 0: Tr -> P1, 1: Ti -> P2
+        const uint32_t th = t_base + (2 * part) * T_TILE, tl = th + T_TILE;
+        const uint32_t td = part ? tP2 : tP1;
+#pragma unroll 1
+        for (int ks = 0; ks < R2 / 16; ++ks) {
+          const uint64_t ah = tc::sdesc(th + ks * 2 * R2 * 16, R2 * 16, 128);
+          const uint64_t al = tc::sdesc(tl + ks * 2 * R2 * 16, R2 * 16, 128);
+          const uint64_t bh = tc::sdesc(zh + ks * 2 * (N2 / 8) * 128, (N2 / 8) * 128, 128);
+          const uint64_t bl = tc::sdesc(zl + ks * 2 * (N2 / 8) * 128, (N2 / 8) * 128, 128);
+          tc::mma_bf16(td, ah, bh, ID_T, ks > 0 ? 1u : 0u);
+          tc::mma_bf16(td, ah, bl, ID_T, 1u);
+          tc::mma_bf16(td, al, bh, ID_T, 1u);
+        }
+      }
+      tc::commit(bar);
+    }
+    failed = !wait_mma();
+  }
+
+  // ---------------- Cm, then E = Re(Cm) Y_block
+  if (!failed) {
+    // this thread: row r = row, complex columns j in [16*half, 16*half + 16)
+    float p1r[16], p1i[16], p2r[16], p2i[16];
+    tc::tmem_ld16(tP1 + lane_base + 16 * half, p1r);
+    tc::tmem_ld16(tP1 + lane_base + 32 + 16 * half, p1i);
+    tc::tmem_ld16(tP2 + lane_base + 16 * half, p2r);
+    tc::tmem_ld16(tP2 + lane_base + 32 + 16 * half, p2i);
+    float cr[16], ci[16];
+#pragma unroll
+    for (int j = 0; j < 16; ++j) { cr[j] = p1r[j] - p2i[j]; ci[j] = p1i[j] + p2r[j]; }
+#pragma unroll
+    for (int g = 0; g < 2; ++g) {
+      uint4 h, l;
+      const int jc = 16 * half + 8 * g;
+      tc::split8(cr + 8 * g, h, l);
+      *reinterpret_cast<uint4*>(sCh + mnmaj(row, jc, N2 / 8)) = h;
+      *reinterpret_cast<uint4*>(sCl + mnmaj(row, jc, N2 / 8)) = l;
+      *reinterpret_cast<uint4*>(sAh + kmaj(row, jc, R2)) = h;
+      *reinterpret_cast<uint4*>(sAl + kmaj(row, jc, R2)) = l;
+      tc::split8(ci + 8 * g, h, l);
+      *reinterpret_cast<uint4*>(sCh + mnmaj(row, NB2 + jc, N2 / 8)) = h;
+      *reinterpret_cast<uint4*>(sCl + mnmaj(row, NB2 + jc, N2 / 8)) = l;
+    }
+    // Y block: B operand (n = token t, k = column j), K-major with 64 rows
+    for (int e = tid; e < C2 * (NB2 / 8); e += THR) {
+      const int t = e % C2, g = e / C2;
+      const bool valid = t < nt;
+      const T* src = q + ((size_t)item * S + t0 + (valid ? t : 0)) * D + j0 + g * 8;
+      stage8(src, valid, sYh + kmaj(t, g * 8, C2), sYl + kmaj(t, g * 8, C2));
+    }
+    tc::fence_proxy_async();
+    tc::fence_before_sync();
+    __syncthreads();
+    if (tid == 0) {
+      tc::fence_after_sync();
+      constexpr uint32_t ID_E = tc::idesc_bf16(128, C2, false, false);
+      const uint32_t ah = tc::smem_addr(sAh), al = tc::smem_addr(sAl);
+      const uint32_t yh = tc::smem_addr(sYh), yl = tc::smem_addr(sYl);
+#pragma unroll 1
+      for (int ks = 0; ks < NB2 / 16; ++ks) {
+        const uint64_t a_h = tc::sdesc(ah + ks * 2 * R2 * 16, R2 * 16, 128);
+        const uint64_t a_l = tc::sdesc(al + ks * 2 * R2 * 16, R2 * 16, 128);
+        const uint64_t b_h = tc::sdesc(yh + ks * 2 * C2 * 16, C2 * 16, 128);
+        tc::mma_bf16(tE, a_h, b_h, ID_E, ks > 0 ? 1u : 0u);
+        tc::mma_bf16(tE, a_l, b_h, ID_E, 1u);
+        if (F32IN) tc::mma_bf16(tE, a_h, tc::sdesc(yl + ks * 2 * C2 * 16, C2 * 16, 128), ID_E, 1u);
+      }
+      tc::commit(bar);
+    }
+    failed = !wait_mma();
+  }
+  if (!failed) {
+    float e[32];
+    tc::tmem_ld16(tE + lane_base + 32 * half, e);
+    tc::tmem_ld16(tE + lane_base + 32 * half + 16, e + 16);
+    float* Eo = Ews + chunk * R2 * C2 + (size_t)row * C2 + 32 * half;
+#pragma unroll
+    for (int t = 0; t < 32; ++t) atomicAdd(Eo + t, e[t]);
+  }
+
+  // ---------------- phase B: S_next[:, block] = S[:, block] + W Cm
+  constexpr uint32_t ID_H = tc::idesc_bf16(128, N2, true, true);
+  for (int i0 = 0; i0 < D && !failed; i0 += KT) {
+    tc::fence_before_sync();
+    __syncthreads();     // previous epilogue's TMEM loads and smem reads are done
+    stage_w<T>(sW, sWl, k, v, item, S, D, t0, nt, bad, i0, tid);
+    tc::fence_proxy_async();
+    __syncthreads();
+    if (tid == 0) {
+      tc::fence_after_sync();
+      const uint32_t aw = tc::smem_addr(sW), awl = tc::smem_addr(sWl);
+      const uint32_t ch = tc::smem_addr(sCh), cl = tc::smem_addr(sCl);
+#pragma unroll 1
+      for (int ks = 0; ks < R2 / 16; ++ks) {
+        // A = W viewed MN-major: M = element index i, K = vector index r
+        const uint64_t a = tc::sdesc(aw + ks * 256, 128, R2 * 16);
+        const uint64_t b_h = tc::sdesc(ch + ks * 2 * (N2 / 8) * 128, (N2 / 8) * 128, 128);
+        const uint64_t b_l = tc::sdesc(cl + ks * 2 * (N2 / 8) * 128, (N2 / 8) * 128, 128);
+        tc::mma_bf16(tDH, a, b_h, ID_H, ks > 0 ? 1u : 0u);
+        tc::mma_bf16(tDH, a, b_l, ID_H, 1u);
+        if (F32IN) tc::mma_bf16(tDH, tc::sdesc(awl + ks * 256, 128, R2 * 16), b_h, ID_H, 1u);
+      }
+      tc::commit(bar);
+    }
+    failed = !wait_mma();
+    if (failed) break;
+    // epilogue: row i0 + row, columns [32*half, 32*half+32) = re (half 0) or im (half 1)
+    float dh[32];
+    tc::tmem_ld16(tDH + lane_base + 32 * half, dh);
+    tc::tmem_ld16(tDH + lane_base + 32 * half + 16, dh + 16);
+    const int gi = i0 + row;
+    const size_t o = soff + (size_t)gi * D + j0;
+    float* dst = (half ? dst_i : dst_r) + o;
+    if (sr) {
+      const float* src = (half ? src_i : src_r) + o;
+#pragma unroll
+      for (int jj = 0; jj < 32; jj += 4) {
+        const float4 a = *reinterpret_cast<const float4*>(src + jj);
+        *reinterpret_cast<float4*>(dst + jj) =
+            make_float4(a.x + dh[jj], a.y + dh[jj + 1], a.z + dh[jj + 2], a.w + dh[jj + 3]);
+      }
+    } else {
+#pragma unroll
+      for (int jj = 0; jj < 32; jj += 4) {
+        float a[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) a[u] = (!half && gi == j0 + jj + u) ? 1.f : 0.f;
+        *reinterpret_cast<float4*>(dst + jj) =
+            make_float4(a[0] + dh[jj], a[1] + dh[jj + 1], a[2] + dh[jj + 2], a[3] + dh[jj + 3]);
+      }
+    }
+  }
+  tc::fence_before_sync();
+  __syncthreads();
+  if (warp == 0) tc::tmem_dealloc(tbase, 512);
+}
+
+// ---------------------------------------------------------------------------------
+// readout: rec[t][i0 + i] = Re(S y_t)_i + sum_r W[i][r] E[r][t] (token block of r <= t)
+// smem: A (S rows, K-major hi/lo 2 x 32K) | Y (K-major, 64 rows, hi/lo 2 x 16K) |
+//       W (32K, + lo 32K for fp32) | E (MN-major hi/lo 2 x 16K) | bar, slot
+constexpr int RD_A = 0, RD_Y = 64 * 1024, RD_W = 96 * 1024, RD_E = 160 * 1024, RD_BAR = 192 * 1024;
+constexpr int READOUT_SMEM = RD_BAR + 64 + SMEM_SLACK;
+
+template <typename T>
+__global__ void __launch_bounds__(THR, 1)
+cham_tc_readout(const T* __restrict__ q, const T* __restrict__ k, const T* __restrict__ v,
+                const float* __restrict__ Ews, const unsigned long long* __restrict__ badws,
+                const float* __restrict__ src_r, T* __restrict__ out, int S, int D, int nch, int c) {
+  extern __shared__ __align__(1024) unsigned char smr[];
+  constexpr bool F32IN = sizeof(T) == 4;
+  unsigned char* sAh = smr + RD_A;
+  unsigned char* sAl = sAh + R2 * KT * 2;
+  unsigned char* sYh = smr + RD_Y;
+  unsigned char* sYl = sYh + C2 * KT * 2;
+  unsigned char* sW = smr + RD_W;
+  unsigned char* sWl = sW + W_TILE;
+  unsigned char* sEh = smr + RD_E;
+  unsigned char* sEl = sEh + R2 * C2 * 2;
+  uint64_t* bar = reinterpret_cast<uint64_t*>(smr + RD_BAR);
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(smr + RD_BAR + 16);
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int item = blockIdx.y, i0 = blockIdx.x * R2;
+  const int t0 = c * C2, nt = min(C2, S - t0);
+  const size_t chunk = (size_t)item * nch + c;
+  const unsigned long long bad = badws[chunk];
+  const float* sr = src_r ? src_r + (size_t)item * D * D : nullptr;
+
+  if (warp == 0) tc::tmem_alloc(tslot, 64);
+  if (tid == 0) { tc::mbar_init(bar, 1); tc::fence_mbar_init(); }
+  tc::fence_before_sync();
+  __syncthreads();
+  tc::fence_after_sync();
+  const uint32_t tO = *tslot;
+  const uint32_t lane_base = (uint32_t)(32 * (warp & 3)) << 16;
+  const int row = 32 * (warp & 3) + lane, half = warp >> 2;
+  uint32_t phase = 0;
+  bool failed = false;
+  auto wait_mma = [&]() -> bool {
+    const bool ok = tc::mbar_wait(bar, phase, MAX_POLLS);
+    phase ^= 1u;
+    if (__syncthreads_or(!ok)) { if (tid == 0) record_timeout(); return false; }
+    tc::fence_after_sync();
+    return true;
+  };
+  constexpr uint32_t ID_O = tc::idesc_bf16(128, C2, false, false);
+
+  // Re(S y_t): A = S rows [i0, i0+128) (K-major over columns j), B = Y (n = t, k = j)
+  for (int j0 = 0; j0 < D && !failed; j0 += KT) {
+    if (j0 > 0) { tc::fence_before_sync(); __syncthreads(); }
+    for (int e = tid; e < R2 * (KT / 8); e += THR) {
+      const int g = e % (KT / 8), i = e / (KT / 8);
+      float x[8];
+      if (sr) load8(sr + (size_t)(i0 + i) * D + j0 + g * 8, x);
+      else {
+#pragma unroll
+        for (int jj = 0; jj < 8; ++jj) x[jj] = (i0 + i == j0 + g * 8 + jj) ? 1.f : 0.f;
+      }
+      uint4 h, l;
+      tc::split8(x, h, l);
+      *reinterpret_cast<uint4*>(sAh + kmaj(i, g * 8, R2)) = h;
+      *reinterpret_cast<uint4*>(sAl + kmaj(i, g * 8, R2)) = l;
+    }
+    for (int e = tid; e < C2 * (KT / 8); e += THR) {
+      const int t = e % C2, g = e / C2;
+      const bool valid = t < nt;
+      const T* src = q + ((size_t)item * S + t0 + (valid ? t : 0)) * D + j0 + g * 8;
+      stage8(src, valid, sYh + kmaj(t, g * 8, C2), sYl + kmaj(t, g * 8, C2));
+    }
+    tc::fence_proxy_async();
+    __syncthreads();
+    if (tid == 0) {
+      tc::fence_after_sync();
+      const uint32_t ah = tc::smem_addr(sAh), al = tc::smem_addr(sAl);
+      const uint32_t yh = tc::smem_addr(sYh), yl = tc::smem_addr(sYl);
+#pragma unroll 1
+      for (int ks = 0; ks < KT / 16; ++ks) {
+        const uint64_t a_h = tc::sdesc(ah + ks * 2 * R2 * 16, R2 * 16, 128);
+        const uint64_t a_l = tc::sdesc(al + ks * 2 * R2 * 16, R2 * 16, 128);
+        const uint64_t b_h = tc::sdesc(yh + ks * 2 * C2 * 16, C2 * 16, 128);
+        tc::mma_bf16(tO, a_h, b_h, ID_O, (j0 > 0 || ks > 0) ? 1u : 0u);
+        tc::mma_bf16(tO, a_l, b_h, ID_O, 1u);
+        if (F32IN) tc::mma_bf16(tO, a_h, tc::sdesc(yl + ks * 2 * C2 * 16, C2 * 16, 128), ID_O, 1u);
+      }
+      tc::commit(bar);
+    }
+    failed = !wait_mma();
+  }
+  // + W E:  A = W rows [i0, i0+128) viewed MN-major (M = i, K = r), B = mask(E) (k = r, n = t)
+  if (!failed) {
+    tc::fence_before_sync();
+    __syncthreads();
+    stage_w<T>(sW, sWl, k, v, item, S, D, t0, nt, bad, i0, tid);
+    const float* Ein = Ews + chunk * R2 * C2;
+    for (int e = tid; e < R2 * (C2 / 8); e += THR) {
+      const int g = e % (C2 / 8), r = e / (C2 / 8);
+      float x[8];
+      load8(Ein + (size_t)r * C2 + g * 8, x);
+#pragma unroll
+      for (int jj = 0; jj < 8; ++jj) if ((r >> 1) > g * 8 + jj) x[jj] = 0.f;
+      uint4 h, l;
+      tc::split8(x, h, l);
+      *reinterpret_cast<uint4*>(sEh + mnmaj(r, g * 8, C2 / 8)) = h;
+      *reinterpret_cast<uint4*>(sEl + mnmaj(r, g * 8, C2 / 8)) = l;
+    }
+    tc::fence_proxy_async();
+    __syncthreads();
+    if (tid == 0) {
+      tc::fence_after_sync();
+      constexpr uint32_t ID_W = tc::idesc_bf16(128, C2, true, true);
+      const uint32_t aw = tc::smem_addr(sW), awl = tc::smem_addr(sWl);
+      const uint32_t eh = tc::smem_addr(sEh), el = tc::smem_addr(sEl);
+#pragma unroll 1
+      for (int ks = 0; ks < R2 / 16; ++ks) {
+        const uint64_t a = tc::sdesc(aw + ks * 256, 128, R2 * 16);
+        const uint64_t b_h = tc::sdesc(eh + ks * 2 * (C2 / 8) * 128, (C2 / 8) * 128, 128);
+        const uint64_t b_l = tc::sdesc(el + ks * 2 * (C2 / 8) * 128, (C2 / 8) * 128, 128);
+        tc::mma_bf16(tO, a, b_h, ID_W, 1u);
+        tc::mma_bf16(tO, a, b_l, ID_W, 1u);
+        if (F32IN) tc::mma_bf16(tO, tc::sdesc(awl + ks * 256, 128, R2 * 16), b_h, ID_W, 1u);
+      }
+      tc::commit(bar);
+    }
+    failed = !wait_mma();
+  }
+  if (!failed) {
+    float o[32];
+    tc::tmem_ld16(tO + lane_base + 32 * half, o);
+    tc::tmem_ld16(tO + lane_base + 32 * half + 16, o + 16);
+#pragma unroll
+    for (int u = 0; u < 32; ++u) {
+      const int t = 32 * half + u;
+      if (t < nt) out[((size_t)item * S + t0 + t) * D + i0 + row] = from_f32<T>(o[u]);
+    }
+  }
+  tc::fence_before_sync();
+  __syncthreads();
+  if (warp == 0) tc::tmem_dealloc(tO, 64);
+}
+
+size_t tc_prep_smem() { return sizeof(float) * (PREP_DT * (R2 + 1) + 3 * R2 * (R2 + 1)); }
+
+template <typename T>
+int launch_cham_tc(const void* q, const void* k, const void* v, const float* gamma,
+                   void* out, float* hr, float* hi, int b, int s, int D, const TcWs& w, cudaStream_t st) {
+  const int nch = (s + C2 - 1) / C2;
+  int rc;
+  const size_t ps = tc_prep_smem();
+  VERACE_CUDA(cudaFuncSetAttribute(cham_tc_prep<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ps));
+  VERACE_CUDA(cudaFuncSetAttribute(cham_tc_colpass<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, COLPASS_SMEM));
+  VERACE_CUDA(cudaFuncSetAttribute(cham_tc_readout<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, READOUT_SMEM));
+  cham_tc_prep<T><<<dim3(nch, b), THR, ps, st>>>((const T*)k, (const T*)v, gamma, w.T, w.E, w.bad, s, D, nch);
+  if ((rc = check_launch("cham_tc_prep"))) return rc;
+  const dim3 gc(D / NB2, b), gr(D / R2, b);
+  const float* cur_r = nullptr;
+  const float* cur_i = nullptr;
+  for (int c = 0; c < nch; ++c) {
+    const bool to_out = ((nch - 1 - c) % 2) == 0;
+    float* dr = to_out ? hr : w.Hre;
+    float* di = to_out ? hi : w.Him;
+    cham_tc_colpass<T><<<gc, THR, COLPASS_SMEM, st>>>((const T*)q, (const T*)k, (const T*)v, w.T, w.E, w.bad,
+                                                      cur_r, cur_i, dr, di, s, D, nch, c);
+    if ((rc = check_launch("cham_tc_colpass"))) return rc;
+    cham_tc_readout<T><<<gr, THR, READOUT_SMEM, st>>>((const T*)q, (const T*)k, (const T*)v, w.E, w.bad,
+                                                      cur_r, (T*)out, s, D, nch, c);
+    if ((rc = check_launch("cham_tc_readout"))) return rc;
+    cur_r = dr;
+    cur_i = di;
+  }
+  return VERACE_OK;
+}
+
+}  // namespace
+
+bool cham_tc_supported(int D, int dtype, bool has_h0) {
+  return !has_h0 && D >= 128 && D % 128 == 0 && (dtype == VERACE_BF16 || dtype == VERACE_F32);
+}
+
+size_t cham_tc_workspace(int b, int s, int D) { return tc_ws_layout(b, s, D, nullptr, nullptr); }
+
+int cham_tc_scan(const void* q, const void* k, const void* v, const float* gamma, void* out,
+                 float* hr, float* hi, int b, int s, int D, int dtype, void* workspace, cudaStream_t st) {
+  TcWs w;
+  char* base = (char*)align_up((size_t)workspace, 256);
+  tc_ws_layout(b, s, D, &w, base);
+  if (dtype == VERACE_BF16)
+    return launch_cham_tc<__nv_bfloat16>(q, k, v, gamma, out, hr, hi, b, s, D, w, st);
+  return launch_cham_tc<float>(q, k, v, gamma, out, hr, hi, b, s, D, w, st);
+}
+
+int tc_read_status(cudaStream_t st, int* status) {
+  int h = 0;
+  VERACE_CUDA(cudaMemcpyFromSymbolAsync(&h, g_tc_status, sizeof(int), 0, cudaMemcpyDeviceToHost, st));
+  VERACE_CUDA(cudaStreamSynchronize(st));
+  if (h) {
+    const int zero = 0;
+    VERACE_CUDA(cudaMemcpyToSymbolAsync(g_tc_status, &zero, sizeof(int), 0, cudaMemcpyHostToDevice, st));
+    VERACE_CUDA(cudaStreamSynchronize(st));
+  }
+  *status = h;
+  return VERACE_OK;
+}
+
+}  // namespace verace
