@@ -41,6 +41,7 @@ size_t cham_tc_workspace(int b, int s, int D);
 int cham_tc_scan(const void* q, const void* k, const void* v, const float* gamma, void* out,
                  float* hr, float* hi, int b, int s, int D, int dtype, void* workspace, cudaStream_t st);
 int tc_read_status(cudaStream_t st, int* status);
+int sssd_tc_read_status(int* status);
 
 namespace {
 
@@ -602,9 +603,12 @@ extern "C" int verace_cham_retract(const float* h_re, const float* h_im, float* 
 }
 
 extern "C" int verace_device_status(void* stream) {
-  int status = 0;
-  const int rc = tc_read_status((cudaStream_t)stream, &status);
+  int status = 0, status2 = 0;
+  int rc = tc_read_status((cudaStream_t)stream, &status);
   if (rc) return rc;
+  rc = sssd_tc_read_status(&status2);
+  if (rc) return rc;
+  status |= status2;
   VERACE_REQUIRE(status == 0, VERACE_ERR_TIMEOUT,
                  "a bounded device-side wait gave up (tensor-core completion never arrived)");
   return VERACE_OK;

@@ -17,9 +17,24 @@
 #include "common.cuh"
 
 #include <mutex>
+#include <stdlib.h>
 
 namespace verace {
+
+// tcgen05 path for head_dim 128 (sssd_tc.cu)
+bool sssd_tc_supported(int d, int dtype);
+size_t sssd_tc_workspace(int b, int s, int h);
+int sssd_tc_scan_launch(const void* q, const void* k, const void* v, const float* delta, const float* psi0,
+                        void* out, float* psi_out, int b, int s, int h, int dtype, void* workspace,
+                        cudaStream_t st);
+
 namespace {
+
+// VERACE_SSSD_SIMT=1 forces the fp32 SIMT kernels (used to compare the two paths).
+bool sssd_force_simt() {
+  const char* e = getenv("VERACE_SSSD_SIMT");
+  return e && e[0] && e[0] != '0';
+}
 
 constexpr int SC = 32;       // tokens per chunk
 constexpr int SR = 2 * SC;   // rank of a chunk transform
@@ -257,12 +272,24 @@ int launch_sssd(const void* q, const void* k, const void* v, const float* delta,
 
 using namespace verace;
 
-extern "C" size_t verace_sssd_scan_workspace(int b, int s, int h, int d) {
-  (void)d;
-  if (b <= 0 || s <= 0 || h <= 0) return 256;
+namespace verace {
+namespace {
+size_t simt_workspace(int b, int s, int h) {
   const size_t chains = (size_t)b * h;
   const size_t nch = ((size_t)s + SC - 1) / SC;
   return align_up(sssd_t_bytes(chains, nch), 256) + align_up(chains * nch * sizeof(unsigned long long), 256);
+}
+}  // namespace
+}  // namespace verace
+
+extern "C" size_t verace_sssd_scan_workspace(int b, int s, int h, int d) {
+  if (b <= 0 || s <= 0 || h <= 0) return 256;
+  size_t n = simt_workspace(b, s, h);
+  if (d == 128) {
+    const size_t t = sssd_tc_workspace(b, s, h);
+    if (t > n) n = t;
+  }
+  return n;
 }
 
 extern "C" int verace_sssd_scan(const void* q, const void* k, const void* v, const float* delta,
@@ -285,10 +312,12 @@ extern "C" int verace_sssd_scan(const void* q, const void* k, const void* v, con
                  workspace ? workspace_bytes : (size_t)0);
   const size_t chains = (size_t)b * h;
   const size_t nch = ((size_t)s + SC - 1) / SC;
+  cudaStream_t st = (cudaStream_t)stream;
+  if (s > 0 && sssd_tc_supported(d, dtype) && !sssd_force_simt())
+    return sssd_tc_scan_launch(q, k, v, delta, psi0, out, psi_out, b, s, h, dtype, workspace, st);
   float* Tws = (float*)workspace;
   unsigned long long* badws =
       (unsigned long long*)((char*)workspace + align_up(sssd_t_bytes(chains, nch), 256));
-  cudaStream_t st = (cudaStream_t)stream;
   switch (dtype) {
     case VERACE_F32: return launch_sssd<float>(q, k, v, delta, psi0, out, psi_out, b, s, h, d, Tws, badws, st);
     case VERACE_BF16: return launch_sssd<__nv_bfloat16>(q, k, v, delta, psi0, out, psi_out, b, s, h, d, Tws, badws, st);
@@ -348,7 +377,7 @@ extern "C" int verace_sssd_scan_noalloc(const void* q, const void* k, const void
   VERACE_REQUIRE(psi_out != nullptr, VERACE_ERR_INVALID, "verace_sssd_scan_noalloc: psi_out is NULL");
   VERACE_REQUIRE(s == 0 || (q && k && v && delta && out), VERACE_ERR_INVALID,
                  "verace_sssd_scan_noalloc: NULL input/output pointer");
-  const size_t need = s > 0 ? verace_sssd_scan_workspace(b, s, h, d) : 0;
+  const size_t need = s > 0 ? simt_workspace(b, s, h) : 0;
   VERACE_REQUIRE(need <= SSSD_NOALLOC_SCRATCH_BYTES, VERACE_ERR_UNSUPPORTED,
                  "verace_sssd_scan_noalloc: this size needs %zu bytes of scratch, more than the "
                  "fixed %zu-byte device array; use verace_sssd_scan with a workspace",

@@ -1,0 +1,466 @@
+// SSSD scan on the tcgen05 tensor cores (sm_100a) for head_dim 128: one CTA per
+// (batch, head) chain with the 128x128 fp32 state resident in tensor memory for the
+// whole sequence.
+//
+// Same chunked compact-WY recurrence as sssd_scan.cu (derivation there), with chunks of
+// C = 64 tokens (chunk rank 128 = one tensor-core tile).  Per chunk, starting from S:
+//     Z = Wᵀ S,  Y = S Q,  Cm = T Z,  E = mask(Cm Q),  S += W Cm,  O = Y + W E
+// Every product runs as tcgen05.mma (kind::f16) with fp32 accumulation in TMEM; fp32
+// operands (the state, Z, Cm, E, T, and fp32 inputs) enter as bf16 hi + lo pairs and
+// products take hi*hi + hi*lo + lo*hi.  The state update accumulates straight into
+// the TMEM copy of S, which is read back to global memory only after the last chunk.
+// T for every chunk comes from sssd_tc_prep (all chunks in parallel, fp32 SIMT).
+#include "common.cuh"
+#include "tc.cuh"
+
+namespace verace {
+namespace {
+
+constexpr int C3 = 64;     // tokens per chunk
+constexpr int R3 = 128;    // chunk rank
+constexpr int HD = 128;    // head_dim handled by this path
+constexpr int THR3 = 256;
+constexpr uint32_t POLLS3 = 1u << 22;
+constexpr int TILE3 = 128 * 128 * 2;  // 32 KB bf16 128 x 128
+
+__device__ int g_sssd_tc_status = 0;
+
+__device__ __forceinline__ int kmaj3(int r, int k, int R) { return ((k >> 3) * R + r) * 16 + (k & 7) * 2; }
+// 128 x 128 "X" layout: element (i, j) at (j/8)*2048 + (i/8)*128 + (i%8)*16 + (j%8)*2
+//   K-major view (rows i, k = j): SBO 128, LBO 2048, K step of 16 -> +4096
+//   MN-major view (n = j, k = i): SBO 2048, LBO 128, K step of 16 -> +256
+__device__ __forceinline__ int xoff(int i, int j) { return kmaj3(i, j, 128); }
+__device__ __forceinline__ int mnmaj3(int k, int n, int NG) { return (((k >> 3) * NG + (n >> 3)) * 128) + (k & 7) * 16 + (n & 7) * 2; }
+
+template <typename T>
+__device__ __forceinline__ void stage8_3(const T* src, bool valid, unsigned char* hi, unsigned char* lo) {
+  if (sizeof(T) == 2) {
+    uint4 u = make_uint4(0, 0, 0, 0);
+    if (valid) u = *reinterpret_cast<const uint4*>(src);
+    *reinterpret_cast<uint4*>(hi) = u;
+  } else {
+    float x[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    if (valid) {
+      const float4 a = *reinterpret_cast<const float4*>(src);
+      const float4 b = *reinterpret_cast<const float4*>(reinterpret_cast<const float*>(src) + 4);
+      x[0] = a.x; x[1] = a.y; x[2] = a.z; x[3] = a.w; x[4] = b.x; x[5] = b.y; x[6] = b.z; x[7] = b.w;
+    }
+    uint4 h, l;
+    tc::split8(x, h, l);
+    *reinterpret_cast<uint4*>(hi) = h;
+    *reinterpret_cast<uint4*>(lo) = l;
+  }
+}
+
+// ---------------------------------------------------------------------------------
+// prep: Gram, M_t, T (fp32 SIMT), T written as bf16 hi/lo K-major 128x128 tiles.
+// smem: Ws [128][129] | Gs [128][129] | Ts [128][129]
+template <typename T>
+__global__ void __launch_bounds__(THR3)
+sssd_tc_prep(const T* __restrict__ k, const T* __restrict__ v, const float* __restrict__ delta,
+             unsigned char* __restrict__ Tws, unsigned long long* __restrict__ badws, int S, int H, int nch) {
+  extern __shared__ float sm3[];
+  constexpr int P = R3 + 1;
+  float* Ws = sm3;
+  float* Gs = Ws + HD * P;
+  float* Ts = Gs + R3 * P;
+  __shared__ float Ms[C3 * 4];
+  __shared__ unsigned long long bad_bits;
+  const int c = blockIdx.x, chain = blockIdx.y, tid = threadIdx.x;
+  const int bi = chain / H, hi = chain % H;
+  const int t0 = c * C3, nt = min(C3, S - t0);
+  if (tid == 0) bad_bits = 0ull;
+  __syncthreads();
+  for (int e = tid; e < HD * R3; e += THR3) {
+    const int r = e % R3, i = e / R3, tau = r >> 1;
+    float val = 0.f;
+    if (tau < nt) {
+      const size_t off = ((size_t)(bi * (size_t)S + t0 + tau) * H + hi) * HD + i;
+      val = to_f32((r & 1) ? v[off] : k[off]);
+    }
+    Ws[i * P + r] = val;
+    if (!isfinite(val)) atomicOr(&bad_bits, 1ull << tau);
+  }
+  __syncthreads();
+  if (tid < C3 && tid < nt && !isfinite(delta[(size_t)(bi * (size_t)S + t0 + tid) * H + hi]))
+    atomicOr(&bad_bits, 1ull << tid);
+  __syncthreads();
+  if (bad_bits) {
+    for (int e = tid; e < HD * R3; e += THR3)
+      if ((bad_bits >> ((e % R3) >> 1)) & 1ull) Ws[(e / R3) * P + e % R3] = 0.f;
+    __syncthreads();
+  }
+  smem_gemm<4, 4, false>(R3, R3, HD, Ws, 1, P, Ws, P, 1, Gs, P, 1, tid, THR3);
+  __syncthreads();
+  if (tid < C3) {
+    const int tau = tid;
+    float m00 = 0.f, m01 = 0.f, m10 = 0.f, m11 = 0.f;
+    bool flagged = (bad_bits >> tau) & 1ull;
+    if (tau < nt && !flagged) {
+      const float kk = Gs[(2 * tau) * P + 2 * tau];
+      const float vv = Gs[(2 * tau + 1) * P + 2 * tau + 1];
+      const float kv = Gs[(2 * tau) * P + 2 * tau + 1];
+      const float a = 0.5f * delta[(size_t)(bi * (size_t)S + t0 + tau) * H + hi];
+      const float det = 1.f + a * a * (kk * vv - kv * kv);
+      const float f = -2.f * a / det;
+      m00 = f * (a * vv); m01 = f * (1.f - a * kv);
+      m10 = f * (-1.f - a * kv); m11 = f * (a * kk);
+      if (!(isfinite(kk) && isfinite(vv) && isfinite(kv) && isfinite(m00) && isfinite(m01) &&
+            isfinite(m10) && isfinite(m11))) {
+        m00 = m01 = m10 = m11 = 0.f;
+        atomicOr(&bad_bits, 1ull << tau);
+        flagged = true;
+      }
+    }
+    if (flagged) {
+      for (int r = 0; r < R3; ++r) {
+        Gs[(2 * tau) * P + r] = 0.f; Gs[(2 * tau + 1) * P + r] = 0.f;
+        Gs[r * P + 2 * tau] = 0.f; Gs[r * P + 2 * tau + 1] = 0.f;
+      }
+    }
+    Ms[tau * 4 + 0] = m00; Ms[tau * 4 + 1] = m01; Ms[tau * 4 + 2] = m10; Ms[tau * 4 + 3] = m11;
+  }
+  __syncthreads();
+  if (tid < R3) {
+    const int sg = tid, blk = sg >> 1;
+    for (int r = 0; r < 2 * blk; ++r) Ts[r * P + sg] = 0.f;
+    for (int t = blk; t < C3; ++t) {
+      float x0 = (sg == 2 * t) ? 1.f : 0.f;
+      float x1 = (sg == 2 * t + 1) ? 1.f : 0.f;
+      for (int tp = blk; tp < t; ++tp) {
+        const float a0 = Ts[(2 * tp) * P + sg], a1 = Ts[(2 * tp + 1) * P + sg];
+        x0 += Gs[(2 * t) * P + 2 * tp] * a0 + Gs[(2 * t) * P + 2 * tp + 1] * a1;
+        x1 += Gs[(2 * t + 1) * P + 2 * tp] * a0 + Gs[(2 * t + 1) * P + 2 * tp + 1] * a1;
+      }
+      Ts[(2 * t) * P + sg] = Ms[t * 4 + 0] * x0 + Ms[t * 4 + 1] * x1;
+      Ts[(2 * t + 1) * P + sg] = Ms[t * 4 + 2] * x0 + Ms[t * 4 + 3] * x1;
+    }
+  }
+  __syncthreads();
+  const size_t chunk = (size_t)chain * nch + c;
+  unsigned char* To = Tws + chunk * 2 * TILE3;
+  for (int e = tid; e < R3 * (R3 / 8); e += THR3) {
+    const int r = e % R3, g = e / R3;
+    float x[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) x[j] = Ts[r * P + g * 8 + j];
+    uint4 h, l;
+    tc::split8(x, h, l);
+    *reinterpret_cast<uint4*>(To + kmaj3(r, g * 8, R3)) = h;
+    *reinterpret_cast<uint4*>(To + TILE3 + kmaj3(r, g * 8, R3)) = l;
+  }
+  if (tid == 0) badws[chunk] = bad_bits;
+}
+
+// ---------------------------------------------------------------------------------
+// scan.  smem (bytes): W hi [0,32K) | W lo [32K,64K) | Q hi [64K,80K) | Q lo [80K,96K) |
+//   T hi/lo [96K,160K) (later: E as an MN-major B operand, hi/lo 2 x 16K) |
+//   X hi/lo [160K,224K): S, then Z, then Cm, as bf16 pairs in the "X" layout | bar
+// TMEM columns: S [0,128) Z [128,256) Cm [256,384) Y/O [384,448) E [448,512)
+constexpr int X_W = 0, X_WL = 32 * 1024, X_Q = 64 * 1024, X_QL = 80 * 1024, X_T = 96 * 1024;
+constexpr int X_X = 160 * 1024, X_BAR = 224 * 1024;
+constexpr int SSSD_TC_SMEM = X_BAR + 64;
+
+template <typename T>
+__global__ void __launch_bounds__(THR3, 1)
+sssd_tc_scan(const T* __restrict__ q, const T* __restrict__ k, const T* __restrict__ v,
+             const float* __restrict__ psi0, T* __restrict__ out, float* __restrict__ psi_out,
+             const unsigned char* __restrict__ Tws, const unsigned long long* __restrict__ badws,
+             int S, int H, int nch) {
+  extern __shared__ __align__(1024) unsigned char sx[];
+  constexpr bool F32IN = sizeof(T) == 4;
+  unsigned char* sW = sx + X_W;
+  unsigned char* sWl = sx + X_WL;
+  unsigned char* sQ = sx + X_Q;
+  unsigned char* sQl = sx + X_QL;
+  unsigned char* sT = sx + X_T;
+  unsigned char* sEh = sx + X_T;
+  unsigned char* sEl = sx + X_T + 16 * 1024;
+  unsigned char* sXh = sx + X_X;
+  unsigned char* sXl = sx + X_X + TILE3;
+  uint64_t* bar = reinterpret_cast<uint64_t*>(sx + X_BAR);
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(sx + X_BAR + 16);
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int chain = blockIdx.x, bi = chain / H, hi = chain % H;
+  if (warp == 0) tc::tmem_alloc(tslot, 512);
+  if (tid == 0) { tc::mbar_init(bar, 1); tc::fence_mbar_init(); }
+  tc::fence_before_sync();
+  __syncthreads();
+  tc::fence_after_sync();
+  const uint32_t tb = *tslot;
+  const uint32_t tS = tb, tZ = tb + 128, tC = tb + 256, tO = tb + 384, tE = tb + 448;
+  const uint32_t lb = (uint32_t)(32 * (warp & 3)) << 16;
+  const int row = 32 * (warp & 3) + lane, half = warp >> 2;
+  uint32_t phase = 0;
+  bool failed = false;
+  auto wait_mma = [&]() -> bool {
+    const bool ok = tc::mbar_wait(bar, phase, POLLS3);
+    phase ^= 1u;
+    if (__syncthreads_or(!ok)) { if (tid == 0) atomicExch(&g_sssd_tc_status, 1); return false; }
+    tc::fence_after_sync();
+    return true;
+  };
+  // this thread's 64 columns [64*half, 64*half+64) of a 128-column TMEM matrix -> X layout
+  auto tmem_to_x = [&](uint32_t tm) {
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      float x[16];
+      tc::tmem_ld16(tm + lb + 64 * half + 16 * u, x);
+#pragma unroll
+      for (int g = 0; g < 2; ++g) {
+        uint4 h, l;
+        tc::split8(x + 8 * g, h, l);
+        const int off = xoff(row, 64 * half + 16 * u + 8 * g);
+        *reinterpret_cast<uint4*>(sXh + off) = h;
+        *reinterpret_cast<uint4*>(sXl + off) = l;
+      }
+    }
+  };
+
+  {  // initial state into TMEM
+    const float* p0 = psi0 ? psi0 + (size_t)chain * HD * HD + (size_t)row * HD : nullptr;
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      float x[16];
+#pragma unroll
+      for (int jj = 0; jj < 16; ++jj) {
+        const int j = 64 * half + 16 * u + jj;
+        x[jj] = p0 ? p0[j] : (row == j ? 1.f : 0.f);
+      }
+      tc::tmem_st16(tS + lb + 64 * half + 16 * u, x);
+    }
+  }
+
+  constexpr uint32_t ID_Z = tc::idesc_bf16(128, 128, false, true);
+  constexpr uint32_t ID_Y = tc::idesc_bf16(128, 64, false, false);
+  constexpr uint32_t ID_C = tc::idesc_bf16(128, 128, false, true);
+  constexpr uint32_t ID_E = tc::idesc_bf16(128, 64, false, false);
+  constexpr uint32_t ID_S = tc::idesc_bf16(128, 128, true, true);
+  constexpr uint32_t ID_O = tc::idesc_bf16(128, 64, true, true);
+
+  for (int c = 0; c < nch && !failed; ++c) {
+    const int t0 = c * C3, nt = min(C3, S - t0);
+    const size_t chunk = (size_t)chain * nch + c;
+    const unsigned long long bad = badws[chunk];
+    // ---- stage W (rows = vector r), Q (rows = token t), T (hi | lo)
+    for (int e = tid; e < R3 * (HD / 8); e += THR3) {
+      const int r = e % R3, g = e / R3, tau = r >> 1;
+      const bool valid = tau < nt && !((bad >> tau) & 1ull);
+      const T* src = ((r & 1) ? v : k) + ((size_t)(bi * (size_t)S + t0 + (valid ? tau : 0)) * H + hi) * HD + g * 8;
+      stage8_3(src, valid, sW + kmaj3(r, g * 8, R3), sWl + kmaj3(r, g * 8, R3));
+    }
+    for (int e = tid; e < C3 * (HD / 8); e += THR3) {
+      const int t = e % C3, g = e / C3;
+      const bool valid = t < nt;
+      const T* src = q + ((size_t)(bi * (size_t)S + t0 + (valid ? t : 0)) * H + hi) * HD + g * 8;
+      stage8_3(src, valid, sQ + kmaj3(t, g * 8, C3), sQl + kmaj3(t, g * 8, C3));
+    }
+    {
+      const uint4* Tin = reinterpret_cast<const uint4*>(Tws + chunk * 2 * TILE3);
+      for (int e = tid; e < 2 * TILE3 / 16; e += THR3) reinterpret_cast<uint4*>(sT)[e] = Tin[e];
+    }
+    tmem_to_x(tS);
+    tc::fence_proxy_async();
+    tc::fence_before_sync();
+    __syncthreads();
+    // ---- Z = Wᵀ S  and  Y = S Q
+    if (tid == 0) {
+      tc::fence_after_sync();
+      const uint32_t w = tc::smem_addr(sW), wl = tc::smem_addr(sWl);
+      const uint32_t xh = tc::smem_addr(sXh), xl = tc::smem_addr(sXl);
+      const uint32_t qh = tc::smem_addr(sQ), ql = tc::smem_addr(sQl);
+#pragma unroll 1
+      for (int ks = 0; ks < 8; ++ks) {
+        const uint64_t a_w = tc::sdesc(w + ks * 4096, 2048, 128);
+        const uint64_t b_sh = tc::sdesc(xh + ks * 256, 128, 2048);
+        const uint64_t b_sl = tc::sdesc(xl + ks * 256, 128, 2048);
+        tc::mma_bf16(tZ, a_w, b_sh, ID_Z, ks > 0 ? 1u : 0u);
+        tc::mma_bf16(tZ, a_w, b_sl, ID_Z, 1u);
+        if (F32IN) tc::mma_bf16(tZ, tc::sdesc(wl + ks * 4096, 2048, 128), b_sh, ID_Z, 1u);
+        const uint64_t a_sh = tc::sdesc(xh + ks * 4096, 2048, 128);
+        const uint64_t a_sl = tc::sdesc(xl + ks * 4096, 2048, 128);
+        const uint64_t b_q = tc::sdesc(qh + ks * 2048, 1024, 128);
+        tc::mma_bf16(tO, a_sh, b_q, ID_Y, ks > 0 ? 1u : 0u);
+        tc::mma_bf16(tO, a_sl, b_q, ID_Y, 1u);
+        if (F32IN) tc::mma_bf16(tO, a_sh, tc::sdesc(ql + ks * 2048, 1024, 128), ID_Y, 1u);
+      }
+      tc::commit(bar);
+    }
+    if (!(failed = !wait_mma())) {
+      // ---- Cm = T Z
+      tmem_to_x(tZ);
+      tc::fence_proxy_async();
+      tc::fence_before_sync();
+      __syncthreads();
+      if (tid == 0) {
+        tc::fence_after_sync();
+        const uint32_t th = tc::smem_addr(sT), tl = th + TILE3;
+        const uint32_t xh = tc::smem_addr(sXh), xl = tc::smem_addr(sXl);
+#pragma unroll 1
+        for (int ks = 0; ks < 8; ++ks) {
+          const uint64_t ah = tc::sdesc(th + ks * 4096, 2048, 128);
+          const uint64_t al = tc::sdesc(tl + ks * 4096, 2048, 128);
+          const uint64_t bh = tc::sdesc(xh + ks * 256, 128, 2048);
+          const uint64_t bl = tc::sdesc(xl + ks * 256, 128, 2048);
+          tc::mma_bf16(tC, ah, bh, ID_C, ks > 0 ? 1u : 0u);
+          tc::mma_bf16(tC, ah, bl, ID_C, 1u);
+          tc::mma_bf16(tC, al, bh, ID_C, 1u);
+        }
+        tc::commit(bar);
+      }
+      failed = !wait_mma();
+    }
+    if (!failed) {
+      // ---- E = Cm Q ; S += W Cm
+      tmem_to_x(tC);
+      tc::fence_proxy_async();
+      tc::fence_before_sync();
+      __syncthreads();
+      if (tid == 0) {
+        tc::fence_after_sync();
+        const uint32_t w = tc::smem_addr(sW), wl = tc::smem_addr(sWl);
+        const uint32_t xh = tc::smem_addr(sXh), xl = tc::smem_addr(sXl);
+        const uint32_t qh = tc::smem_addr(sQ), ql = tc::smem_addr(sQl);
+#pragma unroll 1
+        for (int ks = 0; ks < 8; ++ks) {
+          const uint64_t a_ch = tc::sdesc(xh + ks * 4096, 2048, 128);
+          const uint64_t a_cl = tc::sdesc(xl + ks * 4096, 2048, 128);
+          const uint64_t b_q = tc::sdesc(qh + ks * 2048, 1024, 128);
+          tc::mma_bf16(tE, a_ch, b_q, ID_E, ks > 0 ? 1u : 0u);
+          tc::mma_bf16(tE, a_cl, b_q, ID_E, 1u);
+          if (F32IN) tc::mma_bf16(tE, a_ch, tc::sdesc(ql + ks * 2048, 1024, 128), ID_E, 1u);
+          const uint64_t a_w = tc::sdesc(w + ks * 256, 128, 2048);
+          const uint64_t b_ch = tc::sdesc(xh + ks * 256, 128, 2048);
+          const uint64_t b_cl = tc::sdesc(xl + ks * 256, 128, 2048);
+          tc::mma_bf16(tS, a_w, b_ch, ID_S, 1u);
+          tc::mma_bf16(tS, a_w, b_cl, ID_S, 1u);
+          if (F32IN) tc::mma_bf16(tS, tc::sdesc(wl + ks * 256, 128, 2048), b_ch, ID_S, 1u);
+        }
+        tc::commit(bar);
+      }
+      failed = !wait_mma();
+    }
+    if (!failed) {
+      // ---- O = Y + W mask(E)
+      {
+        float e[32];
+        tc::tmem_ld16(tE + lb + 32 * half, e);
+        tc::tmem_ld16(tE + lb + 32 * half + 16, e + 16);
+#pragma unroll
+        for (int g = 0; g < 4; ++g) {
+          float x[8];
+#pragma unroll
+          for (int jj = 0; jj < 8; ++jj) {
+            const int t = 32 * half + 8 * g + jj;
+            x[jj] = ((row >> 1) <= t) ? e[8 * g + jj] : 0.f;
+          }
+          uint4 h, l;
+          tc::split8(x, h, l);
+          const int off = mnmaj3(row, 32 * half + 8 * g, C3 / 8);
+          *reinterpret_cast<uint4*>(sEh + off) = h;
+          *reinterpret_cast<uint4*>(sEl + off) = l;
+        }
+      }
+      tc::fence_proxy_async();
+      tc::fence_before_sync();
+      __syncthreads();
+      if (tid == 0) {
+        tc::fence_after_sync();
+        const uint32_t w = tc::smem_addr(sW), wl = tc::smem_addr(sWl);
+        const uint32_t eh = tc::smem_addr(sEh), el = tc::smem_addr(sEl);
+#pragma unroll 1
+        for (int ks = 0; ks < 8; ++ks) {
+          const uint64_t a_w = tc::sdesc(w + ks * 256, 128, 2048);
+          const uint64_t b_eh = tc::sdesc(eh + ks * 2048, 1024, 128);
+          const uint64_t b_el = tc::sdesc(el + ks * 2048, 1024, 128);
+          tc::mma_bf16(tO, a_w, b_eh, ID_O, 1u);
+          tc::mma_bf16(tO, a_w, b_el, ID_O, 1u);
+          if (F32IN) tc::mma_bf16(tO, tc::sdesc(wl + ks * 256, 128, 2048), b_eh, ID_O, 1u);
+        }
+        tc::commit(bar);
+      }
+      failed = !wait_mma();
+    }
+    if (!failed) {
+      float o[32];
+      tc::tmem_ld16(tO + lb + 32 * half, o);
+      tc::tmem_ld16(tO + lb + 32 * half + 16, o + 16);
+#pragma unroll 4
+      for (int u = 0; u < 32; ++u) {
+        const int t = 32 * half + u;
+        if (t < nt) out[((size_t)(bi * (size_t)S + t0 + t) * H + hi) * HD + row] = from_f32<T>(o[u]);
+      }
+      tc::fence_before_sync();
+      __syncthreads();
+    }
+  }
+  if (!failed) {
+    float* po = psi_out + (size_t)chain * HD * HD + (size_t)row * HD;
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      float x[16];
+      tc::tmem_ld16(tS + lb + 64 * half + 16 * u, x);
+#pragma unroll
+      for (int jj = 0; jj < 16; jj += 4)
+        *reinterpret_cast<float4*>(po + 64 * half + 16 * u + jj) = make_float4(x[jj], x[jj + 1], x[jj + 2], x[jj + 3]);
+    }
+  }
+  tc::fence_before_sync();
+  __syncthreads();
+  if (warp == 0) tc::tmem_dealloc(tb, 512);
+}
+
+size_t sssd_tc_prep_smem() { return sizeof(float) * (HD * (R3 + 1) + 2 * R3 * (R3 + 1)); }
+
+template <typename T>
+int launch_sssd_tc(const void* q, const void* k, const void* v, const float* delta, const float* psi0,
+                   void* out, float* psi_out, int b, int s, int h, unsigned char* Tws,
+                   unsigned long long* badws, cudaStream_t st) {
+  const int chains = b * h;
+  const int nch = (s + C3 - 1) / C3;
+  int rc;
+  if (nch > 0) {
+    const size_t ps = sssd_tc_prep_smem();
+    VERACE_CUDA(cudaFuncSetAttribute(sssd_tc_prep<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ps));
+    sssd_tc_prep<T><<<dim3(nch, chains), THR3, ps, st>>>((const T*)k, (const T*)v, delta, Tws, badws, s, h, nch);
+    if ((rc = check_launch("sssd_tc_prep"))) return rc;
+  }
+  VERACE_CUDA(cudaFuncSetAttribute(sssd_tc_scan<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, SSSD_TC_SMEM));
+  sssd_tc_scan<T><<<chains, THR3, SSSD_TC_SMEM, st>>>((const T*)q, (const T*)k, (const T*)v, psi0, (T*)out,
+                                                     psi_out, Tws, badws, s, h, nch);
+  return check_launch("sssd_tc_scan");
+}
+
+}  // namespace
+
+bool sssd_tc_supported(int d, int dtype) { return d == HD && (dtype == VERACE_BF16 || dtype == VERACE_F32); }
+
+size_t sssd_tc_workspace(int b, int s, int h) {
+  const size_t chains = (size_t)b * h, nch = ((size_t)s + C3 - 1) / C3;
+  return align_up(chains * nch * 2 * TILE3, 256) + align_up(chains * nch * sizeof(unsigned long long), 256) + 256;
+}
+
+int sssd_tc_scan_launch(const void* q, const void* k, const void* v, const float* delta, const float* psi0,
+                        void* out, float* psi_out, int b, int s, int h, int dtype, void* workspace,
+                        cudaStream_t st) {
+  const size_t chains = (size_t)b * h, nch = ((size_t)s + C3 - 1) / C3;
+  unsigned char* Tws = (unsigned char*)align_up((size_t)workspace, 256);
+  unsigned long long* badws = (unsigned long long*)(Tws + align_up(chains * nch * 2 * TILE3, 256));
+  if (dtype == VERACE_BF16)
+    return launch_sssd_tc<__nv_bfloat16>(q, k, v, delta, psi0, out, psi_out, b, s, h, Tws, badws, st);
+  return launch_sssd_tc<float>(q, k, v, delta, psi0, out, psi_out, b, s, h, Tws, badws, st);
+}
+
+int sssd_tc_read_status(int* status) {
+  int h = 0;
+  VERACE_CUDA(cudaMemcpyFromSymbol(&h, g_sssd_tc_status, sizeof(int)));
+  if (h) {
+    const int zero = 0;
+    VERACE_CUDA(cudaMemcpyToSymbol(g_sssd_tc_status, &zero, sizeof(int)));
+  }
+  *status = h;
+  return VERACE_OK;
+}
+
+}  // namespace verace
