@@ -242,21 +242,21 @@ cham_tc_prep(const T* __restrict__ k, const T* __restrict__ v, const float* __re
 }
 
 // ---------------------------------------------------------------------------------
-// colpass.  Shared memory (bytes):
-//   U   [0, 128K)     phase A/B: W hi (32K) | H hi (16K) | H lo (16K) | W lo (32K, fp32 inputs)
-//                     phase T:   Tr hi | Tr lo | Ti hi | Ti lo (4 x 32K)
-//   Zs  [128K, 160K)  Z as the B operand of T Z (MN-major, hi 16K | lo 16K)
-//   Cs  [160K, 192K)  Cm as the B operand of W Cm (MN-major, hi 16K | lo 16K)
-//   Ca  [192K, 208K)  Re(Cm) as the A operand of E (K-major, hi 8K | lo 8K)
-//   Ys  [208K, 216K)  Y block as the B operand of E (K-major, hi 4K | lo 4K)
-//   bar, tmem slot
-// TMEM columns: Z [0,64) P1 [64,128) P2 [128,192) E [192,256) dH [256,320)
-constexpr int SM_U = 0, SM_Z = 128 * 1024, SM_C = 160 * 1024, SM_CA = 192 * 1024, SM_Y = 208 * 1024;
-constexpr int SM_BAR = 216 * 1024;
-// 8 KB of slack after the last operand tile keeps every tensor-core read of a tile's
-// descriptor footprint inside the allocation.
-constexpr int SMEM_SLACK = 8 * 1024;
-constexpr int COLPASS_SMEM = SM_BAR + 64 + SMEM_SLACK;
+// colpass.  Shared memory (bytes), bf16 inputs (two-stage pipeline over the K tiles):
+//   U [0,128K)     phases A/B: stage s at s*64K = W (32K) | H hi (16K) | H lo (16K)
+//                  phase T:    Tr hi | Tr lo | Ti hi | Ti lo (4 x 32K)
+//                  phase E:    Re(Cm) as the A operand (hi 8K | lo 8K) | Y block (4K)
+//   Zs [128K,160K) Z as the B operand of T Z (MN-major, hi 16K | lo 16K)
+//   Cs [160K,192K) Cm as the B operand of W Cm (MN-major, hi 16K | lo 16K)
+//   barriers, TMEM slot
+// fp32 inputs need the lo halves of W and Y as well and run single-buffered:
+//   U [0,128K) = W hi | H hi | H lo | W lo; Ca at 192K, Y at 208K (hi | lo).
+// TMEM columns: Z [0,64) P1 [64,128) P2 [128,192) E [192,256) dH0 [256,320) dH1 [320,384)
+constexpr int SM_Z = 128 * 1024, SM_C = 160 * 1024;
+constexpr int SM_CA_F32 = 192 * 1024, SM_Y_F32 = 208 * 1024;
+constexpr int SM_BAR_BF16 = 192 * 1024, SM_BAR_F32 = 216 * 1024;
+constexpr int STAGE = 64 * 1024;
+constexpr int colpass_smem(bool f32) { return (f32 ? SM_BAR_F32 : SM_BAR_BF16) + 128; }
 
 template <typename T>
 __global__ void __launch_bounds__(THR, 1)
@@ -267,21 +267,21 @@ cham_tc_colpass(const T* __restrict__ q, const T* __restrict__ k, const T* __res
                 float* __restrict__ dst_r, float* __restrict__ dst_i, int S, int D, int nch, int c) {
   extern __shared__ __align__(1024) unsigned char smc[];
   constexpr bool F32IN = sizeof(T) == 4;
-  unsigned char* sW = smc + SM_U;
-  unsigned char* sHh = smc + SM_U + W_TILE;
-  unsigned char* sHl = sHh + H_TILE;
-  unsigned char* sWl = sHl + H_TILE;
-  unsigned char* sT = smc + SM_U;
+  unsigned char* sT = smc;
   unsigned char* sZh = smc + SM_Z;
   unsigned char* sZl = sZh + Z_TILE;
   unsigned char* sCh = smc + SM_C;
   unsigned char* sCl = sCh + Z_TILE;
-  unsigned char* sAh = smc + SM_CA;
+  unsigned char* sAh = F32IN ? smc + SM_CA_F32 : smc;
   unsigned char* sAl = sAh + CA_TILE;
-  unsigned char* sYh = smc + SM_Y;
+  unsigned char* sYh = F32IN ? smc + SM_Y_F32 : smc + 2 * CA_TILE;
   unsigned char* sYl = sYh + Y_TILE;
-  uint64_t* bar = reinterpret_cast<uint64_t*>(smc + SM_BAR);
-  uint32_t* tslot = reinterpret_cast<uint32_t*>(smc + SM_BAR + 16);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smc + (F32IN ? SM_BAR_F32 : SM_BAR_BF16));
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(bars + 8);
+  // barrier roles: 0,1 = K-tile stages of phases A and B, 2 = single-shot phases
+  auto stage_w_ptr = [&](int st) { return F32IN ? smc : smc + st * STAGE; };
+  auto stage_hh_ptr = [&](int st) { return F32IN ? smc + W_TILE : smc + st * STAGE + W_TILE; };
+  unsigned char* sWl = smc + W_TILE + 2 * H_TILE;   // fp32 inputs only
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int item = blockIdx.y, j0 = blockIdx.x * NB2;
@@ -293,7 +293,10 @@ cham_tc_colpass(const T* __restrict__ q, const T* __restrict__ k, const T* __res
   const float* si = src_i ? src_i + soff : nullptr;
 
   if (warp == 0) tc::tmem_alloc(tslot, 512);
-  if (tid == 0) { tc::mbar_init(bar, 1); tc::fence_mbar_init(); }
+  if (tid == 0) {
+    for (int i = 0; i < 3; ++i) tc::mbar_init(&bars[i], 1);
+    tc::fence_mbar_init();
+  }
   tc::fence_before_sync();
   __syncthreads();
   tc::fence_after_sync();
@@ -302,60 +305,115 @@ cham_tc_colpass(const T* __restrict__ q, const T* __restrict__ k, const T* __res
   const uint32_t lane_base = (uint32_t)(32 * (warp & 3)) << 16;
   const int row = 32 * (warp & 3) + lane;   // TMEM lane == accumulator row of this thread
   const int half = warp >> 2;               // which half of the accumulator columns
-  uint32_t phase = 0;
+  uint32_t ph[3] = {0u, 0u, 0u};
   bool failed = false;
 
-  auto wait_mma = [&]() -> bool {
-    const bool ok = tc::mbar_wait(bar, phase, MAX_POLLS);
-    phase ^= 1u;
+  auto wait_bar = [&](int b) -> bool {
+    const bool ok = tc::mbar_wait(&bars[b], ph[b], MAX_POLLS);
+    ph[b] ^= 1u;
     if (__syncthreads_or(!ok)) { if (tid == 0) record_timeout(); return false; }
     tc::fence_after_sync();
     return true;
   };
+  const int NT = D / KT;
 
-  // ---------------- phase A: Z = Wᵀ S[:, block]
-  constexpr uint32_t ID_Z = tc::idesc_bf16(128, N2, false, true);
-  for (int i0 = 0; i0 < D && !failed; i0 += KT) {
-    stage_w<T>(sW, sWl, k, v, item, S, D, t0, nt, bad, i0, tid);
-    for (int e = tid; e < KT * (N2 / 8); e += THR) {
-      const int g = e % (N2 / 8), i = e / (N2 / 8);   // 8 consecutive columns of row i
-      const int col = j0 + (g & 3) * 8;             // g < 4: re, g >= 4: im
-      const int gi = i0 + i;
-      float x[8];
+  // W tile of K tile kt into stage st: bf16 by cp.async, fp32 through registers (split)
+  auto stage_w_tile = [&](int kt, int st) {
+    if constexpr (F32IN) {
+      stage_w<T>(stage_w_ptr(st), sWl, k, v, item, S, D, t0, nt, bad, kt * KT, tid);
+    } else {
+      unsigned char* sw = stage_w_ptr(st);
+#pragma unroll
+      for (int u = 0; u < (R2 * KT / 8) / THR; ++u) {
+        const int e = tid + THR * u;
+        const int r = e % R2, g = e / R2, tau = r >> 1;
+        const bool valid = tau < nt && !((bad >> tau) & 1ull);
+        const T* src = ((r & 1) ? v : k) + ((size_t)item * S + t0 + (valid ? tau : 0)) * D + kt * KT + g * 8;
+        tc::cp_async16(sw + kmaj(r, g * 8, R2), src, valid);
+      }
+      tc::cp_async_commit();
+    }
+  };
+  // H tile (rows [kt*KT, +KT), columns re|im of this block) into stage st, split hi/lo.
+  // All global loads of the thread are issued before any conversion.
+  auto stage_h_tile = [&](int kt, int st) {
+    unsigned char* hh = stage_hh_ptr(st);
+    unsigned char* hl = hh + H_TILE;
+    constexpr int PER = (KT * (N2 / 8)) / THR;   // 4 chunks of 8 columns per thread
+    float4 buf[PER][2];
+#pragma unroll
+    for (int u = 0; u < PER; ++u) {
+      const int e = tid + THR * u;
+      const int g = e % (N2 / 8), i = e / (N2 / 8);
+      const int col = j0 + (g & 3) * 8, gi = kt * KT + i;
       if (sr) {
         const float* p = ((g < 4) ? sr : si) + (size_t)gi * D + col;
-        load8(p, x);
+        buf[u][0] = *reinterpret_cast<const float4*>(p);
+        buf[u][1] = *reinterpret_cast<const float4*>(p + 4);
       } else {
+        float x[8];
 #pragma unroll
         for (int jj = 0; jj < 8; ++jj) x[jj] = (g < 4 && gi == col + jj) ? 1.f : 0.f;
+        buf[u][0] = make_float4(x[0], x[1], x[2], x[3]);
+        buf[u][1] = make_float4(x[4], x[5], x[6], x[7]);
       }
+    }
+#pragma unroll
+    for (int u = 0; u < PER; ++u) {
+      const int e = tid + THR * u;
+      const int g = e % (N2 / 8), i = e / (N2 / 8);
+      const float x[8] = {buf[u][0].x, buf[u][0].y, buf[u][0].z, buf[u][0].w,
+                          buf[u][1].x, buf[u][1].y, buf[u][1].z, buf[u][1].w};
       uint4 h, l;
       tc::split8(x, h, l);
-      *reinterpret_cast<uint4*>(sHh + mnmaj(i, g * 8, N2 / 8)) = h;
-      *reinterpret_cast<uint4*>(sHl + mnmaj(i, g * 8, N2 / 8)) = l;
+      *reinterpret_cast<uint4*>(hh + mnmaj(i, g * 8, N2 / 8)) = h;
+      *reinterpret_cast<uint4*>(hl + mnmaj(i, g * 8, N2 / 8)) = l;
     }
-    tc::fence_proxy_async();
-    __syncthreads();
-    if (tid == 0) {
-      tc::fence_after_sync();
-      const uint32_t aw = tc::smem_addr(sW), awl = tc::smem_addr(sWl);
-      const uint32_t bh = tc::smem_addr(sHh), bl = tc::smem_addr(sHl);
+  };
+
+  // ---------------- phase A: Z = Wᵀ S[:, block], pipelined over K tiles
+  constexpr uint32_t ID_Z = tc::idesc_bf16(128, N2, false, true);
+  {
+    int outstanding[2] = {0, 0};
+    for (int kt = 0; kt < NT && !failed; ++kt) {
+      const int st = F32IN ? 0 : (kt & 1);
+      if (outstanding[st]) { failed = !wait_bar(st); outstanding[st] = 0; if (failed) break; }
+      stage_w_tile(kt, st);
+      stage_h_tile(kt, st);
+      if constexpr (!F32IN) tc::cp_async_wait_all();
+      tc::fence_proxy_async();
+      __syncthreads();
+      if (tid == 0) {
+        tc::fence_after_sync();
+        const uint32_t aw = tc::smem_addr(stage_w_ptr(st)), awl = tc::smem_addr(sWl);
+        const uint32_t bh = tc::smem_addr(stage_hh_ptr(st)), bl = bh + H_TILE;
 #pragma unroll 1
-      for (int ks = 0; ks < KT / 16; ++ks) {
-        const uint64_t a = tc::sdesc(aw + ks * 2 * R2 * 16, R2 * 16, 128);
-        const uint64_t b_hi = tc::sdesc(bh + ks * 2 * (N2 / 8) * 128, (N2 / 8) * 128, 128);
-        const uint64_t b_lo = tc::sdesc(bl + ks * 2 * (N2 / 8) * 128, (N2 / 8) * 128, 128);
-        tc::mma_bf16(tZ, a, b_hi, ID_Z, (i0 > 0 || ks > 0) ? 1u : 0u);
-        tc::mma_bf16(tZ, a, b_lo, ID_Z, 1u);
-        if (F32IN) tc::mma_bf16(tZ, tc::sdesc(awl + ks * 2 * R2 * 16, R2 * 16, 128), b_hi, ID_Z, 1u);
+        for (int ks = 0; ks < KT / 16; ++ks) {
+          const uint64_t a = tc::sdesc(aw + ks * 2 * R2 * 16, R2 * 16, 128);
+          const uint64_t b_hi = tc::sdesc(bh + ks * 2 * (N2 / 8) * 128, (N2 / 8) * 128, 128);
+          const uint64_t b_lo = tc::sdesc(bl + ks * 2 * (N2 / 8) * 128, (N2 / 8) * 128, 128);
+          tc::mma_bf16(tZ, a, b_hi, ID_Z, (kt > 0 || ks > 0) ? 1u : 0u);
+          tc::mma_bf16(tZ, a, b_lo, ID_Z, 1u);
+          if (F32IN) tc::mma_bf16(tZ, tc::sdesc(awl + ks * 2 * R2 * 16, R2 * 16, 128), b_hi, ID_Z, 1u);
+        }
+        tc::commit(&bars[st]);
       }
-      tc::commit(bar);
+      outstanding[st] = 1;
     }
-    failed = !wait_mma();
+    for (int st = 0; st < 2 && !failed; ++st)
+      if (outstanding[st]) { failed = !wait_bar(st); outstanding[st] = 0; }
   }
 
   // ---------------- phase T: P1 = Tr Z, P2 = Ti Z  (Z split hi/lo, T split hi/lo)
   if (!failed) {
+    const uint4* Tin = reinterpret_cast<const uint4*>(Tws + chunk * 4 * T_TILE);
+    if constexpr (!F32IN) {
+#pragma unroll 4
+      for (int e = tid; e < 4 * T_TILE / 16; e += THR) tc::cp_async16(sT + 16 * e, Tin + e, true);
+      tc::cp_async_commit();
+    } else {
+      for (int e = tid; e < 4 * T_TILE / 16; e += THR) reinterpret_cast<uint4*>(sT)[e] = Tin[e];
+    }
     float z[32];
     tc::tmem_ld16(tZ + lane_base + 32 * half, z);
     tc::tmem_ld16(tZ + lane_base + 32 * half + 16, z + 16);
@@ -367,8 +425,7 @@ cham_tc_colpass(const T* __restrict__ q, const T* __restrict__ k, const T* __res
       *reinterpret_cast<uint4*>(sZh + off) = h;
       *reinterpret_cast<uint4*>(sZl + off) = l;
     }
-    const uint4* Tin = reinterpret_cast<const uint4*>(Tws + chunk * 4 * T_TILE);
-    for (int e = tid; e < 4 * T_TILE / 16; e += THR) reinterpret_cast<uint4*>(sT)[e] = Tin[e];
+    if constexpr (!F32IN) tc::cp_async_wait_all();
     tc::fence_proxy_async();
     tc::fence_before_sync();
     __syncthreads();
@@ -392,14 +449,13 @@ cham_tc_colpass(const T* __restrict__ q, const T* __restrict__ k, const T* __res
           tc::mma_bf16(td, al, bh, ID_T, 1u);
         }
       }
-      tc::commit(bar);
+      tc::commit(&bars[2]);
     }
-    failed = !wait_mma();
+    failed = !wait_bar(2);
   }
 
   // ---------------- Cm, then E = Re(Cm) Y_block
   if (!failed) {
-    // this thread: row r = row, complex columns j in [16*half, 16*half + 16)
     float p1r[16], p1i[16], p2r[16], p2i[16];
     tc::tmem_ld16(tP1 + lane_base + 16 * half, p1r);
     tc::tmem_ld16(tP1 + lane_base + 32 + 16 * half, p1i);
@@ -408,6 +464,7 @@ cham_tc_colpass(const T* __restrict__ q, const T* __restrict__ k, const T* __res
     float cr[16], ci[16];
 #pragma unroll
     for (int j = 0; j < 16; ++j) { cr[j] = p1r[j] - p2i[j]; ci[j] = p1i[j] + p2r[j]; }
+    // the T tiles are dead once P1/P2 are in TMEM, so Ca and Y may reuse region U
 #pragma unroll
     for (int g = 0; g < 2; ++g) {
       uint4 h, l;
@@ -421,7 +478,6 @@ cham_tc_colpass(const T* __restrict__ q, const T* __restrict__ k, const T* __res
       *reinterpret_cast<uint4*>(sCh + mnmaj(row, NB2 + jc, N2 / 8)) = h;
       *reinterpret_cast<uint4*>(sCl + mnmaj(row, NB2 + jc, N2 / 8)) = l;
     }
-    // Y block: B operand (n = token t, k = column j), K-major with 64 rows
     for (int e = tid; e < C2 * (NB2 / 8); e += THR) {
       const int t = e % C2, g = e / C2;
       const bool valid = t < nt;
@@ -445,9 +501,9 @@ cham_tc_colpass(const T* __restrict__ q, const T* __restrict__ k, const T* __res
         tc::mma_bf16(tE, a_l, b_h, ID_E, 1u);
         if (F32IN) tc::mma_bf16(tE, a_h, tc::sdesc(yl + ks * 2 * C2 * 16, C2 * 16, 128), ID_E, 1u);
       }
-      tc::commit(bar);
+      tc::commit(&bars[2]);
     }
-    failed = !wait_mma();
+    failed = !wait_bar(2);
   }
   if (!failed) {
     float e[32];
@@ -458,57 +514,75 @@ cham_tc_colpass(const T* __restrict__ q, const T* __restrict__ k, const T* __res
     for (int t = 0; t < 32; ++t) atomicAdd(Eo + t, e[t]);
   }
 
-  // ---------------- phase B: S_next[:, block] = S[:, block] + W Cm
+  // ---------------- phase B: S_next[:, block] = S[:, block] + W Cm, pipelined:
+  // tile kt's MMAs (into dH[kt&1]) overlap tile kt-1's epilogue and tile kt+1's W load.
   constexpr uint32_t ID_H = tc::idesc_bf16(128, N2, true, true);
-  for (int i0 = 0; i0 < D && !failed; i0 += KT) {
-    tc::fence_before_sync();
-    __syncthreads();     // previous epilogue's TMEM loads and smem reads are done
-    stage_w<T>(sW, sWl, k, v, item, S, D, t0, nt, bad, i0, tid);
-    tc::fence_proxy_async();
-    __syncthreads();
+  auto issue_b = [&](int kt, int st) {
     if (tid == 0) {
       tc::fence_after_sync();
-      const uint32_t aw = tc::smem_addr(sW), awl = tc::smem_addr(sWl);
+      const uint32_t aw = tc::smem_addr(stage_w_ptr(st)), awl = tc::smem_addr(sWl);
       const uint32_t ch = tc::smem_addr(sCh), cl = tc::smem_addr(sCl);
+      const uint32_t td = tDH + 64 * (F32IN ? 0 : st);
 #pragma unroll 1
       for (int ks = 0; ks < R2 / 16; ++ks) {
         // A = W viewed MN-major: M = element index i, K = vector index r
         const uint64_t a = tc::sdesc(aw + ks * 256, 128, R2 * 16);
         const uint64_t b_h = tc::sdesc(ch + ks * 2 * (N2 / 8) * 128, (N2 / 8) * 128, 128);
         const uint64_t b_l = tc::sdesc(cl + ks * 2 * (N2 / 8) * 128, (N2 / 8) * 128, 128);
-        tc::mma_bf16(tDH, a, b_h, ID_H, ks > 0 ? 1u : 0u);
-        tc::mma_bf16(tDH, a, b_l, ID_H, 1u);
-        if (F32IN) tc::mma_bf16(tDH, tc::sdesc(awl + ks * 256, 128, R2 * 16), b_h, ID_H, 1u);
+        tc::mma_bf16(td, a, b_h, ID_H, ks > 0 ? 1u : 0u);
+        tc::mma_bf16(td, a, b_l, ID_H, 1u);
+        if (F32IN) tc::mma_bf16(td, tc::sdesc(awl + ks * 256, 128, R2 * 16), b_h, ID_H, 1u);
       }
-      tc::commit(bar);
+      tc::commit(&bars[st]);
     }
-    failed = !wait_mma();
-    if (failed) break;
-    // epilogue: row i0 + row, columns [32*half, 32*half+32) = re (half 0) or im (half 1)
-    float dh[32];
-    tc::tmem_ld16(tDH + lane_base + 32 * half, dh);
-    tc::tmem_ld16(tDH + lane_base + 32 * half + 16, dh + 16);
-    const int gi = i0 + row;
+  };
+  // epilogue of tile kt: row kt*KT + row, columns [32*half, +32) = re (half 0) / im (half 1)
+  auto epilogue_b = [&](int kt, int st) -> bool {
+    const int gi = kt * KT + row;
     const size_t o = soff + (size_t)gi * D + j0;
-    float* dst = (half ? dst_i : dst_r) + o;
+    float4 hv[8];
     if (sr) {
       const float* src = (half ? src_i : src_r) + o;
 #pragma unroll
-      for (int jj = 0; jj < 32; jj += 4) {
-        const float4 a = *reinterpret_cast<const float4*>(src + jj);
-        *reinterpret_cast<float4*>(dst + jj) =
-            make_float4(a.x + dh[jj], a.y + dh[jj + 1], a.z + dh[jj + 2], a.w + dh[jj + 3]);
-      }
+      for (int jj = 0; jj < 8; ++jj) hv[jj] = *reinterpret_cast<const float4*>(src + 4 * jj);
     } else {
 #pragma unroll
-      for (int jj = 0; jj < 32; jj += 4) {
+      for (int jj = 0; jj < 8; ++jj) {
         float a[4];
 #pragma unroll
-        for (int u = 0; u < 4; ++u) a[u] = (!half && gi == j0 + jj + u) ? 1.f : 0.f;
-        *reinterpret_cast<float4*>(dst + jj) =
-            make_float4(a[0] + dh[jj], a[1] + dh[jj + 1], a[2] + dh[jj + 2], a[3] + dh[jj + 3]);
+        for (int u = 0; u < 4; ++u) a[u] = (!half && gi == j0 + 4 * jj + u) ? 1.f : 0.f;
+        hv[jj] = make_float4(a[0], a[1], a[2], a[3]);
       }
     }
+    if (!wait_bar(st)) return false;
+    float dh[32];
+    const uint32_t td = tDH + 64 * (F32IN ? 0 : st);
+    tc::tmem_ld16(td + lane_base + 32 * half, dh);
+    tc::tmem_ld16(td + lane_base + 32 * half + 16, dh + 16);
+    float* dst = (half ? dst_i : dst_r) + o;
+#pragma unroll
+    for (int jj = 0; jj < 8; ++jj)
+      *reinterpret_cast<float4*>(dst + 4 * jj) =
+          make_float4(hv[jj].x + dh[4 * jj], hv[jj].y + dh[4 * jj + 1], hv[jj].z + dh[4 * jj + 2],
+                      hv[jj].w + dh[4 * jj + 3]);
+    return true;
+  };
+  if (!failed) {
+    // the epilogue of tile kt-1 runs after tile kt's MMAs are issued; tile kt+1's W
+    // stage (kt+1)&1 is free once tile kt-1's MMAs completed (waited in its epilogue)
+    for (int kt = 0; kt < NT && !failed; ++kt) {
+      const int st = F32IN ? 0 : (kt & 1);
+      if (F32IN && kt > 0) { if (!epilogue_b(kt - 1, 0)) { failed = true; break; } }
+      tc::fence_before_sync();
+      __syncthreads();   // previous readers of this stage and of dH[st] are done
+      stage_w_tile(kt, st);
+      if constexpr (!F32IN) tc::cp_async_wait_all();
+      tc::fence_proxy_async();
+      __syncthreads();
+      issue_b(kt, st);
+      if (!F32IN && kt > 0) { if (!epilogue_b(kt - 1, st ^ 1)) { failed = true; break; } }
+    }
+    if (!failed) failed = !epilogue_b(NT - 1, F32IN ? 0 : ((NT - 1) & 1));
   }
   tc::fence_before_sync();
   __syncthreads();
@@ -520,7 +594,7 @@ cham_tc_colpass(const T* __restrict__ q, const T* __restrict__ k, const T* __res
 // smem: A (S rows, K-major hi/lo 2 x 32K) | Y (K-major, 64 rows, hi/lo 2 x 16K) |
 //       W (32K, + lo 32K for fp32) | E (MN-major hi/lo 2 x 16K) | bar, slot
 constexpr int RD_A = 0, RD_Y = 64 * 1024, RD_W = 96 * 1024, RD_E = 160 * 1024, RD_BAR = 192 * 1024;
-constexpr int READOUT_SMEM = RD_BAR + 64 + SMEM_SLACK;
+constexpr int READOUT_SMEM = RD_BAR + 64;
 
 template <typename T>
 __global__ void __launch_bounds__(THR, 1)
@@ -668,7 +742,8 @@ int launch_cham_tc(const void* q, const void* k, const void* v, const float* gam
   int rc;
   const size_t ps = tc_prep_smem();
   VERACE_CUDA(cudaFuncSetAttribute(cham_tc_prep<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ps));
-  VERACE_CUDA(cudaFuncSetAttribute(cham_tc_colpass<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, COLPASS_SMEM));
+  constexpr int CPS = colpass_smem(sizeof(T) == 4);
+  VERACE_CUDA(cudaFuncSetAttribute(cham_tc_colpass<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, CPS));
   VERACE_CUDA(cudaFuncSetAttribute(cham_tc_readout<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, READOUT_SMEM));
   cham_tc_prep<T><<<dim3(nch, b), THR, ps, st>>>((const T*)k, (const T*)v, gamma, w.T, w.E, w.bad, s, D, nch);
   if ((rc = check_launch("cham_tc_prep"))) return rc;
@@ -679,7 +754,7 @@ int launch_cham_tc(const void* q, const void* k, const void* v, const float* gam
     const bool to_out = ((nch - 1 - c) % 2) == 0;
     float* dr = to_out ? hr : w.Hre;
     float* di = to_out ? hi : w.Him;
-    cham_tc_colpass<T><<<gc, THR, COLPASS_SMEM, st>>>((const T*)q, (const T*)k, (const T*)v, w.T, w.E, w.bad,
+    cham_tc_colpass<T><<<gc, THR, CPS, st>>>((const T*)q, (const T*)k, (const T*)v, w.T, w.E, w.bad,
                                                       cur_r, cur_i, dr, di, s, D, nch, c);
     if ((rc = check_launch("cham_tc_colpass"))) return rc;
     cham_tc_readout<T><<<gr, THR, READOUT_SMEM, st>>>((const T*)q, (const T*)k, (const T*)v, w.E, w.bad,
