@@ -20,6 +20,10 @@
 #include "common.cuh"
 #include "tc.cuh"
 
+#include <cuda.h>
+#include <cudaTypedefs.h>
+#include <mutex>
+
 namespace verace {
 namespace {
 
@@ -102,8 +106,13 @@ __device__ __forceinline__ void stage8(const T* src, bool valid, unsigned char* 
   }
 }
 
-// Stage the chunk's k/v vectors, elements [i0, i0+KT), as a K-major tile with rows =
-// vector index r (2*tau + {0: k, 1: v}).
+// Row order of the chunk's W = [k_1 .. k_64, v_1 .. v_64]: row r holds token tok(r) = r % 64,
+// the k vector for r < 64 and the v vector for r >= 64 (so that k and v rows each form
+// one contiguous 64-row block, the shape a TMA box delivers).  T, Z, Cm and E use it too.
+__device__ __forceinline__ int tok(int r) { return r & (C2 - 1); }
+__device__ __forceinline__ bool is_v(int r) { return r >= C2; }
+
+// Stage the chunk's k/v vectors, elements [i0, i0+KT), as a K-major tile with rows = r.
 template <typename T>
 __device__ __forceinline__ void stage_w(unsigned char* sw_hi, unsigned char* sw_lo,
                                         const T* __restrict__ k, const T* __restrict__ v,
@@ -111,9 +120,9 @@ __device__ __forceinline__ void stage_w(unsigned char* sw_hi, unsigned char* sw_
                                         int i0, int tid) {
   for (int e = tid; e < R2 * (KT / 8); e += THR) {
     const int r = e % R2, g = e / R2;  // consecutive threads -> consecutive vectors
-    const int tau = r >> 1;
+    const int tau = tok(r);
     const bool valid = tau < nt && !((bad >> tau) & 1ull);
-    const T* src = ((r & 1) ? v : k) + ((size_t)item * S + t0 + (valid ? tau : 0)) * D + i0 + g * 8;
+    const T* src = (is_v(r) ? v : k) + ((size_t)item * S + t0 + (valid ? tau : 0)) * D + i0 + g * 8;
     stage8(src, valid, sw_hi + kmaj(r, g * 8, R2), sw_lo + kmaj(r, g * 8, R2));
   }
 }
@@ -221,12 +230,19 @@ cham_tc_prep(const T* __restrict__ k, const T* __restrict__ v, const float* __re
   __syncthreads();
   const size_t chunk = (size_t)item * nch + c;
   unsigned char* To = Tws + chunk * 4 * T_TILE;
-  // K-major tiles: A(m = r, k = r') = T[r][r']
+  // K-major tiles: A(m = r, k = r') = T[r][r'] in the kernels' row order (k block, v
+  // block); T was formed with rows interleaved (2*tau + {k, v}).
+  auto src_idx = [](int ro) { return 2 * tok(ro) + (is_v(ro) ? 1 : 0); };
   for (int e = tid; e < R2 * (R2 / 8); e += THR) {
     const int r = e % R2, g = e / R2;
+    const int rs = src_idx(r);
     float xr[8], xi[8];
 #pragma unroll
-    for (int j = 0; j < 8; ++j) { xr[j] = Tr[r * P + g * 8 + j]; xi[j] = Ti[r * P + g * 8 + j]; }
+    for (int j = 0; j < 8; ++j) {
+      const int cs = src_idx(g * 8 + j);
+      xr[j] = Tr[rs * P + cs];
+      xi[j] = Ti[rs * P + cs];
+    }
     uint4 h, l;
     const int off = kmaj(r, g * 8, R2);
     tc::split8(xr, h, l);
@@ -326,9 +342,9 @@ cham_tc_colpass(const T* __restrict__ q, const T* __restrict__ k, const T* __res
 #pragma unroll
       for (int u = 0; u < (R2 * KT / 8) / THR; ++u) {
         const int e = tid + THR * u;
-        const int r = e % R2, g = e / R2, tau = r >> 1;
+        const int r = e % R2, g = e / R2, tau = tok(r);
         const bool valid = tau < nt && !((bad >> tau) & 1ull);
-        const T* src = ((r & 1) ? v : k) + ((size_t)item * S + t0 + (valid ? tau : 0)) * D + kt * KT + g * 8;
+        const T* src = (is_v(r) ? v : k) + ((size_t)item * S + t0 + (valid ? tau : 0)) * D + kt * KT + g * 8;
         tc::cp_async16(sw + kmaj(r, g * 8, R2), src, valid);
       }
       tc::cp_async_commit();
@@ -692,7 +708,7 @@ cham_tc_readout(const T* __restrict__ q, const T* __restrict__ k, const T* __res
       float x[8];
       load8(Ein + (size_t)r * C2 + g * 8, x);
 #pragma unroll
-      for (int jj = 0; jj < 8; ++jj) if ((r >> 1) > g * 8 + jj) x[jj] = 0.f;
+      for (int jj = 0; jj < 8; ++jj) if (tok(r) > g * 8 + jj) x[jj] = 0.f;
       uint4 h, l;
       tc::split8(x, h, l);
       *reinterpret_cast<uint4*>(sEh + mnmaj(r, g * 8, C2 / 8)) = h;
@@ -733,6 +749,403 @@ cham_tc_readout(const T* __restrict__ q, const T* __restrict__ k, const T* __res
   if (warp == 0) tc::tmem_dealloc(tO, 64);
 }
 
+// ---------------------------------------------------------------------------------
+// Warp-specialised colpass for bf16 inputs.  Warp 8 (one thread) is the producer: it
+// issues the TMA loads (k/v tiles straight into the tensor-core layout, fp32 state tiles
+// with 128-byte swizzle, T tiles as bulk copies) and every tcgen05.mma; warps 0-7 are
+// the consumers: they split fp32 state tiles into bf16 hi/lo operands, turn Z and Cm
+// into operands, and run the state-update epilogue.  Producer and consumers hand over
+// through mbarriers; every wait is bounded.  Same arithmetic as cham_tc_colpass.
+//
+// smem: U [0,128K)   stage s = (W 32K | state re 16K | state im 16K) at s*64K
+//                    phase T: T tiles (4 x 32K); phase E: Ca (16K) | Y (4K)
+//       HS[2] [128K,192K)  split state tiles (hi 16K | lo 16K); phase T: Z split in
+//                          HS[0]; phases E/B: Cm split in HS[1]
+//       barriers, TMEM slot, failure flag at 192K
+// TMEM: Z [0,64) P1 [64,128) P2 [128,192) E [192,256) dH[2] [256,384)
+constexpr int CONS = 256;                 // consumer threads
+constexpr int WS_THREADS = CONS + 32;     // + producer warp
+constexpr int WS_HS = 128 * 1024, WS_BAR = 192 * 1024;
+constexpr int WS_SMEM = WS_BAR + 256;
+enum { B_TFULL = 0, B_SFULL = 2, B_MDONE = 4, B_EDONE = 6, B_WFIX = 8, B_TT = 10, B_ZREADY = 11,
+       B_MT = 12, B_CREADY = 13, B_ME = 14, N_BARS = 15 };
+
+__device__ __forceinline__ bool consumers_all(bool ok) {
+  int r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\tsetp.ne.u32 p, %1, 0;\n\tbar.red.and.pred q, 2, 256, p;\n\t"
+      "selp.s32 %0, 1, 0, q;\n\t}\n"
+      : "=r"(r)
+      : "r"((int)ok)
+      : "memory");
+  return r != 0;
+}
+
+__global__ void __launch_bounds__(WS_THREADS, 1)
+cham_tc_colpass_ws(const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
+                   const __grid_constant__ CUtensorMap tm_sr, const __grid_constant__ CUtensorMap tm_si,
+                   const __nv_bfloat16* __restrict__ q, const unsigned char* __restrict__ Tws,
+                   float* __restrict__ Ews, const unsigned long long* __restrict__ badws, int src_identity,
+                   float* __restrict__ dst_r, float* __restrict__ dst_i, int S, int D, int nch, int c) {
+  extern __shared__ __align__(1024) unsigned char smw[];
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smw + WS_BAR);
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(smw + WS_BAR + 8 * N_BARS);
+  volatile int* fail = reinterpret_cast<volatile int*>(smw + WS_BAR + 8 * N_BARS + 16);
+  auto stageW = [&](int s) { return smw + s * STAGE; };
+  auto stageHr = [&](int s) { return smw + s * STAGE + W_TILE; };
+  auto stageHi = [&](int s) { return smw + s * STAGE + W_TILE + 16 * 1024; };
+  auto splitH = [&](int s) { return smw + WS_HS + s * 32 * 1024; };
+  unsigned char* sZh = splitH(0);
+  unsigned char* sZl = sZh + Z_TILE;
+  unsigned char* sCh = splitH(1);
+  unsigned char* sCl = sCh + Z_TILE;
+  unsigned char* sAh = smw;
+  unsigned char* sAl = smw + CA_TILE;
+  unsigned char* sY = smw + 2 * CA_TILE;
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int item = blockIdx.y, j0 = blockIdx.x * NB2;
+  const int t0 = c * C2, nt = min(C2, S - t0);
+  const size_t chunk = (size_t)item * nch + c;
+  const unsigned long long bad = badws[chunk];
+  const bool patch_w = bad != 0ull;   // padded rows come back zero from the TMA bounds
+  const int NT = D / KT;
+
+  if (warp == 0) tc::tmem_alloc(tslot, 512);
+  if (tid == 0) {
+    for (int i = 0; i < N_BARS; ++i) tc::mbar_init(&bars[i], 1);
+    *fail = 0;
+    tc::fence_mbar_init();
+  }
+  tc::fence_before_sync();
+  __syncthreads();
+  tc::fence_after_sync();
+  const uint32_t tbase = *tslot;
+  const uint32_t tZ = tbase, tP1 = tbase + 64, tP2 = tbase + 128, tE = tbase + 192, tDH = tbase + 256;
+
+  if (warp == 8) {
+    // ======================= producer (one thread) =======================
+    if (lane == 0) {
+      bool ok = true;
+      auto pwait = [&](int b, uint32_t par) {
+        if (!ok) return false;
+        if (*fail || !tc::mbar_wait(&bars[b], par, MAX_POLLS)) { ok = false; *fail = 1; record_timeout(); }
+        return ok;
+      };
+      auto issue_tiles = [&](int g, int kt) {   // K tile kt of global tile counter g
+        const int s = g & 1;
+        tc::mbar_expect_tx(&bars[B_TFULL + s], W_TILE + (src_identity ? 0 : 2 * 16 * 1024));
+        unsigned char* w = stageW(s);
+#pragma unroll 1
+        for (int cc = 0; cc < KT / 8; ++cc) {
+          tc::tma_load_3d(w + cc * 2048, &tm_k, kt * KT + cc * 8, t0, item, &bars[B_TFULL + s]);
+          tc::tma_load_3d(w + cc * 2048 + 1024, &tm_v, kt * KT + cc * 8, t0, item, &bars[B_TFULL + s]);
+        }
+        if (!src_identity) {
+          tc::tma_load_2d(stageHr(s), &tm_sr, j0, item * D + kt * KT, &bars[B_TFULL + s]);
+          tc::tma_load_2d(stageHi(s), &tm_si, j0, item * D + kt * KT, &bars[B_TFULL + s]);
+        }
+      };
+      constexpr uint32_t ID_Z = tc::idesc_bf16(128, N2, false, true);
+      constexpr uint32_t ID_H = tc::idesc_bf16(128, N2, true, true);
+      // ---- phase A
+      issue_tiles(0, 0);
+      if (NT > 1) issue_tiles(1, 1);
+      for (int kt = 0; kt < NT && ok; ++kt) {
+        const int g = kt, s = g & 1;
+        if (!pwait(B_TFULL + s, (g >> 1) & 1) || !pwait(B_SFULL + s, (kt >> 1) & 1)) break;
+        tc::fence_after_sync();
+        const uint32_t aw = tc::smem_addr(stageW(s));
+        const uint32_t bh = tc::smem_addr(splitH(s)), bl = bh + H_TILE;
+#pragma unroll 1
+        for (int ks = 0; ks < KT / 16; ++ks) {
+          const uint64_t a = tc::sdesc(aw + ks * 2 * R2 * 16, R2 * 16, 128);
+          tc::mma_bf16(tZ, a, tc::sdesc(bh + ks * 2 * (N2 / 8) * 128, (N2 / 8) * 128, 128), ID_Z,
+                       (kt > 0 || ks > 0) ? 1u : 0u);
+          tc::mma_bf16(tZ, a, tc::sdesc(bl + ks * 2 * (N2 / 8) * 128, (N2 / 8) * 128, 128), ID_Z, 1u);
+        }
+        tc::commit(&bars[B_MDONE + s]);
+        if (kt + 2 < NT) {
+          if (!pwait(B_MDONE + s, (g >> 1) & 1)) break;
+          issue_tiles(g + 2, kt + 2);
+        }
+      }
+      // ---- phase T: bring in T once every phase-A MMA is done, then P1 = Tr Z, P2 = Ti Z
+      if (ok && pwait(B_MDONE + ((NT - 1) & 1), ((NT - 1) >> 1) & 1)) {
+        tc::mbar_expect_tx(&bars[B_TT], 4 * T_TILE);
+        const unsigned char* tsrc = Tws + chunk * 4 * T_TILE;
+        for (int p4 = 0; p4 < 4; ++p4) tc::bulk_load(smw + p4 * T_TILE, tsrc + p4 * T_TILE, T_TILE, &bars[B_TT]);
+        if (pwait(B_ZREADY, 0) && pwait(B_TT, 0)) {
+          tc::fence_after_sync();
+          constexpr uint32_t ID_T = tc::idesc_bf16(128, N2, false, true);
+          const uint32_t zh = tc::smem_addr(sZh), zl = tc::smem_addr(sZl);
+#pragma unroll 1
+          for (int part = 0; part < 2; ++part) {
+            const uint32_t th = tc::smem_addr(smw) + (2 * part) * T_TILE, tl = th + T_TILE;
+            const uint32_t td = part ? tP2 : tP1;
+#pragma unroll 1
+            for (int ks = 0; ks < R2 / 16; ++ks) {
+              const uint64_t ah = tc::sdesc(th + ks * 2 * R2 * 16, R2 * 16, 128);
+              const uint64_t al = tc::sdesc(tl + ks * 2 * R2 * 16, R2 * 16, 128);
+              const uint64_t b_h = tc::sdesc(zh + ks * 2 * (N2 / 8) * 128, (N2 / 8) * 128, 128);
+              const uint64_t b_l = tc::sdesc(zl + ks * 2 * (N2 / 8) * 128, (N2 / 8) * 128, 128);
+              tc::mma_bf16(td, ah, b_h, ID_T, ks > 0 ? 1u : 0u);
+              tc::mma_bf16(td, ah, b_l, ID_T, 1u);
+              tc::mma_bf16(td, al, b_h, ID_T, 1u);
+            }
+          }
+          tc::commit(&bars[B_MT]);
+        }
+      }
+      // ---- phase E: E = Re(Cm) Y
+      if (ok && pwait(B_CREADY, 0)) {
+        tc::fence_after_sync();
+        constexpr uint32_t ID_E = tc::idesc_bf16(128, C2, false, false);
+        const uint32_t ah = tc::smem_addr(sAh), al = tc::smem_addr(sAl), yh = tc::smem_addr(sY);
+#pragma unroll 1
+        for (int ks = 0; ks < NB2 / 16; ++ks) {
+          const uint64_t b_h = tc::sdesc(yh + ks * 2 * C2 * 16, C2 * 16, 128);
+          tc::mma_bf16(tE, tc::sdesc(ah + ks * 2 * R2 * 16, R2 * 16, 128), b_h, ID_E, ks > 0 ? 1u : 0u);
+          tc::mma_bf16(tE, tc::sdesc(al + ks * 2 * R2 * 16, R2 * 16, 128), b_h, ID_E, 1u);
+        }
+        tc::commit(&bars[B_ME]);
+      }
+      // ---- phase B: dH = W Cm per K tile, overlapped with the consumers' epilogues
+      if (ok && pwait(B_ME, 0)) {
+        auto mma_b = [&](int kt) {
+          const int g = NT + kt, s = g & 1, d = kt & 1;
+          if (!pwait(B_TFULL + s, (g >> 1) & 1)) return false;
+          if (patch_w && !pwait(B_WFIX + d, (kt >> 1) & 1)) return false;
+          if (kt >= 2 && !pwait(B_EDONE + d, ((kt - 2) >> 1) & 1)) return false;
+          tc::fence_after_sync();
+          const uint32_t aw = tc::smem_addr(stageW(s));
+          const uint32_t ch = tc::smem_addr(sCh), cl = tc::smem_addr(sCl);
+#pragma unroll 1
+          for (int ks = 0; ks < R2 / 16; ++ks) {
+            const uint64_t a = tc::sdesc(aw + ks * 256, 128, R2 * 16);
+            tc::mma_bf16(tDH + 64 * d, a, tc::sdesc(ch + ks * 2 * (N2 / 8) * 128, (N2 / 8) * 128, 128), ID_H,
+                         ks > 0 ? 1u : 0u);
+            tc::mma_bf16(tDH + 64 * d, a, tc::sdesc(cl + ks * 2 * (N2 / 8) * 128, (N2 / 8) * 128, 128), ID_H, 1u);
+          }
+          tc::commit(&bars[B_MDONE + s]);
+          return true;
+        };
+        issue_tiles(NT, 0);
+        if (NT > 1) issue_tiles(NT + 1, 1);
+        if (mma_b(0)) {
+          for (int kt = 0; kt < NT && ok; ++kt) {
+            if (kt + 1 < NT && !mma_b(kt + 1)) break;
+            if (kt + 2 < NT) {
+              if (!pwait(B_EDONE + (kt & 1), (kt >> 1) & 1)) break;
+              issue_tiles(NT + kt + 2, kt + 2);
+            }
+          }
+        }
+      }
+    }
+  } else {
+    // ======================= consumers (warps 0-7) =======================
+    const uint32_t lane_base = (uint32_t)(32 * (warp & 3)) << 16;
+    const int row = 32 * (warp & 3) + lane, half = warp >> 2;
+    bool ok = true;
+    auto cwait = [&](int b, uint32_t par) {
+      bool mine = ok && !*fail && tc::mbar_wait(&bars[b], par, MAX_POLLS);
+      const bool all = consumers_all(mine);
+      if (!all) { if (ok && tid == 0) record_timeout(); ok = false; *fail = 1; }
+      return ok;
+    };
+    auto zero_bad_rows = [&](unsigned char* w) {
+      for (int e = tid; e < R2 * (KT / 8); e += CONS) {
+        const int r = e % R2, cc = e / R2;
+        if ((bad >> tok(r)) & 1ull) *reinterpret_cast<uint4*>(w + kmaj(r, cc * 8, R2)) = make_uint4(0, 0, 0, 0);
+      }
+    };
+    // ---- phase A: split the state tiles
+    for (int kt = 0; kt < NT && ok; ++kt) {
+      const int g = kt, s = g & 1;
+      if (!cwait(B_TFULL + s, (g >> 1) & 1)) break;
+      if (kt >= 2 && !cwait(B_MDONE + s, ((g - 2) >> 1) & 1)) break;
+      if (patch_w) zero_bad_rows(stageW(s));
+      unsigned char* hh = splitH(s);
+      unsigned char* hl = hh + H_TILE;
+      const unsigned char* hr = stageHr(s);
+      const unsigned char* hi = stageHi(s);
+#pragma unroll
+      for (int u = 0; u < (KT * (N2 / 8)) / CONS; ++u) {
+        const int e = tid + CONS * u;
+        const int i = e % KT, gg = e / KT;        // row i, 8-column group gg (0-3 re, 4-7 im)
+        float x[8];
+        if (src_identity) {
+          const int gi = kt * KT + i, col = j0 + (gg & 3) * 8;
+#pragma unroll
+          for (int jj = 0; jj < 8; ++jj) x[jj] = (gg < 4 && gi == col + jj) ? 1.f : 0.f;
+        } else {
+          const unsigned char* box = gg < 4 ? hr : hi;
+          const int c0 = 2 * (gg & 3);
+          const float4 a = *reinterpret_cast<const float4*>(box + i * 128 + (((c0) ^ (i & 7)) << 4));
+          const float4 b = *reinterpret_cast<const float4*>(box + i * 128 + (((c0 + 1) ^ (i & 7)) << 4));
+          x[0] = a.x; x[1] = a.y; x[2] = a.z; x[3] = a.w; x[4] = b.x; x[5] = b.y; x[6] = b.z; x[7] = b.w;
+        }
+        uint4 h, l;
+        tc::split8(x, h, l);
+        *reinterpret_cast<uint4*>(hh + mnmaj(i, gg * 8, N2 / 8)) = h;
+        *reinterpret_cast<uint4*>(hl + mnmaj(i, gg * 8, N2 / 8)) = l;
+      }
+      tc::fence_proxy_async();
+      tc::named_sync(1, CONS);
+      if (tid == 0) tc::mbar_arrive(&bars[B_SFULL + s]);
+    }
+    // ---- phase T: Z -> operand
+    if (ok && cwait(B_MDONE + ((NT - 1) & 1), ((NT - 1) >> 1) & 1)) {
+      tc::fence_after_sync();
+      float z[32];
+      tc::tmem_ld16(tZ + lane_base + 32 * half, z);
+      tc::tmem_ld16(tZ + lane_base + 32 * half + 16, z + 16);
+#pragma unroll
+      for (int g4 = 0; g4 < 4; ++g4) {
+        uint4 h, l;
+        tc::split8(z + 8 * g4, h, l);
+        const int off = mnmaj(row, 32 * half + 8 * g4, N2 / 8);
+        *reinterpret_cast<uint4*>(sZh + off) = h;
+        *reinterpret_cast<uint4*>(sZl + off) = l;
+      }
+      tc::fence_proxy_async();
+      tc::fence_before_sync();
+      tc::named_sync(1, CONS);
+      if (tid == 0) tc::mbar_arrive(&bars[B_ZREADY]);
+    }
+    // ---- phase E: Cm -> operands, Y, then E partial
+    if (ok && cwait(B_MT, 0)) {
+      tc::fence_after_sync();
+      float p1r[16], p1i[16], p2r[16], p2i[16];
+      tc::tmem_ld16(tP1 + lane_base + 16 * half, p1r);
+      tc::tmem_ld16(tP1 + lane_base + 32 + 16 * half, p1i);
+      tc::tmem_ld16(tP2 + lane_base + 16 * half, p2r);
+      tc::tmem_ld16(tP2 + lane_base + 32 + 16 * half, p2i);
+      float cr[16], ci[16];
+#pragma unroll
+      for (int j = 0; j < 16; ++j) { cr[j] = p1r[j] - p2i[j]; ci[j] = p1i[j] + p2r[j]; }
+#pragma unroll
+      for (int g2 = 0; g2 < 2; ++g2) {
+        uint4 h, l;
+        const int jc = 16 * half + 8 * g2;
+        tc::split8(cr + 8 * g2, h, l);
+        *reinterpret_cast<uint4*>(sCh + mnmaj(row, jc, N2 / 8)) = h;
+        *reinterpret_cast<uint4*>(sCl + mnmaj(row, jc, N2 / 8)) = l;
+        *reinterpret_cast<uint4*>(sAh + kmaj(row, jc, R2)) = h;
+        *reinterpret_cast<uint4*>(sAl + kmaj(row, jc, R2)) = l;
+        tc::split8(ci + 8 * g2, h, l);
+        *reinterpret_cast<uint4*>(sCh + mnmaj(row, NB2 + jc, N2 / 8)) = h;
+        *reinterpret_cast<uint4*>(sCl + mnmaj(row, NB2 + jc, N2 / 8)) = l;
+      }
+      {
+        const int t = tid % C2, gq = tid / C2;   // 64 tokens x 4 groups of 8 columns
+        uint4 u = make_uint4(0, 0, 0, 0);
+        if (t < nt) u = *reinterpret_cast<const uint4*>(q + ((size_t)item * S + t0 + t) * D + j0 + gq * 8);
+        *reinterpret_cast<uint4*>(sY + kmaj(t, gq * 8, C2)) = u;
+      }
+      tc::fence_proxy_async();
+      tc::fence_before_sync();
+      tc::named_sync(1, CONS);
+      if (tid == 0) tc::mbar_arrive(&bars[B_CREADY]);
+    }
+    if (ok && cwait(B_ME, 0)) {
+      tc::fence_after_sync();
+      float e[32];
+      tc::tmem_ld16(tE + lane_base + 32 * half, e);
+      tc::tmem_ld16(tE + lane_base + 32 * half + 16, e + 16);
+      float* Eo = Ews + chunk * R2 * C2 + (size_t)row * C2 + 32 * half;
+#pragma unroll
+      for (int t = 0; t < 32; ++t) atomicAdd(Eo + t, e[t]);
+    }
+    // ---- phase B: epilogues
+    for (int kt = 0; kt < NT && ok; ++kt) {
+      const int g = NT + kt, s = g & 1, d = kt & 1;
+      if (!cwait(B_TFULL + s, (g >> 1) & 1)) break;
+      if (patch_w) {
+        zero_bad_rows(stageW(s));
+        tc::fence_proxy_async();
+        tc::named_sync(1, CONS);
+        if (tid == 0) tc::mbar_arrive(&bars[B_WFIX + d]);
+      }
+      if (!cwait(B_MDONE + s, (g >> 1) & 1)) break;
+      tc::fence_after_sync();
+      const int gi = kt * KT + row;
+      float hv[32];
+      if (src_identity) {
+#pragma unroll
+        for (int jj = 0; jj < 32; ++jj) hv[jj] = (!half && gi == j0 + jj) ? 1.f : 0.f;
+      } else {
+        const unsigned char* box = half ? stageHi(s) : stageHr(s);
+#pragma unroll
+        for (int cc = 0; cc < 8; ++cc) {
+          const float4 a = *reinterpret_cast<const float4*>(box + row * 128 + ((cc ^ (row & 7)) << 4));
+          hv[4 * cc] = a.x; hv[4 * cc + 1] = a.y; hv[4 * cc + 2] = a.z; hv[4 * cc + 3] = a.w;
+        }
+      }
+      float dh[32];
+      tc::tmem_ld16(tDH + 64 * d + lane_base + 32 * half, dh);
+      tc::tmem_ld16(tDH + 64 * d + lane_base + 32 * half + 16, dh + 16);
+      float* dst = (half ? dst_i : dst_r) + (size_t)item * D * D + (size_t)gi * D + j0;
+#pragma unroll
+      for (int cc = 0; cc < 8; ++cc)
+        *reinterpret_cast<float4*>(dst + 4 * cc) =
+            make_float4(hv[4 * cc] + dh[4 * cc], hv[4 * cc + 1] + dh[4 * cc + 1], hv[4 * cc + 2] + dh[4 * cc + 2],
+                        hv[4 * cc + 3] + dh[4 * cc + 3]);
+      tc::fence_before_sync();
+      tc::named_sync(1, CONS);
+      if (tid == 0) tc::mbar_arrive(&bars[B_EDONE + d]);
+    }
+  }
+  tc::fence_before_sync();
+  __syncthreads();
+  if (warp == 0) tc::tmem_dealloc(tbase, 512);
+}
+
+// Tensor maps for the warp-specialised colpass (driver entry point resolved once).
+PFN_cuTensorMapEncodeTiled_v12000 tmap_encoder() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult qr;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &qr) == cudaSuccess &&
+        qr == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+// k or v as a [b][S][D] bf16 tensor, boxes of 8 elements x 64 tokens (rows past S read as 0)
+int make_kv_map(CUtensorMap* m, const void* base, int b, int S, int D) {
+  auto enc = tmap_encoder();
+  VERACE_REQUIRE(enc != nullptr, VERACE_ERR_CUDA, "cuTensorMapEncodeTiled is not available");
+  const cuuint64_t dims[3] = {(cuuint64_t)D, (cuuint64_t)S, (cuuint64_t)b};
+  const cuuint64_t strides[2] = {(cuuint64_t)D * 2, (cuuint64_t)S * D * 2};
+  const cuuint32_t box[3] = {8, (cuuint32_t)C2, 1};
+  const cuuint32_t es[3] = {1, 1, 1};
+  CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box, es,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  VERACE_REQUIRE(r == CUDA_SUCCESS, VERACE_ERR_CUDA, "cuTensorMapEncodeTiled (k/v) failed: %d", (int)r);
+  return VERACE_OK;
+}
+
+// one plane of a [b][D][D] fp32 state as [b*D rows][D], boxes of 32 columns x 128 rows, 128B swizzle
+int make_state_map(CUtensorMap* m, const float* base, int b, int D) {
+  auto enc = tmap_encoder();
+  VERACE_REQUIRE(enc != nullptr, VERACE_ERR_CUDA, "cuTensorMapEncodeTiled is not available");
+  const cuuint64_t dims[2] = {(cuuint64_t)D, (cuuint64_t)b * D};
+  const cuuint64_t strides[1] = {(cuuint64_t)D * 4};
+  const cuuint32_t box[2] = {32, (cuuint32_t)KT};
+  const cuuint32_t es[2] = {1, 1};
+  CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(base), dims, strides, box, es,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  VERACE_REQUIRE(r == CUDA_SUCCESS, VERACE_ERR_CUDA, "cuTensorMapEncodeTiled (state) failed: %d", (int)r);
+  return VERACE_OK;
+}
+
 size_t tc_prep_smem() { return sizeof(float) * (PREP_DT * (R2 + 1) + 3 * R2 * (R2 + 1)); }
 
 template <typename T>
@@ -750,13 +1163,33 @@ int launch_cham_tc(const void* q, const void* k, const void* v, const float* gam
   const dim3 gc(D / NB2, b), gr(D / R2, b);
   const float* cur_r = nullptr;
   const float* cur_i = nullptr;
+  constexpr bool WS = sizeof(T) == 2;   // bf16: warp-specialised TMA colpass
+  CUtensorMap mk, mv, m_out_r, m_out_i, m_ping_r, m_ping_i;
+  if (WS) {
+    VERACE_CUDA(cudaFuncSetAttribute(cham_tc_colpass_ws, cudaFuncAttributeMaxDynamicSharedMemorySize, WS_SMEM));
+    if ((rc = make_kv_map(&mk, k, b, s, D)) || (rc = make_kv_map(&mv, v, b, s, D)) ||
+        (rc = make_state_map(&m_out_r, hr, b, D)) || (rc = make_state_map(&m_out_i, hi, b, D)))
+      return rc;
+    if (nch >= 2 && ((rc = make_state_map(&m_ping_r, w.Hre, b, D)) || (rc = make_state_map(&m_ping_i, w.Him, b, D))))
+      return rc;
+    if (nch < 2) { m_ping_r = m_out_r; m_ping_i = m_out_i; }
+  }
   for (int c = 0; c < nch; ++c) {
     const bool to_out = ((nch - 1 - c) % 2) == 0;
     float* dr = to_out ? hr : w.Hre;
     float* di = to_out ? hi : w.Him;
-    cham_tc_colpass<T><<<gc, THR, CPS, st>>>((const T*)q, (const T*)k, (const T*)v, w.T, w.E, w.bad,
-                                                      cur_r, cur_i, dr, di, s, D, nch, c);
-    if ((rc = check_launch("cham_tc_colpass"))) return rc;
+    if (WS) {
+      // source planes of chunk c: identity (c == 0) or the buffer chunk c-1 wrote
+      const bool src_out = c > 0 && ((nch - c) % 2) == 0;
+      cham_tc_colpass_ws<<<gc, WS_THREADS, WS_SMEM, st>>>(
+          mk, mv, src_out ? m_out_r : m_ping_r, src_out ? m_out_i : m_ping_i, (const __nv_bfloat16*)q, w.T, w.E,
+          w.bad, c == 0 ? 1 : 0, dr, di, s, D, nch, c);
+      if ((rc = check_launch("cham_tc_colpass_ws"))) return rc;
+    } else {
+      cham_tc_colpass<T><<<gc, THR, CPS, st>>>((const T*)q, (const T*)k, (const T*)v, w.T, w.E, w.bad,
+                                                        cur_r, cur_i, dr, di, s, D, nch, c);
+      if ((rc = check_launch("cham_tc_colpass"))) return rc;
+    }
     cham_tc_readout<T><<<gr, THR, READOUT_SMEM, st>>>((const T*)q, (const T*)k, (const T*)v, w.E, w.bad,
                                                       cur_r, (T*)out, s, D, nch, c);
     if ((rc = check_launch("cham_tc_readout"))) return rc;
