@@ -836,10 +836,12 @@ cham_tc_colpass_ws(const __grid_constant__ CUtensorMap tm_k, const __grid_consta
         const int s = g & 1;
         tc::mbar_expect_tx(&bars[B_TFULL + s], W_TILE + (src_identity ? 0 : 2 * 16 * 1024));
         unsigned char* w = stageW(s);
-#pragma unroll 1
-        for (int cc = 0; cc < KT / 8; ++cc) {
-          tc::tma_load_3d(w + cc * 2048, &tm_k, kt * KT + cc * 8, t0, item, &bars[B_TFULL + s]);
-          tc::tma_load_3d(w + cc * 2048 + 1024, &tm_v, kt * KT + cc * 8, t0, item, &bars[B_TFULL + s]);
+        // W tile in the 128-byte-swizzled K-major layout: [element block of 64][row r][128 B],
+        // rows 0-63 = k of the chunk's tokens, 64-127 = v
+#pragma unroll
+        for (int kb = 0; kb < KT / 64; ++kb) {
+          tc::tma_load_3d(w + kb * 16384, &tm_k, kt * KT + kb * 64, t0, item, &bars[B_TFULL + s]);
+          tc::tma_load_3d(w + kb * 16384 + 8192, &tm_v, kt * KT + kb * 64, t0, item, &bars[B_TFULL + s]);
         }
         if (!src_identity) {
           tc::tma_load_2d(stageHr(s), &tm_sr, j0, item * D + kt * KT, &bars[B_TFULL + s]);
@@ -859,7 +861,7 @@ cham_tc_colpass_ws(const __grid_constant__ CUtensorMap tm_k, const __grid_consta
         const uint32_t bh = tc::smem_addr(splitH(s)), bl = bh + H_TILE;
 #pragma unroll 1
         for (int ks = 0; ks < KT / 16; ++ks) {
-          const uint64_t a = tc::sdesc(aw + ks * 2 * R2 * 16, R2 * 16, 128);
+          const uint64_t a = tc::sdesc_sw128(aw + (ks >> 2) * 16384 + (ks & 3) * 32, 16, 1024);
           tc::mma_bf16(tZ, a, tc::sdesc(bh + ks * 2 * (N2 / 8) * 128, (N2 / 8) * 128, 128), ID_Z,
                        (kt > 0 || ks > 0) ? 1u : 0u);
           tc::mma_bf16(tZ, a, tc::sdesc(bl + ks * 2 * (N2 / 8) * 128, (N2 / 8) * 128, 128), ID_Z, 1u);
@@ -922,7 +924,7 @@ cham_tc_colpass_ws(const __grid_constant__ CUtensorMap tm_k, const __grid_consta
           const uint32_t ch = tc::smem_addr(sCh), cl = tc::smem_addr(sCl);
 #pragma unroll 1
           for (int ks = 0; ks < R2 / 16; ++ks) {
-            const uint64_t a = tc::sdesc(aw + ks * 256, 128, R2 * 16);
+            const uint64_t a = tc::sdesc_sw128(aw + ks * 2048, 16384, 1024);
             tc::mma_bf16(tDH + 64 * d, a, tc::sdesc(ch + ks * 2 * (N2 / 8) * 128, (N2 / 8) * 128, 128), ID_H,
                          ks > 0 ? 1u : 0u);
             tc::mma_bf16(tDH + 64 * d, a, tc::sdesc(cl + ks * 2 * (N2 / 8) * 128, (N2 / 8) * 128, 128), ID_H, 1u);
@@ -954,10 +956,12 @@ cham_tc_colpass_ws(const __grid_constant__ CUtensorMap tm_k, const __grid_consta
       if (!all) { if (ok && tid == 0) record_timeout(); ok = false; *fail = 1; }
       return ok;
     };
-    auto zero_bad_rows = [&](unsigned char* w) {
+    auto zero_bad_rows = [&](unsigned char* w) {   // swizzled W tile
       for (int e = tid; e < R2 * (KT / 8); e += CONS) {
-        const int r = e % R2, cc = e / R2;
-        if ((bad >> tok(r)) & 1ull) *reinterpret_cast<uint4*>(w + kmaj(r, cc * 8, R2)) = make_uint4(0, 0, 0, 0);
+        const int r = e % R2, cc = e / R2;             // 16-byte chunk cc of row r
+        if ((bad >> tok(r)) & 1ull)
+          *reinterpret_cast<uint4*>(w + (cc >> 3) * 16384 + r * 128 + (((cc & 7) ^ (r & 7)) << 4)) =
+              make_uint4(0, 0, 0, 0);
       }
     };
     // ---- phase A: split the state tiles
@@ -1116,16 +1120,17 @@ PFN_cuTensorMapEncodeTiled_v12000 tmap_encoder() {
   return fn;
 }
 
-// k or v as a [b][S][D] bf16 tensor, boxes of 8 elements x 64 tokens (rows past S read as 0)
+// k or v as a [b][S][D] bf16 tensor, boxes of 64 elements x 64 tokens with 128-byte swizzle
+// (rows past S read as 0)
 int make_kv_map(CUtensorMap* m, const void* base, int b, int S, int D) {
   auto enc = tmap_encoder();
   VERACE_REQUIRE(enc != nullptr, VERACE_ERR_CUDA, "cuTensorMapEncodeTiled is not available");
   const cuuint64_t dims[3] = {(cuuint64_t)D, (cuuint64_t)S, (cuuint64_t)b};
   const cuuint64_t strides[2] = {(cuuint64_t)D * 2, (cuuint64_t)S * D * 2};
-  const cuuint32_t box[3] = {8, (cuuint32_t)C2, 1};
+  const cuuint32_t box[3] = {64, (cuuint32_t)C2, 1};
   const cuuint32_t es[3] = {1, 1, 1};
   CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box, es,
-                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   VERACE_REQUIRE(r == CUDA_SUCCESS, VERACE_ERR_CUDA, "cuTensorMapEncodeTiled (k/v) failed: %d", (int)r);
   return VERACE_OK;

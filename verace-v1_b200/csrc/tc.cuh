@@ -39,6 +39,16 @@ __device__ __forceinline__ uint64_t sdesc(uint32_t saddr, uint32_t lbo, uint32_t
   return d;
 }
 
+// Shared-memory matrix descriptor for the 128-byte-swizzled canonical layouts (atoms of
+// 8 rows x 128 bytes, 1024-byte aligned; the hardware XORs address bits [4,7) with
+// bits [7,10)).  K-major: rows of 64 bf16 k-elements, SBO = 1024 between 8-row groups,
+// LBO unused (16); a K step of 16 inside an atom adds 32 bytes to the start address.
+// MN-major: 64 contiguous m-elements per 128-byte row, rows are k; SBO = 1024 between
+// 8-k-row groups, LBO = byte distance between 64-element m blocks.
+__device__ __forceinline__ uint64_t sdesc_sw128(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
+  return sdesc(saddr, lbo, sbo) | ((uint64_t)2u << 61);
+}
+
 // Instruction descriptor for kind::f16 with bf16 A/B and an fp32 accumulator.
 __host__ __device__ constexpr uint32_t idesc_bf16(int M, int N, bool a_mn_major, bool b_mn_major,
                                                   bool negate_a = false) {
