@@ -781,12 +781,11 @@ __device__ __forceinline__ bool consumers_all(bool ok) {
   return r != 0;
 }
 
-__global__ void __launch_bounds__(WS_THREADS, 1)
-cham_tc_colpass_ws(const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
-                   const __grid_constant__ CUtensorMap tm_sr, const __grid_constant__ CUtensorMap tm_si,
-                   const __nv_bfloat16* __restrict__ q, const unsigned char* __restrict__ Tws,
-                   float* __restrict__ Ews, const unsigned long long* __restrict__ badws, int src_identity,
-                   float* __restrict__ dst_r, float* __restrict__ dst_i, int S, int D, int nch, int c) {
+__device__ __forceinline__ void
+colpass_ws_body(const CUtensorMap& tm_k, const CUtensorMap& tm_v, const CUtensorMap& tm_sr,
+                const CUtensorMap& tm_si, const __nv_bfloat16* __restrict__ q, const unsigned char* __restrict__ Tws,
+                float* __restrict__ Ews, const unsigned long long* __restrict__ badws, int src_identity,
+                float* __restrict__ dst_r, float* __restrict__ dst_i, int S, int D, int nch, int c, int bx) {
   extern __shared__ __align__(1024) unsigned char smw[];
   uint64_t* bars = reinterpret_cast<uint64_t*>(smw + WS_BAR);
   uint32_t* tslot = reinterpret_cast<uint32_t*>(smw + WS_BAR + 8 * N_BARS);
@@ -804,7 +803,7 @@ cham_tc_colpass_ws(const __grid_constant__ CUtensorMap tm_k, const __grid_consta
   unsigned char* sY = smw + 2 * CA_TILE;
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int item = blockIdx.y, j0 = blockIdx.x * NB2;
+  const int item = blockIdx.y, j0 = bx * NB2;
   const int t0 = c * C2, nt = min(C2, S - t0);
   const size_t chunk = (size_t)item * nch + c;
   const unsigned long long bad = badws[chunk];
@@ -1106,6 +1105,211 @@ cham_tc_colpass_ws(const __grid_constant__ CUtensorMap tm_k, const __grid_consta
   if (warp == 0) tc::tmem_dealloc(tbase, 512);
 }
 
+// ---------------------------------------------------------------------------------
+// Warp-specialised readout for bf16 inputs, run in the same launch as the next chunk's
+// colpass.  It reads the chunk's END state S_end (the next colpass's source) and uses
+//     rec_t = Re(S_end y_t) - sum_{tau > t} U_tau E[tau, t]
+// (S_t = S_end minus the later tokens' rank-2 terms).  One CTA per (item, 128 rows):
+// producer = TMA (state rows as swizzled fp32 boxes, Y and W as swizzled bf16 boxes) +
+// tcgen05 issue; consumers = fp32 -> bf16 hi/lo split of the state rows, the masked E
+// operand and the output epilogue.
+// smem: stage s at s*48K = state rows [128][64] fp32 (2 boxes, 32K) | Y [64 tok][64] (8K)
+//       A split [2] at 96K (hi 16K | lo 16K each); phase 2: W (32K) at 0, E split at 160K
+// TMEM: O [0,64)
+constexpr int RW_STAGE = 48 * 1024, RW_AS = 96 * 1024, RW_E = 160 * 1024;
+constexpr int RKT = 64;   // state columns per K tile
+
+__device__ __forceinline__ void
+readout_ws_body(const CUtensorMap& tm_k, const CUtensorMap& tm_v, const CUtensorMap& tm_q,
+                const CUtensorMap& tm_sr, const float* __restrict__ Ews,
+                const unsigned long long* __restrict__ badws, __nv_bfloat16* __restrict__ out,
+                int S, int D, int nch, int c, int bx) {
+  extern __shared__ __align__(1024) unsigned char smw[];
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smw + WS_BAR);
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(smw + WS_BAR + 8 * N_BARS);
+  volatile int* fail = reinterpret_cast<volatile int*>(smw + WS_BAR + 8 * N_BARS + 16);
+  auto stA = [&](int s) { return smw + s * RW_STAGE; };
+  auto stY = [&](int s) { return smw + s * RW_STAGE + 32 * 1024; };
+  auto splitA = [&](int s) { return smw + RW_AS + s * 32 * 1024; };
+  unsigned char* sW = smw;
+  unsigned char* sEh = smw + RW_E;
+  unsigned char* sEl = sEh + 16 * 1024;
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int item = blockIdx.y, i0 = bx * R2;
+  const int t0 = c * C2, nt = min(C2, S - t0);
+  const size_t chunk = (size_t)item * nch + c;
+  const unsigned long long bad = badws[chunk];
+  const int NTR = D / RKT;
+
+  if (warp == 0) tc::tmem_alloc(tslot, 64);
+  if (tid == 0) {
+    for (int i = 0; i < N_BARS; ++i) tc::mbar_init(&bars[i], 1);
+    *fail = 0;
+    tc::fence_mbar_init();
+  }
+  tc::fence_before_sync();
+  __syncthreads();
+  tc::fence_after_sync();
+  const uint32_t tO = *tslot;
+
+  if (warp == 8) {
+    if (lane == 0) {
+      bool ok = true;
+      auto pwait = [&](int b, uint32_t par) {
+        if (!ok) return false;
+        if (*fail || !tc::mbar_wait(&bars[b], par, MAX_POLLS)) { ok = false; *fail = 1; record_timeout(); }
+        return ok;
+      };
+      auto issue = [&](int kt) {
+        const int s = kt & 1;
+        tc::mbar_expect_tx(&bars[B_TFULL + s], 32 * 1024 + 8 * 1024);
+        tc::tma_load_2d(stA(s), &tm_sr, kt * RKT, item * D + i0, &bars[B_TFULL + s]);
+        tc::tma_load_2d(stA(s) + 16 * 1024, &tm_sr, kt * RKT + 32, item * D + i0, &bars[B_TFULL + s]);
+        tc::tma_load_3d(stY(s), &tm_q, kt * RKT, t0, item, &bars[B_TFULL + s]);
+      };
+      constexpr uint32_t ID_O = tc::idesc_bf16(128, C2, false, false);
+      issue(0);
+      if (NTR > 1) issue(1);
+      for (int kt = 0; kt < NTR && ok; ++kt) {
+        const int s = kt & 1;
+        if (!pwait(B_TFULL + s, (kt >> 1) & 1) || !pwait(B_SFULL + s, (kt >> 1) & 1)) break;
+        tc::fence_after_sync();
+        const uint32_t ah = tc::smem_addr(splitA(s)), al = ah + 16 * 1024;
+        const uint32_t y = tc::smem_addr(stY(s));
+#pragma unroll 1
+        for (int ks = 0; ks < RKT / 16; ++ks) {
+          const uint64_t b = tc::sdesc_sw128(y + ks * 32, 16, 1024);
+          tc::mma_bf16(tO, tc::sdesc(ah + ks * 2 * R2 * 16, R2 * 16, 128), b, ID_O, (kt > 0 || ks > 0) ? 1u : 0u);
+          tc::mma_bf16(tO, tc::sdesc(al + ks * 2 * R2 * 16, R2 * 16, 128), b, ID_O, 1u);
+        }
+        tc::commit(&bars[B_MDONE + s]);
+        if (kt + 2 < NTR) {
+          if (!pwait(B_MDONE + s, (kt >> 1) & 1)) break;
+          issue(kt + 2);
+        }
+      }
+      // W rows [i0, i0+128) of the chunk (k block, v block), then O -= W mask(E)
+      if (ok && pwait(B_MDONE + ((NTR - 1) & 1), ((NTR - 1) >> 1) & 1)) {
+        tc::mbar_expect_tx(&bars[B_TT], W_TILE);
+#pragma unroll
+        for (int kb = 0; kb < R2 / 64; ++kb) {
+          tc::tma_load_3d(sW + kb * 16384, &tm_k, i0 + kb * 64, t0, item, &bars[B_TT]);
+          tc::tma_load_3d(sW + kb * 16384 + 8192, &tm_v, i0 + kb * 64, t0, item, &bars[B_TT]);
+        }
+        if (pwait(B_TT, 0) && pwait(B_CREADY, 0)) {
+          tc::fence_after_sync();
+          constexpr uint32_t ID_W = tc::idesc_bf16(128, C2, true, true);
+          const uint32_t aw = tc::smem_addr(sW), eh = tc::smem_addr(sEh), el = tc::smem_addr(sEl);
+#pragma unroll 1
+          for (int ks = 0; ks < R2 / 16; ++ks) {
+            const uint64_t a = tc::sdesc_sw128(aw + ks * 2048, 16384, 1024);
+            tc::mma_bf16(tO, a, tc::sdesc(eh + ks * 2 * (C2 / 8) * 128, (C2 / 8) * 128, 128), ID_W, 1u);
+            tc::mma_bf16(tO, a, tc::sdesc(el + ks * 2 * (C2 / 8) * 128, (C2 / 8) * 128, 128), ID_W, 1u);
+          }
+          tc::commit(&bars[B_ME]);
+        }
+      }
+    }
+  } else {
+    const uint32_t lane_base = (uint32_t)(32 * (warp & 3)) << 16;
+    const int row = 32 * (warp & 3) + lane, half = warp >> 2;
+    bool ok = true;
+    auto cwait = [&](int b, uint32_t par) {
+      bool mine = ok && !*fail && tc::mbar_wait(&bars[b], par, MAX_POLLS);
+      const bool all = consumers_all(mine);
+      if (!all) { if (ok && tid == 0) record_timeout(); ok = false; *fail = 1; }
+      return ok;
+    };
+    for (int kt = 0; kt < NTR && ok; ++kt) {
+      const int s = kt & 1;
+      if (!cwait(B_TFULL + s, (kt >> 1) & 1)) break;
+      if (kt >= 2 && !cwait(B_MDONE + s, ((kt - 2) >> 1) & 1)) break;
+      unsigned char* ah = splitA(s);
+      unsigned char* al = ah + 16 * 1024;
+      const unsigned char* a = stA(s);
+#pragma unroll
+      for (int u = 0; u < (R2 * (RKT / 8)) / CONS; ++u) {
+        const int e = tid + CONS * u;
+        const int i = e % R2, gg = e / R2;                 // row i, columns 8*gg .. 8*gg+7
+        const unsigned char* box = a + (gg >> 2) * 16384;
+        const int c0 = 2 * (gg & 3);
+        const float4 x0 = *reinterpret_cast<const float4*>(box + i * 128 + ((c0 ^ (i & 7)) << 4));
+        const float4 x1 = *reinterpret_cast<const float4*>(box + i * 128 + (((c0 + 1) ^ (i & 7)) << 4));
+        const float x[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+        uint4 h, l;
+        tc::split8(x, h, l);
+        *reinterpret_cast<uint4*>(ah + kmaj(i, gg * 8, R2)) = h;
+        *reinterpret_cast<uint4*>(al + kmaj(i, gg * 8, R2)) = l;
+      }
+      tc::fence_proxy_async();
+      tc::named_sync(1, CONS);
+      if (tid == 0) tc::mbar_arrive(&bars[B_SFULL + s]);
+    }
+    if (ok) {
+      // -mask(E): keep later tokens (tok(r) > t), zero tokens that are non-finite
+      const float* Ein = Ews + chunk * R2 * C2;
+#pragma unroll
+      for (int u = 0; u < (R2 * (C2 / 8)) / CONS; ++u) {
+        const int e = tid + CONS * u;
+        const int gq = e % (C2 / 8), r = e / (C2 / 8);
+        float x[8];
+        load8(Ein + (size_t)r * C2 + gq * 8, x);
+#pragma unroll
+        for (int jj = 0; jj < 8; ++jj) x[jj] = (tok(r) > gq * 8 + jj) ? -x[jj] : 0.f;
+        uint4 h, l;
+        tc::split8(x, h, l);
+        *reinterpret_cast<uint4*>(sEh + mnmaj(r, gq * 8, C2 / 8)) = h;
+        *reinterpret_cast<uint4*>(sEl + mnmaj(r, gq * 8, C2 / 8)) = l;
+      }
+      // rows of non-finite tokens must not reach the product (their E rows are 0, and
+      // 0 x inf is NaN): zero them in the W tile once it has landed
+      if (cwait(B_TT, 0) && bad) {
+        for (int e = tid; e < R2 * (R2 / 8); e += CONS) {
+          const int r = e % R2, cc = e / R2;
+          if ((bad >> tok(r)) & 1ull)
+            *reinterpret_cast<uint4*>(sW + (cc >> 3) * 16384 + r * 128 + (((cc & 7) ^ (r & 7)) << 4)) =
+                make_uint4(0, 0, 0, 0);
+        }
+      }
+      tc::fence_proxy_async();
+      tc::named_sync(1, CONS);
+      if (ok && tid == 0) tc::mbar_arrive(&bars[B_CREADY]);
+    }
+    if (ok && cwait(B_ME, 0)) {
+      tc::fence_after_sync();
+      float o[32];
+      tc::tmem_ld16(tO + lane_base + 32 * half, o);
+      tc::tmem_ld16(tO + lane_base + 32 * half + 16, o + 16);
+#pragma unroll
+      for (int u = 0; u < 32; ++u) {
+        const int t = 32 * half + u;
+        if (t < nt) out[((size_t)item * S + t0 + t) * D + i0 + row] = __float2bfloat16_rn(o[u]);
+      }
+    }
+  }
+  tc::fence_before_sync();
+  __syncthreads();
+  if (warp == 0) tc::tmem_dealloc(tO, 64);
+}
+
+// One launch per chunk step c: colpass of chunk c (blocks [0, ncol)) and readout of chunk
+// c-1 (the remaining blocks); both read the state at the start of chunk c.
+__global__ void __launch_bounds__(WS_THREADS, 1)
+cham_tc_step_ws(const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
+                const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_sr,
+                const __grid_constant__ CUtensorMap tm_si, const __nv_bfloat16* __restrict__ q,
+                const unsigned char* __restrict__ Tws, float* __restrict__ Ews,
+                const unsigned long long* __restrict__ badws, int src_identity, float* __restrict__ dst_r,
+                float* __restrict__ dst_i, __nv_bfloat16* __restrict__ out, int S, int D, int nch, int c,
+                int ncol) {
+  if ((int)blockIdx.x < ncol)
+    colpass_ws_body(tm_k, tm_v, tm_sr, tm_si, q, Tws, Ews, badws, src_identity, dst_r, dst_i, S, D, nch, c,
+                    blockIdx.x);
+  else
+    readout_ws_body(tm_k, tm_v, tm_q, tm_sr, Ews, badws, out, S, D, nch, c - 1, blockIdx.x - ncol);
+}
+
 // Tensor maps for the warp-specialised colpass (driver entry point resolved once).
 PFN_cuTensorMapEncodeTiled_v12000 tmap_encoder() {
   static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
@@ -1171,7 +1375,6 @@ int launch_cham_tc(const void* q, const void* k, const void* v, const float* gam
   constexpr bool WS = sizeof(T) == 2;   // bf16: warp-specialised TMA colpass
   CUtensorMap mk, mv, m_out_r, m_out_i, m_ping_r, m_ping_i;
   if (WS) {
-    VERACE_CUDA(cudaFuncSetAttribute(cham_tc_colpass_ws, cudaFuncAttributeMaxDynamicSharedMemorySize, WS_SMEM));
     if ((rc = make_kv_map(&mk, k, b, s, D)) || (rc = make_kv_map(&mv, v, b, s, D)) ||
         (rc = make_state_map(&m_out_r, hr, b, D)) || (rc = make_state_map(&m_out_i, hi, b, D)))
       return rc;
@@ -1179,18 +1382,30 @@ int launch_cham_tc(const void* q, const void* k, const void* v, const float* gam
       return rc;
     if (nch < 2) { m_ping_r = m_out_r; m_ping_i = m_out_i; }
   }
+  if (WS) {
+    CUtensorMap mq;
+    if ((rc = make_kv_map(&mq, q, b, s, D))) return rc;
+    VERACE_CUDA(cudaFuncSetAttribute(cham_tc_step_ws, cudaFuncAttributeMaxDynamicSharedMemorySize, WS_SMEM));
+    for (int c = 0; c <= nch; ++c) {
+      const bool to_out = ((nch - 1 - c) % 2) == 0;
+      float* dr = to_out ? hr : w.Hre;
+      float* di = to_out ? hi : w.Him;
+      // state at the start of chunk c: identity (c == 0) or the buffer chunk c-1 wrote
+      const bool src_out = c > 0 && ((nch - c) % 2) == 0;
+      const int ncol = c < nch ? D / NB2 : 0;
+      const int nread = c > 0 ? D / R2 : 0;
+      cham_tc_step_ws<<<dim3(ncol + nread, b), WS_THREADS, WS_SMEM, st>>>(
+          mk, mv, mq, src_out ? m_out_r : m_ping_r, src_out ? m_out_i : m_ping_i, (const __nv_bfloat16*)q, w.T,
+          w.E, w.bad, c == 0 ? 1 : 0, dr, di, (__nv_bfloat16*)out, s, D, nch, c, ncol);
+      if ((rc = check_launch("cham_tc_step_ws"))) return rc;
+    }
+    return VERACE_OK;
+  }
   for (int c = 0; c < nch; ++c) {
     const bool to_out = ((nch - 1 - c) % 2) == 0;
     float* dr = to_out ? hr : w.Hre;
     float* di = to_out ? hi : w.Him;
-    if (WS) {
-      // source planes of chunk c: identity (c == 0) or the buffer chunk c-1 wrote
-      const bool src_out = c > 0 && ((nch - c) % 2) == 0;
-      cham_tc_colpass_ws<<<gc, WS_THREADS, WS_SMEM, st>>>(
-          mk, mv, src_out ? m_out_r : m_ping_r, src_out ? m_out_i : m_ping_i, (const __nv_bfloat16*)q, w.T, w.E,
-          w.bad, c == 0 ? 1 : 0, dr, di, s, D, nch, c);
-      if ((rc = check_launch("cham_tc_colpass_ws"))) return rc;
-    } else {
+    {
       cham_tc_colpass<T><<<gc, THR, CPS, st>>>((const T*)q, (const T*)k, (const T*)v, w.T, w.E, w.bad,
                                                         cur_r, cur_i, dr, di, s, D, nch, c);
       if ((rc = check_launch("cham_tc_colpass"))) return rc;
