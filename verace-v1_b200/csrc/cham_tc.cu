@@ -1293,6 +1293,181 @@ readout_ws_body(const CUtensorMap& tm_k, const CUtensorMap& tm_v, const CUtensor
   if (warp == 0) tc::tmem_dealloc(tO, 64);
 }
 
+// ---------------------------------------------------------------------------------
+// prep for bf16 inputs: the Gram matrix G = W Wᵀ on the tensor cores (W tiles by TMA in
+// the kernels' row order, k block then v block; bf16 inputs are exact, so one product),
+// then N_t, T by block forward substitution (fp32 SIMT) directly in that row order.
+// smem: Gs [128][129] fp32 | W stages (2 x 32K, 1024-aligned) aliased later by Tr | Ti
+constexpr int PW_TR = 67584, PW_TI = PW_TR + R2 * (R2 + 1) * 4;
+constexpr int PREP_WS_SMEM = PW_TI + R2 * (R2 + 1) * 4;
+
+__global__ void __launch_bounds__(THR, 1)
+cham_tc_prep_ws(const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
+                const float* __restrict__ gamma, unsigned char* __restrict__ Tws, float* __restrict__ Ews,
+                unsigned long long* __restrict__ badws, int S, int D, int nch) {
+  extern __shared__ __align__(1024) unsigned char smp[];
+  constexpr int P = R2 + 1;
+  float* Gs = reinterpret_cast<float*>(smp);
+  float* Tr = reinterpret_cast<float*>(smp + PW_TR);
+  float* Ti = reinterpret_cast<float*>(smp + PW_TI);
+  auto stW = [&](int s) { return smp + PW_TR + s * W_TILE; };
+  __shared__ float Ns[C2 * 6];
+  __shared__ unsigned long long bad_bits;
+  __shared__ __align__(8) uint64_t bars[5];   // tfull[2], mdone[2], done
+  __shared__ uint32_t tslot;
+  __shared__ int pfail;
+  const int c = blockIdx.x, item = blockIdx.y, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int t0 = c * C2, nt = min(C2, S - t0);
+  const int NT = D / KT;
+  if (warp == 0) tc::tmem_alloc(&tslot, 128);
+  if (tid == 0) {
+    bad_bits = 0ull;
+    pfail = 0;
+    for (int i = 0; i < 5; ++i) tc::mbar_init(&bars[i], 1);
+    tc::fence_mbar_init();
+  }
+  tc::fence_before_sync();
+  __syncthreads();
+  tc::fence_after_sync();
+  const uint32_t tG = tslot;
+  if (tid == 0) {
+    bool ok = true;
+    auto issue = [&](int kt) {
+      const int s = kt & 1;
+      tc::mbar_expect_tx(&bars[s], W_TILE);
+#pragma unroll
+      for (int kb = 0; kb < KT / 64; ++kb) {
+        tc::tma_load_3d(stW(s) + kb * 16384, &tm_k, kt * KT + kb * 64, t0, item, &bars[s]);
+        tc::tma_load_3d(stW(s) + kb * 16384 + 8192, &tm_v, kt * KT + kb * 64, t0, item, &bars[s]);
+      }
+    };
+    constexpr uint32_t ID_G = tc::idesc_bf16(128, 128, false, false);
+    issue(0);
+    if (NT > 1) issue(1);
+    for (int kt = 0; kt < NT && ok; ++kt) {
+      const int s = kt & 1;
+      if (!tc::mbar_wait(&bars[s], (kt >> 1) & 1, MAX_POLLS)) { ok = false; break; }
+      tc::fence_after_sync();
+      const uint32_t w = tc::smem_addr(stW(s));
+#pragma unroll 1
+      for (int ks = 0; ks < KT / 16; ++ks) {
+        const uint64_t d = tc::sdesc_sw128(w + (ks >> 2) * 16384 + (ks & 3) * 32, 16, 1024);
+        tc::mma_bf16(tG, d, d, ID_G, (kt > 0 || ks > 0) ? 1u : 0u);
+      }
+      tc::commit(&bars[2 + s]);
+      if (kt + 2 < NT) {
+        if (!tc::mbar_wait(&bars[2 + s], (kt >> 1) & 1, MAX_POLLS)) { ok = false; break; }
+        issue(kt + 2);
+      }
+    }
+    if (ok) tc::commit(&bars[4]);
+    else { pfail = 1; record_timeout(); }
+  }
+  const bool got = tc::mbar_wait(&bars[4], 0, MAX_POLLS);
+  if (__syncthreads_or(!got || pfail)) {
+    if (tid == 0) record_timeout();
+  } else {
+    tc::fence_after_sync();
+    {  // G -> Gs: thread = row (TMEM lane), 64 columns per warp half
+      const uint32_t lane_base = (uint32_t)(32 * (warp & 3)) << 16;
+      const int row = 32 * (warp & 3) + lane, half = warp >> 2;
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        float x[16];
+        tc::tmem_ld16(tG + lane_base + 64 * half + 16 * u, x);
+#pragma unroll
+        for (int jj = 0; jj < 16; ++jj) Gs[row * P + 64 * half + 16 * u + jj] = x[jj];
+      }
+    }
+    tc::fence_before_sync();
+    __syncthreads();
+    if (tid < C2) {
+      const int tau = tid;
+      float n00r = 0.f, n00i = 0.f, n01r = 0.f, n01i = 0.f, n11r = 0.f, n11i = 0.f;
+      bool flagged = false;
+      if (tau < nt) {
+        const float kk = Gs[tau * P + tau];
+        const float vv = Gs[(C2 + tau) * P + C2 + tau];
+        const float kv = Gs[tau * P + C2 + tau];
+        const float g = gamma[(size_t)item * S + t0 + tau];
+        const float cc = 0.5f * g;
+        const float dr = 1.f + cc * cc * (kk * vv - kv * kv);
+        const float di = -2.f * cc * kv;
+        const float m2 = dr * dr + di * di;
+        const float fr = 2.f * cc * dr / m2;
+        const float fi = -2.f * cc * di / m2;
+        n00r = fr * (-cc * vv); n00i = fi * (-cc * vv);
+        n11r = fr * (-cc * kk); n11i = fi * (-cc * kk);
+        n01r = fr * (cc * kv) - fi; n01i = fr + fi * (cc * kv);
+        // a non-finite k or v makes its diagonal Gram entries non-finite
+        flagged = !(isfinite(kk) && isfinite(vv) && isfinite(kv) && isfinite(g) && isfinite(n00r) &&
+                    isfinite(n00i) && isfinite(n01r) && isfinite(n01i) && isfinite(n11r) && isfinite(n11i));
+        if (flagged) {
+          n00r = n00i = n01r = n01i = n11r = n11i = 0.f;
+          atomicOr(&bad_bits, 1ull << tau);
+        }
+      }
+      float* n = Ns + tau * 6;
+      n[0] = n00r; n[1] = n00i; n[2] = n01r; n[3] = n01i; n[4] = n11r; n[5] = n11i;
+    }
+    __syncthreads();
+    if (bad_bits) {   // clear the Gram rows/columns of non-finite tokens
+      for (int e = tid; e < R2 * R2; e += THR) {
+        const int r = e / R2, cl = e % R2;
+        if (((bad_bits >> tok(r)) & 1ull) || ((bad_bits >> tok(cl)) & 1ull)) Gs[r * P + cl] = 0.f;
+      }
+      __syncthreads();
+    }
+    if (tid < R2) {
+      const int sg = tid, blk = tok(sg);
+      for (int tp = 0; tp < blk; ++tp) {
+        Tr[tp * P + sg] = 0.f; Ti[tp * P + sg] = 0.f;
+        Tr[(C2 + tp) * P + sg] = 0.f; Ti[(C2 + tp) * P + sg] = 0.f;
+      }
+      for (int t = blk; t < C2; ++t) {
+        float x0r = (sg == t) ? 1.f : 0.f, x0i = 0.f;
+        float x1r = (sg == C2 + t) ? 1.f : 0.f, x1i = 0.f;
+        for (int tp = blk; tp < t; ++tp) {
+          const float a0r = Tr[tp * P + sg], a0i = Ti[tp * P + sg];
+          const float a1r = Tr[(C2 + tp) * P + sg], a1i = Ti[(C2 + tp) * P + sg];
+          const float g00 = Gs[t * P + tp], g01 = Gs[t * P + C2 + tp];
+          const float g10 = Gs[(C2 + t) * P + tp], g11 = Gs[(C2 + t) * P + C2 + tp];
+          x0r += g00 * a0r + g01 * a1r; x0i += g00 * a0i + g01 * a1i;
+          x1r += g10 * a0r + g11 * a1r; x1i += g10 * a0i + g11 * a1i;
+        }
+        const float* n = Ns + t * 6;
+        Tr[t * P + sg] = n[0] * x0r - n[1] * x0i + n[2] * x1r - n[3] * x1i;
+        Ti[t * P + sg] = n[0] * x0i + n[1] * x0r + n[2] * x1i + n[3] * x1r;
+        Tr[(C2 + t) * P + sg] = n[2] * x0r - n[3] * x0i + n[4] * x1r - n[5] * x1i;
+        Ti[(C2 + t) * P + sg] = n[2] * x0i + n[3] * x0r + n[4] * x1i + n[5] * x1r;
+      }
+    }
+    __syncthreads();
+    const size_t chunk = (size_t)item * nch + c;
+    unsigned char* To = Tws + chunk * 4 * T_TILE;
+    for (int e = tid; e < R2 * (R2 / 8); e += THR) {
+      const int r = e % R2, g = e / R2;
+      float xr[8], xi[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) { xr[j] = Tr[r * P + g * 8 + j]; xi[j] = Ti[r * P + g * 8 + j]; }
+      uint4 h, l;
+      const int off = kmaj(r, g * 8, R2);
+      tc::split8(xr, h, l);
+      *reinterpret_cast<uint4*>(To + 0 * T_TILE + off) = h;
+      *reinterpret_cast<uint4*>(To + 1 * T_TILE + off) = l;
+      tc::split8(xi, h, l);
+      *reinterpret_cast<uint4*>(To + 2 * T_TILE + off) = h;
+      *reinterpret_cast<uint4*>(To + 3 * T_TILE + off) = l;
+    }
+    float* Eo = Ews + chunk * R2 * C2;
+    for (int e = tid; e < R2 * C2; e += THR) Eo[e] = 0.f;
+    if (tid == 0) badws[chunk] = bad_bits;
+  }
+  tc::fence_before_sync();
+  __syncthreads();
+  if (warp == 0) tc::tmem_dealloc(tG, 128);
+}
+
 // One launch per chunk step c: colpass of chunk c (blocks [0, ncol)) and readout of chunk
 // c-1 (the remaining blocks); both read the state at the start of chunk c.
 __global__ void __launch_bounds__(WS_THREADS, 1)
@@ -1364,11 +1539,20 @@ int launch_cham_tc(const void* q, const void* k, const void* v, const float* gam
   int rc;
   const size_t ps = tc_prep_smem();
   VERACE_CUDA(cudaFuncSetAttribute(cham_tc_prep<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ps));
+  VERACE_CUDA(cudaFuncSetAttribute(cham_tc_prep_ws, cudaFuncAttributeMaxDynamicSharedMemorySize, PREP_WS_SMEM));
   constexpr int CPS = colpass_smem(sizeof(T) == 4);
   VERACE_CUDA(cudaFuncSetAttribute(cham_tc_colpass<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, CPS));
   VERACE_CUDA(cudaFuncSetAttribute(cham_tc_readout<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, READOUT_SMEM));
-  cham_tc_prep<T><<<dim3(nch, b), THR, ps, st>>>((const T*)k, (const T*)v, gamma, w.T, w.E, w.bad, s, D, nch);
-  if ((rc = check_launch("cham_tc_prep"))) return rc;
+  constexpr bool BF = sizeof(T) == 2;
+  CUtensorMap pk, pv;
+  if (BF) {
+    if ((rc = make_kv_map(&pk, k, b, s, D)) || (rc = make_kv_map(&pv, v, b, s, D))) return rc;
+    cham_tc_prep_ws<<<dim3(nch, b), THR, PREP_WS_SMEM, st>>>(pk, pv, gamma, w.T, w.E, w.bad, s, D, nch);
+    if ((rc = check_launch("cham_tc_prep_ws"))) return rc;
+  } else {
+    cham_tc_prep<T><<<dim3(nch, b), THR, ps, st>>>((const T*)k, (const T*)v, gamma, w.T, w.E, w.bad, s, D, nch);
+    if ((rc = check_launch("cham_tc_prep"))) return rc;
+  }
   const dim3 gc(D / NB2, b), gr(D / R2, b);
   const float* cur_r = nullptr;
   const float* cur_i = nullptr;

@@ -71,15 +71,43 @@ sssd_tc_prep(const T* __restrict__ k, const T* __restrict__ v, const float* __re
   const int t0 = c * C3, nt = min(C3, S - t0);
   if (tid == 0) bad_bits = 0ull;
   __syncthreads();
-  for (int e = tid; e < HD * R3; e += THR3) {
-    const int r = e % R3, i = e / R3, tau = r >> 1;
-    float val = 0.f;
-    if (tau < nt) {
-      const size_t off = ((size_t)(bi * (size_t)S + t0 + tau) * H + hi) * HD + i;
-      val = to_f32((r & 1) ? v[off] : k[off]);
+  {
+    // W^T into Ws[i][r]: each thread takes 8 (vector r, 8 consecutive elements) chunks;
+    // all global loads are issued before any use so their latencies overlap
+    constexpr int PER = (R3 * (HD / 8)) / THR3;
+    float x[PER][8];
+#pragma unroll
+    for (int u = 0; u < PER; ++u) {
+      const int e = tid + THR3 * u, r = e % R3, g = e / R3, tau = r >> 1;
+      if (tau < nt) {
+        const T* src = ((r & 1) ? v : k) + ((size_t)(bi * (size_t)S + t0 + tau) * H + hi) * HD + g * 8;
+        if (sizeof(T) == 2) {
+          const uint4 w = *reinterpret_cast<const uint4*>(src);
+          const __nv_bfloat16* hb = reinterpret_cast<const __nv_bfloat16*>(&w);
+#pragma unroll
+          for (int jj = 0; jj < 8; ++jj) x[u][jj] = __bfloat162float(hb[jj]);
+        } else {
+          const float4 a = *reinterpret_cast<const float4*>(src);
+          const float4 b = *reinterpret_cast<const float4*>(reinterpret_cast<const float*>(src) + 4);
+          x[u][0] = a.x; x[u][1] = a.y; x[u][2] = a.z; x[u][3] = a.w;
+          x[u][4] = b.x; x[u][5] = b.y; x[u][6] = b.z; x[u][7] = b.w;
+        }
+      } else {
+#pragma unroll
+        for (int jj = 0; jj < 8; ++jj) x[u][jj] = 0.f;
+      }
     }
-    Ws[i * P + r] = val;
-    if (!isfinite(val)) atomicOr(&bad_bits, 1ull << tau);
+#pragma unroll
+    for (int u = 0; u < PER; ++u) {
+      const int e = tid + THR3 * u, r = e % R3, g = e / R3;
+      bool fin = true;
+#pragma unroll
+      for (int jj = 0; jj < 8; ++jj) {
+        Ws[(g * 8 + jj) * P + r] = x[u][jj];
+        fin = fin && isfinite(x[u][jj]);
+      }
+      if (!fin) atomicOr(&bad_bits, 1ull << (r >> 1));
+    }
   }
   __syncthreads();
   if (tid < C3 && tid < nt && !isfinite(delta[(size_t)(bi * (size_t)S + t0 + tid) * H + hi]))
