@@ -768,7 +768,7 @@ constexpr int WS_THREADS = CONS + 32;     // + producer warp
 constexpr int WS_HS = 128 * 1024, WS_BAR = 192 * 1024;
 constexpr int WS_SMEM = WS_BAR + 256;
 enum { B_TFULL = 0, B_SFULL = 2, B_MDONE = 4, B_EDONE = 6, B_WFIX = 8, B_TT = 10, B_ZREADY = 11,
-       B_MT = 12, B_CREADY = 13, B_ME = 14, N_BARS = 15 };
+       B_MT = 12, B_CREADY = 13, B_ME = 14, B_DFREE = 15, N_BARS = 17 };
 
 __device__ __forceinline__ bool consumers_all(bool ok) {
   int r;
@@ -783,7 +783,8 @@ __device__ __forceinline__ bool consumers_all(bool ok) {
 
 __device__ __forceinline__ void
 colpass_ws_body(const CUtensorMap& tm_k, const CUtensorMap& tm_v, const CUtensorMap& tm_sr,
-                const CUtensorMap& tm_si, const __nv_bfloat16* __restrict__ q, const unsigned char* __restrict__ Tws,
+                const CUtensorMap& tm_si, const CUtensorMap& tm_dr, const CUtensorMap& tm_di,
+                const __nv_bfloat16* __restrict__ q, const unsigned char* __restrict__ Tws,
                 float* __restrict__ Ews, const unsigned long long* __restrict__ badws, int src_identity,
                 float* __restrict__ dst_r, float* __restrict__ dst_i, int S, int D, int nch, int c, int bx) {
   extern __shared__ __align__(1024) unsigned char smw[];
@@ -796,6 +797,7 @@ colpass_ws_body(const CUtensorMap& tm_k, const CUtensorMap& tm_v, const CUtensor
   auto splitH = [&](int s) { return smw + WS_HS + s * 32 * 1024; };
   unsigned char* sZh = splitH(0);
   unsigned char* sZl = sZh + Z_TILE;
+  unsigned char* sO = splitH(0);   // phase B: updated state tile (re 16K | im 16K, swizzled) for TMA stores
   unsigned char* sCh = splitH(1);
   unsigned char* sCl = sCh + Z_TILE;
   unsigned char* sAh = smw;
@@ -917,7 +919,7 @@ colpass_ws_body(const CUtensorMap& tm_k, const CUtensorMap& tm_v, const CUtensor
           const int g = NT + kt, s = g & 1, d = kt & 1;
           if (!pwait(B_TFULL + s, (g >> 1) & 1)) return false;
           if (patch_w && !pwait(B_WFIX + d, (kt >> 1) & 1)) return false;
-          if (kt >= 2 && !pwait(B_EDONE + d, ((kt - 2) >> 1) & 1)) return false;
+          if (kt >= 2 && !pwait(B_DFREE + d, ((kt - 2) >> 1) & 1)) return false;
           tc::fence_after_sync();
           const uint32_t aw = tc::smem_addr(stageW(s));
           const uint32_t ch = tc::smem_addr(sCh), cl = tc::smem_addr(sCl);
@@ -1057,11 +1059,12 @@ colpass_ws_body(const CUtensorMap& tm_k, const CUtensorMap& tm_v, const CUtensor
       float e[32];
       tc::tmem_ld16(tE + lane_base + 32 * half, e);
       tc::tmem_ld16(tE + lane_base + 32 * half + 16, e + 16);
-      float* Eo = Ews + chunk * R2 * C2 + (size_t)row * C2 + 32 * half;
+      float4* Eo = reinterpret_cast<float4*>(Ews + chunk * R2 * C2 + (size_t)row * C2 + 32 * half);
 #pragma unroll
-      for (int t = 0; t < 32; ++t) atomicAdd(Eo + t, e[t]);
+      for (int t = 0; t < 8; ++t) atomicAdd(Eo + t, make_float4(e[4 * t], e[4 * t + 1], e[4 * t + 2], e[4 * t + 3]));
     }
-    // ---- phase B: epilogues
+    // ---- phase B: epilogues; results go back into the (swizzled) state stage and leave by
+    // TMA stores; a stage is released (edone) once its store has read it
     for (int kt = 0; kt < NT && ok; ++kt) {
       const int g = NT + kt, s = g & 1, d = kt & 1;
       if (!cwait(B_TFULL + s, (g >> 1) & 1)) break;
@@ -1089,16 +1092,29 @@ colpass_ws_body(const CUtensorMap& tm_k, const CUtensorMap& tm_v, const CUtensor
       float dh[32];
       tc::tmem_ld16(tDH + 64 * d + lane_base + 32 * half, dh);
       tc::tmem_ld16(tDH + 64 * d + lane_base + 32 * half + 16, dh + 16);
-      float* dst = (half ? dst_i : dst_r) + (size_t)item * D * D + (size_t)gi * D + j0;
-#pragma unroll
-      for (int cc = 0; cc < 8; ++cc)
-        *reinterpret_cast<float4*>(dst + 4 * cc) =
-            make_float4(hv[4 * cc] + dh[4 * cc], hv[4 * cc + 1] + dh[4 * cc + 1], hv[4 * cc + 2] + dh[4 * cc + 2],
-                        hv[4 * cc + 3] + dh[4 * cc + 3]);
       tc::fence_before_sync();
       tc::named_sync(1, CONS);
-      if (tid == 0) tc::mbar_arrive(&bars[B_EDONE + d]);
+      if (tid == 0) {                            // input stage and dH[d] are free again
+        tc::mbar_arrive(&bars[B_DFREE + d]);
+        tc::mbar_arrive(&bars[B_EDONE + d]);
+        tc::bulk_wait_read<0>();                 // the previous tile's store has read sO
+      }
+      tc::named_sync(1, CONS);
+      unsigned char* obox = sO + half * 16 * 1024;
+#pragma unroll
+      for (int cc = 0; cc < 8; ++cc)
+        *reinterpret_cast<float4*>(obox + row * 128 + ((cc ^ (row & 7)) << 4)) =
+            make_float4(hv[4 * cc] + dh[4 * cc], hv[4 * cc + 1] + dh[4 * cc + 1], hv[4 * cc + 2] + dh[4 * cc + 2],
+                        hv[4 * cc + 3] + dh[4 * cc + 3]);
+      tc::fence_proxy_async();
+      tc::named_sync(1, CONS);
+      if (tid == 0) {
+        tc::tma_store_2d(&tm_dr, j0, item * D + kt * KT, sO);
+        tc::tma_store_2d(&tm_di, j0, item * D + kt * KT, sO + 16 * 1024);
+        tc::bulk_commit();
+      }
     }
+    if (tid == 0) tc::bulk_wait<0>();            // all state writes performed
   }
   tc::fence_before_sync();
   __syncthreads();
@@ -1473,14 +1489,15 @@ cham_tc_prep_ws(const __grid_constant__ CUtensorMap tm_k, const __grid_constant_
 __global__ void __launch_bounds__(WS_THREADS, 1)
 cham_tc_step_ws(const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
                 const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_sr,
-                const __grid_constant__ CUtensorMap tm_si, const __nv_bfloat16* __restrict__ q,
+                const __grid_constant__ CUtensorMap tm_si, const __grid_constant__ CUtensorMap tm_dr,
+                const __grid_constant__ CUtensorMap tm_di, const __nv_bfloat16* __restrict__ q,
                 const unsigned char* __restrict__ Tws, float* __restrict__ Ews,
                 const unsigned long long* __restrict__ badws, int src_identity, float* __restrict__ dst_r,
                 float* __restrict__ dst_i, __nv_bfloat16* __restrict__ out, int S, int D, int nch, int c,
                 int ncol) {
   if ((int)blockIdx.x < ncol)
-    colpass_ws_body(tm_k, tm_v, tm_sr, tm_si, q, Tws, Ews, badws, src_identity, dst_r, dst_i, S, D, nch, c,
-                    blockIdx.x);
+    colpass_ws_body(tm_k, tm_v, tm_sr, tm_si, tm_dr, tm_di, q, Tws, Ews, badws, src_identity, dst_r, dst_i, S, D,
+                    nch, c, blockIdx.x);
   else
     readout_ws_body(tm_k, tm_v, tm_q, tm_sr, Ews, badws, out, S, D, nch, c - 1, blockIdx.x - ncol);
 }
@@ -1579,7 +1596,8 @@ int launch_cham_tc(const void* q, const void* k, const void* v, const float* gam
       const int ncol = c < nch ? D / NB2 : 0;
       const int nread = c > 0 ? D / R2 : 0;
       cham_tc_step_ws<<<dim3(ncol + nread, b), WS_THREADS, WS_SMEM, st>>>(
-          mk, mv, mq, src_out ? m_out_r : m_ping_r, src_out ? m_out_i : m_ping_i, (const __nv_bfloat16*)q, w.T,
+          mk, mv, mq, src_out ? m_out_r : m_ping_r, src_out ? m_out_i : m_ping_i, to_out ? m_out_r : m_ping_r,
+          to_out ? m_out_i : m_ping_i, (const __nv_bfloat16*)q, w.T,
           w.E, w.bad, c == 0 ? 1 : 0, dr, di, (__nv_bfloat16*)out, s, D, nch, c, ncol);
       if ((rc = check_launch("cham_tc_step_ws"))) return rc;
     }

@@ -187,6 +187,24 @@ __device__ __forceinline__ void tma_load_3d(void* smem, const void* tmap, int x,
       "l"(tmap), "r"(x), "r"(y), "r"(z), "r"(smem_addr(mbar))
       : "memory");
 }
+// TMA tiled store shared -> global (bulk-group completion), and its group controls.
+__device__ __forceinline__ void tma_store_2d(const void* tmap, int x, int y, const void* smem) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%1, %2}], [%3];" ::"l"(tmap), "r"(x),
+               "r"(y), "r"(smem_addr(smem))
+               : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// wait until at most N committed bulk groups still read their shared-memory source
+template <int N>
+__device__ __forceinline__ void bulk_wait_read() {
+  asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
+}
+// wait until at most N committed bulk groups are still in flight (writes performed)
+template <int N>
+__device__ __forceinline__ void bulk_wait() {
+  asm volatile("cp.async.bulk.wait_group %0;" ::"n"(N) : "memory");
+}
+
 // Plain bulk copy global -> shared (16-byte aligned, size a multiple of 16).
 __device__ __forceinline__ void bulk_load(void* smem, const void* gmem, uint32_t bytes, uint64_t* mbar) {
   asm volatile(
