@@ -19,6 +19,7 @@
 //   cham_tc_readout  one CTA per (item, 128 rows): Re(S Y) + W mask(E).
 #include "common.cuh"
 #include "tc.cuh"
+#include "wy_solve.cuh"
 
 #include <cuda.h>
 #include <cudaTypedefs.h>
@@ -1315,7 +1316,8 @@ readout_ws_body(const CUtensorMap& tm_k, const CUtensorMap& tm_v, const CUtensor
 // then N_t, T by block forward substitution (fp32 SIMT) directly in that row order.
 // smem: Gs [128][129] fp32 | W stages (2 x 32K, 1024-aligned) aliased later by Tr | Ti
 constexpr int PW_TR = 67584, PW_TI = PW_TR + R2 * (R2 + 1) * 4;
-constexpr int PREP_WS_SMEM = PW_TI + R2 * (R2 + 1) * 4;
+constexpr int PREP_WS_ACC = PW_TI + R2 * (R2 + 1) * 4;
+constexpr int PREP_WS_SMEM = PREP_WS_ACC + 2 * 16 * R2 * 4;
 
 __global__ void __launch_bounds__(THR, 1)
 cham_tc_prep_ws(const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
@@ -1327,9 +1329,10 @@ cham_tc_prep_ws(const __grid_constant__ CUtensorMap tm_k, const __grid_constant_
   float* Tr = reinterpret_cast<float*>(smp + PW_TR);
   float* Ti = reinterpret_cast<float*>(smp + PW_TI);
   auto stW = [&](int s) { return smp + PW_TR + s * W_TILE; };
-  __shared__ float Ns[C2 * 6];
+  __shared__ float Ns[C2 * 8];
   __shared__ unsigned long long bad_bits;
   __shared__ __align__(8) uint64_t bars[5];   // tfull[2], mdone[2], done
+  float* acc = reinterpret_cast<float*>(smp + PREP_WS_ACC);
   __shared__ uint32_t tslot;
   __shared__ int pfail;
   const int c = blockIdx.x, item = blockIdx.y, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -1423,8 +1426,8 @@ cham_tc_prep_ws(const __grid_constant__ CUtensorMap tm_k, const __grid_constant_
           atomicOr(&bad_bits, 1ull << tau);
         }
       }
-      float* n = Ns + tau * 6;
-      n[0] = n00r; n[1] = n00i; n[2] = n01r; n[3] = n01i; n[4] = n11r; n[5] = n11i;
+      float* n = Ns + tau * 8;   // [[n00, n01], [n01, n11]]
+      n[0] = n00r; n[1] = n00i; n[2] = n01r; n[3] = n01i; n[4] = n01r; n[5] = n01i; n[6] = n11r; n[7] = n11i;
     }
     __syncthreads();
     if (bad_bits) {   // clear the Gram rows/columns of non-finite tokens
@@ -1434,31 +1437,7 @@ cham_tc_prep_ws(const __grid_constant__ CUtensorMap tm_k, const __grid_constant_
       }
       __syncthreads();
     }
-    if (tid < R2) {
-      const int sg = tid, blk = tok(sg);
-      for (int tp = 0; tp < blk; ++tp) {
-        Tr[tp * P + sg] = 0.f; Ti[tp * P + sg] = 0.f;
-        Tr[(C2 + tp) * P + sg] = 0.f; Ti[(C2 + tp) * P + sg] = 0.f;
-      }
-      for (int t = blk; t < C2; ++t) {
-        float x0r = (sg == t) ? 1.f : 0.f, x0i = 0.f;
-        float x1r = (sg == C2 + t) ? 1.f : 0.f, x1i = 0.f;
-        for (int tp = blk; tp < t; ++tp) {
-          const float a0r = Tr[tp * P + sg], a0i = Ti[tp * P + sg];
-          const float a1r = Tr[(C2 + tp) * P + sg], a1i = Ti[(C2 + tp) * P + sg];
-          const float g00 = Gs[t * P + tp], g01 = Gs[t * P + C2 + tp];
-          const float g10 = Gs[(C2 + t) * P + tp], g11 = Gs[(C2 + t) * P + C2 + tp];
-          x0r += g00 * a0r + g01 * a1r; x0i += g00 * a0i + g01 * a1i;
-          x1r += g10 * a0r + g11 * a1r; x1i += g10 * a0i + g11 * a1i;
-        }
-        const float* n = Ns + t * 6;
-        Tr[t * P + sg] = n[0] * x0r - n[1] * x0i + n[2] * x1r - n[3] * x1i;
-        Ti[t * P + sg] = n[0] * x0i + n[1] * x0r + n[2] * x1i + n[3] * x1r;
-        Tr[(C2 + t) * P + sg] = n[2] * x0r - n[3] * x0i + n[4] * x1r - n[5] * x1i;
-        Ti[(C2 + t) * P + sg] = n[2] * x0i + n[3] * x0r + n[4] * x1i + n[5] * x1r;
-      }
-    }
-    __syncthreads();
+    wy_solve<true>(Gs, P, Ns, Tr, Ti, acc, [](int t, int kv) { return kv * C2 + t; }, tid);
     const size_t chunk = (size_t)item * nch + c;
     unsigned char* To = Tws + chunk * 4 * T_TILE;
     for (int e = tid; e < R2 * (R2 / 8); e += THR) {

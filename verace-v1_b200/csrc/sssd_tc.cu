@@ -12,6 +12,7 @@
 // T for every chunk comes from sssd_tc_prep (all chunks in parallel, fp32 SIMT).
 #include "common.cuh"
 #include "tc.cuh"
+#include "wy_solve.cuh"
 
 namespace verace {
 namespace {
@@ -64,7 +65,7 @@ sssd_tc_prep(const T* __restrict__ k, const T* __restrict__ v, const float* __re
   float* Ws = sm3;
   float* Gs = Ws + HD * P;
   float* Ts = Gs + R3 * P;
-  __shared__ float Ms[C3 * 4];
+  __shared__ float Ms[C3 * 8];   // per token [[m00, m01], [m10, m11]] as complex with zero imaginary parts
   __shared__ unsigned long long bad_bits;
   const int c = blockIdx.x, chain = blockIdx.y, tid = threadIdx.x;
   const int bi = chain / H, hi = chain % H;
@@ -146,25 +147,12 @@ sssd_tc_prep(const T* __restrict__ k, const T* __restrict__ v, const float* __re
         Gs[r * P + 2 * tau] = 0.f; Gs[r * P + 2 * tau + 1] = 0.f;
       }
     }
-    Ms[tau * 4 + 0] = m00; Ms[tau * 4 + 1] = m01; Ms[tau * 4 + 2] = m10; Ms[tau * 4 + 3] = m11;
+    float* n = Ms + tau * 8;
+    n[0] = m00; n[1] = 0.f; n[2] = m01; n[3] = 0.f; n[4] = m10; n[5] = 0.f; n[6] = m11; n[7] = 0.f;
   }
   __syncthreads();
-  if (tid < R3) {
-    const int sg = tid, blk = sg >> 1;
-    for (int r = 0; r < 2 * blk; ++r) Ts[r * P + sg] = 0.f;
-    for (int t = blk; t < C3; ++t) {
-      float x0 = (sg == 2 * t) ? 1.f : 0.f;
-      float x1 = (sg == 2 * t + 1) ? 1.f : 0.f;
-      for (int tp = blk; tp < t; ++tp) {
-        const float a0 = Ts[(2 * tp) * P + sg], a1 = Ts[(2 * tp + 1) * P + sg];
-        x0 += Gs[(2 * t) * P + 2 * tp] * a0 + Gs[(2 * t) * P + 2 * tp + 1] * a1;
-        x1 += Gs[(2 * t + 1) * P + 2 * tp] * a0 + Gs[(2 * t + 1) * P + 2 * tp + 1] * a1;
-      }
-      Ts[(2 * t) * P + sg] = Ms[t * 4 + 0] * x0 + Ms[t * 4 + 1] * x1;
-      Ts[(2 * t + 1) * P + sg] = Ms[t * 4 + 2] * x0 + Ms[t * 4 + 3] * x1;
-    }
-  }
-  __syncthreads();
+  // Ws is dead once G is formed: it holds the solver's scratch
+  wy_solve<false>(Gs, P, Ms, Ts, nullptr, Ws, [](int t, int kv) { return 2 * t + kv; }, tid);
   const size_t chunk = (size_t)chain * nch + c;
   unsigned char* To = Tws + chunk * 2 * TILE3;
   for (int e = tid; e < R3 * (R3 / 8); e += THR3) {

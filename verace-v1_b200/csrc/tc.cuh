@@ -171,7 +171,7 @@ __device__ __forceinline__ void mbar_expect_tx(uint64_t* mbar, uint32_t bytes) {
   asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(mbar)), "r"(bytes)
                : "memory");
 }
-// TMA tiled loads (no multicast): box at coordinates (x innermost) -> shared memory,
+// TMA tiled loads into this CTA's own shared memory: box at coordinates (x innermost),
 // completion counted in bytes on `mbar`.
 __device__ __forceinline__ void tma_load_2d(void* smem, const void* tmap, int x, int y, uint64_t* mbar) {
   asm volatile(
