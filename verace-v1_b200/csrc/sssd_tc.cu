@@ -67,12 +67,86 @@ sssd_tc_prep(const T* __restrict__ k, const T* __restrict__ v, const float* __re
   float* Ts = Gs + R3 * P;
   __shared__ float Ms[C3 * 8];   // per token [[m00, m01], [m10, m11]] as complex with zero imaginary parts
   __shared__ unsigned long long bad_bits;
-  const int c = blockIdx.x, chain = blockIdx.y, tid = threadIdx.x;
+  __shared__ __align__(8) uint64_t gbar;
+  __shared__ uint32_t gslot;
+  constexpr bool BF = sizeof(T) == 2;   // bf16 inputs: G on the tensor cores (W is exact in bf16)
+  const int c = blockIdx.x, chain = blockIdx.y, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int bi = chain / H, hi = chain % H;
   const int t0 = c * C3, nt = min(C3, S - t0);
-  if (tid == 0) bad_bits = 0ull;
+  if (BF && warp == 0) tc::tmem_alloc(&gslot, 128);
+  if (tid == 0) {
+    bad_bits = 0ull;
+    if (BF) { tc::mbar_init(&gbar, 1); tc::fence_mbar_init(); }
+  }
+  tc::fence_before_sync();
   __syncthreads();
-  {
+  tc::fence_after_sync();
+  if constexpr (BF) {
+    // W as a bf16 K-major tile (rows r = 2*tau + {k, v}) in the front of Ws
+    unsigned char* Wb = reinterpret_cast<unsigned char*>(Ws);
+    constexpr int PER = (R3 * (HD / 8)) / THR3;
+    uint4 raw[PER];
+#pragma unroll
+    for (int u = 0; u < PER; ++u) {
+      const int e = tid + THR3 * u, r = e % R3, g = e / R3, tau = r >> 1;
+      raw[u] = make_uint4(0, 0, 0, 0);
+      if (tau < nt)
+        raw[u] = *reinterpret_cast<const uint4*>(((r & 1) ? v : k) +
+                                                 ((size_t)(bi * (size_t)S + t0 + tau) * H + hi) * HD + g * 8);
+    }
+#pragma unroll
+    for (int u = 0; u < PER; ++u) {
+      const int e = tid + THR3 * u, r = e % R3, g = e / R3;
+      const __nv_bfloat16* hb = reinterpret_cast<const __nv_bfloat16*>(&raw[u]);
+      bool fin = true;
+#pragma unroll
+      for (int jj = 0; jj < 8; ++jj) fin = fin && isfinite(__bfloat162float(hb[jj]));
+      if (!fin) atomicOr(&bad_bits, 1ull << (r >> 1));
+      *reinterpret_cast<uint4*>(Wb + kmaj3(r, g * 8, R3)) = raw[u];
+    }
+    __syncthreads();
+    if (tid < C3 && tid < nt && !isfinite(delta[(size_t)(bi * (size_t)S + t0 + tid) * H + hi]))
+      atomicOr(&bad_bits, 1ull << tid);
+    __syncthreads();
+    if (bad_bits) {
+      for (int e = tid; e < R3 * (HD / 8); e += THR3) {
+        const int r = e % R3, g = e / R3;
+        if ((bad_bits >> (r >> 1)) & 1ull) *reinterpret_cast<uint4*>(Wb + kmaj3(r, g * 8, R3)) = make_uint4(0, 0, 0, 0);
+      }
+    }
+    tc::fence_proxy_async();
+    __syncthreads();
+    const uint32_t tG = gslot;
+    if (tid == 0) {
+      tc::fence_after_sync();
+      constexpr uint32_t ID_G = tc::idesc_bf16(128, 128, false, false);
+      const uint32_t w = tc::smem_addr(Wb);
+#pragma unroll 1
+      for (int ks = 0; ks < HD / 16; ++ks) {
+        const uint64_t d = tc::sdesc(w + ks * 4096, 2048, 128);
+        tc::mma_bf16(tG, d, d, ID_G, ks > 0 ? 1u : 0u);
+      }
+      tc::commit(&gbar);
+    }
+    const bool ok = tc::mbar_wait(&gbar, 0, POLLS3);
+    if (__syncthreads_or(!ok)) {
+      if (tid == 0) atomicExch(&g_sssd_tc_status, 1);
+    } else {
+      tc::fence_after_sync();
+      const uint32_t lb = (uint32_t)(32 * (warp & 3)) << 16;
+      const int row = 32 * (warp & 3) + lane, half = warp >> 2;
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        float x[16];
+        tc::tmem_ld16(tG + lb + 64 * half + 16 * u, x);
+#pragma unroll
+        for (int jj = 0; jj < 16; ++jj) Gs[row * P + 64 * half + 16 * u + jj] = x[jj];
+      }
+    }
+    tc::fence_before_sync();
+    __syncthreads();
+    if (warp == 0) tc::tmem_dealloc(tG, 128);
+  } else {
     // W^T into Ws[i][r]: each thread takes 8 (vector r, 8 consecutive elements) chunks;
     // all global loads are issued before any use so their latencies overlap
     constexpr int PER = (R3 * (HD / 8)) / THR3;
@@ -109,7 +183,6 @@ sssd_tc_prep(const T* __restrict__ k, const T* __restrict__ v, const float* __re
       }
       if (!fin) atomicOr(&bad_bits, 1ull << (r >> 1));
     }
-  }
   __syncthreads();
   if (tid < C3 && tid < nt && !isfinite(delta[(size_t)(bi * (size_t)S + t0 + tid) * H + hi]))
     atomicOr(&bad_bits, 1ull << tid);
@@ -121,6 +194,7 @@ sssd_tc_prep(const T* __restrict__ k, const T* __restrict__ v, const float* __re
   }
   smem_gemm<4, 4, false>(R3, R3, HD, Ws, 1, P, Ws, P, 1, Gs, P, 1, tid, THR3);
   __syncthreads();
+  }
   if (tid < C3) {
     const int tau = tid;
     float m00 = 0.f, m01 = 0.f, m10 = 0.f, m11 = 0.f;
