@@ -14,6 +14,12 @@ token before layer 12, so every token runs all 12 layers.
 
 Unit: token-layers/s (one token through SSSD + CHAM of one layer).
 
+Decode (reported under "decode"): the same 12 layers, 64 items per
+GPU, a 1024-token prompt prefilled with the scans, then 256 single-token steps with
+teacher-forced random ids, each step one CUDA graph of the layer glue and the fused
+decode kernels (verace_decode_step) that update the resident SSSD and CHAM states in
+place.  Reported as µs per step and µs per token (= step / 64).
+
 Multi-GPU (torchrun, one rank per GPU): each rank runs the full config-2 batch on its
 own items (weak scaling: batch shards, no collective on the data path); time is the
 max over ranks of the CUDA-event time.
@@ -35,7 +41,7 @@ sys.path.insert(0, ROOT)
 METRIC = "SSSD+CHAM scan tokens/s at 1/2/4/8 B200 + % roofline; decode step µs/token"
 UNIT = "token-layers/s"
 CFG = dict(layers=12, batch=8, seq=2048, hidden=1024, heads=8, head_dim=128, holo=1024, vocab=32000)
-CHAM_CHUNK = 32  # tokens per chunk of the CHAM scan kernels (cham_scan.cu)
+DEC = dict(batch=64, prompt=1024, steps=256)
 
 
 def _load_package():
@@ -206,8 +212,18 @@ def run_ours(args):
 
     hbm, bf16_burst, bf16_sus, peak_kind = _peaks()
     D, b, s = c["holo"], c["batch"], c["seq"]
+    nch = (s + 63) // 64
+    # Algorithmic bytes of one verace_cham_scan call (chunked scan, 64-token chunks): the
+    # D x D complex fp32 state read (except the identity start) and written once per chunk,
+    # q/k/v in and the readout out (bf16), and the per-chunk T coefficients (128 KB per
+    # item and chunk) written by the prep and read by the column pass.
+    cham_bytes = (2 * nch - 1) * b * 2 * D * D * 4 + 4 * b * s * D * 2 + 2 * nch * b * 131072
+    achieved = cham_bytes / (cham_ms * 1e-3) / 1e9
     cham_flop = 18.0 * D * D * b * s              # 9 D² MAC per token (8 state update + 1 readout)
-    achieved = cham_flop / (cham_ms * 1e-3) / 1e12
+    # DRAM bytes per (item, chunk) measured by ncu (profiles/cham_tc_step_ws_b16_s256.md:
+    # 247.7 MB per step launch at b=16; cham_tc_prep_ws_b16_s256.md: 16.8 MB per 64
+    # item-chunks), scaled to this call's items and chunks
+    traffic = (247.7e6 / 16 + 16.8e6 / 64) * b * nch
     result = {
         "metric": METRIC, "value": world * tokens_per_step / (ms * 1e-3), "unit": UNIT,
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
@@ -218,23 +234,146 @@ def run_ours(args):
                    "global_batch": b * world, "seq_len": s, "layers": c["layers"],
                    "parallelism": f"dp{world} (batch shards, no collective)",
                    "l2": "no flush: per-step working set (weights 190 MB + activations) > 126 MB L2"},
-        "roofline": {"kernel": "verace_cham_scan (prep + per-chunk colpass/readout)",
-                     "bound": "tensor", "achieved": achieved, "peak": bf16_sus, "unit": "TFLOP/s",
-                     "frac": achieved / bf16_sus, "traffic": None,
-                     "flop_per_launch": cham_flop, "ms_per_launch": cham_ms,
-                     "peak_source": f"{peak_kind} bf16 sustained (MEASURED_PEAKS.json)"},
+        "roofline": {"kernel": "verace_cham_scan (cham_tc_prep_ws + one cham_tc_step_ws per 64-token chunk)",
+                     "bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
+                     "frac": achieved / hbm, "traffic": traffic,
+                     "bytes_per_launch": cham_bytes, "ms_per_launch": cham_ms,
+                     "peak_source": f"{peak_kind} HBM copy bandwidth (MEASURED_PEAKS.json)",
+                     "tensor_tflops": cham_flop / (cham_ms * 1e-3) / 1e12,
+                     "tensor_frac": cham_flop / (cham_ms * 1e-3) / 1e12 / bf16_sus},
         "e2e": {"value": world * tokens_per_step / (e2e_ms * 1e-3), "unit": UNIT,
                 "h2d_bytes_per_step": x.numel() * x.element_size(),
                 "d2h_bytes_per_step": x.numel() * x.element_size()},
         "clocks": clocks,
         "gpu_launches": int(launches),
     }
+    if not args.no_decode:
+        del x
+        torch.cuda.empty_cache()
+        result["decode"] = run_decode(args, layers, embed, V, dev, rank, barrier, max_over_ranks)
     if world == 1 and not args.no_cpu_baseline:
         result["cpu_baseline"] = cpu_sample(tokens=args.cpu_tokens)
     if rank == 0:
         print(json.dumps(result), flush=True)
     if world > 1:
         dist.destroy_process_group()
+
+
+def run_decode(args, layers, embed, V, dev, rank, barrier, max_over_ranks):
+    """Config 3: prefill a prompt, then time single-token decode steps (CUDA graphs)."""
+    import torch
+    from verace_v1_b200 import _lib
+    from verace_v1_b200.kernels import launch_cham_update
+    c = CFG
+    b, P, n = DEC["batch"], DEC["prompt"], DEC["steps"]
+    nh, d, D = c["heads"], c["head_dim"], c["holo"]
+    nl = len(layers)
+    gen = torch.Generator().manual_seed(100 + rank)
+    prompt = torch.randint(0, c["vocab"], (b, P), generator=gen).to(dev)
+    toks = torch.randint(0, c["vocab"], (b, n + args.warmup), generator=gen).to(dev)
+    st = V.DecodeState(nl, b, nh, d, D, device=dev)
+    with torch.no_grad():
+        x = embed(prompt)
+        for l, L in enumerate(layers):
+            o, psi = L["sssd"](L["sssd_norm"](x), return_state=True)
+            x = x + o
+            cm = L["cham"]
+            q, k, v, g = cm.project(L["cham_norm"](x))
+            rec, holo = launch_cham_update(q, k, v, g)
+            x = x + cm.finish(rec)
+            st.load_layer(l, psi, holo)
+            del o, psi, q, k, v, g, rec, holo
+        del x
+        saved = (st.psi.clone(), st.H_real.clone(), st.H_imag.clone())
+        torch.cuda.empty_cache()
+        tok = torch.zeros(b, dtype=torch.long, device=dev)
+
+        def dstep():
+            hcur = embed(tok).unsqueeze(1)
+            for l, L in enumerate(layers):
+                sm, cm = L["sssd"], L["cham"]
+                q, k, v, dl = sm.project(L["sssd_norm"](hcur))
+                o = st.step_sssd(l, q, k, v, dl)
+                hcur = hcur + sm.finish(o.view(b, 1, nh, d))
+                q, k, v, g = cm.project(L["cham_norm"](hcur))
+                rec = st.step_cham(l, q, k, v, g)
+                hcur = hcur + cm.finish(rec.view(b, 1, D))
+            return hcur
+
+        side = torch.cuda.Stream(dev)
+        side.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(side):
+            for _ in range(2):
+                dstep()
+        torch.cuda.current_stream(dev).wait_stream(side)
+        graph = torch.cuda.CUDAGraph()
+        l0 = _lib.lib().verace_kernel_launches()
+        with torch.cuda.graph(graph):
+            dstep()
+        launches_per_step = int(_lib.lib().verace_kernel_launches() - l0)
+
+        def restore():
+            st.psi.copy_(saved[0])
+            st.H_real.copy_(saved[1])
+            st.H_imag.copy_(saved[2])
+
+        for i in range(args.warmup):
+            tok.copy_(toks[:, n + i])
+            graph.replay()
+        restore()
+        barrier()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for i in range(n):
+            tok.copy_(toks[:, i])
+            graph.replay()
+        e1.record()
+        barrier()
+        us_step = max_over_ranks(e0.elapsed_time(e1)) * 1e3 / n
+        if V.device_status(dev) != 0:
+            raise RuntimeError("decode steps reported a device status")
+
+        # the dominant kernel alone: CHAM half of verace_decode_step, one launch per layer
+        g1 = torch.Generator().manual_seed(7)
+        nrm = torch.nn.functional.normalize
+        cq, ck, cv = (nrm(torch.randn(b, D, generator=g1), dim=-1).to(dev, torch.bfloat16) for _ in range(3))
+        cg = (0.1 * torch.sigmoid(torch.randn(b, generator=g1))).to(dev)
+        for l in range(nl):
+            st.step_cham(l, cq, ck, cv, cg)
+        torch.cuda.synchronize()
+        e2 = torch.cuda.Event(enable_timing=True)
+        e3 = torch.cuda.Event(enable_timing=True)
+        reps = 3
+        e2.record()
+        for _ in range(reps):
+            for l in range(nl):
+                st.step_cham(l, cq, ck, cv, cg)
+        e3.record()
+        torch.cuda.synchronize()
+        us_launch = e2.elapsed_time(e3) * 1e3 / (reps * nl)
+    graph.reset()
+    del graph, saved, st
+    torch.cuda.empty_cache()
+    hbm = _peaks()[0]
+    cham_bytes = 2 * 2 * b * D * D * 4                  # Hr, Hi read once and written once
+    sssd_bytes = 2 * b * nh * d * d * 4
+    w_bytes = sum(p.numel() * p.element_size() for L in layers for p in L.parameters())
+    step_bytes = nl * (cham_bytes + sssd_bytes) + w_bytes
+    achieved = cham_bytes / (us_launch * 1e-6) / 1e9
+    return {
+        "workload": f"config 3: 12-layer decode, b={b} per GPU, prompt {P} (prefilled by the scans), "
+                    f"{n} single-token steps (teacher-forced random ids), bf16, one CUDA graph per step",
+        "us_per_step": us_step, "us_per_token": us_step / b, "steps": n, "batch": b,
+        "readout": "unitary (Re(H q); exact for unitary holograms)",
+        "gpu_launches_per_step": launches_per_step,
+        "step_hbm_roofline_us": step_bytes / (hbm * 1e9) * 1e6,
+        "step_frac_of_hbm_roofline": step_bytes / (hbm * 1e9) * 1e6 / us_step,
+        "roofline": {"kernel": "decode_step_kernel (CHAM half: hologram read + update + write, readout)",
+                     "bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
+                     "frac": achieved / hbm, "traffic": None, "bytes_per_launch": cham_bytes,
+                     "us_per_launch": us_launch},
+    }
 
 
 # ------------------------------------------------------------------------------ CPU arm
@@ -301,7 +440,14 @@ def run_only(args):
     b, s = args.batch or c["batch"], args.seq or c["seq"]
     g = torch.Generator().manual_seed(0)
     nrm = torch.nn.functional.normalize
-    if args.only == "cham":
+    if args.only == "decode":
+        V = sys.modules["verace_v1_b200"]
+        D = c["holo"]
+        st = V.DecodeState(1, b, c["heads"], c["head_dim"], D, device=dev)
+        q, k, v = (nrm(torch.randn(b, D, generator=g), dim=-1).to(dev, torch.bfloat16) for _ in range(3))
+        gam = (0.1 * torch.sigmoid(torch.randn(b, generator=g))).to(dev)
+        fn = lambda: st.step_cham(0, q, k, v, gam)
+    elif args.only == "cham":
         D = c["holo"]
         q, k, v = (nrm(torch.randn(b, s, D, generator=g), dim=-1).to(dev, torch.bfloat16) for _ in range(3))
         gam = (0.1 * torch.sigmoid(torch.randn(b, s, generator=g))).to(dev)
@@ -334,7 +480,8 @@ def main():
     ap.add_argument("--cpu-tokens", type=int, default=32)
     ap.add_argument("--ref-tokens", type=int, default=8)
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--only", choices=["cham", "sssd"], default=None,
+    ap.add_argument("--no-decode", action="store_true", help="skip the config-3 decode measurement")
+    ap.add_argument("--only", choices=["cham", "sssd", "decode"], default=None,
                     help="time one scan entry point alone (kernel-level case for profiling)")
     ap.add_argument("--batch", type=int, default=None)
     ap.add_argument("--seq", type=int, default=None)

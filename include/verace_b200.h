@@ -40,7 +40,8 @@ enum {
   VERACE_ERR_UNSUPPORTED = 2, /* valid but unsupported shape (e.g. head_dim > 128) */
   VERACE_ERR_CUDA = 3,        /* a CUDA runtime call or kernel launch failed */
   VERACE_ERR_WORKSPACE = 4,   /* workspace missing or smaller than required */
-  VERACE_ERR_TIMEOUT = 5      /* a bounded device-side wait gave up */
+  VERACE_ERR_TIMEOUT = 5,     /* a bounded device-side wait gave up */
+  VERACE_ERR_STATE = 6        /* a decode step met a hologram too far from unitary */
 };
 
 enum { VERACE_F32 = 0, VERACE_BF16 = 1, VERACE_F16 = 2 };
@@ -51,10 +52,11 @@ VERACE_API int verace_version(void);
 /* Message describing the last error returned on the calling host thread. */
 VERACE_API const char* verace_last_error(void);
 
-/* Synchronises `stream`, then reports (and clears) the device-side status of this
- * library's bounded waits: VERACE_ERR_TIMEOUT if a kernel gave up waiting for a
- * tensor-core completion since the last call, else 0.  No reference counterpart: the
- * reference has no device-side waits. */
+/* Synchronises `stream`, then reports (and clears) the device-side status words of
+ * this library: VERACE_ERR_TIMEOUT if a kernel gave up waiting for a tensor-core
+ * completion since the last call, else VERACE_ERR_STATE if a VERACE_DECODE_FIRST_ORDER
+ * decode step found |(H^H H - I) q| > 1e-2 |q| for some item, else 0.  No reference
+ * counterpart: the reference has no device-side waits and no decode precondition. */
 VERACE_API int verace_device_status(void* stream);
 
 /* Number of kernels this library has launched in the process so far (all devices,
@@ -128,6 +130,42 @@ VERACE_API size_t verace_cham_retract_workspace(int b, int D);
 VERACE_API int verace_cham_retract(const float* h_re, const float* h_im, float* out_re, float* out_im,
                         int b, int D, int steps, void* workspace, size_t workspace_bytes,
                         void* stream);
+
+/* ------------------------------------------------------------------------------
+ * Fused single-token decode step of one layer for a batch: SSSD state rotation and
+ * CHAM hologram update with both readouts, states updated IN PLACE.
+ * Replaces, for all b items at once, what one incremental-decode step runs per layer
+ * and per item through layer_states (verace_v1/serving/hyper_generate.py:58-77,
+ * verace_v1/modules/backbone.py:53-101): SSSDAttention.forward with s = 1 and
+ * initial_state (sssd_attention.py:103-182, launcher triton_kernels.py:603-636) and
+ * ContinuousHolographicMemory.forward with s = 1 and initial_hologram
+ * (cham_memory.py:117-243, launcher triton_kernels.py:639-685 / _cham_tiled_step :477-549).
+ *   SSSD:  Psi <- R Psi,  sssd_out = Psi q           (per item and head)
+ *   CHAM:  H <- U H,      cham_out = Re(NS3(H) q)    (per item; H = h_re + i h_im)
+ * sssd_q, sssd_k, sssd_v, sssd_out : [b, h, d] (dtype)   delta : [b, h] fp32
+ * psi                              : [b, h, d, d] fp32, read and overwritten
+ * cham_q, cham_k, cham_v, cham_out : [b, D] (dtype)      gamma : [b] fp32
+ * h_re, h_im                       : [b, D, D] fp32, read and overwritten
+ * The readout retraction NS3 uses that U is unitary: NS3(U H) = U H p(H^H H) for the
+ * Newton-Schulz polynomial p, and p(I + E) = I - E/2 + O(E^2).
+ *   mode VERACE_DECODE_UNITARY:     cham_out = Re(H q) (p = I); exact for H^H H = I,
+ *                                   which holds to fp32 rounding for every state grown
+ *                                   from an identity start.  One launch.
+ *   mode VERACE_DECODE_FIRST_ORDER: cham_out = Re(H (q - E q / 2)), an O(|E|^2)
+ *                                   difference; one extra pass over H (two launches);
+ *                                   flags |E q| > 1e-2 |q| (see verace_device_status).
+ * h == 0 or d == 0 skips SSSD (its pointers may be NULL); D == 0 skips CHAM.
+ * Supports d % 4 == 0, d <= 128; D % 128 == 0, D <= 1024.  Workspace (CHAM only):
+ * verace_decode_workspace(b, D) bytes; calls sharing a workspace must not overlap.
+ * ---------------------------------------------------------------------------- */
+enum { VERACE_DECODE_UNITARY = 0, VERACE_DECODE_FIRST_ORDER = 1 };
+VERACE_API size_t verace_decode_workspace(int b, int D);
+VERACE_API int verace_decode_step(const void* sssd_q, const void* sssd_k, const void* sssd_v,
+                                  const float* delta, float* psi, void* sssd_out,
+                                  const void* cham_q, const void* cham_k, const void* cham_v,
+                                  const float* gamma, float* h_re, float* h_im, void* cham_out,
+                                  int b, int h, int d, int D, int dtype, int mode,
+                                  void* workspace, size_t workspace_bytes, void* stream);
 
 #ifdef __cplusplus
 }

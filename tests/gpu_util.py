@@ -6,8 +6,10 @@ import verace_v1_b200 as V
 
 
 def rel_fro(a, b):
-    a = np.asarray(a, dtype=np.float64)
-    b = np.asarray(b, dtype=np.float64)
+    """Relative Frobenius error; complex inputs are compared as complex."""
+    cplx = np.iscomplexobj(a) or np.iscomplexobj(b)
+    a = np.asarray(a, dtype=np.complex128 if cplx else np.float64)
+    b = np.asarray(b, dtype=np.complex128 if cplx else np.float64)
     return float(np.linalg.norm(a - b) / max(np.linalg.norm(b), 1e-30))
 
 

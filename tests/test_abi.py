@@ -60,3 +60,34 @@ def test_cham_rejects_bad_arguments_without_a_device():
 def test_status_error_raises_runtime_error():
     with pytest.raises(RuntimeError, match="status 2"):
         _lib.check(2, "probe")
+
+
+def test_decode_step_rejects_bad_arguments_without_a_device():
+    L = _lib.lib()
+    fake = ctypes.c_void_p(256)
+    f = [fake] * 13
+    ws = L.verace_decode_workspace(4, 1024)
+    assert ws >= 4 * 32 * 1024 * 4 and L.verace_decode_workspace(4, 512) < ws
+    rc = L.verace_decode_step(*f, 2, 8, 128, 1024, 0, 7, fake, ws, None)
+    assert rc == 1 and "mode" in _err()
+    rc = L.verace_decode_step(*f, 2, 8, 128, 1024, 5, 0, fake, ws, None)
+    assert rc == 1 and "dtype" in _err()
+    rc = L.verace_decode_step(*f, 2, 8, 128, 96, 0, 0, fake, ws, None)
+    assert rc == 2 and "holographic" in _err()
+    rc = L.verace_decode_step(*f, 2, 8, 130, 0, 0, 0, fake, ws, None)
+    assert rc == 2 and "head_dim" in _err()
+    rc = L.verace_decode_step(*f, 2, 8, 128, 1024, 0, 0, None, 0, None)
+    assert rc == 4 and "workspace" in _err()
+    rc = L.verace_decode_step(*([None] * 6), *f[:7], 2, 8, 128, 1024, 0, 0, fake, ws, None)
+    assert rc == 1 and "SSSD" in _err()
+    # nothing to do: returns before touching the device
+    assert L.verace_decode_step(*f, 0, 8, 128, 1024, 0, 0, None, 0, None) == 0
+    assert L.verace_decode_step(*f, 2, 0, 0, 0, 0, 0, None, 0, None) == 0
+
+
+def test_decode_python_api_requires_cuda_tensors():
+    import torch
+    from verace_v1_b200 import decode
+    x = torch.zeros(1, 2, 4)
+    with pytest.raises(AssertionError, match="CUDA"):
+        decode.launch_decode_step((x, x, x, torch.zeros(1, 2), torch.zeros(1, 2, 4, 4)), None)

@@ -1,0 +1,247 @@
+"""The fused single-token decode step (verace_decode_step) against the fp64 oracle.
+
+One decode step of the reference is SSSDAttention / ContinuousHolographicMemory forward
+with s = 1 and the previous state (verace_v1/serving/hyper_generate.py:58-77); the oracle
+for it is the launcher-level scan over that one token from the given state, including
+the CHAM readout's Newton-Schulz retraction.  Also: several steps in a row, incremental
+decode against a full-sequence scan (the reference's
+tests/test_incremental_generation.py:27-57 property), the first-order readout on a
+hologram that is not unitary, the drift status, non-finite tokens, and shape limits.
+
+Tolerances: relative Frobenius <= 1e-4 for fp32 outputs and for every fp32 state,
+<= 2e-2 for bf16 outputs.
+"""
+import numpy as np
+import pytest
+import torch
+
+import oracle
+import verace_v1_b200 as V
+from gpu_util import random_cham_inputs, random_sssd_inputs, rel_fro, to_np
+
+pytestmark = pytest.mark.gpu
+
+VERACE_ERR_STATE = 6
+
+
+def _unitary(b, D, seed):
+    """Random unitary matrices (QR of a complex Gaussian, phases fixed), complex128."""
+    rng = np.random.default_rng(seed)
+    Z = rng.standard_normal((b, D, D)) + 1j * rng.standard_normal((b, D, D))
+    Q, R = np.linalg.qr(Z)
+    ph = np.diagonal(R, axis1=-2, axis2=-1)
+    return Q * (ph / np.abs(ph))[..., None, :]
+
+
+def _holo(H):
+    return (torch.from_numpy(H.real.astype(np.float32)).cuda().contiguous(),
+            torch.from_numpy(H.imag.astype(np.float32)).cuda().contiguous())
+
+
+def _psi0(b, h, d, seed):
+    g = torch.Generator().manual_seed(seed)
+    return (torch.randn(b, h, d, d, generator=g) / d ** 0.5).cuda().contiguous()
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("b,h,d", [(3, 8, 128), (2, 3, 64), (1, 2, 12)])
+def test_sssd_decode_matches_oracle(dtype, b, h, d):
+    q, k, v, dl = random_sssd_inputs(b, 1, h, d, seed=700 + d, dtype=dtype)
+    psi0 = _psi0(b, h, d, 701)
+    psi = psi0.clone()
+    out, none = V.launch_decode_step((q[:, 0], k[:, 0], v[:, 0], dl[:, 0], psi), None)
+    assert none is None and out.dtype == dtype and tuple(out.shape) == (b, h, d)
+    assert V.device_status() == 0
+    o_ref, psi_ref = oracle.sssd_scan(to_np(q), to_np(k), to_np(v), to_np(dl), initial_state=to_np(psi0))
+    assert rel_fro(to_np(out), o_ref[:, 0]) <= (1e-4 if dtype == torch.float32 else 2e-2)
+    assert rel_fro(to_np(psi), psi_ref) <= 1e-5
+
+
+@pytest.mark.parametrize("dtype,mode", [(torch.float32, "first_order"), (torch.float32, "unitary"),
+                                        (torch.bfloat16, "unitary"), (torch.bfloat16, "first_order")])
+@pytest.mark.parametrize("b,D", [(3, 128), (2, 256), (2, 1024)])
+def test_cham_decode_matches_oracle(dtype, mode, b, D):
+    q, k, v, g = random_cham_inputs(b, 1, D, seed=710 + D, dtype=dtype)
+    H0 = _unitary(b, D, 711 + D)
+    hr, hi = _holo(H0)
+    h0r, h0i = hr.clone(), hi.clone()
+    none, out = V.launch_decode_step(None, (q[:, 0], k[:, 0], v[:, 0], g[:, 0], hr, hi), mode=mode)
+    assert none is None and out.dtype == dtype and tuple(out.shape) == (b, D)
+    assert V.device_status() == 0
+    r_ref, (Hr_ref, Hi_ref) = oracle.cham_scan(to_np(q), to_np(k), to_np(v), to_np(g),
+                                               initial_hologram=(to_np(h0r), to_np(h0i)))
+    assert rel_fro(to_np(out), r_ref[:, 0]) <= (1e-4 if dtype == torch.float32 else 2e-2)
+    H_ref = Hr_ref + 1j * Hi_ref
+    assert rel_fro(to_np(hr) + 1j * to_np(hi), H_ref) <= 1e-5
+
+
+@pytest.mark.parametrize("mode", ["first_order", "unitary"])
+def test_fused_layer_steps_match_oracle(mode):
+    """SSSD and CHAM in the same launch, 6 tokens in a row (fp32)."""
+    b, h, d, D, s = 3, 4, 128, 256, 6
+    sq, sk, sv, dl = random_sssd_inputs(b, s, h, d, seed=720)
+    cq, ck, cv, g = random_cham_inputs(b, s, D, seed=721)
+    psi0 = _psi0(b, h, d, 722)
+    H0 = _unitary(b, D, 723)
+    psi = psi0.clone()
+    hr, hi = _holo(H0)
+    h0r, h0i = hr.clone(), hi.clone()
+    so, co = [], []
+    for t in range(s):
+        o1, o2 = V.launch_decode_step((sq[:, t], sk[:, t], sv[:, t], dl[:, t], psi),
+                                      (cq[:, t], ck[:, t], cv[:, t], g[:, t], hr, hi), mode=mode)
+        so.append(o1)
+        co.append(o2)
+    assert V.device_status() == 0
+    so = torch.stack(so, 1)
+    co = torch.stack(co, 1)
+    o_ref, psi_ref = oracle.sssd_scan(to_np(sq), to_np(sk), to_np(sv), to_np(dl), initial_state=to_np(psi0))
+    r_ref, (Hr_ref, Hi_ref) = oracle.cham_scan(to_np(cq), to_np(ck), to_np(cv), to_np(g),
+                                               initial_hologram=(to_np(h0r), to_np(h0i)))
+    assert rel_fro(to_np(so), o_ref) <= 1e-4
+    assert rel_fro(to_np(psi), psi_ref) <= 1e-5
+    assert rel_fro(to_np(co), r_ref) <= 1e-4
+    assert rel_fro(to_np(hr) + 1j * to_np(hi), Hr_ref + 1j * Hi_ref) <= 1e-5
+
+
+def test_first_order_readout_on_a_non_unitary_hologram():
+    """H0 = Q (I + eps S): the unitary readout is off by about |E q| / 2, the first-order
+    readout by O(eps²); neither trips the drift status (|E q| < 1e-2 |q|)."""
+    b, D, eps = 2, 256, 1.5e-3
+    rng = np.random.default_rng(730)
+    S = rng.standard_normal((b, D, D)) + 1j * rng.standard_normal((b, D, D))
+    S = 0.5 * (S + np.conj(np.swapaxes(S, -1, -2)))
+    S /= np.linalg.norm(S, ord=2, axis=(-2, -1))[:, None, None]
+    H0 = _unitary(b, D, 731) @ (np.eye(D) + eps * S)
+    q, k, v, g = random_cham_inputs(b, 1, D, seed=732)
+    r_ref, _ = oracle.cham_scan(to_np(q), to_np(k), to_np(v), to_np(g),
+                                initial_hologram=(H0.real, H0.imag))
+    errs = {}
+    for mode in ("unitary", "first_order"):
+        hr, hi = _holo(H0)
+        _, out = V.launch_decode_step(None, (q[:, 0], k[:, 0], v[:, 0], g[:, 0], hr, hi), mode=mode)
+        assert V.device_status() == 0
+        errs[mode] = rel_fro(to_np(out), r_ref[:, 0])
+    assert errs["first_order"] <= 1e-4
+    assert errs["unitary"] >= 5 * errs["first_order"]
+
+
+def test_first_order_mode_flags_a_hologram_far_from_unitary():
+    b, D = 2, 128
+    q, k, v, g = random_cham_inputs(b, 1, D, seed=740)
+    H0 = 1.2 * _unitary(b, D, 741)      # E = 0.44 I
+    hr, hi = _holo(H0)
+    V.launch_decode_step(None, (q[:, 0], k[:, 0], v[:, 0], g[:, 0], hr, hi), mode="first_order")
+    assert V.device_status() == VERACE_ERR_STATE
+    assert V.device_status() == 0      # reading clears it
+    hr, hi = _holo(_unitary(b, D, 742))
+    V.launch_decode_step(None, (q[:, 0], k[:, 0], v[:, 0], g[:, 0], hr, hi), mode="first_order")
+    assert V.device_status() == 0
+
+
+def test_nonfinite_tokens_take_the_identity_factor():
+    b, h, d, D = 3, 2, 128, 128
+    sq, sk, sv, dl = random_sssd_inputs(b, 1, h, d, seed=750)
+    cq, ck, cv, g = random_cham_inputs(b, 1, D, seed=751)
+    dl[2, 0, 0] = float("inf")
+    sk[1, 0, 1, 5] = float("nan")
+    ck[1, 0, 7] = float("nan")
+    g[2, 0] = float("nan")
+    psi0 = _psi0(b, h, d, 752)
+    H0 = _unitary(b, D, 753)
+    psi = psi0.clone()
+    hr, hi = _holo(H0)
+    h0r, h0i = hr.clone(), hi.clone()
+    so, co = V.launch_decode_step((sq[:, 0], sk[:, 0], sv[:, 0], dl[:, 0], psi),
+                                  (cq[:, 0], ck[:, 0], cv[:, 0], g[:, 0], hr, hi), mode="first_order")
+    assert V.device_status() == 0
+    # untouched states where the factor is the identity
+    assert torch.equal(psi[2, 0], psi0[2, 0]) and torch.equal(psi[1, 1], psi0[1, 1])
+    assert torch.equal(hr[1], h0r[1]) and torch.equal(hi[2], h0i[2])
+    # the oracle sees the same tokens made identity by a zero gate instead
+    dl_id, sk_id, ck_id, g_id = (to_np(x).copy() for x in (dl, sk, ck, g))
+    dl_id[2, 0, 0] = 0.0
+    dl_id[1, 0, 1] = 0.0
+    sk_id[1, 0, 1, 5] = 0.0
+    ck_id[1, 0, 7] = 0.0
+    g_id[1, 0] = 0.0
+    g_id[2, 0] = 0.0
+    o_ref, psi_ref = oracle.sssd_scan(to_np(sq), sk_id, to_np(sv), dl_id, initial_state=to_np(psi0))
+    r_ref, (Hr_ref, Hi_ref) = oracle.cham_scan(to_np(cq), ck_id, to_np(cv), g_id,
+                                               initial_hologram=(to_np(h0r), to_np(h0i)))
+    assert np.isfinite(to_np(so)).all() and np.isfinite(to_np(co)).all()
+    assert rel_fro(to_np(so), o_ref[:, 0]) <= 1e-4
+    assert rel_fro(to_np(psi), psi_ref) <= 1e-5
+    assert rel_fro(to_np(co), r_ref[:, 0]) <= 1e-4
+    assert rel_fro(to_np(hr) + 1j * to_np(hi), Hr_ref + 1j * Hi_ref) <= 1e-5
+
+
+def test_either_half_alone_matches_the_fused_call():
+    b, h, d, D = 2, 4, 128, 256
+    sq, sk, sv, dl = random_sssd_inputs(b, 1, h, d, seed=760, dtype=torch.bfloat16)
+    cq, ck, cv, g = random_cham_inputs(b, 1, D, seed=761, dtype=torch.bfloat16)
+    psi0 = _psi0(b, h, d, 762)
+    H0 = _holo(_unitary(b, D, 763))
+    p1, p2 = psi0.clone(), psi0.clone()
+    h1 = [x.clone() for x in H0]
+    h2 = [x.clone() for x in H0]
+    so1, co1 = V.launch_decode_step((sq[:, 0], sk[:, 0], sv[:, 0], dl[:, 0], p1),
+                                    (cq[:, 0], ck[:, 0], cv[:, 0], g[:, 0], h1[0], h1[1]))
+    so2, _ = V.launch_decode_step((sq[:, 0], sk[:, 0], sv[:, 0], dl[:, 0], p2), None)
+    _, co2 = V.launch_decode_step(None, (cq[:, 0], ck[:, 0], cv[:, 0], g[:, 0], h2[0], h2[1]))
+    assert torch.equal(so1, so2) and torch.equal(p1, p2)
+    assert torch.equal(co1, co2) and torch.equal(h1[0], h2[0]) and torch.equal(h1[1], h2[1])
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_incremental_decode_matches_full_scan(dtype):
+    """Prefill s0 tokens with the scans, decode n more with DecodeState: the decode
+    outputs and final states equal one scan over all s0 + n tokens."""
+    b, h, d, D, s0, n = 2, 8, 128, 1024, 70, 5
+    sq, sk, sv, dl = random_sssd_inputs(b, s0 + n, h, d, seed=770, dtype=dtype)
+    cq, ck, cv, g = random_cham_inputs(b, s0 + n, D, seed=771, dtype=dtype)
+    so_full, psi_full = V.launch_sssd_scan(sq, sk, sv, dl)
+    co_full, (hr_full, hi_full) = V.launch_cham_update(cq, ck, cv, g)
+    _, psi_p = V.launch_sssd_scan(sq[:, :s0], sk[:, :s0], sv[:, :s0], dl[:, :s0])
+    _, holo_p = V.launch_cham_update(cq[:, :s0], ck[:, :s0], cv[:, :s0], g[:, :s0])
+    st = V.DecodeState(1, b, h, d, D)
+    st.load_layer(0, psi_p, holo_p)
+    so, co = [], []
+    for t in range(s0, s0 + n):
+        o1, o2 = st.step(0, (sq[:, t], sk[:, t], sv[:, t], dl[:, t]), (cq[:, t], ck[:, t], cv[:, t], g[:, t]))
+        so.append(o1)
+        co.append(o2)
+    assert V.device_status() == 0
+    tol = 1e-4 if dtype == torch.float32 else 2e-2
+    assert rel_fro(to_np(torch.stack(so, 1)), to_np(so_full[:, s0:])) <= tol
+    assert rel_fro(to_np(torch.stack(co, 1)), to_np(co_full[:, s0:])) <= tol
+    assert rel_fro(to_np(st.psi[0]), to_np(psi_full)) <= 1e-4
+    assert rel_fro(to_np(st.H_real[0]), to_np(hr_full)) <= 1e-4
+    assert rel_fro(to_np(st.H_imag[0]), to_np(hi_full)) <= 1e-4
+
+
+def test_decode_state_layer_states_round_trip():
+    st = V.DecodeState(2, 3, 2, 64, 128)
+    st.psi.copy_(torch.randn_like(st.psi))
+    st.H_real.copy_(torch.randn_like(st.H_real))
+    st.H_imag.copy_(torch.randn_like(st.H_imag))
+    ls = st.layer_states()
+    assert len(ls) == 2 and len(ls[0]) == 3
+    psi, (hr, hi) = ls[1][2]
+    assert tuple(psi.shape) == (1, 2, 64, 64) and tuple(hr.shape) == (1, 128, 128)
+    st2 = V.DecodeState.from_layer_states(ls)
+    assert torch.equal(st2.psi, st.psi) and torch.equal(st2.H_real, st.H_real)
+    assert torch.equal(st2.H_imag, st.H_imag)
+
+
+def test_unsupported_shapes_are_refused():
+    q, k, v, g = random_cham_inputs(1, 1, 96, seed=780)
+    hr, hi = _holo(_unitary(1, 96, 781))
+    with pytest.raises(RuntimeError, match="unsupported"):
+        V.launch_decode_step(None, (q[:, 0], k[:, 0], v[:, 0], g[:, 0], hr, hi))
+    sq, sk, sv, dl = random_sssd_inputs(1, 1, 1, 130, seed=782)
+    psi = _psi0(1, 1, 130, 783)
+    with pytest.raises(RuntimeError, match="unsupported"):
+        V.launch_decode_step((sq[:, 0], sk[:, 0], sv[:, 0], dl[:, 0], psi), None)
+    with pytest.raises(ValueError):
+        V.launch_decode_step((sq[:, 0], sk[:, 0], sv[:, 0], dl[:, 0], psi), None, mode="exact")

@@ -31,6 +31,8 @@ _SIGNATURES = {
     "verace_cham_scan": (_i, [_p, _p, _p, _p, _p, _p, _p, _p, _p, _i, _i, _i, _i, _p, _c_size, _p]),
     "verace_cham_retract_workspace": (_c_size, [_i, _i]),
     "verace_cham_retract": (_i, [_p, _p, _p, _p, _i, _i, _i, _p, _c_size, _p]),
+    "verace_decode_workspace": (_c_size, [_i, _i]),
+    "verace_decode_step": (_i, [_p] * 13 + [_i] * 6 + [_p, _c_size, _p]),
 }
 
 _lib = None

@@ -56,5 +56,8 @@ class ContinuousHolographicMemory(nn.Module):
         _require_inference(x, "ContinuousHolographicMemory.forward")
         q, k, v, gamma = self.project(x, active_mask)
         rec, (h_real, h_imag) = launch_cham_update(q, k, v, gamma, initial_hologram)
-        y = self.norm(self.w_out(rec))
-        return y, (h_real, h_imag)
+        return self.finish(rec), (h_real, h_imag)
+
+    def finish(self, rec: torch.Tensor) -> torch.Tensor:
+        """Module output from the scan's readout rec [b, s, D] (cham_memory.py:241)."""
+        return self.norm(self.w_out(rec))

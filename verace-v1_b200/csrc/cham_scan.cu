@@ -42,6 +42,7 @@ int cham_tc_scan(const void* q, const void* k, const void* v, const float* gamma
                  float* hr, float* hi, int b, int s, int D, int dtype, void* workspace, cudaStream_t st);
 int tc_read_status(cudaStream_t st, int* status);
 int sssd_tc_read_status(int* status);
+int decode_read_status(unsigned int* status);
 
 namespace {
 
@@ -609,7 +610,12 @@ extern "C" int verace_device_status(void* stream) {
   rc = sssd_tc_read_status(&status2);
   if (rc) return rc;
   status |= status2;
+  unsigned int dstat = 0;
+  rc = decode_read_status(&dstat);
+  if (rc) return rc;
   VERACE_REQUIRE(status == 0, VERACE_ERR_TIMEOUT,
                  "a bounded device-side wait gave up (tensor-core completion never arrived)");
+  VERACE_REQUIRE(dstat == 0, VERACE_ERR_STATE,
+                 "a decode step met a hologram too far from unitary (|(H^H H - I) q| > 1e-2 |q|)");
   return VERACE_OK;
 }

@@ -61,6 +61,9 @@ class SSSDAttention(nn.Module):
         b, s, _ = x.shape
         q, k, v, delta = self.project(x, active_mask)
         o, psi = launch_sssd_scan(q, k, v, delta, initial_state)
-        o_norm = self.head_rmsnorm(o).view(b, s, self.num_heads * self.head_dim)
-        output = self.w_out(o_norm)
-        return output, (psi if return_state else None)
+        return self.finish(o), (psi if return_state else None)
+
+    def finish(self, o: torch.Tensor) -> torch.Tensor:
+        """Module output from the scan's readout o [b, s, h, d] (sssd_attention.py:177-182)."""
+        b, s = o.shape[0], o.shape[1]
+        return self.w_out(self.head_rmsnorm(o).view(b, s, self.num_heads * self.head_dim))
