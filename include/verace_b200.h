@@ -155,7 +155,7 @@ VERACE_API int verace_cham_retract(const float* h_re, const float* h_im, float* 
  *                                   difference; one extra pass over H (two launches);
  *                                   flags |E q| > 1e-2 |q| (see verace_device_status).
  * h == 0 or d == 0 skips SSSD (its pointers may be NULL); D == 0 skips CHAM.
- * Supports d % 4 == 0, d <= 128; D % 128 == 0, D <= 1024.  Workspace (CHAM only):
+ * Supports d % 4 == 0, d <= 128; D % 32 == 0, D <= 2048.  Workspace (CHAM only):
  * verace_decode_workspace(b, D) bytes; calls sharing a workspace must not overlap.
  * ---------------------------------------------------------------------------- */
 enum { VERACE_DECODE_UNITARY = 0, VERACE_DECODE_FIRST_ORDER = 1 };

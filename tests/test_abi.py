@@ -72,7 +72,7 @@ def test_decode_step_rejects_bad_arguments_without_a_device():
     assert rc == 1 and "mode" in _err()
     rc = L.verace_decode_step(*f, 2, 8, 128, 1024, 5, 0, fake, ws, None)
     assert rc == 1 and "dtype" in _err()
-    rc = L.verace_decode_step(*f, 2, 8, 128, 96, 0, 0, fake, ws, None)
+    rc = L.verace_decode_step(*f, 2, 8, 128, 80, 0, 0, fake, ws, None)
     assert rc == 2 and "holographic" in _err()
     rc = L.verace_decode_step(*f, 2, 8, 130, 0, 0, 0, fake, ws, None)
     assert rc == 2 and "head_dim" in _err()

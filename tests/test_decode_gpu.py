@@ -59,7 +59,7 @@ def test_sssd_decode_matches_oracle(dtype, b, h, d):
 
 @pytest.mark.parametrize("dtype,mode", [(torch.float32, "first_order"), (torch.float32, "unitary"),
                                         (torch.bfloat16, "unitary"), (torch.bfloat16, "first_order")])
-@pytest.mark.parametrize("b,D", [(3, 128), (2, 256), (2, 1024)])
+@pytest.mark.parametrize("b,D", [(3, 128), (2, 160), (2, 256), (2, 1024)])
 def test_cham_decode_matches_oracle(dtype, mode, b, D):
     q, k, v, g = random_cham_inputs(b, 1, D, seed=710 + D, dtype=dtype)
     H0 = _unitary(b, D, 711 + D)
@@ -235,8 +235,8 @@ def test_decode_state_layer_states_round_trip():
 
 
 def test_unsupported_shapes_are_refused():
-    q, k, v, g = random_cham_inputs(1, 1, 96, seed=780)
-    hr, hi = _holo(_unitary(1, 96, 781))
+    q, k, v, g = random_cham_inputs(1, 1, 80, seed=780)
+    hr, hi = _holo(_unitary(1, 80, 781))
     with pytest.raises(RuntimeError, match="unsupported"):
         V.launch_decode_step(None, (q[:, 0], k[:, 0], v[:, 0], g[:, 0], hr, hi))
     sq, sk, sv, dl = random_sssd_inputs(1, 1, 1, 130, seed=782)

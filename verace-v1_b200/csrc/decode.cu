@@ -29,19 +29,16 @@
 //                              decode status flag when |E q| > 1e-2 |q| (state too far
 //                              from unitary for either mode).
 //
-// Work split: CTA i < b·h handles SSSD (item, head) i with the whole 128 x 128 state in
-// registers.  The CHAM hologram is cut into column stripes of 32; a cluster of 4 CTAs owns
-// one stripe, each CTA a quarter of its rows, held in registers between the read and the
-// write.  The column reductions kᵀH, vᵀH (and Hᴴu) are summed over the cluster through
-// distributed shared memory, in rank order.  Each CTA writes the readout partial of its
-// rows over its 32 columns; the last CTA of an (item, row quarter) to finish sums the
-// stripes' partials in stripe order and writes y.  No CTA waits on another outside the
-// cluster's hardware barrier.
+// Work split: CTA i < b·h handles SSSD (item, head) i: two passes over its 128 x 128
+// state (column sums, then update, readout and store; the second pass re-reads the rows
+// from L2).  The CHAM hologram is cut into column stripes of 32; one CTA owns a stripe
+// over all D rows and streams it twice: pass 1 forms the column reductions kᵀH, vᵀH
+// (and Hᴴu), pass 2 re-reads the stripe (from L2), updates it, stores it and forms the
+// readout partials of all rows over the stripe's columns, last-read rows first so that
+// the re-read finds them in L2.  The last CTA of an item to
+// finish sums the stripes' partials in stripe order and writes y.  No CTA waits on
+// another.
 #include "common.cuh"
-
-#include <cooperative_groups.h>
-
-namespace cg = cooperative_groups;
 
 namespace verace {
 
@@ -51,9 +48,9 @@ namespace {
 
 constexpr int DT = 256;        // threads per CTA
 constexpr int CWD = 32;        // CHAM stripe width (columns)
-constexpr int CLU = 4;         // CTAs per CHAM cluster (row quarters of a stripe)
-constexpr int MAXD = 1024;     // largest hologram dimension held in registers
+constexpr int MAXD = 2048;     // largest hologram dimension
 constexpr int MAXHD = 128;     // largest SSSD head dimension
+constexpr int UNR = 4;         // row groups of 32 in flight per thread and pass
 constexpr float DRIFT_TOL = 1e-2f;
 
 struct DecodeArgs {
@@ -63,9 +60,9 @@ struct DecodeArgs {
   float* hr; float* hi; void* cout;
   const float* u;              // FIRST_ORDER: [b][2][D] (re, im) of H q
   float* part;                 // [b][D/32][D] readout partials
-  unsigned int* cnt;           // [b][4] stripe counters
+  unsigned int* cnt;           // [b] stripe counters
   float* err2;                 // [b] |E q|² accumulators
-  int b, h, d, D, mode, ns_pad;
+  int b, h, d, D, mode, ns;
 };
 
 template <typename T>
@@ -79,63 +76,76 @@ __device__ __forceinline__ float warp_sum(float x) {
   return x;
 }
 
+__device__ __forceinline__ float& comp(float4& v, int j) {
+  return j == 0 ? v.x : (j == 1 ? v.y : (j == 2 ? v.z : v.w));
+}
+
+// Block-wide sums of four per-thread values (all threads), and the AND of a flag.
+__device__ __forceinline__ void block_sum4(float (&x)[4], bool& flag, float (*scratch)[4]) {
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) x[j] = warp_sum(x[j]);
+  if (lane == 0) {
+#pragma unroll
+    for (int j = 0; j < 4; ++j) scratch[w][j] = x[j];
+  }
+  flag = __syncthreads_and(flag) != 0;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    float t = 0.f;
+#pragma unroll
+    for (int ww = 0; ww < DT / 32; ++ww) t += scratch[ww][j];
+    x[j] = t;
+  }
+}
+
 // ------------------------------------------------------------------------- SSSD
 template <typename T>
 __device__ void sssd_part(const DecodeArgs& A, int chain) {
   __shared__ float ks[MAXHD], vs[MAXHD], qs[MAXHD];
   __shared__ float red[8][MAXHD][2];
-  __shared__ float fac[5];     // m00 m01 m10 m11, ok flag
+  __shared__ float dsc[8][4];
   const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
   const int d = A.d;
   const size_t vec = (size_t)chain * d;
-  for (int i = tid; i < d; i += DT) {
-    ks[i] = ld1<T>(A.sk, vec + i);
-    vs[i] = ld1<T>(A.sv, vec + i);
-    qs[i] = ld1<T>(A.sq, vec + i);
-  }
-  // state rows w + 8 m, columns 4 lane .. 4 lane + 3
   float* P = A.psi + (size_t)chain * d * d;
   const bool colok = 4 * lane < d;
-  float4 ps[MAXHD / 8];
+  // state rows w + 8 m, columns 4 lane .. 4 lane + 3; pass 1: column sums kᵀΨ, vᵀΨ
+  float4 ps[MAXHD / 16];
 #pragma unroll
-  for (int m = 0; m < MAXHD / 8; ++m) {
+  for (int m = 0; m < MAXHD / 16; ++m) {
     const int r = w + 8 * m;
-    ps[m] = (colok && r < d) ? __ldcs(reinterpret_cast<const float4*>(P + (size_t)r * d + 4 * lane))
+    ps[m] = (colok && r < d) ? *reinterpret_cast<const float4*>(P + (size_t)r * d + 4 * lane)
                              : make_float4(0.f, 0.f, 0.f, 0.f);
   }
-  __syncthreads();
-  if (w == 0) {
-    float kk = 0.f, vv = 0.f, kv = 0.f;
-    bool fin = true;
-    for (int i = lane; i < d; i += 32) {
-      kk += ks[i] * ks[i]; vv += vs[i] * vs[i]; kv += ks[i] * vs[i];
-      fin = fin && isfinite(ks[i]) && isfinite(vs[i]);
-    }
-    kk = warp_sum(kk); vv = warp_sum(vv); kv = warp_sum(kv);
-    fin = __all_sync(0xffffffffu, fin);
-    if (lane == 0) {
-      const float dl = A.delta[chain];
-      const float a = 0.5f * dl;
-      const float det = 1.f + a * a * (kk * vv - kv * kv);
-      const float f = -2.f * a / det;
-      const float m00 = f * (a * vv), m01 = f * (1.f - a * kv);
-      const float m10 = f * (-1.f - a * kv), m11 = f * (a * kk);
-      // Non-finite k, v, gate or factor: identity, as the reference's _solve_cayley
-      // substitution does (sssd_attention.py:52-71).
-      const bool ok = fin && isfinite(dl) && isfinite(m00) && isfinite(m01) && isfinite(m10) &&
-                      isfinite(m11);
-      fac[0] = m00; fac[1] = m01; fac[2] = m10; fac[3] = m11; fac[4] = ok ? 1.f : 0.f;
-    }
+  float dots[4] = {0.f, 0.f, 0.f, 0.f};
+  bool fin = true;
+  for (int i = tid; i < d; i += DT) {
+    const float kx = ld1<T>(A.sk, vec + i), vx = ld1<T>(A.sv, vec + i);
+    ks[i] = kx; vs[i] = vx; qs[i] = ld1<T>(A.sq, vec + i);
+    dots[0] += kx * kx; dots[1] += vx * vx; dots[2] += kx * vx;
+    fin = fin && isfinite(kx) && isfinite(vx);
   }
-  // column sums kᵀΨ, vᵀΨ
+  block_sum4(dots, fin, dsc);      // also makes ks/vs/qs visible
   float ak[4] = {0.f, 0.f, 0.f, 0.f}, av[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-  for (int m = 0; m < MAXHD / 8; ++m) {
-    const int r = w + 8 * m;
-    if (r < d) {
-      const float kr = ks[r], vr = vs[r];
-      ak[0] += kr * ps[m].x; ak[1] += kr * ps[m].y; ak[2] += kr * ps[m].z; ak[3] += kr * ps[m].w;
-      av[0] += vr * ps[m].x; av[1] += vr * ps[m].y; av[2] += vr * ps[m].z; av[3] += vr * ps[m].w;
+  for (int half = 0; half < 2; ++half) {
+    if (half == 1) {
+#pragma unroll
+      for (int m = 0; m < MAXHD / 16; ++m) {
+        const int r = w + 8 * (m + MAXHD / 16);
+        ps[m] = (colok && r < d) ? *reinterpret_cast<const float4*>(P + (size_t)r * d + 4 * lane)
+                                 : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+    }
+#pragma unroll
+    for (int m = 0; m < MAXHD / 16; ++m) {
+      const int r = w + 8 * (m + half * MAXHD / 16);
+      if (r < d) {
+        const float kr = ks[r], vr = vs[r];
+        ak[0] += kr * ps[m].x; ak[1] += kr * ps[m].y; ak[2] += kr * ps[m].z; ak[3] += kr * ps[m].w;
+        av[0] += vr * ps[m].x; av[1] += vr * ps[m].y; av[2] += vr * ps[m].z; av[3] += vr * ps[m].w;
+      }
     }
   }
   if (colok) {
@@ -143,7 +153,16 @@ __device__ void sssd_part(const DecodeArgs& A, int chain) {
     for (int j = 0; j < 4; ++j) { red[w][4 * lane + j][0] = ak[j]; red[w][4 * lane + j][1] = av[j]; }
   }
   __syncthreads();
-  const bool ok = fac[4] != 0.f;
+  const float kk = dots[0], vv = dots[1], kv = dots[2];
+  const float dl = A.delta[chain];
+  const float a = 0.5f * dl;
+  const float det = 1.f + a * a * (kk * vv - kv * kv);
+  const float f = -2.f * a / det;
+  const float m00 = f * (a * vv), m01 = f * (1.f - a * kv);
+  const float m10 = f * (-1.f - a * kv), m11 = f * (a * kk);
+  // Non-finite k, v, gate or factor: identity, as the reference's _solve_cayley
+  // substitution does (sssd_attention.py:52-71).
+  const bool ok = fin && isfinite(dl) && isfinite(m00) && isfinite(m01) && isfinite(m10) && isfinite(m11);
   float al[4], be[4];
 #pragma unroll
   for (int j = 0; j < 4; ++j) {
@@ -152,17 +171,19 @@ __device__ void sssd_part(const DecodeArgs& A, int chain) {
 #pragma unroll
       for (int ww = 0; ww < 8; ++ww) { sa += red[ww][4 * lane + j][0]; sb += red[ww][4 * lane + j][1]; }
     }
-    al[j] = fac[0] * sa + fac[1] * sb;   // coefficient of k_r
-    be[j] = fac[2] * sa + fac[3] * sb;   // coefficient of v_r
+    al[j] = m00 * sa + m01 * sb;   // coefficient of k_r
+    be[j] = m10 * sa + m11 * sb;   // coefficient of v_r
   }
   const float4 q4 = colok ? make_float4(qs[4 * lane], qs[4 * lane + 1], qs[4 * lane + 2], qs[4 * lane + 3])
                           : make_float4(0.f, 0.f, 0.f, 0.f);
   T* out = static_cast<T*>(A.sout) + vec;
-#pragma unroll
+  // pass 2: update, readout, store (rows re-read from L2)
+#pragma unroll 4
   for (int m = 0; m < MAXHD / 8; ++m) {
     const int r = w + 8 * m;
-    if (r >= d) continue;            // warp-uniform
-    float4 x = ps[m];
+    if (r >= d) break;               // warp-uniform
+    float4 x = colok ? *reinterpret_cast<const float4*>(P + (size_t)r * d + 4 * lane)
+                     : make_float4(0.f, 0.f, 0.f, 0.f);
     if (ok) {
       const float kr = ks[r], vr = vs[r];
       x.x += kr * al[0] + vr * be[0]; x.y += kr * al[1] + vr * be[1];
@@ -176,116 +197,90 @@ __device__ void sssd_part(const DecodeArgs& A, int chain) {
 }
 
 // ------------------------------------------------------------------------- CHAM
-// Per-column quantities summed over the stripe's rows: kᵀHr, kᵀHi, vᵀHr, vᵀHi, and for
+// Per-column quantities summed over the rows: kᵀHr, kᵀHi, vᵀHr, vᵀHi, and for
 // FIRST_ORDER (Hᴴu)re, (Hᴴu)im.
 constexpr int NQ = 6;
 
-template <typename T, int NP>
-__device__ void cham_part(const DecodeArgs& A, int local) {
-  __shared__ float ks[MAXD], vs[MAXD], qs[MAXD];
-  __shared__ float ur[MAXD / CLU], ui[MAXD / CLU];
+// Thread layout over a stripe (D rows x 32 columns, re and im): 8 threads per row
+// (columns 4 c8 .. 4 c8 + 3), 32 rows per row group (warp w: rows 4 w .. 4 w + 3).
+template <typename T, bool FO>
+__device__ void cham_part(const DecodeArgs& A, int unit) {
+  __shared__ float ks[MAXD], vs[MAXD];
+  __shared__ float qs[CWD];
   __shared__ float red[8][CWD][NQ];
-  __shared__ float mine[CWD][NQ];        // this CTA's sums, read by the whole cluster
-  __shared__ float tot[CWD][NQ];
-  __shared__ float sc[16];
+  __shared__ float coef[CWD][6];         // per column: α (re, im), β (re, im), z (re, im)
+  __shared__ float dsc[8][4];
   __shared__ int last_flag;
-  cg::cluster_group cluster = cg::this_cluster();
   const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
   const int D = A.D;
   const int nst = D / CWD;
-  const int rank = local % CLU;
-  const int sidx = local / CLU;
-  const int item = sidx / nst, stripe = sidx % nst;
-  const int RQ = D / CLU;               // rows of this CTA (= 32 NP)
-  const int row0 = rank * RQ;
-  const int cg8 = lane & 7;             // column group: columns 4 cg8 .. 4 cg8 + 3 of the stripe
-  const int c0 = stripe * CWD + 4 * cg8;
-  const int rp = w * 4 + (lane >> 3);   // row within a 32-row pass
-  const bool fo = A.mode == VERACE_DECODE_FIRST_ORDER;
+  const int item = unit / nst, stripe = unit % nst;
+  const int c8 = lane & 7;
+  const int c0 = stripe * CWD + 4 * c8;
+  const int rp = w * 4 + (lane >> 3);   // row within a group of 32
+  constexpr int nq = FO ? NQ : 4;
 
   const size_t hoff = (size_t)item * D * D;
   float* Hr = A.hr + hoff;
   float* Hi = A.hi + hoff;
-  float4 xr[NP], xi[NP];
-#pragma unroll
-  for (int p = 0; p < NP; ++p) {
-    const size_t e = (size_t)(row0 + p * 32 + rp) * D + c0;
-    xr[p] = __ldcs(reinterpret_cast<const float4*>(Hr + e));
-    xi[p] = __ldcs(reinterpret_cast<const float4*>(Hi + e));
-  }
   const size_t voff = (size_t)item * D;
+  float dots[4] = {0.f, 0.f, 0.f, 0.f};
+  bool fin = true;
+  const int cs0 = stripe * CWD;
   for (int i = tid; i < D; i += DT) {
-    ks[i] = ld1<T>(A.ck, voff + i);
-    vs[i] = ld1<T>(A.cv, voff + i);
-    qs[i] = ld1<T>(A.cq, voff + i);
+    const float kx = ld1<T>(A.ck, voff + i), vx = ld1<T>(A.cv, voff + i), qx = ld1<T>(A.cq, voff + i);
+    ks[i] = kx; vs[i] = vx;
+    if (i >= cs0 && i < cs0 + CWD) qs[i - cs0] = qx;
+    dots[0] += kx * kx; dots[1] += vx * vx; dots[2] += kx * vx; dots[3] += qx * qx;
+    fin = fin && isfinite(kx) && isfinite(vx);
   }
-  if (fo) {
-    for (int i = tid; i < RQ; i += DT) {
-      ur[i] = A.u[(size_t)item * 2 * D + row0 + i];
-      ui[i] = A.u[(size_t)item * 2 * D + D + row0 + i];
-    }
-  }
-  __syncthreads();
-  if (w == 0) {
-    float kk = 0.f, vv = 0.f, kv = 0.f, qq = 0.f;
-    bool fin = true;
-    for (int i = lane; i < D; i += 32) {
-      const float kx = ks[i], vx = vs[i], qx = qs[i];
-      kk += kx * kx; vv += vx * vx; kv += kx * vx; qq += qx * qx;
-      fin = fin && isfinite(kx) && isfinite(vx);
-    }
-    kk = warp_sum(kk); vv = warp_sum(vv); kv = warp_sum(kv); qq = warp_sum(qq);
-    fin = __all_sync(0xffffffffu, fin);
-    if (lane == 0) {
-      const float g = A.gamma[item];
-      const float cc = 0.5f * g;
-      const float dr = 1.f + cc * cc * (kk * vv - kv * kv);
-      const float di = -2.f * cc * kv;
-      const float m2 = dr * dr + di * di;
-      const float fr = 2.f * cc * dr / m2;     // 2c / det
-      const float fi = -2.f * cc * di / m2;
-      // N00 = f (-c vv), N01 = N10 = f (c kv + i), N11 = f (-c kk)
-      const float n00r = fr * (-cc * vv), n00i = fi * (-cc * vv);
-      const float n11r = fr * (-cc * kk), n11i = fi * (-cc * kk);
-      const float n01r = fr * (cc * kv) - fi, n01i = fr + fi * (cc * kv);
-      // Non-finite k, v, gate or factor: identity (the reference's _solve_cham_cayley
-      // substitution, cham_memory.py:54-96).
-      const bool ok = fin && isfinite(g) && isfinite(n00r) && isfinite(n00i) && isfinite(n01r) &&
-                      isfinite(n01i) && isfinite(n11r) && isfinite(n11i);
-      sc[0] = n00r; sc[1] = n00i; sc[2] = n01r; sc[3] = n01i; sc[4] = n11r; sc[5] = n11i;
-      sc[6] = ok ? 1.f : 0.f;
-      sc[7] = qq;
-    }
-  }
-  // per-thread partial column sums over its NP rows
+  block_sum4(dots, fin, dsc);      // also makes ks/vs/qs visible
+  const float* ur = A.u + (size_t)item * 2 * D;
+  const float* ui = ur + D;
+
+  // ---- pass 1: column sums over all rows
   float acc[NQ][4];
 #pragma unroll
   for (int qn = 0; qn < NQ; ++qn)
 #pragma unroll
     for (int j = 0; j < 4; ++j) acc[qn][j] = 0.f;
+  for (int g0 = 0; g0 < D; g0 += 32 * UNR) {
+    float4 xr[UNR], xi[UNR];
 #pragma unroll
-  for (int p = 0; p < NP; ++p) {
-    const int rl = p * 32 + rp;
-    const float kr = ks[row0 + rl], vr = vs[row0 + rl];
-    const float hr4[4] = {xr[p].x, xr[p].y, xr[p].z, xr[p].w};
-    const float hi4[4] = {xi[p].x, xi[p].y, xi[p].z, xi[p].w};
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      acc[0][j] += kr * hr4[j]; acc[1][j] += kr * hi4[j];
-      acc[2][j] += vr * hr4[j]; acc[3][j] += vr * hi4[j];
+    for (int u = 0; u < UNR; ++u) {
+      const int r = g0 + 32 * u + rp;
+      if (r < D) {
+        xr[u] = *reinterpret_cast<const float4*>(Hr + (size_t)r * D + c0);
+        xi[u] = *reinterpret_cast<const float4*>(Hi + (size_t)r * D + c0);
+      } else {
+        xr[u] = xi[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+      }
     }
-    if (fo) {
-      const float a = ur[rl], bq = ui[rl];
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {   // conj(H) u
-        acc[4][j] += hr4[j] * a + hi4[j] * bq;
-        acc[5][j] += hr4[j] * bq - hi4[j] * a;
+    for (int u = 0; u < UNR; ++u) {
+      const int r = g0 + 32 * u + rp;
+      if (r >= D) continue;
+      const float kr = ks[r], vr = vs[r];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float hr_ = comp(xr[u], j), hi_ = comp(xi[u], j);
+        acc[0][j] += kr * hr_; acc[1][j] += kr * hi_;
+        acc[2][j] += vr * hr_; acc[3][j] += vr * hi_;
+      }
+      if (FO) {
+        const float a = __ldg(ur + r), bq = __ldg(ui + r);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {   // conj(H) u
+          const float hr_ = comp(xr[u], j), hi_ = comp(xi[u], j);
+          acc[4][j] += hr_ * a + hi_ * bq;
+          acc[5][j] += hr_ * bq - hi_ * a;
+        }
       }
     }
   }
-  // lanes l, l^8, l^16, l^24 share columns
+  // lanes l, l^8, l^16, l^24 share columns; then the 8 warps
 #pragma unroll
-  for (int qn = 0; qn < NQ; ++qn)
+  for (int qn = 0; qn < nq; ++qn)
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
       float x = acc[qn][j];
@@ -295,114 +290,141 @@ __device__ void cham_part(const DecodeArgs& A, int local) {
     }
   if (lane < 8) {
 #pragma unroll
-    for (int qn = 0; qn < NQ; ++qn)
+    for (int qn = 0; qn < nq; ++qn)
 #pragma unroll
       for (int j = 0; j < 4; ++j) red[w][4 * lane + j][qn] = acc[qn][j];
   }
   __syncthreads();
-  if (tid < CWD * NQ) {
-    const int c = tid / NQ, qn = tid % NQ;
-    float s = 0.f;
+  const float kk = dots[0], vv = dots[1], kv = dots[2], qq = dots[3];
+  const float g = A.gamma[item];
+  const float cc = 0.5f * g;
+  const float dr = 1.f + cc * cc * (kk * vv - kv * kv);
+  const float di = -2.f * cc * kv;
+  const float m2 = dr * dr + di * di;
+  const float fr = 2.f * cc * dr / m2;     // 2c / det
+  const float fi = -2.f * cc * di / m2;
+  // N00 = f (-c vv), N01 = N10 = f (c kv + i), N11 = f (-c kk)
+  const float n00r = fr * (-cc * vv), n00i = fi * (-cc * vv);
+  const float n11r = fr * (-cc * kk), n11i = fi * (-cc * kk);
+  const float n01r = fr * (cc * kv) - fi, n01i = fr + fi * (cc * kv);
+  // Non-finite k, v, gate or factor: identity (the reference's _solve_cham_cayley
+  // substitution, cham_memory.py:54-96).
+  const bool ok = fin && isfinite(g) && isfinite(n00r) && isfinite(n00i) && isfinite(n01r) &&
+                  isfinite(n01i) && isfinite(n11r) && isfinite(n11i);
+  float e2 = 0.f;
+  if (tid < CWD) {
+    const int c = tid;
+    float t[NQ];
 #pragma unroll
-    for (int ww = 0; ww < 8; ++ww) s += red[ww][c][qn];
-    mine[c][qn] = s;
-  }
-  cluster.sync();
-  if (tid < CWD * NQ) {
-    const int c = tid / NQ, qn = tid % NQ;
-    float s = 0.f;
+    for (int qn = 0; qn < NQ; ++qn) {
+      float x = 0.f;
+      if (qn < nq) {
 #pragma unroll
-    for (int r = 0; r < CLU; ++r) {
-      const float* rem = cluster.map_shared_rank(&mine[0][0], r);
-      s += rem[c * NQ + qn];
+        for (int ww = 0; ww < 8; ++ww) x += red[ww][c][qn];
+      }
+      t[qn] = x;
     }
-    tot[c][qn] = s;
+    // α = N00 a + N01 b (coefficient of k_r), β = N01 a + N11 b (coefficient of v_r)
+    coef[c][0] = n00r * t[0] - n00i * t[1] + n01r * t[2] - n01i * t[3];
+    coef[c][1] = n00r * t[1] + n00i * t[0] + n01r * t[3] + n01i * t[2];
+    coef[c][2] = n01r * t[0] - n01i * t[1] + n11r * t[2] - n11i * t[3];
+    coef[c][3] = n01r * t[1] + n01i * t[0] + n11r * t[3] + n11i * t[2];
+    const float qc = qs[c];
+    if (FO) {
+      coef[c][4] = 1.5f * qc - 0.5f * t[4];
+      coef[c][5] = -0.5f * t[5];
+      e2 = (t[4] - qc) * (t[4] - qc) + t[5] * t[5];
+    } else {
+      coef[c][4] = qc;
+      coef[c][5] = 0.f;
+    }
   }
   __syncthreads();
-  const bool ok = sc[6] != 0.f;
-  const float n00r = sc[0], n00i = sc[1], n01r = sc[2], n01i = sc[3], n11r = sc[4], n11i = sc[5];
   float alr[4], ali[4], ber[4], bei[4], zr[4], zi[4];
-  float e2 = 0.f;
 #pragma unroll
   for (int j = 0; j < 4; ++j) {
-    const int c = 4 * cg8 + j;
-    const float akr = tot[c][0], aki = tot[c][1], bkr = tot[c][2], bki = tot[c][3];
-    // α = N00 a + N01 b (coefficient of k_r), β = N01 a + N11 b (coefficient of v_r)
-    alr[j] = n00r * akr - n00i * aki + n01r * bkr - n01i * bki;
-    ali[j] = n00r * aki + n00i * akr + n01r * bki + n01i * bkr;
-    ber[j] = n01r * akr - n01i * aki + n11r * bkr - n11i * bki;
-    bei[j] = n01r * aki + n01i * akr + n11r * bki + n11i * bkr;
-    const float qc = qs[c0 + j];
-    if (fo) {
-      const float wr = tot[c][4], wi = tot[c][5];
-      zr[j] = 1.5f * qc - 0.5f * wr;
-      zi[j] = -0.5f * wi;
-      e2 += (wr - qc) * (wr - qc) + wi * wi;
-    } else {
-      zr[j] = qc;
-      zi[j] = 0.f;
-    }
+    const float* cf = coef[4 * c8 + j];
+    alr[j] = cf[0]; ali[j] = cf[1]; ber[j] = cf[2]; bei[j] = cf[3]; zr[j] = cf[4]; zi[j] = cf[5];
   }
+
+  // ---- pass 2: update, store, readout partials (rows re-read from L2, last-read first)
   float* part = A.part + ((size_t)item * nst + stripe) * D;
+  for (int g0 = (D - 1) / (32 * UNR) * (32 * UNR); g0 >= 0; g0 -= 32 * UNR) {
+    float4 xr[UNR], xi[UNR];
 #pragma unroll
-  for (int p = 0; p < NP; ++p) {
-    const int rl = p * 32 + rp;
-    float4 a = xr[p], bb = xi[p];
-    if (ok) {
-      const float kr = ks[row0 + rl], vr = vs[row0 + rl];
-      a.x += kr * alr[0] + vr * ber[0]; a.y += kr * alr[1] + vr * ber[1];
-      a.z += kr * alr[2] + vr * ber[2]; a.w += kr * alr[3] + vr * ber[3];
-      bb.x += kr * ali[0] + vr * bei[0]; bb.y += kr * ali[1] + vr * bei[1];
-      bb.z += kr * ali[2] + vr * bei[2]; bb.w += kr * ali[3] + vr * bei[3];
+    for (int u = 0; u < UNR; ++u) {
+      const int r = g0 + 32 * u + rp;
+      if (r < D) {
+        xr[u] = __ldcs(reinterpret_cast<const float4*>(Hr + (size_t)r * D + c0));
+        xi[u] = __ldcs(reinterpret_cast<const float4*>(Hi + (size_t)r * D + c0));
+      } else {
+        xr[u] = xi[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+      }
     }
-    float o = a.x * zr[0] + a.y * zr[1] + a.z * zr[2] + a.w * zr[3];
-    if (fo) o -= bb.x * zi[0] + bb.y * zi[1] + bb.z * zi[2] + bb.w * zi[3];
-    o += __shfl_xor_sync(0xffffffffu, o, 1);
-    o += __shfl_xor_sync(0xffffffffu, o, 2);
-    o += __shfl_xor_sync(0xffffffffu, o, 4);
-    if (cg8 == 0) part[row0 + rl] = o;
-    const size_t e = (size_t)(row0 + rl) * D + c0;
-    __stcs(reinterpret_cast<float4*>(Hr + e), a);
-    __stcs(reinterpret_cast<float4*>(Hi + e), bb);
+#pragma unroll
+    for (int u = 0; u < UNR; ++u) {
+      const int r = g0 + 32 * u + rp;
+      float o = 0.f;
+      if (r < D) {
+        if (ok) {
+          const float kr = ks[r], vr = vs[r];
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            comp(xr[u], j) += kr * alr[j] + vr * ber[j];
+            comp(xi[u], j) += kr * ali[j] + vr * bei[j];
+          }
+        }
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          o += comp(xr[u], j) * zr[j];
+          if (FO) o -= comp(xi[u], j) * zi[j];
+        }
+        __stcs(reinterpret_cast<float4*>(Hr + (size_t)r * D + c0), xr[u]);
+        __stcs(reinterpret_cast<float4*>(Hi + (size_t)r * D + c0), xi[u]);
+      }
+      o += __shfl_xor_sync(0xffffffffu, o, 1);
+      o += __shfl_xor_sync(0xffffffffu, o, 2);
+      o += __shfl_xor_sync(0xffffffffu, o, 4);
+      if (c8 == 0 && r < D) part[r] = o;
+    }
   }
-  if (fo && rank == 0) {   // |E q|² of this stripe's columns (the same in every rank)
-    e2 += __shfl_xor_sync(0xffffffffu, e2, 1);
-    e2 += __shfl_xor_sync(0xffffffffu, e2, 2);
-    e2 += __shfl_xor_sync(0xffffffffu, e2, 4);
+  if (FO && w == 0) {   // |E q|² of this stripe's columns
+    e2 = warp_sum(e2);
     if (tid == 0) atomicAdd(&A.err2[item], e2);
   }
-  __threadfence();
+  // publish the partials: CTA barrier, then one release fence and the stripe count
   __syncthreads();
   if (tid == 0) {
-    const unsigned int prev = atomicAdd(&A.cnt[item * CLU + rank], 1u);
+    __threadfence();
+    const unsigned int prev = atomicAdd(&A.cnt[item], 1u);
     last_flag = (prev == (unsigned int)(nst - 1));
+    if (last_flag) __threadfence();
   }
   __syncthreads();
   if (last_flag) {
-    __threadfence();
     const float* pb = A.part + (size_t)item * nst * D;
     T* y = static_cast<T*>(A.cout) + voff;
-    for (int i = tid; i < RQ; i += DT) {
+    for (int i = tid; i < D; i += DT) {
       float s = 0.f;
-      for (int st = 0; st < nst; ++st) s += __ldcg(pb + (size_t)st * D + row0 + i);
-      y[row0 + i] = from_f32<T>(s);
+#pragma unroll 8
+      for (int st = 0; st < nst; ++st) s += __ldcg(pb + (size_t)st * D + i);
+      y[i] = from_f32<T>(s);
     }
-    if (fo && rank == 0 && tid == 0) {
+    if (FO && tid == 0) {
       const float err = __ldcg(&A.err2[item]);
-      if (!(err <= DRIFT_TOL * DRIFT_TOL * sc[7])) atomicOr(&g_decode_status, 1u);
+      if (!(err <= DRIFT_TOL * DRIFT_TOL * qq)) atomicOr(&g_decode_status, 1u);
     }
   }
-  cluster.sync();   // keep this CTA's shared memory alive until the cluster has read it
 }
 
-template <typename T, int NP>
-__global__ void __launch_bounds__(DT, 2) decode_step_kernel(DecodeArgs A) {
+template <typename T, bool CHAM, bool FO>
+__global__ void __launch_bounds__(DT, 3) decode_step_kernel(DecodeArgs A) {
   const int bid = blockIdx.x;
-  if (bid < A.ns_pad) {
-    if (bid < A.b * A.h) sssd_part<T>(A, bid);
+  if (bid < A.ns) {
+    sssd_part<T>(A, bid);
     return;
   }
-  if constexpr (NP > 0) cham_part<T, NP>(A, bid - A.ns_pad);
+  if constexpr (CHAM) cham_part<T, FO>(A, bid - A.ns);
 }
 
 // u = H q for FIRST_ORDER: one warp per row; u layout [b][2][D].
@@ -450,7 +472,7 @@ WsLayout ws_layout(int b, int D) {
   WsLayout L{};
   size_t off = 0;
   L.part = off; off = align_up(off + (size_t)b * (D / CWD) * D * sizeof(float), 256);
-  L.cnt = off;  off = align_up(off + (size_t)b * CLU * sizeof(unsigned int), 256);
+  L.cnt = off;  off = align_up(off + (size_t)b * sizeof(unsigned int), 256);
   L.err2 = off; off = align_up(off + (size_t)b * sizeof(float), 256);
   L.u = off;    off = align_up(off + (size_t)b * 2 * D * sizeof(float), 256);
   L.total = off + 256;
@@ -458,38 +480,16 @@ WsLayout ws_layout(int b, int D) {
 }
 
 template <typename T>
-int launch_typed(const DecodeArgs& A, int np, cudaStream_t st) {
-  const int ncham = (A.D > 0) ? A.b * (A.D / CWD) * CLU : 0;
-  const int grid = A.ns_pad + ncham;
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(grid);
-  cfg.blockDim = dim3(DT);
-  cfg.dynamicSmemBytes = 0;
-  cfg.stream = st;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = CLU;
-  attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  cudaError_t e;
-  switch (np) {
-    case 0: e = cudaLaunchKernelEx(&cfg, decode_step_kernel<T, 0>, A); break;
-    case 1: e = cudaLaunchKernelEx(&cfg, decode_step_kernel<T, 1>, A); break;
-    case 2: e = cudaLaunchKernelEx(&cfg, decode_step_kernel<T, 2>, A); break;
-    case 3: e = cudaLaunchKernelEx(&cfg, decode_step_kernel<T, 3>, A); break;
-    case 4: e = cudaLaunchKernelEx(&cfg, decode_step_kernel<T, 4>, A); break;
-    case 5: e = cudaLaunchKernelEx(&cfg, decode_step_kernel<T, 5>, A); break;
-    case 6: e = cudaLaunchKernelEx(&cfg, decode_step_kernel<T, 6>, A); break;
-    case 7: e = cudaLaunchKernelEx(&cfg, decode_step_kernel<T, 7>, A); break;
-    case 8: e = cudaLaunchKernelEx(&cfg, decode_step_kernel<T, 8>, A); break;
-    default: set_error("verace_decode_step: unsupported D"); return VERACE_ERR_UNSUPPORTED;
-  }
-  if (e != cudaSuccess) {
-    set_error("verace_decode_step: launch failed: %s", cudaGetErrorString(e));
-    return VERACE_ERR_CUDA;
-  }
+int launch_typed(const DecodeArgs& A, cudaStream_t st) {
+  const int ncham = (A.D > 0) ? A.b * (A.D / CWD) : 0;
+  const int grid = A.ns + ncham;
+  const bool fo = A.mode == VERACE_DECODE_FIRST_ORDER;
+  if (A.D == 0)
+    decode_step_kernel<T, false, false><<<grid, DT, 0, st>>>(A);
+  else if (fo)
+    decode_step_kernel<T, true, true><<<grid, DT, 0, st>>>(A);
+  else
+    decode_step_kernel<T, true, false><<<grid, DT, 0, st>>>(A);
   return check_launch("decode_step_kernel");
 }
 
@@ -538,9 +538,9 @@ extern "C" int verace_decode_step(const void* sssd_q, const void* sssd_k, const 
   if (do_cham) {
     VERACE_REQUIRE(cham_q && cham_k && cham_v && gamma && h_re && h_im && cham_out, VERACE_ERR_INVALID,
                    "verace_decode_step: NULL CHAM pointer");
-    VERACE_REQUIRE(D % (CWD * CLU) == 0 && D <= MAXD, VERACE_ERR_UNSUPPORTED,
-                   "verace_decode_step: holographic dim %d unsupported (multiple of %d, at most %d)", D,
-                   CWD * CLU, MAXD);
+    VERACE_REQUIRE(D % CWD == 0 && D <= MAXD, VERACE_ERR_UNSUPPORTED,
+                   "verace_decode_step: holographic dim %d unsupported (a multiple of %d, at most %d)", D, CWD,
+                   MAXD);
     VERACE_REQUIRE((((uintptr_t)h_re | (uintptr_t)h_im) & 15) == 0, VERACE_ERR_INVALID,
                    "verace_decode_step: hologram must be 16-byte aligned");
     const size_t need = verace_decode_workspace(b, D);
@@ -557,7 +557,7 @@ extern "C" int verace_decode_step(const void* sssd_q, const void* sssd_k, const 
   A.d = do_sssd ? d : 0;
   A.D = do_cham ? D : 0;
   A.mode = mode;
-  A.ns_pad = (A.b * A.h + CLU - 1) / CLU * CLU;
+  A.ns = A.b * A.h;
   if (do_cham) {
     const WsLayout L = ws_layout(b, D);
     char* base = (char*)align_up((size_t)workspace, 256);
@@ -575,10 +575,9 @@ extern "C" int verace_decode_step(const void* sssd_q, const void* sssd_k, const 
       if (rc) return rc;
     }
   }
-  const int np = do_cham ? D / (CWD * CLU) : 0;
   switch (dtype) {
-    case VERACE_F32: return launch_typed<float>(A, np, st);
-    case VERACE_BF16: return launch_typed<__nv_bfloat16>(A, np, st);
-    default: return launch_typed<__half>(A, np, st);
+    case VERACE_F32: return launch_typed<float>(A, st);
+    case VERACE_BF16: return launch_typed<__nv_bfloat16>(A, st);
+    default: return launch_typed<__half>(A, st);
   }
 }
