@@ -158,6 +158,22 @@ VERACE_API int verace_cham_retract(const float* h_re, const float* h_im, float* 
  * Supports d % 4 == 0, d <= 128; D % 32 == 0, D <= 2048.  Workspace (CHAM only):
  * verace_decode_workspace(b, D) bytes; calls sharing a workspace must not overlap.
  * ---------------------------------------------------------------------------- */
+/* ------------------------------------------------------------------------------
+ * Mixer prologue: the elementwise tail of the q/k/v/gate projections of both mixers,
+ * fused into one pass over one concatenated projection (the GEMM itself stays with the
+ * caller's BLAS).  Replaces the normalisation and gate code of SSSDAttention.project
+ * (verace_v1/modules/sssd_attention.py:116-126) and ContinuousHolographicMemory.project
+ * (verace_v1/modules/cham_memory.py:129-153).
+ * y      : [n, ld] (dtype), row = q | k | v (each heads*head_dim) | gate (gate_cols)
+ * q, k, v: [n, heads*head_dim] (dtype): F.normalize(., p=2, dim=-1) per head (eps 1e-12),
+ *          v first through SiLU when silu_v != 0 (CHAM)
+ * gate   : [n, gate_cols] fp32: 0.1 * sigmoid(.) * mask[row] (mask [n] bytes, or NULL)
+ * Supports head_dim % 8 == 0, head_dim <= 2048; ld % 8 == 0.
+ * ---------------------------------------------------------------------------- */
+VERACE_API int verace_mixer_prologue(const void* y, long long ld, void* q, void* k, void* v, float* gate,
+                                     const unsigned char* mask, long long n, int heads, int head_dim,
+                                     int gate_cols, int silu_v, int dtype, void* stream);
+
 enum { VERACE_DECODE_UNITARY = 0, VERACE_DECODE_FIRST_ORDER = 1 };
 VERACE_API size_t verace_decode_workspace(int b, int D);
 VERACE_API int verace_decode_step(const void* sssd_q, const void* sssd_k, const void* sssd_v,

@@ -23,9 +23,10 @@ def test_workspace_queries_grow_with_problem_size():
     a = L.verace_sssd_scan_workspace(2, 512, 8, 128)
     b = L.verace_sssd_scan_workspace(2, 1024, 8, 128)
     assert 0 < a < b
-    c0 = L.verace_cham_scan_workspace(2, 512, 1024, 0)
-    c1 = L.verace_cham_scan_workspace(2, 512, 1024, 1)
-    assert 0 < c0 < c1
+    for has_h0 in (0, 1):
+        c0 = L.verace_cham_scan_workspace(2, 512, 1024, has_h0)
+        c1 = L.verace_cham_scan_workspace(2, 1024, 1024, has_h0)
+        assert 0 < c0 < c1
     assert L.verace_cham_retract_workspace(2, 1024) >= 4 * 2 * 1024 * 1024 * 4
 
 

@@ -82,3 +82,23 @@ def test_tc_scan_zero_gamma_and_nonfinite_tokens():
     _status_ok()
     torch.testing.assert_close(Hr_b, Hr_i)
     torch.testing.assert_close(out_b, out_i)
+
+
+@pytest.mark.parametrize("b,s,D", [(3, 600, 256), (2, 130, 1024), (1, 64, 128)])
+def test_batched_readout_schedule_matches_merged_schedule(b, s, D):
+    """Column passes two CTAs per SM with readouts batched over up to 8 chunks
+    (VERACE_CHAM_BATCHED=1) against the merged one-launch-per-chunk schedule (the
+    default): same arithmetic, so the results agree to fp32 accumulation order (the E
+    partials are summed atomically)."""
+    q, k, v, g = random_cham_inputs(b, s, D, seed=800 + s, dtype=torch.bfloat16)
+    k[0, min(5, s - 1), 3] = float("nan")
+    out_m, (Hr_m, Hi_m) = V.launch_cham_update(q, k, v, g)
+    os.environ["VERACE_CHAM_BATCHED"] = "1"
+    try:
+        out, (Hr, Hi) = V.launch_cham_update(q, k, v, g)
+    finally:
+        del os.environ["VERACE_CHAM_BATCHED"]
+    _status_ok()
+    assert rel_fro(to_np(Hr), to_np(Hr_m)) <= 1e-6 and rel_fro(to_np(Hi), to_np(Hi_m)) <= 1e-6
+    assert rel_fro(to_np(out), to_np(out_m)) <= 1e-2   # bf16 outputs: at most one rounding step apart
+    assert torch.isfinite(out.float()).all()

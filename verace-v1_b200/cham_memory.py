@@ -17,7 +17,7 @@ import torch
 import torch.nn as nn
 import torch.nn.functional as F
 
-from .kernels import cham_retract, launch_cham_update
+from .kernels import cham_retract, concat_weights, launch_cham_update, mixer_prologue
 from .sssd_attention import _require_inference
 
 
@@ -39,15 +39,22 @@ class ContinuousHolographicMemory(nn.Module):
         self.norm = nn.RMSNorm(hidden_dim)
 
     def project(self, x: torch.Tensor, active_mask: Optional[torch.Tensor] = None):
-        """q, k, v [b, s, D] and gamma [b, s] (cham_memory.py:129-153)."""
+        """q, k, v [b, s, D] and gamma [b, s] (cham_memory.py:129-153): one GEMM with the
+        concatenated projection weights, then the fused normalisation/SiLU/gate pass."""
         b, s, _ = x.shape
-        q = F.normalize(self.w_q(x), p=2, dim=-1)
-        k = F.normalize(self.w_k(x), p=2, dim=-1)
-        v = F.normalize(F.silu(self.w_v(x)), p=2, dim=-1)
-        gamma = 0.1 * torch.sigmoid(self.w_gamma(x)).view(b, s)
-        if active_mask is not None:
-            gamma = gamma * active_mask.reshape(b, s).to(gamma.dtype)
-        return q, k, v, gamma
+        D = self.holographic_dim
+        if D % 8:   # widths the fused pass does not tile: the same math as torch ops on the GPU
+            q = F.normalize(self.w_q(x), p=2, dim=-1)
+            k = F.normalize(self.w_k(x), p=2, dim=-1)
+            v = F.normalize(F.silu(self.w_v(x)), p=2, dim=-1)
+            gamma = 0.1 * torch.sigmoid(self.w_gamma(x)).view(b, s)
+            if active_mask is not None:
+                gamma = gamma * active_mask.reshape(b, s).to(gamma.dtype)
+            return q, k, v, gamma
+        W = concat_weights(self, [self.w_q.weight, self.w_k.weight, self.w_v.weight, self.w_gamma.weight])
+        y = F.linear(x, W).reshape(b * s, -1)
+        q, k, v, gamma = mixer_prologue(y, 1, D, 1, True, active_mask)
+        return q.view(b, s, D), k.view(b, s, D), v.view(b, s, D), gamma.view(b, s)
 
     def forward(self, x: torch.Tensor,
                 initial_hologram: Optional[Tuple[torch.Tensor, torch.Tensor]] = None,

@@ -18,6 +18,9 @@
 //                    that column block of S_next.  TMEM: 320 of 512 columns.
 //   cham_tc_readout  one CTA per (item, 128 rows): Re(S Y) + W mask(E).
 #include "common.cuh"
+
+#include <algorithm>
+#include <cstdlib>
 #include "tc.cuh"
 #include "wy_solve.cuh"
 
@@ -47,12 +50,16 @@ constexpr int Z_TILE = R2 * N2 * 2;        // 16 KB: 128 x 64 bf16
 constexpr int CA_TILE = R2 * NB2 * 2;      //  8 KB: 128 x 32 bf16
 constexpr int Y_TILE = C2 * NB2 * 2;       //  4 KB: 64 tokens x 32 columns bf16
 
+constexpr int RING = 8;          // chunk end states kept for one batched readout launch
+
 struct TcWs {
   unsigned char* T;          // [b][nch][4][T_TILE]: Tr_hi, Tr_lo, Ti_hi, Ti_lo
   float* E;                  // [b][nch][R2][C2]
   unsigned long long* bad;   // [b][nch]
   float* Hre;
   float* Him;
+  float* ring;               // [min(nch, RING)][b][D][D]: real parts of chunk end states
+  int nring;
 };
 
 size_t tc_ws_layout(int b, int s, int D, TcWs* w, char* base) {
@@ -66,6 +73,8 @@ size_t tc_ws_layout(int b, int s, int D, TcWs* w, char* base) {
   const bool ping = nch >= 2;
   t.Hre = (float*)take(ping ? (size_t)b * D * D * sizeof(float) : 0);
   t.Him = (float*)take(ping ? (size_t)b * D * D * sizeof(float) : 0);
+  t.nring = (int)std::min<size_t>(nch, RING);
+  t.ring = (float*)take((size_t)t.nring * b * D * D * sizeof(float));
   if (w) *w = t;
   return off + 256;
 }
@@ -1140,7 +1149,7 @@ __device__ __forceinline__ void
 readout_ws_body(const CUtensorMap& tm_k, const CUtensorMap& tm_v, const CUtensorMap& tm_q,
                 const CUtensorMap& tm_sr, const float* __restrict__ Ews,
                 const unsigned long long* __restrict__ badws, __nv_bfloat16* __restrict__ out,
-                int S, int D, int nch, int c, int bx) {
+                int S, int D, int nch, int c, int bx, int item, int srow) {
   extern __shared__ __align__(1024) unsigned char smw[];
   uint64_t* bars = reinterpret_cast<uint64_t*>(smw + WS_BAR);
   uint32_t* tslot = reinterpret_cast<uint32_t*>(smw + WS_BAR + 8 * N_BARS);
@@ -1153,7 +1162,7 @@ readout_ws_body(const CUtensorMap& tm_k, const CUtensorMap& tm_v, const CUtensor
   unsigned char* sEl = sEh + 16 * 1024;
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int item = blockIdx.y, i0 = bx * R2;
+  const int i0 = bx * R2;
   const int t0 = c * C2, nt = min(C2, S - t0);
   const size_t chunk = (size_t)item * nch + c;
   const unsigned long long bad = badws[chunk];
@@ -1181,8 +1190,8 @@ readout_ws_body(const CUtensorMap& tm_k, const CUtensorMap& tm_v, const CUtensor
       auto issue = [&](int kt) {
         const int s = kt & 1;
         tc::mbar_expect_tx(&bars[B_TFULL + s], 32 * 1024 + 8 * 1024);
-        tc::tma_load_2d(stA(s), &tm_sr, kt * RKT, item * D + i0, &bars[B_TFULL + s]);
-        tc::tma_load_2d(stA(s) + 16 * 1024, &tm_sr, kt * RKT + 32, item * D + i0, &bars[B_TFULL + s]);
+        tc::tma_load_2d(stA(s), &tm_sr, kt * RKT, srow + i0, &bars[B_TFULL + s]);
+        tc::tma_load_2d(stA(s) + 16 * 1024, &tm_sr, kt * RKT + 32, srow + i0, &bars[B_TFULL + s]);
         tc::tma_load_3d(stY(s), &tm_q, kt * RKT, t0, item, &bars[B_TFULL + s]);
       };
       constexpr uint32_t ID_O = tc::idesc_bf16(128, C2, false, false);
@@ -1478,7 +1487,390 @@ cham_tc_step_ws(const __grid_constant__ CUtensorMap tm_k, const __grid_constant_
     colpass_ws_body(tm_k, tm_v, tm_sr, tm_si, tm_dr, tm_di, q, Tws, Ews, badws, src_identity, dst_r, dst_i, S, D,
                     nch, c, blockIdx.x);
   else
-    readout_ws_body(tm_k, tm_v, tm_q, tm_sr, Ews, badws, out, S, D, nch, c - 1, blockIdx.x - ncol);
+    readout_ws_body(tm_k, tm_v, tm_q, tm_sr, Ews, badws, out, S, D, nch, c - 1, blockIdx.x - ncol, blockIdx.y,
+                    blockIdx.y * D);
+}
+
+// ---------------------------------------------------------------------------------
+// Column pass, two CTAs per SM (bf16 inputs).  Same arithmetic as colpass_ws_body, laid
+// out so that 96 KB of shared memory and 256 TMEM columns suffice: at b = 8, D = 1024
+// all 256 column blocks of a chunk are resident at once (the 320-CTA merged launch took
+// three CTA generations per SM).  The readout runs in separate launches over batches of
+// chunks (cham_tc_readout_batch), from the chunks' end states kept in a ring of buffers.
+//
+// smem: ring [0, 64K) = 2 slots of 32 KB
+//         phase A: slot = W half tile (64 state rows x 128 vectors: k box 8K | v box 8K)
+//                  | state half tile (re 8K | im 8K, fp32 SW128), split in place into
+//                  bf16 hi 8K | lo 8K (the MMA B operand)
+//         phase T: Tr (hi | lo) across both slots, then Ti (hi | lo)
+//         phase E: Ca hi/lo (16K) | Y (4K) in slot 0
+//         phase B: slot = W tile (128 state rows x 128 vectors, 32K)
+//       ZC [64K, 96K): Z split (hi 16K | lo 16K), then Cm split
+//       barriers, TMEM slot, failure flag at 96K
+// TMEM (256 columns): Z [0,64) P1 [64,128) P2 [128,192) E [192,256); dH[2] reuse P1/P2.
+// Phase B reads the state rows from global memory and writes the updated rows with
+// vector stores (each thread one row of 32 columns of one plane).
+constexpr int CP2_SLOT = 32 * 1024, CP2_ZC = 64 * 1024, CP2_BAR = 96 * 1024;
+constexpr int CP2_SMEM = CP2_BAR + 256;
+constexpr int KH = 64;   // state rows per phase-A half tile
+enum { B2_FULL = 0, B2_SPL = 2, B2_MD = 4, B2_TT = 6, B2_ZR = 7, B2_P1 = 8, B2_MT = 9, B2_CR = 10, B2_ME = 11,
+       B2_DH = 12, B2_DF = 14, N_BARS2 = 16 };
+
+__global__ void __launch_bounds__(WS_THREADS, 2)
+cham_tc_colpass2(const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
+                 const __grid_constant__ CUtensorMap tm_sr, const __grid_constant__ CUtensorMap tm_si,
+                 int src_row_re, int src_row_im, const float* __restrict__ src_r, const float* __restrict__ src_i,
+                 float* __restrict__ dst_r, float* __restrict__ dst_i, const __nv_bfloat16* __restrict__ q,
+                 const unsigned char* __restrict__ Tws, float* __restrict__ Ews,
+                 const unsigned long long* __restrict__ badws, int src_identity, int S, int D, int nch, int c) {
+  extern __shared__ __align__(1024) unsigned char smc[];
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smc + CP2_BAR);
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(smc + CP2_BAR + 8 * N_BARS2);
+  volatile int* fail = reinterpret_cast<volatile int*>(smc + CP2_BAR + 8 * N_BARS2 + 16);
+  auto slot = [&](int s) { return smc + s * CP2_SLOT; };
+  unsigned char* sZh = smc + CP2_ZC;      // Z split, then Cm split (MN-major, 16K each)
+  unsigned char* sZl = sZh + Z_TILE;
+  unsigned char* sAh = smc;               // phase E: Re(Cm) K-major hi/lo, Y
+  unsigned char* sAl = smc + CA_TILE;
+  unsigned char* sY = smc + 2 * CA_TILE;
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int item = blockIdx.y, j0 = blockIdx.x * NB2;
+  const int t0 = c * C2, nt = min(C2, S - t0);
+  const size_t chunk = (size_t)item * nch + c;
+  const unsigned long long bad = badws[chunk];
+  const bool patch_w = bad != 0ull;       // padded rows come back zero from the TMA bounds
+  const int NH = D / KH, NT = D / KT;
+
+  if (warp == 0) tc::tmem_alloc(tslot, 256);
+  if (tid == 0) {
+    for (int i = 0; i < N_BARS2; ++i) tc::mbar_init(&bars[i], 1);
+    *fail = 0;
+    tc::fence_mbar_init();
+  }
+  tc::fence_before_sync();
+  __syncthreads();
+  tc::fence_after_sync();
+  const uint32_t tbase = *tslot;
+  const uint32_t tZ = tbase, tP1 = tbase + 64, tP2 = tbase + 128, tE = tbase + 192, tDH = tbase + 64;
+
+  if (warp == 8) {
+    // ======================= producer (one thread) =======================
+    if (lane == 0) {
+      bool ok = true;
+      uint32_t nfull[2] = {0, 0}, nspl[2] = {0, 0}, nmd[2] = {0, 0}, ndh[2] = {0, 0}, ndf[2] = {0, 0};
+      auto pwait = [&](int b, uint32_t par) {
+        if (!ok) return false;
+        if (*fail || !tc::mbar_wait(&bars[b], par, MAX_POLLS)) { ok = false; *fail = 1; record_timeout(); }
+        return ok;
+      };
+      auto issue_a = [&](int h) {   // phase-A half tile h into slot h & 1
+        const int s = h & 1;
+        unsigned char* w = slot(s);
+        tc::mbar_expect_tx(&bars[B2_FULL + s], 16 * 1024 + (src_identity ? 0 : 16 * 1024));
+        tc::tma_load_3d(w, &tm_k, h * KH, t0, item, &bars[B2_FULL + s]);
+        tc::tma_load_3d(w + 8192, &tm_v, h * KH, t0, item, &bars[B2_FULL + s]);
+        if (!src_identity) {
+          tc::tma_load_2d(w + 16384, &tm_sr, j0, (src_row_re + item) * D + h * KH, &bars[B2_FULL + s]);
+          tc::tma_load_2d(w + 24576, &tm_si, j0, (src_row_im + item) * D + h * KH, &bars[B2_FULL + s]);
+        }
+      };
+      auto issue_b = [&](int kt) {  // phase-B W tile kt into slot (kt + 1) & 1
+        const int s = (kt + 1) & 1;
+        unsigned char* w = slot(s);
+        tc::mbar_expect_tx(&bars[B2_FULL + s], W_TILE);
+#pragma unroll
+        for (int kb = 0; kb < KT / 64; ++kb) {
+          tc::tma_load_3d(w + kb * 16384, &tm_k, kt * KT + kb * 64, t0, item, &bars[B2_FULL + s]);
+          tc::tma_load_3d(w + kb * 16384 + 8192, &tm_v, kt * KT + kb * 64, t0, item, &bars[B2_FULL + s]);
+        }
+      };
+      constexpr uint32_t ID_Z = tc::idesc_bf16(128, N2, false, true);
+      constexpr uint32_t ID_H = tc::idesc_bf16(128, N2, true, true);
+      // ---- phase A: Z = Wᵀ S over 64-row half tiles
+      issue_a(0);
+      if (NH > 1) issue_a(1);
+      for (int h = 0; h < NH && ok; ++h) {
+        const int s = h & 1;
+        if (!pwait(B2_FULL + s, nfull[s]++ & 1) || !pwait(B2_SPL + s, nspl[s]++ & 1)) break;
+        tc::fence_after_sync();
+        const uint32_t aw = tc::smem_addr(slot(s));
+        const uint32_t bh = aw + 16384, bl = aw + 24576;
+#pragma unroll 1
+        for (int ks = 0; ks < KH / 16; ++ks) {
+          const uint64_t a = tc::sdesc_sw128(aw + ks * 32, 16, 1024);
+          tc::mma_bf16(tZ, a, tc::sdesc(bh + ks * 2 * (N2 / 8) * 128, (N2 / 8) * 128, 128), ID_Z,
+                       (h > 0 || ks > 0) ? 1u : 0u);
+          tc::mma_bf16(tZ, a, tc::sdesc(bl + ks * 2 * (N2 / 8) * 128, (N2 / 8) * 128, 128), ID_Z, 1u);
+        }
+        tc::commit(&bars[B2_MD + s]);
+        ++nmd[s];
+        if (h + 2 < NH) {
+          if (!pwait(B2_MD + s, (nmd[s] - 1) & 1)) break;
+          issue_a(h + 2);
+        }
+      }
+      // ---- phase T: P1 = Tr Z, then P2 = Ti Z, T halves through the ring
+      const int sl = (NH - 1) & 1;
+      const unsigned char* tsrc = Tws + chunk * 4 * T_TILE;
+      constexpr uint32_t ID_T = tc::idesc_bf16(128, N2, false, true);
+      auto t_mmas = [&](uint32_t td) {
+        const uint32_t th = tc::smem_addr(slot(0)), tl = tc::smem_addr(slot(1));
+        const uint32_t zh = tc::smem_addr(sZh), zl = tc::smem_addr(sZl);
+#pragma unroll 1
+        for (int ks = 0; ks < R2 / 16; ++ks) {
+          const uint64_t ah = tc::sdesc(th + ks * 2 * R2 * 16, R2 * 16, 128);
+          const uint64_t al = tc::sdesc(tl + ks * 2 * R2 * 16, R2 * 16, 128);
+          const uint64_t b_h = tc::sdesc(zh + ks * 2 * (N2 / 8) * 128, (N2 / 8) * 128, 128);
+          const uint64_t b_l = tc::sdesc(zl + ks * 2 * (N2 / 8) * 128, (N2 / 8) * 128, 128);
+          tc::mma_bf16(td, ah, b_h, ID_T, ks > 0 ? 1u : 0u);
+          tc::mma_bf16(td, ah, b_l, ID_T, 1u);
+          tc::mma_bf16(td, al, b_h, ID_T, 1u);
+        }
+      };
+      if (ok && pwait(B2_MD + sl, (nmd[sl] - 1) & 1)) {   // every phase-A MMA done: ring free
+        tc::mbar_expect_tx(&bars[B2_TT], 2 * T_TILE);
+        tc::bulk_load(slot(0), tsrc, T_TILE, &bars[B2_TT]);
+        tc::bulk_load(slot(1), tsrc + T_TILE, T_TILE, &bars[B2_TT]);
+        if (pwait(B2_ZR, 0) && pwait(B2_TT, 0)) {
+          tc::fence_after_sync();
+          t_mmas(tP1);
+          tc::commit(&bars[B2_P1]);
+          if (pwait(B2_P1, 0)) {
+            tc::mbar_expect_tx(&bars[B2_TT], 2 * T_TILE);
+            tc::bulk_load(slot(0), tsrc + 2 * T_TILE, T_TILE, &bars[B2_TT]);
+            tc::bulk_load(slot(1), tsrc + 3 * T_TILE, T_TILE, &bars[B2_TT]);
+            if (pwait(B2_TT, 1)) {
+              tc::fence_after_sync();
+              t_mmas(tP2);
+              tc::commit(&bars[B2_MT]);
+            }
+          }
+        }
+      }
+      // ---- phase E: E = Re(Cm) Y (slot 0); the first phase-B W tile goes to slot 1
+      if (ok && pwait(B2_MT, 0)) {
+        issue_b(0);
+        if (pwait(B2_CR, 0)) {
+          tc::fence_after_sync();
+          constexpr uint32_t ID_E = tc::idesc_bf16(128, C2, false, false);
+          const uint32_t ah = tc::smem_addr(sAh), al = tc::smem_addr(sAl), yh = tc::smem_addr(sY);
+#pragma unroll 1
+          for (int ks = 0; ks < NB2 / 16; ++ks) {
+            const uint64_t b_h = tc::sdesc(yh + ks * 2 * C2 * 16, C2 * 16, 128);
+            tc::mma_bf16(tE, tc::sdesc(ah + ks * 2 * R2 * 16, R2 * 16, 128), b_h, ID_E, ks > 0 ? 1u : 0u);
+            tc::mma_bf16(tE, tc::sdesc(al + ks * 2 * R2 * 16, R2 * 16, 128), b_h, ID_E, 1u);
+          }
+          tc::commit(&bars[B2_ME]);
+        }
+      }
+      // ---- phase B: dH = W Cm per 128-row tile, double-buffered in TMEM
+      if (ok && pwait(B2_ME, 0)) {
+        if (NT > 1) issue_b(1);
+        for (int kt = 0; kt < NT && ok; ++kt) {
+          const int s = (kt + 1) & 1, d = kt & 1;
+          if (!pwait(B2_FULL + s, nfull[s]++ & 1)) break;
+          if (patch_w && !pwait(B2_SPL + s, nspl[s]++ & 1)) break;
+          if (kt >= 2 && !pwait(B2_DF + d, ndf[d]++ & 1)) break;
+          tc::fence_after_sync();
+          const uint32_t aw = tc::smem_addr(slot(s));
+          const uint32_t ch = tc::smem_addr(sZh), cl = tc::smem_addr(sZl);
+#pragma unroll 1
+          for (int ks = 0; ks < R2 / 16; ++ks) {
+            const uint64_t a = tc::sdesc_sw128(aw + ks * 2048, 16384, 1024);
+            tc::mma_bf16(tDH + 64 * d, a, tc::sdesc(ch + ks * 2 * (N2 / 8) * 128, (N2 / 8) * 128, 128), ID_H,
+                         ks > 0 ? 1u : 0u);
+            tc::mma_bf16(tDH + 64 * d, a, tc::sdesc(cl + ks * 2 * (N2 / 8) * 128, (N2 / 8) * 128, 128), ID_H, 1u);
+          }
+          tc::commit(&bars[B2_DH + d]);
+          ++ndh[d];
+          if (kt + 2 < NT) {
+            if (!pwait(B2_DH + d, (ndh[d] - 1) & 1)) break;
+            issue_b(kt + 2);
+          }
+        }
+      }
+    }
+  } else {
+    // ======================= consumers (warps 0-7) =======================
+    const uint32_t lane_base = (uint32_t)(32 * (warp & 3)) << 16;
+    const int row = 32 * (warp & 3) + lane, half = warp >> 2;
+    bool ok = true;
+    uint32_t nfull[2] = {0, 0};
+    auto cwait = [&](int b, uint32_t par) {
+      bool mine = ok && !*fail && tc::mbar_wait(&bars[b], par, MAX_POLLS);
+      const bool all = consumers_all(mine);
+      if (!all) { if (ok && tid == 0) record_timeout(); ok = false; *fail = 1; }
+      return ok;
+    };
+    auto zero_bad_rows = [&](unsigned char* w, int nblk) {   // swizzled W (half) tile, nblk blocks of 16K
+      for (int e = tid; e < R2 * 8 * nblk; e += CONS) {
+        const int r = e % R2, cc = e / R2;                    // 16-byte chunk cc of row r
+        if ((bad >> tok(r)) & 1ull)
+          *reinterpret_cast<uint4*>(w + (cc >> 3) * 16384 + r * 128 + (((cc & 7) ^ (r & 7)) << 4)) =
+              make_uint4(0, 0, 0, 0);
+      }
+    };
+    // ---- phase A: split each state half tile in place
+    for (int h = 0; h < NH && ok; ++h) {
+      const int s = h & 1;
+      if (!cwait(B2_FULL + s, nfull[s]++ & 1)) break;
+      unsigned char* w = slot(s);
+      if (patch_w) zero_bad_rows(w, 1);
+      float x[2][8];
+#pragma unroll
+      for (int u = 0; u < 2; ++u) {
+        const int e = tid + CONS * u;
+        const int i = e % KH, gg = e / KH;        // row i, 8-column group gg (0-3 re, 4-7 im)
+        if (src_identity) {
+          const int gi = h * KH + i, col = j0 + (gg & 3) * 8;
+#pragma unroll
+          for (int jj = 0; jj < 8; ++jj) x[u][jj] = (gg < 4 && gi == col + jj) ? 1.f : 0.f;
+        } else {
+          const unsigned char* box = w + (gg < 4 ? 16384 : 24576);
+          const int c0 = 2 * (gg & 3);
+          const float4 a = *reinterpret_cast<const float4*>(box + i * 128 + ((c0 ^ (i & 7)) << 4));
+          const float4 b = *reinterpret_cast<const float4*>(box + i * 128 + (((c0 + 1) ^ (i & 7)) << 4));
+          x[u][0] = a.x; x[u][1] = a.y; x[u][2] = a.z; x[u][3] = a.w;
+          x[u][4] = b.x; x[u][5] = b.y; x[u][6] = b.z; x[u][7] = b.w;
+        }
+      }
+      tc::named_sync(1, CONS);                    // every fp32 value read before the split overwrites it
+#pragma unroll
+      for (int u = 0; u < 2; ++u) {
+        const int e = tid + CONS * u;
+        const int i = e % KH, gg = e / KH;
+        uint4 hv, lv;
+        tc::split8(x[u], hv, lv);
+        *reinterpret_cast<uint4*>(w + 16384 + mnmaj(i, gg * 8, N2 / 8)) = hv;
+        *reinterpret_cast<uint4*>(w + 24576 + mnmaj(i, gg * 8, N2 / 8)) = lv;
+      }
+      tc::fence_proxy_async();
+      tc::named_sync(1, CONS);
+      if (tid == 0) tc::mbar_arrive(&bars[B2_SPL + s]);
+    }
+    // ---- phase T: Z -> operand (MD of the last half tile: every phase-A MMA done)
+    const int sl = (NH - 1) & 1;
+    if (ok && cwait(B2_MD + sl, ((NH - 1) >> 1) & 1)) {
+      tc::fence_after_sync();
+      float z[32];
+      tc::tmem_ld16(tZ + lane_base + 32 * half, z);
+      tc::tmem_ld16(tZ + lane_base + 32 * half + 16, z + 16);
+#pragma unroll
+      for (int g4 = 0; g4 < 4; ++g4) {
+        uint4 hv, lv;
+        tc::split8(z + 8 * g4, hv, lv);
+        const int off = mnmaj(row, 32 * half + 8 * g4, N2 / 8);
+        *reinterpret_cast<uint4*>(sZh + off) = hv;
+        *reinterpret_cast<uint4*>(sZl + off) = lv;
+      }
+      tc::fence_proxy_async();
+      tc::fence_before_sync();
+      tc::named_sync(1, CONS);
+      if (tid == 0) tc::mbar_arrive(&bars[B2_ZR]);
+    }
+    // ---- phase E: Cm -> operands (ZC: MN-major re | im; slot 0: Re(Cm) K-major, Y)
+    if (ok && cwait(B2_MT, 0)) {
+      tc::fence_after_sync();
+      float p1r[16], p1i[16], p2r[16], p2i[16];
+      tc::tmem_ld16(tP1 + lane_base + 16 * half, p1r);
+      tc::tmem_ld16(tP1 + lane_base + 32 + 16 * half, p1i);
+      tc::tmem_ld16(tP2 + lane_base + 16 * half, p2r);
+      tc::tmem_ld16(tP2 + lane_base + 32 + 16 * half, p2i);
+      float cr[16], ci[16];
+#pragma unroll
+      for (int j = 0; j < 16; ++j) { cr[j] = p1r[j] - p2i[j]; ci[j] = p1i[j] + p2r[j]; }
+#pragma unroll
+      for (int g2 = 0; g2 < 2; ++g2) {
+        uint4 hv, lv;
+        const int jc = 16 * half + 8 * g2;
+        tc::split8(cr + 8 * g2, hv, lv);
+        *reinterpret_cast<uint4*>(sZh + mnmaj(row, jc, N2 / 8)) = hv;
+        *reinterpret_cast<uint4*>(sZl + mnmaj(row, jc, N2 / 8)) = lv;
+        *reinterpret_cast<uint4*>(sAh + kmaj(row, jc, R2)) = hv;
+        *reinterpret_cast<uint4*>(sAl + kmaj(row, jc, R2)) = lv;
+        tc::split8(ci + 8 * g2, hv, lv);
+        *reinterpret_cast<uint4*>(sZh + mnmaj(row, NB2 + jc, N2 / 8)) = hv;
+        *reinterpret_cast<uint4*>(sZl + mnmaj(row, NB2 + jc, N2 / 8)) = lv;
+      }
+      {
+        const int t = tid % C2, gq = tid / C2;   // 64 tokens x 4 groups of 8 columns
+        uint4 u = make_uint4(0, 0, 0, 0);
+        if (t < nt) u = *reinterpret_cast<const uint4*>(q + ((size_t)item * S + t0 + t) * D + j0 + gq * 8);
+        *reinterpret_cast<uint4*>(sY + kmaj(t, gq * 8, C2)) = u;
+      }
+      tc::fence_proxy_async();
+      tc::fence_before_sync();
+      tc::named_sync(1, CONS);
+      if (tid == 0) tc::mbar_arrive(&bars[B2_CR]);
+    }
+    if (ok && cwait(B2_ME, 0)) {
+      tc::fence_after_sync();
+      float e[32];
+      tc::tmem_ld16(tE + lane_base + 32 * half, e);
+      tc::tmem_ld16(tE + lane_base + 32 * half + 16, e + 16);
+      float4* Eo = reinterpret_cast<float4*>(Ews + chunk * R2 * C2 + (size_t)row * C2 + 32 * half);
+#pragma unroll
+      for (int t = 0; t < 8; ++t) atomicAdd(Eo + t, make_float4(e[4 * t], e[4 * t + 1], e[4 * t + 2], e[4 * t + 3]));
+    }
+    // ---- phase B: S_next = S + dH, one row of 32 columns of one plane per thread
+    const size_t plane = (size_t)item * D * D;
+    const float* srcp = (half ? src_i : src_r) + plane;
+    float* dstp = (half ? dst_i : dst_r) + plane;
+    for (int kt = 0; kt < NT && ok; ++kt) {
+      const int s = (kt + 1) & 1, d = kt & 1;
+      const int gi = kt * KT + row;
+      float hv[32];
+      if (src_identity) {
+#pragma unroll
+        for (int jj = 0; jj < 32; ++jj) hv[jj] = (!half && gi == j0 + jj) ? 1.f : 0.f;
+      } else {
+        const float4* sp = reinterpret_cast<const float4*>(srcp + (size_t)gi * D + j0);
+#pragma unroll
+        for (int cc = 0; cc < 8; ++cc) {
+          const float4 a = sp[cc];
+          hv[4 * cc] = a.x; hv[4 * cc + 1] = a.y; hv[4 * cc + 2] = a.z; hv[4 * cc + 3] = a.w;
+        }
+      }
+      if (patch_w) {
+        if (!cwait(B2_FULL + s, nfull[s]++ & 1)) break;
+        zero_bad_rows(slot(s), 2);
+        tc::fence_proxy_async();
+        tc::named_sync(1, CONS);
+        if (tid == 0) tc::mbar_arrive(&bars[B2_SPL + s]);
+      }
+      if (!cwait(B2_DH + d, (kt >> 1) & 1)) break;
+      tc::fence_after_sync();
+      float dh[32];
+      tc::tmem_ld16(tDH + 64 * d + lane_base + 32 * half, dh);
+      tc::tmem_ld16(tDH + 64 * d + lane_base + 32 * half + 16, dh + 16);
+      tc::fence_before_sync();
+      tc::named_sync(1, CONS);
+      if (tid == 0) tc::mbar_arrive(&bars[B2_DF + d]);   // dH[d] may be overwritten
+      float4* op = reinterpret_cast<float4*>(dstp + (size_t)gi * D + j0);
+#pragma unroll
+      for (int cc = 0; cc < 8; ++cc)
+        op[cc] = make_float4(hv[4 * cc] + dh[4 * cc], hv[4 * cc + 1] + dh[4 * cc + 1], hv[4 * cc + 2] + dh[4 * cc + 2],
+                             hv[4 * cc + 3] + dh[4 * cc + 3]);
+    }
+  }
+  tc::fence_before_sync();
+  __syncthreads();
+  if (warp == 0) tc::tmem_dealloc(tbase, 256);
+}
+
+// Readout of a batch of chunks from their end states (rows of a ring of state buffers):
+// CTA (x, y) = (chunk c0 + x / (D/128), item y, rows 128 (x % (D/128)) ...).
+__global__ void __launch_bounds__(WS_THREADS, 1)
+cham_tc_readout_batch(const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
+                      const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_ring,
+                      const float* __restrict__ Ews, const unsigned long long* __restrict__ badws,
+                      __nv_bfloat16* __restrict__ out, int S, int D, int nch, int c0, int ring, int b) {
+  const int nrb = D / R2;
+  const int c = c0 + (int)blockIdx.x / nrb, bx = (int)blockIdx.x % nrb;
+  const int item = blockIdx.y;
+  readout_ws_body(tm_k, tm_v, tm_q, tm_ring, Ews, badws, out, S, D, nch, c, bx, item,
+                  ((c % ring) * b + item) * D);
 }
 
 // Tensor maps for the warp-specialised colpass (driver entry point resolved once).
@@ -1512,18 +1904,26 @@ int make_kv_map(CUtensorMap* m, const void* base, int b, int S, int D) {
 }
 
 // one plane of a [b][D][D] fp32 state as [b*D rows][D], boxes of 32 columns x 128 rows, 128B swizzle
-int make_state_map(CUtensorMap* m, const float* base, int b, int D) {
+int make_state_map(CUtensorMap* m, const float* base, int b, int D, int rows = KT) {
   auto enc = tmap_encoder();
   VERACE_REQUIRE(enc != nullptr, VERACE_ERR_CUDA, "cuTensorMapEncodeTiled is not available");
   const cuuint64_t dims[2] = {(cuuint64_t)D, (cuuint64_t)b * D};
   const cuuint64_t strides[1] = {(cuuint64_t)D * 4};
-  const cuuint32_t box[2] = {32, (cuuint32_t)KT};
+  const cuuint32_t box[2] = {32, (cuuint32_t)rows};
   const cuuint32_t es[2] = {1, 1};
   CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(base), dims, strides, box, es,
                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   VERACE_REQUIRE(r == CUDA_SUCCESS, VERACE_ERR_CUDA, "cuTensorMapEncodeTiled (state) failed: %d", (int)r);
   return VERACE_OK;
+}
+
+// Schedule of the bf16 path: one merged column-pass + readout launch per chunk (one CTA
+// per SM; the default), or VERACE_CHAM_BATCHED=1: column passes two CTAs per SM with
+// readouts batched over up to RING chunks.  Both are tested against each other.
+bool merged_readout() {
+  const char* e = getenv("VERACE_CHAM_BATCHED");
+  return !(e != nullptr && e[0] == '1');
 }
 
 size_t tc_prep_smem() { return sizeof(float) * (PREP_DT * (R2 + 1) + 3 * R2 * (R2 + 1)); }
@@ -1561,6 +1961,37 @@ int launch_cham_tc(const void* q, const void* k, const void* v, const float* gam
     if (nch >= 2 && ((rc = make_state_map(&m_ping_r, w.Hre, b, D)) || (rc = make_state_map(&m_ping_i, w.Him, b, D))))
       return rc;
     if (nch < 2) { m_ping_r = m_out_r; m_ping_i = m_out_i; }
+  }
+  if (WS && !merged_readout()) {
+    // column passes two CTAs per SM, readouts batched over up to RING chunks
+    CUtensorMap mq, m_ring, m_ring64, m_him64, m_hi64;
+    const size_t plane = (size_t)b * D * D;
+    if ((rc = make_kv_map(&mq, q, b, s, D)) || (rc = make_state_map(&m_ring, w.ring, w.nring * b, D)) ||
+        (rc = make_state_map(&m_ring64, w.ring, w.nring * b, D, KH)) ||
+        (rc = make_state_map(&m_hi64, hi, b, D, KH)))
+      return rc;
+    if (nch >= 2 && (rc = make_state_map(&m_him64, w.Him, b, D, KH))) return rc;
+    if (nch < 2) m_him64 = m_hi64;
+    VERACE_CUDA(cudaFuncSetAttribute(cham_tc_colpass2, cudaFuncAttributeMaxDynamicSharedMemorySize, CP2_SMEM));
+    VERACE_CUDA(cudaFuncSetAttribute(cham_tc_readout_batch, cudaFuncAttributeMaxDynamicSharedMemorySize, WS_SMEM));
+    auto im_dst = [&](int c) { return ((nch - 1 - c) % 2 == 0) ? hi : w.Him; };
+    for (int c = 0; c < nch; ++c) {
+      const int rs = (c + w.nring - 1) % w.nring, rd = c % w.nring;
+      float* si = c > 0 ? im_dst(c - 1) : hi;
+      cham_tc_colpass2<<<dim3(D / NB2, b), WS_THREADS, CP2_SMEM, st>>>(
+          mk, mv, m_ring64, si == hi ? m_hi64 : m_him64, rs * b, 0, w.ring + rs * plane, si, w.ring + rd * plane,
+          im_dst(c), (const __nv_bfloat16*)q, w.T, w.E, w.bad, c == 0 ? 1 : 0, s, D, nch, c);
+      if ((rc = check_launch("cham_tc_colpass2"))) return rc;
+      if ((c + 1) % w.nring == 0 || c == nch - 1) {
+        const int cb = c - c % w.nring;
+        cham_tc_readout_batch<<<dim3((D / R2) * (c - cb + 1), b), WS_THREADS, WS_SMEM, st>>>(
+            mk, mv, mq, m_ring, w.E, w.bad, (__nv_bfloat16*)out, s, D, nch, cb, w.nring, b);
+        if ((rc = check_launch("cham_tc_readout_batch"))) return rc;
+      }
+    }
+    VERACE_CUDA(cudaMemcpyAsync(hr, w.ring + ((nch - 1) % w.nring) * plane, plane * sizeof(float),
+                                cudaMemcpyDeviceToDevice, st));
+    return VERACE_OK;
   }
   if (WS) {
     CUtensorMap mq;

@@ -119,6 +119,48 @@ def cham_retract(H_real: torch.Tensor, H_imag: torch.Tensor, steps: int = 3
     return out_r, out_i
 
 
+def mixer_prologue(y: torch.Tensor, heads: int, head_dim: int, gate_cols: int, silu_v: bool,
+                   active_mask: Optional[torch.Tensor] = None
+                   ) -> Tuple[torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor]:
+    """One pass over a concatenated projection y [n, ld] (row = q | k | v | gate): q, k, v
+    [n, heads*head_dim] L2-normalised per head (v through SiLU first when `silu_v`), and
+    gate [n, gate_cols] fp32 = 0.1 sigmoid(.) * mask.  The elementwise tail of
+    sssd_attention.py:116-126 and cham_memory.py:129-153."""
+    assert y.is_cuda, "This kernel requires CUDA tensors"
+    y = _prep(y)
+    n, ld = y.shape
+    hd = heads * head_dim
+    q = torch.empty(n, hd, device=y.device, dtype=y.dtype)
+    k = torch.empty_like(q)
+    v = torch.empty_like(q)
+    gate = torch.empty(n, gate_cols, device=y.device, dtype=torch.float32)
+    m = None
+    if active_mask is not None:
+        m = active_mask.reshape(n).to(torch.uint8).contiguous()
+    with torch.cuda.device(y.device):
+        rc = lib().verace_mixer_prologue(y.data_ptr(), ld, q.data_ptr(), k.data_ptr(), v.data_ptr(),
+                                         gate.data_ptr(), _ptr(m), n, heads, head_dim, gate_cols,
+                                         1 if silu_v else 0, _DTYPE[y.dtype], _stream(y.device))
+    check(rc, "verace_mixer_prologue")
+    return q, k, v, gate
+
+
+def concat_weights(module: torch.nn.Module, weights) -> torch.Tensor:
+    """[W_q; W_k; W_v; W_gate] with zero rows up to a multiple of 8, cached on `module`
+    and rebuilt whenever one of the weights is replaced or modified in place."""
+    key = tuple((w.data_ptr(), w._version, w.dtype, w.device) for w in weights)
+    cached = getattr(module, "_verace_cat", None)
+    if cached is not None and cached[0] == key:
+        return cached[1]
+    with torch.no_grad():
+        W = torch.cat([w.detach() for w in weights], dim=0)
+        pad = (-W.shape[0]) % 8
+        if pad:
+            W = torch.cat([W, W.new_zeros(pad, W.shape[1])], dim=0)
+    module._verace_cat = (key, W.contiguous())
+    return module._verace_cat[1]
+
+
 # drop-in aliases with the reference's launcher names
 launch_sssd_triton_scan = launch_sssd_scan
 launch_cham_triton_update = launch_cham_update

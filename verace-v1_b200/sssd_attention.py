@@ -17,7 +17,7 @@ import torch
 import torch.nn as nn
 import torch.nn.functional as F
 
-from .kernels import launch_sssd_scan
+from .kernels import concat_weights, launch_sssd_scan, mixer_prologue
 
 
 def _require_inference(x: torch.Tensor, who: str):
@@ -43,16 +43,22 @@ class SSSDAttention(nn.Module):
         self.w_out = nn.Linear(num_heads * head_dim, hidden_dim, bias=False)
 
     def project(self, x: torch.Tensor, active_mask: Optional[torch.Tensor] = None):
-        """q, k, v [b, s, h, d] and delta [b, s, h] (sssd_attention.py:116-126)."""
+        """q, k, v [b, s, h, d] and delta [b, s, h] (sssd_attention.py:116-126): one GEMM
+        with the concatenated projection weights, then the fused normalisation/gate pass."""
         b, s, _ = x.shape
         h, d = self.num_heads, self.head_dim
-        q = F.normalize(self.w_q(x).view(b, s, h, d), p=2, dim=-1)
-        k = F.normalize(self.w_k(x).view(b, s, h, d), p=2, dim=-1)
-        v = F.normalize(self.w_v(x).view(b, s, h, d), p=2, dim=-1)
-        delta = 0.1 * torch.sigmoid(self.w_delta(x)).view(b, s, h)
-        if active_mask is not None:
-            delta = delta * active_mask.reshape(b, s, 1).to(delta.dtype)
-        return q, k, v, delta
+        if d % 8:   # head widths the fused pass does not tile: the same math as torch ops on the GPU
+            q = F.normalize(self.w_q(x).view(b, s, h, d), p=2, dim=-1)
+            k = F.normalize(self.w_k(x).view(b, s, h, d), p=2, dim=-1)
+            v = F.normalize(self.w_v(x).view(b, s, h, d), p=2, dim=-1)
+            delta = 0.1 * torch.sigmoid(self.w_delta(x)).view(b, s, h)
+            if active_mask is not None:
+                delta = delta * active_mask.reshape(b, s, 1).to(delta.dtype)
+            return q, k, v, delta
+        W = concat_weights(self, [self.w_q.weight, self.w_k.weight, self.w_v.weight, self.w_delta.weight])
+        y = F.linear(x, W).reshape(b * s, -1)
+        q, k, v, delta = mixer_prologue(y, h, d, h, False, active_mask)
+        return q.view(b, s, h, d), k.view(b, s, h, d), v.view(b, s, h, d), delta.view(b, s, h)
 
     def forward(self, x: torch.Tensor, initial_state: Optional[torch.Tensor] = None,
                 return_state: bool = False, active_mask: Optional[torch.Tensor] = None
