@@ -87,14 +87,15 @@ def test_tc_scan_zero_gamma_and_nonfinite_tokens():
 @pytest.mark.parametrize("b,s,D", [(3, 600, 256), (2, 130, 1024), (1, 64, 128)])
 def test_batched_readout_schedule_matches_merged_schedule(b, s, D):
     """Column passes two CTAs per SM with readouts batched over up to 8 chunks
-    (VERACE_CHAM_BATCHED=1) against the merged one-launch-per-chunk schedule (the
-    default): same arithmetic, so the results agree to fp32 accumulation order (the E
-    partials are summed atomically)."""
+    (VERACE_CHAM_BATCHED=1) against the merged one-launch-per-chunk schedule
+    (VERACE_CHAM_BATCHED=0): same arithmetic, so the results agree to fp32 accumulation
+    order (the E partials are summed atomically)."""
     q, k, v, g = random_cham_inputs(b, s, D, seed=800 + s, dtype=torch.bfloat16)
     k[0, min(5, s - 1), 3] = float("nan")
-    out_m, (Hr_m, Hi_m) = V.launch_cham_update(q, k, v, g)
-    os.environ["VERACE_CHAM_BATCHED"] = "1"
     try:
+        os.environ["VERACE_CHAM_BATCHED"] = "0"
+        out_m, (Hr_m, Hi_m) = V.launch_cham_update(q, k, v, g)
+        os.environ["VERACE_CHAM_BATCHED"] = "1"
         out, (Hr, Hi) = V.launch_cham_update(q, k, v, g)
     finally:
         del os.environ["VERACE_CHAM_BATCHED"]

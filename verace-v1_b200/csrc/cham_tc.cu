@@ -1499,35 +1499,37 @@ cham_tc_step_ws(const __grid_constant__ CUtensorMap tm_k, const __grid_constant_
 // chunks (cham_tc_readout_batch), from the chunks' end states kept in a ring of buffers.
 //
 // smem: ring [0, 64K) = 2 slots of 32 KB
-//         phase A: slot = W half tile (64 state rows x 128 vectors: k box 8K | v box 8K)
+//         phase A: three slots (the two ring slots and ZC, idle until phase T);
+//                  slot = W half tile (64 state rows x 128 vectors: k box 8K | v box 8K)
 //                  | state half tile (re 8K | im 8K, fp32 SW128), split in place into
 //                  bf16 hi 8K | lo 8K (the MMA B operand)
 //         phase T: Tr (hi | lo) across both slots, then Ti (hi | lo)
 //         phase E: Ca hi/lo (16K) | Y (4K) in slot 0
-//         phase B: slot = W tile (128 state rows x 128 vectors, 32K)
+//         phase B: slot = W tile (128 state rows x 128 vectors, 32K); once the tile's
+//                  MMA is done, the same slot takes the state tile (re 16K | im 16K, fp32
+//                  SW128), which the epilogue updates in place and TMA stores
 //       ZC [64K, 96K): Z split (hi 16K | lo 16K), then Cm split
 //       barriers, TMEM slot, failure flag at 96K
 // TMEM (256 columns): Z [0,64) P1 [64,128) P2 [128,192) E [192,256); dH[2] reuse P1/P2.
-// Phase B reads the state rows from global memory and writes the updated rows with
-// vector stores (each thread one row of 32 columns of one plane).
 constexpr int CP2_SLOT = 32 * 1024, CP2_ZC = 64 * 1024, CP2_BAR = 96 * 1024;
 constexpr int CP2_SMEM = CP2_BAR + 256;
 constexpr int KH = 64;   // state rows per phase-A half tile
-enum { B2_FULL = 0, B2_SPL = 2, B2_MD = 4, B2_TT = 6, B2_ZR = 7, B2_P1 = 8, B2_MT = 9, B2_CR = 10, B2_ME = 11,
-       B2_DH = 12, B2_DF = 14, N_BARS2 = 16 };
+enum { B2_FULL = 0, B2_SPL = 3, B2_MD = 6, B2_TT = 9, B2_ZR = 10, B2_P1 = 11, B2_MT = 12, B2_CR = 13, B2_ME = 14,
+       B2_DH = 15, B2_DF = 17, B2_SF = 19, B2_SR = 21, N_BARS2 = 23 };
 
 __global__ void __launch_bounds__(WS_THREADS, 2)
 cham_tc_colpass2(const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
                  const __grid_constant__ CUtensorMap tm_sr, const __grid_constant__ CUtensorMap tm_si,
-                 int src_row_re, int src_row_im, const float* __restrict__ src_r, const float* __restrict__ src_i,
-                 float* __restrict__ dst_r, float* __restrict__ dst_i, const __nv_bfloat16* __restrict__ q,
-                 const unsigned char* __restrict__ Tws, float* __restrict__ Ews,
+                 const __grid_constant__ CUtensorMap tm_sr128, const __grid_constant__ CUtensorMap tm_si128,
+                 const __grid_constant__ CUtensorMap tm_dr, const __grid_constant__ CUtensorMap tm_di,
+                 int src_row_re, int src_row_im, int dst_row_re, int dst_row_im,
+                 const __nv_bfloat16* __restrict__ q, const unsigned char* __restrict__ Tws, float* __restrict__ Ews,
                  const unsigned long long* __restrict__ badws, int src_identity, int S, int D, int nch, int c) {
   extern __shared__ __align__(1024) unsigned char smc[];
   uint64_t* bars = reinterpret_cast<uint64_t*>(smc + CP2_BAR);
   uint32_t* tslot = reinterpret_cast<uint32_t*>(smc + CP2_BAR + 8 * N_BARS2);
   volatile int* fail = reinterpret_cast<volatile int*>(smc + CP2_BAR + 8 * N_BARS2 + 16);
-  auto slot = [&](int s) { return smc + s * CP2_SLOT; };
+  auto slot = [&](int s) { return smc + s * CP2_SLOT; };   // slot 2 = the ZC region, phase A only
   unsigned char* sZh = smc + CP2_ZC;      // Z split, then Cm split (MN-major, 16K each)
   unsigned char* sZl = sZh + Z_TILE;
   unsigned char* sAh = smc;               // phase E: Re(Cm) K-major hi/lo, Y
@@ -1558,14 +1560,14 @@ cham_tc_colpass2(const __grid_constant__ CUtensorMap tm_k, const __grid_constant
     // ======================= producer (one thread) =======================
     if (lane == 0) {
       bool ok = true;
-      uint32_t nfull[2] = {0, 0}, nspl[2] = {0, 0}, nmd[2] = {0, 0}, ndh[2] = {0, 0}, ndf[2] = {0, 0};
+      uint32_t nfull[3] = {0, 0, 0}, nspl[3] = {0, 0, 0}, nmd[3] = {0, 0, 0}, ndh[2] = {0, 0}, ndf[2] = {0, 0};
       auto pwait = [&](int b, uint32_t par) {
         if (!ok) return false;
         if (*fail || !tc::mbar_wait(&bars[b], par, MAX_POLLS)) { ok = false; *fail = 1; record_timeout(); }
         return ok;
       };
-      auto issue_a = [&](int h) {   // phase-A half tile h into slot h & 1
-        const int s = h & 1;
+      auto issue_a = [&](int h) {   // phase-A half tile h into slot h % 3
+        const int s = h % 3;
         unsigned char* w = slot(s);
         tc::mbar_expect_tx(&bars[B2_FULL + s], 16 * 1024 + (src_identity ? 0 : 16 * 1024));
         tc::tma_load_3d(w, &tm_k, h * KH, t0, item, &bars[B2_FULL + s]);
@@ -1588,10 +1590,9 @@ cham_tc_colpass2(const __grid_constant__ CUtensorMap tm_k, const __grid_constant
       constexpr uint32_t ID_Z = tc::idesc_bf16(128, N2, false, true);
       constexpr uint32_t ID_H = tc::idesc_bf16(128, N2, true, true);
       // ---- phase A: Z = Wᵀ S over 64-row half tiles
-      issue_a(0);
-      if (NH > 1) issue_a(1);
+      for (int h = 0; h < 3 && h < NH; ++h) issue_a(h);
       for (int h = 0; h < NH && ok; ++h) {
-        const int s = h & 1;
+        const int s = h % 3;
         if (!pwait(B2_FULL + s, nfull[s]++ & 1) || !pwait(B2_SPL + s, nspl[s]++ & 1)) break;
         tc::fence_after_sync();
         const uint32_t aw = tc::smem_addr(slot(s));
@@ -1605,13 +1606,13 @@ cham_tc_colpass2(const __grid_constant__ CUtensorMap tm_k, const __grid_constant
         }
         tc::commit(&bars[B2_MD + s]);
         ++nmd[s];
-        if (h + 2 < NH) {
+        if (h + 3 < NH) {
           if (!pwait(B2_MD + s, (nmd[s] - 1) & 1)) break;
-          issue_a(h + 2);
+          issue_a(h + 3);
         }
       }
       // ---- phase T: P1 = Tr Z, then P2 = Ti Z, T halves through the ring
-      const int sl = (NH - 1) & 1;
+      const int sl = (NH - 1) % 3;
       const unsigned char* tsrc = Tws + chunk * 4 * T_TILE;
       constexpr uint32_t ID_T = tc::idesc_bf16(128, N2, false, true);
       auto t_mmas = [&](uint32_t td) {
@@ -1664,9 +1665,11 @@ cham_tc_colpass2(const __grid_constant__ CUtensorMap tm_k, const __grid_constant
           tc::commit(&bars[B2_ME]);
         }
       }
-      // ---- phase B: dH = W Cm per 128-row tile, double-buffered in TMEM
+      // ---- phase B: per 128-row tile: W tile -> dH = W Cm (TMEM, double-buffered) ->
+      // the state tile into the same slot -> consumers' epilogue -> TMA store -> slot free
       if (ok && pwait(B2_ME, 0)) {
         if (NT > 1) issue_b(1);
+        uint32_t nsr[2] = {0, 0};
         for (int kt = 0; kt < NT && ok; ++kt) {
           const int s = (kt + 1) & 1, d = kt & 1;
           if (!pwait(B2_FULL + s, nfull[s]++ & 1)) break;
@@ -1684,9 +1687,18 @@ cham_tc_colpass2(const __grid_constant__ CUtensorMap tm_k, const __grid_constant
           }
           tc::commit(&bars[B2_DH + d]);
           ++ndh[d];
-          if (kt + 2 < NT) {
-            if (!pwait(B2_DH + d, (ndh[d] - 1) & 1)) break;
-            issue_b(kt + 2);
+          // the W tile has been read: the state tile takes its slot
+          if (!pwait(B2_DH + d, (ndh[d] - 1) & 1)) break;
+          if (!src_identity) {
+            tc::mbar_expect_tx(&bars[B2_SF + s], 32 * 1024);
+            tc::tma_load_2d(slot(s), &tm_sr128, j0, (src_row_re + item) * D + kt * KT, &bars[B2_SF + s]);
+            tc::tma_load_2d(slot(s) + 16384, &tm_si128, j0, (src_row_im + item) * D + kt * KT, &bars[B2_SF + s]);
+          }
+          // tile kt-1's slot, once its store has read it, takes W tile kt+1
+          if (kt >= 1 && kt + 1 < NT) {
+            const int sp = kt & 1;
+            if (!pwait(B2_SR + sp, nsr[sp]++ & 1)) break;
+            issue_b(kt + 1);
           }
         }
       }
@@ -1696,7 +1708,7 @@ cham_tc_colpass2(const __grid_constant__ CUtensorMap tm_k, const __grid_constant
     const uint32_t lane_base = (uint32_t)(32 * (warp & 3)) << 16;
     const int row = 32 * (warp & 3) + lane, half = warp >> 2;
     bool ok = true;
-    uint32_t nfull[2] = {0, 0};
+    uint32_t nfull[3] = {0, 0, 0};
     auto cwait = [&](int b, uint32_t par) {
       bool mine = ok && !*fail && tc::mbar_wait(&bars[b], par, MAX_POLLS);
       const bool all = consumers_all(mine);
@@ -1713,7 +1725,7 @@ cham_tc_colpass2(const __grid_constant__ CUtensorMap tm_k, const __grid_constant
     };
     // ---- phase A: split each state half tile in place
     for (int h = 0; h < NH && ok; ++h) {
-      const int s = h & 1;
+      const int s = h % 3;
       if (!cwait(B2_FULL + s, nfull[s]++ & 1)) break;
       unsigned char* w = slot(s);
       if (patch_w) zero_bad_rows(w, 1);
@@ -1750,8 +1762,8 @@ cham_tc_colpass2(const __grid_constant__ CUtensorMap tm_k, const __grid_constant
       if (tid == 0) tc::mbar_arrive(&bars[B2_SPL + s]);
     }
     // ---- phase T: Z -> operand (MD of the last half tile: every phase-A MMA done)
-    const int sl = (NH - 1) & 1;
-    if (ok && cwait(B2_MD + sl, ((NH - 1) >> 1) & 1)) {
+    const int sl = (NH - 1) % 3;
+    if (ok && cwait(B2_MD + sl, ((NH - 1) / 3) & 1)) {
       tc::fence_after_sync();
       float z[32];
       tc::tmem_ld16(tZ + lane_base + 32 * half, z);
@@ -1813,28 +1825,14 @@ cham_tc_colpass2(const __grid_constant__ CUtensorMap tm_k, const __grid_constant
 #pragma unroll
       for (int t = 0; t < 8; ++t) atomicAdd(Eo + t, make_float4(e[4 * t], e[4 * t + 1], e[4 * t + 2], e[4 * t + 3]));
     }
-    // ---- phase B: S_next = S + dH, one row of 32 columns of one plane per thread
-    const size_t plane = (size_t)item * D * D;
-    const float* srcp = (half ? src_i : src_r) + plane;
-    float* dstp = (half ? dst_i : dst_r) + plane;
+    // ---- phase B: S_next = S + dH in the slot (thread: one row of one plane), TMA store
+    uint32_t nsf[2] = {0, 0};
     for (int kt = 0; kt < NT && ok; ++kt) {
       const int s = (kt + 1) & 1, d = kt & 1;
-      const int gi = kt * KT + row;
-      float hv[32];
-      if (src_identity) {
-#pragma unroll
-        for (int jj = 0; jj < 32; ++jj) hv[jj] = (!half && gi == j0 + jj) ? 1.f : 0.f;
-      } else {
-        const float4* sp = reinterpret_cast<const float4*>(srcp + (size_t)gi * D + j0);
-#pragma unroll
-        for (int cc = 0; cc < 8; ++cc) {
-          const float4 a = sp[cc];
-          hv[4 * cc] = a.x; hv[4 * cc + 1] = a.y; hv[4 * cc + 2] = a.z; hv[4 * cc + 3] = a.w;
-        }
-      }
+      unsigned char* w = slot(s);
       if (patch_w) {
         if (!cwait(B2_FULL + s, nfull[s]++ & 1)) break;
-        zero_bad_rows(slot(s), 2);
+        zero_bad_rows(w, 2);
         tc::fence_proxy_async();
         tc::named_sync(1, CONS);
         if (tid == 0) tc::mbar_arrive(&bars[B2_SPL + s]);
@@ -1847,12 +1845,36 @@ cham_tc_colpass2(const __grid_constant__ CUtensorMap tm_k, const __grid_constant
       tc::fence_before_sync();
       tc::named_sync(1, CONS);
       if (tid == 0) tc::mbar_arrive(&bars[B2_DF + d]);   // dH[d] may be overwritten
-      float4* op = reinterpret_cast<float4*>(dstp + (size_t)gi * D + j0);
+      unsigned char* box = w + half * 16384;
+      if (src_identity) {
+        const int gi = kt * KT + row;
 #pragma unroll
-      for (int cc = 0; cc < 8; ++cc)
-        op[cc] = make_float4(hv[4 * cc] + dh[4 * cc], hv[4 * cc + 1] + dh[4 * cc + 1], hv[4 * cc + 2] + dh[4 * cc + 2],
-                             hv[4 * cc + 3] + dh[4 * cc + 3]);
+        for (int cc = 0; cc < 8; ++cc) {
+          float v4[4];
+#pragma unroll
+          for (int jj = 0; jj < 4; ++jj) v4[jj] = dh[4 * cc + jj] + ((!half && gi == j0 + 4 * cc + jj) ? 1.f : 0.f);
+          *reinterpret_cast<float4*>(box + row * 128 + ((cc ^ (row & 7)) << 4)) = make_float4(v4[0], v4[1], v4[2], v4[3]);
+        }
+      } else {
+        if (!cwait(B2_SF + s, nsf[s]++ & 1)) break;
+#pragma unroll
+        for (int cc = 0; cc < 8; ++cc) {
+          float4* p4 = reinterpret_cast<float4*>(box + row * 128 + ((cc ^ (row & 7)) << 4));
+          const float4 a = *p4;
+          *p4 = make_float4(a.x + dh[4 * cc], a.y + dh[4 * cc + 1], a.z + dh[4 * cc + 2], a.w + dh[4 * cc + 3]);
+        }
+      }
+      tc::fence_proxy_async();
+      tc::named_sync(1, CONS);
+      if (tid == 0) {
+        tc::tma_store_2d(&tm_dr, j0, (dst_row_re + item) * D + kt * KT, w);
+        tc::tma_store_2d(&tm_di, j0, (dst_row_im + item) * D + kt * KT, w + 16384);
+        tc::bulk_commit();
+        tc::bulk_wait_read<0>();                 // the store has read the slot
+        tc::mbar_arrive(&bars[B2_SR + s]);
+      }
     }
+    if (tid == 0) tc::bulk_wait<0>();            // all state writes performed
   }
   tc::fence_before_sync();
   __syncthreads();
@@ -1918,12 +1940,18 @@ int make_state_map(CUtensorMap* m, const float* base, int b, int D, int rows = K
   return VERACE_OK;
 }
 
-// Schedule of the bf16 path: one merged column-pass + readout launch per chunk (one CTA
-// per SM; the default), or VERACE_CHAM_BATCHED=1: column passes two CTAs per SM with
-// readouts batched over up to RING chunks.  Both are tested against each other.
-bool merged_readout() {
+// Schedule of the bf16 path.  Merged: one column-pass + readout launch per chunk, one
+// CTA per SM (lowest latency while a launch's CTAs fit on the SMs at once).  Batched:
+// column passes two CTAs per SM, readouts batched over up to RING chunks (better once
+// the merged launch needs more than one CTA generation per SM).  VERACE_CHAM_BATCHED=1
+// or =0 forces one; both are tested against each other.
+bool merged_readout(int b, int D) {
   const char* e = getenv("VERACE_CHAM_BATCHED");
-  return !(e != nullptr && e[0] == '1');
+  if (e != nullptr && e[0] == '1') return false;
+  if (e != nullptr && e[0] == '0') return true;
+  int dev = 0, sms = 148;
+  if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  return (long long)b * (D / NB2 + D / R2) <= sms;
 }
 
 size_t tc_prep_smem() { return sizeof(float) * (PREP_DT * (R2 + 1) + 3 * R2 * (R2 + 1)); }
@@ -1962,25 +1990,29 @@ int launch_cham_tc(const void* q, const void* k, const void* v, const float* gam
       return rc;
     if (nch < 2) { m_ping_r = m_out_r; m_ping_i = m_out_i; }
   }
-  if (WS && !merged_readout()) {
+  if (WS && !merged_readout(b, D)) {
     // column passes two CTAs per SM, readouts batched over up to RING chunks
-    CUtensorMap mq, m_ring, m_ring64, m_him64, m_hi64;
+    CUtensorMap mq, m_ring, m_ring64, m_him64, m_hi64, m_him128, m_hi128;
     const size_t plane = (size_t)b * D * D;
     if ((rc = make_kv_map(&mq, q, b, s, D)) || (rc = make_state_map(&m_ring, w.ring, w.nring * b, D)) ||
         (rc = make_state_map(&m_ring64, w.ring, w.nring * b, D, KH)) ||
-        (rc = make_state_map(&m_hi64, hi, b, D, KH)))
+        (rc = make_state_map(&m_hi64, hi, b, D, KH)) || (rc = make_state_map(&m_hi128, hi, b, D)))
       return rc;
-    if (nch >= 2 && (rc = make_state_map(&m_him64, w.Him, b, D, KH))) return rc;
-    if (nch < 2) m_him64 = m_hi64;
+    if (nch >= 2 && ((rc = make_state_map(&m_him64, w.Him, b, D, KH)) ||
+                     (rc = make_state_map(&m_him128, w.Him, b, D))))
+      return rc;
+    if (nch < 2) { m_him64 = m_hi64; m_him128 = m_hi128; }
     VERACE_CUDA(cudaFuncSetAttribute(cham_tc_colpass2, cudaFuncAttributeMaxDynamicSharedMemorySize, CP2_SMEM));
     VERACE_CUDA(cudaFuncSetAttribute(cham_tc_readout_batch, cudaFuncAttributeMaxDynamicSharedMemorySize, WS_SMEM));
     auto im_dst = [&](int c) { return ((nch - 1 - c) % 2 == 0) ? hi : w.Him; };
     for (int c = 0; c < nch; ++c) {
       const int rs = (c + w.nring - 1) % w.nring, rd = c % w.nring;
       float* si = c > 0 ? im_dst(c - 1) : hi;
+      float* di = im_dst(c);
       cham_tc_colpass2<<<dim3(D / NB2, b), WS_THREADS, CP2_SMEM, st>>>(
-          mk, mv, m_ring64, si == hi ? m_hi64 : m_him64, rs * b, 0, w.ring + rs * plane, si, w.ring + rd * plane,
-          im_dst(c), (const __nv_bfloat16*)q, w.T, w.E, w.bad, c == 0 ? 1 : 0, s, D, nch, c);
+          mk, mv, m_ring64, si == hi ? m_hi64 : m_him64, m_ring, si == hi ? m_hi128 : m_him128, m_ring,
+          di == hi ? m_hi128 : m_him128, rs * b, 0, rd * b, 0, (const __nv_bfloat16*)q, w.T, w.E, w.bad,
+          c == 0 ? 1 : 0, s, D, nch, c);
       if ((rc = check_launch("cham_tc_colpass2"))) return rc;
       if ((c + 1) % w.nring == 0 || c == nch - 1) {
         const int cb = c - c % w.nring;
