@@ -1320,6 +1320,198 @@ readout_ws_body(const CUtensorMap& tm_k, const CUtensorMap& tm_v, const CUtensor
 }
 
 // ---------------------------------------------------------------------------------
+// Readout for the batched schedule, two CTAs per SM: readout_ws_body with the fp32
+// state rows split in place (no separate split buffers).
+// smem: stage s at s*40K = state rows [128][64] fp32 (2 boxes, 32K; split in place into
+//       bf16 hi 16K | lo 16K) | Y [64 tok][64] (8K); phase 2: W (32K) at 0, E split at 40K
+// TMEM: O [0,64)
+constexpr int RW2_STAGE = 40 * 1024, RW2_BAR = 80 * 1024;
+constexpr int RW2_SMEM = RW2_BAR + 256;
+
+__device__ __forceinline__ void
+readout2_body(const CUtensorMap& tm_k, const CUtensorMap& tm_v, const CUtensorMap& tm_q,
+                const CUtensorMap& tm_sr, const float* __restrict__ Ews,
+                const unsigned long long* __restrict__ badws, __nv_bfloat16* __restrict__ out,
+                int S, int D, int nch, int c, int bx, int item, int srow) {
+  extern __shared__ __align__(1024) unsigned char smw[];
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smw + RW2_BAR);
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(smw + RW2_BAR + 8 * N_BARS);
+  volatile int* fail = reinterpret_cast<volatile int*>(smw + RW2_BAR + 8 * N_BARS + 16);
+  auto stA = [&](int s) { return smw + s * RW2_STAGE; };
+  auto stY = [&](int s) { return smw + s * RW2_STAGE + 32 * 1024; };
+  auto splitA = [&](int s) { return smw + s * RW2_STAGE; };   // in place of the fp32 rows
+  unsigned char* sW = smw;
+  unsigned char* sEh = smw + RW2_STAGE;
+  unsigned char* sEl = sEh + 16 * 1024;
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int i0 = bx * R2;
+  const int t0 = c * C2, nt = min(C2, S - t0);
+  const size_t chunk = (size_t)item * nch + c;
+  const unsigned long long bad = badws[chunk];
+  const int NTR = D / RKT;
+
+  if (warp == 0) tc::tmem_alloc(tslot, 64);
+  if (tid == 0) {
+    for (int i = 0; i < N_BARS; ++i) tc::mbar_init(&bars[i], 1);
+    *fail = 0;
+    tc::fence_mbar_init();
+  }
+  tc::fence_before_sync();
+  __syncthreads();
+  tc::fence_after_sync();
+  const uint32_t tO = *tslot;
+
+  if (warp == 8) {
+    if (lane == 0) {
+      bool ok = true;
+      auto pwait = [&](int b, uint32_t par) {
+        if (!ok) return false;
+        if (*fail || !tc::mbar_wait(&bars[b], par, MAX_POLLS)) { ok = false; *fail = 1; record_timeout(); }
+        return ok;
+      };
+      auto issue = [&](int kt) {
+        const int s = kt & 1;
+        tc::mbar_expect_tx(&bars[B_TFULL + s], 32 * 1024 + 8 * 1024);
+        tc::tma_load_2d(stA(s), &tm_sr, kt * RKT, srow + i0, &bars[B_TFULL + s]);
+        tc::tma_load_2d(stA(s) + 16 * 1024, &tm_sr, kt * RKT + 32, srow + i0, &bars[B_TFULL + s]);
+        tc::tma_load_3d(stY(s), &tm_q, kt * RKT, t0, item, &bars[B_TFULL + s]);
+      };
+      constexpr uint32_t ID_O = tc::idesc_bf16(128, C2, false, false);
+      issue(0);
+      if (NTR > 1) issue(1);
+      for (int kt = 0; kt < NTR && ok; ++kt) {
+        const int s = kt & 1;
+        if (!pwait(B_TFULL + s, (kt >> 1) & 1) || !pwait(B_SFULL + s, (kt >> 1) & 1)) break;
+        tc::fence_after_sync();
+        const uint32_t ah = tc::smem_addr(splitA(s)), al = ah + 16 * 1024;
+        const uint32_t y = tc::smem_addr(stY(s));
+#pragma unroll 1
+        for (int ks = 0; ks < RKT / 16; ++ks) {
+          const uint64_t b = tc::sdesc_sw128(y + ks * 32, 16, 1024);
+          tc::mma_bf16(tO, tc::sdesc(ah + ks * 2 * R2 * 16, R2 * 16, 128), b, ID_O, (kt > 0 || ks > 0) ? 1u : 0u);
+          tc::mma_bf16(tO, tc::sdesc(al + ks * 2 * R2 * 16, R2 * 16, 128), b, ID_O, 1u);
+        }
+        tc::commit(&bars[B_MDONE + s]);
+        if (kt + 2 < NTR) {
+          if (!pwait(B_MDONE + s, (kt >> 1) & 1)) break;
+          issue(kt + 2);
+        }
+      }
+      // W rows [i0, i0+128) of the chunk (k block, v block), then O -= W mask(E)
+      if (ok && pwait(B_MDONE + ((NTR - 1) & 1), ((NTR - 1) >> 1) & 1)) {
+        tc::mbar_expect_tx(&bars[B_TT], W_TILE);
+#pragma unroll
+        for (int kb = 0; kb < R2 / 64; ++kb) {
+          tc::tma_load_3d(sW + kb * 16384, &tm_k, i0 + kb * 64, t0, item, &bars[B_TT]);
+          tc::tma_load_3d(sW + kb * 16384 + 8192, &tm_v, i0 + kb * 64, t0, item, &bars[B_TT]);
+        }
+        if (pwait(B_TT, 0) && pwait(B_CREADY, 0)) {
+          tc::fence_after_sync();
+          constexpr uint32_t ID_W = tc::idesc_bf16(128, C2, true, true);
+          const uint32_t aw = tc::smem_addr(sW), eh = tc::smem_addr(sEh), el = tc::smem_addr(sEl);
+#pragma unroll 1
+          for (int ks = 0; ks < R2 / 16; ++ks) {
+            const uint64_t a = tc::sdesc_sw128(aw + ks * 2048, 16384, 1024);
+            tc::mma_bf16(tO, a, tc::sdesc(eh + ks * 2 * (C2 / 8) * 128, (C2 / 8) * 128, 128), ID_W, 1u);
+            tc::mma_bf16(tO, a, tc::sdesc(el + ks * 2 * (C2 / 8) * 128, (C2 / 8) * 128, 128), ID_W, 1u);
+          }
+          tc::commit(&bars[B_ME]);
+        }
+      }
+    }
+  } else {
+    const uint32_t lane_base = (uint32_t)(32 * (warp & 3)) << 16;
+    const int row = 32 * (warp & 3) + lane, half = warp >> 2;
+    bool ok = true;
+    auto cwait = [&](int b, uint32_t par) {
+      bool mine = ok && !*fail && tc::mbar_wait(&bars[b], par, MAX_POLLS);
+      const bool all = consumers_all(mine);
+      if (!all) { if (ok && tid == 0) record_timeout(); ok = false; *fail = 1; }
+      return ok;
+    };
+    for (int kt = 0; kt < NTR && ok; ++kt) {
+      const int s = kt & 1;
+      if (!cwait(B_TFULL + s, (kt >> 1) & 1)) break;
+      unsigned char* ah = splitA(s);
+      unsigned char* al = ah + 16 * 1024;
+      const unsigned char* a = stA(s);
+      constexpr int UN = (R2 * (RKT / 8)) / CONS;
+      float x[UN][8];
+#pragma unroll
+      for (int u = 0; u < UN; ++u) {
+        const int e = tid + CONS * u;
+        const int i = e % R2, gg = e / R2;                 // row i, columns 8*gg .. 8*gg+7
+        const unsigned char* box = a + (gg >> 2) * 16384;
+        const int c0 = 2 * (gg & 3);
+        const float4 x0 = *reinterpret_cast<const float4*>(box + i * 128 + ((c0 ^ (i & 7)) << 4));
+        const float4 x1 = *reinterpret_cast<const float4*>(box + i * 128 + (((c0 + 1) ^ (i & 7)) << 4));
+        x[u][0] = x0.x; x[u][1] = x0.y; x[u][2] = x0.z; x[u][3] = x0.w;
+        x[u][4] = x1.x; x[u][5] = x1.y; x[u][6] = x1.z; x[u][7] = x1.w;
+      }
+      tc::named_sync(1, CONS);   // every fp32 value read before the split overwrites it
+#pragma unroll
+      for (int u = 0; u < UN; ++u) {
+        const int e = tid + CONS * u;
+        const int i = e % R2, gg = e / R2;
+        uint4 h, l;
+        tc::split8(x[u], h, l);
+        *reinterpret_cast<uint4*>(ah + kmaj(i, gg * 8, R2)) = h;
+        *reinterpret_cast<uint4*>(al + kmaj(i, gg * 8, R2)) = l;
+      }
+      tc::fence_proxy_async();
+      tc::named_sync(1, CONS);
+      if (tid == 0) tc::mbar_arrive(&bars[B_SFULL + s]);
+    }
+    // the E operand goes into stage 1: wait until the last main-loop MMA has read it
+    if (ok && cwait(B_MDONE + ((NTR - 1) & 1), ((NTR - 1) >> 1) & 1)) {
+      // -mask(E): keep later tokens (tok(r) > t), zero tokens that are non-finite
+      const float* Ein = Ews + chunk * R2 * C2;
+#pragma unroll
+      for (int u = 0; u < (R2 * (C2 / 8)) / CONS; ++u) {
+        const int e = tid + CONS * u;
+        const int gq = e % (C2 / 8), r = e / (C2 / 8);
+        float x[8];
+        load8(Ein + (size_t)r * C2 + gq * 8, x);
+#pragma unroll
+        for (int jj = 0; jj < 8; ++jj) x[jj] = (tok(r) > gq * 8 + jj) ? -x[jj] : 0.f;
+        uint4 h, l;
+        tc::split8(x, h, l);
+        *reinterpret_cast<uint4*>(sEh + mnmaj(r, gq * 8, C2 / 8)) = h;
+        *reinterpret_cast<uint4*>(sEl + mnmaj(r, gq * 8, C2 / 8)) = l;
+      }
+      // rows of non-finite tokens must not reach the product (their E rows are 0, and
+      // 0 x inf is NaN): zero them in the W tile once it has landed
+      if (cwait(B_TT, 0) && bad) {
+        for (int e = tid; e < R2 * (R2 / 8); e += CONS) {
+          const int r = e % R2, cc = e / R2;
+          if ((bad >> tok(r)) & 1ull)
+            *reinterpret_cast<uint4*>(sW + (cc >> 3) * 16384 + r * 128 + (((cc & 7) ^ (r & 7)) << 4)) =
+                make_uint4(0, 0, 0, 0);
+        }
+      }
+      tc::fence_proxy_async();
+      tc::named_sync(1, CONS);
+      if (ok && tid == 0) tc::mbar_arrive(&bars[B_CREADY]);
+    }
+    if (ok && cwait(B_ME, 0)) {
+      tc::fence_after_sync();
+      float o[32];
+      tc::tmem_ld16(tO + lane_base + 32 * half, o);
+      tc::tmem_ld16(tO + lane_base + 32 * half + 16, o + 16);
+#pragma unroll
+      for (int u = 0; u < 32; ++u) {
+        const int t = 32 * half + u;
+        if (t < nt) out[((size_t)item * S + t0 + t) * D + i0 + row] = __float2bfloat16_rn(o[u]);
+      }
+    }
+  }
+  tc::fence_before_sync();
+  __syncthreads();
+  if (warp == 0) tc::tmem_dealloc(tO, 64);
+}
+
+// ---------------------------------------------------------------------------------
 // prep for bf16 inputs: the Gram matrix G = W Wᵀ on the tensor cores (W tiles by TMA in
 // the kernels' row order, k block then v block; bf16 inputs are exact, so one product),
 // then N_t, T by block forward substitution (fp32 SIMT) directly in that row order.
@@ -1883,7 +2075,7 @@ cham_tc_colpass2(const __grid_constant__ CUtensorMap tm_k, const __grid_constant
 
 // Readout of a batch of chunks from their end states (rows of a ring of state buffers):
 // CTA (x, y) = (chunk c0 + x / (D/128), item y, rows 128 (x % (D/128)) ...).
-__global__ void __launch_bounds__(WS_THREADS, 1)
+__global__ void __launch_bounds__(WS_THREADS, 2)
 cham_tc_readout_batch(const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
                       const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_ring,
                       const float* __restrict__ Ews, const unsigned long long* __restrict__ badws,
@@ -1891,8 +2083,8 @@ cham_tc_readout_batch(const __grid_constant__ CUtensorMap tm_k, const __grid_con
   const int nrb = D / R2;
   const int c = c0 + (int)blockIdx.x / nrb, bx = (int)blockIdx.x % nrb;
   const int item = blockIdx.y;
-  readout_ws_body(tm_k, tm_v, tm_q, tm_ring, Ews, badws, out, S, D, nch, c, bx, item,
-                  ((c % ring) * b + item) * D);
+  readout2_body(tm_k, tm_v, tm_q, tm_ring, Ews, badws, out, S, D, nch, c, bx, item,
+                ((c % ring) * b + item) * D);
 }
 
 // Tensor maps for the warp-specialised colpass (driver entry point resolved once).
@@ -2003,7 +2195,7 @@ int launch_cham_tc(const void* q, const void* k, const void* v, const float* gam
       return rc;
     if (nch < 2) { m_him64 = m_hi64; m_him128 = m_hi128; }
     VERACE_CUDA(cudaFuncSetAttribute(cham_tc_colpass2, cudaFuncAttributeMaxDynamicSharedMemorySize, CP2_SMEM));
-    VERACE_CUDA(cudaFuncSetAttribute(cham_tc_readout_batch, cudaFuncAttributeMaxDynamicSharedMemorySize, WS_SMEM));
+    VERACE_CUDA(cudaFuncSetAttribute(cham_tc_readout_batch, cudaFuncAttributeMaxDynamicSharedMemorySize, RW2_SMEM));
     auto im_dst = [&](int c) { return ((nch - 1 - c) % 2 == 0) ? hi : w.Him; };
     for (int c = 0; c < nch; ++c) {
       const int rs = (c + w.nring - 1) % w.nring, rd = c % w.nring;
@@ -2016,7 +2208,7 @@ int launch_cham_tc(const void* q, const void* k, const void* v, const float* gam
       if ((rc = check_launch("cham_tc_colpass2"))) return rc;
       if ((c + 1) % w.nring == 0 || c == nch - 1) {
         const int cb = c - c % w.nring;
-        cham_tc_readout_batch<<<dim3((D / R2) * (c - cb + 1), b), WS_THREADS, WS_SMEM, st>>>(
+        cham_tc_readout_batch<<<dim3((D / R2) * (c - cb + 1), b), WS_THREADS, RW2_SMEM, st>>>(
             mk, mv, mq, m_ring, w.E, w.bad, (__nv_bfloat16*)out, s, D, nch, cb, w.nring, b);
         if ((rc = check_launch("cham_tc_readout_batch"))) return rc;
       }
