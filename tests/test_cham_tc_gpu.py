@@ -84,22 +84,24 @@ def test_tc_scan_zero_gamma_and_nonfinite_tokens():
     torch.testing.assert_close(out_b, out_i)
 
 
-@pytest.mark.parametrize("b,s,D", [(3, 600, 256), (2, 130, 1024), (1, 64, 128)])
-def test_batched_readout_schedule_matches_merged_schedule(b, s, D):
-    """Column passes two CTAs per SM with readouts batched over up to 8 chunks
-    (VERACE_CHAM_BATCHED=1) against the merged one-launch-per-chunk schedule
-    (VERACE_CHAM_BATCHED=0): same arithmetic, so the results agree to fp32 accumulation
-    order (the E partials are summed atomically)."""
+@pytest.mark.parametrize("b,s,D", [(3, 600, 256), (2, 130, 1024), (1, 64, 128), (2, 10, 128)])
+def test_schedules_agree(b, s, D):
+    """The three bf16 schedules (merged per-chunk launches; column passes two CTAs per SM
+    with batched readouts; one fused pass per chunk) run the same arithmetic, so the
+    results agree to fp32 accumulation order (the E partials are summed atomically)."""
     q, k, v, g = random_cham_inputs(b, s, D, seed=800 + s, dtype=torch.bfloat16)
     k[0, min(5, s - 1), 3] = float("nan")
+    res = {}
     try:
-        os.environ["VERACE_CHAM_BATCHED"] = "0"
-        out_m, (Hr_m, Hi_m) = V.launch_cham_update(q, k, v, g)
-        os.environ["VERACE_CHAM_BATCHED"] = "1"
-        out, (Hr, Hi) = V.launch_cham_update(q, k, v, g)
+        for sched in ("merged", "batched", "fused"):
+            os.environ["VERACE_CHAM_SCHEDULE"] = sched
+            res[sched] = V.launch_cham_update(q, k, v, g)
     finally:
-        del os.environ["VERACE_CHAM_BATCHED"]
+        del os.environ["VERACE_CHAM_SCHEDULE"]
     _status_ok()
-    assert rel_fro(to_np(Hr), to_np(Hr_m)) <= 1e-6 and rel_fro(to_np(Hi), to_np(Hi_m)) <= 1e-6
-    assert rel_fro(to_np(out), to_np(out_m)) <= 1e-2   # bf16 outputs: at most one rounding step apart
-    assert torch.isfinite(out.float()).all()
+    out_m, (Hr_m, Hi_m) = res["merged"]
+    for sched in ("batched", "fused"):
+        out, (Hr, Hi) = res[sched]
+        assert rel_fro(to_np(Hr), to_np(Hr_m)) <= 1e-6 and rel_fro(to_np(Hi), to_np(Hi_m)) <= 1e-6, sched
+        assert rel_fro(to_np(out), to_np(out_m)) <= 1e-2, sched   # bf16 outputs: one rounding step apart
+        assert torch.isfinite(out.float()).all()

@@ -21,6 +21,7 @@
 
 #include <algorithm>
 #include <cstdlib>
+#include <cstring>
 #include "tc.cuh"
 #include "wy_solve.cuh"
 
@@ -60,6 +61,7 @@ struct TcWs {
   float* Him;
   float* ring;               // [min(nch, RING)][b][D][D]: real parts of chunk end states
   int nring;
+  unsigned char* cm;         // [2][b][D/64][64 KB]: fused schedule, Cm operands between launches
 };
 
 size_t tc_ws_layout(int b, int s, int D, TcWs* w, char* base) {
@@ -75,6 +77,7 @@ size_t tc_ws_layout(int b, int s, int D, TcWs* w, char* base) {
   t.Him = (float*)take(ping ? (size_t)b * D * D * sizeof(float) : 0);
   t.nring = (int)std::min<size_t>(nch, RING);
   t.ring = (float*)take((size_t)t.nring * b * D * D * sizeof(float));
+  t.cm = (unsigned char*)take((size_t)2 * b * (D / 64) * (64 * 1024));
   if (w) *w = t;
   return off + 256;
 }
@@ -2073,6 +2076,397 @@ cham_tc_colpass2(const __grid_constant__ CUtensorMap tm_k, const __grid_constant
   if (warp == 0) tc::tmem_dealloc(tbase, 256);
 }
 
+// ---------------------------------------------------------------------------------
+// Fused column pass (bf16 inputs): launch c makes ONE pass over the state rows that
+// finishes chunk c-1 and starts chunk c,
+//     S_c = S_{c-1} + W_{c-1} Cm_{c-1}        (stored: re -> ring[c-1], im -> ping)
+//     Z_c = W_cᵀ S_c                          (accumulated tile by tile in TMEM)
+// then Cm_c = T_c Z_c (written to global as the next launch's MMA operand) and the E
+// partial of chunk c.  Launch 0 starts from the identity; launch nch only finishes.
+// The state is read once and written once per chunk.  One CTA per (item, 64 complex
+// columns), one per SM; rows in tiles of 64 (dH = W_{c-1} Cm_{c-1} with M = 64: row r of
+// the tile in TMEM lane (r mod 16) + 32 (r / 16)).
+//
+// smem: stage s (2) at s*64K = W_{c-1} half (16K) | W_c half (16K) | state tile (64 rows
+//       x (re 64 | im 64) fp32: four 32-column SW128 boxes of 8K; after the store, split in
+//       place into bf16 hi 16K | lo 16K); phase T: T tiles (4 x 32K) over both stages,
+//       then Re(Cm) K-major hi/lo (32K) | Y (8K)
+//       CZ [128K, 192K): Cm_{c-1} operand (hi 32K | lo 32K), then Z_c operand
+//       barriers, TMEM slot, failure flag at 192K
+// TMEM (512 columns): Z [0,128)  dH[2] [128,384) (M = 64)  P1 [128,256) P2 [256,384)
+//       E [384,448)
+constexpr int NB3 = 64, N3 = 2 * NB3, KH3 = 64;
+constexpr int CP3_STAGE = 64 * 1024, CP3_CZ = 128 * 1024, CP3_BAR = 192 * 1024;
+constexpr int CP3_SMEM = CP3_BAR + 256;
+constexpr int CM3_BYTES = 64 * 1024;   // Cm operand per CTA (hi | lo), MN-major K = 128, N = 128
+enum { B3_FULL = 0, B3_WFIX = 2, B3_DH = 4, B3_DF = 6, B3_SPL = 8, B3_MD = 10, B3_CMF = 12, B3_TT = 13,
+       B3_ZR = 14, B3_MT = 15, B3_CR = 16, B3_ME = 17, N_BARS3 = 18 };
+
+__global__ void __launch_bounds__(WS_THREADS, 1)
+cham_tc_colpass3(const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
+                 const __grid_constant__ CUtensorMap tm_sr, const __grid_constant__ CUtensorMap tm_si,
+                 const __grid_constant__ CUtensorMap tm_dr, const __grid_constant__ CUtensorMap tm_di,
+                 int src_row_re, int src_row_im, int dst_row_re, int dst_row_im,
+                 const unsigned char* __restrict__ cm_in, unsigned char* __restrict__ cm_out,
+                 const __nv_bfloat16* __restrict__ q, const unsigned char* __restrict__ Tws,
+                 float* __restrict__ Ews, const unsigned long long* __restrict__ badws, int S, int D, int nch,
+                 int c) {
+  extern __shared__ __align__(1024) unsigned char smf[];
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smf + CP3_BAR);
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(smf + CP3_BAR + 8 * N_BARS3);
+  volatile int* fail = reinterpret_cast<volatile int*>(smf + CP3_BAR + 8 * N_BARS3 + 16);
+  auto stage = [&](int s) { return smf + s * CP3_STAGE; };
+  unsigned char* sCZ = smf + CP3_CZ;
+  unsigned char* sAh = smf;                      // phase E: Re(Cm) K-major hi/lo, Y
+  unsigned char* sAl = smf + 16384;
+  unsigned char* sY = smf + 32768;
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int item = blockIdx.y, j0 = blockIdx.x * NB3;
+  const bool has_prev = c > 0, has_next = c < nch;
+  const bool prev_identity = c == 1;             // S_0 = I is not in memory
+  const int tp = (c - 1) * C2, tc0 = c * C2;     // first tokens of chunks c-1 and c
+  const unsigned long long bad_prev = has_prev ? badws[(size_t)item * nch + c - 1] : 0ull;
+  const unsigned long long bad_next = has_next ? badws[(size_t)item * nch + c] : 0ull;
+  const bool patch_w = (bad_prev | bad_next) != 0ull;
+  const int NH = D / KH3;
+  const size_t cm_off = ((size_t)item * (D / NB3) + blockIdx.x) * CM3_BYTES;
+
+  if (warp == 0) tc::tmem_alloc(tslot, 512);
+  if (tid == 0) {
+    for (int i = 0; i < N_BARS3; ++i) tc::mbar_init(&bars[i], 1);
+    *fail = 0;
+    tc::fence_mbar_init();
+  }
+  tc::fence_before_sync();
+  __syncthreads();
+  tc::fence_after_sync();
+  const uint32_t tbase = *tslot;
+  const uint32_t tZ = tbase, tDH = tbase + 128, tP1 = tbase + 128, tP2 = tbase + 256, tE = tbase + 384;
+
+  if (warp == 8) {
+    // ======================= producer (one thread) =======================
+    if (lane == 0) {
+      bool ok = true;
+      auto pwait = [&](int b, uint32_t par) {
+        if (!ok) return false;
+        if (*fail || !tc::mbar_wait(&bars[b], par, MAX_POLLS)) { ok = false; *fail = 1; record_timeout(); }
+        return ok;
+      };
+      auto issue = [&](int i) {   // tile i into stage i & 1
+        const int s = i & 1;
+        unsigned char* st = stage(s);
+        tc::mbar_expect_tx(&bars[B3_FULL + s], (has_prev ? 16384 + (prev_identity ? 0 : 32768) : 0) +
+                                                     (has_next ? 16384 : 0));
+        if (has_prev) {
+          tc::tma_load_3d(st, &tm_k, i * KH3, tp, item, &bars[B3_FULL + s]);
+          tc::tma_load_3d(st + 8192, &tm_v, i * KH3, tp, item, &bars[B3_FULL + s]);
+#pragma unroll
+          for (int bx = 0; bx < 2 && !prev_identity; ++bx) {
+            tc::tma_load_2d(st + 32768 + bx * 8192, &tm_sr, j0 + 32 * bx, (src_row_re + item) * D + i * KH3,
+                            &bars[B3_FULL + s]);
+            tc::tma_load_2d(st + 49152 + bx * 8192, &tm_si, j0 + 32 * bx, (src_row_im + item) * D + i * KH3,
+                            &bars[B3_FULL + s]);
+          }
+        }
+        if (has_next) {
+          tc::tma_load_3d(st + 16384, &tm_k, i * KH3, tc0, item, &bars[B3_FULL + s]);
+          tc::tma_load_3d(st + 16384 + 8192, &tm_v, i * KH3, tc0, item, &bars[B3_FULL + s]);
+        }
+      };
+      constexpr uint32_t ID_H = tc::idesc_bf16(64, N3, true, true);
+      constexpr uint32_t ID_Z = tc::idesc_bf16(128, N3, false, true);
+      uint32_t ndh[2] = {0, 0}, nmd[2] = {0, 0};
+      auto do_dh = [&](int i) {   // dH[i & 1] = W_{c-1} rows of tile i x Cm_{c-1}
+        const int s = i & 1, d = i & 1;
+        if (!pwait(B3_FULL + s, (i >> 1) & 1)) return false;
+        if (patch_w && !pwait(B3_WFIX + s, (i >> 1) & 1)) return false;
+        if (i == 0 && !pwait(B3_CMF, 0)) return false;
+        if (i >= 2 && !pwait(B3_DF + d, ((i - 2) >> 1) & 1)) return false;
+        tc::fence_after_sync();
+        const uint32_t aw = tc::smem_addr(stage(s));
+        const uint32_t ch = tc::smem_addr(sCZ), cl = ch + 32768;
+#pragma unroll 1
+        for (int ks = 0; ks < R2 / 16; ++ks) {
+          const uint64_t a = tc::sdesc_sw128(aw + ks * 2048, 16384, 1024);
+          tc::mma_bf16(tDH + 128 * d, a, tc::sdesc(ch + ks * 2 * (N3 / 8) * 128, (N3 / 8) * 128, 128), ID_H,
+                       ks > 0 ? 1u : 0u);
+          tc::mma_bf16(tDH + 128 * d, a, tc::sdesc(cl + ks * 2 * (N3 / 8) * 128, (N3 / 8) * 128, 128), ID_H, 1u);
+        }
+        tc::commit(&bars[B3_DH + d]);
+        ++ndh[d];
+        return true;
+      };
+      if (has_prev) {
+        tc::mbar_expect_tx(&bars[B3_CMF], CM3_BYTES);
+        tc::bulk_load(sCZ, cm_in + cm_off, CM3_BYTES / 2, &bars[B3_CMF]);
+        tc::bulk_load(sCZ + CM3_BYTES / 2, cm_in + cm_off + CM3_BYTES / 2, CM3_BYTES / 2, &bars[B3_CMF]);
+      }
+      issue(0);
+      if (NH > 1) issue(1);
+      if (has_prev && !do_dh(0)) ok = false;
+      for (int i = 0; i < NH && ok; ++i) {
+        const int s = i & 1;
+        if (has_prev && i + 1 < NH && !do_dh(i + 1)) break;
+        if (!has_prev) {
+          if (!pwait(B3_FULL + s, (i >> 1) & 1)) break;
+          if (patch_w && !pwait(B3_WFIX + s, (i >> 1) & 1)) break;
+        }
+        if (!pwait(B3_SPL + s, (i >> 1) & 1)) break;   // stored (and split) by the consumers
+        if (has_next) {
+          tc::fence_after_sync();
+          const uint32_t aw = tc::smem_addr(stage(s)) + 16384;
+          const uint32_t bh = tc::smem_addr(stage(s)) + 32768, bl = bh + 16384;
+#pragma unroll 1
+          for (int ks = 0; ks < KH3 / 16; ++ks) {
+            const uint64_t a = tc::sdesc_sw128(aw + ks * 32, 16, 1024);
+            tc::mma_bf16(tZ, a, tc::sdesc(bh + ks * 2 * (N3 / 8) * 128, (N3 / 8) * 128, 128), ID_Z,
+                         (i > 0 || ks > 0) ? 1u : 0u);
+            tc::mma_bf16(tZ, a, tc::sdesc(bl + ks * 2 * (N3 / 8) * 128, (N3 / 8) * 128, 128), ID_Z, 1u);
+          }
+          tc::commit(&bars[B3_MD + s]);
+          ++nmd[s];
+          if (!pwait(B3_MD + s, (nmd[s] - 1) & 1)) break;
+        }
+        if (i + 2 < NH) issue(i + 2);
+      }
+      // ---- phase T (chunk c): Cm_c = T_c Z_c; stages are free, CZ is free (every MMA done)
+      if (ok && has_next) {
+        const unsigned char* tsrc = Tws + ((size_t)item * nch + c) * 4 * T_TILE;
+        tc::mbar_expect_tx(&bars[B3_TT], 4 * T_TILE);
+        for (int p4 = 0; p4 < 4; ++p4) tc::bulk_load(smf + p4 * T_TILE, tsrc + p4 * T_TILE, T_TILE, &bars[B3_TT]);
+        if (pwait(B3_ZR, 0) && pwait(B3_TT, 0)) {
+          tc::fence_after_sync();
+          constexpr uint32_t ID_T = tc::idesc_bf16(128, N3, false, true);
+          const uint32_t zh = tc::smem_addr(sCZ), zl = zh + 32768;
+#pragma unroll 1
+          for (int part = 0; part < 2; ++part) {
+            const uint32_t th = tc::smem_addr(smf) + (2 * part) * T_TILE, tl = th + T_TILE;
+            const uint32_t td = part ? tP2 : tP1;
+#pragma unroll 1
+            for (int ks = 0; ks < R2 / 16; ++ks) {
+              const uint64_t ah = tc::sdesc(th + ks * 2 * R2 * 16, R2 * 16, 128);
+              const uint64_t al = tc::sdesc(tl + ks * 2 * R2 * 16, R2 * 16, 128);
+              const uint64_t b_h = tc::sdesc(zh + ks * 2 * (N3 / 8) * 128, (N3 / 8) * 128, 128);
+              const uint64_t b_l = tc::sdesc(zl + ks * 2 * (N3 / 8) * 128, (N3 / 8) * 128, 128);
+              tc::mma_bf16(td, ah, b_h, ID_T, ks > 0 ? 1u : 0u);
+              tc::mma_bf16(td, ah, b_l, ID_T, 1u);
+              tc::mma_bf16(td, al, b_h, ID_T, 1u);
+            }
+          }
+          tc::commit(&bars[B3_MT]);
+        }
+        // ---- phase E: E = Re(Cm_c) Y_c
+        if (ok && pwait(B3_CR, 0)) {
+          tc::fence_after_sync();
+          constexpr uint32_t ID_E = tc::idesc_bf16(128, C2, false, false);
+          const uint32_t ah = tc::smem_addr(sAh), al = tc::smem_addr(sAl), yh = tc::smem_addr(sY);
+#pragma unroll 1
+          for (int ks = 0; ks < NB3 / 16; ++ks) {
+            const uint64_t b_h = tc::sdesc(yh + ks * 2 * C2 * 16, C2 * 16, 128);
+            tc::mma_bf16(tE, tc::sdesc(ah + ks * 2 * R2 * 16, R2 * 16, 128), b_h, ID_E, ks > 0 ? 1u : 0u);
+            tc::mma_bf16(tE, tc::sdesc(al + ks * 2 * R2 * 16, R2 * 16, 128), b_h, ID_E, 1u);
+          }
+          tc::commit(&bars[B3_ME]);
+        }
+      }
+    }
+  } else {
+    // ======================= consumers (warps 0-7) =======================
+    const uint32_t lane_base = (uint32_t)(32 * (warp & 3)) << 16;
+    const int row = 32 * (warp & 3) + lane, half = warp >> 2;
+    const int hrow = 16 * (warp & 3) + lane;     // dH row of this thread (lanes 0-15)
+    bool ok = true;
+    auto cwait = [&](int b, uint32_t par) {
+      bool mine = ok && !*fail && tc::mbar_wait(&bars[b], par, MAX_POLLS);
+      const bool all = consumers_all(mine);
+      if (!all) { if (ok && tid == 0) record_timeout(); ok = false; *fail = 1; }
+      return ok;
+    };
+    auto zero_rows = [&](unsigned char* w, unsigned long long bad) {   // swizzled W half tile
+      for (int e = tid; e < R2 * 8; e += CONS) {
+        const int r = e % R2, cc = e / R2;
+        if ((bad >> tok(r)) & 1ull)
+          *reinterpret_cast<uint4*>(w + r * 128 + ((cc ^ (r & 7)) << 4)) = make_uint4(0, 0, 0, 0);
+      }
+    };
+    for (int i = 0; i < NH && ok; ++i) {
+      const int s = i & 1, d = i & 1;
+      unsigned char* st = stage(s);
+      unsigned char* sbox = st + 32768;
+      bool waited_full = false;
+      if (patch_w) {
+        if (!cwait(B3_FULL + s, (i >> 1) & 1)) break;
+        waited_full = true;
+        if (bad_prev) zero_rows(st, bad_prev);
+        if (bad_next) zero_rows(st + 16384, bad_next);
+        tc::fence_proxy_async();
+        tc::named_sync(1, CONS);
+        if (tid == 0) tc::mbar_arrive(&bars[B3_WFIX + s]);
+      }
+      if (has_prev) {
+        if (!cwait(B3_DH + d, (i >> 1) & 1)) break;
+        tc::fence_after_sync();
+        float dh[64];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) tc::tmem_ld16(tDH + 128 * d + lane_base + 64 * half + 16 * u, dh + 16 * u);
+        tc::fence_before_sync();
+        tc::named_sync(1, CONS);
+        if (tid == 0) tc::mbar_arrive(&bars[B3_DF + d]);
+        if (!waited_full && !cwait(B3_FULL + s, (i >> 1) & 1)) break;
+        if (lane < 16) {   // S_c = S_{c-1} + dH for row hrow, plane `half` (two 32-column boxes)
+          const int gi = i * KH3 + hrow;
+#pragma unroll
+          for (int bx = 0; bx < 2; ++bx) {
+            unsigned char* box = sbox + half * 16384 + bx * 8192;
+#pragma unroll
+            for (int cc = 0; cc < 8; ++cc) {
+              float4* p4 = reinterpret_cast<float4*>(box + hrow * 128 + ((cc ^ (hrow & 7)) << 4));
+              const int gc = j0 + 32 * bx + 4 * cc;
+              const float4 a = prev_identity ? make_float4(!half && gi == gc ? 1.f : 0.f, !half && gi == gc + 1 ? 1.f : 0.f,
+                                                           !half && gi == gc + 2 ? 1.f : 0.f, !half && gi == gc + 3 ? 1.f : 0.f)
+                                             : *p4;
+              const float* x = dh + 32 * bx + 4 * cc;
+              *p4 = make_float4(a.x + x[0], a.y + x[1], a.z + x[2], a.w + x[3]);
+            }
+          }
+        }
+        tc::fence_proxy_async();
+        tc::named_sync(1, CONS);
+        if (tid == 0) {
+#pragma unroll
+          for (int bx = 0; bx < 2; ++bx) {
+            tc::tma_store_2d(&tm_dr, j0 + 32 * bx, (dst_row_re + item) * D + i * KH3, sbox + bx * 8192);
+            tc::tma_store_2d(&tm_di, j0 + 32 * bx, (dst_row_im + item) * D + i * KH3, sbox + 16384 + bx * 8192);
+          }
+          tc::bulk_commit();
+          tc::bulk_wait_read<0>();               // the stores have read the tile
+        }
+        tc::named_sync(1, CONS);
+      } else if (!waited_full) {
+        if (!cwait(B3_FULL + s, (i >> 1) & 1)) break;
+      }
+      if (has_next) {
+        // split S_c (or the identity for c == 0) in place: MN-major B operand, K = 64 rows
+        float x[4][8];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const int e = tid + CONS * u;
+          const int ri = e % KH3, gg = e / KH3;   // row ri, 8-column group gg (0-7 re, 8-15 im)
+          if (!has_prev) {
+            const int gi = i * KH3 + ri, col = j0 + (gg & 7) * 8;
+#pragma unroll
+            for (int jj = 0; jj < 8; ++jj) x[u][jj] = (gg < 8 && gi == col + jj) ? 1.f : 0.f;
+          } else {
+            const unsigned char* box = sbox + (gg >> 3) * 16384 + ((gg >> 2) & 1) * 8192;
+            const int q0 = 2 * (gg & 3);
+            const float4 a = *reinterpret_cast<const float4*>(box + ri * 128 + ((q0 ^ (ri & 7)) << 4));
+            const float4 b = *reinterpret_cast<const float4*>(box + ri * 128 + (((q0 + 1) ^ (ri & 7)) << 4));
+            x[u][0] = a.x; x[u][1] = a.y; x[u][2] = a.z; x[u][3] = a.w;
+            x[u][4] = b.x; x[u][5] = b.y; x[u][6] = b.z; x[u][7] = b.w;
+          }
+        }
+        tc::named_sync(1, CONS);
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const int e = tid + CONS * u;
+          const int ri = e % KH3, gg = e / KH3;
+          uint4 hv, lv;
+          tc::split8(x[u], hv, lv);
+          *reinterpret_cast<uint4*>(sbox + mnmaj(ri, gg * 8, N3 / 8)) = hv;
+          *reinterpret_cast<uint4*>(sbox + 16384 + mnmaj(ri, gg * 8, N3 / 8)) = lv;
+        }
+        tc::fence_proxy_async();
+      }
+      tc::named_sync(1, CONS);
+      if (tid == 0) tc::mbar_arrive(&bars[B3_SPL + s]);
+    }
+    if (tid == 0) tc::bulk_wait<0>();            // this launch's state writes performed
+    // ---- phase T: Z -> operand in CZ (the last tile's Z MMA done: every MMA done)
+    if (ok && has_next) {
+      const int sl = (NH - 1) & 1;
+      if (cwait(B3_MD + sl, ((NH - 1) >> 1) & 1)) {
+        tc::fence_after_sync();
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          float z[16];
+          tc::tmem_ld16(tZ + lane_base + 64 * half + 16 * u, z);
+#pragma unroll
+          for (int g2 = 0; g2 < 2; ++g2) {
+            uint4 hv, lv;
+            tc::split8(z + 8 * g2, hv, lv);
+            const int off = mnmaj(row, 64 * half + 16 * u + 8 * g2, N3 / 8);
+            *reinterpret_cast<uint4*>(sCZ + off) = hv;
+            *reinterpret_cast<uint4*>(sCZ + 32768 + off) = lv;
+          }
+        }
+        tc::fence_proxy_async();
+        tc::fence_before_sync();
+        tc::named_sync(1, CONS);
+        if (tid == 0) tc::mbar_arrive(&bars[B3_ZR]);
+      }
+      // ---- Cm_c -> global operand (next launch), Re(Cm_c) K-major + Y -> smem (phase E)
+      if (ok && cwait(B3_MT, 0)) {
+        tc::fence_after_sync();
+        unsigned char* cmg = cm_out + cm_off;
+#pragma unroll
+        for (int u = 0; u < 2; ++u) {   // complex columns 32 * half + 16 * u .. + 15
+          float p1r[16], p1i[16], p2r[16], p2i[16];
+          const int jc = 32 * half + 16 * u;
+          tc::tmem_ld16(tP1 + lane_base + jc, p1r);
+          tc::tmem_ld16(tP1 + lane_base + NB3 + jc, p1i);
+          tc::tmem_ld16(tP2 + lane_base + jc, p2r);
+          tc::tmem_ld16(tP2 + lane_base + NB3 + jc, p2i);
+          float cr[16], ci[16];
+#pragma unroll
+          for (int j = 0; j < 16; ++j) { cr[j] = p1r[j] - p2i[j]; ci[j] = p1i[j] + p2r[j]; }
+#pragma unroll
+          for (int g2 = 0; g2 < 2; ++g2) {
+            uint4 hv, lv;
+            const int jj = jc + 8 * g2;
+            tc::split8(cr + 8 * g2, hv, lv);
+            *reinterpret_cast<uint4*>(cmg + mnmaj(row, jj, N3 / 8)) = hv;
+            *reinterpret_cast<uint4*>(cmg + 32768 + mnmaj(row, jj, N3 / 8)) = lv;
+            *reinterpret_cast<uint4*>(sAh + kmaj(row, jj, R2)) = hv;
+            *reinterpret_cast<uint4*>(sAl + kmaj(row, jj, R2)) = lv;
+            tc::split8(ci + 8 * g2, hv, lv);
+            *reinterpret_cast<uint4*>(cmg + mnmaj(row, NB3 + jj, N3 / 8)) = hv;
+            *reinterpret_cast<uint4*>(cmg + 32768 + mnmaj(row, NB3 + jj, N3 / 8)) = lv;
+          }
+        }
+        {
+          const int nt = min(C2, S - tc0);
+          const int t = tid % C2, gq = tid / C2;   // 64 tokens x 4 groups of 8 columns, twice
+#pragma unroll
+          for (int u = 0; u < 2; ++u) {
+            const int g8 = gq + 4 * u;
+            uint4 w = make_uint4(0, 0, 0, 0);
+            if (t < nt) w = *reinterpret_cast<const uint4*>(q + ((size_t)item * S + tc0 + t) * D + j0 + g8 * 8);
+            *reinterpret_cast<uint4*>(sY + kmaj(t, g8 * 8, C2)) = w;
+          }
+        }
+        tc::fence_proxy_async();
+        tc::fence_before_sync();
+        tc::named_sync(1, CONS);
+        if (tid == 0) tc::mbar_arrive(&bars[B3_CR]);
+      }
+      if (ok && cwait(B3_ME, 0)) {
+        tc::fence_after_sync();
+        float e[32];
+        tc::tmem_ld16(tE + lane_base + 32 * half, e);
+        tc::tmem_ld16(tE + lane_base + 32 * half + 16, e + 16);
+        float4* Eo = reinterpret_cast<float4*>(Ews + ((size_t)item * nch + c) * R2 * C2 + (size_t)row * C2 +
+                                               32 * half);
+#pragma unroll
+        for (int t = 0; t < 8; ++t) atomicAdd(Eo + t, make_float4(e[4 * t], e[4 * t + 1], e[4 * t + 2], e[4 * t + 3]));
+      }
+    }
+  }
+  tc::fence_before_sync();
+  __syncthreads();
+  if (warp == 0) tc::tmem_dealloc(tbase, 512);
+}
+
 // Readout of a batch of chunks from their end states (rows of a ring of state buffers):
 // CTA (x, y) = (chunk c0 + x / (D/128), item y, rows 128 (x % (D/128)) ...).
 __global__ void __launch_bounds__(WS_THREADS, 2)
@@ -2132,18 +2526,23 @@ int make_state_map(CUtensorMap* m, const float* base, int b, int D, int rows = K
   return VERACE_OK;
 }
 
-// Schedule of the bf16 path.  Merged: one column-pass + readout launch per chunk, one
-// CTA per SM (lowest latency while a launch's CTAs fit on the SMs at once).  Batched:
-// column passes two CTAs per SM, readouts batched over up to RING chunks (better once
-// the merged launch needs more than one CTA generation per SM).  VERACE_CHAM_BATCHED=1
-// or =0 forces one; both are tested against each other.
-bool merged_readout(int b, int D) {
-  const char* e = getenv("VERACE_CHAM_BATCHED");
-  if (e != nullptr && e[0] == '1') return false;
-  if (e != nullptr && e[0] == '0') return true;
+// Schedule of the bf16 path.
+//   merged:  one column-pass + readout launch per chunk, one CTA per SM.
+//   batched: column passes two CTAs per SM, readouts batched over up to RING chunks.
+//   fused:   one pass over the state per chunk (finish chunk c-1, start chunk c), one CTA
+//            per 64 columns, readouts batched as above.
+// VERACE_CHAM_SCHEDULE=merged|batched|fused forces one; all are tested against each other.
+enum Schedule { SCHED_MERGED, SCHED_BATCHED, SCHED_FUSED };
+Schedule cham_schedule(int b, int D) {
+  const char* e = getenv("VERACE_CHAM_SCHEDULE");
+  if (e != nullptr) {
+    if (!strcmp(e, "merged")) return SCHED_MERGED;
+    if (!strcmp(e, "batched")) return SCHED_BATCHED;
+    if (!strcmp(e, "fused")) return SCHED_FUSED;
+  }
   int dev = 0, sms = 148;
   if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  return (long long)b * (D / NB2 + D / R2) <= sms;
+  return (long long)b * (D / NB2 + D / R2) <= sms ? SCHED_MERGED : SCHED_BATCHED;
 }
 
 size_t tc_prep_smem() { return sizeof(float) * (PREP_DT * (R2 + 1) + 3 * R2 * (R2 + 1)); }
@@ -2182,7 +2581,42 @@ int launch_cham_tc(const void* q, const void* k, const void* v, const float* gam
       return rc;
     if (nch < 2) { m_ping_r = m_out_r; m_ping_i = m_out_i; }
   }
-  if (WS && !merged_readout(b, D)) {
+  const Schedule sched = WS ? cham_schedule(b, D) : SCHED_MERGED;
+  if (sched == SCHED_FUSED) {
+    CUtensorMap mq, m_ring, m_ring64, m_him64, m_hi64;
+    const size_t plane = (size_t)b * D * D;
+    if ((rc = make_kv_map(&mq, q, b, s, D)) || (rc = make_state_map(&m_ring, w.ring, w.nring * b, D)) ||
+        (rc = make_state_map(&m_ring64, w.ring, w.nring * b, D, KH3)) ||
+        (rc = make_state_map(&m_hi64, hi, b, D, KH3)))
+      return rc;
+    if (nch >= 2 && (rc = make_state_map(&m_him64, w.Him, b, D, KH3))) return rc;
+    if (nch < 2) m_him64 = m_hi64;
+    VERACE_CUDA(cudaFuncSetAttribute(cham_tc_colpass3, cudaFuncAttributeMaxDynamicSharedMemorySize, CP3_SMEM));
+    VERACE_CUDA(cudaFuncSetAttribute(cham_tc_readout_batch, cudaFuncAttributeMaxDynamicSharedMemorySize, RW2_SMEM));
+    auto im_buf = [&](int j) { return ((nch - 1 - j) % 2 == 0) ? hi : w.Him; };   // im of S_{j+1}
+    const size_t cm_half = (size_t)b * (D / 64) * (64 * 1024);
+    for (int c = 0; c <= nch; ++c) {
+      // launch c finishes chunk c-1 (S_c into ring[(c-1) % RING] and im_buf(c-1)) and starts chunk c
+      const int rs = c >= 2 ? (c - 2) % w.nring : 0, rd = c >= 1 ? (c - 1) % w.nring : 0;
+      float* si = c >= 2 ? im_buf(c - 2) : hi;
+      float* di = c >= 1 ? im_buf(c - 1) : hi;
+      cham_tc_colpass3<<<dim3(D / 64, b), WS_THREADS, CP3_SMEM, st>>>(
+          mk, mv, m_ring64, si == hi ? m_hi64 : m_him64, m_ring64, di == hi ? m_hi64 : m_him64, rs * b, 0, rd * b, 0,
+          w.cm + ((c + 1) & 1) * cm_half, w.cm + (c & 1) * cm_half, (const __nv_bfloat16*)q, w.T, w.E, w.bad, s, D,
+          nch, c);
+      if ((rc = check_launch("cham_tc_colpass3"))) return rc;
+      if (c >= 1 && (c % w.nring == 0 || c == nch)) {
+        const int cb = ((c - 1) / w.nring) * w.nring;
+        cham_tc_readout_batch<<<dim3((D / R2) * (c - cb), b), WS_THREADS, RW2_SMEM, st>>>(
+            mk, mv, mq, m_ring, w.E, w.bad, (__nv_bfloat16*)out, s, D, nch, cb, w.nring, b);
+        if ((rc = check_launch("cham_tc_readout_batch"))) return rc;
+      }
+    }
+    VERACE_CUDA(cudaMemcpyAsync(hr, w.ring + ((nch - 1) % w.nring) * plane, plane * sizeof(float),
+                                cudaMemcpyDeviceToDevice, st));
+    return VERACE_OK;
+  }
+  if (sched == SCHED_BATCHED) {
     // column passes two CTAs per SM, readouts batched over up to RING chunks
     CUtensorMap mq, m_ring, m_ring64, m_him64, m_hi64, m_him128, m_hi128;
     const size_t plane = (size_t)b * D * D;

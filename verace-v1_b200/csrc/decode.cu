@@ -47,7 +47,12 @@ __device__ unsigned int g_decode_status;
 namespace {
 
 constexpr int DT = 256;        // threads per CTA
-constexpr int CWD = 32;        // CHAM stripe width (columns)
+#ifndef VERACE_DECODE_CWD
+#define VERACE_DECODE_CWD 32
+#endif
+constexpr int CWD = VERACE_DECODE_CWD;   // CHAM stripe width (columns)
+constexpr int TPR = CWD / 4;             // threads per row (4 columns each)
+constexpr int RPG = 256 / TPR;           // rows per row group
 constexpr int MAXD = 2048;     // largest hologram dimension
 constexpr int MAXHD = 128;     // largest SSSD head dimension
 constexpr int UNR = 4;         // row groups of 32 in flight per thread and pass
@@ -201,8 +206,8 @@ __device__ void sssd_part(const DecodeArgs& A, int chain) {
 // FIRST_ORDER (Hᴴu)re, (Hᴴu)im.
 constexpr int NQ = 6;
 
-// Thread layout over a stripe (D rows x 32 columns, re and im): 8 threads per row
-// (columns 4 c8 .. 4 c8 + 3), 32 rows per row group (warp w: rows 4 w .. 4 w + 3).
+// Thread layout over a stripe (D rows x CWD columns, re and im): TPR = CWD / 4 threads per
+// row (columns 4 c8 .. 4 c8 + 3), RPG = 256 / TPR rows per row group.
 template <typename T, bool FO>
 __device__ void cham_part(const DecodeArgs& A, int unit) {
   __shared__ float ks[MAXD], vs[MAXD];
@@ -215,9 +220,9 @@ __device__ void cham_part(const DecodeArgs& A, int unit) {
   const int D = A.D;
   const int nst = D / CWD;
   const int item = unit / nst, stripe = unit % nst;
-  const int c8 = lane & 7;
+  const int c8 = lane % TPR;
   const int c0 = stripe * CWD + 4 * c8;
-  const int rp = w * 4 + (lane >> 3);   // row within a group of 32
+  const int rp = threadIdx.x / TPR;     // row within a row group
   constexpr int nq = FO ? NQ : 4;
 
   const size_t hoff = (size_t)item * D * D;
@@ -244,11 +249,11 @@ __device__ void cham_part(const DecodeArgs& A, int unit) {
   for (int qn = 0; qn < NQ; ++qn)
 #pragma unroll
     for (int j = 0; j < 4; ++j) acc[qn][j] = 0.f;
-  for (int g0 = 0; g0 < D; g0 += 32 * UNR) {
+  for (int g0 = 0; g0 < D; g0 += RPG * UNR) {
     float4 xr[UNR], xi[UNR];
 #pragma unroll
     for (int u = 0; u < UNR; ++u) {
-      const int r = g0 + 32 * u + rp;
+      const int r = g0 + RPG * u + rp;
       if (r < D) {
         xr[u] = *reinterpret_cast<const float4*>(Hr + (size_t)r * D + c0);
         xi[u] = *reinterpret_cast<const float4*>(Hi + (size_t)r * D + c0);
@@ -258,7 +263,7 @@ __device__ void cham_part(const DecodeArgs& A, int unit) {
     }
 #pragma unroll
     for (int u = 0; u < UNR; ++u) {
-      const int r = g0 + 32 * u + rp;
+      const int r = g0 + RPG * u + rp;
       if (r >= D) continue;
       const float kr = ks[r], vr = vs[r];
 #pragma unroll
@@ -284,11 +289,11 @@ __device__ void cham_part(const DecodeArgs& A, int unit) {
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
       float x = acc[qn][j];
-      x += __shfl_xor_sync(0xffffffffu, x, 8);
-      x += __shfl_xor_sync(0xffffffffu, x, 16);
+#pragma unroll
+      for (int o = TPR; o < 32; o <<= 1) x += __shfl_xor_sync(0xffffffffu, x, o);
       acc[qn][j] = x;
     }
-  if (lane < 8) {
+  if (lane < TPR) {
 #pragma unroll
     for (int qn = 0; qn < nq; ++qn)
 #pragma unroll
@@ -349,11 +354,11 @@ __device__ void cham_part(const DecodeArgs& A, int unit) {
 
   // ---- pass 2: update, store, readout partials (rows re-read from L2, last-read first)
   float* part = A.part + ((size_t)item * nst + stripe) * D;
-  for (int g0 = (D - 1) / (32 * UNR) * (32 * UNR); g0 >= 0; g0 -= 32 * UNR) {
+  for (int g0 = (D - 1) / (RPG * UNR) * (RPG * UNR); g0 >= 0; g0 -= RPG * UNR) {
     float4 xr[UNR], xi[UNR];
 #pragma unroll
     for (int u = 0; u < UNR; ++u) {
-      const int r = g0 + 32 * u + rp;
+      const int r = g0 + RPG * u + rp;
       if (r < D) {
         xr[u] = __ldcs(reinterpret_cast<const float4*>(Hr + (size_t)r * D + c0));
         xi[u] = __ldcs(reinterpret_cast<const float4*>(Hi + (size_t)r * D + c0));
@@ -363,7 +368,7 @@ __device__ void cham_part(const DecodeArgs& A, int unit) {
     }
 #pragma unroll
     for (int u = 0; u < UNR; ++u) {
-      const int r = g0 + 32 * u + rp;
+      const int r = g0 + RPG * u + rp;
       float o = 0.f;
       if (r < D) {
         if (ok) {
@@ -382,9 +387,8 @@ __device__ void cham_part(const DecodeArgs& A, int unit) {
         __stcs(reinterpret_cast<float4*>(Hr + (size_t)r * D + c0), xr[u]);
         __stcs(reinterpret_cast<float4*>(Hi + (size_t)r * D + c0), xi[u]);
       }
-      o += __shfl_xor_sync(0xffffffffu, o, 1);
-      o += __shfl_xor_sync(0xffffffffu, o, 2);
-      o += __shfl_xor_sync(0xffffffffu, o, 4);
+#pragma unroll
+      for (int sh = 1; sh < TPR; sh <<= 1) o += __shfl_xor_sync(0xffffffffu, o, sh);
       if (c8 == 0 && r < D) part[r] = o;
     }
   }

@@ -83,16 +83,35 @@ __device__ __forceinline__ void fence_mbar_init() {
 
 // Wait for the phase with parity `parity` of `mbar` to complete; gives up after
 // `max_polls` polls and returns false (the caller records a timeout status).
+#ifndef VERACE_MBAR_WAIT
+#define VERACE_MBAR_WAIT 0   // 0: try_wait; 1: test_wait spin; 2: try_wait with a short suspend hint
+#endif
 __device__ __forceinline__ bool mbar_wait(uint64_t* mbar, uint32_t parity, uint32_t max_polls) {
   const uint32_t a = smem_addr(mbar);
   for (uint32_t it = 0; it < max_polls; ++it) {
     uint32_t done;
+#if VERACE_MBAR_WAIT == 1
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tmbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}\n"
+        : "=r"(done)
+        : "r"(a), "r"(parity)
+        : "memory");
+#elif VERACE_MBAR_WAIT == 2
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}\n"
+        : "=r"(done)
+        : "r"(a), "r"(parity), "r"(20u)
+        : "memory");
+#else
     asm volatile(
         "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
         "selp.u32 %0, 1, 0, p;\n\t}\n"
         : "=r"(done)
         : "r"(a), "r"(parity)
         : "memory");
+#endif
     if (done) return true;
   }
   return false;
