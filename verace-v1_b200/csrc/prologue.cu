@@ -7,8 +7,9 @@
 // The reference runs these as separate projections and a dozen elementwise and reduction
 // kernels; here they are one GEMM (outside this file) and one pass over its output.
 //
-// Work split: one warp per (row, vector, head) normalises d values with 16-byte loads
-// (norms in fp32); the gates are a grid-stride tail of the same launch.
+// Work split: each head vector is normalised by a group of lanes of one warp (16-byte
+// loads, fp32 norms, segmented shuffle reductions): several short vectors share a warp,
+// long ones take a whole warp.  The gates are a grid-stride tail of the same launch.
 #include "common.cuh"
 
 namespace verace {
@@ -70,31 +71,36 @@ __device__ __forceinline__ void store8v(T* p, const float* x) {
 __device__ __forceinline__ float silu_f(float x) { return x / (1.f + expf(-x)); }
 __device__ __forceinline__ float sigmoid_f(float x) { return 1.f / (1.f + expf(-x)); }
 
-// Up to MAXV values per lane are held between the norm and the scaling.
+// A "unit" is one head vector of d values (d/8 chunks of 8).  Units of at most 16 chunks
+// share a warp (32 / L lanes per unit, one chunk per lane); longer units take the whole
+// warp with CPL chunks per lane.
 constexpr int MAXV = 8;   // chunks of 8 per lane: d <= 32 * 8 * 8 = 2048
 
-template <typename T>
+template <typename T, int CPL>
 __global__ void __launch_bounds__(PT)
 mixer_prologue_kernel(const T* __restrict__ y, long long ld, T* __restrict__ q, T* __restrict__ k,
                       T* __restrict__ v, float* __restrict__ gate, const unsigned char* __restrict__ mask,
-                      long long n, int h, int d, int g, int silu_v, long long nvec_blocks) {
+                      long long n, int h, int d, int g, int silu_v, int L, long long nvec_blocks) {
   const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
   const int hd = h * d;
   if ((long long)blockIdx.x < nvec_blocks) {
-    const long long unit = (long long)blockIdx.x * (PT / 32) + w;   // (row, part, head)
-    if (unit >= n * 3 * h) return;
-    const long long r = unit / (3 * h);
-    const int rem = (int)(unit % (3 * h)), part = rem / h, head = rem % h;
+    const int upw = 32 / L;                                    // units per warp
+    const long long unit = ((long long)blockIdx.x * (PT / 32) + w) * upw + lane / L;   // (row, part, head)
+    const int sl = lane % L;                                   // lane within the unit
+    const bool active = unit < n * 3 * h;
+    const long long uu = active ? unit : 0;
+    const long long r = uu / (3 * h);
+    const int rem = (int)(uu % (3 * h)), part = rem / h, head = rem % h;
     const T* src = y + r * ld + (long long)part * hd + (long long)head * d;
     T* dst = (part == 0 ? q : part == 1 ? k : v) + r * hd + (long long)head * d;
     const bool act = part == 2 && silu_v;
     const int nc = d / 8;
-    float x[MAXV][8];
+    float x[CPL][8];
     float ss = 0.f;
 #pragma unroll
-    for (int i = 0; i < MAXV; ++i) {
-      const int cc = lane + 32 * i;
-      if (cc < nc) {
+    for (int i = 0; i < CPL; ++i) {
+      const int cc = sl + L * i;
+      if (active && cc < nc) {
         load8v<T>(src + 8 * cc, x[i]);
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
@@ -103,12 +109,14 @@ mixer_prologue_kernel(const T* __restrict__ y, long long ld, T* __restrict__ q, 
         }
       }
     }
-    ss = warp_sum32(ss);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1)
+      if (o < L) ss += __shfl_xor_sync(0xffffffffu, ss, o);
     const float inv = 1.f / fmaxf(sqrtf(ss), 1e-12f);
 #pragma unroll
-    for (int i = 0; i < MAXV; ++i) {
-      const int cc = lane + 32 * i;
-      if (cc < nc) {
+    for (int i = 0; i < CPL; ++i) {
+      const int cc = sl + L * i;
+      if (active && cc < nc) {
 #pragma unroll
         for (int j = 0; j < 8; ++j) x[i][j] *= inv;
         store8v<T>(dst + 8 * cc, x[i]);
@@ -124,6 +132,33 @@ mixer_prologue_kernel(const T* __restrict__ y, long long ld, T* __restrict__ q, 
   float val = 0.1f * sigmoid_f(to_f32(y[r * ld + 3LL * hd + j]));
   if (mask && !mask[r]) val = 0.f;
   gate[e] = val;
+}
+
+template <typename T>
+int launch_prologue(const void* y, long long ld, void* q, void* k, void* v, float* gate, const unsigned char* mask,
+                    long long n, int h, int d, int g, int silu_v, cudaStream_t st) {
+  const int nc = d / 8;
+  int L, cpl;
+  if (nc <= 16 && (16 % nc) == 0) { L = nc; cpl = 1; }
+  else { L = 32; cpl = (nc + 31) / 32; }
+  const long long units = n * 3 * h;
+  const long long per_block = (long long)(PT / 32) * (32 / L);
+  const long long nvec_blocks = (units + per_block - 1) / per_block;
+  const long long ngate_blocks = (n * g + PT - 1) / PT;
+  const long long grid = nvec_blocks + ngate_blocks;
+  VERACE_REQUIRE(grid < (1LL << 31), VERACE_ERR_UNSUPPORTED, "verace_mixer_prologue: too many rows");
+  const T* yy = (const T*)y;
+  T *qq = (T*)q, *kk = (T*)k, *vv = (T*)v;
+  if (cpl == 1)
+    mixer_prologue_kernel<T, 1><<<(unsigned)grid, PT, 0, st>>>(yy, ld, qq, kk, vv, gate, mask, n, h, d, g, silu_v, L,
+                                                                nvec_blocks);
+  else if (cpl <= 4)
+    mixer_prologue_kernel<T, 4><<<(unsigned)grid, PT, 0, st>>>(yy, ld, qq, kk, vv, gate, mask, n, h, d, g, silu_v, L,
+                                                                nvec_blocks);
+  else
+    mixer_prologue_kernel<T, MAXV><<<(unsigned)grid, PT, 0, st>>>(yy, ld, qq, kk, vv, gate, mask, n, h, d, g, silu_v,
+                                                                   L, nvec_blocks);
+  return check_launch("mixer_prologue_kernel");
 }
 
 }  // namespace
@@ -148,26 +183,14 @@ extern "C" int verace_mixer_prologue(const void* y, long long ld, void* q, void*
   if (n == 0) return VERACE_OK;
   VERACE_REQUIRE(y && q && k && v && (gate || gate_cols == 0), VERACE_ERR_INVALID,
                  "verace_mixer_prologue: NULL pointer");
-  const long long nvec_blocks = (n * 3 * heads + PT / 32 - 1) / (PT / 32);
-  const long long ngate_blocks = (n * gate_cols + PT - 1) / PT;
-  const long long grid = nvec_blocks + ngate_blocks;
-  VERACE_REQUIRE(grid < (1LL << 31), VERACE_ERR_UNSUPPORTED, "verace_mixer_prologue: too many rows");
   cudaStream_t st = (cudaStream_t)stream;
   switch (dtype) {
     case VERACE_F32:
-      mixer_prologue_kernel<float><<<(unsigned)grid, PT, 0, st>>>(
-          (const float*)y, ld, (float*)q, (float*)k, (float*)v, gate, mask, n, heads, head_dim, gate_cols, silu_v,
-          nvec_blocks);
-      break;
+      return launch_prologue<float>(y, ld, q, k, v, gate, mask, n, heads, head_dim, gate_cols, silu_v, st);
     case VERACE_BF16:
-      mixer_prologue_kernel<__nv_bfloat16><<<(unsigned)grid, PT, 0, st>>>(
-          (const __nv_bfloat16*)y, ld, (__nv_bfloat16*)q, (__nv_bfloat16*)k, (__nv_bfloat16*)v, gate, mask, n, heads,
-          head_dim, gate_cols, silu_v, nvec_blocks);
-      break;
+      return launch_prologue<__nv_bfloat16>(y, ld, q, k, v, gate, mask, n, heads, head_dim, gate_cols, silu_v, st);
     default:
-      mixer_prologue_kernel<__half><<<(unsigned)grid, PT, 0, st>>>(
-          (const __half*)y, ld, (__half*)q, (__half*)k, (__half*)v, gate, mask, n, heads, head_dim, gate_cols, silu_v,
-          nvec_blocks);
+      return launch_prologue<__half>(y, ld, q, k, v, gate, mask, n, heads, head_dim, gate_cols, silu_v, st);
   }
-  return check_launch("mixer_prologue_kernel");
 }
+
