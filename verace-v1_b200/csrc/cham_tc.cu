@@ -1755,7 +1755,9 @@ cham_tc_colpass2(const __grid_constant__ CUtensorMap tm_k, const __grid_constant
     // ======================= producer (one thread) =======================
     if (lane == 0) {
       bool ok = true;
-      uint32_t nfull[3] = {0, 0, 0}, nspl[3] = {0, 0, 0}, nmd[3] = {0, 0, 0}, ndh[2] = {0, 0}, ndf[2] = {0, 0};
+      // Barrier parities are closed forms of the tile indices (no counters indexed by a
+      // runtime slot, which would live in local memory): phase-A half tile h is use h / 3
+      // of slot h % 3; phase-B tile kt is use a_uses(s) + kt / 2 of slot s = (kt + 1) & 1.
       auto pwait = [&](int b, uint32_t par) {
         if (!ok) return false;
         if (*fail || !tc::mbar_wait(&bars[b], par, MAX_POLLS)) { ok = false; *fail = 1; record_timeout(); }
@@ -1788,7 +1790,7 @@ cham_tc_colpass2(const __grid_constant__ CUtensorMap tm_k, const __grid_constant
       for (int h = 0; h < 3 && h < NH; ++h) issue_a(h);
       for (int h = 0; h < NH && ok; ++h) {
         const int s = h % 3;
-        if (!pwait(B2_FULL + s, nfull[s]++ & 1) || !pwait(B2_SPL + s, nspl[s]++ & 1)) break;
+        if (!pwait(B2_FULL + s, (h / 3) & 1) || !pwait(B2_SPL + s, (h / 3) & 1)) break;
         tc::fence_after_sync();
         const uint32_t aw = tc::smem_addr(slot(s));
         const uint32_t bh = aw + 16384, bl = aw + 24576;
@@ -1800,9 +1802,8 @@ cham_tc_colpass2(const __grid_constant__ CUtensorMap tm_k, const __grid_constant
           tc::mma_bf16(tZ, a, tc::sdesc(bl + ks * 2 * (N2 / 8) * 128, (N2 / 8) * 128, 128), ID_Z, 1u);
         }
         tc::commit(&bars[B2_MD + s]);
-        ++nmd[s];
         if (h + 3 < NH) {
-          if (!pwait(B2_MD + s, (nmd[s] - 1) & 1)) break;
+          if (!pwait(B2_MD + s, (h / 3) & 1)) break;
           issue_a(h + 3);
         }
       }
@@ -1824,7 +1825,7 @@ cham_tc_colpass2(const __grid_constant__ CUtensorMap tm_k, const __grid_constant
           tc::mma_bf16(td, al, b_h, ID_T, 1u);
         }
       };
-      if (ok && pwait(B2_MD + sl, (nmd[sl] - 1) & 1)) {   // every phase-A MMA done: ring free
+      if (ok && pwait(B2_MD + sl, ((NH - 1) / 3) & 1)) {   // every phase-A MMA done: ring free
         tc::mbar_expect_tx(&bars[B2_TT], 2 * T_TILE);
         tc::bulk_load(slot(0), tsrc, T_TILE, &bars[B2_TT]);
         tc::bulk_load(slot(1), tsrc + T_TILE, T_TILE, &bars[B2_TT]);
@@ -1864,12 +1865,12 @@ cham_tc_colpass2(const __grid_constant__ CUtensorMap tm_k, const __grid_constant
       // the state tile into the same slot -> consumers' epilogue -> TMA store -> slot free
       if (ok && pwait(B2_ME, 0)) {
         if (NT > 1) issue_b(1);
-        uint32_t nsr[2] = {0, 0};
         for (int kt = 0; kt < NT && ok; ++kt) {
           const int s = (kt + 1) & 1, d = kt & 1;
-          if (!pwait(B2_FULL + s, nfull[s]++ & 1)) break;
-          if (patch_w && !pwait(B2_SPL + s, nspl[s]++ & 1)) break;
-          if (kt >= 2 && !pwait(B2_DF + d, ndf[d]++ & 1)) break;
+          const uint32_t use = (uint32_t)((NH + 2 - s) / 3 + (kt >> 1));   // use of slot s
+          if (!pwait(B2_FULL + s, use & 1)) break;
+          if (patch_w && !pwait(B2_SPL + s, use & 1)) break;
+          if (kt >= 2 && !pwait(B2_DF + d, ((kt - 2) >> 1) & 1)) break;
           tc::fence_after_sync();
           const uint32_t aw = tc::smem_addr(slot(s));
           const uint32_t ch = tc::smem_addr(sZh), cl = tc::smem_addr(sZl);
@@ -1881,9 +1882,8 @@ cham_tc_colpass2(const __grid_constant__ CUtensorMap tm_k, const __grid_constant
             tc::mma_bf16(tDH + 64 * d, a, tc::sdesc(cl + ks * 2 * (N2 / 8) * 128, (N2 / 8) * 128, 128), ID_H, 1u);
           }
           tc::commit(&bars[B2_DH + d]);
-          ++ndh[d];
           // the W tile has been read: the state tile takes its slot
-          if (!pwait(B2_DH + d, (ndh[d] - 1) & 1)) break;
+          if (!pwait(B2_DH + d, (kt >> 1) & 1)) break;
           if (!src_identity) {
             tc::mbar_expect_tx(&bars[B2_SF + s], 32 * 1024);
             tc::tma_load_2d(slot(s), &tm_sr128, j0, (src_row_re + item) * D + kt * KT, &bars[B2_SF + s]);
@@ -1892,7 +1892,7 @@ cham_tc_colpass2(const __grid_constant__ CUtensorMap tm_k, const __grid_constant
           // tile kt-1's slot, once its store has read it, takes W tile kt+1
           if (kt >= 1 && kt + 1 < NT) {
             const int sp = kt & 1;
-            if (!pwait(B2_SR + sp, nsr[sp]++ & 1)) break;
+            if (!pwait(B2_SR + sp, ((kt - 1) >> 1) & 1)) break;
             issue_b(kt + 1);
           }
         }
@@ -1903,7 +1903,6 @@ cham_tc_colpass2(const __grid_constant__ CUtensorMap tm_k, const __grid_constant
     const uint32_t lane_base = (uint32_t)(32 * (warp & 3)) << 16;
     const int row = 32 * (warp & 3) + lane, half = warp >> 2;
     bool ok = true;
-    uint32_t nfull[3] = {0, 0, 0};
     auto cwait = [&](int b, uint32_t par) {
       bool mine = ok && !*fail && tc::mbar_wait(&bars[b], par, MAX_POLLS);
       const bool all = consumers_all(mine);
@@ -1921,7 +1920,7 @@ cham_tc_colpass2(const __grid_constant__ CUtensorMap tm_k, const __grid_constant
     // ---- phase A: split each state half tile in place
     for (int h = 0; h < NH && ok; ++h) {
       const int s = h % 3;
-      if (!cwait(B2_FULL + s, nfull[s]++ & 1)) break;
+      if (!cwait(B2_FULL + s, (h / 3) & 1)) break;
       unsigned char* w = slot(s);
       if (patch_w) zero_bad_rows(w, 1);
       float x[2][8];
@@ -2021,12 +2020,11 @@ cham_tc_colpass2(const __grid_constant__ CUtensorMap tm_k, const __grid_constant
       for (int t = 0; t < 8; ++t) atomicAdd(Eo + t, make_float4(e[4 * t], e[4 * t + 1], e[4 * t + 2], e[4 * t + 3]));
     }
     // ---- phase B: S_next = S + dH in the slot (thread: one row of one plane), TMA store
-    uint32_t nsf[2] = {0, 0};
     for (int kt = 0; kt < NT && ok; ++kt) {
       const int s = (kt + 1) & 1, d = kt & 1;
       unsigned char* w = slot(s);
       if (patch_w) {
-        if (!cwait(B2_FULL + s, nfull[s]++ & 1)) break;
+        if (!cwait(B2_FULL + s, ((NH + 2 - s) / 3 + (kt >> 1)) & 1)) break;
         zero_bad_rows(w, 2);
         tc::fence_proxy_async();
         tc::named_sync(1, CONS);
@@ -2051,7 +2049,7 @@ cham_tc_colpass2(const __grid_constant__ CUtensorMap tm_k, const __grid_constant
           *reinterpret_cast<float4*>(box + row * 128 + ((cc ^ (row & 7)) << 4)) = make_float4(v4[0], v4[1], v4[2], v4[3]);
         }
       } else {
-        if (!cwait(B2_SF + s, nsf[s]++ & 1)) break;
+        if (!cwait(B2_SF + s, (kt >> 1) & 1)) break;
 #pragma unroll
         for (int cc = 0; cc < 8; ++cc) {
           float4* p4 = reinterpret_cast<float4*>(box + row * 128 + ((cc ^ (row & 7)) << 4));
@@ -2176,7 +2174,6 @@ cham_tc_colpass3(const __grid_constant__ CUtensorMap tm_k, const __grid_constant
       };
       constexpr uint32_t ID_H = tc::idesc_bf16(64, N3, true, true);
       constexpr uint32_t ID_Z = tc::idesc_bf16(128, N3, false, true);
-      uint32_t ndh[2] = {0, 0}, nmd[2] = {0, 0};
       auto do_dh = [&](int i) {   // dH[i & 1] = W_{c-1} rows of tile i x Cm_{c-1}
         const int s = i & 1, d = i & 1;
         if (!pwait(B3_FULL + s, (i >> 1) & 1)) return false;
@@ -2194,7 +2191,6 @@ cham_tc_colpass3(const __grid_constant__ CUtensorMap tm_k, const __grid_constant
           tc::mma_bf16(tDH + 128 * d, a, tc::sdesc(cl + ks * 2 * (N3 / 8) * 128, (N3 / 8) * 128, 128), ID_H, 1u);
         }
         tc::commit(&bars[B3_DH + d]);
-        ++ndh[d];
         return true;
       };
       if (has_prev) {
@@ -2225,8 +2221,7 @@ cham_tc_colpass3(const __grid_constant__ CUtensorMap tm_k, const __grid_constant
             tc::mma_bf16(tZ, a, tc::sdesc(bl + ks * 2 * (N3 / 8) * 128, (N3 / 8) * 128, 128), ID_Z, 1u);
           }
           tc::commit(&bars[B3_MD + s]);
-          ++nmd[s];
-          if (!pwait(B3_MD + s, (nmd[s] - 1) & 1)) break;
+          if (!pwait(B3_MD + s, (i >> 1) & 1)) break;
         }
         if (i + 2 < NH) issue(i + 2);
       }
