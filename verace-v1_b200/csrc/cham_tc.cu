@@ -123,6 +123,8 @@ __device__ __forceinline__ void stage8(const T* src, bool valid, unsigned char* 
 // the k vector for r < 64 and the v vector for r >= 64 (so that k and v rows each form
 // one contiguous 64-row block, the shape a TMA box delivers).  T, Z, Cm and E use it too.
 __device__ __forceinline__ int tok(int r) { return r & (C2 - 1); }
+// split-order row r (k block 0..63, v block 64..127) -> interleaved row 2 * token + kv
+__device__ __forceinline__ int ilv(int r) { return 2 * (r & (C2 - 1)) + (r >> 6); }
 __device__ __forceinline__ bool is_v(int r) { return r >= C2; }
 
 // Stage the chunk's k/v vectors, elements [i0, i0+KT), as a K-major tile with rows = r.
@@ -1518,17 +1520,19 @@ readout2_body(const CUtensorMap& tm_k, const CUtensorMap& tm_v, const CUtensorMa
 // prep for bf16 inputs: the Gram matrix G = W Wᵀ on the tensor cores (W tiles by TMA in
 // the kernels' row order, k block then v block; bf16 inputs are exact, so one product),
 // then N_t, T by block forward substitution (fp32 SIMT) directly in that row order.
-// smem: Gs [128][129] fp32 | W stages (2 x 32K, 1024-aligned) aliased later by Tr | Ti
-constexpr int PW_TR = 67584, PW_TI = PW_TR + R2 * (R2 + 1) * 4;
-constexpr int PREP_WS_ACC = PW_TI + R2 * (R2 + 1) * 4;
-constexpr int PREP_WS_SMEM = PREP_WS_ACC + 2 * 16 * R2 * 4;
+// smem: Gs [128][132] fp32 | W stages (2 x 32K, 1024-aligned) aliased later by Tr | Ti
+constexpr int PW_P = 132;   // row pitch of Gs / Tr / Ti in floats (a multiple of 4: float4 rows)
+constexpr int PW_TR = 67584, PW_TI = PW_TR + R2 * PW_P * 4;
+constexpr int PREP_WS_END = PW_TI + R2 * PW_P * 4;
+static_assert(R2 * PW_P * 4 <= PW_TR, "Gs overlaps the W stages");
+constexpr int PREP_WS_SMEM = PREP_WS_END;
 
 __global__ void __launch_bounds__(THR, 1)
 cham_tc_prep_ws(const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
                 const float* __restrict__ gamma, unsigned char* __restrict__ Tws, float* __restrict__ Ews,
                 unsigned long long* __restrict__ badws, int S, int D, int nch) {
   extern __shared__ __align__(1024) unsigned char smp[];
-  constexpr int P = R2 + 1;
+  constexpr int P = PW_P;
   float* Gs = reinterpret_cast<float*>(smp);
   float* Tr = reinterpret_cast<float*>(smp + PW_TR);
   float* Ti = reinterpret_cast<float*>(smp + PW_TI);
@@ -1536,7 +1540,6 @@ cham_tc_prep_ws(const __grid_constant__ CUtensorMap tm_k, const __grid_constant_
   __shared__ float Ns[C2 * 8];
   __shared__ unsigned long long bad_bits;
   __shared__ __align__(8) uint64_t bars[5];   // tfull[2], mdone[2], done
-  float* acc = reinterpret_cast<float*>(smp + PREP_WS_ACC);
   __shared__ uint32_t tslot;
   __shared__ int pfail;
   const int c = blockIdx.x, item = blockIdx.y, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -1591,15 +1594,17 @@ cham_tc_prep_ws(const __grid_constant__ CUtensorMap tm_k, const __grid_constant_
     if (tid == 0) record_timeout();
   } else {
     tc::fence_after_sync();
-    {  // G -> Gs: thread = row (TMEM lane), 64 columns per warp half
+    {  // G -> Gs in the solver's interleaved order (row 2t + kv): thread = TMEM lane
+       // (split-order row), 64 columns per warp half (the k half or the v half)
       const uint32_t lane_base = (uint32_t)(32 * (warp & 3)) << 16;
       const int row = 32 * (warp & 3) + lane, half = warp >> 2;
+      float* grow = Gs + ilv(row) * P + half;
 #pragma unroll
       for (int u = 0; u < 4; ++u) {
         float x[16];
         tc::tmem_ld16(tG + lane_base + 64 * half + 16 * u, x);
 #pragma unroll
-        for (int jj = 0; jj < 16; ++jj) Gs[row * P + 64 * half + 16 * u + jj] = x[jj];
+        for (int jj = 0; jj < 16; ++jj) grow[2 * (16 * u + jj)] = x[jj];
       }
     }
     tc::fence_before_sync();
@@ -1609,9 +1614,9 @@ cham_tc_prep_ws(const __grid_constant__ CUtensorMap tm_k, const __grid_constant_
       float n00r = 0.f, n00i = 0.f, n01r = 0.f, n01i = 0.f, n11r = 0.f, n11i = 0.f;
       bool flagged = false;
       if (tau < nt) {
-        const float kk = Gs[tau * P + tau];
-        const float vv = Gs[(C2 + tau) * P + C2 + tau];
-        const float kv = Gs[tau * P + C2 + tau];
+        const float kk = Gs[(2 * tau) * P + 2 * tau];
+        const float vv = Gs[(2 * tau + 1) * P + 2 * tau + 1];
+        const float kv = Gs[(2 * tau) * P + 2 * tau + 1];
         const float g = gamma[(size_t)item * S + t0 + tau];
         const float cc = 0.5f * g;
         const float dr = 1.f + cc * cc * (kk * vv - kv * kv);
@@ -1637,18 +1642,20 @@ cham_tc_prep_ws(const __grid_constant__ CUtensorMap tm_k, const __grid_constant_
     if (bad_bits) {   // clear the Gram rows/columns of non-finite tokens
       for (int e = tid; e < R2 * R2; e += THR) {
         const int r = e / R2, cl = e % R2;
-        if (((bad_bits >> tok(r)) & 1ull) || ((bad_bits >> tok(cl)) & 1ull)) Gs[r * P + cl] = 0.f;
+        if (((bad_bits >> (r >> 1)) & 1ull) || ((bad_bits >> (cl >> 1)) & 1ull)) Gs[r * P + cl] = 0.f;
       }
       __syncthreads();
     }
-    wy_solve<true>(Gs, P, Ns, Tr, Ti, acc, [](int t, int kv) { return kv * C2 + t; }, tid);
+    wy_solve<true>(Gs, P, Ns, Tr, Ti, tid);
     const size_t chunk = (size_t)item * nch + c;
     unsigned char* To = Tws + chunk * 4 * T_TILE;
     for (int e = tid; e < R2 * (R2 / 8); e += THR) {
       const int r = e % R2, g = e / R2;
+      // T in the kernels' split order: element (r, c) is the solver's (ilv(r), ilv(c))
       float xr[8], xi[8];
+      const int ro = ilv(r) * P, c0 = ilv(g * 8);
 #pragma unroll
-      for (int j = 0; j < 8; ++j) { xr[j] = Tr[r * P + g * 8 + j]; xi[j] = Ti[r * P + g * 8 + j]; }
+      for (int j = 0; j < 8; ++j) { xr[j] = Tr[ro + c0 + 2 * j]; xi[j] = Ti[ro + c0 + 2 * j]; }
       uint4 h, l;
       const int off = kmaj(r, g * 8, R2);
       tc::split8(xr, h, l);

@@ -55,15 +55,16 @@ __device__ __forceinline__ void stage8_3(const T* src, bool valid, unsigned char
 
 // ---------------------------------------------------------------------------------
 // prep: Gram, M_t, T (fp32 SIMT), T written as bf16 hi/lo K-major 128x128 tiles.
-// smem: Ws [128][129] | Gs [128][129] | Ts [128][129]
+// smem: Ws [128][129] | Gs [128][132] | Ts [128][132] (row pitch a multiple of 4: the
+// solver reads G rows as float4)
 template <typename T>
-__global__ void __launch_bounds__(THR3)
+__global__ void __launch_bounds__(THR3, 1)
 sssd_tc_prep(const T* __restrict__ k, const T* __restrict__ v, const float* __restrict__ delta,
              unsigned char* __restrict__ Tws, unsigned long long* __restrict__ badws, int S, int H, int nch) {
   extern __shared__ float sm3[];
-  constexpr int P = R3 + 1;
+  constexpr int PW = R3 + 1, P = 132;
   float* Ws = sm3;
-  float* Gs = Ws + HD * P;
+  float* Gs = Ws + HD * PW;
   float* Ts = Gs + R3 * P;
   __shared__ float Ms[C3 * 8];   // per token [[m00, m01], [m10, m11]] as complex with zero imaginary parts
   __shared__ unsigned long long bad_bits;
@@ -140,7 +141,9 @@ sssd_tc_prep(const T* __restrict__ k, const T* __restrict__ v, const float* __re
         float x[16];
         tc::tmem_ld16(tG + lb + 64 * half + 16 * u, x);
 #pragma unroll
-        for (int jj = 0; jj < 16; ++jj) Gs[row * P + 64 * half + 16 * u + jj] = x[jj];
+        for (int jj = 0; jj < 16; jj += 4)
+          *reinterpret_cast<float4*>(Gs + row * P + 64 * half + 16 * u + jj) =
+              make_float4(x[jj], x[jj + 1], x[jj + 2], x[jj + 3]);
       }
     }
     tc::fence_before_sync();
@@ -178,7 +181,7 @@ sssd_tc_prep(const T* __restrict__ k, const T* __restrict__ v, const float* __re
       bool fin = true;
 #pragma unroll
       for (int jj = 0; jj < 8; ++jj) {
-        Ws[(g * 8 + jj) * P + r] = x[u][jj];
+        Ws[(g * 8 + jj) * PW + r] = x[u][jj];
         fin = fin && isfinite(x[u][jj]);
       }
       if (!fin) atomicOr(&bad_bits, 1ull << (r >> 1));
@@ -189,10 +192,10 @@ sssd_tc_prep(const T* __restrict__ k, const T* __restrict__ v, const float* __re
   __syncthreads();
   if (bad_bits) {
     for (int e = tid; e < HD * R3; e += THR3)
-      if ((bad_bits >> ((e % R3) >> 1)) & 1ull) Ws[(e / R3) * P + e % R3] = 0.f;
+      if ((bad_bits >> ((e % R3) >> 1)) & 1ull) Ws[(e / R3) * PW + e % R3] = 0.f;
     __syncthreads();
   }
-  smem_gemm<4, 4, false>(R3, R3, HD, Ws, 1, P, Ws, P, 1, Gs, P, 1, tid, THR3);
+  smem_gemm<4, 4, false>(R3, R3, HD, Ws, 1, PW, Ws, PW, 1, Gs, P, 1, tid, THR3);
   __syncthreads();
   }
   if (tid < C3) {
@@ -225,15 +228,14 @@ sssd_tc_prep(const T* __restrict__ k, const T* __restrict__ v, const float* __re
     n[0] = m00; n[1] = 0.f; n[2] = m01; n[3] = 0.f; n[4] = m10; n[5] = 0.f; n[6] = m11; n[7] = 0.f;
   }
   __syncthreads();
-  // Ws is dead once G is formed: it holds the solver's scratch
-  wy_solve<false>(Gs, P, Ms, Ts, nullptr, Ws, [](int t, int kv) { return 2 * t + kv; }, tid);
+  wy_solve<false>(Gs, P, Ms, Ts, nullptr, tid);
   const size_t chunk = (size_t)chain * nch + c;
   unsigned char* To = Tws + chunk * 2 * TILE3;
   for (int e = tid; e < R3 * (R3 / 8); e += THR3) {
     const int r = e % R3, g = e / R3;
-    float x[8];
-#pragma unroll
-    for (int j = 0; j < 8; ++j) x[j] = Ts[r * P + g * 8 + j];
+    const float4 a = *reinterpret_cast<const float4*>(Ts + r * P + g * 8);
+    const float4 b = *reinterpret_cast<const float4*>(Ts + r * P + g * 8 + 4);
+    float x[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
     uint4 h, l;
     tc::split8(x, h, l);
     *reinterpret_cast<uint4*>(To + kmaj3(r, g * 8, R3)) = h;
@@ -501,7 +503,7 @@ sssd_tc_scan(const T* __restrict__ q, const T* __restrict__ k, const T* __restri
   if (warp == 0) tc::tmem_dealloc(tb, 512);
 }
 
-size_t sssd_tc_prep_smem() { return sizeof(float) * (HD * (R3 + 1) + 2 * R3 * (R3 + 1)); }
+size_t sssd_tc_prep_smem() { return sizeof(float) * (HD * (R3 + 1) + 2 * R3 * 132); }
 
 template <typename T>
 int launch_sssd_tc(const void* q, const void* k, const void* v, const float* delta, const float* psi0,

@@ -1,99 +1,184 @@
-// Coefficient matrix of a chunk's compact-WY product, by block forward substitution.
+// Coefficient matrix of a chunk's compact-WY product, by recursive block inversion.
 //
 // For a chunk of 64 tokens whose factors are I + U_t N_t U_tᵀ (U_t = [k_t, v_t]), the
 // product is I + W T Wᵀ with
 //     T = (I - Nblk L)^-1 Nblk,   i.e.  T_t = N_t (e_t + sum_{tau < t} G_{t,tau} T_tau)
-// where G = WᵀW (real) and T_t is the 2-row block of token t.  Rows and columns are
-// addressed through row(t, kv) (kv = 0: k, 1: v), so callers may use any row order.
+// where G = WᵀW (real, symmetric), L its strictly block-lower part and T_t the 2-row
+// block of token t.  Rows are interleaved: row 2t + kv holds token t's k (kv = 0) or
+// v (kv = 1), so a run of tokens is a run of rows.
 //
-// The tokens are processed in 8 groups of 8.  For each group, the contribution of all
-// earlier groups, ACC = sum_{tau in earlier groups} G_{t,tau} T_tau, is one small matrix
-// product spread over all 256 threads; the 8-token recurrence inside the group then
-// runs with one thread per column.  This replaces a 64-step dependent chain per column
-// by 8 short ones.  Entries of T above the diagonal blocks come out exactly zero.
+// Splitting the tokens of any run into a first half a and a second half b,
+//     T = [[T_aa, 0], [T_bb G_ba T_aa, T_bb]],
+// where T_aa and T_bb are the same matrices for the halves on their own.  So T is built
+// bottom-up: the 8 diagonal blocks of 8 tokens (16 rows) by forward substitution, one
+// thread per column with the column in registers; then three levels that join pairs of
+// 16-, 32- and 64-row blocks with two register-tiled products each,
+//     X = G_ba T_aa   (written where T_ba goes: nothing reads that block yet)
+//     T_ba = T_bb X   (every thread holds its 4 x 4 tile before any is stored).
+// Entries above the diagonal blocks are exactly zero.  All arithmetic is fp32.
 #pragma once
 
 namespace verace {
 
 constexpr int WY_C = 64;     // tokens per chunk
 constexpr int WY_R = 128;    // rows of T
-constexpr int WY_GS = 8;     // tokens per group
 
-// G: [128][P] fp32 Gram matrix; N8: [64][8] per-token 2x2 complex blocks
-// (m00r, m00i, m01r, m01i, m10r, m10i, m11r, m11i); Tr/Ti: [128][P] outputs (Ti unused
-// when !CPLX); acc: scratch of 2 * 16 * 128 floats.  Must be called by all 256 threads.
-template <bool CPLX, typename Row>
-__device__ __forceinline__ void wy_solve(const float* __restrict__ G, int P, const float* __restrict__ N8,
-                                         float* __restrict__ Tr, float* __restrict__ Ti, float* __restrict__ acc,
-                                         Row row, int tid) {
-  float* accr = acc;
-  float* acci = acc + 2 * WY_GS * WY_R;
-  const int col = tid % WY_R, rh = tid / WY_R;   // rh: which 8 of the group's 16 rows
-  for (int g = 0; g < WY_C / WY_GS; ++g) {
-    {
-      float ar[8], ai[8];
-      int grow[8];
+namespace wy {
+
+__device__ __forceinline__ void fma44(float (&c)[4][4], const float4 (&a)[4], const float4 (&b)[4], float sgn) {
 #pragma unroll
-      for (int u = 0; u < 8; ++u) {
-        const int i16 = rh * 8 + u;
-        grow[u] = row(g * WY_GS + (i16 >> 1), i16 & 1) * P;
-        ar[u] = 0.f;
-        ai[u] = 0.f;
-      }
-      for (int tp = 0; tp < g * WY_GS; ++tp) {
+  for (int i = 0; i < 4; ++i) {
+    const float av[4] = {sgn * a[i].x, sgn * a[i].y, sgn * a[i].z, sgn * a[i].w};
 #pragma unroll
-        for (int kv = 0; kv < 2; ++kv) {
-          const int rr = row(tp, kv);
-          const float xr = Tr[rr * P + col];
-          const float xi = CPLX ? Ti[rr * P + col] : 0.f;
-#pragma unroll
-          for (int u = 0; u < 8; ++u) {
-            const float gg = G[grow[u] + rr];
-            ar[u] = fmaf(gg, xr, ar[u]);
-            if (CPLX) ai[u] = fmaf(gg, xi, ai[u]);
-          }
-        }
-      }
-#pragma unroll
-      for (int u = 0; u < 8; ++u) {
-        accr[(rh * 8 + u) * WY_R + col] = ar[u];
-        if (CPLX) acci[(rh * 8 + u) * WY_R + col] = ai[u];
-      }
+    for (int k = 0; k < 4; ++k) {
+      c[i][0] = fmaf(av[k], b[k].x, c[i][0]);
+      c[i][1] = fmaf(av[k], b[k].y, c[i][1]);
+      c[i][2] = fmaf(av[k], b[k].z, c[i][2]);
+      c[i][3] = fmaf(av[k], b[k].w, c[i][3]);
     }
-    __syncthreads();
-    if (tid < WY_R) {
-      for (int tt = 0; tt < WY_GS; ++tt) {
-        const int t = g * WY_GS + tt;
-        const int r0 = row(t, 0), r1 = row(t, 1);
-        float x0r = accr[(2 * tt) * WY_R + col] + (r0 == col ? 1.f : 0.f);
-        float x1r = accr[(2 * tt + 1) * WY_R + col] + (r1 == col ? 1.f : 0.f);
-        float x0i = CPLX ? acci[(2 * tt) * WY_R + col] : 0.f;
-        float x1i = CPLX ? acci[(2 * tt + 1) * WY_R + col] : 0.f;
-        for (int tp = g * WY_GS; tp < t; ++tp) {
-          const int q0 = row(tp, 0), q1 = row(tp, 1);
-          const float a0r = Tr[q0 * P + col], a1r = Tr[q1 * P + col];
-          const float a0i = CPLX ? Ti[q0 * P + col] : 0.f, a1i = CPLX ? Ti[q1 * P + col] : 0.f;
-          const float g00 = G[r0 * P + q0], g01 = G[r0 * P + q1];
-          const float g10 = G[r1 * P + q0], g11 = G[r1 * P + q1];
-          x0r += g00 * a0r + g01 * a1r;
-          x1r += g10 * a0r + g11 * a1r;
-          if (CPLX) {
-            x0i += g00 * a0i + g01 * a1i;
-            x1i += g10 * a0i + g11 * a1i;
-          }
-        }
-        const float* n = N8 + t * 8;
-        // [T_r0; T_r1] = [[m00, m01], [m10, m11]] [x0; x1]  (complex)
-        Tr[r0 * P + col] = n[0] * x0r - n[1] * x0i + n[2] * x1r - n[3] * x1i;
-        Tr[r1 * P + col] = n[4] * x0r - n[5] * x0i + n[6] * x1r - n[7] * x1i;
-        if (CPLX) {
-          Ti[r0 * P + col] = n[0] * x0i + n[1] * x0r + n[2] * x1i + n[3] * x1r;
-          Ti[r1 * P + col] = n[4] * x0i + n[5] * x0r + n[6] * x1i + n[7] * x1r;
-        }
-      }
-    }
-    __syncthreads();
   }
+}
+
+__device__ __forceinline__ void ld4(float4 (&x)[4], const float* p, int P) {
+#pragma unroll
+  for (int i = 0; i < 4; ++i) x[i] = *reinterpret_cast<const float4*>(p + i * P);
+}
+
+__device__ __forceinline__ void st44(float* p, int P, const float (&c)[4][4]) {
+#pragma unroll
+  for (int i = 0; i < 4; ++i) *reinterpret_cast<float4*>(p + i * P) = make_float4(c[i][0], c[i][1], c[i][2], c[i][3]);
+}
+
+__device__ __forceinline__ void zero44(float (&c)[4][4]) {
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) c[i][j] = 0.f;
+}
+
+// One join level: blocks of B rows, pairs (a, b) = rows [2pB, 2pB + B), [2pB + B, 2pB + 2B).
+template <int B, bool CPLX>
+__device__ __forceinline__ void join_level(const float* __restrict__ G, int P, float* __restrict__ Tr,
+                                           float* __restrict__ Ti, int tid) {
+  constexpr int TPB = B / 4;                  // tiles per block side
+  constexpr int TILES = (WY_R / (2 * B)) * TPB * TPB;
+  const bool act = tid < TILES;
+  const int pair = tid / (TPB * TPB), tt = tid % (TPB * TPB), tm = tt / TPB, tn = tt % TPB;
+  const int a0 = 2 * B * pair, b0 = a0 + B;
+  const int row = b0 + 4 * tm, col = a0 + 4 * tn;
+  float cr[4][4], ci[4][4];
+  // X = G_ba T_aa
+  if (act) {
+    zero44(cr);
+    if (CPLX) zero44(ci);
+    const float* ga = G + row * P + a0;
+    const float* tr = Tr + a0 * P + col;
+    const float* ti = CPLX ? Ti + a0 * P + col : nullptr;
+#pragma unroll 4
+    for (int k = 0; k < B; k += 4) {
+      float4 a[4], b[4];
+      ld4(a, ga + k, P);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) b[j] = *reinterpret_cast<const float4*>(tr + (k + j) * P);
+      fma44(cr, a, b, 1.f);
+      if (CPLX) {
+#pragma unroll
+        for (int j = 0; j < 4; ++j) b[j] = *reinterpret_cast<const float4*>(ti + (k + j) * P);
+        fma44(ci, a, b, 1.f);
+      }
+    }
+    st44(Tr + row * P + col, P, cr);
+    if (CPLX) st44(Ti + row * P + col, P, ci);
+  }
+  __syncthreads();
+  // T_ba = T_bb X   (complex: (Tr + i Ti)(Xr + i Xi))
+  if (act) {
+    zero44(cr);
+    if (CPLX) zero44(ci);
+    const float* ar = Tr + row * P + b0;
+    const float* ai = CPLX ? Ti + row * P + b0 : nullptr;
+    const float* xr = Tr + b0 * P + col;
+    const float* xi = CPLX ? Ti + b0 * P + col : nullptr;
+#pragma unroll 2
+    for (int k = 0; k < B; k += 4) {
+      float4 a[4], b[4];
+      ld4(a, ar + k, P);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) b[j] = *reinterpret_cast<const float4*>(xr + (k + j) * P);
+      fma44(cr, a, b, 1.f);
+      if (CPLX) {
+        float4 a2[4], b2[4];
+        ld4(a2, ai + k, P);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) b2[j] = *reinterpret_cast<const float4*>(xi + (k + j) * P);
+        fma44(cr, a2, b2, -1.f);
+        fma44(ci, a, b2, 1.f);
+        fma44(ci, a2, b, 1.f);
+      }
+    }
+  }
+  __syncthreads();
+  if (act) {
+    st44(Tr + row * P + col, P, cr);
+    if (CPLX) st44(Ti + row * P + col, P, ci);
+  }
+  __syncthreads();
+}
+
+}  // namespace wy
+
+// G: [128][P] fp32 Gram matrix in the interleaved row order, P a multiple of 4 and every
+// array 16-byte aligned; N8: [64][8] per-token 2x2 complex blocks
+// (m00r, m00i, m01r, m01i, m10r, m10i, m11r, m11i); Tr/Ti: [128][P] outputs (Ti unused
+// when !CPLX).  Must be called by all 256 threads of the CTA; ends with a barrier.
+template <bool CPLX>
+__device__ __forceinline__ void wy_solve(const float* __restrict__ G, int P, const float* __restrict__ N8,
+                                         float* __restrict__ Tr, float* __restrict__ Ti, int tid) {
+  // zero T (the blocks above the diagonal stay zero)
+  for (int e = tid; e < WY_R * (WY_R / 4); e += 256) {
+    const int r = e / (WY_R / 4), c4 = e % (WY_R / 4);
+    *reinterpret_cast<float4*>(Tr + r * P + 4 * c4) = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (CPLX) *reinterpret_cast<float4*>(Ti + r * P + 4 * c4) = make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+  __syncthreads();
+  // diagonal blocks: leaf j = tokens [8j, 8j + 8) = rows [16j, 16j + 16); thread = one
+  // of the leaf's 16 columns, the column kept in registers
+  if (tid < 128) {
+    const int j = tid >> 4, c = tid & 15, r0 = 16 * j;
+    const float* Gl = G + r0 * P + r0;
+    float xr[16], xi[16];
+#pragma unroll
+    for (int t = 0; t < 8; ++t) {
+      float a0r = (2 * t == c) ? 1.f : 0.f, a1r = (2 * t + 1 == c) ? 1.f : 0.f;
+      float a0i = 0.f, a1i = 0.f;
+#pragma unroll
+      for (int tp = 0; tp < t; ++tp) {
+        const float2 g0 = *reinterpret_cast<const float2*>(Gl + (2 * t) * P + 2 * tp);
+        const float2 g1 = *reinterpret_cast<const float2*>(Gl + (2 * t + 1) * P + 2 * tp);
+        a0r += g0.x * xr[2 * tp] + g0.y * xr[2 * tp + 1];
+        a1r += g1.x * xr[2 * tp] + g1.y * xr[2 * tp + 1];
+        if (CPLX) {
+          a0i += g0.x * xi[2 * tp] + g0.y * xi[2 * tp + 1];
+          a1i += g1.x * xi[2 * tp] + g1.y * xi[2 * tp + 1];
+        }
+      }
+      const float* n = N8 + (8 * j + t) * 8;
+      // [T_r0; T_r1] = [[m00, m01], [m10, m11]] [a0; a1]  (complex)
+      xr[2 * t] = n[0] * a0r - n[1] * a0i + n[2] * a1r - n[3] * a1i;
+      xr[2 * t + 1] = n[4] * a0r - n[5] * a0i + n[6] * a1r - n[7] * a1i;
+      xi[2 * t] = n[0] * a0i + n[1] * a0r + n[2] * a1i + n[3] * a1r;
+      xi[2 * t + 1] = n[4] * a0i + n[5] * a0r + n[6] * a1i + n[7] * a1r;
+    }
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      Tr[(r0 + i) * P + r0 + c] = xr[i];
+      if (CPLX) Ti[(r0 + i) * P + r0 + c] = xi[i];
+    }
+  }
+  __syncthreads();
+  wy::join_level<16, CPLX>(G, P, Tr, Ti, tid);
+  wy::join_level<32, CPLX>(G, P, Tr, Ti, tid);
+  wy::join_level<64, CPLX>(G, P, Tr, Ti, tid);
 }
 
 }  // namespace verace
