@@ -25,9 +25,7 @@
 #include "tc.cuh"
 #include "wy_solve.cuh"
 
-#include <cuda.h>
-#include <cudaTypedefs.h>
-#include <mutex>
+#include "tmap.cuh"
 
 namespace verace {
 namespace {
@@ -2483,20 +2481,6 @@ cham_tc_readout_batch(const __grid_constant__ CUtensorMap tm_k, const __grid_con
                 ((c % ring) * b + item) * D);
 }
 
-// Tensor maps for the warp-specialised colpass (driver entry point resolved once).
-PFN_cuTensorMapEncodeTiled_v12000 tmap_encoder() {
-  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
-  static std::once_flag once;
-  std::call_once(once, [] {
-    void* p = nullptr;
-    cudaDriverEntryPointQueryResult qr;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &qr) == cudaSuccess &&
-        qr == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
-  });
-  return fn;
-}
-
 // k or v as a [b][S][D] bf16 tensor, boxes of 64 elements x 64 tokens with 128-byte swizzle
 // (rows past S read as 0)
 int make_kv_map(CUtensorMap* m, const void* base, int b, int S, int D) {
@@ -2673,20 +2657,20 @@ int launch_cham_tc(const void* q, const void* k, const void* v, const float* gam
     }
     return VERACE_OK;
   }
-  for (int c = 0; c < nch; ++c) {
-    const bool to_out = ((nch - 1 - c) % 2) == 0;
-    float* dr = to_out ? hr : w.Hre;
-    float* di = to_out ? hi : w.Him;
-    {
-      cham_tc_colpass<T><<<gc, THR, CPS, st>>>((const T*)q, (const T*)k, (const T*)v, w.T, w.E, w.bad,
-                                                        cur_r, cur_i, dr, di, s, D, nch, c);
+  if constexpr (!WS) {
+    for (int c = 0; c < nch; ++c) {
+      const bool to_out = ((nch - 1 - c) % 2) == 0;
+      float* dr = to_out ? hr : w.Hre;
+      float* di = to_out ? hi : w.Him;
+      cham_tc_colpass<T><<<gc, THR, CPS, st>>>((const T*)q, (const T*)k, (const T*)v, w.T, w.E, w.bad, cur_r, cur_i,
+                                               dr, di, s, D, nch, c);
       if ((rc = check_launch("cham_tc_colpass"))) return rc;
+      cham_tc_readout<T><<<gr, THR, READOUT_SMEM, st>>>((const T*)q, (const T*)k, (const T*)v, w.E, w.bad, cur_r,
+                                                        (T*)out, s, D, nch, c);
+      if ((rc = check_launch("cham_tc_readout"))) return rc;
+      cur_r = dr;
+      cur_i = di;
     }
-    cham_tc_readout<T><<<gr, THR, READOUT_SMEM, st>>>((const T*)q, (const T*)k, (const T*)v, w.E, w.bad,
-                                                      cur_r, (T*)out, s, D, nch, c);
-    if ((rc = check_launch("cham_tc_readout"))) return rc;
-    cur_r = dr;
-    cur_i = di;
   }
   return VERACE_OK;
 }

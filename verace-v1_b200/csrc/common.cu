@@ -1,7 +1,9 @@
 // Status plumbing of the C ABI: per-host-thread last-error message and version.
 #include "common.cuh"
+#include "tmap.cuh"
 
 #include <atomic>
+#include <mutex>
 #include <stdarg.h>
 #include <stdio.h>
 
@@ -25,6 +27,19 @@ int check_launch(const char* what) {
     return VERACE_ERR_CUDA;
   }
   return VERACE_OK;
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 tmap_encoder() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult qr;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &qr) == cudaSuccess &&
+        qr == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
 }
 
 }  // namespace verace

@@ -17,12 +17,6 @@ namespace {
 
 constexpr int PT = 256;   // threads per CTA
 
-__device__ __forceinline__ float warp_sum32(float x) {
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) x += __shfl_xor_sync(0xffffffffu, x, o);
-  return x;
-}
-
 template <typename T>
 __device__ __forceinline__ void load8v(const T* p, float* x);
 template <>

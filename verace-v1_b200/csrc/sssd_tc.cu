@@ -12,6 +12,7 @@
 // T for every chunk comes from sssd_tc_prep (all chunks in parallel, fp32 SIMT).
 #include "common.cuh"
 #include "tc.cuh"
+#include "tmap.cuh"
 #include "wy_solve.cuh"
 
 namespace verace {
@@ -32,6 +33,10 @@ __device__ __forceinline__ int kmaj3(int r, int k, int R) { return ((k >> 3) * R
 //   MN-major view (n = j, k = i): SBO 2048, LBO 128, K step of 16 -> +256
 __device__ __forceinline__ int xoff(int i, int j) { return kmaj3(i, j, 128); }
 __device__ __forceinline__ int mnmaj3(int k, int n, int NG) { return (((k >> 3) * NG + (n >> 3)) * 128) + (k & 7) * 16 + (n & 7) * 2; }
+// Row orders of a chunk's 128 vectors: interleaved (row 2t + kv: the solver's, and the
+// fp32 scan's) and split (row t for k_t, 64 + t for v_t: the bf16 scan's, whose W tiles
+// arrive as one TMA box of k rows and one of v rows).  ilv3 maps split -> interleaved.
+__device__ __forceinline__ int ilv3(int r) { return 2 * (r & (C3 - 1)) + (r >> 6); }
 
 template <typename T>
 __device__ __forceinline__ void stage8_3(const T* src, bool valid, unsigned char* hi, unsigned char* lo) {
@@ -54,7 +59,8 @@ __device__ __forceinline__ void stage8_3(const T* src, bool valid, unsigned char
 }
 
 // ---------------------------------------------------------------------------------
-// prep: Gram, M_t, T (fp32 SIMT), T written as bf16 hi/lo K-major 128x128 tiles.
+// prep: Gram, M_t, T (fp32 SIMT), T written as bf16 hi/lo K-major 128x128 tiles (split
+// row order for bf16 inputs, interleaved for fp32).
 // smem: Ws [128][129] | Gs [128][132] | Ts [128][132] (row pitch a multiple of 4: the
 // solver reads G rows as float4)
 template <typename T>
@@ -233,9 +239,17 @@ sssd_tc_prep(const T* __restrict__ k, const T* __restrict__ v, const float* __re
   unsigned char* To = Tws + chunk * 2 * TILE3;
   for (int e = tid; e < R3 * (R3 / 8); e += THR3) {
     const int r = e % R3, g = e / R3;
-    const float4 a = *reinterpret_cast<const float4*>(Ts + r * P + g * 8);
-    const float4 b = *reinterpret_cast<const float4*>(Ts + r * P + g * 8 + 4);
-    float x[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+    float x[8];
+    if constexpr (BF) {
+      // the bf16 scan's split row order: element (r, c) is the solver's (ilv3(r), ilv3(c))
+      const float* src = Ts + ilv3(r) * P + ilv3(g * 8);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) x[j] = src[2 * j];
+    } else {
+      const float4 a = *reinterpret_cast<const float4*>(Ts + r * P + g * 8);
+      const float4 b = *reinterpret_cast<const float4*>(Ts + r * P + g * 8 + 4);
+      x[0] = a.x; x[1] = a.y; x[2] = a.z; x[3] = a.w; x[4] = b.x; x[5] = b.y; x[6] = b.z; x[7] = b.w;
+    }
     uint4 h, l;
     tc::split8(x, h, l);
     *reinterpret_cast<uint4*>(To + kmaj3(r, g * 8, R3)) = h;
@@ -503,6 +517,304 @@ sssd_tc_scan(const T* __restrict__ q, const T* __restrict__ k, const T* __restri
   if (warp == 0) tc::tmem_dealloc(tb, 512);
 }
 
+// ---------------------------------------------------------------------------------
+// scan for bf16 inputs, chunk inputs prefetched: W (k rows | v rows) and Q of chunk c + 1
+// arrive by TMA in a second buffer while chunk c runs, and T of chunk c + 1 by one bulk
+// copy as soon as chunk c's Cm product has read T(c).  Rows in the split order; same
+// products as sssd_tc_scan.
+// smem (bytes): W[2] [0, 64K), 128B-swizzled K-major (per 64-element K block 128 rows x
+//   128 B; rows 0-63 k, 64-127 v) | Q[2] [64K, 96K) (per K block 64 token rows x 128 B) |
+//   T hi/lo [96K, 160K) | X hi/lo [160K, 224K): S, Z, Cm as bf16 pairs in the "X" layout,
+//   then E (MN-major hi/lo) | barriers.  O leaves through the chunk's W slot (free once
+//   the O product is done) as [64 tokens][128] bf16 rows, for 16-byte coalesced stores.
+constexpr int Y_W = 0, Y_Q = 64 * 1024, Y_T = 96 * 1024, Y_X = 160 * 1024, Y_BAR = 224 * 1024;
+constexpr int SSSD_TC2_SMEM = Y_BAR + 64;
+constexpr int Q_TILE = 64 * 128 * 2;   // 16 KB bf16 64 x 128
+
+__global__ void __launch_bounds__(THR3, 1)
+sssd_tc_scan_bf16(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
+                  const __grid_constant__ CUtensorMap tm_v, const float* __restrict__ psi0,
+                  __nv_bfloat16* __restrict__ out, float* __restrict__ psi_out,
+                  const unsigned char* __restrict__ Tws, const unsigned long long* __restrict__ badws,
+                  int S, int H, int nch) {
+  extern __shared__ __align__(1024) unsigned char sx[];
+  auto sW = [&](int s) { return sx + Y_W + s * TILE3; };
+  auto sQ = [&](int s) { return sx + Y_Q + s * Q_TILE; };
+  unsigned char* sT = sx + Y_T;
+  unsigned char* sXh = sx + Y_X;
+  unsigned char* sXl = sx + Y_X + TILE3;
+  unsigned char* sEh = sx + Y_X;
+  unsigned char* sEl = sx + Y_X + 16 * 1024;
+  uint64_t* bar = reinterpret_cast<uint64_t*>(sx + Y_BAR);   // [0] MMA, [1 + s] W/Q slot s, [3] T
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(sx + Y_BAR + 32);
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int chain = blockIdx.x, bi = chain / H, hi = chain % H;
+  if (warp == 0) tc::tmem_alloc(tslot, 512);
+  if (tid == 0) {
+    for (int i = 0; i < 4; ++i) tc::mbar_init(&bar[i], 1);
+    tc::fence_mbar_init();
+  }
+  tc::fence_before_sync();
+  __syncthreads();
+  tc::fence_after_sync();
+  const uint32_t tb = *tslot;
+  const uint32_t tS = tb, tZ = tb + 128, tC = tb + 256, tO = tb + 384, tE = tb + 448;
+  const uint32_t lb = (uint32_t)(32 * (warp & 3)) << 16;
+  const int row = 32 * (warp & 3) + lane, half = warp >> 2;
+
+  // chunk j's W and Q into slot j & 1; chunk j's T into the T buffer (thread 0)
+  auto issue_wq = [&](int j) {
+    const int s = j & 1;
+    tc::mbar_expect_tx(&bar[1 + s], TILE3 + Q_TILE);
+#pragma unroll
+    for (int kb = 0; kb < 2; ++kb) {
+      tc::tma_load_4d(sW(s) + kb * 16384, &tm_k, 64 * kb, hi, j * C3, bi, &bar[1 + s]);
+      tc::tma_load_4d(sW(s) + kb * 16384 + 8192, &tm_v, 64 * kb, hi, j * C3, bi, &bar[1 + s]);
+      tc::tma_load_4d(sQ(s) + kb * 8192, &tm_q, 64 * kb, hi, j * C3, bi, &bar[1 + s]);
+    }
+  };
+  auto issue_t = [&](int j) {
+    tc::mbar_expect_tx(&bar[3], 2 * TILE3);
+    tc::bulk_load(sT, Tws + ((size_t)chain * nch + j) * 2 * TILE3, 2 * TILE3, &bar[3]);
+  };
+  int wq_issued = min(nch, 2), wq_done = 0, t_issued = nch > 0 ? 1 : 0, t_done = 0;
+  if (tid == 0 && nch > 0) {
+    issue_wq(0);
+    if (nch > 1) issue_wq(1);
+    issue_t(0);
+  }
+
+  uint32_t phase = 0;
+  bool failed = false;
+  auto wait_all = [&](uint64_t* b, uint32_t parity) -> bool {
+    const bool ok = tc::mbar_wait(b, parity, POLLS3);
+    if (__syncthreads_or(!ok)) {
+      if (tid == 0) atomicExch(&g_sssd_tc_status, 1);
+      return false;
+    }
+    tc::fence_after_sync();
+    return true;
+  };
+  auto wait_mma = [&]() -> bool {
+    const bool ok = wait_all(&bar[0], phase);
+    phase ^= 1u;
+    return ok;
+  };
+  // this thread's 64 columns [64*half, 64*half+64) of a 128-column TMEM matrix -> X layout
+  auto tmem_to_x = [&](uint32_t tm) {
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      float x[16];
+      tc::tmem_ld16(tm + lb + 64 * half + 16 * u, x);
+#pragma unroll
+      for (int g = 0; g < 2; ++g) {
+        uint4 h, l;
+        tc::split8(x + 8 * g, h, l);
+        const int off = xoff(row, 64 * half + 16 * u + 8 * g);
+        *reinterpret_cast<uint4*>(sXh + off) = h;
+        *reinterpret_cast<uint4*>(sXl + off) = l;
+      }
+    }
+  };
+  auto sync_for_mma = [&]() {
+    tc::fence_proxy_async();
+    tc::fence_before_sync();
+    __syncthreads();
+  };
+
+  {  // initial state into TMEM
+    const float* p0 = psi0 ? psi0 + (size_t)chain * HD * HD + (size_t)row * HD : nullptr;
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      float x[16];
+#pragma unroll
+      for (int jj = 0; jj < 16; ++jj) {
+        const int j = 64 * half + 16 * u + jj;
+        x[jj] = p0 ? p0[j] : (row == j ? 1.f : 0.f);
+      }
+      tc::tmem_st16(tS + lb + 64 * half + 16 * u, x);
+    }
+  }
+
+  constexpr uint32_t ID_Z = tc::idesc_bf16(128, 128, false, true);
+  constexpr uint32_t ID_Y = tc::idesc_bf16(128, 64, false, false);
+  constexpr uint32_t ID_C = tc::idesc_bf16(128, 128, false, true);
+  constexpr uint32_t ID_S = tc::idesc_bf16(128, 128, true, true);
+  constexpr uint32_t ID_O = tc::idesc_bf16(128, 64, true, true);
+
+  for (int c = 0; c < nch; ++c) {
+    const int s = c & 1, t0 = c * C3, nt = min(C3, S - t0);
+    const unsigned long long bad = badws[(size_t)chain * nch + c];
+    tmem_to_x(tS);
+    if (!wait_all(&bar[1 + s], (c >> 1) & 1)) { failed = true; break; }
+    wq_done = c + 1;
+    if (bad) {   // zero the k and v rows of non-finite tokens (both K blocks)
+      for (int e = tid; e < C3 * 32; e += THR3) {
+        const int tau = e >> 5, kv = (e >> 4) & 1, kb = (e >> 3) & 1, ch = e & 7;
+        if ((bad >> tau) & 1ull)
+          *reinterpret_cast<uint4*>(sW(s) + kb * 16384 + (kv * C3 + tau) * 128 + ch * 16) = make_uint4(0, 0, 0, 0);
+      }
+    }
+    sync_for_mma();
+    // ---- Z = Wᵀ S  and  Y = S Q
+    if (tid == 0) {
+      tc::fence_after_sync();
+      const uint32_t w = tc::smem_addr(sW(s)), q = tc::smem_addr(sQ(s));
+      const uint32_t xh = tc::smem_addr(sXh), xl = tc::smem_addr(sXl);
+#pragma unroll 1
+      for (int ks = 0; ks < 8; ++ks) {
+        const uint64_t a_w = tc::sdesc_sw128(w + (ks >> 2) * 16384 + (ks & 3) * 32, 16, 1024);
+        tc::mma_bf16(tZ, a_w, tc::sdesc(xh + ks * 256, 128, 2048), ID_Z, ks > 0 ? 1u : 0u);
+        tc::mma_bf16(tZ, a_w, tc::sdesc(xl + ks * 256, 128, 2048), ID_Z, 1u);
+        const uint64_t b_q = tc::sdesc_sw128(q + (ks >> 2) * 8192 + (ks & 3) * 32, 16, 1024);
+        tc::mma_bf16(tO, tc::sdesc(xh + ks * 4096, 2048, 128), b_q, ID_Y, ks > 0 ? 1u : 0u);
+        tc::mma_bf16(tO, tc::sdesc(xl + ks * 4096, 2048, 128), b_q, ID_Y, 1u);
+      }
+      tc::commit(&bar[0]);
+    }
+    if (!wait_mma()) { failed = true; break; }
+    // ---- Cm = T Z
+    tmem_to_x(tZ);
+    sync_for_mma();
+    if (!wait_all(&bar[3], c & 1)) { failed = true; break; }
+    t_done = c + 1;
+    if (tid == 0) {
+      const uint32_t th = tc::smem_addr(sT), tl = th + TILE3;
+      const uint32_t xh = tc::smem_addr(sXh), xl = tc::smem_addr(sXl);
+#pragma unroll 1
+      for (int ks = 0; ks < 8; ++ks) {
+        const uint64_t ah = tc::sdesc(th + ks * 4096, 2048, 128);
+        const uint64_t al = tc::sdesc(tl + ks * 4096, 2048, 128);
+        const uint64_t bh = tc::sdesc(xh + ks * 256, 128, 2048);
+        const uint64_t bl = tc::sdesc(xl + ks * 256, 128, 2048);
+        tc::mma_bf16(tC, ah, bh, ID_C, ks > 0 ? 1u : 0u);
+        tc::mma_bf16(tC, ah, bl, ID_C, 1u);
+        tc::mma_bf16(tC, al, bh, ID_C, 1u);
+      }
+      tc::commit(&bar[0]);
+    }
+    if (!wait_mma()) { failed = true; break; }
+    if (c + 1 < nch) {   // T(c) has been read
+      if (tid == 0) issue_t(c + 1);
+      t_issued = c + 2;
+    }
+    // ---- E = Cm Q ; S += W Cm
+    tmem_to_x(tC);
+    sync_for_mma();
+    if (tid == 0) {
+      tc::fence_after_sync();
+      const uint32_t w = tc::smem_addr(sW(s)), q = tc::smem_addr(sQ(s));
+      const uint32_t xh = tc::smem_addr(sXh), xl = tc::smem_addr(sXl);
+#pragma unroll 1
+      for (int ks = 0; ks < 8; ++ks) {
+        const uint64_t b_q = tc::sdesc_sw128(q + (ks >> 2) * 8192 + (ks & 3) * 32, 16, 1024);
+        tc::mma_bf16(tE, tc::sdesc(xh + ks * 4096, 2048, 128), b_q, ID_Y, ks > 0 ? 1u : 0u);
+        tc::mma_bf16(tE, tc::sdesc(xl + ks * 4096, 2048, 128), b_q, ID_Y, 1u);
+        const uint64_t a_w = tc::sdesc_sw128(w + ks * 2048, 16384, 1024);
+        tc::mma_bf16(tS, a_w, tc::sdesc(xh + ks * 256, 128, 2048), ID_S, 1u);
+        tc::mma_bf16(tS, a_w, tc::sdesc(xl + ks * 256, 128, 2048), ID_S, 1u);
+      }
+      tc::commit(&bar[0]);
+    }
+    if (!wait_mma()) { failed = true; break; }
+    // ---- O = Y + W mask(E); E goes where Cm was
+    {
+      float e[32];
+      tc::tmem_ld16(tE + lb + 32 * half, e);
+      tc::tmem_ld16(tE + lb + 32 * half + 16, e + 16);
+#pragma unroll
+      for (int g = 0; g < 4; ++g) {
+        float x[8];
+#pragma unroll
+        for (int jj = 0; jj < 8; ++jj) {
+          const int t = 32 * half + 8 * g + jj;
+          x[jj] = ((row & (C3 - 1)) <= t) ? e[8 * g + jj] : 0.f;
+        }
+        uint4 h, l;
+        tc::split8(x, h, l);
+        const int off = mnmaj3(row, 32 * half + 8 * g, C3 / 8);
+        *reinterpret_cast<uint4*>(sEh + off) = h;
+        *reinterpret_cast<uint4*>(sEl + off) = l;
+      }
+    }
+    sync_for_mma();
+    if (tid == 0) {
+      tc::fence_after_sync();
+      const uint32_t w = tc::smem_addr(sW(s));
+      const uint32_t eh = tc::smem_addr(sEh), el = tc::smem_addr(sEl);
+#pragma unroll 1
+      for (int ks = 0; ks < 8; ++ks) {
+        const uint64_t a_w = tc::sdesc_sw128(w + ks * 2048, 16384, 1024);
+        tc::mma_bf16(tO, a_w, tc::sdesc(eh + ks * 2048, 1024, 128), ID_O, 1u);
+        tc::mma_bf16(tO, a_w, tc::sdesc(el + ks * 2048, 1024, 128), ID_O, 1u);
+      }
+      tc::commit(&bar[0]);
+    }
+    if (!wait_mma()) { failed = true; break; }
+    // ---- O -> [token][dim] bf16 rows in the W slot -> 16-byte coalesced stores
+    {
+      __nv_bfloat16* stg = reinterpret_cast<__nv_bfloat16*>(sW(s));
+      float o[32];
+      tc::tmem_ld16(tO + lb + 32 * half, o);
+      tc::tmem_ld16(tO + lb + 32 * half + 16, o + 16);
+#pragma unroll
+      for (int u = 0; u < 32; ++u) stg[(32 * half + u) * HD + row] = __float2bfloat16_rn(o[u]);
+      tc::fence_before_sync();
+      __syncthreads();
+      for (int e = tid; e < C3 * (HD / 8); e += THR3) {
+        const int t = e >> 4, part = e & 15;
+        if (t < nt)
+          *reinterpret_cast<uint4*>(out + ((size_t)(bi * (size_t)S + t0 + t) * H + hi) * HD + part * 8) =
+              *reinterpret_cast<const uint4*>(stg + t * HD + part * 8);
+      }
+    }
+    // the slot is free again: chunk c + 2's W and Q go there
+    tc::fence_proxy_async();
+    __syncthreads();
+    if (c + 2 < nch) {
+      if (tid == 0) issue_wq(c + 2);
+      wq_issued = c + 3;
+    }
+  }
+  if (failed) {
+    // let copies still in flight land before the CTA's shared memory is released
+    if (tid == 0) {
+      for (int j = wq_done; j < wq_issued; ++j) tc::mbar_wait(&bar[1 + (j & 1)], (j >> 1) & 1, POLLS3);
+      if (t_done < t_issued) tc::mbar_wait(&bar[3], (t_issued - 1) & 1, POLLS3);
+    }
+  } else {
+    float* po = psi_out + (size_t)chain * HD * HD + (size_t)row * HD;
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      float x[16];
+      tc::tmem_ld16(tS + lb + 64 * half + 16 * u, x);
+#pragma unroll
+      for (int jj = 0; jj < 16; jj += 4)
+        *reinterpret_cast<float4*>(po + 64 * half + 16 * u + jj) = make_float4(x[jj], x[jj + 1], x[jj + 2], x[jj + 3]);
+    }
+  }
+  tc::fence_before_sync();
+  __syncthreads();
+  if (warp == 0) tc::tmem_dealloc(tb, 512);
+}
+
+// q, k or v as a [b][S][H][128] bf16 tensor; boxes of 64 elements x 1 head x 64 tokens with
+// 128-byte swizzle (tokens past S read as 0)
+int make_head_map(CUtensorMap* m, const void* base, int b, int S, int H) {
+  auto enc = tmap_encoder();
+  VERACE_REQUIRE(enc != nullptr, VERACE_ERR_CUDA, "cuTensorMapEncodeTiled is not available");
+  const cuuint64_t dims[4] = {(cuuint64_t)HD, (cuuint64_t)H, (cuuint64_t)S, (cuuint64_t)b};
+  const cuuint64_t strides[3] = {(cuuint64_t)HD * 2, (cuuint64_t)H * HD * 2, (cuuint64_t)S * H * HD * 2};
+  const cuuint32_t box[4] = {64, 1, (cuuint32_t)C3, 1};
+  const cuuint32_t es[4] = {1, 1, 1, 1};
+  CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(base), dims, strides, box, es,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  VERACE_REQUIRE(r == CUDA_SUCCESS, VERACE_ERR_CUDA, "cuTensorMapEncodeTiled (q/k/v heads) failed: %d", (int)r);
+  return VERACE_OK;
+}
+
 size_t sssd_tc_prep_smem() { return sizeof(float) * (HD * (R3 + 1) + 2 * R3 * 132); }
 
 template <typename T>
@@ -518,10 +830,23 @@ int launch_sssd_tc(const void* q, const void* k, const void* v, const float* del
     sssd_tc_prep<T><<<dim3(nch, chains), THR3, ps, st>>>((const T*)k, (const T*)v, delta, Tws, badws, s, h, nch);
     if ((rc = check_launch("sssd_tc_prep"))) return rc;
   }
-  VERACE_CUDA(cudaFuncSetAttribute(sssd_tc_scan<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, SSSD_TC_SMEM));
-  sssd_tc_scan<T><<<chains, THR3, SSSD_TC_SMEM, st>>>((const T*)q, (const T*)k, (const T*)v, psi0, (T*)out,
-                                                     psi_out, Tws, badws, s, h, nch);
-  return check_launch("sssd_tc_scan");
+  if constexpr (sizeof(T) == 2) {
+    // (an empty sequence issues no copies; its maps only need valid extents)
+    const int sm = s > 0 ? s : 1;
+    CUtensorMap mq, mk, mv;
+    if ((rc = make_head_map(&mq, q, b, sm, h)) || (rc = make_head_map(&mk, k, b, sm, h)) ||
+        (rc = make_head_map(&mv, v, b, sm, h)))
+      return rc;
+    VERACE_CUDA(cudaFuncSetAttribute(sssd_tc_scan_bf16, cudaFuncAttributeMaxDynamicSharedMemorySize, SSSD_TC2_SMEM));
+    sssd_tc_scan_bf16<<<chains, THR3, SSSD_TC2_SMEM, st>>>(mq, mk, mv, psi0, (__nv_bfloat16*)out, psi_out, Tws, badws,
+                                                          s, h, nch);
+    return check_launch("sssd_tc_scan_bf16");
+  } else {
+    VERACE_CUDA(cudaFuncSetAttribute(sssd_tc_scan<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, SSSD_TC_SMEM));
+    sssd_tc_scan<T><<<chains, THR3, SSSD_TC_SMEM, st>>>((const T*)q, (const T*)k, (const T*)v, psi0, (T*)out,
+                                                       psi_out, Tws, badws, s, h, nch);
+    return check_launch("sssd_tc_scan");
+  }
 }
 
 }  // namespace

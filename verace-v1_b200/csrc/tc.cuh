@@ -208,6 +208,13 @@ __device__ __forceinline__ void tma_load_3d(void* smem, const void* tmap, int x,
       "l"(tmap), "r"(x), "r"(y), "r"(z), "r"(smem_addr(mbar))
       : "memory");
 }
+__device__ __forceinline__ void tma_load_4d(void* smem, const void* tmap, int x, int y, int z, int w, uint64_t* mbar) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4, %5}], [%6];" ::"r"(
+          smem_addr(smem)),
+      "l"(tmap), "r"(x), "r"(y), "r"(z), "r"(w), "r"(smem_addr(mbar))
+      : "memory");
+}
 // TMA tiled store shared -> global (bulk-group completion), and its group controls.
 __device__ __forceinline__ void tma_store_2d(const void* tmap, int x, int y, const void* smem) {
   asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%1, %2}], [%3];" ::"l"(tmap), "r"(x),
