@@ -8,7 +8,8 @@ stack (hidden 1024, 8 heads x 128, holographic width 1024) over a prefill batch 
 8 sequences x 2048 tokens in bf16 (fp32 recurrent state), random-init weights
 (seed 0), synthetic token embeddings (uniform ids over [0, 32000), seed 0).  One
 step = every layer's h <- h + SSSD(RMSNorm(h)); h <- h + CHAM(RMSNorm(h)), through
-the package's module API (projections on cuBLAS, scans on the sm_100a kernels).
+the package's module API (projections on cuBLAS, scans, RMSNorms and residual adds on the
+sm_100a kernels).
 The M-CMoE FFN and ACDE halting are outside this path; random-init ACDE halts no
 token before layer 12, so every token runs all 12 layers.
 
@@ -142,12 +143,17 @@ def run_ours(args):
 
     cham_events = []
 
-    def step(h, record=False):
-        for L in layers:
-            o, _ = L["sssd"](L["sssd_norm"](h), return_state=True)
-            h = h + o
+    def step(h, record=False, inplace=False):
+        # the residual stream h is updated in place by the fused residual + RMSNorm glue:
+        # h <- h + SSSD(n), n <- RMSNorm(h); h <- h + RMSNorm(CHAM(n)), n <- next pre-norm
+        if not inplace:
+            h = h.clone()
+        n = V.rmsnorm(h, layers[0]["sssd_norm"])
+        for li, L in enumerate(layers):
+            o, _ = L["sssd"](n, return_state=True)
+            n = V.add_rmsnorm(h, o, out_norm=L["cham_norm"])
             cm = L["cham"]
-            q, k, v, g = cm.project(L["cham_norm"](h))
+            q, k, v, g = cm.project(n)
             if record:
                 e0 = torch.cuda.Event(enable_timing=True)
                 e1 = torch.cuda.Event(enable_timing=True)
@@ -156,7 +162,8 @@ def run_ours(args):
             if record:
                 e1.record()
                 cham_events.append((e0, e1))
-            h = h + cm.norm(cm.w_out(rec))
+            nxt = layers[li + 1]["sssd_norm"] if li + 1 < len(layers) else None
+            n = V.add_rmsnorm(h, cm.w_out(rec), y_norm=cm.norm, out_norm=nxt)
         return h
 
     def barrier():
@@ -198,14 +205,14 @@ def run_ours(args):
         x_host = x.cpu().pin_memory()
         out_host = torch.empty_like(x_host).pin_memory()
         for _ in range(max(1, args.warmup // 2)):
-            out_host.copy_(step(x_host.to(dev, non_blocking=True)), non_blocking=True)
+            out_host.copy_(step(x_host.to(dev, non_blocking=True), inplace=True), non_blocking=True)
         barrier()
         e2 = torch.cuda.Event(enable_timing=True)
         e3 = torch.cuda.Event(enable_timing=True)
         e2.record()
         for _ in range(args.steps):
             xd = x_host.to(dev, non_blocking=True)
-            out_host.copy_(step(xd), non_blocking=True)
+            out_host.copy_(step(xd, inplace=True), non_blocking=True)
         e3.record()
         barrier()
         e2e_ms = max_over_ranks(e2.elapsed_time(e3)) / args.steps
@@ -275,31 +282,35 @@ def run_decode(args, layers, embed, V, dev, rank, barrier, max_over_ranks):
     toks = torch.randint(0, c["vocab"], (b, n + args.warmup), generator=gen).to(dev)
     st = V.DecodeState(nl, b, nh, d, D, device=dev)
     with torch.no_grad():
-        x = embed(prompt)
+        x = embed(prompt).contiguous()
+        nrm = V.rmsnorm(x, layers[0]["sssd_norm"])
         for l, L in enumerate(layers):
-            o, psi = L["sssd"](L["sssd_norm"](x), return_state=True)
-            x = x + o
+            o, psi = L["sssd"](nrm, return_state=True)
+            nrm = V.add_rmsnorm(x, o, out_norm=L["cham_norm"])
             cm = L["cham"]
-            q, k, v, g = cm.project(L["cham_norm"](x))
+            q, k, v, g = cm.project(nrm)
             rec, holo = launch_cham_update(q, k, v, g)
-            x = x + cm.finish(rec)
+            nxt = layers[l + 1]["sssd_norm"] if l + 1 < nl else None
+            nrm = V.add_rmsnorm(x, cm.w_out(rec), y_norm=cm.norm, out_norm=nxt)
             st.load_layer(l, psi, holo)
             del o, psi, q, k, v, g, rec, holo
-        del x
+        del x, nrm
         saved = (st.psi.clone(), st.H_real.clone(), st.H_imag.clone())
         torch.cuda.empty_cache()
         tok = torch.zeros(b, dtype=torch.long, device=dev)
 
         def dstep():
-            hcur = embed(tok).unsqueeze(1)
+            hcur = embed(tok).unsqueeze(1).contiguous()
+            nrm = V.rmsnorm(hcur, layers[0]["sssd_norm"])
             for l, L in enumerate(layers):
                 sm, cm = L["sssd"], L["cham"]
-                q, k, v, dl = sm.project(L["sssd_norm"](hcur))
+                q, k, v, dl = sm.project(nrm)
                 o = st.step_sssd(l, q, k, v, dl)
-                hcur = hcur + sm.finish(o.view(b, 1, nh, d))
-                q, k, v, g = cm.project(L["cham_norm"](hcur))
+                nrm = V.add_rmsnorm(hcur, sm.finish(o.view(b, 1, nh, d)), out_norm=L["cham_norm"])
+                q, k, v, g = cm.project(nrm)
                 rec = st.step_cham(l, q, k, v, g)
-                hcur = hcur + cm.finish(rec.view(b, 1, D))
+                nxt = layers[l + 1]["sssd_norm"] if l + 1 < nl else None
+                nrm = V.add_rmsnorm(hcur, cm.w_out(rec.view(b, 1, D)), y_norm=cm.norm, out_norm=nxt)
             return hcur
 
         side = torch.cuda.Stream(dev)

@@ -174,6 +174,23 @@ VERACE_API int verace_mixer_prologue(const void* y, long long ld, void* q, void*
                                      const unsigned char* mask, long long n, int heads, int head_dim,
                                      int gate_cols, int silu_v, int dtype, void* stream);
 
+/* ------------------------------------------------------------------------------
+ * Block glue: the RMSNorms and residual adds around the two mixers
+ * (verace_v1/modules/backbone.py: h <- h + SSSD(RMSNorm(h)); h <- h + CHAM(RMSNorm(h));
+ * SSSDAttention's per-head RMSNorm, sssd_attention.py:177-182; CHAM's output RMSNorm,
+ * cham_memory.py:241).  RMSNorm as torch.nn.RMSNorm: x * rsqrt(mean(x^2) + eps) in fp32,
+ * rounded to the dtype, then times the weight (rounded); no weight when weight is NULL.
+ * Rows of `cols` contiguous elements; cols % 8 == 0, cols <= 2048.
+ * verace_rmsnorm:     y = RMSNorm(x)                   (x and y may alias)
+ * verace_add_rmsnorm: h <- h + (norm_y ? RMSNorm(y; y_weight, y_eps) : y), in place;
+ *                     then n = RMSNorm(h; n_weight, n_eps) when n is not NULL.
+ * ---------------------------------------------------------------------------- */
+VERACE_API int verace_rmsnorm(const void* x, const void* weight, void* y, long long rows, int cols, float eps,
+                              int dtype, void* stream);
+VERACE_API int verace_add_rmsnorm(void* h, const void* y, int norm_y, const void* y_weight, float y_eps,
+                                  const void* n_weight, float n_eps, void* n, long long rows, int cols, int dtype,
+                                  void* stream);
+
 enum { VERACE_DECODE_UNITARY = 0, VERACE_DECODE_FIRST_ORDER = 1 };
 VERACE_API size_t verace_decode_workspace(int b, int D);
 VERACE_API int verace_decode_step(const void* sssd_q, const void* sssd_k, const void* sssd_v,

@@ -92,3 +92,15 @@ def test_decode_python_api_requires_cuda_tensors():
     x = torch.zeros(1, 2, 4)
     with pytest.raises(AssertionError, match="CUDA"):
         decode.launch_decode_step((x, x, x, torch.zeros(1, 2), torch.zeros(1, 2, 4, 4)), None)
+
+
+def test_norm_glue_rejects_bad_arguments_without_a_device():
+    L = _lib.lib()
+    fake = ctypes.c_void_p(256)
+    assert L.verace_rmsnorm(fake, None, fake, 4, 12, 1e-6, 1, None) == 2 and "cols 12" in _err()
+    assert L.verace_rmsnorm(fake, None, fake, 4, 64, 1e-6, 9, None) == 1 and "dtype" in _err()
+    assert L.verace_rmsnorm(fake, None, fake, -1, 64, 1e-6, 1, None) == 1 and "rows" in _err()
+    assert L.verace_rmsnorm(None, None, None, 0, 64, 1e-6, 1, None) == 0     # nothing to do
+    assert L.verace_add_rmsnorm(fake, fake, 0, None, 0.0, None, 0.0, None, 4, 4096, 1, None) == 2
+    assert L.verace_add_rmsnorm(None, fake, 0, None, 0.0, None, 0.0, None, 4, 64, 1, None) == 1
+    assert "NULL" in _err()

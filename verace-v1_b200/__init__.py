@@ -6,12 +6,13 @@ Public surface (mirrors the reference package verace_v1 for this path):
     SSSDAttention, ContinuousHolographicMemory, newton_schulz_unitary_retraction
     launch_sssd_scan / launch_sssd_triton_scan
     launch_cham_update / launch_cham_triton_update
+    rmsnorm, add_rmsnorm                             (block glue: RMSNorm, residual + RMSNorm)
     DecodeState, launch_decode_step, device_status   (batched incremental decode)
 The kernels live in libverace_b200.so (C ABI: include/verace_b200.h), built by
 build.py; nothing here falls back to CPU or Python arithmetic.
 """
-from .kernels import (cham_retract, launch_cham_triton_update, launch_cham_update,
-                      launch_sssd_scan, launch_sssd_triton_scan)
+from .kernels import (add_rmsnorm, cham_retract, launch_cham_triton_update, launch_cham_update,
+                      launch_sssd_scan, launch_sssd_triton_scan, rmsnorm)
 from .decode import DecodeState, device_status, launch_decode_step
 from .sssd_attention import SSSDAttention
 from .cham_memory import ContinuousHolographicMemory, newton_schulz_unitary_retraction
@@ -20,5 +21,5 @@ __all__ = [
     "SSSDAttention", "ContinuousHolographicMemory", "newton_schulz_unitary_retraction",
     "launch_sssd_scan", "launch_sssd_triton_scan", "launch_cham_update",
     "launch_cham_triton_update", "cham_retract", "DecodeState", "launch_decode_step",
-    "device_status",
+    "device_status", "rmsnorm", "add_rmsnorm",
 ]

@@ -17,7 +17,7 @@ import torch
 import torch.nn as nn
 import torch.nn.functional as F
 
-from .kernels import cham_retract, concat_weights, launch_cham_update, mixer_prologue
+from .kernels import apply_rmsnorm, cham_retract, concat_weights, launch_cham_update, mixer_prologue
 from .sssd_attention import _require_inference
 
 
@@ -67,4 +67,4 @@ class ContinuousHolographicMemory(nn.Module):
 
     def finish(self, rec: torch.Tensor) -> torch.Tensor:
         """Module output from the scan's readout rec [b, s, D] (cham_memory.py:241)."""
-        return self.norm(self.w_out(rec))
+        return apply_rmsnorm(self.norm, self.w_out(rec))

@@ -164,3 +164,66 @@ def concat_weights(module: torch.nn.Module, weights) -> torch.Tensor:
 # drop-in aliases with the reference's launcher names
 launch_sssd_triton_scan = launch_sssd_scan
 launch_cham_triton_update = launch_cham_update
+
+
+def _norm_args(norm: Optional[torch.nn.Module], x: torch.Tensor):
+    """(weight pointer, eps) of a torch.nn.RMSNorm over x's last dimension (eps None means
+    torch.finfo(x.dtype).eps, as torch.nn.RMSNorm does)."""
+    if norm is None:
+        return 0, 0.0
+    assert tuple(norm.normalized_shape) == (x.shape[-1],), "RMSNorm must normalise the last dimension"
+    eps = norm.eps if norm.eps is not None else torch.finfo(x.dtype).eps
+    w = norm.weight
+    if w is None:
+        return 0, float(eps)
+    assert w.dtype == x.dtype and w.is_contiguous() and w.device == x.device, \
+        "RMSNorm weight must be contiguous, on the input's device and in its dtype"
+    return w.data_ptr(), float(eps)
+
+
+def fused_norm_supported(x: torch.Tensor) -> bool:
+    """Whether rmsnorm / add_rmsnorm take rows of x's last dimension."""
+    c = x.shape[-1]
+    return x.dtype in _DTYPE and c % 8 == 0 and c <= 2048
+
+
+def rmsnorm(x: torch.Tensor, norm: torch.nn.Module) -> torch.Tensor:
+    """`norm` (a torch.nn.RMSNorm over the last dimension) applied to x in one pass."""
+    assert x.is_cuda, "This kernel requires CUDA tensors"
+    x = x.contiguous()
+    y = torch.empty_like(x)
+    w, eps = _norm_args(norm, x)
+    cols = x.shape[-1]
+    with torch.cuda.device(x.device):
+        rc = lib().verace_rmsnorm(x.data_ptr(), w, y.data_ptr(), x.numel() // cols, cols, eps,
+                                  _DTYPE[x.dtype], _stream(x.device))
+    check(rc, "verace_rmsnorm")
+    return y
+
+
+def add_rmsnorm(h: torch.Tensor, y: torch.Tensor, y_norm: Optional[torch.nn.Module] = None,
+                out_norm: Optional[torch.nn.Module] = None) -> Optional[torch.Tensor]:
+    """A block's residual step in one pass: h <- h + (y_norm(y) if y_norm else y) in place
+    (h contiguous), then out_norm(h) is returned (None without out_norm)."""
+    assert h.is_cuda and h.is_contiguous(), "h must be a contiguous CUDA tensor (updated in place)"
+    assert y.shape == h.shape and y.dtype == h.dtype, "h and y must match"
+    y = y.contiguous()
+    wy, ey = _norm_args(y_norm, h)
+    wn, en = _norm_args(out_norm, h)
+    n = torch.empty_like(h) if out_norm is not None else None
+    cols = h.shape[-1]
+    with torch.cuda.device(h.device):
+        rc = lib().verace_add_rmsnorm(h.data_ptr(), y.data_ptr(), 1 if y_norm is not None else 0, wy, ey, wn, en,
+                                      _ptr(n), h.numel() // cols, cols, _DTYPE[h.dtype], _stream(h.device))
+    check(rc, "verace_add_rmsnorm")
+    return n
+
+
+def apply_rmsnorm(norm: torch.nn.Module, x: torch.Tensor) -> torch.Tensor:
+    """norm(x) through the fused kernel where it applies (CUDA input, the weight in x's
+    dtype, rows of a multiple of 8 up to 2048), else through the module itself."""
+    w = getattr(norm, "weight", None)
+    if (x.is_cuda and fused_norm_supported(x) and tuple(norm.normalized_shape) == (x.shape[-1],)
+            and (w is None or (w.dtype == x.dtype and w.device == x.device))):
+        return rmsnorm(x, norm)
+    return norm(x)

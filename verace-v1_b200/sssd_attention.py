@@ -17,7 +17,7 @@ import torch
 import torch.nn as nn
 import torch.nn.functional as F
 
-from .kernels import concat_weights, launch_sssd_scan, mixer_prologue
+from .kernels import apply_rmsnorm, concat_weights, launch_sssd_scan, mixer_prologue
 
 
 def _require_inference(x: torch.Tensor, who: str):
@@ -72,4 +72,4 @@ class SSSDAttention(nn.Module):
     def finish(self, o: torch.Tensor) -> torch.Tensor:
         """Module output from the scan's readout o [b, s, h, d] (sssd_attention.py:177-182)."""
         b, s = o.shape[0], o.shape[1]
-        return self.w_out(self.head_rmsnorm(o).view(b, s, self.num_heads * self.head_dim))
+        return self.w_out(apply_rmsnorm(self.head_rmsnorm, o).view(b, s, self.num_heads * self.head_dim))
