@@ -1714,10 +1714,11 @@ cham_tc_step_ws(const __grid_constant__ CUtensorMap tm_k, const __grid_constant_
 constexpr int CP2_SLOT = 32 * 1024, CP2_ZC = 64 * 1024, CP2_BAR = 96 * 1024;
 constexpr int CP2_SMEM = CP2_BAR + 256;
 constexpr int KH = 64;   // state rows per phase-A half tile
+constexpr int CP2_THREADS = CONS + 64;    // consumers + producer warp (MMAs, phases T/E/B) + phase-A loader warp
 enum { B2_FULL = 0, B2_SPL = 3, B2_MD = 6, B2_TT = 9, B2_ZR = 10, B2_P1 = 11, B2_MT = 12, B2_CR = 13, B2_ME = 14,
        B2_DH = 15, B2_DF = 17, B2_SF = 19, B2_SR = 21, N_BARS2 = 23 };
 
-__global__ void __launch_bounds__(WS_THREADS, 2)
+__global__ void __launch_bounds__(CP2_THREADS, 2)
 cham_tc_colpass2(const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
                  const __grid_constant__ CUtensorMap tm_sr, const __grid_constant__ CUtensorMap tm_si,
                  const __grid_constant__ CUtensorMap tm_sr128, const __grid_constant__ CUtensorMap tm_si128,
@@ -1756,7 +1757,30 @@ cham_tc_colpass2(const __grid_constant__ CUtensorMap tm_k, const __grid_constant
   const uint32_t tbase = *tslot;
   const uint32_t tZ = tbase, tP1 = tbase + 64, tP2 = tbase + 128, tE = tbase + 192, tDH = tbase + 64;
 
-  if (warp == 8) {
+  auto issue_a = [&](int h) {   // phase-A half tile h into slot h % 3
+    const int s = h % 3;
+    unsigned char* w = slot(s);
+    tc::mbar_expect_tx(&bars[B2_FULL + s], 16 * 1024 + (src_identity ? 0 : 16 * 1024));
+    tc::tma_load_3d(w, &tm_k, h * KH, t0, item, &bars[B2_FULL + s]);
+    tc::tma_load_3d(w + 8192, &tm_v, h * KH, t0, item, &bars[B2_FULL + s]);
+    if (!src_identity) {
+      tc::tma_load_2d(w + 16384, &tm_sr, j0, (src_row_re + item) * D + h * KH, &bars[B2_FULL + s]);
+      tc::tma_load_2d(w + 24576, &tm_si, j0, (src_row_im + item) * D + h * KH, &bars[B2_FULL + s]);
+    }
+  };
+  if (warp == 9) {
+    // ============ phase-A loader (one thread): refill each slot once its MMAs are done ============
+    if (lane == 0) {
+      for (int h = 0; h + 3 < NH; ++h) {
+        if (*fail || !tc::mbar_wait(&bars[B2_MD + h % 3], (h / 3) & 1, MAX_POLLS)) {
+          *fail = 1;
+          record_timeout();
+          break;
+        }
+        issue_a(h + 3);
+      }
+    }
+  } else if (warp == 8) {
     // ======================= producer (one thread) =======================
     if (lane == 0) {
       bool ok = true;
@@ -1767,17 +1791,6 @@ cham_tc_colpass2(const __grid_constant__ CUtensorMap tm_k, const __grid_constant
         if (!ok) return false;
         if (*fail || !tc::mbar_wait(&bars[b], par, MAX_POLLS)) { ok = false; *fail = 1; record_timeout(); }
         return ok;
-      };
-      auto issue_a = [&](int h) {   // phase-A half tile h into slot h % 3
-        const int s = h % 3;
-        unsigned char* w = slot(s);
-        tc::mbar_expect_tx(&bars[B2_FULL + s], 16 * 1024 + (src_identity ? 0 : 16 * 1024));
-        tc::tma_load_3d(w, &tm_k, h * KH, t0, item, &bars[B2_FULL + s]);
-        tc::tma_load_3d(w + 8192, &tm_v, h * KH, t0, item, &bars[B2_FULL + s]);
-        if (!src_identity) {
-          tc::tma_load_2d(w + 16384, &tm_sr, j0, (src_row_re + item) * D + h * KH, &bars[B2_FULL + s]);
-          tc::tma_load_2d(w + 24576, &tm_si, j0, (src_row_im + item) * D + h * KH, &bars[B2_FULL + s]);
-        }
       };
       auto issue_b = [&](int kt) {  // phase-B W tile kt into slot (kt + 1) & 1
         const int s = (kt + 1) & 1;
@@ -1791,7 +1804,7 @@ cham_tc_colpass2(const __grid_constant__ CUtensorMap tm_k, const __grid_constant
       };
       constexpr uint32_t ID_Z = tc::idesc_bf16(128, N2, false, true);
       constexpr uint32_t ID_H = tc::idesc_bf16(128, N2, true, true);
-      // ---- phase A: Z = Wᵀ S over 64-row half tiles
+      // ---- phase A: Z = Wᵀ S over 64-row half tiles (the loader warp refills the slots)
       for (int h = 0; h < 3 && h < NH; ++h) issue_a(h);
       for (int h = 0; h < NH && ok; ++h) {
         const int s = h % 3;
@@ -1807,10 +1820,6 @@ cham_tc_colpass2(const __grid_constant__ CUtensorMap tm_k, const __grid_constant
           tc::mma_bf16(tZ, a, tc::sdesc(bl + ks * 2 * (N2 / 8) * 128, (N2 / 8) * 128, 128), ID_Z, 1u);
         }
         tc::commit(&bars[B2_MD + s]);
-        if (h + 3 < NH) {
-          if (!pwait(B2_MD + s, (h / 3) & 1)) break;
-          issue_a(h + 3);
-        }
       }
       // ---- phase T: P1 = Tr Z, then P2 = Ti Z, T halves through the ring
       const int sl = (NH - 1) % 3;
@@ -2621,7 +2630,7 @@ int launch_cham_tc(const void* q, const void* k, const void* v, const float* gam
       const int rs = (c + w.nring - 1) % w.nring, rd = c % w.nring;
       float* si = c > 0 ? im_dst(c - 1) : hi;
       float* di = im_dst(c);
-      cham_tc_colpass2<<<dim3(D / NB2, b), WS_THREADS, CP2_SMEM, st>>>(
+      cham_tc_colpass2<<<dim3(D / NB2, b), CP2_THREADS, CP2_SMEM, st>>>(
           mk, mv, m_ring64, si == hi ? m_hi64 : m_him64, m_ring, si == hi ? m_hi128 : m_him128, m_ring,
           di == hi ? m_hi128 : m_him128, rs * b, 0, rd * b, 0, (const __nv_bfloat16*)q, w.T, w.E, w.bad,
           c == 0 ? 1 : 0, s, D, nch, c);
