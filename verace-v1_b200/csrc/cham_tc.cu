@@ -1720,12 +1720,12 @@ enum { B2_FULL = 0, B2_SPL = 3, B2_MD = 6, B2_TT = 9, B2_ZR = 10, B2_P1 = 11, B2
 
 __global__ void __launch_bounds__(CP2_THREADS, 2)
 cham_tc_colpass2(const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
-                 const __grid_constant__ CUtensorMap tm_sr, const __grid_constant__ CUtensorMap tm_si,
-                 const __grid_constant__ CUtensorMap tm_sr128, const __grid_constant__ CUtensorMap tm_si128,
-                 const __grid_constant__ CUtensorMap tm_dr, const __grid_constant__ CUtensorMap tm_di,
-                 int src_row_re, int src_row_im, int dst_row_re, int dst_row_im,
-                 const __nv_bfloat16* __restrict__ q, const unsigned char* __restrict__ Tws, float* __restrict__ Ews,
-                 const unsigned long long* __restrict__ badws, int src_identity, int S, int D, int nch, int c) {
+                 const __grid_constant__ CUtensorMap tm_ring64, const __grid_constant__ CUtensorMap tm_ring128,
+                 const __grid_constant__ CUtensorMap tm_hi64, const __grid_constant__ CUtensorMap tm_him64,
+                 const __grid_constant__ CUtensorMap tm_hi128, const __grid_constant__ CUtensorMap tm_him128,
+                 int nring, int b, const __nv_bfloat16* __restrict__ q, const unsigned char* __restrict__ Tws,
+                 float* __restrict__ Ews, const unsigned long long* __restrict__ badws, int S, int D, int nch, int c0,
+                 int c1) {
   extern __shared__ __align__(1024) unsigned char smc[];
   uint64_t* bars = reinterpret_cast<uint64_t*>(smc + CP2_BAR);
   uint32_t* tslot = reinterpret_cast<uint32_t*>(smc + CP2_BAR + 8 * N_BARS2);
@@ -1739,10 +1739,6 @@ cham_tc_colpass2(const __grid_constant__ CUtensorMap tm_k, const __grid_constant
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int item = blockIdx.y, j0 = blockIdx.x * NB2;
-  const int t0 = c * C2, nt = min(C2, S - t0);
-  const size_t chunk = (size_t)item * nch + c;
-  const unsigned long long bad = badws[chunk];
-  const bool patch_w = bad != 0ull;       // padded rows come back zero from the TMA bounds
   const int NH = D / KH, NT = D / KT;
 
   if (warp == 0) tc::tmem_alloc(tslot, 256);
@@ -1757,331 +1753,370 @@ cham_tc_colpass2(const __grid_constant__ CUtensorMap tm_k, const __grid_constant
   const uint32_t tbase = *tslot;
   const uint32_t tZ = tbase, tP1 = tbase + 64, tP2 = tbase + 128, tE = tbase + 192, tDH = tbase + 64;
 
-  auto issue_a = [&](int h) {   // phase-A half tile h into slot h % 3
-    const int s = h % 3;
-    unsigned char* w = slot(s);
-    tc::mbar_expect_tx(&bars[B2_FULL + s], 16 * 1024 + (src_identity ? 0 : 16 * 1024));
-    tc::tma_load_3d(w, &tm_k, h * KH, t0, item, &bars[B2_FULL + s]);
-    tc::tma_load_3d(w + 8192, &tm_v, h * KH, t0, item, &bars[B2_FULL + s]);
-    if (!src_identity) {
-      tc::tma_load_2d(w + 16384, &tm_sr, j0, (src_row_re + item) * D + h * KH, &bars[B2_FULL + s]);
-      tc::tma_load_2d(w + 24576, &tm_si, j0, (src_row_im + item) * D + h * KH, &bars[B2_FULL + s]);
-    }
-  };
-  if (warp == 9) {
-    // ============ phase-A loader (one thread): refill each slot once its MMAs are done ============
-    if (lane == 0) {
-      for (int h = 0; h + 3 < NH; ++h) {
-        if (*fail || !tc::mbar_wait(&bars[B2_MD + h % 3], (h / 3) & 1, MAX_POLLS)) {
-          *fail = 1;
-          record_timeout();
-          break;
-        }
-        issue_a(h + 3);
+  // The chunks [c0, c1) one after another: a column block depends only on its own
+  // column block of the previous chunk, so the CTAs never wait for one another.
+  for (int c = c0; c < c1; ++c) {
+    const int t0 = c * C2, nt = min(C2, S - t0);
+    const size_t chunk = (size_t)item * nch + c;
+    const unsigned long long bad = badws[chunk];
+    const bool patch_w = bad != 0ull;       // padded rows come back zero from the TMA bounds
+    const int src_identity = c == 0;
+    // real part: ring slot of chunk c-1 -> ring slot of chunk c; imaginary part: two
+    // planes in turn, the last chunk's landing in the output
+    const int src_row_re = ((c + nring - 1) % nring) * b, dst_row_re = (c % nring) * b;
+    const int src_row_im = 0, dst_row_im = 0;
+    const bool src_hi = (nch - c) % 2 == 0, dst_hi = (nch - 1 - c) % 2 == 0;
+    const CUtensorMap* tm_sr = &tm_ring64;
+    const CUtensorMap* tm_sr128 = &tm_ring128;
+    const CUtensorMap* tm_dr = &tm_ring128;
+    const CUtensorMap* tm_si = src_hi ? &tm_hi64 : &tm_him64;
+    const CUtensorMap* tm_si128 = src_hi ? &tm_hi128 : &tm_him128;
+    const CUtensorMap* tm_di = dst_hi ? &tm_hi128 : &tm_him128;
+
+    auto issue_a = [&](int h) {   // phase-A half tile h into slot h % 3
+      const int s = h % 3;
+      unsigned char* w = slot(s);
+      tc::mbar_expect_tx(&bars[B2_FULL + s], 16 * 1024 + (src_identity ? 0 : 16 * 1024));
+      tc::tma_load_3d(w, &tm_k, h * KH, t0, item, &bars[B2_FULL + s]);
+      tc::tma_load_3d(w + 8192, &tm_v, h * KH, t0, item, &bars[B2_FULL + s]);
+      if (!src_identity) {
+        tc::tma_load_2d(w + 16384, tm_sr, j0, (src_row_re + item) * D + h * KH, &bars[B2_FULL + s]);
+        tc::tma_load_2d(w + 24576, tm_si, j0, (src_row_im + item) * D + h * KH, &bars[B2_FULL + s]);
       }
-    }
-  } else if (warp == 8) {
-    // ======================= producer (one thread) =======================
-    if (lane == 0) {
-      bool ok = true;
-      // Barrier parities are closed forms of the tile indices (no counters indexed by a
-      // runtime slot, which would live in local memory): phase-A half tile h is use h / 3
-      // of slot h % 3; phase-B tile kt is use a_uses(s) + kt / 2 of slot s = (kt + 1) & 1.
-      auto pwait = [&](int b, uint32_t par) {
-        if (!ok) return false;
-        if (*fail || !tc::mbar_wait(&bars[b], par, MAX_POLLS)) { ok = false; *fail = 1; record_timeout(); }
-        return ok;
-      };
-      auto issue_b = [&](int kt) {  // phase-B W tile kt into slot (kt + 1) & 1
-        const int s = (kt + 1) & 1;
-        unsigned char* w = slot(s);
-        tc::mbar_expect_tx(&bars[B2_FULL + s], W_TILE);
-#pragma unroll
-        for (int kb = 0; kb < KT / 64; ++kb) {
-          tc::tma_load_3d(w + kb * 16384, &tm_k, kt * KT + kb * 64, t0, item, &bars[B2_FULL + s]);
-          tc::tma_load_3d(w + kb * 16384 + 8192, &tm_v, kt * KT + kb * 64, t0, item, &bars[B2_FULL + s]);
+    };
+    if (warp == 9) {
+      // ============ phase-A loader (one thread): refill each slot once its MMAs are done ============
+      if (lane == 0) {
+        for (int h = 0; h + 3 < NH; ++h) {
+          if (*fail || !tc::mbar_wait(&bars[B2_MD + h % 3], (h / 3) & 1, MAX_POLLS)) {
+            *fail = 1;
+            record_timeout();
+            break;
+          }
+          issue_a(h + 3);
         }
-      };
-      constexpr uint32_t ID_Z = tc::idesc_bf16(128, N2, false, true);
-      constexpr uint32_t ID_H = tc::idesc_bf16(128, N2, true, true);
-      // ---- phase A: Z = Wᵀ S over 64-row half tiles (the loader warp refills the slots)
-      for (int h = 0; h < 3 && h < NH; ++h) issue_a(h);
-      for (int h = 0; h < NH && ok; ++h) {
-        const int s = h % 3;
-        if (!pwait(B2_FULL + s, (h / 3) & 1) || !pwait(B2_SPL + s, (h / 3) & 1)) break;
-        tc::fence_after_sync();
-        const uint32_t aw = tc::smem_addr(slot(s));
-        const uint32_t bh = aw + 16384, bl = aw + 24576;
-#pragma unroll 1
-        for (int ks = 0; ks < KH / 16; ++ks) {
-          const uint64_t a = tc::sdesc_sw128(aw + ks * 32, 16, 1024);
-          tc::mma_bf16(tZ, a, tc::sdesc(bh + ks * 2 * (N2 / 8) * 128, (N2 / 8) * 128, 128), ID_Z,
-                       (h > 0 || ks > 0) ? 1u : 0u);
-          tc::mma_bf16(tZ, a, tc::sdesc(bl + ks * 2 * (N2 / 8) * 128, (N2 / 8) * 128, 128), ID_Z, 1u);
-        }
-        tc::commit(&bars[B2_MD + s]);
       }
-      // ---- phase T: P1 = Tr Z, then P2 = Ti Z, T halves through the ring
-      const int sl = (NH - 1) % 3;
-      const unsigned char* tsrc = Tws + chunk * 4 * T_TILE;
-      constexpr uint32_t ID_T = tc::idesc_bf16(128, N2, false, true);
-      auto t_mmas = [&](uint32_t td) {
-        const uint32_t th = tc::smem_addr(slot(0)), tl = tc::smem_addr(slot(1));
-        const uint32_t zh = tc::smem_addr(sZh), zl = tc::smem_addr(sZl);
-#pragma unroll 1
-        for (int ks = 0; ks < R2 / 16; ++ks) {
-          const uint64_t ah = tc::sdesc(th + ks * 2 * R2 * 16, R2 * 16, 128);
-          const uint64_t al = tc::sdesc(tl + ks * 2 * R2 * 16, R2 * 16, 128);
-          const uint64_t b_h = tc::sdesc(zh + ks * 2 * (N2 / 8) * 128, (N2 / 8) * 128, 128);
-          const uint64_t b_l = tc::sdesc(zl + ks * 2 * (N2 / 8) * 128, (N2 / 8) * 128, 128);
-          tc::mma_bf16(td, ah, b_h, ID_T, ks > 0 ? 1u : 0u);
-          tc::mma_bf16(td, ah, b_l, ID_T, 1u);
-          tc::mma_bf16(td, al, b_h, ID_T, 1u);
-        }
-      };
-      if (ok && pwait(B2_MD + sl, ((NH - 1) / 3) & 1)) {   // every phase-A MMA done: ring free
-        tc::mbar_expect_tx(&bars[B2_TT], 2 * T_TILE);
-        tc::bulk_load(slot(0), tsrc, T_TILE, &bars[B2_TT]);
-        tc::bulk_load(slot(1), tsrc + T_TILE, T_TILE, &bars[B2_TT]);
-        if (pwait(B2_ZR, 0) && pwait(B2_TT, 0)) {
+    } else if (warp == 8) {
+      // ======================= producer (one thread) =======================
+      if (lane == 0) {
+        bool ok = true;
+        // Barrier parities are closed forms of the tile indices (no counters indexed by a
+        // runtime slot, which would live in local memory): phase-A half tile h is use h / 3
+        // of slot h % 3; phase-B tile kt is use a_uses(s) + kt / 2 of slot s = (kt + 1) & 1.
+        auto pwait = [&](int b, uint32_t par) {
+          if (!ok) return false;
+          if (*fail || !tc::mbar_wait(&bars[b], par, MAX_POLLS)) { ok = false; *fail = 1; record_timeout(); }
+          return ok;
+        };
+        auto issue_b = [&](int kt) {  // phase-B W tile kt into slot (kt + 1) & 1
+          const int s = (kt + 1) & 1;
+          unsigned char* w = slot(s);
+          tc::mbar_expect_tx(&bars[B2_FULL + s], W_TILE);
+  #pragma unroll
+          for (int kb = 0; kb < KT / 64; ++kb) {
+            tc::tma_load_3d(w + kb * 16384, &tm_k, kt * KT + kb * 64, t0, item, &bars[B2_FULL + s]);
+            tc::tma_load_3d(w + kb * 16384 + 8192, &tm_v, kt * KT + kb * 64, t0, item, &bars[B2_FULL + s]);
+          }
+        };
+        constexpr uint32_t ID_Z = tc::idesc_bf16(128, N2, false, true);
+        constexpr uint32_t ID_H = tc::idesc_bf16(128, N2, true, true);
+        // ---- phase A: Z = Wᵀ S over 64-row half tiles (the loader warp refills the slots)
+        for (int h = 0; h < 3 && h < NH; ++h) issue_a(h);
+        for (int h = 0; h < NH && ok; ++h) {
+          const int s = h % 3;
+          if (!pwait(B2_FULL + s, (h / 3) & 1) || !pwait(B2_SPL + s, (h / 3) & 1)) break;
           tc::fence_after_sync();
-          t_mmas(tP1);
-          tc::commit(&bars[B2_P1]);
-          if (pwait(B2_P1, 0)) {
-            tc::mbar_expect_tx(&bars[B2_TT], 2 * T_TILE);
-            tc::bulk_load(slot(0), tsrc + 2 * T_TILE, T_TILE, &bars[B2_TT]);
-            tc::bulk_load(slot(1), tsrc + 3 * T_TILE, T_TILE, &bars[B2_TT]);
-            if (pwait(B2_TT, 1)) {
-              tc::fence_after_sync();
-              t_mmas(tP2);
-              tc::commit(&bars[B2_MT]);
+          const uint32_t aw = tc::smem_addr(slot(s));
+          const uint32_t bh = aw + 16384, bl = aw + 24576;
+  #pragma unroll 1
+          for (int ks = 0; ks < KH / 16; ++ks) {
+            const uint64_t a = tc::sdesc_sw128(aw + ks * 32, 16, 1024);
+            tc::mma_bf16(tZ, a, tc::sdesc(bh + ks * 2 * (N2 / 8) * 128, (N2 / 8) * 128, 128), ID_Z,
+                         (h > 0 || ks > 0) ? 1u : 0u);
+            tc::mma_bf16(tZ, a, tc::sdesc(bl + ks * 2 * (N2 / 8) * 128, (N2 / 8) * 128, 128), ID_Z, 1u);
+          }
+          tc::commit(&bars[B2_MD + s]);
+        }
+        // ---- phase T: P1 = Tr Z, then P2 = Ti Z, T halves through the ring
+        const int sl = (NH - 1) % 3;
+        const unsigned char* tsrc = Tws + chunk * 4 * T_TILE;
+        constexpr uint32_t ID_T = tc::idesc_bf16(128, N2, false, true);
+        auto t_mmas = [&](uint32_t td) {
+          const uint32_t th = tc::smem_addr(slot(0)), tl = tc::smem_addr(slot(1));
+          const uint32_t zh = tc::smem_addr(sZh), zl = tc::smem_addr(sZl);
+  #pragma unroll 1
+          for (int ks = 0; ks < R2 / 16; ++ks) {
+            const uint64_t ah = tc::sdesc(th + ks * 2 * R2 * 16, R2 * 16, 128);
+            const uint64_t al = tc::sdesc(tl + ks * 2 * R2 * 16, R2 * 16, 128);
+            const uint64_t b_h = tc::sdesc(zh + ks * 2 * (N2 / 8) * 128, (N2 / 8) * 128, 128);
+            const uint64_t b_l = tc::sdesc(zl + ks * 2 * (N2 / 8) * 128, (N2 / 8) * 128, 128);
+            tc::mma_bf16(td, ah, b_h, ID_T, ks > 0 ? 1u : 0u);
+            tc::mma_bf16(td, ah, b_l, ID_T, 1u);
+            tc::mma_bf16(td, al, b_h, ID_T, 1u);
+          }
+        };
+        if (ok && pwait(B2_MD + sl, ((NH - 1) / 3) & 1)) {   // every phase-A MMA done: ring free
+          tc::mbar_expect_tx(&bars[B2_TT], 2 * T_TILE);
+          tc::bulk_load(slot(0), tsrc, T_TILE, &bars[B2_TT]);
+          tc::bulk_load(slot(1), tsrc + T_TILE, T_TILE, &bars[B2_TT]);
+          if (pwait(B2_ZR, 0) && pwait(B2_TT, 0)) {
+            tc::fence_after_sync();
+            t_mmas(tP1);
+            tc::commit(&bars[B2_P1]);
+            if (pwait(B2_P1, 0)) {
+              tc::mbar_expect_tx(&bars[B2_TT], 2 * T_TILE);
+              tc::bulk_load(slot(0), tsrc + 2 * T_TILE, T_TILE, &bars[B2_TT]);
+              tc::bulk_load(slot(1), tsrc + 3 * T_TILE, T_TILE, &bars[B2_TT]);
+              if (pwait(B2_TT, 1)) {
+                tc::fence_after_sync();
+                t_mmas(tP2);
+                tc::commit(&bars[B2_MT]);
+              }
+            }
+          }
+        }
+        // ---- phase E: E = Re(Cm) Y (slot 0); the first phase-B W tile goes to slot 1
+        if (ok && pwait(B2_MT, 0)) {
+          issue_b(0);
+          if (pwait(B2_CR, 0)) {
+            tc::fence_after_sync();
+            constexpr uint32_t ID_E = tc::idesc_bf16(128, C2, false, false);
+            const uint32_t ah = tc::smem_addr(sAh), al = tc::smem_addr(sAl), yh = tc::smem_addr(sY);
+  #pragma unroll 1
+            for (int ks = 0; ks < NB2 / 16; ++ks) {
+              const uint64_t b_h = tc::sdesc(yh + ks * 2 * C2 * 16, C2 * 16, 128);
+              tc::mma_bf16(tE, tc::sdesc(ah + ks * 2 * R2 * 16, R2 * 16, 128), b_h, ID_E, ks > 0 ? 1u : 0u);
+              tc::mma_bf16(tE, tc::sdesc(al + ks * 2 * R2 * 16, R2 * 16, 128), b_h, ID_E, 1u);
+            }
+            tc::commit(&bars[B2_ME]);
+          }
+        }
+        // ---- phase B: per 128-row tile: W tile -> dH = W Cm (TMEM, double-buffered) ->
+        // the state tile into the same slot -> consumers' epilogue -> TMA store -> slot free
+        if (ok && pwait(B2_ME, 0)) {
+          if (NT > 1) issue_b(1);
+          for (int kt = 0; kt < NT && ok; ++kt) {
+            const int s = (kt + 1) & 1, d = kt & 1;
+            const uint32_t use = (uint32_t)((NH + 2 - s) / 3 + (kt >> 1));   // use of slot s
+            if (!pwait(B2_FULL + s, use & 1)) break;
+            if (patch_w && !pwait(B2_SPL + s, use & 1)) break;
+            if (kt >= 2 && !pwait(B2_DF + d, ((kt - 2) >> 1) & 1)) break;
+            tc::fence_after_sync();
+            const uint32_t aw = tc::smem_addr(slot(s));
+            const uint32_t ch = tc::smem_addr(sZh), cl = tc::smem_addr(sZl);
+  #pragma unroll 1
+            for (int ks = 0; ks < R2 / 16; ++ks) {
+              const uint64_t a = tc::sdesc_sw128(aw + ks * 2048, 16384, 1024);
+              tc::mma_bf16(tDH + 64 * d, a, tc::sdesc(ch + ks * 2 * (N2 / 8) * 128, (N2 / 8) * 128, 128), ID_H,
+                           ks > 0 ? 1u : 0u);
+              tc::mma_bf16(tDH + 64 * d, a, tc::sdesc(cl + ks * 2 * (N2 / 8) * 128, (N2 / 8) * 128, 128), ID_H, 1u);
+            }
+            tc::commit(&bars[B2_DH + d]);
+            // the W tile has been read: the state tile takes its slot
+            if (!pwait(B2_DH + d, (kt >> 1) & 1)) break;
+            if (!src_identity) {
+              tc::mbar_expect_tx(&bars[B2_SF + s], 32 * 1024);
+              tc::tma_load_2d(slot(s), tm_sr128, j0, (src_row_re + item) * D + kt * KT, &bars[B2_SF + s]);
+              tc::tma_load_2d(slot(s) + 16384, tm_si128, j0, (src_row_im + item) * D + kt * KT, &bars[B2_SF + s]);
+            }
+            // tile kt-1's slot, once its store has read it, takes W tile kt+1
+            if (kt >= 1 && kt + 1 < NT) {
+              const int sp = kt & 1;
+              if (!pwait(B2_SR + sp, ((kt - 1) >> 1) & 1)) break;
+              issue_b(kt + 1);
             }
           }
         }
       }
-      // ---- phase E: E = Re(Cm) Y (slot 0); the first phase-B W tile goes to slot 1
-      if (ok && pwait(B2_MT, 0)) {
-        issue_b(0);
-        if (pwait(B2_CR, 0)) {
-          tc::fence_after_sync();
-          constexpr uint32_t ID_E = tc::idesc_bf16(128, C2, false, false);
-          const uint32_t ah = tc::smem_addr(sAh), al = tc::smem_addr(sAl), yh = tc::smem_addr(sY);
-#pragma unroll 1
-          for (int ks = 0; ks < NB2 / 16; ++ks) {
-            const uint64_t b_h = tc::sdesc(yh + ks * 2 * C2 * 16, C2 * 16, 128);
-            tc::mma_bf16(tE, tc::sdesc(ah + ks * 2 * R2 * 16, R2 * 16, 128), b_h, ID_E, ks > 0 ? 1u : 0u);
-            tc::mma_bf16(tE, tc::sdesc(al + ks * 2 * R2 * 16, R2 * 16, 128), b_h, ID_E, 1u);
-          }
-          tc::commit(&bars[B2_ME]);
+    } else {
+      // ======================= consumers (warps 0-7) =======================
+      const uint32_t lane_base = (uint32_t)(32 * (warp & 3)) << 16;
+      const int row = 32 * (warp & 3) + lane, half = warp >> 2;
+      bool ok = true;
+      auto cwait = [&](int b, uint32_t par) {
+        bool mine = ok && !*fail && tc::mbar_wait(&bars[b], par, MAX_POLLS);
+        const bool all = consumers_all(mine);
+        if (!all) { if (ok && tid == 0) record_timeout(); ok = false; *fail = 1; }
+        return ok;
+      };
+      auto zero_bad_rows = [&](unsigned char* w, int nblk) {   // swizzled W (half) tile, nblk blocks of 16K
+        for (int e = tid; e < R2 * 8 * nblk; e += CONS) {
+          const int r = e % R2, cc = e / R2;                    // 16-byte chunk cc of row r
+          if ((bad >> tok(r)) & 1ull)
+            *reinterpret_cast<uint4*>(w + (cc >> 3) * 16384 + r * 128 + (((cc & 7) ^ (r & 7)) << 4)) =
+                make_uint4(0, 0, 0, 0);
         }
-      }
-      // ---- phase B: per 128-row tile: W tile -> dH = W Cm (TMEM, double-buffered) ->
-      // the state tile into the same slot -> consumers' epilogue -> TMA store -> slot free
-      if (ok && pwait(B2_ME, 0)) {
-        if (NT > 1) issue_b(1);
-        for (int kt = 0; kt < NT && ok; ++kt) {
-          const int s = (kt + 1) & 1, d = kt & 1;
-          const uint32_t use = (uint32_t)((NH + 2 - s) / 3 + (kt >> 1));   // use of slot s
-          if (!pwait(B2_FULL + s, use & 1)) break;
-          if (patch_w && !pwait(B2_SPL + s, use & 1)) break;
-          if (kt >= 2 && !pwait(B2_DF + d, ((kt - 2) >> 1) & 1)) break;
-          tc::fence_after_sync();
-          const uint32_t aw = tc::smem_addr(slot(s));
-          const uint32_t ch = tc::smem_addr(sZh), cl = tc::smem_addr(sZl);
-#pragma unroll 1
-          for (int ks = 0; ks < R2 / 16; ++ks) {
-            const uint64_t a = tc::sdesc_sw128(aw + ks * 2048, 16384, 1024);
-            tc::mma_bf16(tDH + 64 * d, a, tc::sdesc(ch + ks * 2 * (N2 / 8) * 128, (N2 / 8) * 128, 128), ID_H,
-                         ks > 0 ? 1u : 0u);
-            tc::mma_bf16(tDH + 64 * d, a, tc::sdesc(cl + ks * 2 * (N2 / 8) * 128, (N2 / 8) * 128, 128), ID_H, 1u);
-          }
-          tc::commit(&bars[B2_DH + d]);
-          // the W tile has been read: the state tile takes its slot
-          if (!pwait(B2_DH + d, (kt >> 1) & 1)) break;
-          if (!src_identity) {
-            tc::mbar_expect_tx(&bars[B2_SF + s], 32 * 1024);
-            tc::tma_load_2d(slot(s), &tm_sr128, j0, (src_row_re + item) * D + kt * KT, &bars[B2_SF + s]);
-            tc::tma_load_2d(slot(s) + 16384, &tm_si128, j0, (src_row_im + item) * D + kt * KT, &bars[B2_SF + s]);
-          }
-          // tile kt-1's slot, once its store has read it, takes W tile kt+1
-          if (kt >= 1 && kt + 1 < NT) {
-            const int sp = kt & 1;
-            if (!pwait(B2_SR + sp, ((kt - 1) >> 1) & 1)) break;
-            issue_b(kt + 1);
+      };
+      // ---- phase A: split each state half tile in place
+      for (int h = 0; h < NH && ok; ++h) {
+        const int s = h % 3;
+        if (!cwait(B2_FULL + s, (h / 3) & 1)) break;
+        unsigned char* w = slot(s);
+        if (patch_w) zero_bad_rows(w, 1);
+        float x[2][8];
+  #pragma unroll
+        for (int u = 0; u < 2; ++u) {
+          const int e = tid + CONS * u;
+          const int i = e % KH, gg = e / KH;        // row i, 8-column group gg (0-3 re, 4-7 im)
+          if (src_identity) {
+            const int gi = h * KH + i, col = j0 + (gg & 3) * 8;
+  #pragma unroll
+            for (int jj = 0; jj < 8; ++jj) x[u][jj] = (gg < 4 && gi == col + jj) ? 1.f : 0.f;
+          } else {
+            const unsigned char* box = w + (gg < 4 ? 16384 : 24576);
+            const int c0 = 2 * (gg & 3);
+            const float4 a = *reinterpret_cast<const float4*>(box + i * 128 + ((c0 ^ (i & 7)) << 4));
+            const float4 b = *reinterpret_cast<const float4*>(box + i * 128 + (((c0 + 1) ^ (i & 7)) << 4));
+            x[u][0] = a.x; x[u][1] = a.y; x[u][2] = a.z; x[u][3] = a.w;
+            x[u][4] = b.x; x[u][5] = b.y; x[u][6] = b.z; x[u][7] = b.w;
           }
         }
-      }
-    }
-  } else {
-    // ======================= consumers (warps 0-7) =======================
-    const uint32_t lane_base = (uint32_t)(32 * (warp & 3)) << 16;
-    const int row = 32 * (warp & 3) + lane, half = warp >> 2;
-    bool ok = true;
-    auto cwait = [&](int b, uint32_t par) {
-      bool mine = ok && !*fail && tc::mbar_wait(&bars[b], par, MAX_POLLS);
-      const bool all = consumers_all(mine);
-      if (!all) { if (ok && tid == 0) record_timeout(); ok = false; *fail = 1; }
-      return ok;
-    };
-    auto zero_bad_rows = [&](unsigned char* w, int nblk) {   // swizzled W (half) tile, nblk blocks of 16K
-      for (int e = tid; e < R2 * 8 * nblk; e += CONS) {
-        const int r = e % R2, cc = e / R2;                    // 16-byte chunk cc of row r
-        if ((bad >> tok(r)) & 1ull)
-          *reinterpret_cast<uint4*>(w + (cc >> 3) * 16384 + r * 128 + (((cc & 7) ^ (r & 7)) << 4)) =
-              make_uint4(0, 0, 0, 0);
-      }
-    };
-    // ---- phase A: split each state half tile in place
-    for (int h = 0; h < NH && ok; ++h) {
-      const int s = h % 3;
-      if (!cwait(B2_FULL + s, (h / 3) & 1)) break;
-      unsigned char* w = slot(s);
-      if (patch_w) zero_bad_rows(w, 1);
-      float x[2][8];
-#pragma unroll
-      for (int u = 0; u < 2; ++u) {
-        const int e = tid + CONS * u;
-        const int i = e % KH, gg = e / KH;        // row i, 8-column group gg (0-3 re, 4-7 im)
-        if (src_identity) {
-          const int gi = h * KH + i, col = j0 + (gg & 3) * 8;
-#pragma unroll
-          for (int jj = 0; jj < 8; ++jj) x[u][jj] = (gg < 4 && gi == col + jj) ? 1.f : 0.f;
-        } else {
-          const unsigned char* box = w + (gg < 4 ? 16384 : 24576);
-          const int c0 = 2 * (gg & 3);
-          const float4 a = *reinterpret_cast<const float4*>(box + i * 128 + ((c0 ^ (i & 7)) << 4));
-          const float4 b = *reinterpret_cast<const float4*>(box + i * 128 + (((c0 + 1) ^ (i & 7)) << 4));
-          x[u][0] = a.x; x[u][1] = a.y; x[u][2] = a.z; x[u][3] = a.w;
-          x[u][4] = b.x; x[u][5] = b.y; x[u][6] = b.z; x[u][7] = b.w;
+        tc::named_sync(1, CONS);                    // every fp32 value read before the split overwrites it
+  #pragma unroll
+        for (int u = 0; u < 2; ++u) {
+          const int e = tid + CONS * u;
+          const int i = e % KH, gg = e / KH;
+          uint4 hv, lv;
+          tc::split8(x[u], hv, lv);
+          *reinterpret_cast<uint4*>(w + 16384 + mnmaj(i, gg * 8, N2 / 8)) = hv;
+          *reinterpret_cast<uint4*>(w + 24576 + mnmaj(i, gg * 8, N2 / 8)) = lv;
         }
-      }
-      tc::named_sync(1, CONS);                    // every fp32 value read before the split overwrites it
-#pragma unroll
-      for (int u = 0; u < 2; ++u) {
-        const int e = tid + CONS * u;
-        const int i = e % KH, gg = e / KH;
-        uint4 hv, lv;
-        tc::split8(x[u], hv, lv);
-        *reinterpret_cast<uint4*>(w + 16384 + mnmaj(i, gg * 8, N2 / 8)) = hv;
-        *reinterpret_cast<uint4*>(w + 24576 + mnmaj(i, gg * 8, N2 / 8)) = lv;
-      }
-      tc::fence_proxy_async();
-      tc::named_sync(1, CONS);
-      if (tid == 0) tc::mbar_arrive(&bars[B2_SPL + s]);
-    }
-    // ---- phase T: Z -> operand (MD of the last half tile: every phase-A MMA done)
-    const int sl = (NH - 1) % 3;
-    if (ok && cwait(B2_MD + sl, ((NH - 1) / 3) & 1)) {
-      tc::fence_after_sync();
-      float z[32];
-      tc::tmem_ld16(tZ + lane_base + 32 * half, z);
-      tc::tmem_ld16(tZ + lane_base + 32 * half + 16, z + 16);
-#pragma unroll
-      for (int g4 = 0; g4 < 4; ++g4) {
-        uint4 hv, lv;
-        tc::split8(z + 8 * g4, hv, lv);
-        const int off = mnmaj(row, 32 * half + 8 * g4, N2 / 8);
-        *reinterpret_cast<uint4*>(sZh + off) = hv;
-        *reinterpret_cast<uint4*>(sZl + off) = lv;
-      }
-      tc::fence_proxy_async();
-      tc::fence_before_sync();
-      tc::named_sync(1, CONS);
-      if (tid == 0) tc::mbar_arrive(&bars[B2_ZR]);
-    }
-    // ---- phase E: Cm -> operands (ZC: MN-major re | im; slot 0: Re(Cm) K-major, Y)
-    if (ok && cwait(B2_MT, 0)) {
-      tc::fence_after_sync();
-      float p1r[16], p1i[16], p2r[16], p2i[16];
-      tc::tmem_ld16(tP1 + lane_base + 16 * half, p1r);
-      tc::tmem_ld16(tP1 + lane_base + 32 + 16 * half, p1i);
-      tc::tmem_ld16(tP2 + lane_base + 16 * half, p2r);
-      tc::tmem_ld16(tP2 + lane_base + 32 + 16 * half, p2i);
-      float cr[16], ci[16];
-#pragma unroll
-      for (int j = 0; j < 16; ++j) { cr[j] = p1r[j] - p2i[j]; ci[j] = p1i[j] + p2r[j]; }
-#pragma unroll
-      for (int g2 = 0; g2 < 2; ++g2) {
-        uint4 hv, lv;
-        const int jc = 16 * half + 8 * g2;
-        tc::split8(cr + 8 * g2, hv, lv);
-        *reinterpret_cast<uint4*>(sZh + mnmaj(row, jc, N2 / 8)) = hv;
-        *reinterpret_cast<uint4*>(sZl + mnmaj(row, jc, N2 / 8)) = lv;
-        *reinterpret_cast<uint4*>(sAh + kmaj(row, jc, R2)) = hv;
-        *reinterpret_cast<uint4*>(sAl + kmaj(row, jc, R2)) = lv;
-        tc::split8(ci + 8 * g2, hv, lv);
-        *reinterpret_cast<uint4*>(sZh + mnmaj(row, NB2 + jc, N2 / 8)) = hv;
-        *reinterpret_cast<uint4*>(sZl + mnmaj(row, NB2 + jc, N2 / 8)) = lv;
-      }
-      {
-        const int t = tid % C2, gq = tid / C2;   // 64 tokens x 4 groups of 8 columns
-        uint4 u = make_uint4(0, 0, 0, 0);
-        if (t < nt) u = *reinterpret_cast<const uint4*>(q + ((size_t)item * S + t0 + t) * D + j0 + gq * 8);
-        *reinterpret_cast<uint4*>(sY + kmaj(t, gq * 8, C2)) = u;
-      }
-      tc::fence_proxy_async();
-      tc::fence_before_sync();
-      tc::named_sync(1, CONS);
-      if (tid == 0) tc::mbar_arrive(&bars[B2_CR]);
-    }
-    if (ok && cwait(B2_ME, 0)) {
-      tc::fence_after_sync();
-      float e[32];
-      tc::tmem_ld16(tE + lane_base + 32 * half, e);
-      tc::tmem_ld16(tE + lane_base + 32 * half + 16, e + 16);
-      float4* Eo = reinterpret_cast<float4*>(Ews + chunk * R2 * C2 + (size_t)row * C2 + 32 * half);
-#pragma unroll
-      for (int t = 0; t < 8; ++t) atomicAdd(Eo + t, make_float4(e[4 * t], e[4 * t + 1], e[4 * t + 2], e[4 * t + 3]));
-    }
-    // ---- phase B: S_next = S + dH in the slot (thread: one row of one plane), TMA store
-    for (int kt = 0; kt < NT && ok; ++kt) {
-      const int s = (kt + 1) & 1, d = kt & 1;
-      unsigned char* w = slot(s);
-      if (patch_w) {
-        if (!cwait(B2_FULL + s, ((NH + 2 - s) / 3 + (kt >> 1)) & 1)) break;
-        zero_bad_rows(w, 2);
         tc::fence_proxy_async();
         tc::named_sync(1, CONS);
         if (tid == 0) tc::mbar_arrive(&bars[B2_SPL + s]);
       }
-      if (!cwait(B2_DH + d, (kt >> 1) & 1)) break;
-      tc::fence_after_sync();
-      float dh[32];
-      tc::tmem_ld16(tDH + 64 * d + lane_base + 32 * half, dh);
-      tc::tmem_ld16(tDH + 64 * d + lane_base + 32 * half + 16, dh + 16);
-      tc::fence_before_sync();
-      tc::named_sync(1, CONS);
-      if (tid == 0) tc::mbar_arrive(&bars[B2_DF + d]);   // dH[d] may be overwritten
-      unsigned char* box = w + half * 16384;
-      if (src_identity) {
-        const int gi = kt * KT + row;
-#pragma unroll
-        for (int cc = 0; cc < 8; ++cc) {
-          float v4[4];
-#pragma unroll
-          for (int jj = 0; jj < 4; ++jj) v4[jj] = dh[4 * cc + jj] + ((!half && gi == j0 + 4 * cc + jj) ? 1.f : 0.f);
-          *reinterpret_cast<float4*>(box + row * 128 + ((cc ^ (row & 7)) << 4)) = make_float4(v4[0], v4[1], v4[2], v4[3]);
+      // ---- phase T: Z -> operand (MD of the last half tile: every phase-A MMA done)
+      const int sl = (NH - 1) % 3;
+      if (ok && cwait(B2_MD + sl, ((NH - 1) / 3) & 1)) {
+        tc::fence_after_sync();
+        float z[32];
+        tc::tmem_ld16(tZ + lane_base + 32 * half, z);
+        tc::tmem_ld16(tZ + lane_base + 32 * half + 16, z + 16);
+  #pragma unroll
+        for (int g4 = 0; g4 < 4; ++g4) {
+          uint4 hv, lv;
+          tc::split8(z + 8 * g4, hv, lv);
+          const int off = mnmaj(row, 32 * half + 8 * g4, N2 / 8);
+          *reinterpret_cast<uint4*>(sZh + off) = hv;
+          *reinterpret_cast<uint4*>(sZl + off) = lv;
         }
-      } else {
-        if (!cwait(B2_SF + s, (kt >> 1) & 1)) break;
-#pragma unroll
-        for (int cc = 0; cc < 8; ++cc) {
-          float4* p4 = reinterpret_cast<float4*>(box + row * 128 + ((cc ^ (row & 7)) << 4));
-          const float4 a = *p4;
-          *p4 = make_float4(a.x + dh[4 * cc], a.y + dh[4 * cc + 1], a.z + dh[4 * cc + 2], a.w + dh[4 * cc + 3]);
+        tc::fence_proxy_async();
+        tc::fence_before_sync();
+        tc::named_sync(1, CONS);
+        if (tid == 0) tc::mbar_arrive(&bars[B2_ZR]);
+      }
+      // ---- phase E: Cm -> operands (ZC: MN-major re | im; slot 0: Re(Cm) K-major, Y)
+      if (ok && cwait(B2_MT, 0)) {
+        tc::fence_after_sync();
+        float p1r[16], p1i[16], p2r[16], p2i[16];
+        tc::tmem_ld16(tP1 + lane_base + 16 * half, p1r);
+        tc::tmem_ld16(tP1 + lane_base + 32 + 16 * half, p1i);
+        tc::tmem_ld16(tP2 + lane_base + 16 * half, p2r);
+        tc::tmem_ld16(tP2 + lane_base + 32 + 16 * half, p2i);
+        float cr[16], ci[16];
+  #pragma unroll
+        for (int j = 0; j < 16; ++j) { cr[j] = p1r[j] - p2i[j]; ci[j] = p1i[j] + p2r[j]; }
+  #pragma unroll
+        for (int g2 = 0; g2 < 2; ++g2) {
+          uint4 hv, lv;
+          const int jc = 16 * half + 8 * g2;
+          tc::split8(cr + 8 * g2, hv, lv);
+          *reinterpret_cast<uint4*>(sZh + mnmaj(row, jc, N2 / 8)) = hv;
+          *reinterpret_cast<uint4*>(sZl + mnmaj(row, jc, N2 / 8)) = lv;
+          *reinterpret_cast<uint4*>(sAh + kmaj(row, jc, R2)) = hv;
+          *reinterpret_cast<uint4*>(sAl + kmaj(row, jc, R2)) = lv;
+          tc::split8(ci + 8 * g2, hv, lv);
+          *reinterpret_cast<uint4*>(sZh + mnmaj(row, NB2 + jc, N2 / 8)) = hv;
+          *reinterpret_cast<uint4*>(sZl + mnmaj(row, NB2 + jc, N2 / 8)) = lv;
+        }
+        {
+          const int t = tid % C2, gq = tid / C2;   // 64 tokens x 4 groups of 8 columns
+          uint4 u = make_uint4(0, 0, 0, 0);
+          if (t < nt) u = *reinterpret_cast<const uint4*>(q + ((size_t)item * S + t0 + t) * D + j0 + gq * 8);
+          *reinterpret_cast<uint4*>(sY + kmaj(t, gq * 8, C2)) = u;
+        }
+        tc::fence_proxy_async();
+        tc::fence_before_sync();
+        tc::named_sync(1, CONS);
+        if (tid == 0) tc::mbar_arrive(&bars[B2_CR]);
+      }
+      if (ok && cwait(B2_ME, 0)) {
+        tc::fence_after_sync();
+        float e[32];
+        tc::tmem_ld16(tE + lane_base + 32 * half, e);
+        tc::tmem_ld16(tE + lane_base + 32 * half + 16, e + 16);
+        float4* Eo = reinterpret_cast<float4*>(Ews + chunk * R2 * C2 + (size_t)row * C2 + 32 * half);
+  #pragma unroll
+        for (int t = 0; t < 8; ++t) atomicAdd(Eo + t, make_float4(e[4 * t], e[4 * t + 1], e[4 * t + 2], e[4 * t + 3]));
+      }
+      // ---- phase B: S_next = S + dH in the slot (thread: one row of one plane), TMA store
+      for (int kt = 0; kt < NT && ok; ++kt) {
+        const int s = (kt + 1) & 1, d = kt & 1;
+        unsigned char* w = slot(s);
+        if (patch_w) {
+          if (!cwait(B2_FULL + s, ((NH + 2 - s) / 3 + (kt >> 1)) & 1)) break;
+          zero_bad_rows(w, 2);
+          tc::fence_proxy_async();
+          tc::named_sync(1, CONS);
+          if (tid == 0) tc::mbar_arrive(&bars[B2_SPL + s]);
+        }
+        if (!cwait(B2_DH + d, (kt >> 1) & 1)) break;
+        tc::fence_after_sync();
+        float dh[32];
+        tc::tmem_ld16(tDH + 64 * d + lane_base + 32 * half, dh);
+        tc::tmem_ld16(tDH + 64 * d + lane_base + 32 * half + 16, dh + 16);
+        tc::fence_before_sync();
+        tc::named_sync(1, CONS);
+        if (tid == 0) tc::mbar_arrive(&bars[B2_DF + d]);   // dH[d] may be overwritten
+        unsigned char* box = w + half * 16384;
+        if (src_identity) {
+          const int gi = kt * KT + row;
+  #pragma unroll
+          for (int cc = 0; cc < 8; ++cc) {
+            float v4[4];
+  #pragma unroll
+            for (int jj = 0; jj < 4; ++jj) v4[jj] = dh[4 * cc + jj] + ((!half && gi == j0 + 4 * cc + jj) ? 1.f : 0.f);
+            *reinterpret_cast<float4*>(box + row * 128 + ((cc ^ (row & 7)) << 4)) = make_float4(v4[0], v4[1], v4[2], v4[3]);
+          }
+        } else {
+          if (!cwait(B2_SF + s, (kt >> 1) & 1)) break;
+  #pragma unroll
+          for (int cc = 0; cc < 8; ++cc) {
+            float4* p4 = reinterpret_cast<float4*>(box + row * 128 + ((cc ^ (row & 7)) << 4));
+            const float4 a = *p4;
+            *p4 = make_float4(a.x + dh[4 * cc], a.y + dh[4 * cc + 1], a.z + dh[4 * cc + 2], a.w + dh[4 * cc + 3]);
+          }
+        }
+        tc::fence_proxy_async();
+        tc::named_sync(1, CONS);
+        if (tid == 0) {
+          tc::tma_store_2d(tm_dr, j0, (dst_row_re + item) * D + kt * KT, w);
+          tc::tma_store_2d(tm_di, j0, (dst_row_im + item) * D + kt * KT, w + 16384);
+          tc::bulk_commit();
+          tc::bulk_wait_read<0>();                 // the store has read the slot
+          tc::mbar_arrive(&bars[B2_SR + s]);
         }
       }
-      tc::fence_proxy_async();
-      tc::named_sync(1, CONS);
       if (tid == 0) {
-        tc::tma_store_2d(&tm_dr, j0, (dst_row_re + item) * D + kt * KT, w);
-        tc::tma_store_2d(&tm_di, j0, (dst_row_im + item) * D + kt * KT, w + 16384);
-        tc::bulk_commit();
-        tc::bulk_wait_read<0>();                 // the store has read the slot
-        tc::mbar_arrive(&bars[B2_SR + s]);
+        tc::bulk_wait<0>();                        // all state writes performed
+        tc::fence_proxy_async_global();            // before the next chunk's loads read them
       }
     }
-    if (tid == 0) tc::bulk_wait<0>();            // all state writes performed
+    // chunk done: every load consumed, every MMA waited for, every store performed
+    tc::fence_before_sync();
+    __syncthreads();
+    if (*fail) break;
+    if (c + 1 < c1) {
+      if (tid == 0) {
+        for (int i = 0; i < N_BARS2; ++i) {
+          tc::mbar_inval(&bars[i]);
+          tc::mbar_init(&bars[i], 1);
+        }
+        tc::fence_mbar_init();
+      }
+      __syncthreads();
+      tc::fence_after_sync();
+    }
   }
   tc::fence_before_sync();
   __syncthreads();
@@ -2625,22 +2660,17 @@ int launch_cham_tc(const void* q, const void* k, const void* v, const float* gam
     if (nch < 2) { m_him64 = m_hi64; m_him128 = m_hi128; }
     VERACE_CUDA(cudaFuncSetAttribute(cham_tc_colpass2, cudaFuncAttributeMaxDynamicSharedMemorySize, CP2_SMEM));
     VERACE_CUDA(cudaFuncSetAttribute(cham_tc_readout_batch, cudaFuncAttributeMaxDynamicSharedMemorySize, RW2_SMEM));
-    auto im_dst = [&](int c) { return ((nch - 1 - c) % 2 == 0) ? hi : w.Him; };
-    for (int c = 0; c < nch; ++c) {
-      const int rs = (c + w.nring - 1) % w.nring, rd = c % w.nring;
-      float* si = c > 0 ? im_dst(c - 1) : hi;
-      float* di = im_dst(c);
+    // one column-pass launch per group of up to RING chunks (each CTA runs the group's
+    // chunks in turn), then one readout launch for the group from the ring
+    for (int cb = 0; cb < nch; cb += w.nring) {
+      const int ce = std::min(nch, cb + w.nring);
       cham_tc_colpass2<<<dim3(D / NB2, b), CP2_THREADS, CP2_SMEM, st>>>(
-          mk, mv, m_ring64, si == hi ? m_hi64 : m_him64, m_ring, si == hi ? m_hi128 : m_him128, m_ring,
-          di == hi ? m_hi128 : m_him128, rs * b, 0, rd * b, 0, (const __nv_bfloat16*)q, w.T, w.E, w.bad,
-          c == 0 ? 1 : 0, s, D, nch, c);
+          mk, mv, m_ring64, m_ring, m_hi64, m_him64, m_hi128, m_him128, w.nring, b, (const __nv_bfloat16*)q, w.T,
+          w.E, w.bad, s, D, nch, cb, ce);
       if ((rc = check_launch("cham_tc_colpass2"))) return rc;
-      if ((c + 1) % w.nring == 0 || c == nch - 1) {
-        const int cb = c - c % w.nring;
-        cham_tc_readout_batch<<<dim3((D / R2) * (c - cb + 1), b), WS_THREADS, RW2_SMEM, st>>>(
-            mk, mv, mq, m_ring, w.E, w.bad, (__nv_bfloat16*)out, s, D, nch, cb, w.nring, b);
-        if ((rc = check_launch("cham_tc_readout_batch"))) return rc;
-      }
+      cham_tc_readout_batch<<<dim3((D / R2) * (ce - cb), b), WS_THREADS, RW2_SMEM, st>>>(
+          mk, mv, mq, m_ring, w.E, w.bad, (__nv_bfloat16*)out, s, D, nch, cb, w.nring, b);
+      if ((rc = check_launch("cham_tc_readout_batch"))) return rc;
     }
     VERACE_CUDA(cudaMemcpyAsync(hr, w.ring + ((nch - 1) % w.nring) * plane, plane * sizeof(float),
                                 cudaMemcpyDeviceToDevice, st));

@@ -77,6 +77,10 @@ __device__ __forceinline__ void mbar_init(uint64_t* mbar, uint32_t count) {
   asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(mbar)), "r"(count) : "memory");
 }
 
+// Invalidate an mbarrier with no pending operations, so that it can be initialised again.
+__device__ __forceinline__ void mbar_inval(uint64_t* mbar) {
+  asm volatile("mbarrier.inval.shared::cta.b64 [%0];" ::"r"(smem_addr(mbar)) : "memory");
+}
 __device__ __forceinline__ void fence_mbar_init() {
   asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
 }
@@ -215,12 +219,18 @@ __device__ __forceinline__ void tma_load_4d(void* smem, const void* tmap, int x,
       "l"(tmap), "r"(x), "r"(y), "r"(z), "r"(w), "r"(smem_addr(mbar))
       : "memory");
 }
+// Prefetch a box of a tensor into L2 (no shared memory, no completion to wait for).
+__device__ __forceinline__ void tma_prefetch_2d(const void* tmap, int x, int y) {
+  asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global [%0, {%1, %2}];" ::"l"(tmap), "r"(x), "r"(y) : "memory");
+}
 // TMA tiled store shared -> global (bulk-group completion), and its group controls.
 __device__ __forceinline__ void tma_store_2d(const void* tmap, int x, int y, const void* smem) {
   asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%1, %2}], [%3];" ::"l"(tmap), "r"(x),
                "r"(y), "r"(smem_addr(smem))
                : "memory");
 }
+// Order this thread's completed bulk (async-proxy) global writes before later async-proxy reads.
+__device__ __forceinline__ void fence_proxy_async_global() { asm volatile("fence.proxy.async.global;" ::: "memory"); }
 __device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
 // wait until at most N committed bulk groups still read their shared-memory source
 template <int N>
