@@ -1702,37 +1702,40 @@ cham_tc_step_ws(const __grid_constant__ CUtensorMap tm_k, const __grid_constant_
 //         phase A: three slots (the two ring slots and ZC, idle until phase T);
 //                  slot = W half tile (64 state rows x 128 vectors: k box 8K | v box 8K)
 //                  | state half tile (re 8K | im 8K, fp32 SW128), split in place into
-//                  bf16 hi 8K | lo 8K (the MMA B operand)
+//                  one bf16 MN-major operand [64 rows][hi 64 | lo 64] (16K)
 //         phase T: Tr (hi | lo) across both slots, then Ti (hi | lo)
 //         phase E: Ca hi/lo (16K) | Y (4K) in slot 0
 //         phase B: slot = W tile (128 state rows x 128 vectors, 32K); once the tile's
-//                  MMA is done, the same slot takes the state tile (re 16K | im 16K, fp32
-//                  SW128), which the epilogue updates in place and TMA stores
-//       ZC [64K, 96K): Z split (hi 16K | lo 16K), then Cm split
+//                  MMA is done, the same slot takes dH (re 16K | im 16K, fp32 SW128),
+//                  which TMA adds onto the state
+//       ZC [64K, 96K): Z as [128][hi 64 | lo 64] bf16, then Cm the same way
 //       barriers, TMEM slot, failure flag at 96K
-// TMEM (256 columns): Z [0,64) P1 [64,128) P2 [128,192) E [192,256); dH[2] reuse P1/P2.
+// Each hi/lo operand pair is one N = 128 operand, so an A tile is read once per K step
+// (the MMAs are bound by shared-memory operand bandwidth); the accumulator halves are
+// summed by the consumers.
+// TMEM (256 columns): phase A Z [0,128); phase T P1 [0,128) P2 [128,256); phase E E [0,64);
+// phase B dH[2] at [0,128) and [128,256).
 constexpr int CP2_SLOT = 32 * 1024, CP2_ZC = 64 * 1024, CP2_BAR = 96 * 1024;
 constexpr int CP2_SMEM = CP2_BAR + 256;
 constexpr int KH = 64;   // state rows per phase-A half tile
 constexpr int CP2_THREADS = CONS + 64;    // consumers + producer warp (MMAs, phases T/E/B) + phase-A loader warp
 enum { B2_FULL = 0, B2_SPL = 3, B2_MD = 6, B2_TT = 9, B2_ZR = 10, B2_P1 = 11, B2_MT = 12, B2_CR = 13, B2_ME = 14,
-       B2_DH = 15, B2_DF = 17, B2_SF = 19, B2_SR = 21, N_BARS2 = 23 };
+       B2_DH = 15, B2_DF = 17, B2_ER = 19, B2_SR = 21, N_BARS2 = 23 };
 
 __global__ void __launch_bounds__(CP2_THREADS, 2)
 cham_tc_colpass2(const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
-                 const __grid_constant__ CUtensorMap tm_ring64, const __grid_constant__ CUtensorMap tm_ring128,
-                 const __grid_constant__ CUtensorMap tm_hi64, const __grid_constant__ CUtensorMap tm_him64,
-                 const __grid_constant__ CUtensorMap tm_hi128, const __grid_constant__ CUtensorMap tm_him128,
-                 int nring, int b, const __nv_bfloat16* __restrict__ q, const unsigned char* __restrict__ Tws,
-                 float* __restrict__ Ews, const unsigned long long* __restrict__ badws, int S, int D, int nch, int c0,
-                 int c1) {
+                 const __grid_constant__ CUtensorMap tm_hr64, const __grid_constant__ CUtensorMap tm_hi64,
+                 const __grid_constant__ CUtensorMap tm_hr128, const __grid_constant__ CUtensorMap tm_hi128,
+                 const __grid_constant__ CUtensorMap tm_ring64, int nring, int b, const __nv_bfloat16* __restrict__ q,
+                 const unsigned char* __restrict__ Tws, float* __restrict__ Ews,
+                 const unsigned long long* __restrict__ badws, int S, int D, int nch, int c0, int c1) {
   extern __shared__ __align__(1024) unsigned char smc[];
   uint64_t* bars = reinterpret_cast<uint64_t*>(smc + CP2_BAR);
   uint32_t* tslot = reinterpret_cast<uint32_t*>(smc + CP2_BAR + 8 * N_BARS2);
   volatile int* fail = reinterpret_cast<volatile int*>(smc + CP2_BAR + 8 * N_BARS2 + 16);
   auto slot = [&](int s) { return smc + s * CP2_SLOT; };   // slot 2 = the ZC region, phase A only
-  unsigned char* sZh = smc + CP2_ZC;      // Z split, then Cm split (MN-major, 16K each)
-  unsigned char* sZl = sZh + Z_TILE;
+  unsigned char* sZ = smc + CP2_ZC;       // Z, then Cm: [128][hi 64 | lo 64] bf16 MN-major (32K)
+  constexpr int NGW = 2 * N2 / 8;          // core-matrix columns of an N = 128 operand
   unsigned char* sAh = smc;               // phase E: Re(Cm) K-major hi/lo, Y
   unsigned char* sAl = smc + CA_TILE;
   unsigned char* sY = smc + 2 * CA_TILE;
@@ -1751,7 +1754,7 @@ cham_tc_colpass2(const __grid_constant__ CUtensorMap tm_k, const __grid_constant
   __syncthreads();
   tc::fence_after_sync();
   const uint32_t tbase = *tslot;
-  const uint32_t tZ = tbase, tP1 = tbase + 64, tP2 = tbase + 128, tE = tbase + 192, tDH = tbase + 64;
+  const uint32_t tZ = tbase, tP1 = tbase, tP2 = tbase + 128, tE = tbase, tDH = tbase;
 
   // The chunks [c0, c1) one after another: a column block depends only on its own
   // column block of the previous chunk, so the CTAs never wait for one another.
@@ -1761,17 +1764,15 @@ cham_tc_colpass2(const __grid_constant__ CUtensorMap tm_k, const __grid_constant
     const unsigned long long bad = badws[chunk];
     const bool patch_w = bad != 0ull;       // padded rows come back zero from the TMA bounds
     const int src_identity = c == 0;
-    // real part: ring slot of chunk c-1 -> ring slot of chunk c; imaginary part: two
-    // planes in turn, the last chunk's landing in the output
-    const int src_row_re = ((c + nring - 1) % nring) * b, dst_row_re = (c % nring) * b;
-    const int src_row_im = 0, dst_row_im = 0;
-    const bool src_hi = (nch - c) % 2 == 0, dst_hi = (nch - 1 - c) % 2 == 0;
-    const CUtensorMap* tm_sr = &tm_ring64;
-    const CUtensorMap* tm_sr128 = &tm_ring128;
-    const CUtensorMap* tm_dr = &tm_ring128;
-    const CUtensorMap* tm_si = src_hi ? &tm_hi64 : &tm_him64;
-    const CUtensorMap* tm_si128 = src_hi ? &tm_hi128 : &tm_him128;
-    const CUtensorMap* tm_di = dst_hi ? &tm_hi128 : &tm_him128;
+    // The state is updated in place in the output planes (phase A reads its column
+    // block, phase B adds dH with TMA reductions); phase A also stores the real part it
+    // reads (the end state of chunk c-1) to that chunk's ring slot for the readout.
+    const CUtensorMap* tm_sr = &tm_hr64;
+    const CUtensorMap* tm_si = &tm_hi64;
+    const CUtensorMap* tm_dr = &tm_hr128;
+    const CUtensorMap* tm_di = &tm_hi128;
+    const int src_row_re = 0, src_row_im = 0, dst_row_re = 0, dst_row_im = 0;
+    const int ring_row = c > 0 ? (((c - 1) % nring) * b + item) * D : -1;
 
     auto issue_a = [&](int h) {   // phase-A half tile h into slot h % 3
       const int s = h % 3;
@@ -1812,14 +1813,14 @@ cham_tc_colpass2(const __grid_constant__ CUtensorMap tm_k, const __grid_constant
           const int s = (kt + 1) & 1;
           unsigned char* w = slot(s);
           tc::mbar_expect_tx(&bars[B2_FULL + s], W_TILE);
-  #pragma unroll
+#pragma unroll
           for (int kb = 0; kb < KT / 64; ++kb) {
             tc::tma_load_3d(w + kb * 16384, &tm_k, kt * KT + kb * 64, t0, item, &bars[B2_FULL + s]);
             tc::tma_load_3d(w + kb * 16384 + 8192, &tm_v, kt * KT + kb * 64, t0, item, &bars[B2_FULL + s]);
           }
         };
-        constexpr uint32_t ID_Z = tc::idesc_bf16(128, N2, false, true);
-        constexpr uint32_t ID_H = tc::idesc_bf16(128, N2, true, true);
+        constexpr uint32_t ID_Z = tc::idesc_bf16(128, 2 * N2, false, true);
+        constexpr uint32_t ID_H = tc::idesc_bf16(128, 2 * N2, true, true);
         // ---- phase A: Z = Wᵀ S over 64-row half tiles (the loader warp refills the slots)
         for (int h = 0; h < 3 && h < NH; ++h) issue_a(h);
         for (int h = 0; h < NH && ok; ++h) {
@@ -1827,32 +1828,29 @@ cham_tc_colpass2(const __grid_constant__ CUtensorMap tm_k, const __grid_constant
           if (!pwait(B2_FULL + s, (h / 3) & 1) || !pwait(B2_SPL + s, (h / 3) & 1)) break;
           tc::fence_after_sync();
           const uint32_t aw = tc::smem_addr(slot(s));
-          const uint32_t bh = aw + 16384, bl = aw + 24576;
-  #pragma unroll 1
+          const uint32_t bb = aw + 16384;
+#pragma unroll 1
           for (int ks = 0; ks < KH / 16; ++ks) {
             const uint64_t a = tc::sdesc_sw128(aw + ks * 32, 16, 1024);
-            tc::mma_bf16(tZ, a, tc::sdesc(bh + ks * 2 * (N2 / 8) * 128, (N2 / 8) * 128, 128), ID_Z,
-                         (h > 0 || ks > 0) ? 1u : 0u);
-            tc::mma_bf16(tZ, a, tc::sdesc(bl + ks * 2 * (N2 / 8) * 128, (N2 / 8) * 128, 128), ID_Z, 1u);
+            tc::mma_bf16(tZ, a, tc::sdesc(bb + ks * 2 * NGW * 128, NGW * 128, 128), ID_Z, (h > 0 || ks > 0) ? 1u : 0u);
           }
           tc::commit(&bars[B2_MD + s]);
         }
         // ---- phase T: P1 = Tr Z, then P2 = Ti Z, T halves through the ring
         const int sl = (NH - 1) % 3;
         const unsigned char* tsrc = Tws + chunk * 4 * T_TILE;
-        constexpr uint32_t ID_T = tc::idesc_bf16(128, N2, false, true);
+        constexpr uint32_t ID_T = tc::idesc_bf16(128, 2 * N2, false, true);
+        constexpr uint32_t ID_T64 = tc::idesc_bf16(128, N2, false, true);
         auto t_mmas = [&](uint32_t td) {
           const uint32_t th = tc::smem_addr(slot(0)), tl = tc::smem_addr(slot(1));
-          const uint32_t zh = tc::smem_addr(sZh), zl = tc::smem_addr(sZl);
-  #pragma unroll 1
+          const uint32_t z = tc::smem_addr(sZ);
+#pragma unroll 1
           for (int ks = 0; ks < R2 / 16; ++ks) {
             const uint64_t ah = tc::sdesc(th + ks * 2 * R2 * 16, R2 * 16, 128);
             const uint64_t al = tc::sdesc(tl + ks * 2 * R2 * 16, R2 * 16, 128);
-            const uint64_t b_h = tc::sdesc(zh + ks * 2 * (N2 / 8) * 128, (N2 / 8) * 128, 128);
-            const uint64_t b_l = tc::sdesc(zl + ks * 2 * (N2 / 8) * 128, (N2 / 8) * 128, 128);
-            tc::mma_bf16(td, ah, b_h, ID_T, ks > 0 ? 1u : 0u);
-            tc::mma_bf16(td, ah, b_l, ID_T, 1u);
-            tc::mma_bf16(td, al, b_h, ID_T, 1u);
+            const uint64_t bz = tc::sdesc(z + ks * 2 * NGW * 128, NGW * 128, 128);   // [Z_hi | Z_lo]
+            tc::mma_bf16(td, ah, bz, ID_T, ks > 0 ? 1u : 0u);
+            tc::mma_bf16(td, al, bz, ID_T64, 1u);                                    // Tr_lo Z_hi
           }
         };
         if (ok && pwait(B2_MD + sl, ((NH - 1) / 3) & 1)) {   // every phase-A MMA done: ring free
@@ -1882,7 +1880,7 @@ cham_tc_colpass2(const __grid_constant__ CUtensorMap tm_k, const __grid_constant
             tc::fence_after_sync();
             constexpr uint32_t ID_E = tc::idesc_bf16(128, C2, false, false);
             const uint32_t ah = tc::smem_addr(sAh), al = tc::smem_addr(sAl), yh = tc::smem_addr(sY);
-  #pragma unroll 1
+#pragma unroll 1
             for (int ks = 0; ks < NB2 / 16; ++ks) {
               const uint64_t b_h = tc::sdesc(yh + ks * 2 * C2 * 16, C2 * 16, 128);
               tc::mma_bf16(tE, tc::sdesc(ah + ks * 2 * R2 * 16, R2 * 16, 128), b_h, ID_E, ks > 0 ? 1u : 0u);
@@ -1900,25 +1898,17 @@ cham_tc_colpass2(const __grid_constant__ CUtensorMap tm_k, const __grid_constant
             const uint32_t use = (uint32_t)((NH + 2 - s) / 3 + (kt >> 1));   // use of slot s
             if (!pwait(B2_FULL + s, use & 1)) break;
             if (patch_w && !pwait(B2_SPL + s, use & 1)) break;
+            if (kt == 0 && !pwait(B2_ER, 0)) break;   // dH[0] overlaps E: the consumers have read it
             if (kt >= 2 && !pwait(B2_DF + d, ((kt - 2) >> 1) & 1)) break;
             tc::fence_after_sync();
             const uint32_t aw = tc::smem_addr(slot(s));
-            const uint32_t ch = tc::smem_addr(sZh), cl = tc::smem_addr(sZl);
-  #pragma unroll 1
+            const uint32_t cm = tc::smem_addr(sZ);
+#pragma unroll 1
             for (int ks = 0; ks < R2 / 16; ++ks) {
               const uint64_t a = tc::sdesc_sw128(aw + ks * 2048, 16384, 1024);
-              tc::mma_bf16(tDH + 64 * d, a, tc::sdesc(ch + ks * 2 * (N2 / 8) * 128, (N2 / 8) * 128, 128), ID_H,
-                           ks > 0 ? 1u : 0u);
-              tc::mma_bf16(tDH + 64 * d, a, tc::sdesc(cl + ks * 2 * (N2 / 8) * 128, (N2 / 8) * 128, 128), ID_H, 1u);
+              tc::mma_bf16(tDH + 128 * d, a, tc::sdesc(cm + ks * 2 * NGW * 128, NGW * 128, 128), ID_H, ks > 0 ? 1u : 0u);
             }
             tc::commit(&bars[B2_DH + d]);
-            // the W tile has been read: the state tile takes its slot
-            if (!pwait(B2_DH + d, (kt >> 1) & 1)) break;
-            if (!src_identity) {
-              tc::mbar_expect_tx(&bars[B2_SF + s], 32 * 1024);
-              tc::tma_load_2d(slot(s), tm_sr128, j0, (src_row_re + item) * D + kt * KT, &bars[B2_SF + s]);
-              tc::tma_load_2d(slot(s) + 16384, tm_si128, j0, (src_row_im + item) * D + kt * KT, &bars[B2_SF + s]);
-            }
             // tile kt-1's slot, once its store has read it, takes W tile kt+1
             if (kt >= 1 && kt + 1 < NT) {
               const int sp = kt & 1;
@@ -1952,15 +1942,19 @@ cham_tc_colpass2(const __grid_constant__ CUtensorMap tm_k, const __grid_constant
         const int s = h % 3;
         if (!cwait(B2_FULL + s, (h / 3) & 1)) break;
         unsigned char* w = slot(s);
+        if (ring_row >= 0 && tid == 0) {   // the real half as read: chunk c-1's end state, for its readout
+          tc::tma_store_2d(&tm_ring64, j0, ring_row + h * KH, w + 16384);
+          tc::bulk_commit();
+        }
         if (patch_w) zero_bad_rows(w, 1);
         float x[2][8];
-  #pragma unroll
+#pragma unroll
         for (int u = 0; u < 2; ++u) {
           const int e = tid + CONS * u;
           const int i = e % KH, gg = e / KH;        // row i, 8-column group gg (0-3 re, 4-7 im)
           if (src_identity) {
             const int gi = h * KH + i, col = j0 + (gg & 3) * 8;
-  #pragma unroll
+#pragma unroll
             for (int jj = 0; jj < 8; ++jj) x[u][jj] = (gg < 4 && gi == col + jj) ? 1.f : 0.f;
           } else {
             const unsigned char* box = w + (gg < 4 ? 16384 : 24576);
@@ -1971,15 +1965,16 @@ cham_tc_colpass2(const __grid_constant__ CUtensorMap tm_k, const __grid_constant
             x[u][4] = b.x; x[u][5] = b.y; x[u][6] = b.z; x[u][7] = b.w;
           }
         }
-        tc::named_sync(1, CONS);                    // every fp32 value read before the split overwrites it
-  #pragma unroll
+        if (ring_row >= 0 && tid == 0) tc::bulk_wait_read<0>();
+        tc::named_sync(1, CONS);   // every fp32 value (and the ring copy) read before the split overwrites it
+#pragma unroll
         for (int u = 0; u < 2; ++u) {
           const int e = tid + CONS * u;
           const int i = e % KH, gg = e / KH;
           uint4 hv, lv;
           tc::split8(x[u], hv, lv);
-          *reinterpret_cast<uint4*>(w + 16384 + mnmaj(i, gg * 8, N2 / 8)) = hv;
-          *reinterpret_cast<uint4*>(w + 24576 + mnmaj(i, gg * 8, N2 / 8)) = lv;
+          *reinterpret_cast<uint4*>(w + 16384 + mnmaj(i, gg * 8, NGW)) = hv;
+          *reinterpret_cast<uint4*>(w + 16384 + mnmaj(i, N2 + gg * 8, NGW)) = lv;
         }
         tc::fence_proxy_async();
         tc::named_sync(1, CONS);
@@ -1989,16 +1984,19 @@ cham_tc_colpass2(const __grid_constant__ CUtensorMap tm_k, const __grid_constant
       const int sl = (NH - 1) % 3;
       if (ok && cwait(B2_MD + sl, ((NH - 1) / 3) & 1)) {
         tc::fence_after_sync();
-        float z[32];
+        float z[32], zl[32];
         tc::tmem_ld16(tZ + lane_base + 32 * half, z);
         tc::tmem_ld16(tZ + lane_base + 32 * half + 16, z + 16);
-  #pragma unroll
+        tc::tmem_ld16(tZ + lane_base + N2 + 32 * half, zl);
+        tc::tmem_ld16(tZ + lane_base + N2 + 32 * half + 16, zl + 16);
+#pragma unroll
+        for (int j = 0; j < 32; ++j) z[j] += zl[j];
+#pragma unroll
         for (int g4 = 0; g4 < 4; ++g4) {
           uint4 hv, lv;
           tc::split8(z + 8 * g4, hv, lv);
-          const int off = mnmaj(row, 32 * half + 8 * g4, N2 / 8);
-          *reinterpret_cast<uint4*>(sZh + off) = hv;
-          *reinterpret_cast<uint4*>(sZl + off) = lv;
+          *reinterpret_cast<uint4*>(sZ + mnmaj(row, 32 * half + 8 * g4, NGW)) = hv;
+          *reinterpret_cast<uint4*>(sZ + mnmaj(row, N2 + 32 * half + 8 * g4, NGW)) = lv;
         }
         tc::fence_proxy_async();
         tc::fence_before_sync();
@@ -2008,26 +2006,33 @@ cham_tc_colpass2(const __grid_constant__ CUtensorMap tm_k, const __grid_constant
       // ---- phase E: Cm -> operands (ZC: MN-major re | im; slot 0: Re(Cm) K-major, Y)
       if (ok && cwait(B2_MT, 0)) {
         tc::fence_after_sync();
-        float p1r[16], p1i[16], p2r[16], p2i[16];
-        tc::tmem_ld16(tP1 + lane_base + 16 * half, p1r);
-        tc::tmem_ld16(tP1 + lane_base + 32 + 16 * half, p1i);
-        tc::tmem_ld16(tP2 + lane_base + 16 * half, p2r);
-        tc::tmem_ld16(tP2 + lane_base + 32 + 16 * half, p2i);
-        float cr[16], ci[16];
-  #pragma unroll
-        for (int j = 0; j < 16; ++j) { cr[j] = p1r[j] - p2i[j]; ci[j] = p1i[j] + p2r[j]; }
-  #pragma unroll
-        for (int g2 = 0; g2 < 2; ++g2) {
-          uint4 hv, lv;
-          const int jc = 16 * half + 8 * g2;
-          tc::split8(cr + 8 * g2, hv, lv);
-          *reinterpret_cast<uint4*>(sZh + mnmaj(row, jc, N2 / 8)) = hv;
-          *reinterpret_cast<uint4*>(sZl + mnmaj(row, jc, N2 / 8)) = lv;
-          *reinterpret_cast<uint4*>(sAh + kmaj(row, jc, R2)) = hv;
-          *reinterpret_cast<uint4*>(sAl + kmaj(row, jc, R2)) = lv;
-          tc::split8(ci + 8 * g2, hv, lv);
-          *reinterpret_cast<uint4*>(sZh + mnmaj(row, NB2 + jc, N2 / 8)) = hv;
-          *reinterpret_cast<uint4*>(sZl + mnmaj(row, NB2 + jc, N2 / 8)) = lv;
+        // Cm = P1 - i P2 term by term (Re = P1r - P2i, Im = P1i + P2r), each product's two
+        // accumulator halves (hi-operand and lo-operand parts) summed; real part first
+#pragma unroll
+        for (int part = 0; part < 2; ++part) {
+          const int c1 = part == 0 ? 0 : 32, c2 = part == 0 ? 32 : 0;
+          const float sg = part == 0 ? -1.f : 1.f;
+          float cv[16], a[16], b2[16];
+          tc::tmem_ld16(tP1 + lane_base + c1 + 16 * half, a);
+          tc::tmem_ld16(tP1 + lane_base + N2 + c1 + 16 * half, b2);
+#pragma unroll
+          for (int j = 0; j < 16; ++j) cv[j] = a[j] + b2[j];
+          tc::tmem_ld16(tP2 + lane_base + c2 + 16 * half, a);
+          tc::tmem_ld16(tP2 + lane_base + N2 + c2 + 16 * half, b2);
+#pragma unroll
+          for (int j = 0; j < 16; ++j) cv[j] += sg * (a[j] + b2[j]);
+#pragma unroll
+          for (int g2 = 0; g2 < 2; ++g2) {
+            uint4 hv, lv;
+            const int jc = 16 * half + 8 * g2;
+            tc::split8(cv + 8 * g2, hv, lv);
+            *reinterpret_cast<uint4*>(sZ + mnmaj(row, c1 + jc, NGW)) = hv;
+            *reinterpret_cast<uint4*>(sZ + mnmaj(row, N2 + c1 + jc, NGW)) = lv;
+            if (part == 0) {
+              *reinterpret_cast<uint4*>(sAh + kmaj(row, jc, R2)) = hv;
+              *reinterpret_cast<uint4*>(sAl + kmaj(row, jc, R2)) = lv;
+            }
+          }
         }
         {
           const int t = tid % C2, gq = tid / C2;   // 64 tokens x 4 groups of 8 columns
@@ -2045,8 +2050,11 @@ cham_tc_colpass2(const __grid_constant__ CUtensorMap tm_k, const __grid_constant
         float e[32];
         tc::tmem_ld16(tE + lane_base + 32 * half, e);
         tc::tmem_ld16(tE + lane_base + 32 * half + 16, e + 16);
+        tc::fence_before_sync();
+        tc::named_sync(1, CONS);
+        if (tid == 0) tc::mbar_arrive(&bars[B2_ER]);   // E read: the first dH may overwrite it
         float4* Eo = reinterpret_cast<float4*>(Ews + chunk * R2 * C2 + (size_t)row * C2 + 32 * half);
-  #pragma unroll
+#pragma unroll
         for (int t = 0; t < 8; ++t) atomicAdd(Eo + t, make_float4(e[4 * t], e[4 * t + 1], e[4 * t + 2], e[4 * t + 3]));
       }
       // ---- phase B: S_next = S + dH in the slot (thread: one row of one plane), TMA store
@@ -2062,36 +2070,38 @@ cham_tc_colpass2(const __grid_constant__ CUtensorMap tm_k, const __grid_constant
         }
         if (!cwait(B2_DH + d, (kt >> 1) & 1)) break;
         tc::fence_after_sync();
-        float dh[32];
-        tc::tmem_ld16(tDH + 64 * d + lane_base + 32 * half, dh);
-        tc::tmem_ld16(tDH + 64 * d + lane_base + 32 * half + 16, dh + 16);
+        float dh[32], dl[32];
+        tc::tmem_ld16(tDH + 128 * d + lane_base + 32 * half, dh);
+        tc::tmem_ld16(tDH + 128 * d + lane_base + 32 * half + 16, dh + 16);
+        tc::tmem_ld16(tDH + 128 * d + lane_base + N2 + 32 * half, dl);
+        tc::tmem_ld16(tDH + 128 * d + lane_base + N2 + 32 * half + 16, dl + 16);
+#pragma unroll
+        for (int j = 0; j < 32; ++j) dh[j] += dl[j];
         tc::fence_before_sync();
         tc::named_sync(1, CONS);
         if (tid == 0) tc::mbar_arrive(&bars[B2_DF + d]);   // dH[d] may be overwritten
+        // the slot (its W tile read) takes dH, which TMA adds onto the state in place; the
+        // first chunk stores I + dH instead
         unsigned char* box = w + half * 16384;
-        if (src_identity) {
-          const int gi = kt * KT + row;
-  #pragma unroll
-          for (int cc = 0; cc < 8; ++cc) {
-            float v4[4];
-  #pragma unroll
-            for (int jj = 0; jj < 4; ++jj) v4[jj] = dh[4 * cc + jj] + ((!half && gi == j0 + 4 * cc + jj) ? 1.f : 0.f);
-            *reinterpret_cast<float4*>(box + row * 128 + ((cc ^ (row & 7)) << 4)) = make_float4(v4[0], v4[1], v4[2], v4[3]);
-          }
-        } else {
-          if (!cwait(B2_SF + s, (kt >> 1) & 1)) break;
-  #pragma unroll
-          for (int cc = 0; cc < 8; ++cc) {
-            float4* p4 = reinterpret_cast<float4*>(box + row * 128 + ((cc ^ (row & 7)) << 4));
-            const float4 a = *p4;
-            *p4 = make_float4(a.x + dh[4 * cc], a.y + dh[4 * cc + 1], a.z + dh[4 * cc + 2], a.w + dh[4 * cc + 3]);
-          }
+        const int gi = kt * KT + row;
+#pragma unroll
+        for (int cc = 0; cc < 8; ++cc) {
+          float v4[4];
+#pragma unroll
+          for (int jj = 0; jj < 4; ++jj)
+            v4[jj] = dh[4 * cc + jj] + ((src_identity && !half && gi == j0 + 4 * cc + jj) ? 1.f : 0.f);
+          *reinterpret_cast<float4*>(box + row * 128 + ((cc ^ (row & 7)) << 4)) = make_float4(v4[0], v4[1], v4[2], v4[3]);
         }
         tc::fence_proxy_async();
         tc::named_sync(1, CONS);
         if (tid == 0) {
-          tc::tma_store_2d(tm_dr, j0, (dst_row_re + item) * D + kt * KT, w);
-          tc::tma_store_2d(tm_di, j0, (dst_row_im + item) * D + kt * KT, w + 16384);
+          if (src_identity) {
+            tc::tma_store_2d(tm_dr, j0, (dst_row_re + item) * D + kt * KT, w);
+            tc::tma_store_2d(tm_di, j0, (dst_row_im + item) * D + kt * KT, w + 16384);
+          } else {
+            tc::tma_reduce_add_2d(tm_dr, j0, (dst_row_re + item) * D + kt * KT, w);
+            tc::tma_reduce_add_2d(tm_di, j0, (dst_row_im + item) * D + kt * KT, w + 16384);
+          }
           tc::bulk_commit();
           tc::bulk_wait_read<0>();                 // the store has read the slot
           tc::mbar_arrive(&bars[B2_SR + s]);
@@ -2516,13 +2526,16 @@ cham_tc_colpass3(const __grid_constant__ CUtensorMap tm_k, const __grid_constant
 __global__ void __launch_bounds__(WS_THREADS, 2)
 cham_tc_readout_batch(const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
                       const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_ring,
-                      const float* __restrict__ Ews, const unsigned long long* __restrict__ badws,
-                      __nv_bfloat16* __restrict__ out, int S, int D, int nch, int c0, int ring, int b) {
+                      const __grid_constant__ CUtensorMap tm_last, const float* __restrict__ Ews,
+                      const unsigned long long* __restrict__ badws, __nv_bfloat16* __restrict__ out, int S, int D,
+                      int nch, int c0, int ring, int b, int c_last) {
   const int nrb = D / R2;
   const int c = c0 + (int)blockIdx.x / nrb, bx = (int)blockIdx.x % nrb;
   const int item = blockIdx.y;
-  readout2_body(tm_k, tm_v, tm_q, tm_ring, Ews, badws, out, S, D, nch, c, bx, item,
-                ((c % ring) * b + item) * D);
+  // chunk c's end state: its ring slot, or for chunk c_last (if any) tm_last, a [b*D] plane
+  const bool last = c == c_last;
+  readout2_body(tm_k, tm_v, tm_q, last ? tm_last : tm_ring, Ews, badws, out, S, D, nch, c, bx, item,
+                last ? item * D : ((c % ring) * b + item) * D);
 }
 
 // k or v as a [b][S][D] bf16 tensor, boxes of 64 elements x 64 tokens with 128-byte swizzle
@@ -2638,7 +2651,7 @@ int launch_cham_tc(const void* q, const void* k, const void* v, const float* gam
       if (c >= 1 && (c % w.nring == 0 || c == nch)) {
         const int cb = ((c - 1) / w.nring) * w.nring;
         cham_tc_readout_batch<<<dim3((D / R2) * (c - cb), b), WS_THREADS, RW2_SMEM, st>>>(
-            mk, mv, mq, m_ring, w.E, w.bad, (__nv_bfloat16*)out, s, D, nch, cb, w.nring, b);
+            mk, mv, mq, m_ring, m_ring, w.E, w.bad, (__nv_bfloat16*)out, s, D, nch, cb, w.nring, b, -1);
         if ((rc = check_launch("cham_tc_readout_batch"))) return rc;
       }
     }
@@ -2647,33 +2660,30 @@ int launch_cham_tc(const void* q, const void* k, const void* v, const float* gam
     return VERACE_OK;
   }
   if (sched == SCHED_BATCHED) {
-    // column passes two CTAs per SM, readouts batched over up to RING chunks
-    CUtensorMap mq, m_ring, m_ring64, m_him64, m_hi64, m_him128, m_hi128;
-    const size_t plane = (size_t)b * D * D;
+    // column passes two CTAs per SM over groups of up to RING chunks (state in place in
+    // hr / hi), each followed by a readout launch for the chunks whose end states are ready
+    CUtensorMap mq, m_ring, m_ring64, m_hr64, m_hi64, m_hr128, m_hi128;
     if ((rc = make_kv_map(&mq, q, b, s, D)) || (rc = make_state_map(&m_ring, w.ring, w.nring * b, D)) ||
         (rc = make_state_map(&m_ring64, w.ring, w.nring * b, D, KH)) ||
-        (rc = make_state_map(&m_hi64, hi, b, D, KH)) || (rc = make_state_map(&m_hi128, hi, b, D)))
+        (rc = make_state_map(&m_hr64, hr, b, D, KH)) || (rc = make_state_map(&m_hi64, hi, b, D, KH)) ||
+        (rc = make_state_map(&m_hr128, hr, b, D)) || (rc = make_state_map(&m_hi128, hi, b, D)))
       return rc;
-    if (nch >= 2 && ((rc = make_state_map(&m_him64, w.Him, b, D, KH)) ||
-                     (rc = make_state_map(&m_him128, w.Him, b, D))))
-      return rc;
-    if (nch < 2) { m_him64 = m_hi64; m_him128 = m_hi128; }
     VERACE_CUDA(cudaFuncSetAttribute(cham_tc_colpass2, cudaFuncAttributeMaxDynamicSharedMemorySize, CP2_SMEM));
     VERACE_CUDA(cudaFuncSetAttribute(cham_tc_readout_batch, cudaFuncAttributeMaxDynamicSharedMemorySize, RW2_SMEM));
-    // one column-pass launch per group of up to RING chunks (each CTA runs the group's
-    // chunks in turn), then one readout launch for the group from the ring
     for (int cb = 0; cb < nch; cb += w.nring) {
       const int ce = std::min(nch, cb + w.nring);
       cham_tc_colpass2<<<dim3(D / NB2, b), CP2_THREADS, CP2_SMEM, st>>>(
-          mk, mv, m_ring64, m_ring, m_hi64, m_him64, m_hi128, m_him128, w.nring, b, (const __nv_bfloat16*)q, w.T,
-          w.E, w.bad, s, D, nch, cb, ce);
+          mk, mv, m_hr64, m_hi64, m_hr128, m_hi128, m_ring64, w.nring, b, (const __nv_bfloat16*)q, w.T, w.E, w.bad, s,
+          D, nch, cb, ce);
       if ((rc = check_launch("cham_tc_colpass2"))) return rc;
-      cham_tc_readout_batch<<<dim3((D / R2) * (ce - cb), b), WS_THREADS, RW2_SMEM, st>>>(
-          mk, mv, mq, m_ring, w.E, w.bad, (__nv_bfloat16*)out, s, D, nch, cb, w.nring, b);
-      if ((rc = check_launch("cham_tc_readout_batch"))) return rc;
+      // chunk c's end state is copied by chunk c+1's column pass; the last chunk's is hr
+      const int r0 = std::max(cb - 1, 0), r1 = ce == nch ? nch : ce - 1;
+      if (r1 > r0) {
+        cham_tc_readout_batch<<<dim3((D / R2) * (r1 - r0), b), WS_THREADS, RW2_SMEM, st>>>(
+            mk, mv, mq, m_ring, m_hr128, w.E, w.bad, (__nv_bfloat16*)out, s, D, nch, r0, w.nring, b, nch - 1);
+        if ((rc = check_launch("cham_tc_readout_batch"))) return rc;
+      }
     }
-    VERACE_CUDA(cudaMemcpyAsync(hr, w.ring + ((nch - 1) % w.nring) * plane, plane * sizeof(float),
-                                cudaMemcpyDeviceToDevice, st));
     return VERACE_OK;
   }
   if (WS) {

@@ -229,6 +229,12 @@ __device__ __forceinline__ void tma_store_2d(const void* tmap, int x, int y, con
                "r"(y), "r"(smem_addr(smem))
                : "memory");
 }
+// TMA tiled reduce shared -> global: global += smem element-wise (fp32 add for an fp32 map).
+__device__ __forceinline__ void tma_reduce_add_2d(const void* tmap, int x, int y, const void* smem) {
+  asm volatile("cp.reduce.async.bulk.tensor.2d.global.shared::cta.add.tile.bulk_group [%0, {%1, %2}], [%3];" ::"l"(tmap),
+               "r"(x), "r"(y), "r"(smem_addr(smem))
+               : "memory");
+}
 // Order this thread's completed bulk (async-proxy) global writes before later async-proxy reads.
 __device__ __forceinline__ void fence_proxy_async_global() { asm volatile("fence.proxy.async.global;" ::: "memory"); }
 __device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
