@@ -227,11 +227,11 @@ def run_ours(args):
     cham_bytes = (2 * nch - 1) * b * 2 * D * D * 4 + 4 * b * s * D * 2 + 2 * nch * b * 131072
     achieved = cham_bytes / (cham_ms * 1e-3) / 1e9
     cham_flop = 18.0 * D * D * b * s              # 9 D² MAC per token (8 state update + 1 readout)
-    # DRAM bytes per (item, chunk) measured by ncu at b=16, s=256 (batched schedule:
-    # profiles/cham_tc_colpass2_b16_s256.md 304.6 MB per column-pass launch;
-    # cham_tc_readout_batch_b16_s256.md 305.6 MB per 4-chunk readout launch;
-    # cham_tc_prep_ws_b16_s256.md 16.8 MB per 64 item-chunks), scaled to this call
-    traffic = (304.6e6 / 16 + 305.6e6 / 64 + 16.8e6 / 64) * b * nch
+    # DRAM bytes per (item, chunk) measured by ncu at b=16, s=256 (batched schedule, 64
+    # item-chunks per launch: profiles/cham_tc_colpass2_b16_s256.md 884.2 MB per column-pass
+    # launch; cham_tc_readout_batch_b16_s256.md 304.6 MB per readout launch;
+    # cham_tc_prep_ws_b16_s256.md 16.8 MB per prep launch), scaled to this call
+    traffic = (884.2e6 + 304.6e6 + 16.8e6) / 64 * b * nch
     result = {
         "metric": METRIC, "value": world * tokens_per_step / (ms * 1e-3), "unit": UNIT,
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
@@ -242,8 +242,8 @@ def run_ours(args):
                    "global_batch": b * world, "seq_len": s, "layers": c["layers"],
                    "parallelism": f"dp{world} (batch shards, no collective)",
                    "l2": "no flush: per-step working set (weights 190 MB + activations) > 126 MB L2"},
-        "roofline": {"kernel": "verace_cham_scan (cham_tc_prep_ws, one cham_tc_colpass2 per 64-token chunk, "
-                               "cham_tc_readout_batch per 8 chunks)",
+        "roofline": {"kernel": "verace_cham_scan (cham_tc_prep_ws, then per group of 8 chunks one cham_tc_colpass2 "
+                               "and one cham_tc_readout_batch)",
                      "bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
                      "frac": achieved / hbm, "traffic": traffic,
                      "bytes_per_launch": cham_bytes, "ms_per_launch": cham_ms,
