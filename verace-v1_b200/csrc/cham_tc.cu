@@ -49,7 +49,7 @@ constexpr int Z_TILE = R2 * N2 * 2;        // 16 KB: 128 x 64 bf16
 constexpr int CA_TILE = R2 * NB2 * 2;      //  8 KB: 128 x 32 bf16
 constexpr int Y_TILE = C2 * NB2 * 2;       //  4 KB: 64 tokens x 32 columns bf16
 
-constexpr int RING = 8;          // chunk end states kept for one batched readout launch
+constexpr int RING = 8;          // chunks per column-pass group; the ring keeps two groups' end states
 
 struct TcWs {
   unsigned char* T;          // [b][nch][4][T_TILE]: Tr_hi, Tr_lo, Ti_hi, Ti_lo
@@ -73,7 +73,7 @@ size_t tc_ws_layout(int b, int s, int D, TcWs* w, char* base) {
   const bool ping = nch >= 2;
   t.Hre = (float*)take(ping ? (size_t)b * D * D * sizeof(float) : 0);
   t.Him = (float*)take(ping ? (size_t)b * D * D * sizeof(float) : 0);
-  t.nring = (int)std::min<size_t>(nch, RING);
+  t.nring = (int)std::min<size_t>(nch, 2 * RING);
   t.ring = (float*)take((size_t)t.nring * b * D * D * sizeof(float));
   t.cm = (unsigned char*)take((size_t)2 * b * (D / 64) * (64 * 1024));
   if (w) *w = t;
@@ -1423,7 +1423,7 @@ readout2_body(const CUtensorMap& tm_k, const CUtensorMap& tm_v, const CUtensorMa
         }
       }
     }
-  } else {
+  } else if (warp < 8) {   // (a launch shared with the column pass has a tenth, idle warp)
     const uint32_t lane_base = (uint32_t)(32 * (warp & 3)) << 16;
     const int row = 32 * (warp & 3) + lane, half = warp >> 2;
     bool ok = true;
@@ -1722,13 +1722,11 @@ constexpr int CP2_THREADS = CONS + 64;    // consumers + producer warp (MMAs, ph
 enum { B2_FULL = 0, B2_SPL = 3, B2_MD = 6, B2_TT = 9, B2_ZR = 10, B2_P1 = 11, B2_MT = 12, B2_CR = 13, B2_ME = 14,
        B2_DH = 15, B2_DF = 17, B2_ER = 19, B2_SR = 21, N_BARS2 = 23 };
 
-__global__ void __launch_bounds__(CP2_THREADS, 2)
-cham_tc_colpass2(const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
-                 const __grid_constant__ CUtensorMap tm_hr64, const __grid_constant__ CUtensorMap tm_hi64,
-                 const __grid_constant__ CUtensorMap tm_hr128, const __grid_constant__ CUtensorMap tm_hi128,
-                 const __grid_constant__ CUtensorMap tm_ring64, int nring, int b, const __nv_bfloat16* __restrict__ q,
-                 const unsigned char* __restrict__ Tws, float* __restrict__ Ews,
-                 const unsigned long long* __restrict__ badws, int S, int D, int nch, int c0, int c1) {
+__device__ __forceinline__ void
+colpass2_body(const CUtensorMap& tm_k, const CUtensorMap& tm_v, const CUtensorMap& tm_hr64, const CUtensorMap& tm_hi64,
+              const CUtensorMap& tm_hr128, const CUtensorMap& tm_hi128, const CUtensorMap& tm_ring64, int nring, int b,
+              const __nv_bfloat16* __restrict__ q, const unsigned char* __restrict__ Tws, float* __restrict__ Ews,
+              const unsigned long long* __restrict__ badws, int S, int D, int nch, int c0, int c1, int item, int jb) {
   extern __shared__ __align__(1024) unsigned char smc[];
   uint64_t* bars = reinterpret_cast<uint64_t*>(smc + CP2_BAR);
   uint32_t* tslot = reinterpret_cast<uint32_t*>(smc + CP2_BAR + 8 * N_BARS2);
@@ -1741,7 +1739,7 @@ cham_tc_colpass2(const __grid_constant__ CUtensorMap tm_k, const __grid_constant
   unsigned char* sY = smc + 2 * CA_TILE;
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int item = blockIdx.y, j0 = blockIdx.x * NB2;
+  const int j0 = jb * NB2;
   const int NH = D / KH, NT = D / KT;
 
   if (warp == 0) tc::tmem_alloc(tslot, 256);
@@ -2131,6 +2129,29 @@ cham_tc_colpass2(const __grid_constant__ CUtensorMap tm_k, const __grid_constant
   tc::fence_before_sync();
   __syncthreads();
   if (warp == 0) tc::tmem_dealloc(tbase, 256);
+}
+
+// One launch per group of chunks: CTAs [0, D/32 * b) run the column pass of chunks
+// [c0, c1) (item-major); the rest run the readouts of chunks [r0, r0 + nr), whose end
+// states the previous group left in the ring, on the SM slots the column pass leaves free.
+__global__ void __launch_bounds__(CP2_THREADS, 2)
+cham_tc_colpass2(const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
+                 const __grid_constant__ CUtensorMap tm_hr64, const __grid_constant__ CUtensorMap tm_hi64,
+                 const __grid_constant__ CUtensorMap tm_hr128, const __grid_constant__ CUtensorMap tm_hi128,
+                 const __grid_constant__ CUtensorMap tm_ring64, const __grid_constant__ CUtensorMap tm_q,
+                 const __grid_constant__ CUtensorMap tm_ring128, int nring, int b, const __nv_bfloat16* __restrict__ q,
+                 const unsigned char* __restrict__ Tws, float* __restrict__ Ews,
+                 const unsigned long long* __restrict__ badws, __nv_bfloat16* __restrict__ out, int S, int D, int nch,
+                 int c0, int c1, int r0, int nr) {
+  const int ncol = D / NB2, nrb = D / R2;
+  const int bid = blockIdx.x;
+  if (bid < ncol * b) {
+    colpass2_body(tm_k, tm_v, tm_hr64, tm_hi64, tm_hr128, tm_hi128, tm_ring64, nring, b, q, Tws, Ews, badws, S, D, nch,
+                  c0, c1, bid / ncol, bid % ncol);
+  } else {
+    const int r = bid - ncol * b, item = r / (nrb * nr), c = r0 + (r % (nrb * nr)) / nrb, bx = r % nrb;
+    readout2_body(tm_k, tm_v, tm_q, tm_ring128, Ews, badws, out, S, D, nch, c, bx, item, ((c % nring) * b + item) * D);
+  }
 }
 
 // ---------------------------------------------------------------------------------
@@ -2660,8 +2681,11 @@ int launch_cham_tc(const void* q, const void* k, const void* v, const float* gam
     return VERACE_OK;
   }
   if (sched == SCHED_BATCHED) {
-    // column passes two CTAs per SM over groups of up to RING chunks (state in place in
-    // hr / hi), each followed by a readout launch for the chunks whose end states are ready
+    // Column passes two CTAs per SM over groups of RING chunks, the state in place in
+    // hr / hi.  Chunk c's end state is copied into the ring by chunk c+1's column pass
+    // (the last chunk's is hr), so group g's launch also runs the readouts of the chunks
+    // group g-1 completed, in the SM slots its column pass leaves free; one readout
+    // launch finishes the sequence.  The ring holds two groups, so the two never meet.
     CUtensorMap mq, m_ring, m_ring64, m_hr64, m_hi64, m_hr128, m_hi128;
     if ((rc = make_kv_map(&mq, q, b, s, D)) || (rc = make_state_map(&m_ring, w.ring, w.nring * b, D)) ||
         (rc = make_state_map(&m_ring64, w.ring, w.nring * b, D, KH)) ||
@@ -2670,20 +2694,19 @@ int launch_cham_tc(const void* q, const void* k, const void* v, const float* gam
       return rc;
     VERACE_CUDA(cudaFuncSetAttribute(cham_tc_colpass2, cudaFuncAttributeMaxDynamicSharedMemorySize, CP2_SMEM));
     VERACE_CUDA(cudaFuncSetAttribute(cham_tc_readout_batch, cudaFuncAttributeMaxDynamicSharedMemorySize, RW2_SMEM));
-    for (int cb = 0; cb < nch; cb += w.nring) {
-      const int ce = std::min(nch, cb + w.nring);
-      cham_tc_colpass2<<<dim3(D / NB2, b), CP2_THREADS, CP2_SMEM, st>>>(
-          mk, mv, m_hr64, m_hi64, m_hr128, m_hi128, m_ring64, w.nring, b, (const __nv_bfloat16*)q, w.T, w.E, w.bad, s,
-          D, nch, cb, ce);
+    int r0 = 0;   // first chunk not read out yet
+    for (int cb = 0; cb < nch; cb += RING) {
+      const int ce = std::min(nch, cb + RING);
+      const int nr = std::max(cb - 1, 0) - r0;   // chunks [r0, cb - 1) have their end states in the ring
+      cham_tc_colpass2<<<(D / NB2) * b + (D / R2) * nr * b, CP2_THREADS, CP2_SMEM, st>>>(
+          mk, mv, m_hr64, m_hi64, m_hr128, m_hi128, m_ring64, mq, m_ring, w.nring, b, (const __nv_bfloat16*)q, w.T,
+          w.E, w.bad, (__nv_bfloat16*)out, s, D, nch, cb, ce, r0, nr);
       if ((rc = check_launch("cham_tc_colpass2"))) return rc;
-      // chunk c's end state is copied by chunk c+1's column pass; the last chunk's is hr
-      const int r0 = std::max(cb - 1, 0), r1 = ce == nch ? nch : ce - 1;
-      if (r1 > r0) {
-        cham_tc_readout_batch<<<dim3((D / R2) * (r1 - r0), b), WS_THREADS, RW2_SMEM, st>>>(
-            mk, mv, mq, m_ring, m_hr128, w.E, w.bad, (__nv_bfloat16*)out, s, D, nch, r0, w.nring, b, nch - 1);
-        if ((rc = check_launch("cham_tc_readout_batch"))) return rc;
-      }
+      r0 += nr;
     }
+    cham_tc_readout_batch<<<dim3((D / R2) * (nch - r0), b), WS_THREADS, RW2_SMEM, st>>>(
+        mk, mv, mq, m_ring, m_hr128, w.E, w.bad, (__nv_bfloat16*)out, s, D, nch, r0, w.nring, b, nch - 1);
+    if ((rc = check_launch("cham_tc_readout_batch"))) return rc;
     return VERACE_OK;
   }
   if (WS) {
