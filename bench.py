@@ -17,9 +17,11 @@ Unit: token-layers/s (one token through SSSD + CHAM of one layer).
 
 Decode (reported under "decode"): the same 12 layers, 64 items per
 GPU, a 1024-token prompt prefilled with the scans, then 256 single-token steps with
-teacher-forced random ids, each step one CUDA graph of the layer glue and the fused
-decode kernels (verace_decode_step) that update the resident SSSD and CHAM states in
-place.  Reported as µs per step and µs per token (= step / 64).
+teacher-forced random ids, each step one CUDA graph of the layer glue and the decode
+kernels that update the resident states in place (verace_decode_step for the SSSD heads;
+verace_decode_cham_lazy for the holograms: one read of each hologram per step, the rank-2
+updates deferred and folded in every 8th step).  Reported as µs per step and µs per token
+(= step / 64).
 
 Multi-GPU (torchrun, one rank per GPU): each rank runs the full config-2 batch on its
 own items (weak scaling: batch shards, no collective on the data path); time is the
@@ -42,7 +44,7 @@ sys.path.insert(0, ROOT)
 METRIC = "SSSD+CHAM scan tokens/s at 1/2/4/8 B200 + % roofline; decode step µs/token"
 UNIT = "token-layers/s"
 CFG = dict(layers=12, batch=8, seq=2048, hidden=1024, heads=8, head_dim=128, holo=1024, vocab=32000)
-DEC = dict(batch=64, prompt=1024, steps=256)
+DEC = dict(batch=64, prompt=1024, steps=256, pending=8)
 
 
 def _load_package():
@@ -280,7 +282,7 @@ def run_decode(args, layers, embed, V, dev, rank, barrier, max_over_ranks):
     gen = torch.Generator().manual_seed(100 + rank)
     prompt = torch.randint(0, c["vocab"], (b, P), generator=gen).to(dev)
     toks = torch.randint(0, c["vocab"], (b, n + args.warmup), generator=gen).to(dev)
-    st = V.DecodeState(nl, b, nh, d, D, device=dev)
+    st = V.DecodeState(nl, b, nh, d, D, device=dev, pending_depth=DEC["pending"])
     with torch.no_grad():
         x = embed(prompt).contiguous()
         nrm = V.rmsnorm(x, layers[0]["sssd_norm"])
@@ -329,6 +331,8 @@ def run_decode(args, layers, embed, V, dev, rank, barrier, max_over_ranks):
             st.psi.copy_(saved[0])
             st.H_real.copy_(saved[1])
             st.H_imag.copy_(saved[2])
+            if st.P > 0:
+                st.pending.zero_()
 
         for i in range(args.warmup):
             tok.copy_(toks[:, n + i])
@@ -347,7 +351,9 @@ def run_decode(args, layers, embed, V, dev, rank, barrier, max_over_ranks):
         if V.device_status(dev) != 0:
             raise RuntimeError("decode steps reported a device status")
 
-        # the dominant kernel alone: CHAM half of verace_decode_step, one launch per layer
+        # the dominant kernel alone: the CHAM decode step (deferred updates: one read pass
+        # over the hologram per step, the pending factors folded in every P-th step), timed
+        # over P steps per layer so that each layer folds once
         g1 = torch.Generator().manual_seed(7)
         nrm = torch.nn.functional.normalize
         cq, ck, cv = (nrm(torch.randn(b, D, generator=g1), dim=-1).to(dev, torch.bfloat16) for _ in range(3))
@@ -357,7 +363,7 @@ def run_decode(args, layers, embed, V, dev, rank, barrier, max_over_ranks):
         torch.cuda.synchronize()
         e2 = torch.cuda.Event(enable_timing=True)
         e3 = torch.cuda.Event(enable_timing=True)
-        reps = 3
+        reps = max(st.P, 1)
         e2.record()
         for _ in range(reps):
             for l in range(nl):
@@ -369,20 +375,24 @@ def run_decode(args, layers, embed, V, dev, rank, barrier, max_over_ranks):
     del graph, saved, st
     torch.cuda.empty_cache()
     hbm = _peaks()[0]
-    cham_bytes = 2 * 2 * b * D * D * 4                  # Hr, Hi read once and written once
+    # Hr, Hi read once per step and written once per P steps (deferred updates)
+    pdepth = DEC["pending"]
+    cham_bytes = 2 * b * D * D * 4 * (1 + 1 / pdepth)
     sssd_bytes = 2 * b * nh * d * d * 4
     w_bytes = sum(p.numel() * p.element_size() for L in layers for p in L.parameters())
     step_bytes = nl * (cham_bytes + sssd_bytes) + w_bytes
     achieved = cham_bytes / (us_launch * 1e-6) / 1e9
     return {
         "workload": f"config 3: 12-layer decode, b={b} per GPU, prompt {P} (prefilled by the scans), "
-                    f"{n} single-token steps (teacher-forced random ids), bf16, one CUDA graph per step",
+                    f"{n} single-token steps (teacher-forced random ids), bf16, one CUDA graph per step, "
+                    f"hologram updates deferred {DEC['pending']} steps",
         "us_per_step": us_step, "us_per_token": us_step / b, "steps": n, "batch": b,
         "readout": "unitary (Re(H q); exact for unitary holograms)",
         "gpu_launches_per_step": launches_per_step,
         "step_hbm_roofline_us": step_bytes / (hbm * 1e9) * 1e6,
         "step_frac_of_hbm_roofline": step_bytes / (hbm * 1e9) * 1e6 / us_step,
-        "roofline": {"kernel": "decode_step_kernel (CHAM half: hologram read + update + write, readout)",
+        "roofline": {"kernel": "lazy_pre_kernel + lazy_cham_kernel (CHAM decode step: one read of the hologram, "
+                               "the pending rank-2 factors folded in every 8th step)",
                      "bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
                      "frac": achieved / hbm, "traffic": None, "bytes_per_launch": cham_bytes,
                      "us_per_launch": us_launch},

@@ -175,6 +175,26 @@ VERACE_API int verace_mixer_prologue(const void* y, long long ld, void* q, void*
                                      int gate_cols, int silu_v, int dtype, void* stream);
 
 /* ------------------------------------------------------------------------------
+ * Lazy CHAM decode (unitary readout): the hologram's rank-2 step updates are kept as
+ * pending factors, H = S + sum_j [k_j v_j] B_j with S the stored planes, and folded
+ * into S every P steps, so that a step reads S once instead of reading it twice and
+ * writing it.  Same step and readout as verace_decode_step with
+ * VERACE_DECODE_UNITARY, up to fp32 rounding order.
+ * pending: verace_decode_pending_bytes(b, D, P) bytes per layer, zero-filled before the
+ *          first step (an empty list); S is the true state only after
+ *          verace_decode_cham_flush.  P in [1, 16].
+ * Supports D % 32 == 0, D <= 2048; calls sharing a workspace must not overlap.
+ * ---------------------------------------------------------------------------- */
+VERACE_API size_t verace_decode_lazy_workspace(int b, int D);
+VERACE_API size_t verace_decode_pending_bytes(int b, int D, int P);
+VERACE_API int verace_decode_cham_lazy(const void* cham_q, const void* cham_k, const void* cham_v,
+                                       const float* gamma, float* h_re, float* h_im, void* pending, int P,
+                                       void* cham_out, int b, int D, int dtype, void* workspace,
+                                       size_t workspace_bytes, void* stream);
+VERACE_API int verace_decode_cham_flush(float* h_re, float* h_im, void* pending, int P, int b, int D,
+                                        void* stream);
+
+/* ------------------------------------------------------------------------------
  * Block glue: the RMSNorms and residual adds around the two mixers
  * (verace_v1/modules/backbone.py: h <- h + SSSD(RMSNorm(h)); h <- h + CHAM(RMSNorm(h));
  * SSSDAttention's per-head RMSNorm, sssd_attention.py:177-182; CHAM's output RMSNorm,

@@ -104,3 +104,20 @@ def test_norm_glue_rejects_bad_arguments_without_a_device():
     assert L.verace_add_rmsnorm(fake, fake, 0, None, 0.0, None, 0.0, None, 4, 4096, 1, None) == 2
     assert L.verace_add_rmsnorm(None, fake, 0, None, 0.0, None, 0.0, None, 4, 64, 1, None) == 1
     assert "NULL" in _err()
+
+
+def test_lazy_decode_rejects_bad_arguments_without_a_device():
+    L = _lib.lib()
+    fake = ctypes.c_void_p(256)
+    ws = L.verace_decode_lazy_workspace(4, 1024)
+    assert ws > L.verace_decode_lazy_workspace(4, 512) > 0
+    assert L.verace_decode_pending_bytes(4, 1024, 8) == 256 + 4 * 8 * 6 * 1024 * 4
+    f = [fake] * 7
+    assert L.verace_decode_cham_lazy(*f, 0, fake, 4, 1024, 1, fake, ws, None) == 1 and "pending depth" in _err()
+    assert L.verace_decode_cham_lazy(*f, 17, fake, 4, 1024, 1, fake, ws, None) == 1
+    assert L.verace_decode_cham_lazy(*f, 8, fake, 4, 80, 1, fake, ws, None) == 2 and "holographic" in _err()
+    assert L.verace_decode_cham_lazy(*f, 8, fake, 4, 1024, 1, fake, 16, None) == 4 and "workspace" in _err()
+    assert L.verace_decode_cham_lazy(*f, 8, fake, 4, 1024, 7, fake, ws, None) == 1 and "dtype" in _err()
+    assert L.verace_decode_cham_lazy(*f, 8, fake, 0, 1024, 1, None, 0, None) == 0    # nothing to do
+    assert L.verace_decode_cham_flush(fake, fake, fake, 0, 4, 1024, None) == 1
+    assert L.verace_decode_cham_flush(fake, fake, fake, 8, 0, 1024, None) == 0

@@ -7,6 +7,8 @@ the CHAM readout's Newton-Schulz retraction.  Also: several steps in a row, incr
 decode against a full-sequence scan (the reference's
 tests/test_incremental_generation.py:27-57 property), the first-order readout on a
 hologram that is not unitary, the drift status, non-finite tokens, and shape limits.
+And the deferred-update CHAM step (verace_decode_cham_lazy) against the eager unitary
+step, across folds of the pending list.
 
 Tolerances: relative Frobenius <= 1e-4 for fp32 outputs and for every fp32 state,
 <= 2e-2 for bf16 outputs.
@@ -212,6 +214,7 @@ def test_incremental_decode_matches_full_scan(dtype):
         so.append(o1)
         co.append(o2)
     assert V.device_status() == 0
+    st.flush()   # bf16 takes the unitary readout with deferred hologram updates
     tol = 1e-4 if dtype == torch.float32 else 2e-2
     assert rel_fro(to_np(torch.stack(so, 1)), to_np(so_full[:, s0:])) <= tol
     assert rel_fro(to_np(torch.stack(co, 1)), to_np(co_full[:, s0:])) <= tol
@@ -245,3 +248,51 @@ def test_unsupported_shapes_are_refused():
         V.launch_decode_step((sq[:, 0], sk[:, 0], sv[:, 0], dl[:, 0], psi), None)
     with pytest.raises(ValueError):
         V.launch_decode_step((sq[:, 0], sk[:, 0], sv[:, 0], dl[:, 0], psi), None, mode="exact")
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("b,D,P", [(3, 256, 4), (2, 1024, 8), (1, 128, 1)])
+def test_lazy_cham_decode_matches_eager_unitary_steps(dtype, b, D, P):
+    """21 steps from a unitary hologram (folds every P steps; one non-finite token):
+    the deferred-update step's outputs and, after a flush, its planes equal the eager
+    unitary step's to fp32 rounding order."""
+    n = 21
+    q, k, v, g = random_cham_inputs(b, n, D, seed=790 + D + P, dtype=dtype)
+    k[0, 5, 3] = float("nan")
+    hr0, hi0 = _holo(_unitary(b, D, 791))
+    er, ei = hr0.clone(), hi0.clone()
+    lr, li = hr0.clone(), hi0.clone()
+    pend = V.pending_storage(b, D, P)
+    for t in range(n):
+        _, ye = V.launch_decode_step(None, (q[:, t], k[:, t], v[:, t], g[:, t], er, ei), mode="unitary")
+        yl = V.launch_decode_cham_lazy(q[:, t], k[:, t], v[:, t], g[:, t], lr, li, pend, P)
+        assert yl.dtype == dtype and tuple(yl.shape) == (b, D)
+        assert rel_fro(to_np(yl), to_np(ye)) <= (2e-6 if dtype == torch.float32 else 1e-2), t
+    assert V.device_status() == 0
+    V.flush_pending(lr, li, pend, P)
+    assert rel_fro(to_np(lr) + 1j * to_np(li), to_np(er) + 1j * to_np(ei)) <= 2e-6
+    V.flush_pending(lr, li, pend, P)   # an empty list: no change
+    assert rel_fro(to_np(lr) + 1j * to_np(li), to_np(er) + 1j * to_np(ei)) <= 2e-6
+
+
+def test_decode_state_defers_unitary_steps_and_flushes_for_layer_states():
+    b, h, d, D, n = 2, 2, 64, 256, 11
+    sq, sk, sv, dl = random_sssd_inputs(b, n, h, d, seed=795, dtype=torch.bfloat16)
+    cq, ck, cv, g = random_cham_inputs(b, n, D, seed=796, dtype=torch.bfloat16)
+    lazy = V.DecodeState(2, b, h, d, D, pending_depth=4)
+    eager = V.DecodeState(2, b, h, d, D, pending_depth=0)
+    for t in range(n):
+        for l in range(2):
+            a = lazy.step(l, (sq[:, t], sk[:, t], sv[:, t], dl[:, t]), (cq[:, t], ck[:, t], cv[:, t], g[:, t]))
+            e = eager.step(l, (sq[:, t], sk[:, t], sv[:, t], dl[:, t]), (cq[:, t], ck[:, t], cv[:, t], g[:, t]))
+            assert rel_fro(to_np(a[0]), to_np(e[0])) <= 1e-6 and rel_fro(to_np(a[1]), to_np(e[1])) <= 1e-2
+    ls = lazy.layer_states()           # folds the pending factors in
+    for l in range(2):
+        H = to_np(lazy.H_real[l]) + 1j * to_np(lazy.H_imag[l])
+        He = to_np(eager.H_real[l]) + 1j * to_np(eager.H_imag[l])
+        assert rel_fro(H, He) <= 2e-6
+    assert torch.equal(ls[1][0][1][0], lazy.H_real[1, 0:1])
+    # an eager (first-order) step after deferred ones folds the list first
+    o_l = lazy.step_cham(0, cq[:, 0].float(), ck[:, 0].float(), cv[:, 0].float(), g[:, 0], mode="first_order")
+    o_e = eager.step_cham(0, cq[:, 0].float(), ck[:, 0].float(), cv[:, 0].float(), g[:, 0], mode="first_order")
+    assert rel_fro(to_np(o_l), to_np(o_e)) <= 1e-5

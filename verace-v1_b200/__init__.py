@@ -8,12 +8,14 @@ Public surface (mirrors the reference package verace_v1 for this path):
     launch_cham_update / launch_cham_triton_update
     rmsnorm, add_rmsnorm                             (block glue: RMSNorm, residual + RMSNorm)
     DecodeState, launch_decode_step, device_status   (batched incremental decode)
+    launch_decode_cham_lazy, flush_pending, pending_storage (deferred hologram updates)
 The kernels live in libverace_b200.so (C ABI: include/verace_b200.h), built by
 build.py; nothing here falls back to CPU or Python arithmetic.
 """
 from .kernels import (add_rmsnorm, cham_retract, launch_cham_triton_update, launch_cham_update,
                       launch_sssd_scan, launch_sssd_triton_scan, rmsnorm)
-from .decode import DecodeState, device_status, launch_decode_step
+from .decode import (DecodeState, device_status, flush_pending, launch_decode_cham_lazy, launch_decode_step,
+                     pending_storage)
 from .sssd_attention import SSSDAttention
 from .cham_memory import ContinuousHolographicMemory, newton_schulz_unitary_retraction
 
@@ -21,5 +23,5 @@ __all__ = [
     "SSSDAttention", "ContinuousHolographicMemory", "newton_schulz_unitary_retraction",
     "launch_sssd_scan", "launch_sssd_triton_scan", "launch_cham_update",
     "launch_cham_triton_update", "cham_retract", "DecodeState", "launch_decode_step",
-    "device_status", "rmsnorm", "add_rmsnorm",
+    "device_status", "rmsnorm", "add_rmsnorm", "launch_decode_cham_lazy", "flush_pending", "pending_storage",
 ]

@@ -610,9 +610,11 @@ extern "C" int verace_device_status(void* stream) {
   rc = sssd_tc_read_status(&status2);
   if (rc) return rc;
   status |= status2;
-  unsigned int dstat = 0;
+  unsigned int dstat = 0;   // bit 0: a hologram far from unitary; bit 1: a decode wait gave up
   rc = decode_read_status(&dstat);
   if (rc) return rc;
+  if (dstat & 2u) status = 1;
+  dstat &= 1u;
   VERACE_REQUIRE(status == 0, VERACE_ERR_TIMEOUT,
                  "a bounded device-side wait gave up (tensor-core completion never arrived)");
   VERACE_REQUIRE(dstat == 0, VERACE_ERR_STATE,

@@ -39,6 +39,8 @@
 // finish sums the stripes' partials in stripe order and writes y.  No CTA waits on
 // another.
 #include "common.cuh"
+#include "tc.cuh"
+#include "tmap.cuh"
 
 namespace verace {
 
@@ -82,6 +84,9 @@ __device__ __forceinline__ float warp_sum(float x) {
 }
 
 __device__ __forceinline__ float& comp(float4& v, int j) {
+  return j == 0 ? v.x : (j == 1 ? v.y : (j == 2 ? v.z : v.w));
+}
+__device__ __forceinline__ float compc(const float4& v, int j) {
   return j == 0 ? v.x : (j == 1 ? v.y : (j == 2 ? v.z : v.w));
 }
 
@@ -421,6 +426,397 @@ __device__ void cham_part(const DecodeArgs& A, int unit) {
   }
 }
 
+// ------------------------------------------------------------------------- lazy CHAM
+// Deferred hologram updates (unitary readout).  The stored state S lags the true state by
+// the pending rank-2 factors of up to P earlier steps:
+//     H = S + sum_j A_j B_j,   A_j = [k_j v_j] (D x 2, real),   B_j = N_j [k_jᵀH_j; v_jᵀH_j]
+// (2 x D, complex; H_j the state before step j).  A step needs kᵀH, vᵀH and Re(H' q):
+//     kᵀH = kᵀS + sum_j (kᵀk_j) B_j0 + (kᵀv_j) B_j1,      likewise vᵀH,
+//     Re(H' q) = S_re q + sum_j (k_j Re(B_j0 q) + v_j Re(B_j1 q)) + k Re(B0' q) + v Re(B1' q)
+// with B' = N [kᵀH; vᵀH] the step's new factor, so one read pass over S suffices.  A step
+// that finds all P slots taken first folds them into S during its pass (read + write) and
+// starts the list again with its own factor.  Exact up to fp32 rounding order.
+// Pending storage per item: count (int) | A [P][2][D] | B [P][4][D] (row 0 re, im; row 1 re, im).
+constexpr int LP_MAX = 16;
+
+struct LazyArgs {
+  const void* cq; const void* ck; const void* cv; const float* gamma;
+  float* hr; float* hi; void* cout;
+  int* pcount;                 // [b]
+  float* pa;                   // [b][P][2][D]
+  float* pb;                   // [b][P][4][D]
+  float* g;                    // [b][LP_MAX][4]: kᵀk_j, kᵀv_j, vᵀk_j, vᵀv_j
+  float* bq;                   // [b][LP_MAX][2]: Re(B_j0 q), Re(B_j1 q)
+  float* part;                 // [b][D/32][D] readout partials
+  float* cqp;                  // [b][D/32][4] per stripe: kᵀH q (re, im), vᵀH q (re, im)
+  unsigned int* cnt;           // [b]
+  int b, D, P;
+};
+
+// The dot products between this step's k, v, q and the pending factors: one CTA per
+// (item, factor slot) (slots past the item's count return at once), each thread a few
+// rows of the six contiguous vectors, then a block reduction.
+template <typename T>
+__global__ void __launch_bounds__(DT) lazy_pre_kernel(LazyArgs A) {
+  __shared__ float red[DT / 32][6];
+  const int D = A.D, P = A.P;
+  const int item = blockIdx.x / P, j = blockIdx.x % P;
+  const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
+  const int p = A.pcount[item];
+  if (p >= P || j >= p) return;       // a folding step needs none of them
+  const size_t voff = (size_t)item * D;
+  const float* a0 = A.pa + ((size_t)item * P + j) * 2 * D;
+  const float* a1 = a0 + D;
+  const float* b0 = A.pb + ((size_t)item * P + j) * 4 * D;   // Re(B_j0)
+  const float* b1 = b0 + 2 * (size_t)D;                       // Re(B_j1)
+  float x[6] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f};   // k.k_j, k.v_j, v.k_j, v.v_j, Re(B_j0) q, Re(B_j1) q
+#pragma unroll 4
+  for (int i = tid; i < D; i += DT) {
+    const float kx = ld1<T>(A.ck, voff + i), vx = ld1<T>(A.cv, voff + i), qx = ld1<T>(A.cq, voff + i);
+    const float y0 = a0[i], y1 = a1[i];
+    x[0] += kx * y0; x[1] += kx * y1; x[2] += vx * y0; x[3] += vx * y1;
+    x[4] += b0[i] * qx; x[5] += b1[i] * qx;
+  }
+#pragma unroll
+  for (int e = 0; e < 6; ++e) {
+    x[e] = warp_sum(x[e]);
+    if (lane == 0) red[w][e] = x[e];
+  }
+  __syncthreads();
+  if (tid < 6) {
+    float t = 0.f;
+#pragma unroll
+    for (int ww = 0; ww < DT / 32; ++ww) t += red[ww][tid];
+    if (tid < 4) A.g[((size_t)item * LP_MAX + j) * 4 + tid] = t;
+    else A.bq[((size_t)item * LP_MAX + j) * 2 + (tid - 4)] = t;
+  }
+}
+
+// The stripe streams through NSTG shared-memory stages of 64 rows (re box 8 KB | im box
+// 8 KB, 128-byte rows, no swizzle), loaded by TMA: thread 0 keeps every stage in flight,
+// so the read pass is not limited by the loads a thread can hold in registers.  A
+// folding step updates each stage in place and TMA-stores it back.
+constexpr int LROWS = 64;                    // rows per stage
+constexpr int NSTG = 5;                      // stages
+constexpr int LSTAGE = 2 * LROWS * CWD * 4;  // 16 KB
+// dynamic smem: stages | A rows of the stage (fold steps) [LP_MAX][2][LROWS] | ks [D] | vs [D] | barriers
+constexpr int LAS_OFF = NSTG * LSTAGE;
+constexpr int LKS_OFF = LAS_OFF + LP_MAX * 2 * LROWS * 4;
+size_t lazy_smem(int D) { return LKS_OFF + 2 * (size_t)D * 4 + 8 * NSTG + 16; }
+constexpr uint32_t LPOLLS = 1u << 22;
+
+template <typename T>
+__global__ void __launch_bounds__(DT, 2)
+lazy_cham_kernel(LazyArgs A, const __grid_constant__ CUtensorMap tm_r, const __grid_constant__ CUtensorMap tm_i) {
+  extern __shared__ __align__(128) unsigned char lsm[];
+  float* as = reinterpret_cast<float*>(lsm + LAS_OFF);   // [j][kv][row of the stage]
+  float* ks = reinterpret_cast<float*>(lsm + LKS_OFF);
+  float* vs = ks + A.D;
+  uint64_t* full = reinterpret_cast<uint64_t*>(vs + A.D);   // TMA landed (8-byte aligned: D % 32 == 0)
+  __shared__ float qs[CWD];
+  __shared__ float red[8][CWD][4];
+  __shared__ float pbs[LP_MAX][4][CWD];   // pending B_j over this stripe's columns
+  __shared__ float gs[LP_MAX][4];
+  __shared__ float dsc[8][4];
+  __shared__ float cq4[8][4];
+  __shared__ int last_flag;
+  const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
+  const int D = A.D, P = A.P;
+  const int nst = D / CWD;
+  const int item = blockIdx.x / nst, stripe = blockIdx.x % nst;
+  const int c8 = lane % TPR;
+  const int rp = threadIdx.x / TPR;       // rows rp and rp + 32 of each stage
+  const int p = A.pcount[item];
+  const bool fold = p >= P;               // fold the P pending factors into S this step
+  const int np = fold ? P : p;            // pending factors read by this step
+  const int snew = fold ? 0 : p;          // slot of this step's factor
+  const int NRB = D / LROWS;
+  auto stage = [&](int s) { return reinterpret_cast<float*>(lsm + s * LSTAGE); };
+  auto issue = [&](int rb) {
+    const int s = rb % NSTG;
+    tc::mbar_expect_tx(&full[s], LSTAGE);
+    tc::tma_load_2d(stage(s), &tm_r, stripe * CWD, item * D + rb * LROWS, &full[s]);
+    tc::tma_load_2d(stage(s) + LROWS * CWD, &tm_i, stripe * CWD, item * D + rb * LROWS, &full[s]);
+  };
+  if (tid == 0) {
+    for (int s = 0; s < NSTG; ++s) tc::mbar_init(&full[s], 1);
+    tc::fence_mbar_init();
+    for (int rb = 0; rb < NSTG && rb < NRB; ++rb) issue(rb);
+  }
+
+  const size_t voff = (size_t)item * D;
+  const float* pa = A.pa + (size_t)item * P * 2 * D;
+  float* pb = A.pb + (size_t)item * P * 4 * D;
+  float dots[4] = {0.f, 0.f, 0.f, 0.f};
+  bool fin = true;
+  const int cs0 = stripe * CWD;
+  for (int i = tid; i < D; i += DT) {
+    const float kx = ld1<T>(A.ck, voff + i), vx = ld1<T>(A.cv, voff + i), qx = ld1<T>(A.cq, voff + i);
+    ks[i] = kx; vs[i] = vx;
+    if (i >= cs0 && i < cs0 + CWD) qs[i - cs0] = qx;
+    dots[0] += kx * kx; dots[1] += vx * vx; dots[2] += kx * vx; dots[3] += qx * qx;
+    fin = fin && isfinite(kx) && isfinite(vx);
+  }
+  for (int e = tid; e < np * 4 * CWD; e += DT) {
+    const int j = e / (4 * CWD), rr = (e / CWD) % 4, c = e % CWD;
+    pbs[j][rr][c] = pb[((size_t)j * 4 + rr) * D + cs0 + c];
+  }
+  if (!fold && tid < 4 * p) gs[tid / 4][tid % 4] = A.g[((size_t)item * LP_MAX + tid / 4) * 4 + tid % 4];
+  block_sum4(dots, fin, dsc);      // also makes ks/vs/qs/pbs/gs and the barrier inits visible
+
+  // ---- one pass: column sums kᵀS, vᵀS and the readout partials S_re q, folding first
+  float acc[4][4];
+#pragma unroll
+  for (int qn = 0; qn < 4; ++qn)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) acc[qn][j] = 0.f;
+  float* part = A.part + ((size_t)item * nst + stripe) * D;
+  int issued = NSTG < NRB ? NSTG : NRB;    // row blocks whose loads thread 0 has issued
+  bool failed = false;
+  for (int rb = 0; rb < NRB; ++rb) {
+    const int s = rb % NSTG;
+    // (a wait that gives up still reaches this stage's barrier, which votes on it)
+    const bool got = tc::mbar_wait(&full[s], (rb / NSTG) & 1, LPOLLS);
+    float* sr = stage(s);
+    float* si = sr + LROWS * CWD;
+    float4 xr2[2], xi2[2];
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int i = rp + 32 * h;
+      xr2[h] = *reinterpret_cast<const float4*>(sr + i * CWD + 4 * c8);
+      xi2[h] = *reinterpret_cast<const float4*>(si + i * CWD + 4 * c8);
+    }
+    if (fold) {   // S += sum_j A_j B_j; each factor's four columns of B serve both rows
+      for (int e = tid; e < P * 2 * LROWS; e += DT)   // the stage's rows of every A_j (coalesced)
+        as[e] = __ldg(pa + (size_t)(e / LROWS) * D + rb * LROWS + e % LROWS);
+      __syncthreads();
+#pragma unroll 2
+      for (int j = 0; j < P; ++j) {
+        const float4 b0r = *reinterpret_cast<const float4*>(&pbs[j][0][4 * c8]);
+        const float4 b0i = *reinterpret_cast<const float4*>(&pbs[j][1][4 * c8]);
+        const float4 b1r = *reinterpret_cast<const float4*>(&pbs[j][2][4 * c8]);
+        const float4 b1i = *reinterpret_cast<const float4*>(&pbs[j][3][4 * c8]);
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const int i = rp + 32 * h;
+          const float a0 = as[(2 * j) * LROWS + i], a1 = as[(2 * j + 1) * LROWS + i];
+#pragma unroll
+          for (int jj = 0; jj < 4; ++jj) {
+            comp(xr2[h], jj) += a0 * compc(b0r, jj) + a1 * compc(b1r, jj);
+            comp(xi2[h], jj) += a0 * compc(b0i, jj) + a1 * compc(b1i, jj);
+          }
+        }
+      }
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const int i = rp + 32 * h;
+        *reinterpret_cast<float4*>(sr + i * CWD + 4 * c8) = xr2[h];
+        *reinterpret_cast<float4*>(si + i * CWD + 4 * c8) = xi2[h];
+      }
+    }
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int i = rp + 32 * h, r = rb * LROWS + i;
+      const float4 xr = xr2[h], xi = xi2[h];
+      const float kr = ks[r], vr = vs[r];
+      float o = 0.f;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float hr_ = compc(xr, j), hi_ = compc(xi, j);
+        acc[0][j] += kr * hr_; acc[1][j] += kr * hi_;
+        acc[2][j] += vr * hr_; acc[3][j] += vr * hi_;
+        o += hr_ * qs[4 * c8 + j];
+      }
+#pragma unroll
+      for (int sh = 1; sh < TPR; sh <<= 1) o += __shfl_xor_sync(0xffffffffu, o, sh);
+      if (c8 == 0) part[r] = o;
+    }
+    if (fold) tc::fence_proxy_async();     // the in-place updates, before the store reads them
+    if (__syncthreads_or(!got)) {          // stage s consumed; any wait that gave up stops all
+      failed = true;
+      break;
+    }
+    if (tid == 0) {
+      if (fold) {
+        tc::tma_store_2d(&tm_r, stripe * CWD, item * D + rb * LROWS, sr);
+        tc::tma_store_2d(&tm_i, stripe * CWD, item * D + rb * LROWS, si);
+        tc::bulk_commit();
+        tc::bulk_wait_read<0>();
+      }
+      tc::fence_proxy_async();
+      if (rb + NSTG < NRB) {
+        issue(rb + NSTG);
+        issued = rb + NSTG + 1;
+      }
+    }
+  }
+  if (failed) {
+    // let the copies in flight land before the shared memory is released; no partials
+    if (tid == 0) {
+      atomicOr(&g_decode_status, 2u);
+      for (int rb = issued - NSTG < 0 ? 0 : issued - NSTG; rb < issued; ++rb)
+        tc::mbar_wait(&full[rb % NSTG], (rb / NSTG) & 1, LPOLLS);
+      tc::bulk_wait<0>();
+    }
+    return;
+  }
+  if (fold && tid == 0) tc::bulk_wait<0>();   // the folded state is written
+#pragma unroll
+  for (int qn = 0; qn < 4; ++qn)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      float x = acc[qn][j];
+#pragma unroll
+      for (int o = TPR; o < 32; o <<= 1) x += __shfl_xor_sync(0xffffffffu, x, o);
+      acc[qn][j] = x;
+    }
+  if (lane < TPR) {
+#pragma unroll
+    for (int qn = 0; qn < 4; ++qn)
+#pragma unroll
+      for (int j = 0; j < 4; ++j) red[w][4 * lane + j][qn] = acc[qn][j];
+  }
+  __syncthreads();
+  const float kk = dots[0], vv = dots[1], kv = dots[2];
+  const float gm = A.gamma[item];
+  const float cc = 0.5f * gm;
+  const float dr = 1.f + cc * cc * (kk * vv - kv * kv);
+  const float di = -2.f * cc * kv;
+  const float m2 = dr * dr + di * di;
+  const float fr = 2.f * cc * dr / m2;
+  const float fi = -2.f * cc * di / m2;
+  const float n00r = fr * (-cc * vv), n00i = fi * (-cc * vv);
+  const float n11r = fr * (-cc * kk), n11i = fi * (-cc * kk);
+  const float n01r = fr * (cc * kv) - fi, n01i = fr + fi * (cc * kv);
+  // non-finite k, v, gate or factor: identity (cham_memory.py:54-96)
+  const bool ok = fin && isfinite(gm) && isfinite(n00r) && isfinite(n00i) && isfinite(n01r) && isfinite(n01i) &&
+                  isfinite(n11r) && isfinite(n11i);
+  float cqv[4] = {0.f, 0.f, 0.f, 0.f};
+  if (tid < CWD) {
+    const int c = tid;
+    float t[4];
+#pragma unroll
+    for (int qn = 0; qn < 4; ++qn) {
+      float x = 0.f;
+#pragma unroll
+      for (int ww = 0; ww < 8; ++ww) x += red[ww][c][qn];
+      t[qn] = x;
+    }
+    // the pending factors' share of kᵀH and vᵀH (none after a fold)
+    for (int j = 0; j < (fold ? 0 : p); ++j) {
+      const float gkk = gs[j][0], gkv = gs[j][1], gvk = gs[j][2], gvv = gs[j][3];
+      t[0] += gkk * pbs[j][0][c] + gkv * pbs[j][2][c];
+      t[1] += gkk * pbs[j][1][c] + gkv * pbs[j][3][c];
+      t[2] += gvk * pbs[j][0][c] + gvv * pbs[j][2][c];
+      t[3] += gvk * pbs[j][1][c] + gvv * pbs[j][3][c];
+    }
+    const float qc = qs[c];
+    cqv[0] = t[0] * qc; cqv[1] = t[1] * qc; cqv[2] = t[2] * qc; cqv[3] = t[3] * qc;
+    float b0r = 0.f, b0i = 0.f, b1r = 0.f, b1i = 0.f;
+    if (ok) {
+      b0r = n00r * t[0] - n00i * t[1] + n01r * t[2] - n01i * t[3];
+      b0i = n00r * t[1] + n00i * t[0] + n01r * t[3] + n01i * t[2];
+      b1r = n01r * t[0] - n01i * t[1] + n11r * t[2] - n11i * t[3];
+      b1i = n01r * t[1] + n01i * t[0] + n11r * t[3] + n11i * t[2];
+    }
+    float* nb = pb + (size_t)snew * 4 * D + cs0 + c;
+    nb[0] = b0r; nb[D] = b0i; nb[2 * D] = b1r; nb[3 * D] = b1i;
+  }
+  if (w == 0) {   // this stripe's share of kᵀH q and vᵀH q
+#pragma unroll
+    for (int j = 0; j < 4; ++j) cqv[j] = warp_sum(cqv[j]);
+    if (lane == 0) {
+      float* dst = A.cqp + ((size_t)item * nst + stripe) * 4;
+      dst[0] = cqv[0]; dst[1] = cqv[1]; dst[2] = cqv[2]; dst[3] = cqv[3];
+    }
+  }
+  // publish: CTA barrier, one release fence and the stripe count
+  __syncthreads();
+  if (tid == 0) {
+    __threadfence();
+    const unsigned int prev = atomicAdd(&A.cnt[item], 1u);
+    last_flag = (prev == (unsigned int)(nst - 1));
+    if (last_flag) __threadfence();
+  }
+  __syncthreads();
+  if (!last_flag) return;
+  // ---- last CTA of the item: the readout and the new factor's A part
+  {
+    float x[4] = {0.f, 0.f, 0.f, 0.f};
+    for (int st = tid; st < nst; st += DT) {
+      const float* src = A.cqp + ((size_t)item * nst + st) * 4;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) x[j] += __ldcg(src + j);
+    }
+    bool dummy = true;
+    block_sum4(x, dummy, dsc);
+    if (tid == 0) {
+      // Re of the new factor times q: B0'q = N00 (kᵀHq) + N01 (vᵀHq), B1'q = N01 (kᵀHq) + N11 (vᵀHq)
+      cq4[0][0] = ok ? n00r * x[0] - n00i * x[1] + n01r * x[2] - n01i * x[3] : 0.f;
+      cq4[0][1] = ok ? n01r * x[0] - n01i * x[1] + n11r * x[2] - n11i * x[3] : 0.f;
+    }
+    __syncthreads();
+  }
+  const float u0 = cq4[0][0], u1 = cq4[0][1];
+  const float* pbq = A.bq + (size_t)item * LP_MAX * 2;
+  const float* pb0 = A.part + (size_t)item * nst * D;
+  T* y = static_cast<T*>(A.cout) + voff;
+  const int npend = fold ? 0 : p;
+  for (int i = tid; i < D; i += DT) {
+    float sacc = 0.f;
+#pragma unroll 8
+    for (int st = 0; st < nst; ++st) sacc += __ldcg(pb0 + (size_t)st * D + i);
+    for (int j = 0; j < npend; ++j)
+      sacc += pa[(size_t)j * 2 * D + i] * __ldcg(pbq + 2 * j) + pa[((size_t)j * 2 + 1) * D + i] * __ldcg(pbq + 2 * j + 1);
+    if (ok) sacc += ks[i] * u0 + vs[i] * u1;   // (an identity step adds nothing; k, v may be non-finite)
+    y[i] = from_f32<T>(sacc);
+  }
+  // this step's A part (zero for an identity step, so that nothing non-finite is kept)
+  __syncthreads();
+  float* na = A.pa + ((size_t)item * P + snew) * 2 * D;
+  for (int i = tid; i < D; i += DT) {
+    na[i] = ok ? ks[i] : 0.f;
+    na[D + i] = ok ? vs[i] : 0.f;
+  }
+  if (tid == 0) A.pcount[item] = snew + 1;
+}
+
+// Fold every pending factor into S and empty the list (one CTA per (item, stripe)).
+__global__ void __launch_bounds__(DT) lazy_flush_kernel(float* __restrict__ hr, float* __restrict__ hi,
+                                                        const int* __restrict__ pcount, const float* __restrict__ pa,
+                                                        const float* __restrict__ pb, int D, int P) {
+  __shared__ float pbs[LP_MAX][4][CWD];
+  const int nst = D / CWD;
+  const int item = blockIdx.x / nst, stripe = blockIdx.x % nst, tid = threadIdx.x, lane = tid & 31;
+  const int p = pcount[item];
+  if (p == 0) return;
+  const int cs0 = stripe * CWD, c8 = lane % TPR, c0 = cs0 + 4 * c8, rp = tid / TPR;
+  const float* a = pa + (size_t)item * P * 2 * D;
+  const float* bb = pb + (size_t)item * P * 4 * D;
+  for (int e = tid; e < p * 4 * CWD; e += DT) {
+    const int j = e / (4 * CWD), rr = (e / CWD) % 4, c = e % CWD;
+    pbs[j][rr][c] = bb[((size_t)j * 4 + rr) * D + cs0 + c];
+  }
+  __syncthreads();
+  float* Hr = hr + (size_t)item * D * D;
+  float* Hi = hi + (size_t)item * D * D;
+  for (int r = rp; r < D; r += RPG) {
+    float4 xr = *reinterpret_cast<const float4*>(Hr + (size_t)r * D + c0);
+    float4 xi = *reinterpret_cast<const float4*>(Hi + (size_t)r * D + c0);
+    for (int j = 0; j < p; ++j) {
+      const float2 av = make_float2(__ldg(a + (size_t)j * 2 * D + r), __ldg(a + ((size_t)j * 2 + 1) * D + r));
+#pragma unroll
+      for (int jj = 0; jj < 4; ++jj) {
+        const int c = 4 * c8 + jj;
+        comp(xr, jj) += av.x * pbs[j][0][c] + av.y * pbs[j][2][c];
+        comp(xi, jj) += av.x * pbs[j][1][c] + av.y * pbs[j][3][c];
+      }
+    }
+    *reinterpret_cast<float4*>(Hr + (size_t)r * D + c0) = xr;
+    *reinterpret_cast<float4*>(Hi + (size_t)r * D + c0) = xi;
+  }
+}
+
 template <typename T, bool CHAM, bool FO>
 __global__ void __launch_bounds__(DT, 3) decode_step_kernel(DecodeArgs A) {
   const int bid = blockIdx.x;
@@ -495,6 +891,50 @@ int launch_typed(const DecodeArgs& A, cudaStream_t st) {
   else
     decode_step_kernel<T, true, false><<<grid, DT, 0, st>>>(A);
   return check_launch("decode_step_kernel");
+}
+
+// one hologram plane as a [b*D rows][D] fp32 tensor, boxes of 32 columns x 64 rows, no swizzle
+int make_plane_map(CUtensorMap* m, const float* base, int b, int D) {
+  auto enc = tmap_encoder();
+  VERACE_REQUIRE(enc != nullptr, VERACE_ERR_CUDA, "cuTensorMapEncodeTiled is not available");
+  const cuuint64_t dims[2] = {(cuuint64_t)D, (cuuint64_t)b * D};
+  const cuuint64_t strides[1] = {(cuuint64_t)D * 4};
+  const cuuint32_t box[2] = {(cuuint32_t)CWD, (cuuint32_t)LROWS};
+  const cuuint32_t es[2] = {1, 1};
+  CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(base), dims, strides, box, es,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  VERACE_REQUIRE(r == CUDA_SUCCESS, VERACE_ERR_CUDA, "cuTensorMapEncodeTiled (hologram plane) failed: %d", (int)r);
+  return VERACE_OK;
+}
+
+struct LazyWs {
+  size_t part, cqp, cnt, g, bq, total;
+};
+
+LazyWs lazy_ws_layout(int b, int D) {
+  LazyWs L{};
+  size_t off = 0;
+  const int nst = D / CWD;
+  L.part = off; off = align_up(off + (size_t)b * nst * D * sizeof(float), 256);
+  L.cqp = off;  off = align_up(off + (size_t)b * nst * 4 * sizeof(float), 256);
+  L.cnt = off;  off = align_up(off + (size_t)b * sizeof(unsigned int), 256);
+  L.g = off;    off = align_up(off + (size_t)b * LP_MAX * 4 * sizeof(float), 256);
+  L.bq = off;   off = align_up(off + (size_t)b * LP_MAX * 2 * sizeof(float), 256);
+  L.total = off + 256;
+  return L;
+}
+
+// pending storage: counts [b] (256-byte block) | A [b][P][2][D] | B [b][P][4][D]
+size_t pending_bytes(int b, int D, int P) {
+  return align_up((size_t)b * sizeof(int), 256) + (size_t)b * P * 6 * D * sizeof(float);
+}
+
+void pending_ptrs(void* pending, int b, int D, int P, int** cnt, float** pa, float** pb) {
+  char* base = (char*)pending;
+  *cnt = (int*)base;
+  *pa = (float*)(base + align_up((size_t)b * sizeof(int), 256));
+  *pb = *pa + (size_t)b * P * 2 * D;
 }
 
 }  // namespace
@@ -584,4 +1024,94 @@ extern "C" int verace_decode_step(const void* sssd_q, const void* sssd_k, const 
     case VERACE_BF16: return launch_typed<__nv_bfloat16>(A, st);
     default: return launch_typed<__half>(A, st);
   }
+}
+
+extern "C" size_t verace_decode_lazy_workspace(int b, int D) {
+  if (b <= 0 || D <= 0 || D % CWD) return 256;
+  return lazy_ws_layout(b, D).total;
+}
+
+extern "C" size_t verace_decode_pending_bytes(int b, int D, int P) {
+  if (b <= 0 || D <= 0 || P <= 0) return 0;
+  return pending_bytes(b, D, P);
+}
+
+extern "C" int verace_decode_cham_lazy(const void* cham_q, const void* cham_k, const void* cham_v, const float* gamma,
+                                       float* h_re, float* h_im, void* pending, int P, void* cham_out, int b, int D,
+                                       int dtype, void* workspace, size_t workspace_bytes, void* stream) {
+  VERACE_REQUIRE(b >= 0 && D >= 0, VERACE_ERR_INVALID, "verace_decode_cham_lazy: invalid sizes b=%d D=%d", b, D);
+  VERACE_REQUIRE(dtype == VERACE_F32 || dtype == VERACE_BF16 || dtype == VERACE_F16, VERACE_ERR_INVALID,
+                 "verace_decode_cham_lazy: unknown dtype %d", dtype);
+  VERACE_REQUIRE(P >= 1 && P <= LP_MAX, VERACE_ERR_INVALID,
+                 "verace_decode_cham_lazy: pending depth %d outside [1, %d]", P, LP_MAX);
+  if (b == 0 || D == 0) return VERACE_OK;
+  VERACE_REQUIRE(cham_q && cham_k && cham_v && gamma && h_re && h_im && pending && cham_out, VERACE_ERR_INVALID,
+                 "verace_decode_cham_lazy: NULL pointer");
+  VERACE_REQUIRE(D % CWD == 0 && D <= MAXD, VERACE_ERR_UNSUPPORTED,
+                 "verace_decode_cham_lazy: holographic dim %d unsupported (a multiple of %d, at most %d)", D, CWD,
+                 MAXD);
+  VERACE_REQUIRE((((uintptr_t)h_re | (uintptr_t)h_im | (uintptr_t)pending) & 15) == 0, VERACE_ERR_INVALID,
+                 "verace_decode_cham_lazy: hologram and pending storage must be 16-byte aligned");
+  const size_t need = verace_decode_lazy_workspace(b, D);
+  VERACE_REQUIRE(workspace != nullptr && workspace_bytes >= need, VERACE_ERR_WORKSPACE,
+                 "verace_decode_cham_lazy: workspace of %zu bytes required, %zu given", need,
+                 workspace ? workspace_bytes : (size_t)0);
+  cudaStream_t st = (cudaStream_t)stream;
+  const LazyWs L = lazy_ws_layout(b, D);
+  char* base = (char*)align_up((size_t)workspace, 256);
+  LazyArgs A{};
+  A.cq = cham_q; A.ck = cham_k; A.cv = cham_v; A.gamma = gamma; A.hr = h_re; A.hi = h_im; A.cout = cham_out;
+  pending_ptrs(pending, b, D, P, &A.pcount, &A.pa, &A.pb);
+  A.g = (float*)(base + L.g);
+  A.bq = (float*)(base + L.bq);
+  A.part = (float*)(base + L.part);
+  A.cqp = (float*)(base + L.cqp);
+  A.cnt = (unsigned int*)(base + L.cnt);
+  A.b = b; A.D = D; A.P = P;
+  VERACE_CUDA(cudaMemsetAsync(A.cnt, 0, (size_t)b * sizeof(unsigned int), st));
+  const unsigned grid = (unsigned)(b * (D / CWD));
+  CUtensorMap mr, mi;
+  if (int rc = make_plane_map(&mr, h_re, b, D)) return rc;
+  if (int rc = make_plane_map(&mi, h_im, b, D)) return rc;
+  switch (dtype) {
+    case VERACE_F32:
+      lazy_pre_kernel<float><<<b * P, DT, 0, st>>>(A);
+      if (int rc = check_launch("lazy_pre_kernel")) return rc;
+      VERACE_CUDA(cudaFuncSetAttribute(lazy_cham_kernel<float>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       (int)lazy_smem(D)));
+      lazy_cham_kernel<float><<<grid, DT, lazy_smem(D), st>>>(A, mr, mi);
+      break;
+    case VERACE_BF16:
+      lazy_pre_kernel<__nv_bfloat16><<<b * P, DT, 0, st>>>(A);
+      if (int rc = check_launch("lazy_pre_kernel")) return rc;
+      VERACE_CUDA(cudaFuncSetAttribute(lazy_cham_kernel<__nv_bfloat16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       (int)lazy_smem(D)));
+      lazy_cham_kernel<__nv_bfloat16><<<grid, DT, lazy_smem(D), st>>>(A, mr, mi);
+      break;
+    default:
+      lazy_pre_kernel<__half><<<b * P, DT, 0, st>>>(A);
+      if (int rc = check_launch("lazy_pre_kernel")) return rc;
+      VERACE_CUDA(cudaFuncSetAttribute(lazy_cham_kernel<__half>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       (int)lazy_smem(D)));
+      lazy_cham_kernel<__half><<<grid, DT, lazy_smem(D), st>>>(A, mr, mi);
+      break;
+  }
+  return check_launch("lazy_cham_kernel");
+}
+
+extern "C" int verace_decode_cham_flush(float* h_re, float* h_im, void* pending, int P, int b, int D, void* stream) {
+  VERACE_REQUIRE(b >= 0 && D >= 0 && P >= 1 && P <= LP_MAX, VERACE_ERR_INVALID,
+                 "verace_decode_cham_flush: invalid sizes b=%d D=%d P=%d", b, D, P);
+  if (b == 0 || D == 0) return VERACE_OK;
+  VERACE_REQUIRE(h_re && h_im && pending, VERACE_ERR_INVALID, "verace_decode_cham_flush: NULL pointer");
+  VERACE_REQUIRE(D % CWD == 0 && D <= MAXD, VERACE_ERR_UNSUPPORTED,
+                 "verace_decode_cham_flush: holographic dim %d unsupported", D);
+  cudaStream_t st = (cudaStream_t)stream;
+  int* cnt;
+  float *pa, *pb;
+  pending_ptrs(pending, b, D, P, &cnt, &pa, &pb);
+  lazy_flush_kernel<<<(unsigned)(b * (D / CWD)), DT, 0, st>>>(h_re, h_im, cnt, pa, pb, D, P);
+  if (int rc = check_launch("lazy_flush_kernel")) return rc;
+  VERACE_CUDA(cudaMemsetAsync(cnt, 0, (size_t)b * sizeof(int), st));
+  return VERACE_OK;
 }

@@ -23,6 +23,12 @@ Readout modes (the CHAM readout is Re(NS3(H) q), cham_memory.py:233-241):
   (``device_status()``) when |E q| > 1e-2 |q|.
 
 The default is ``"first_order"`` for fp32 inputs and ``"unitary"`` for bf16 / fp16.
+
+Lazy hologram updates (unitary readout, :func:`launch_decode_cham_lazy`,
+``DecodeState(pending_depth=P)``): the rank-2 step updates are kept as pending factors,
+H = S + sum_j [k_j v_j] B_j, and folded into the stored planes S every P steps, so that a
+step reads S once instead of reading it twice and writing it.  The stored planes are
+the true state only after a flush (:func:`flush_pending`, ``DecodeState.flush``).
 """
 from typing import List, Optional, Sequence, Tuple
 
@@ -120,6 +126,63 @@ def launch_decode_step(sssd: Optional[Sequence[torch.Tensor]],
     return sout, cout
 
 
+def pending_storage(b: int, D: int, P: int, device="cuda") -> torch.Tensor:
+    """Zero-filled pending-factor storage for one layer's holograms (an empty list)."""
+    return torch.zeros(int(lib().verace_decode_pending_bytes(b, D, P)), dtype=torch.uint8, device=device)
+
+
+_lazy_ws_cache = {}
+
+
+def _lazy_workspace(b: int, D: int, device) -> torch.Tensor:
+    n = int(lib().verace_decode_lazy_workspace(b, D))
+    key = (torch.device(device), n)
+    ws = _lazy_ws_cache.get(key)
+    if ws is None:
+        ws = torch.empty(n, dtype=torch.uint8, device=device)
+        _lazy_ws_cache[key] = ws
+    return ws
+
+
+def launch_decode_cham_lazy(q, k, v, gamma, H_real, H_imag, pending: torch.Tensor, P: int,
+                            workspace: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """One unitary-readout CHAM decode step with deferred hologram updates.
+
+    q/k/v [b, D] (or [b, 1, D]), gamma [b] (or [b, 1]); H_real/H_imag [b, D, D] fp32, the
+    stored planes; pending: storage from :func:`pending_storage` for these planes and P.
+    Returns the readout [b, D] in q's dtype; the planes and the pending list are updated
+    in place (the planes change only on the steps that fold the list into them)."""
+    assert q.is_cuda, "This kernel requires CUDA tensors"
+    dt = q.dtype if q.dtype in _DTYPE else torch.float32
+    b, D = q.shape[0], q.shape[-1]
+    for H in (H_real, H_imag):
+        assert H.dtype == torch.float32 and H.is_contiguous() and tuple(H.shape) == (b, D, D), \
+            "H_real / H_imag must be contiguous fp32 [b, D, D] tensors (updated in place)"
+    assert pending.dtype == torch.uint8 and pending.numel() >= lib().verace_decode_pending_bytes(b, D, P), \
+        "pending storage too small for (b, D, P)"
+    qc, kc, vc = (_vec(x.reshape(b, D), dt) for x in (q, k, v))
+    gc = gamma.reshape(b).float().contiguous()
+    out = torch.empty(b, D, device=q.device, dtype=dt)
+    if workspace is None:
+        workspace = _lazy_workspace(b, D, q.device)
+    with torch.cuda.device(q.device):
+        rc = lib().verace_decode_cham_lazy(qc.data_ptr(), kc.data_ptr(), vc.data_ptr(), gc.data_ptr(),
+                                           H_real.data_ptr(), H_imag.data_ptr(), pending.data_ptr(), P,
+                                           out.data_ptr(), b, D, _DTYPE[dt], workspace.data_ptr(),
+                                           workspace.numel(), torch.cuda.current_stream(q.device).cuda_stream)
+    check(rc, "verace_decode_cham_lazy")
+    return out
+
+
+def flush_pending(H_real: torch.Tensor, H_imag: torch.Tensor, pending: torch.Tensor, P: int) -> None:
+    """Fold the pending factors into the stored planes and empty the list."""
+    b, D = H_real.shape[0], H_real.shape[-1]
+    with torch.cuda.device(H_real.device):
+        rc = lib().verace_decode_cham_flush(H_real.data_ptr(), H_imag.data_ptr(), pending.data_ptr(), P, b, D,
+                                            torch.cuda.current_stream(H_real.device).cuda_stream)
+    check(rc, "verace_decode_cham_flush")
+
+
 def device_status(device=None) -> int:
     """Synchronise and return (then clear) the library's device status: 0, or
     VERACE_ERR_TIMEOUT (5) / VERACE_ERR_STATE (6)."""
@@ -134,10 +197,15 @@ class DecodeState:
     psi: [layers, batch, h, d, d] fp32; H_real, H_imag: [layers, batch, D, D] fp32,
     initialised to the identity (the reference's ``None`` state).  :meth:`step` advances
     one layer in place; a whole decode step calls it once per layer.
+
+    With ``pending_depth`` P > 0 (the default, 8) unitary-readout CHAM steps defer their
+    hologram updates (module docstring); H_real / H_imag then hold the stored part, and
+    :meth:`flush` (called by :meth:`layer_states`, and before any step that needs the
+    planes themselves) folds the pending factors in.
     """
 
     def __init__(self, layers: int, batch: int, num_heads: int, head_dim: int,
-                 holographic_dim: int, device="cuda"):
+                 holographic_dim: int, device="cuda", pending_depth: int = 8):
         self.layers, self.batch = layers, batch
         self.h, self.d, self.D = num_heads, head_dim, holographic_dim
         eye_d = torch.eye(head_dim, device=device, dtype=torch.float32)
@@ -146,11 +214,22 @@ class DecodeState:
         self.H_real = eye_D.expand(layers, batch, holographic_dim, holographic_dim).contiguous()
         self.H_imag = torch.zeros_like(self.H_real)
         self.workspace = _workspace(batch, holographic_dim, device)
+        self.P = pending_depth
+        if self.P > 0:
+            nb = int(lib().verace_decode_pending_bytes(batch, holographic_dim, self.P))
+            self.pending = torch.zeros(layers, nb, dtype=torch.uint8, device=device)
+            self.lazy_workspace = _lazy_workspace(batch, holographic_dim, device)
+
+    def _lazy(self, q: torch.Tensor, mode: Optional[str]) -> bool:
+        return self.P > 0 and _mode(mode, q.dtype if q.dtype in _DTYPE else torch.float32) == 0
 
     def step(self, layer: int, sssd: Sequence[torch.Tensor], cham: Sequence[torch.Tensor],
              mode: Optional[str] = None) -> Tuple[torch.Tensor, torch.Tensor]:
         """sssd: (q, k, v, delta); cham: (q, k, v, gamma) of one token per item.
         Returns (sssd_out [b, h, d], cham_out [b, D])."""
+        if self._lazy(cham[0], mode):
+            return self.step_sssd(layer, *sssd, mode=mode), self.step_cham(layer, *cham, mode=mode)
+        self.flush(layer)
         return launch_decode_step(tuple(sssd) + (self.psi[layer],),
                                   tuple(cham) + (self.H_real[layer], self.H_imag[layer]),
                                   mode=mode, workspace=self.workspace)
@@ -161,9 +240,20 @@ class DecodeState:
                                   workspace=self.workspace)[0]
 
     def step_cham(self, layer: int, q, k, v, gamma, mode: Optional[str] = None) -> torch.Tensor:
-        """CHAM half only."""
+        """CHAM half only (deferred updates for the unitary readout when pending_depth > 0)."""
+        if self._lazy(q, mode):
+            return launch_decode_cham_lazy(q, k, v, gamma, self.H_real[layer], self.H_imag[layer],
+                                           self.pending[layer], self.P, workspace=self.lazy_workspace)
+        self.flush(layer)
         return launch_decode_step(None, (q, k, v, gamma, self.H_real[layer], self.H_imag[layer]),
                                   mode=mode, workspace=self.workspace)[1]
+
+    def flush(self, layer: Optional[int] = None) -> None:
+        """Fold the pending hologram factors of one layer (or all) into H_real / H_imag."""
+        if self.P <= 0:
+            return
+        for l in (range(self.layers) if layer is None else (layer,)):
+            flush_pending(self.H_real[l], self.H_imag[l], self.pending[l], self.P)
 
     def load_layer(self, layer: int, psi: Optional[torch.Tensor],
                    hologram: Optional[Tuple[torch.Tensor, torch.Tensor]]) -> None:
@@ -171,6 +261,8 @@ class DecodeState:
         if psi is not None:
             self.psi[layer].copy_(psi)
         if hologram is not None:
+            if self.P > 0:
+                self.pending[layer].zero_()   # the loaded planes are the whole state
             self.H_real[layer].copy_(hologram[0])
             self.H_imag[layer].copy_(hologram[1])
 
@@ -188,6 +280,8 @@ class DecodeState:
         return st
 
     def layer_states(self) -> List[List[Tuple]]:
-        """The reference's per-layer, per-item tuples, as views of this container."""
+        """The reference's per-layer, per-item tuples, as views of this container (after
+        folding any pending hologram factors in)."""
+        self.flush()
         return [[(self.psi[l, i:i + 1], (self.H_real[l, i:i + 1], self.H_imag[l, i:i + 1]))
                  for i in range(self.batch)] for l in range(self.layers)]
