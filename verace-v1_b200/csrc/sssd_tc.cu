@@ -61,22 +61,28 @@ __device__ __forceinline__ void stage8_3(const T* src, bool valid, unsigned char
 // ---------------------------------------------------------------------------------
 // prep: Gram, M_t, T (fp32 SIMT), T written as bf16 hi/lo K-major 128x128 tiles (split
 // row order for bf16 inputs, interleaved for fp32).
-// smem: Ws [128][129] | Gs [128][132] | Ts [128][132] (row pitch a multiple of 4: the
-// solver reads G rows as float4)
+// smem: [Ws [128][129] fp32, fp32 inputs only] | Gs [128][132] (row pitch a multiple of 4:
+// the solver reads G rows as float4), overwritten in place by T.  For bf16 inputs the bf16
+// W tile (32 KB) sits in the front of Gs: the Gram product has completed (its commit
+// barrier) before G is read out of TMEM into Gs, so 68 KB suffice and three CTAs share an
+// SM.
 template <typename T>
-__global__ void __launch_bounds__(THR3, 1)
+constexpr int prep_ctas() { return sizeof(T) == 2 ? 3 : 1; }
+
+template <typename T>
+__global__ void __launch_bounds__(THR3, prep_ctas<T>())
 sssd_tc_prep(const T* __restrict__ k, const T* __restrict__ v, const float* __restrict__ delta,
              unsigned char* __restrict__ Tws, unsigned long long* __restrict__ badws, int S, int H, int nch) {
-  extern __shared__ float sm3[];
+  extern __shared__ __align__(16) float sm3[];
   constexpr int PW = R3 + 1, P = 132;
+  constexpr bool BF = sizeof(T) == 2;   // bf16 inputs: G on the tensor cores (W is exact in bf16)
   float* Ws = sm3;
-  float* Gs = Ws + HD * PW;
-  float* Ts = Gs + R3 * P;
+  float* Gs = BF ? sm3 : Ws + HD * PW;
+  float* Ts = Gs;
   __shared__ float Ms[C3 * 8];   // per token [[m00, m01], [m10, m11]] as complex with zero imaginary parts
   __shared__ unsigned long long bad_bits;
   __shared__ __align__(8) uint64_t gbar;
   __shared__ uint32_t gslot;
-  constexpr bool BF = sizeof(T) == 2;   // bf16 inputs: G on the tensor cores (W is exact in bf16)
   const int c = blockIdx.x, chain = blockIdx.y, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int bi = chain / H, hi = chain % H;
   const int t0 = c * C3, nt = min(C3, S - t0);
@@ -234,7 +240,7 @@ sssd_tc_prep(const T* __restrict__ k, const T* __restrict__ v, const float* __re
     n[0] = m00; n[1] = 0.f; n[2] = m01; n[3] = 0.f; n[4] = m10; n[5] = 0.f; n[6] = m11; n[7] = 0.f;
   }
   __syncthreads();
-  wy_solve<false>(Gs, P, Ms, Ts, nullptr, tid);
+  wy_solve<false>(Gs, P, Ms, Ts, nullptr, tid);   // T overwrites G
   const size_t chunk = (size_t)chain * nch + c;
   unsigned char* To = Tws + chunk * 2 * TILE3;
   for (int e = tid; e < R3 * (R3 / 8); e += THR3) {
@@ -815,7 +821,8 @@ int make_head_map(CUtensorMap* m, const void* base, int b, int S, int H) {
   return VERACE_OK;
 }
 
-size_t sssd_tc_prep_smem() { return sizeof(float) * (HD * (R3 + 1) + 2 * R3 * 132); }
+template <typename T>
+size_t sssd_tc_prep_smem() { return sizeof(float) * ((sizeof(T) == 2 ? 0 : HD * (R3 + 1)) + R3 * 132); }
 
 template <typename T>
 int launch_sssd_tc(const void* q, const void* k, const void* v, const float* delta, const float* psi0,
@@ -825,7 +832,7 @@ int launch_sssd_tc(const void* q, const void* k, const void* v, const float* del
   const int nch = (s + C3 - 1) / C3;
   int rc;
   if (nch > 0) {
-    const size_t ps = sssd_tc_prep_smem();
+    const size_t ps = sssd_tc_prep_smem<T>();
     VERACE_CUDA(cudaFuncSetAttribute(sssd_tc_prep<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ps));
     sssd_tc_prep<T><<<dim3(nch, chains), THR3, ps, st>>>((const T*)k, (const T*)v, delta, Tws, badws, s, h, nch);
     if ((rc = check_launch("sssd_tc_prep"))) return rc;

@@ -16,6 +16,12 @@
 //     X = G_ba T_aa   (written where T_ba goes: nothing reads that block yet)
 //     T_ba = T_bb X   (every thread holds its 4 x 4 tile before any is stored).
 // Entries above the diagonal blocks are exactly zero.  All arithmetic is fp32.
+//
+// The solver reads only the lower blocks of G (the diagonal blocks' lower triangles and
+// the G_ba blocks), each of them for the last time in the step that writes T's entries
+// at the same place, and every such step finishes its reads (a barrier) before its
+// stores.  So T may overwrite G in place (Tr == G), which keeps one 128 x 128 fp32 array
+// out of shared memory.
 #pragma once
 
 namespace verace {
@@ -58,8 +64,7 @@ __device__ __forceinline__ void zero44(float (&c)[4][4]) {
 
 // One join level: blocks of B rows, pairs (a, b) = rows [2pB, 2pB + B), [2pB + B, 2pB + 2B).
 template <int B, bool CPLX>
-__device__ __forceinline__ void join_level(const float* __restrict__ G, int P, float* __restrict__ Tr,
-                                           float* __restrict__ Ti, int tid) {
+__device__ __forceinline__ void join_level(const float* G, int P, float* Tr, float* __restrict__ Ti, int tid) {
   constexpr int TPB = B / 4;                  // tiles per block side
   constexpr int TILES = (WY_R / (2 * B)) * TPB * TPB;
   const bool act = tid < TILES;
@@ -87,6 +92,9 @@ __device__ __forceinline__ void join_level(const float* __restrict__ G, int P, f
         fma44(ci, a, b, 1.f);
       }
     }
+  }
+  __syncthreads();   // every read of G_ba is done (X replaces it when Tr == G)
+  if (act) {
     st44(Tr + row * P + col, P, cr);
     if (CPLX) st44(Ti + row * P + col, P, ci);
   }
@@ -130,23 +138,26 @@ __device__ __forceinline__ void join_level(const float* __restrict__ G, int P, f
 // G: [128][P] fp32 Gram matrix in the interleaved row order, P a multiple of 4 and every
 // array 16-byte aligned; N8: [64][8] per-token 2x2 complex blocks
 // (m00r, m00i, m01r, m01i, m10r, m10i, m11r, m11i); Tr/Ti: [128][P] outputs (Ti unused
-// when !CPLX).  Must be called by all 256 threads of the CTA; ends with a barrier.
+// when !CPLX).  Tr may be G itself (G is then destroyed); Ti must not overlap G.  Must be
+// called by all 256 threads of the CTA; ends with a barrier.
 template <bool CPLX>
-__device__ __forceinline__ void wy_solve(const float* __restrict__ G, int P, const float* __restrict__ N8,
-                                         float* __restrict__ Tr, float* __restrict__ Ti, int tid) {
-  // zero T (the blocks above the diagonal stay zero)
+__device__ __forceinline__ void wy_solve(const float* G, int P, const float* __restrict__ N8, float* Tr,
+                                         float* __restrict__ Ti, int tid) {
+  // zero the blocks of T above the 16-row diagonal blocks (every other entry is written
+  // below; G's entries there are never read)
   for (int e = tid; e < WY_R * (WY_R / 4); e += 256) {
     const int r = e / (WY_R / 4), c4 = e % (WY_R / 4);
+    if ((4 * c4) / 16 <= r / 16) continue;
     *reinterpret_cast<float4*>(Tr + r * P + 4 * c4) = make_float4(0.f, 0.f, 0.f, 0.f);
     if (CPLX) *reinterpret_cast<float4*>(Ti + r * P + 4 * c4) = make_float4(0.f, 0.f, 0.f, 0.f);
   }
   __syncthreads();
   // diagonal blocks: leaf j = tokens [8j, 8j + 8) = rows [16j, 16j + 16); thread = one
   // of the leaf's 16 columns, the column kept in registers
+  const int j = tid >> 4, c = tid & 15, r0 = 16 * j;
+  float xr[16], xi[16];
   if (tid < 128) {
-    const int j = tid >> 4, c = tid & 15, r0 = 16 * j;
     const float* Gl = G + r0 * P + r0;
-    float xr[16], xi[16];
 #pragma unroll
     for (int t = 0; t < 8; ++t) {
       float a0r = (2 * t == c) ? 1.f : 0.f, a1r = (2 * t + 1 == c) ? 1.f : 0.f;
@@ -169,6 +180,9 @@ __device__ __forceinline__ void wy_solve(const float* __restrict__ G, int P, con
       xi[2 * t] = n[0] * a0i + n[1] * a0r + n[2] * a1i + n[3] * a1r;
       xi[2 * t + 1] = n[4] * a0i + n[5] * a0r + n[6] * a1i + n[7] * a1r;
     }
+  }
+  __syncthreads();   // the leaf's reads of G are done (T replaces it when Tr == G)
+  if (tid < 128) {
 #pragma unroll
     for (int i = 0; i < 16; ++i) {
       Tr[(r0 + i) * P + r0 + c] = xr[i];
