@@ -110,6 +110,18 @@ __device__ __forceinline__ void block_sum4(float (&x)[4], bool& flag, float (*sc
 }
 
 // ------------------------------------------------------------------------- SSSD
+// The 2x2 Woodbury factor M of the Cayley transform for gate delta (a = delta / 2),
+//     M = -2a / (1 + a²(kk vv - kv²)) [[a vv, 1 - a kv], [-1 - a kv, a kk]],
+// with every fused multiply-add written out, so that the two SSSD decode kernels round alike.
+__device__ __forceinline__ void sssd_factor(float kk, float vv, float kv, float dl, float& m00, float& m01,
+                                            float& m10, float& m11) {
+  const float a = 0.5f * dl;
+  const float det = fmaf(a * a, fmaf(kk, vv, -(kv * kv)), 1.f);
+  const float f = -2.f * a / det;
+  m00 = f * (a * vv); m01 = f * fmaf(-a, kv, 1.f);
+  m10 = f * fmaf(-a, kv, -1.f); m11 = f * (a * kk);
+}
+
 template <typename T>
 __device__ void sssd_part(const DecodeArgs& A, int chain) {
   __shared__ float ks[MAXHD], vs[MAXHD], qs[MAXHD];
@@ -153,8 +165,10 @@ __device__ void sssd_part(const DecodeArgs& A, int chain) {
       const int r = w + 8 * (m + half * MAXHD / 16);
       if (r < d) {
         const float kr = ks[r], vr = vs[r];
-        ak[0] += kr * ps[m].x; ak[1] += kr * ps[m].y; ak[2] += kr * ps[m].z; ak[3] += kr * ps[m].w;
-        av[0] += vr * ps[m].x; av[1] += vr * ps[m].y; av[2] += vr * ps[m].z; av[3] += vr * ps[m].w;
+        ak[0] = fmaf(kr, ps[m].x, ak[0]); ak[1] = fmaf(kr, ps[m].y, ak[1]);
+        ak[2] = fmaf(kr, ps[m].z, ak[2]); ak[3] = fmaf(kr, ps[m].w, ak[3]);
+        av[0] = fmaf(vr, ps[m].x, av[0]); av[1] = fmaf(vr, ps[m].y, av[1]);
+        av[2] = fmaf(vr, ps[m].z, av[2]); av[3] = fmaf(vr, ps[m].w, av[3]);
       }
     }
   }
@@ -163,13 +177,9 @@ __device__ void sssd_part(const DecodeArgs& A, int chain) {
     for (int j = 0; j < 4; ++j) { red[w][4 * lane + j][0] = ak[j]; red[w][4 * lane + j][1] = av[j]; }
   }
   __syncthreads();
-  const float kk = dots[0], vv = dots[1], kv = dots[2];
   const float dl = A.delta[chain];
-  const float a = 0.5f * dl;
-  const float det = 1.f + a * a * (kk * vv - kv * kv);
-  const float f = -2.f * a / det;
-  const float m00 = f * (a * vv), m01 = f * (1.f - a * kv);
-  const float m10 = f * (-1.f - a * kv), m11 = f * (a * kk);
+  float m00, m01, m10, m11;
+  sssd_factor(dots[0], dots[1], dots[2], dl, m00, m01, m10, m11);
   // Non-finite k, v, gate or factor: identity, as the reference's _solve_cayley
   // substitution does (sssd_attention.py:52-71).
   const bool ok = fin && isfinite(dl) && isfinite(m00) && isfinite(m01) && isfinite(m10) && isfinite(m11);
@@ -181,8 +191,8 @@ __device__ void sssd_part(const DecodeArgs& A, int chain) {
 #pragma unroll
       for (int ww = 0; ww < 8; ++ww) { sa += red[ww][4 * lane + j][0]; sb += red[ww][4 * lane + j][1]; }
     }
-    al[j] = m00 * sa + m01 * sb;   // coefficient of k_r
-    be[j] = m10 * sa + m11 * sb;   // coefficient of v_r
+    al[j] = fmaf(m00, sa, m01 * sb);   // coefficient of k_r
+    be[j] = fmaf(m10, sa, m11 * sb);   // coefficient of v_r
   }
   const float4 q4 = colok ? make_float4(qs[4 * lane], qs[4 * lane + 1], qs[4 * lane + 2], qs[4 * lane + 3])
                           : make_float4(0.f, 0.f, 0.f, 0.f);
@@ -196,13 +206,88 @@ __device__ void sssd_part(const DecodeArgs& A, int chain) {
                      : make_float4(0.f, 0.f, 0.f, 0.f);
     if (ok) {
       const float kr = ks[r], vr = vs[r];
-      x.x += kr * al[0] + vr * be[0]; x.y += kr * al[1] + vr * be[1];
-      x.z += kr * al[2] + vr * be[2]; x.w += kr * al[3] + vr * be[3];
+      x.x += fmaf(kr, al[0], vr * be[0]); x.y += fmaf(kr, al[1], vr * be[1]);
+      x.z += fmaf(kr, al[2], vr * be[2]); x.w += fmaf(kr, al[3], vr * be[3]);
     }
-    float o = x.x * q4.x + x.y * q4.y + x.z * q4.z + x.w * q4.w;
+    float o = fmaf(x.w, q4.w, fmaf(x.z, q4.z, fmaf(x.y, q4.y, x.x * q4.x)));
     o = warp_sum(o);
     if (lane == 0) out[r] = from_f32<T>(o);
     if (colok) __stcs(reinterpret_cast<float4*>(P + (size_t)r * d + 4 * lane), x);
+  }
+}
+
+// SSSD-only step for head_dim 128 (the step's SSSD half when the CHAM half runs deferred):
+// one CTA per (item, head) holds the whole 128 x 128 state in registers (thread: rows
+// w + 8m, m < 16, columns 4 lane .. 4 lane + 3), so the state is read once, with all 16
+// loads of a thread in flight together, and written once; same arithmetic as sssd_part.
+// Two CTAs per SM.
+template <typename T>
+__global__ void __launch_bounds__(DT, 2) sssd_decode128_kernel(DecodeArgs A) {
+  constexpr int HD = 128, NR = HD / 8;
+  __shared__ float ks[HD], vs[HD], qs[HD];
+  __shared__ float4 red[8][HD / 4][2];
+  __shared__ float dsc[8][4];
+  const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
+  const int chain = blockIdx.x;
+  const size_t vec = (size_t)chain * HD;
+  float* P = A.psi + (size_t)chain * HD * HD;
+  float4 ps[NR];
+#pragma unroll
+  for (int m = 0; m < NR; ++m) ps[m] = __ldcs(reinterpret_cast<const float4*>(P + (size_t)(w + 8 * m) * HD) + lane);
+  float dots[4] = {0.f, 0.f, 0.f, 0.f};
+  bool fin = true;
+  if (tid < HD) {
+    const float kx = ld1<T>(A.sk, vec + tid), vx = ld1<T>(A.sv, vec + tid);
+    ks[tid] = kx; vs[tid] = vx; qs[tid] = ld1<T>(A.sq, vec + tid);
+    dots[0] = kx * kx; dots[1] = vx * vx; dots[2] = kx * vx;
+    fin = isfinite(kx) && isfinite(vx);
+  }
+  block_sum4(dots, fin, dsc);      // also makes ks/vs/qs visible
+  float4 ak = make_float4(0.f, 0.f, 0.f, 0.f), av = ak;
+#pragma unroll
+  for (int m = 0; m < NR; ++m) {
+    const float kr = ks[w + 8 * m], vr = vs[w + 8 * m];
+    ak.x = fmaf(kr, ps[m].x, ak.x); ak.y = fmaf(kr, ps[m].y, ak.y);
+    ak.z = fmaf(kr, ps[m].z, ak.z); ak.w = fmaf(kr, ps[m].w, ak.w);
+    av.x = fmaf(vr, ps[m].x, av.x); av.y = fmaf(vr, ps[m].y, av.y);
+    av.z = fmaf(vr, ps[m].z, av.z); av.w = fmaf(vr, ps[m].w, av.w);
+  }
+  red[w][lane][0] = ak;
+  red[w][lane][1] = av;
+  __syncthreads();
+  const float dl = A.delta[chain];
+  float m00, m01, m10, m11;
+  sssd_factor(dots[0], dots[1], dots[2], dl, m00, m01, m10, m11);
+  // Non-finite k, v, gate or factor: identity, as the reference's _solve_cayley
+  // substitution does (sssd_attention.py:52-71).
+  const bool ok = fin && isfinite(dl) && isfinite(m00) && isfinite(m01) && isfinite(m10) && isfinite(m11);
+  float4 sa = make_float4(0.f, 0.f, 0.f, 0.f), sb = sa;
+#pragma unroll
+  for (int ww = 0; ww < 8; ++ww) {
+    const float4 x = red[ww][lane][0], y = red[ww][lane][1];
+    sa.x += x.x; sa.y += x.y; sa.z += x.z; sa.w += x.w;
+    sb.x += y.x; sb.y += y.y; sb.z += y.z; sb.w += y.w;
+  }
+  // coefficients of k_r (al) and v_r (be) in each of the thread's columns
+  const float4 al = make_float4(fmaf(m00, sa.x, m01 * sb.x), fmaf(m00, sa.y, m01 * sb.y),
+                                fmaf(m00, sa.z, m01 * sb.z), fmaf(m00, sa.w, m01 * sb.w));
+  const float4 be = make_float4(fmaf(m10, sa.x, m11 * sb.x), fmaf(m10, sa.y, m11 * sb.y),
+                                fmaf(m10, sa.z, m11 * sb.z), fmaf(m10, sa.w, m11 * sb.w));
+  const float4 q4 = make_float4(qs[4 * lane], qs[4 * lane + 1], qs[4 * lane + 2], qs[4 * lane + 3]);
+  T* out = static_cast<T*>(A.sout) + vec;
+#pragma unroll
+  for (int m = 0; m < NR; ++m) {
+    const int r = w + 8 * m;
+    float4 x = ps[m];
+    if (ok) {
+      const float kr = ks[r], vr = vs[r];
+      x.x += fmaf(kr, al.x, vr * be.x); x.y += fmaf(kr, al.y, vr * be.y);
+      x.z += fmaf(kr, al.z, vr * be.z); x.w += fmaf(kr, al.w, vr * be.w);
+    }
+    __stcs(reinterpret_cast<float4*>(P + (size_t)r * HD) + lane, x);
+    float o = fmaf(x.w, q4.w, fmaf(x.z, q4.z, fmaf(x.y, q4.y, x.x * q4.x)));
+    o = warp_sum(o);
+    if (lane == 0) out[r] = from_f32<T>(o);
   }
 }
 
@@ -884,7 +969,9 @@ int launch_typed(const DecodeArgs& A, cudaStream_t st) {
   const int ncham = (A.D > 0) ? A.b * (A.D / CWD) : 0;
   const int grid = A.ns + ncham;
   const bool fo = A.mode == VERACE_DECODE_FIRST_ORDER;
-  if (A.D == 0)
+  if (A.D == 0 && A.d == 128)
+    sssd_decode128_kernel<T><<<grid, DT, 0, st>>>(A);
+  else if (A.D == 0)
     decode_step_kernel<T, false, false><<<grid, DT, 0, st>>>(A);
   else if (fo)
     decode_step_kernel<T, true, true><<<grid, DT, 0, st>>>(A);

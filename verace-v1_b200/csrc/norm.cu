@@ -8,7 +8,9 @@
 // fp32 sum once.  The fused entry point does a block's residual step in one pass:
 //     h <- h + (y_weight ? RMSNorm(y) : y);   n <- RMSNorm(h)   (when n is given)
 // Work split: one row per group of L lanes (L = 16 for rows of 128, else 32), 16-byte
-// vector loads, fp32 sums by segmented shuffles.
+// vector loads, fp32 sums by segmented shuffles.  For rows of up to 1024 the weights are
+// loaded together with the rows, so a small launch (a decode step's 64 rows) waits for
+// one round trip to memory before its reductions instead of one per weight vector.
 #include "common.cuh"
 
 namespace verace {
@@ -59,10 +61,54 @@ __device__ __forceinline__ float group_sum(float s) {
   return s;
 }
 
-// x[V][8] <- RMSNorm(x) (with weight w when given), rounded as torch does
+// 8 consecutive elements as loaded (16 bytes for 2-byte types, 32 for fp32)
+template <typename T>
+struct Raw8 {
+  uint4 u[sizeof(T) / 2];
+};
+
+template <typename T>
+__device__ __forceinline__ void ldraw(const T* p, Raw8<T>& r) {
+#pragma unroll
+  for (int k = 0; k < (int)(sizeof(T) / 2); ++k) r.u[k] = __ldg(reinterpret_cast<const uint4*>(p) + k);
+}
+
+template <typename T>
+__device__ __forceinline__ void unraw(const Raw8<T>& r, float* x) {
+  if constexpr (sizeof(T) == 4) {
+    x[0] = __uint_as_float(r.u[0].x); x[1] = __uint_as_float(r.u[0].y);
+    x[2] = __uint_as_float(r.u[0].z); x[3] = __uint_as_float(r.u[0].w);
+    x[4] = __uint_as_float(r.u[1].x); x[5] = __uint_as_float(r.u[1].y);
+    x[6] = __uint_as_float(r.u[1].z); x[7] = __uint_as_float(r.u[1].w);
+  } else {
+    const uint4 u = r.u[0];
+    const T* e = reinterpret_cast<const T*>(&u);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) x[i] = to_f32(e[i]);
+  }
+}
+
+// weights loaded up front for rows of at most 4 chunks per lane
+template <int V>
+constexpr bool prefetch_w() { return V <= 4; }
+
+// the lane's weight chunks (when prefetch_w<V>() and w is given)
 template <typename T, int L, int V>
-__device__ __forceinline__ void rms_apply(float (&x)[V][8], const T* __restrict__ w, int sl, int nc, int cols,
-                                          float eps) {
+__device__ __forceinline__ void load_w(const T* __restrict__ w, int sl, int nc, Raw8<T> (&wr)[V]) {
+  if constexpr (prefetch_w<V>()) {
+    if (w) {
+#pragma unroll
+      for (int i = 0; i < V; ++i)
+        if (sl + L * i < nc) ldraw<T>(w + 8 * (sl + L * i), wr[i]);
+    }
+  }
+}
+
+// x[V][8] <- RMSNorm(x) (with weight w when given; its chunks in wr when prefetched),
+// rounded as torch does
+template <typename T, int L, int V>
+__device__ __forceinline__ void rms_apply(float (&x)[V][8], const T* __restrict__ w, const Raw8<T> (&wr)[V], int sl,
+                                          int nc, int cols, float eps) {
   float ss = 0.f;
 #pragma unroll
   for (int i = 0; i < V; ++i)
@@ -76,7 +122,10 @@ __device__ __forceinline__ void rms_apply(float (&x)[V][8], const T* __restrict_
     const int cc = sl + L * i;
     if (cc < nc) {
       float wv[8];
-      if (w) ld8<T>(w + 8 * cc, wv);
+      if (w) {
+        if constexpr (prefetch_w<V>()) unraw<T>(wr[i], wv);
+        else ld8<T>(w + 8 * cc, wv);
+      }
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
         const float r = rnd<T>(x[i][j] * rs);
@@ -95,6 +144,8 @@ rmsnorm_kernel(const T* __restrict__ x, const T* __restrict__ w, T* __restrict__
   const int sl = lane % L, nc = cols / 8;
   const bool act = row < rows;
   const T* xr = x + (act ? row : 0) * cols;
+  Raw8<T> wr[V];
+  load_w<T, L, V>(w, sl, nc, wr);
   float v[V][8];
 #pragma unroll
   for (int i = 0; i < V; ++i) {
@@ -104,7 +155,7 @@ rmsnorm_kernel(const T* __restrict__ x, const T* __restrict__ w, T* __restrict__
 #pragma unroll
       for (int j = 0; j < 8; ++j) v[i][j] = 0.f;
   }
-  rms_apply<T, L, V>(v, w, sl, nc, cols, eps);
+  rms_apply<T, L, V>(v, w, wr, sl, nc, cols, eps);
   if (!act) return;
   T* yr = y + row * cols;
 #pragma unroll
@@ -123,6 +174,9 @@ add_rmsnorm_kernel(T* __restrict__ h, const T* __restrict__ y, const T* __restri
   const int sl = lane % L, nc = cols / 8;
   const bool act = row < rows;
   const long long off = (act ? row : 0) * cols;
+  Raw8<T> wyr[V], wnr[V];
+  load_w<T, L, V>(norm_y ? wy : nullptr, sl, nc, wyr);
+  load_w<T, L, V>(n ? wn : nullptr, sl, nc, wnr);
   float a[V][8], b[V][8];
 #pragma unroll
   for (int i = 0; i < V; ++i) {
@@ -135,7 +189,7 @@ add_rmsnorm_kernel(T* __restrict__ h, const T* __restrict__ y, const T* __restri
       for (int j = 0; j < 8; ++j) a[i][j] = b[i][j] = 0.f;
     }
   }
-  if (norm_y) rms_apply<T, L, V>(b, wy, sl, nc, cols, eps_y);
+  if (norm_y) rms_apply<T, L, V>(b, wy, wyr, sl, nc, cols, eps_y);
 #pragma unroll
   for (int i = 0; i < V; ++i)
 #pragma unroll
@@ -148,7 +202,7 @@ add_rmsnorm_kernel(T* __restrict__ h, const T* __restrict__ y, const T* __restri
     }
   }
   if (!n) return;
-  rms_apply<T, L, V>(a, wn, sl, nc, cols, eps_n);
+  rms_apply<T, L, V>(a, wn, wnr, sl, nc, cols, eps_n);
   if (!act) return;
 #pragma unroll
   for (int i = 0; i < V; ++i) {
