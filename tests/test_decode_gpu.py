@@ -251,11 +251,12 @@ def test_unsupported_shapes_are_refused():
 
 
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
-@pytest.mark.parametrize("b,D,P", [(3, 256, 4), (2, 1024, 8), (1, 128, 1)])
+@pytest.mark.parametrize("b,D,P", [(3, 256, 4), (2, 1024, 8), (1, 128, 1), (1, 256, 16)])
 def test_lazy_cham_decode_matches_eager_unitary_steps(dtype, b, D, P):
     """21 steps from a unitary hologram (folds every P steps; one non-finite token):
     the deferred-update step's outputs and, after a flush, its planes equal the eager
-    unitary step's to fp32 rounding order."""
+    unitary step's to fp32 rounding order.  P <= 8 folds with double-buffered factor
+    rows, P = 16 with one buffer."""
     n = 21
     q, k, v, g = random_cham_inputs(b, n, D, seed=790 + D + P, dtype=dtype)
     k[0, 5, 3] = float("nan")

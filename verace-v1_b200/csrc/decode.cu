@@ -584,7 +584,8 @@ __global__ void __launch_bounds__(DT) lazy_pre_kernel(LazyArgs A) {
 constexpr int LROWS = 64;                    // rows per stage
 constexpr int NSTG = 5;                      // stages
 constexpr int LSTAGE = 2 * LROWS * CWD * 4;  // 16 KB
-// dynamic smem: stages | A rows of the stage (fold steps) [LP_MAX][2][LROWS] | ks [D] | vs [D] | barriers
+// dynamic smem: stages | A rows of the stage (fold steps) [LP_MAX][2][LROWS], two buffers of
+// [LP_MAX / 2][2][LROWS] when P <= LP_MAX / 2 | ks [D] | vs [D] | barriers
 constexpr int LAS_OFF = NSTG * LSTAGE;
 constexpr int LKS_OFF = LAS_OFF + LP_MAX * 2 * LROWS * 4;
 size_t lazy_smem(int D) { return LKS_OFF + 2 * (size_t)D * 4 + 8 * NSTG + 16; }
@@ -647,7 +648,33 @@ lazy_cham_kernel(LazyArgs A, const __grid_constant__ CUtensorMap tm_r, const __g
     pbs[j][rr][c] = pb[((size_t)j * 4 + rr) * D + cs0 + c];
   }
   if (!fold && tid < 4 * p) gs[tid / 4][tid % 4] = A.g[((size_t)item * LP_MAX + tid / 4) * 4 + tid % 4];
-  block_sum4(dots, fin, dsc);      // also makes ks/vs/qs/pbs/gs and the barrier inits visible
+  // Fold steps with P <= LP_MAX / 2 double-buffer the A rows: stage rb + 1's rows are
+  // loaded into registers during stage rb and stored to the other buffer after its
+  // compute, so no stage waits for them.
+  const bool adbl = fold && P <= LP_MAX / 2;
+  const int an = P * 2 * LROWS;            // A values per stage
+  float apre[LP_MAX / 2];
+  auto a_fetch = [&](int rb) {
+#pragma unroll
+    for (int u = 0; u < LP_MAX / 2; ++u) {
+      const int e = tid + DT * u;
+      if (e < an) apre[u] = __ldg(pa + (size_t)(e / LROWS) * D + rb * LROWS + e % LROWS);
+    }
+  };
+  auto a_put = [&](int rb) {
+    float* dst = as + (rb & 1) * (LP_MAX / 2) * 2 * LROWS;
+#pragma unroll
+    for (int u = 0; u < LP_MAX / 2; ++u) {
+      const int e = tid + DT * u;
+      if (e < an) dst[e] = apre[u];
+    }
+  };
+  if (adbl) {
+    a_fetch(0);
+    a_put(0);
+    if (NRB > 1) a_fetch(1);
+  }
+  block_sum4(dots, fin, dsc);      // also makes ks/vs/qs/pbs/gs, stage 0's A rows and the barrier inits visible
 
   // ---- one pass: column sums kᵀS, vᵀS and the readout partials S_re q, folding first
   float acc[4][4];
@@ -672,9 +699,14 @@ lazy_cham_kernel(LazyArgs A, const __grid_constant__ CUtensorMap tm_r, const __g
       xi2[h] = *reinterpret_cast<const float4*>(si + i * CWD + 4 * c8);
     }
     if (fold) {   // S += sum_j A_j B_j; each factor's four columns of B serve both rows
-      for (int e = tid; e < P * 2 * LROWS; e += DT)   // the stage's rows of every A_j (coalesced)
-        as[e] = __ldg(pa + (size_t)(e / LROWS) * D + rb * LROWS + e % LROWS);
-      __syncthreads();
+      const float* asb = as;
+      if (adbl) {
+        asb = as + (rb & 1) * (LP_MAX / 2) * 2 * LROWS;
+      } else {
+        for (int e = tid; e < an; e += DT)   // the stage's rows of every A_j (coalesced)
+          as[e] = __ldg(pa + (size_t)(e / LROWS) * D + rb * LROWS + e % LROWS);
+        __syncthreads();
+      }
 #pragma unroll 2
       for (int j = 0; j < P; ++j) {
         const float4 b0r = *reinterpret_cast<const float4*>(&pbs[j][0][4 * c8]);
@@ -684,7 +716,7 @@ lazy_cham_kernel(LazyArgs A, const __grid_constant__ CUtensorMap tm_r, const __g
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
           const int i = rp + 32 * h;
-          const float a0 = as[(2 * j) * LROWS + i], a1 = as[(2 * j + 1) * LROWS + i];
+          const float a0 = asb[(2 * j) * LROWS + i], a1 = asb[(2 * j + 1) * LROWS + i];
 #pragma unroll
           for (int jj = 0; jj < 4; ++jj) {
             comp(xr2[h], jj) += a0 * compc(b0r, jj) + a1 * compc(b1r, jj);
@@ -697,6 +729,10 @@ lazy_cham_kernel(LazyArgs A, const __grid_constant__ CUtensorMap tm_r, const __g
         const int i = rp + 32 * h;
         *reinterpret_cast<float4*>(sr + i * CWD + 4 * c8) = xr2[h];
         *reinterpret_cast<float4*>(si + i * CWD + 4 * c8) = xi2[h];
+      }
+      if (adbl && rb + 1 < NRB) {   // the other buffer was last read in stage rb - 1
+        a_put(rb + 1);
+        if (rb + 2 < NRB) a_fetch(rb + 2);
       }
     }
 #pragma unroll
@@ -723,15 +759,25 @@ lazy_cham_kernel(LazyArgs A, const __grid_constant__ CUtensorMap tm_r, const __g
     }
     if (tid == 0) {
       if (fold) {
+        // stage rb leaves by TMA store; the stage stored one step earlier, whose store has
+        // had a stage's compute to read it, takes the next load
         tc::tma_store_2d(&tm_r, stripe * CWD, item * D + rb * LROWS, sr);
         tc::tma_store_2d(&tm_i, stripe * CWD, item * D + rb * LROWS, si);
         tc::bulk_commit();
-        tc::bulk_wait_read<0>();
-      }
-      tc::fence_proxy_async();
-      if (rb + NSTG < NRB) {
-        issue(rb + NSTG);
-        issued = rb + NSTG + 1;
+        if (rb >= 1) {
+          tc::bulk_wait_read<1>();
+          tc::fence_proxy_async();
+          if (rb - 1 + NSTG < NRB) {
+            issue(rb - 1 + NSTG);
+            issued = rb + NSTG;
+          }
+        }
+      } else {
+        tc::fence_proxy_async();
+        if (rb + NSTG < NRB) {
+          issue(rb + NSTG);
+          issued = rb + NSTG + 1;
+        }
       }
     }
   }
@@ -847,14 +893,27 @@ lazy_cham_kernel(LazyArgs A, const __grid_constant__ CUtensorMap tm_r, const __g
   const float* pb0 = A.part + (size_t)item * nst * D;
   T* y = static_cast<T*>(A.cout) + voff;
   const int npend = fold ? 0 : p;
-  for (int i = tid; i < D; i += DT) {
-    float sacc = 0.f;
-#pragma unroll 8
-    for (int st = 0; st < nst; ++st) sacc += __ldcg(pb0 + (size_t)st * D + i);
-    for (int j = 0; j < npend; ++j)
-      sacc += pa[(size_t)j * 2 * D + i] * __ldcg(pbq + 2 * j) + pa[((size_t)j * 2 + 1) * D + i] * __ldcg(pbq + 2 * j + 1);
-    if (ok) sacc += ks[i] * u0 + vs[i] * u1;   // (an identity step adds nothing; k, v may be non-finite)
-    y[i] = from_f32<T>(sacc);
+  // rows i .. i + 3 per thread: one 16-byte load per stripe, 16 stripes in flight (the
+  // stripes summed in order)
+  for (int i = 4 * tid; i < D; i += 4 * DT) {
+    float sacc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll 16
+    for (int st = 0; st < nst; ++st) {
+      const float4 x = __ldcg(reinterpret_cast<const float4*>(pb0 + (size_t)st * D + i));
+      sacc[0] += x.x; sacc[1] += x.y; sacc[2] += x.z; sacc[3] += x.w;
+    }
+    for (int j = 0; j < npend; ++j) {
+      const float4 a0 = *reinterpret_cast<const float4*>(pa + (size_t)j * 2 * D + i);
+      const float4 a1 = *reinterpret_cast<const float4*>(pa + ((size_t)j * 2 + 1) * D + i);
+      const float q0 = __ldcg(pbq + 2 * j), q1 = __ldcg(pbq + 2 * j + 1);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) sacc[e] += compc(a0, e) * q0 + compc(a1, e) * q1;
+    }
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      if (ok) sacc[e] += ks[i + e] * u0 + vs[i + e] * u1;   // (an identity step adds nothing; k, v may be non-finite)
+      y[i + e] = from_f32<T>(sacc[e]);
+    }
   }
   // this step's A part (zero for an identity step, so that nothing non-finite is kept)
   __syncthreads();
