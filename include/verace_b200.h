@@ -211,6 +211,35 @@ VERACE_API int verace_add_rmsnorm(void* h, const void* y, int norm_y, const void
                                   const void* n_weight, float n_eps, void* n, long long rows, int cols, int dtype,
                                   void* stream);
 
+/* ------------------------------------------------------------------------------
+ * M-CMoE (Manifold Continuous Mixture-of-Experts), ManifoldContinuousMoE.forward
+ * (verace_v1/modules/mcmoe.py:58-120).
+ * verace_mcmoe_route: the router's top-K and gate weights (mcmoe.py:91-96): for each of
+ *   n rows of C logits, the K largest (descending; NaN ranks first, ties to the lower
+ *   index) as int64 indices [n][K] and softmax over those K logits [n][K] in `dtype`.
+ *   C <= 256, K <= min(C, 16).
+ * verace_mcmoe_projection: replaces launch_mcmoe_triton_projection
+ *   (verace_v1/serving/triton_kernels.py:688-723; kernel :313-353):
+ *   out[t] = sum_k w[t,k] U[c] (sigma[t,c,:] * (V[c] x_t)),  c = idx[t,k], with x [n][d],
+ *   u_basis [C][d][r], v_basis [C][r][d], idx/w [n][K], sigma [n][C][r], out [n][d], all
+ *   in `dtype` except idx (int64).  sigma_is_logits != 0: sigma holds the hyper-network's
+ *   pre-activation and sigmoid (rounded to dtype) is applied inside.  bf16 with
+ *   d % 128 == 0 and C*r % 128 == 0 runs on the tensor cores and needs
+ *   verace_mcmoe_workspace bytes of workspace; other cases need none.
+ * verace_situ_glu: SiTUGLU.forward's activation (verace_v1/modules/activations.py):
+ *   out = [b1 tanh(g/b1) sigmoid(g)] * [b2 tanh(u/b2)] elementwise over [n][cols], g and
+ *   u with row stride ld (e.g. the two halves of one [n][2 cols] projection), out dense.
+ * ---------------------------------------------------------------------------- */
+VERACE_API size_t verace_mcmoe_workspace(long long n, int d, int C, int r, int dtype);
+VERACE_API int verace_mcmoe_route(const void* logits, long long n, int C, int K, long long* idx, void* weights,
+                                  int dtype, void* stream);
+VERACE_API int verace_mcmoe_projection(const void* x, const void* u_basis, const void* v_basis, const long long* idx,
+                                       const void* weights, const void* sigma, int sigma_is_logits, void* out,
+                                       long long n, int d, int C, int r, int K, int dtype, void* workspace,
+                                       size_t workspace_bytes, void* stream);
+VERACE_API int verace_situ_glu(const void* gate, const void* up, long long ld, void* out, long long n, int cols,
+                               float beta1, float beta2, int dtype, void* stream);
+
 enum { VERACE_DECODE_UNITARY = 0, VERACE_DECODE_FIRST_ORDER = 1 };
 VERACE_API size_t verace_decode_workspace(int b, int D);
 VERACE_API int verace_decode_step(const void* sssd_q, const void* sssd_k, const void* sssd_v,

@@ -21,6 +21,12 @@ with, and the one its tests treat as ground truth), not its Triton kernels:
     rec_t = Re(NS(H_t)) q_t, y = RMSNorm(w_out rec):239-241
     exported state = raw H_s (never retracted)     :243
 * ``newton_schulz_unitary_retraction``             cham_memory.py:21-51
+* M-CMoE -- ``verace_v1/modules/mcmoe.py``, ``verace_v1/modules/activations.py``
+    base FFN w_down(SiTU-GLU(x))                  :66   (``SiTUGLU.forward``)
+    router top-K, softmax over the kept logits     :91-96
+    sigma = sigmoid(hyper_sigma x)                 :98
+    manifold = sum_k w_k U_c (sigma_c * (V_c x))   :108-117 (eager loop)
+    y = base + RMSNorm(manifold)                   :119
 
 The prefix products are formed sequentially (P_t = R_t P_{t-1}); the reference's
 Blelloch scan forms the same products in a different association order, which only
@@ -42,6 +48,7 @@ __all__ = [
     "sssd_cayley_factors", "sssd_scan", "sssd_forward",
     "cham_cayley_factors", "cham_scan", "cham_forward",
     "newton_schulz_unitary_retraction", "sssd_projections", "cham_projections",
+    "situ_glu", "mcmoe_route", "mcmoe_projection", "mcmoe_forward",
 ]
 
 
@@ -218,3 +225,55 @@ def cham_forward(p, x, initial_hologram=None, active_mask=None, dtype=np.float64
     rec, H = cham_scan(q, k, v, gamma, initial_hologram, dtype=dtype)
     y = rms_norm(_linear(rec, p["w_out.weight"]), p["norm.weight"])
     return y, H
+
+
+# --------------------------------------------------------------------------------------
+# M-CMoE
+# --------------------------------------------------------------------------------------
+def situ_glu(p, x, beta1=4.0, beta2=25.0, prefix="base_situ_glu."):
+    """``SiTUGLU.forward`` (activations.py): [b1 tanh(g/b1) sigmoid(g)] * [b2 tanh(u/b2)]."""
+    g = _linear(x, p[prefix + "w_gate.weight"])
+    u = _linear(x, p[prefix + "w_up.weight"])
+    return (beta1 * np.tanh(g / beta1) * sigmoid(g)) * (beta2 * np.tanh(u / beta2))
+
+
+def mcmoe_route(logits, k):
+    """Top-k of each row (descending; ties to the lower index) and the softmax over the
+    kept logits, i.e. softmax of the row with the others masked to -inf (mcmoe.py:91-96).
+    Returns (indices [n, k], weights [n, k])."""
+    logits = np.asarray(logits)
+    idx = np.argsort(-logits, axis=-1, kind="stable")[:, :k]
+    top = np.take_along_axis(logits, idx, -1)
+    e = np.exp(top - top[:, :1])
+    return idx, e / e.sum(-1, keepdims=True)
+
+
+def mcmoe_projection(x, u_basis, v_basis, idx, w, sigma):
+    """The eager loop of mcmoe.py:108-117 (and the reference kernel's formula):
+    out[t] = sum_k w[t,k] U[c] (sigma[t,c,:] * (V[c] x_t)),  c = idx[t,k].
+    x [n,d], u_basis [C,d,r], v_basis [C,r,d], idx/w [n,K], sigma [n,C,r]."""
+    n, d = x.shape
+    out = np.zeros((n, d), dtype=np.result_type(x, u_basis))
+    rows = np.arange(n)
+    for k in range(idx.shape[1]):
+        c = idx[:, k]
+        vp = np.einsum("nrd,nd->nr", v_basis[c], x) * sigma[rows, c]
+        out += w[:, k:k + 1] * np.einsum("ndr,nr->nd", u_basis[c], vp)
+    return out
+
+
+def mcmoe_forward(p, x, rank, num_components, top_k, beta1=4.0, beta2=25.0, dtype=np.float64, norm_eps=None):
+    """``ManifoldContinuousMoE.forward`` (mcmoe.py:58-120), eager path.  norm_eps None means
+    the fp32 machine epsilon (torch.nn.RMSNorm(eps=None) on fp32 activations)."""
+    x = np.asarray(x, dtype=dtype)
+    p = {n: np.asarray(w, dtype=dtype) for n, w in p.items()}
+    b, s, d = x.shape
+    xf = x.reshape(b * s, d)
+    base = _linear(situ_glu(p, xf, beta1, beta2), p["base_w_down.weight"])
+    k = min(top_k, num_components)
+    idx, w = mcmoe_route(_linear(xf, p["router.weight"]), k)
+    sig = sigmoid(_linear(xf, p["hyper_sigma.weight"])).reshape(b * s, num_components, rank)
+    m = mcmoe_projection(xf, p["u_basis"], p["v_basis"], idx, w, sig)
+    eps = np.finfo(np.float32).eps if norm_eps is None else norm_eps
+    y = base + rms_norm(m, p["norm.weight"], eps)
+    return y.reshape(b, s, d)

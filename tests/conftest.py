@@ -50,3 +50,22 @@ def load_golden(name):
         else:
             d[rest] = z[key]
     return out
+
+
+def mcmoe_weights(g):
+    """The fp32 weights of an M-CMoE golden case, re-created with the module's constructor
+    under seed 0 (as tests/golden/make_golden.py built the reference's) and checked
+    against the fingerprints the reference's weights left in the golden file."""
+    import torch
+    import verace_v1_b200 as V
+    b, s, d, rank, C, K = (int(x) for x in g["dims"])
+    torch.manual_seed(0)
+    m = V.ManifoldContinuousMoE(hidden_dim=d, rank=rank, num_components=C, top_k_components=K)
+    sd = {k: v.detach().numpy().astype(np.float32) for k, v in m.state_dict().items()}
+    fps = {k[3:]: v for k, v in g.items() if k.startswith("fp/")}
+    assert sorted(fps) == sorted(sd), "parameter names differ from the reference's"
+    for k, v in sd.items():
+        f = v.astype(np.float64).ravel()
+        mine = np.concatenate([[f.sum(), (f * f).sum()], f[:16]])
+        np.testing.assert_allclose(mine, fps[k], rtol=1e-6, atol=1e-6, err_msg=f"weights of {k} differ")
+    return sd

@@ -13,8 +13,11 @@ the reference's test sweeps (tests/test_triton_kernels.py:86-225, tests/test_cha
 tests/test_sssd.py).  Module weights are saved with the inputs so that the oracle and
 the CUDA path can be run on exactly the same parameters.
 
-The output files (``sssd_golden.npz``, ``cham_golden.npz``, ``ns_golden.npz``) are
-committed; the GPU box never runs this script.
+M-CMoE (``ManifoldContinuousMoE.forward`` mcmoe.py:58-120) follows the reference's
+tests/test_mcmoe.py shape and the model's configuration (config.py:39-40).
+
+The output files (``sssd_golden.npz``, ``cham_golden.npz``, ``ns_golden.npz``,
+``mcmoe_golden.npz``) are committed; the GPU box never runs this script.
 """
 
 import argparse
@@ -42,7 +45,13 @@ def _put(store, prefix, **arrays):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", default=os.environ.get("VERACE_REFERENCE", ""))
+    ap.add_argument("--only", action="append", choices=["sssd", "cham", "ns", "mcmoe"],
+                    help="regenerate only these files (default: all)")
     args = ap.parse_args()
+
+    def want(name):
+        return not args.only or name in args.only
+
     if args.reference:
         sys.path.insert(0, args.reference)
     import torch
@@ -53,130 +62,163 @@ def main():
     # explicit multi-thread setting on this host (CLASWP parameter errors).
     torch.set_num_threads(1)
 
-    # ------------------------------------------------------------------ SSSD
-    sssd = {}
-    cases = []
-    # shape sweep of tests/test_triton_kernels.py:86-106 (seed 0)
-    for (b, s, d, h) in [(2, 8, 16, 2), (1, 1, 16, 1), (2, 13, 16, 2), (2, 8, 24, 2)]:
-        cases.append((f"sweep_b{b}_s{s}_d{d}_h{h}", 0, b, s, d, h, h * d, None))
-    # halted back half (tests/test_triton_kernels.py:109-125, seed 1)
-    cases.append(("halted", 1, 2, 10, 16, 2, 32, "back_half"))
-    # production head size, small hidden width (weights stay small)
-    cases.append(("d128", 11, 1, 16, 128, 2, 16, None))
-    cases.append(("d64_norm", 12, 2, 8, 64, 2, 128, None))  # tests/test_sssd.py:10-26 shape
-    for name, seed, b, s, d, h, hid, mask_kind in cases:
-        torch.manual_seed(seed)
-        m = SSSDAttention(hidden_dim=hid, num_heads=h, head_dim=d)
-        x = torch.randn(b, s, hid)
-        mask = None
-        if mask_kind == "back_half":
-            mask = torch.ones(b, s, dtype=torch.bool)
-            mask[:, s // 2:] = False
+    if want("sssd"):
+        # ------------------------------------------------------------------ SSSD
+        sssd = {}
+        cases = []
+        # shape sweep of tests/test_triton_kernels.py:86-106 (seed 0)
+        for (b, s, d, h) in [(2, 8, 16, 2), (1, 1, 16, 1), (2, 13, 16, 2), (2, 8, 24, 2)]:
+            cases.append((f"sweep_b{b}_s{s}_d{d}_h{h}", 0, b, s, d, h, h * d, None))
+        # halted back half (tests/test_triton_kernels.py:109-125, seed 1)
+        cases.append(("halted", 1, 2, 10, 16, 2, 32, "back_half"))
+        # production head size, small hidden width (weights stay small)
+        cases.append(("d128", 11, 1, 16, 128, 2, 16, None))
+        cases.append(("d64_norm", 12, 2, 8, 64, 2, 128, None))  # tests/test_sssd.py:10-26 shape
+        for name, seed, b, s, d, h, hid, mask_kind in cases:
+            torch.manual_seed(seed)
+            m = SSSDAttention(hidden_dim=hid, num_heads=h, head_dim=d)
+            x = torch.randn(b, s, hid)
+            mask = None
+            if mask_kind == "back_half":
+                mask = torch.ones(b, s, dtype=torch.bool)
+                mask[:, s // 2:] = False
+            with torch.no_grad():
+                out, state = m(x, return_state=True, active_mask=mask)
+            _put(sssd, name, x=x, out=out, state=state, mask=mask,
+                 dims=np.array([b, s, d, h, hid]))
+            for k, v in _sd(m).items():
+                sssd[f"{name}/p/{k}"] = v
+        # initial_state round trip (tests/test_triton_kernels.py:128-148, seed 2)
+        torch.manual_seed(2)
+        b, s, d, h = 2, 6, 16, 2
+        m = SSSDAttention(hidden_dim=h * d, num_heads=h, head_dim=d)
+        x1 = torch.randn(b, s, h * d)
+        x2 = torch.randn(b, s, h * d)
         with torch.no_grad():
-            out, state = m(x, return_state=True, active_mask=mask)
-        _put(sssd, name, x=x, out=out, state=state, mask=mask,
-             dims=np.array([b, s, d, h, hid]))
+            out1, st1 = m(x1, return_state=True)
+            out2, st2 = m(x2, initial_state=st1, return_state=True)
+        _put(sssd, "roundtrip", x1=x1, x2=x2, out1=out1, state1=st1, out2=out2, state2=st2,
+             dims=np.array([b, s, d, h, h * d]))
         for k, v in _sd(m).items():
-            sssd[f"{name}/p/{k}"] = v
-    # initial_state round trip (tests/test_triton_kernels.py:128-148, seed 2)
-    torch.manual_seed(2)
-    b, s, d, h = 2, 6, 16, 2
-    m = SSSDAttention(hidden_dim=h * d, num_heads=h, head_dim=d)
-    x1 = torch.randn(b, s, h * d)
-    x2 = torch.randn(b, s, h * d)
-    with torch.no_grad():
-        out1, st1 = m(x1, return_state=True)
-        out2, st2 = m(x2, initial_state=st1, return_state=True)
-    _put(sssd, "roundtrip", x1=x1, x2=x2, out1=out1, state1=st1, out2=out2, state2=st2,
-         dims=np.array([b, s, d, h, h * d]))
-    for k, v in _sd(m).items():
-        sssd[f"roundtrip/p/{k}"] = v
-    np.savez_compressed(os.path.join(HERE, "sssd_golden.npz"), **sssd)
+            sssd[f"roundtrip/p/{k}"] = v
+        np.savez_compressed(os.path.join(HERE, "sssd_golden.npz"), **sssd)
 
-    # ------------------------------------------------------------------ CHAM
-    cham = {}
-    cases = []
-    # shape sweep of tests/test_triton_kernels.py:151-173 (seed 3, hidden 32)
-    for (b, s, D) in [(2, 8, 16), (1, 1, 16), (2, 5, 16), (2, 8, 20), (2, 6, 160)]:
-        cases.append((f"sweep_b{b}_s{s}_D{D}", 3, b, s, D, 32, None))
-    cases.append(("halted", 4, 2, 10, 16, 32, "back_half"))      # :176-197
-    cases.append(("zero_gamma", 5, 2, 12, 16, 32, "all_off"))    # :200-223
-    cases.append(("long_s100", 7, 2, 100, 16, 32, None))         # :243-275
-    cases.append(("D64_s64", 13, 2, 64, 64, 64, None))
-    for name, seed, b, s, D, hid, mask_kind in cases:
-        print("cham case", name, flush=True)
-        torch.manual_seed(seed)
+    if want("cham"):
+        # ------------------------------------------------------------------ CHAM
+        cham = {}
+        cases = []
+        # shape sweep of tests/test_triton_kernels.py:151-173 (seed 3, hidden 32)
+        for (b, s, D) in [(2, 8, 16), (1, 1, 16), (2, 5, 16), (2, 8, 20), (2, 6, 160)]:
+            cases.append((f"sweep_b{b}_s{s}_D{D}", 3, b, s, D, 32, None))
+        cases.append(("halted", 4, 2, 10, 16, 32, "back_half"))      # :176-197
+        cases.append(("zero_gamma", 5, 2, 12, 16, 32, "all_off"))    # :200-223
+        cases.append(("long_s100", 7, 2, 100, 16, 32, None))         # :243-275
+        cases.append(("D64_s64", 13, 2, 64, 64, 64, None))
+        for name, seed, b, s, D, hid, mask_kind in cases:
+            print("cham case", name, flush=True)
+            torch.manual_seed(seed)
+            m = ContinuousHolographicMemory(hidden_dim=hid, holographic_dim=D)
+            x = torch.randn(b, s, hid)
+            mask = None
+            if mask_kind == "back_half":
+                mask = torch.ones(b, s, dtype=torch.bool)
+                mask[:, s // 2:] = False
+            elif mask_kind == "all_off":
+                mask = torch.zeros(b, s, dtype=torch.bool)
+            with torch.no_grad():
+                y, (Hr, Hi) = m(x, active_mask=mask)
+            _put(cham, name, x=x, out=y, Hr=Hr, Hi=Hi, mask=mask, dims=np.array([b, s, D, hid]))
+            for k, v in _sd(m).items():
+                cham[f"{name}/p/{k}"] = v
+        # initial_hologram round trip: two chunks through initial_hologram
+        torch.manual_seed(8)
+        b, s, D, hid = 2, 7, 24, 32
+        m = ContinuousHolographicMemory(hidden_dim=hid, holographic_dim=D)
+        x1 = torch.randn(b, s, hid)
+        x2 = torch.randn(b, s, hid)
+        with torch.no_grad():
+            y1, H1 = m(x1)
+            y2, H2 = m(x2, initial_hologram=H1)
+        _put(cham, "roundtrip", x1=x1, x2=x2, out1=y1, Hr1=H1[0], Hi1=H1[1], out2=y2,
+             Hr2=H2[0], Hi2=H2[1], dims=np.array([b, s, D, hid]))
+        for k, v in _sd(m).items():
+            cham[f"roundtrip/p/{k}"] = v
+        # non-unitary initial hologram (exercises the readout retraction of H_0)
+        torch.manual_seed(9)
+        b, s, D, hid = 2, 5, 16, 32
         m = ContinuousHolographicMemory(hidden_dim=hid, holographic_dim=D)
         x = torch.randn(b, s, hid)
-        mask = None
-        if mask_kind == "back_half":
-            mask = torch.ones(b, s, dtype=torch.bool)
-            mask[:, s // 2:] = False
-        elif mask_kind == "all_off":
-            mask = torch.zeros(b, s, dtype=torch.bool)
+        H0r = torch.eye(D).expand(b, D, D) + 0.05 * torch.randn(b, D, D)
+        H0i = 0.05 * torch.randn(b, D, D)
         with torch.no_grad():
-            y, (Hr, Hi) = m(x, active_mask=mask)
-        _put(cham, name, x=x, out=y, Hr=Hr, Hi=Hi, mask=mask, dims=np.array([b, s, D, hid]))
+            y, (Hr, Hi) = m(x, initial_hologram=(H0r, H0i))
+        _put(cham, "nonunitary_h0", x=x, H0r=H0r, H0i=H0i, out=y, Hr=Hr, Hi=Hi,
+             dims=np.array([b, s, D, hid]))
         for k, v in _sd(m).items():
-            cham[f"{name}/p/{k}"] = v
-    # initial_hologram round trip: two chunks through initial_hologram
-    torch.manual_seed(8)
-    b, s, D, hid = 2, 7, 24, 32
-    m = ContinuousHolographicMemory(hidden_dim=hid, holographic_dim=D)
-    x1 = torch.randn(b, s, hid)
-    x2 = torch.randn(b, s, hid)
-    with torch.no_grad():
-        y1, H1 = m(x1)
-        y2, H2 = m(x2, initial_hologram=H1)
-    _put(cham, "roundtrip", x1=x1, x2=x2, out1=y1, Hr1=H1[0], Hi1=H1[1], out2=y2,
-         Hr2=H2[0], Hi2=H2[1], dims=np.array([b, s, D, hid]))
-    for k, v in _sd(m).items():
-        cham[f"roundtrip/p/{k}"] = v
-    # non-unitary initial hologram (exercises the readout retraction of H_0)
-    torch.manual_seed(9)
-    b, s, D, hid = 2, 5, 16, 32
-    m = ContinuousHolographicMemory(hidden_dim=hid, holographic_dim=D)
-    x = torch.randn(b, s, hid)
-    H0r = torch.eye(D).expand(b, D, D) + 0.05 * torch.randn(b, D, D)
-    H0i = 0.05 * torch.randn(b, D, D)
-    with torch.no_grad():
-        y, (Hr, Hi) = m(x, initial_hologram=(H0r, H0i))
-    _put(cham, "nonunitary_h0", x=x, H0r=H0r, H0i=H0i, out=y, Hr=Hr, Hi=Hi,
-         dims=np.array([b, s, D, hid]))
-    for k, v in _sd(m).items():
-        cham[f"nonunitary_h0/p/{k}"] = v
-    # production holographic width D = 1024 (small hidden so the weights stay small);
-    # the 8 MiB state is summarised by its first rows, diagonal and column sums.
-    torch.manual_seed(10)
-    b, s, D, hid = 1, 3, 1024, 16
-    m = ContinuousHolographicMemory(hidden_dim=hid, holographic_dim=D)
-    x = torch.randn(b, s, hid)
-    with torch.no_grad():
-        y, (Hr, Hi) = m(x)
-    _put(cham, "D1024", x=x, out=y, dims=np.array([b, s, D, hid]),
-         Hr_rows=Hr[:, :4], Hi_rows=Hi[:, :4],
-         Hr_diag=torch.diagonal(Hr, dim1=-2, dim2=-1), Hi_diag=torch.diagonal(Hi, dim1=-2, dim2=-1),
-         Hr_colsum=Hr.sum(-2), Hi_colsum=Hi.sum(-2))
-    for k, v in _sd(m).items():
-        cham[f"D1024/p/{k}"] = v
-    np.savez_compressed(os.path.join(HERE, "cham_golden.npz"), **cham)
+            cham[f"nonunitary_h0/p/{k}"] = v
+        # production holographic width D = 1024 (small hidden so the weights stay small);
+        # the 8 MiB state is summarised by its first rows, diagonal and column sums.
+        torch.manual_seed(10)
+        b, s, D, hid = 1, 3, 1024, 16
+        m = ContinuousHolographicMemory(hidden_dim=hid, holographic_dim=D)
+        x = torch.randn(b, s, hid)
+        with torch.no_grad():
+            y, (Hr, Hi) = m(x)
+        _put(cham, "D1024", x=x, out=y, dims=np.array([b, s, D, hid]),
+             Hr_rows=Hr[:, :4], Hi_rows=Hi[:, :4],
+             Hr_diag=torch.diagonal(Hr, dim1=-2, dim2=-1), Hi_diag=torch.diagonal(Hi, dim1=-2, dim2=-1),
+             Hr_colsum=Hr.sum(-2), Hi_colsum=Hi.sum(-2))
+        for k, v in _sd(m).items():
+            cham[f"D1024/p/{k}"] = v
+        np.savez_compressed(os.path.join(HERE, "cham_golden.npz"), **cham)
 
-    # ------------------------------------------------------------------ NS retraction
-    ns = {}
-    torch.manual_seed(0)  # tests/test_cham.py:129-160
-    d = 16
-    Hr = torch.randn(2, d, d) * 0.1 + torch.eye(d)
-    Hi = torch.randn(2, d, d) * 0.1
-    r, i = newton_schulz_unitary_retraction(Hr.clone(), Hi.clone())
-    _put(ns, "d16", Hr=Hr, Hi=Hi, out_r=r, out_i=i)
-    torch.manual_seed(1)
-    d = 160
-    Hr = torch.randn(1, d, d) * 0.02 + torch.eye(d)
-    Hi = torch.randn(1, d, d) * 0.02
-    r, i = newton_schulz_unitary_retraction(Hr.clone(), Hi.clone())
-    _put(ns, "d160", Hr=Hr, Hi=Hi, out_r=r, out_i=i)
-    np.savez_compressed(os.path.join(HERE, "ns_golden.npz"), **ns)
-    for f in ("sssd_golden.npz", "cham_golden.npz", "ns_golden.npz"):
+    if want("ns"):
+        # ------------------------------------------------------------------ NS retraction
+        ns = {}
+        torch.manual_seed(0)  # tests/test_cham.py:129-160
+        d = 16
+        Hr = torch.randn(2, d, d) * 0.1 + torch.eye(d)
+        Hi = torch.randn(2, d, d) * 0.1
+        r, i = newton_schulz_unitary_retraction(Hr.clone(), Hi.clone())
+        _put(ns, "d16", Hr=Hr, Hi=Hi, out_r=r, out_i=i)
+        torch.manual_seed(1)
+        d = 160
+        Hr = torch.randn(1, d, d) * 0.02 + torch.eye(d)
+        Hi = torch.randn(1, d, d) * 0.02
+        r, i = newton_schulz_unitary_retraction(Hr.clone(), Hi.clone())
+        _put(ns, "d160", Hr=Hr, Hi=Hi, out_r=r, out_i=i)
+        np.savez_compressed(os.path.join(HERE, "ns_golden.npz"), **ns)
+    if want("mcmoe"):
+        # ------------------------------------------------------------------ M-CMoE
+        from verace_v1.modules.mcmoe import ManifoldContinuousMoE
+        mc = {}
+        # the reference test's shape (tests/test_mcmoe.py:8-12) and the model's M-CMoE
+        # (config.py: rank 32, 64 components, top-8) at hidden 256 and 1024
+        for name, b, s, d, rank, C, K in [("t256", 2, 8, 256, 16, 8, 8), ("m256", 2, 12, 256, 32, 64, 8),
+                                          ("m1024", 1, 16, 1024, 32, 64, 8)]:
+            torch.manual_seed(0)
+            m = ManifoldContinuousMoE(hidden_dim=d, rank=rank, num_components=C, top_k_components=K)
+            torch.manual_seed(1)
+            x = torch.randn(b, s, d)
+            with torch.no_grad():
+                y = m(x)
+                xf = x.reshape(b * s, d)
+                base = m.base_w_down(m.base_situ_glu(xf))
+                logits = m.router(xf)
+                # the routing lines of mcmoe.py:91-96, for the intermediate values
+                tl, ti = torch.topk(logits, k=min(K, C), dim=-1)
+                masked = torch.full_like(logits, float("-inf"))
+                masked.scatter_(-1, ti, tl)
+                tw = torch.gather(torch.softmax(masked, dim=-1), -1, ti)
+            _put(mc, name, x=x, y=y, base=base, logits=logits, topk_idx=ti, topk_w=tw,
+                 dims=np.array([b, s, d, rank, C, K]))
+            # the weights themselves are re-created by the tests (same constructor, seed 0);
+            # a fingerprint of each (sum, sum of squares, first 16 values) pins them
+            for k, v in _sd(m).items():
+                f = v.astype(np.float64).ravel()
+                mc[f"{name}/fp/{k}"] = np.concatenate([[f.sum(), (f * f).sum()], f[:16]])
+        np.savez_compressed(os.path.join(HERE, "mcmoe_golden.npz"), **mc)
+    for f in ("sssd_golden.npz", "cham_golden.npz", "ns_golden.npz", "mcmoe_golden.npz"):
         print(f, os.path.getsize(os.path.join(HERE, f)), "bytes")
 
 

@@ -121,3 +121,21 @@ def test_lazy_decode_rejects_bad_arguments_without_a_device():
     assert L.verace_decode_cham_lazy(*f, 8, fake, 0, 1024, 1, None, 0, None) == 0    # nothing to do
     assert L.verace_decode_cham_flush(fake, fake, fake, 0, 4, 1024, None) == 1
     assert L.verace_decode_cham_flush(fake, fake, fake, 8, 0, 1024, None) == 0
+
+
+def test_mcmoe_rejects_bad_arguments_without_a_device():
+    L = _lib.lib()
+    fake = ctypes.c_void_p(256)
+    assert L.verace_mcmoe_route(fake, 4, 300, 8, fake, fake, 1, None) == 2 and "C=300" in _err()
+    assert L.verace_mcmoe_route(fake, 4, 64, 17, fake, fake, 1, None) == 2
+    assert L.verace_mcmoe_route(fake, 4, 64, 8, fake, fake, 7, None) == 1 and "dtype" in _err()
+    assert L.verace_mcmoe_route(None, 0, 64, 8, None, None, 1, None) == 0   # nothing to do
+    assert L.verace_mcmoe_projection(fake, fake, fake, fake, fake, None, 0, fake, 4, 256, 64, 32, 8, 1, None, 0,
+                                     None) == 1 and "NULL" in _err()
+    # bf16 tensor-core path without its workspace
+    assert L.verace_mcmoe_projection(fake, fake, fake, fake, fake, fake, 0, fake, 4, 256, 64, 32, 8, 1, None, 0,
+                                     None) == 4 and "workspace" in _err()
+    assert L.verace_mcmoe_workspace(4, 256, 64, 32, 1) > L.verace_mcmoe_workspace(1, 256, 64, 32, 1)
+    assert L.verace_mcmoe_workspace(4, 100, 64, 32, 1) == 256            # direct path: none
+    assert L.verace_situ_glu(fake, fake, 4, fake, 2, 8, 4.0, 25.0, 1, None) == 1 and "ld" in _err()
+    assert L.verace_situ_glu(fake, fake, 8, fake, 2, 8, 4.0, 25.0, 5, None) == 1 and "dtype" in _err()

@@ -10,13 +10,14 @@ import numpy as np
 import pytest
 
 import oracle
-from conftest import load_golden
+from conftest import load_golden, mcmoe_weights
 
 TOL = dict(rtol=1e-3, atol=1e-4)
 
 SSSD = load_golden("sssd")
 CHAM = load_golden("cham")
 NS = load_golden("ns")
+MCMOE = load_golden("mcmoe")
 
 
 @pytest.mark.parametrize("case", [c for c in SSSD if c != "roundtrip"])
@@ -105,3 +106,20 @@ def test_oracle_detects_a_planted_error():
     p["w_k.weight"][:d] *= -1.0
     out, _ = oracle.sssd_forward(p, g["x"], h, d, return_state=True)
     assert not np.allclose(out, g["out"], **TOL)
+
+
+@pytest.mark.parametrize("case", sorted(MCMOE))
+def test_oracle_mcmoe_matches_reference(case):
+    """ManifoldContinuousMoE.forward (mcmoe.py:58-120): routing, base FFN and output."""
+    g = MCMOE[case]
+    b, s, d, rank, C, K = (int(x) for x in g["dims"])
+    p = mcmoe_weights(g)
+    xf = g["x"].reshape(b * s, d).astype(np.float64)
+    idx, w = oracle.mcmoe_route(g["logits"].astype(np.float64), min(K, C))
+    assert np.array_equal(idx, g["topk_idx"])
+    np.testing.assert_allclose(w, g["topk_w"], rtol=1e-5, atol=1e-7)
+    pd = {k: v.astype(np.float64) for k, v in p.items()}
+    base = oracle.situ_glu(pd, xf) @ pd["base_w_down.weight"].T
+    np.testing.assert_allclose(base, g["base"], **TOL)
+    y = oracle.mcmoe_forward(p, g["x"], rank, C, K)
+    np.testing.assert_allclose(y, g["y"], **TOL)

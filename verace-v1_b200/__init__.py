@@ -9,6 +9,8 @@ Public surface (mirrors the reference package verace_v1 for this path):
     rmsnorm, add_rmsnorm                             (block glue: RMSNorm, residual + RMSNorm)
     DecodeState, launch_decode_step, device_status   (batched incremental decode)
     launch_decode_cham_lazy, flush_pending, pending_storage (deferred hologram updates)
+    ManifoldContinuousMoE, SiTUGLU, launch_mcmoe_projection / launch_mcmoe_triton_projection,
+    launch_mcmoe_route, situ_glu                     (M-CMoE sub-layer)
 The kernels live in libverace_b200.so (C ABI: include/verace_b200.h), built by
 build.py; nothing here falls back to CPU or Python arithmetic.
 """
@@ -18,10 +20,14 @@ from .decode import (DecodeState, device_status, flush_pending, launch_decode_ch
                      pending_storage)
 from .sssd_attention import SSSDAttention
 from .cham_memory import ContinuousHolographicMemory, newton_schulz_unitary_retraction
+from .mcmoe import (ManifoldContinuousMoE, SiTUGLU, launch_mcmoe_projection, launch_mcmoe_route,
+                    launch_mcmoe_triton_projection, situ_glu)
 
 __all__ = [
     "SSSDAttention", "ContinuousHolographicMemory", "newton_schulz_unitary_retraction",
     "launch_sssd_scan", "launch_sssd_triton_scan", "launch_cham_update",
     "launch_cham_triton_update", "cham_retract", "DecodeState", "launch_decode_step",
     "device_status", "rmsnorm", "add_rmsnorm", "launch_decode_cham_lazy", "flush_pending", "pending_storage",
+    "ManifoldContinuousMoE", "SiTUGLU", "launch_mcmoe_projection", "launch_mcmoe_triton_projection",
+    "launch_mcmoe_route", "situ_glu",
 ]

@@ -41,6 +41,11 @@ _SIGNATURES = {
     "verace_rmsnorm": (_i, [_p, _p, _p, ctypes.c_longlong, _i, ctypes.c_float, _i, _p]),
     "verace_add_rmsnorm": (_i, [_p, _p, _i, _p, ctypes.c_float, _p, ctypes.c_float, _p, ctypes.c_longlong, _i, _i,
                                 _p]),
+    "verace_mcmoe_workspace": (_c_size, [ctypes.c_longlong, _i, _i, _i, _i]),
+    "verace_mcmoe_route": (_i, [_p, ctypes.c_longlong, _i, _i, _p, _p, _i, _p]),
+    "verace_mcmoe_projection": (_i, [_p] * 6 + [_i, _p, ctypes.c_longlong, _i, _i, _i, _i, _i, _p, _c_size, _p]),
+    "verace_situ_glu": (_i, [_p, _p, ctypes.c_longlong, _p, ctypes.c_longlong, _i, ctypes.c_float, ctypes.c_float,
+                             _i, _p]),
 }
 
 _lib = None

@@ -43,6 +43,7 @@ int cham_tc_scan(const void* q, const void* k, const void* v, const float* gamma
 int tc_read_status(cudaStream_t st, int* status);
 int sssd_tc_read_status(int* status);
 int decode_read_status(unsigned int* status);
+int mcmoe_read_status(int* status);
 
 namespace {
 
@@ -608,6 +609,9 @@ extern "C" int verace_device_status(void* stream) {
   int rc = tc_read_status((cudaStream_t)stream, &status);
   if (rc) return rc;
   rc = sssd_tc_read_status(&status2);
+  if (rc) return rc;
+  status |= status2;
+  rc = mcmoe_read_status(&status2);
   if (rc) return rc;
   status |= status2;
   unsigned int dstat = 0;   // bit 0: a hologram far from unitary; bit 1: a decode wait gave up

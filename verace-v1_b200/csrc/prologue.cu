@@ -9,7 +9,10 @@
 //
 // Work split: each head vector is normalised by a group of lanes of one warp (16-byte
 // loads, fp32 norms, segmented shuffle reductions): several short vectors share a warp,
-// long ones take a whole warp.  The gates are a grid-stride tail of the same launch.
+// long ones take a whole warp.  A lane group takes UPT consecutive vectors (adjacent
+// heads of a row) and issues all of their loads before the first reduction, so short
+// vectors still keep several 16-byte loads per thread in flight.  The gates are a
+// grid-stride tail of the same launch.
 #include "common.cuh"
 
 namespace verace {
@@ -70,50 +73,73 @@ __device__ __forceinline__ float sigmoid_f(float x) { return 1.f / (1.f + expf(-
 // warp with CPL chunks per lane.
 constexpr int MAXV = 8;   // chunks of 8 per lane: d <= 32 * 8 * 8 = 2048
 
-template <typename T, int CPL>
-__global__ void __launch_bounds__(PT)
+template <typename T, int CPL, int UPT>
+__global__ void __launch_bounds__(PT, 2)
 mixer_prologue_kernel(const T* __restrict__ y, long long ld, T* __restrict__ q, T* __restrict__ k,
                       T* __restrict__ v, float* __restrict__ gate, const unsigned char* __restrict__ mask,
                       long long n, int h, int d, int g, int silu_v, int L, long long nvec_blocks) {
   const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
   const int hd = h * d;
   if ((long long)blockIdx.x < nvec_blocks) {
-    const int upw = 32 / L;                                    // units per warp
-    const long long unit = ((long long)blockIdx.x * (PT / 32) + w) * upw + lane / L;   // (row, part, head)
-    const int sl = lane % L;                                   // lane within the unit
-    const bool active = unit < n * 3 * h;
-    const long long uu = active ? unit : 0;
-    const long long r = uu / (3 * h);
-    const int rem = (int)(uu % (3 * h)), part = rem / h, head = rem % h;
-    const T* src = y + r * ld + (long long)part * hd + (long long)head * d;
-    T* dst = (part == 0 ? q : part == 1 ? k : v) + r * hd + (long long)head * d;
-    const bool act = part == 2 && silu_v;
+    const int upw = 32 / L;                                    // lane groups per warp
+    const long long unit0 = (((long long)blockIdx.x * (PT / 32) + w) * upw + lane / L) * UPT;   // (row, part, head)
+    const int sl = lane % L;                                   // lane within the group
     const int nc = d / 8;
-    float x[CPL][8];
-    float ss = 0.f;
+    const long long nunits = n * 3 * h;
+    // unit = (row * 3 + part) * h + head: one 64-bit division per lane group, then steps
+    long long row0;
+    int rem0;
+    if (nunits < (1LL << 31)) {   // 32-bit division when it fits
+      row0 = (int)unit0 / (3 * h);
+      rem0 = (int)unit0 - (int)row0 * (3 * h);
+    } else {
+      row0 = unit0 / (3 * h);
+      rem0 = (int)(unit0 - row0 * (3 * h));
+    }
+    float x[UPT][CPL][8];
 #pragma unroll
-    for (int i = 0; i < CPL; ++i) {
-      const int cc = sl + L * i;
-      if (active && cc < nc) {
-        load8v<T>(src + 8 * cc, x[i]);
+    for (int u = 0; u < UPT; ++u) {
+      const bool active = unit0 + u < nunits;
+      const int wrap = (rem0 + u) / (3 * h), rem = rem0 + u - wrap * (3 * h);
+      const int part = rem / h, head = rem - part * h;
+      const T* src = y + (row0 + wrap) * ld + (long long)part * hd + (long long)head * d;
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          if (act) x[i][j] = silu_f(x[i][j]);
-          ss += x[i][j] * x[i][j];
-        }
+      for (int i = 0; i < CPL; ++i) {
+        const int cc = sl + L * i;
+        if (active && cc < nc) load8v<T>(src + 8 * cc, x[u][i]);
       }
     }
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1)
-      if (o < L) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-    const float inv = 1.f / fmaxf(sqrtf(ss), 1e-12f);
+    for (int u = 0; u < UPT; ++u) {
+      const bool active = unit0 + u < nunits;
+      const int wrap = (rem0 + u) / (3 * h), rem = rem0 + u - wrap * (3 * h);
+      const int part = rem / h, head = rem - part * h;
+      T* dst = (part == 0 ? q : part == 1 ? k : v) + (row0 + wrap) * hd + (long long)head * d;
+      const bool act = part == 2 && silu_v;
+      float ss = 0.f;
 #pragma unroll
-    for (int i = 0; i < CPL; ++i) {
-      const int cc = sl + L * i;
-      if (active && cc < nc) {
+      for (int i = 0; i < CPL; ++i) {
+        const int cc = sl + L * i;
+        if (active && cc < nc) {
 #pragma unroll
-        for (int j = 0; j < 8; ++j) x[i][j] *= inv;
-        store8v<T>(dst + 8 * cc, x[i]);
+          for (int j = 0; j < 8; ++j) {
+            if (act) x[u][i][j] = silu_f(x[u][i][j]);
+            ss += x[u][i][j] * x[u][i][j];
+          }
+        }
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1)
+        if (o < L) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+      const float inv = 1.f / fmaxf(sqrtf(ss), 1e-12f);
+#pragma unroll
+      for (int i = 0; i < CPL; ++i) {
+        const int cc = sl + L * i;
+        if (active && cc < nc) {
+#pragma unroll
+          for (int j = 0; j < 8; ++j) x[u][i][j] *= inv;
+          store8v<T>(dst + 8 * cc, x[u][i]);
+        }
       }
     }
     return;
@@ -121,8 +147,15 @@ mixer_prologue_kernel(const T* __restrict__ y, long long ld, T* __restrict__ q, 
   // gates: 0.1 sigmoid(y_gate) * mask
   const long long e = ((long long)blockIdx.x - nvec_blocks) * PT + threadIdx.x;
   if (e >= n * g) return;
-  const long long r = e / g;
-  const int j = (int)(e % g);
+  long long r;
+  int j;
+  if (n * g < (1LL << 31)) {   // 32-bit division when it fits
+    r = (int)e / g;
+    j = (int)e - (int)r * g;
+  } else {
+    r = e / g;
+    j = (int)(e - r * g);
+  }
   float val = 0.1f * sigmoid_f(to_f32(y[r * ld + 3LL * hd + j]));
   if (mask && !mask[r]) val = 0.f;
   gate[e] = val;
@@ -135,8 +168,9 @@ int launch_prologue(const void* y, long long ld, void* q, void* k, void* v, floa
   int L, cpl;
   if (nc <= 16 && (16 % nc) == 0) { L = nc; cpl = 1; }
   else { L = 32; cpl = (nc + 31) / 32; }
+  const int upt = 1;                  // vectors per lane group
   const long long units = n * 3 * h;
-  const long long per_block = (long long)(PT / 32) * (32 / L);
+  const long long per_block = (long long)(PT / 32) * (32 / L) * upt;
   const long long nvec_blocks = (units + per_block - 1) / per_block;
   const long long ngate_blocks = (n * g + PT - 1) / PT;
   const long long grid = nvec_blocks + ngate_blocks;
@@ -144,14 +178,14 @@ int launch_prologue(const void* y, long long ld, void* q, void* k, void* v, floa
   const T* yy = (const T*)y;
   T *qq = (T*)q, *kk = (T*)k, *vv = (T*)v;
   if (cpl == 1)
-    mixer_prologue_kernel<T, 1><<<(unsigned)grid, PT, 0, st>>>(yy, ld, qq, kk, vv, gate, mask, n, h, d, g, silu_v, L,
-                                                                nvec_blocks);
-  else if (cpl <= 4)
-    mixer_prologue_kernel<T, 4><<<(unsigned)grid, PT, 0, st>>>(yy, ld, qq, kk, vv, gate, mask, n, h, d, g, silu_v, L,
-                                                                nvec_blocks);
-  else
-    mixer_prologue_kernel<T, MAXV><<<(unsigned)grid, PT, 0, st>>>(yy, ld, qq, kk, vv, gate, mask, n, h, d, g, silu_v,
+    mixer_prologue_kernel<T, 1, 1><<<(unsigned)grid, PT, 0, st>>>(yy, ld, qq, kk, vv, gate, mask, n, h, d, g, silu_v,
                                                                    L, nvec_blocks);
+  else if (cpl <= 4)
+    mixer_prologue_kernel<T, 4, 1><<<(unsigned)grid, PT, 0, st>>>(yy, ld, qq, kk, vv, gate, mask, n, h, d, g, silu_v,
+                                                                   L, nvec_blocks);
+  else
+    mixer_prologue_kernel<T, MAXV, 1><<<(unsigned)grid, PT, 0, st>>>(yy, ld, qq, kk, vv, gate, mask, n, h, d, g,
+                                                                      silu_v, L, nvec_blocks);
   return check_launch("mixer_prologue_kernel");
 }
 
