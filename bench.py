@@ -262,12 +262,66 @@ def run_ours(args):
         del x
         torch.cuda.empty_cache()
         result["decode"] = run_decode(args, layers, embed, V, dev, rank, barrier, max_over_ranks)
+    if not args.no_mcmoe:
+        torch.cuda.empty_cache()
+        result["mcmoe"] = run_mcmoe(args, V, dev, barrier, max_over_ranks)
     if world == 1 and not args.no_cpu_baseline:
         result["cpu_baseline"] = cpu_sample(tokens=args.cpu_tokens)
     if rank == 0:
         print(json.dumps(result), flush=True)
     if world > 1:
         dist.destroy_process_group()
+
+
+def run_mcmoe(args, V, dev, barrier, max_over_ranks):
+    """The M-CMoE sub-layer (ManifoldContinuousMoE, mcmoe.py:58-120) at the config-2 token
+    count per GPU (b*s = 16384 tokens, hidden 1024, rank 32, 64 components, top-8, the
+    reference config's M-CMoE), bf16, random init; inputs resident in HBM, larger than L2
+    together (x 32 MB, hyper-network output 64 MB, the projection's intermediate 64 MB).
+    Times the manifold projection alone (verace_mcmoe_projection: two tcgen05 GEMMs) and
+    the whole sub-layer (base SiTU-GLU FFN, routing, projection, RMSNorm + residual)."""
+    import torch
+    c = CFG
+    n, d, r, C, K = c["batch"] * c["seq"], c["hidden"], 32, 64, 8
+    torch.manual_seed(0)
+    m = V.ManifoldContinuousMoE(hidden_dim=d, rank=r, num_components=C, top_k_components=K).to(dev, torch.bfloat16)
+    m.eval()
+    g = torch.Generator(device=dev).manual_seed(1)
+    x = torch.randn(1, n, d, generator=g, device=dev).to(torch.bfloat16)
+    with torch.no_grad():
+        xf = x.view(n, d)
+        idx, w = V.launch_mcmoe_route(m.router(xf), K)
+        pre = m.hyper_sigma(xf)
+        proj = lambda: V.launch_mcmoe_projection(xf, m.u_basis, m.v_basis, idx, w, pre, sigma_is_logits=True)
+        full = lambda: m(x)
+
+        def timed(fn, reps):
+            for _ in range(max(args.warmup, 3)):
+                fn()
+            barrier()
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for _ in range(reps):
+                fn()
+            e1.record()
+            torch.cuda.synchronize()
+            barrier()
+            return max_over_ranks(e0.elapsed_time(e1) / reps)
+
+        p_ms = timed(proj, 20)
+        f_ms = timed(full, 10)
+    _, bf16_burst, _, peak_kind = _peaks()
+    dense = 4.0 * n * d * C * r            # the two GEMMs over all components
+    active = 4.0 * n * d * K * r           # the selected components only (the reference's count)
+    tf = dense / (p_ms * 1e-3) / 1e12
+    return {"workload": f"M-CMoE sub-layer, {n} tokens, hidden {d}, rank {r}, {C} components, top-{K}, bf16",
+            "projection_us": p_ms * 1e3, "sublayer_us": f_ms * 1e3,
+            "tokens_per_s": n / (f_ms * 1e-3),
+            "roofline": {"kernel": "mcmoe_gemm_kernel x2 (verace_mcmoe_projection)", "bound": "tensor",
+                         "achieved": tf, "peak": bf16_burst, "unit": "TFLOP/s", "frac": tf / bf16_burst,
+                         "flop_per_call": dense, "active_flop_per_call": active,
+                         "peak_source": f"{peak_kind} bf16 dense GEMM (MEASURED_PEAKS.json, burst)"}}
 
 
 def run_decode(args, layers, embed, V, dev, rank, barrier, max_over_ranks):
@@ -463,7 +517,18 @@ def run_only(args):
     b, s = args.batch or c["batch"], args.seq or c["seq"]
     g = torch.Generator().manual_seed(0)
     nrm = torch.nn.functional.normalize
-    if args.only == "decode":
+    if args.only == "mcmoe":
+        V = sys.modules["verace_v1_b200"]
+        n, d, r, C, K = b * s, c["hidden"], 32, 64, 8
+        torch.manual_seed(0)
+        m = V.ManifoldContinuousMoE(hidden_dim=d, rank=r, num_components=C, top_k_components=K)
+        m = m.to(dev, torch.bfloat16).eval()
+        xf = torch.randn(n, d, generator=g).to(dev, torch.bfloat16)
+        with torch.no_grad():
+            idx, w = V.launch_mcmoe_route(m.router(xf), K)
+            pre = m.hyper_sigma(xf)
+        fn = lambda: V.launch_mcmoe_projection(xf, m.u_basis, m.v_basis, idx, w, pre, sigma_is_logits=True)
+    elif args.only == "decode":
         V = sys.modules["verace_v1_b200"]
         D = c["holo"]
         st = V.DecodeState(1, b, c["heads"], c["head_dim"], D, device=dev)
@@ -504,7 +569,8 @@ def main():
     ap.add_argument("--ref-tokens", type=int, default=8)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-decode", action="store_true", help="skip the config-3 decode measurement")
-    ap.add_argument("--only", choices=["cham", "sssd", "decode"], default=None,
+    ap.add_argument("--no-mcmoe", action="store_true", help="skip the M-CMoE sub-layer measurement")
+    ap.add_argument("--only", choices=["cham", "sssd", "decode", "mcmoe"], default=None,
                     help="time one scan entry point alone (kernel-level case for profiling)")
     ap.add_argument("--batch", type=int, default=None)
     ap.add_argument("--seq", type=int, default=None)

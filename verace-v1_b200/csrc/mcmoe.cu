@@ -17,10 +17,12 @@
 //     Yhat[t, c*r + j] = (x_t . V[c, j, :]) * sigma[t, c, j] * wsel[t, c]     (bf16)
 //     out[t, f]        = sum_{c, j} Yhat[t, c*r + j] * U[c, f, j]
 // with wsel[t, c] the routing weight of component c for token t and 0 when it is not
-// selected, so every unselected term is an exact zero.  Each GEMM: 128 x 128 output tiles,
+// selected, so every unselected term is an exact zero (r % 8 == 0: each 8-column group of
+// Yhat belongs to one component).  Each GEMM: 128 x 128 output tiles,
 // K blocks of 64 loaded by TMA with 128-byte swizzle, tcgen05 MMAs (M = N = 128, K = 16)
-// into a 128-column TMEM accumulator, three stages, two CTAs per SM; the epilogue stages
-// the tile in shared memory and leaves by TMA store.  U is first re-laid out as
+// into a 128-column TMEM accumulator, three stages, two CTAs per SM; eight epilogue warps
+// (a TMEM lane quarter and half of the columns each) stage the tile in shared memory and
+// it leaves by TMA store.  U is first re-laid out as
 // [d][C*r] so that the second GEMM's B operand is K-major like the first one's.
 // Other dtypes and shapes: one CTA per token evaluates the reference's formula in fp32.
 #include "common.cuh"
@@ -50,6 +52,9 @@ __device__ __forceinline__ float rnd(float x) {
 }
 
 __device__ __forceinline__ float sigmoid_f(float x) { return 1.f / (1.f + expf(-x)); }
+// The GEMM epilogue's sigmoid, whose result is rounded to bf16 at once: the fast exponent
+// and reciprocal intrinsics are well inside that rounding.
+__device__ __forceinline__ float sigmoid_fast(float x) { return __frcp_rn(1.f + __expf(-x)); }
 
 // ------------------------------------------------------------------------- routing
 // One warp per token: K rounds of a warp arg-max over the C logits (NaN ranks above every
@@ -133,7 +138,7 @@ constexpr int GBM = 128, GBN = 128, GBK = 64, GST = 3;
 constexpr int G_STAGE = (GBM + GBN) * GBK * 2;   // 32 KB
 constexpr int G_BAR = GST * G_STAGE;             // 96 KB
 constexpr int G_SMEM = G_BAR + 128;
-constexpr int G_THREADS = 192;                   // warp 0 TMA, warp 1 MMA (+ TMEM), warps 2-5 epilogue
+constexpr int G_THREADS = 320;                   // warp 0 TMA, warp 1 MMA (+ TMEM), warps 2-9 epilogue
 enum { EPI_STORE = 0, EPI_MASK = 1 };
 
 struct MaskArgs {
@@ -214,66 +219,71 @@ mcmoe_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant
       if (!ok) tc::mbar_wait(accf, 0, GPOLLS);
     }
   } else {
-    // ---- epilogue: warps 2-5, TMEM lane quarter warp % 4; thread = one output row
-    const int q = warp & 3, rl = 32 * q + lane, row = m0 + rl;
-    const bool got = tc::mbar_wait(accf, 0, GPOLLS) && !*fail;
+    // ---- epilogue: warps 2-9; TMEM lane quarter warp % 4, columns [64 hf, 64 hf + 64) with
+    // hf = (warp - 2) / 4; thread = one output row
+    const int q = warp & 3, hf = (warp - 2) >> 2, rl = 32 * q + lane, row = m0 + rl;
+    float wg[8];    // routing weight of each 8-column group of the thread's 64 columns (r % 8 == 0)
+    uint4 sgn[2];   // the next chunk's sigma (bf16), loaded while the current one is processed
+    auto load_sigma = [&](int u) {
+      if (row < M) {
+        const uint4* sp = reinterpret_cast<const uint4*>(ma.sigma + (size_t)row * N + n0 + 64 * hf + 16 * u);
+        sgn[0] = __ldg(sp);
+        sgn[1] = __ldg(sp + 1);
+      } else {
+        sgn[0] = sgn[1] = make_uint4(0, 0, 0, 0);
+      }
+    };
+    if constexpr (EPI == EPI_MASK) {   // (while the MMAs run)
+#pragma unroll
+      for (int gi = 0; gi < 8; ++gi) wg[gi] = 0.f;
+      if (row < M) {
+        int cg[8];   // component of each group
+#pragma unroll
+        for (int gi = 0; gi < 8; ++gi) cg[gi] = (n0 + 64 * hf + 8 * gi) / ma.r;
+#pragma unroll 1
+        for (int k = 0; k < ma.K; ++k) {
+          const int c = (int)ma.idx[(size_t)row * ma.K + k];
+          const float wk = to_f32(ma.w[(size_t)row * ma.K + k]);
+#pragma unroll
+          for (int gi = 0; gi < 8; ++gi)
+            if (c == cg[gi]) wg[gi] += wk;
+        }
+      }
+      load_sigma(0);
+    }
+    // one thread waits for the accumulator; the others sleep at the named barrier
+    __shared__ int acc_ok;
+    if (tid == 64) acc_ok = tc::mbar_wait(accf, 0, GPOLLS) && !*fail;
+    tc::named_sync(1, G_THREADS - 64);
+    const bool got = acc_ok != 0;
     if (!got) {
       atomicExch(&g_mcmoe_status, 1);
     } else {
       tc::fence_after_sync();
-      long long sel[MAX_TOPK];
-      float wsel_k[MAX_TOPK];
-      if constexpr (EPI == EPI_MASK) {
-#pragma unroll
-        for (int k = 0; k < MAX_TOPK; ++k) {
-          sel[k] = -1;
-          wsel_k[k] = 0.f;
-          if (k < ma.K && row < M) {
-            sel[k] = ma.idx[(size_t)row * ma.K + k];
-            wsel_k[k] = to_f32(ma.w[(size_t)row * ma.K + k]);
-          }
-        }
-      }
       const uint32_t lb = (uint32_t)(32 * q) << 16;
 #pragma unroll 1
-      for (int u = 0; u < GBN / 16; ++u) {
+      for (int u = 0; u < 4; ++u) {
+        const int cl = 64 * hf + 16 * u;   // tile column of the chunk
         float v[16];
-        tc::tmem_ld16(tacc + lb + 16 * u, v);
-        const int col0 = n0 + 16 * u;
+        tc::tmem_ld16(tacc + lb + cl, v);
         if constexpr (EPI == EPI_MASK) {
           float sg[16];
-          if (row < M) {
-            const uint4* sp = reinterpret_cast<const uint4*>(ma.sigma + (size_t)row * N + col0);
 #pragma unroll
-            for (int h = 0; h < 2; ++h) {
-              const uint4 raw = __ldg(sp + h);
-              const __nv_bfloat16* e = reinterpret_cast<const __nv_bfloat16*>(&raw);
+          for (int h = 0; h < 2; ++h) {
+            const __nv_bfloat16* e = reinterpret_cast<const __nv_bfloat16*>(&sgn[h]);
 #pragma unroll
-              for (int j = 0; j < 8; ++j) sg[8 * h + j] = __bfloat162float(e[j]);
-            }
-          } else {
-#pragma unroll
-            for (int j = 0; j < 16; ++j) sg[j] = 0.f;
+            for (int j = 0; j < 8; ++j) sg[8 * h + j] = __bfloat162float(e[j]);
           }
-          int cprev = -1;
-          float wc = 0.f;
+          if (u + 1 < 4) load_sigma(u + 1);
 #pragma unroll
           for (int j = 0; j < 16; ++j) {
-            const int c = (col0 + j) / ma.r;
-            if (c != cprev) {
-              cprev = c;
-              wc = 0.f;
-#pragma unroll
-              for (int k = 0; k < MAX_TOPK; ++k)
-                if (sel[k] == c) wc += wsel_k[k];
-            }
-            float s = sg[j];
-            if (ma.sigma_is_logits) s = rnd<__nv_bfloat16>(sigmoid_f(s));
-            v[j] = v[j] * s * wc;
+            float sv = sg[j];
+            if (ma.sigma_is_logits) sv = rnd<__nv_bfloat16>(sigmoid_fast(sv));
+            v[j] = v[j] * sv * wg[2 * u + (j >> 3)];
           }
         }
         // bf16 into the staged tile: two 64-column boxes, 128-byte rows, 128-byte swizzle
-        const int cl = 16 * u, box = cl >> 6, cb = cl & 63;
+        const int box = cl >> 6, cb = cl & 63;
         unsigned char* base = gsm + box * (GBM * 128) + rl * 128;
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
@@ -287,7 +297,7 @@ mcmoe_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant
       }
       tc::fence_proxy_async();
     }
-    tc::named_sync(1, 128);
+    tc::named_sync(1, G_THREADS - 64);
     if (got && tid == 64) {
       tc::tma_store_2d(&tmC, n0, m0, gsm);
       tc::tma_store_2d(&tmC, n0 + 64, m0, gsm + GBM * 128);
@@ -406,7 +416,7 @@ McWs mc_ws(long long n, int d, int C, int r) {
 
 bool tc_path(int dtype, int d, int C, int r, int K) {
   return dtype == VERACE_BF16 && d % GBN == 0 && d % GBK == 0 && ((long long)C * r) % GBN == 0 &&
-         ((long long)C * r) % GBK == 0 && K <= MAX_TOPK;
+         ((long long)C * r) % GBK == 0 && r % 8 == 0 && K <= MAX_TOPK;
 }
 
 }  // namespace
