@@ -45,7 +45,7 @@ def _put(store, prefix, **arrays):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", default=os.environ.get("VERACE_REFERENCE", ""))
-    ap.add_argument("--only", action="append", choices=["sssd", "cham", "ns", "mcmoe"],
+    ap.add_argument("--only", action="append", choices=["sssd", "cham", "ns", "mcmoe", "layer"],
                     help="regenerate only these files (default: all)")
     args = ap.parse_args()
 
@@ -218,7 +218,73 @@ def main():
                 f = v.astype(np.float64).ravel()
                 mc[f"{name}/fp/{k}"] = np.concatenate([[f.sum(), (f * f).sum()], f[:16]])
         np.savez_compressed(os.path.join(HERE, "mcmoe_golden.npz"), **mc)
-    for f in ("sssd_golden.npz", "cham_golden.npz", "ns_golden.npz", "mcmoe_golden.npz"):
+    if want("layer"):
+        # ------------------------------------------------------------------ layer + ACDE
+        # VeraceV1Layer.forward (backbone.py:53-101) and
+        # AdaptiveCognitiveDepthEngine.execute_adaptive_recurrent_loop (acd_engine.py:36-167)
+        # at a small configuration (head_dim 128 and D = 256, the widths the tensor-core
+        # paths take).  States are stored as sketches: psi @ r (r a fixed random vector)
+        # and H @ r, which the tests form from their own states.
+        from verace_v1.config import VeraceV1Config
+        from verace_v1.modules.backbone import VeraceV1Layer
+        from verace_v1.modules.acd_engine import AdaptiveCognitiveDepthEngine
+        ly = {}
+        cfg = VeraceV1Config(vocab_size=100, hidden_dim=256, num_layers=4, num_heads=2, head_dim=128,
+                             spectral_dim=64, chams_holographic_dim=256, mcmoe_rank=16, mcmoe_num_components=8)
+        g = torch.Generator().manual_seed(5)
+        r_d = torch.randn(128, generator=g)
+        r_D = torch.randn(256, generator=g)
+        ly["sketch/r_d"] = r_d.numpy()
+        ly["sketch/r_D"] = r_D.numpy()
+
+        def sk(prefix, psi, holo):
+            _put(ly, prefix, psi_r=psi @ r_d, hr_r=holo[0] @ r_D, hi_r=holo[1] @ r_D)
+
+        torch.manual_seed(0)
+        layers = torch.nn.ModuleList([VeraceV1Layer(i, cfg) for i in range(4)])
+        acde = AdaptiveCognitiveDepthEngine(hidden_dim=256, energy_threshold=0.99)
+        with torch.no_grad():   # halting that varies per token: some halt at layer 2, most at 3
+            acde.w_halting.bias.fill_(3.0)
+            acde.w_halting.weight.normal_(0.0, 0.2, generator=g)
+        ly["acde/w_halting.weight"] = acde.w_halting.weight.detach().numpy()
+        ly["acde/w_halting.bias"] = acde.w_halting.bias.detach().numpy()
+        torch.manual_seed(1)
+        x = torch.randn(2, 16, 256)
+        mask = torch.ones(2, 16, dtype=torch.bool)
+        mask[0, 3] = mask[1, 10:] = False
+        with torch.no_grad():
+            # layer 0: snapshot commit, fresh states
+            h1, br1, s1, c1 = layers[0](x)
+            _put(ly, "L0", x=x, h=h1, br=br1)
+            sk("L0", s1, c1)
+            # layer 1: AttnRes mixing over br1, carried states, partial active mask
+            h2, br2, s2, c2 = layers[1](h1, block_residual=br1, sssd_state=s1, cham_hologram=c1, active_mask=mask)
+            _put(ly, "L1", h=h2, br=br2, mask=mask)
+            sk("L1", s2, c2)
+            # ACDE over the four layers, then a continuation with 4 new tokens
+            torch.manual_seed(2)
+            xa = torch.randn(2, 12, 256)
+            fh, dc, st = acde.execute_adaptive_recurrent_loop(layers, xa, max_depth=12, min_depth=2)
+            _put(ly, "A0", x=xa, final_h=fh, depth=dc)
+            for l in range(4):
+                for i in range(2):
+                    if st[l][i] is None:
+                        ly[f"A0/none_{l}_{i}"] = np.array(1)
+                    else:
+                        sk(f"A0/s{l}_{i}", st[l][i][0], st[l][i][1])
+            xb = torch.randn(2, 4, 256)
+            fh2, dc2, st2 = acde.execute_adaptive_recurrent_loop(layers, xb, max_depth=12, min_depth=2,
+                                                                 initial_layer_states=st)
+            _put(ly, "A1", x=xb, final_h=fh2, depth=dc2)
+            for l in range(4):
+                for i in range(2):
+                    if st2[l][i] is not None:
+                        sk(f"A1/s{l}_{i}", st2[l][i][0], st2[l][i][1])
+        for k, v in _sd(layers).items():
+            f = v.astype(np.float64).ravel()
+            ly[f"layers/fp/{k}"] = np.concatenate([[f.sum(), (f * f).sum()], f[:16]])
+        np.savez_compressed(os.path.join(HERE, "layer_golden.npz"), **ly)
+    for f in ("sssd_golden.npz", "cham_golden.npz", "ns_golden.npz", "mcmoe_golden.npz", "layer_golden.npz"):
         print(f, os.path.getsize(os.path.join(HERE, f)), "bytes")
 
 

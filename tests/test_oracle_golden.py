@@ -123,3 +123,24 @@ def test_oracle_mcmoe_matches_reference(case):
     np.testing.assert_allclose(base, g["base"], **TOL)
     y = oracle.mcmoe_forward(p, g["x"], rank, C, K)
     np.testing.assert_allclose(y, g["y"], **TOL)
+
+
+def test_layer_and_acde_weights_match_the_reference_construction():
+    """Our VeraceV1Layer (and its SSSD / CHAM / M-CMoE modules) consume the RNG in the
+    reference's order, so seeded construction gives the reference's weights (the layer
+    goldens rely on it)."""
+    import torch
+    import verace_v1_b200 as V
+    from conftest import GOLDEN
+    z = np.load(f"{GOLDEN}/layer_golden.npz")
+    cfg = V.VeraceV1Config(vocab_size=100, hidden_dim=256, num_layers=4, num_heads=2, head_dim=128,
+                           spectral_dim=64, chams_holographic_dim=256, mcmoe_rank=16, mcmoe_num_components=8)
+    torch.manual_seed(0)
+    layers = torch.nn.ModuleList([V.VeraceV1Layer(i, cfg) for i in range(4)])
+    sd = layers.state_dict()
+    fps = {k[len("layers/fp/"):]: z[k] for k in z.files if k.startswith("layers/fp/")}
+    assert sorted(fps) == sorted(sd)
+    for k, v in sd.items():
+        f = v.detach().double().numpy().ravel()
+        np.testing.assert_allclose(np.concatenate([[f.sum(), (f * f).sum()], f[:16]]), fps[k], rtol=1e-6,
+                                   atol=1e-6, err_msg=k)

@@ -11,6 +11,8 @@ Public surface (mirrors the reference package verace_v1 for this path):
     launch_decode_cham_lazy, flush_pending, pending_storage (deferred hologram updates)
     ManifoldContinuousMoE, SiTUGLU, launch_mcmoe_projection / launch_mcmoe_triton_projection,
     launch_mcmoe_route, situ_glu                     (M-CMoE sub-layer)
+    VeraceV1Layer, AdaptiveCognitiveDepthEngine, VeraceV1Config (a decoder layer; the
+                                                     ACDE loop batched over items)
 The kernels live in libverace_b200.so (C ABI: include/verace_b200.h), built by
 build.py; nothing here falls back to CPU or Python arithmetic.
 """
@@ -22,6 +24,8 @@ from .sssd_attention import SSSDAttention
 from .cham_memory import ContinuousHolographicMemory, newton_schulz_unitary_retraction
 from .mcmoe import (ManifoldContinuousMoE, SiTUGLU, launch_mcmoe_projection, launch_mcmoe_route,
                     launch_mcmoe_triton_projection, situ_glu)
+from .config import VeraceV1Config
+from .layer import AdaptiveCognitiveDepthEngine, VeraceV1Layer
 
 __all__ = [
     "SSSDAttention", "ContinuousHolographicMemory", "newton_schulz_unitary_retraction",
@@ -29,5 +33,5 @@ __all__ = [
     "launch_cham_triton_update", "cham_retract", "DecodeState", "launch_decode_step",
     "device_status", "rmsnorm", "add_rmsnorm", "launch_decode_cham_lazy", "flush_pending", "pending_storage",
     "ManifoldContinuousMoE", "SiTUGLU", "launch_mcmoe_projection", "launch_mcmoe_triton_projection",
-    "launch_mcmoe_route", "situ_glu",
+    "launch_mcmoe_route", "situ_glu", "VeraceV1Config", "VeraceV1Layer", "AdaptiveCognitiveDepthEngine",
 ]
