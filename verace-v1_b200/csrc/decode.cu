@@ -59,6 +59,7 @@ constexpr int MAXD = 2048;     // largest hologram dimension
 constexpr int MAXHD = 128;     // largest SSSD head dimension
 constexpr int UNR = 4;         // row groups of 32 in flight per thread and pass
 constexpr float DRIFT_TOL = 1e-2f;
+constexpr uint32_t LPOLLS_SD = 1u << 22;   // bounded wait of the SSSD decode state copy
 
 struct DecodeArgs {
   const void* sq; const void* sk; const void* sv; const float* delta;
@@ -217,23 +218,35 @@ __device__ void sssd_part(const DecodeArgs& A, int chain) {
 }
 
 // SSSD-only step for head_dim 128 (the step's SSSD half when the CHAM half runs deferred):
-// one CTA per (item, head) holds the whole 128 x 128 state in registers (thread: rows
-// w + 8m, m < 16, columns 4 lane .. 4 lane + 3), so the state is read once, with all 16
-// loads of a thread in flight together, and written once; same arithmetic as sssd_part.
-// Two CTAs per SM.
+// one CTA per (item, head) holds the 128 x 128 state on chip, rows 0..39 in registers
+// (thread: rows w + 8m, m < 5, columns 4 lane .. 4 lane + 3) and rows 40..127 (44 KB,
+// contiguous in memory) in shared memory by one bulk copy, so the state is read once and
+// written once and four CTAs share an SM (all b*h chains of a decode batch of 64 in one
+// wave).  Same arithmetic and summation order as sssd_part.
+constexpr int SD_NREG = 5;                                  // row groups of 8 held in registers
+constexpr int SD_SROWS = 128 - 8 * SD_NREG;                 // rows in shared memory
+constexpr int SD_SMEM = SD_SROWS * 128 * 4;                 // 44 KB
 template <typename T>
-__global__ void __launch_bounds__(DT, 2) sssd_decode128_kernel(DecodeArgs A) {
+__global__ void __launch_bounds__(DT, 4) sssd_decode128_kernel(DecodeArgs A) {
   constexpr int HD = 128, NR = HD / 8;
+  extern __shared__ __align__(128) float4 srow[];           // [SD_SROWS][HD / 4]
   __shared__ float ks[HD], vs[HD], qs[HD];
   __shared__ float4 red[8][HD / 4][2];
   __shared__ float dsc[8][4];
+  __shared__ __align__(8) uint64_t sbar;
   const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
   const int chain = blockIdx.x;
   const size_t vec = (size_t)chain * HD;
   float* P = A.psi + (size_t)chain * HD * HD;
-  float4 ps[NR];
+  if (tid == 0) {
+    tc::mbar_init(&sbar, 1);
+    tc::fence_mbar_init();
+    tc::mbar_expect_tx(&sbar, SD_SMEM);
+    tc::bulk_load(srow, P + 8 * SD_NREG * HD, SD_SMEM, &sbar);
+  }
+  float4 ps[SD_NREG];
 #pragma unroll
-  for (int m = 0; m < NR; ++m) ps[m] = __ldcs(reinterpret_cast<const float4*>(P + (size_t)(w + 8 * m) * HD) + lane);
+  for (int m = 0; m < SD_NREG; ++m) ps[m] = __ldcs(reinterpret_cast<const float4*>(P + (size_t)(w + 8 * m) * HD) + lane);
   float dots[4] = {0.f, 0.f, 0.f, 0.f};
   bool fin = true;
   if (tid < HD) {
@@ -242,15 +255,28 @@ __global__ void __launch_bounds__(DT, 2) sssd_decode128_kernel(DecodeArgs A) {
     dots[0] = kx * kx; dots[1] = vx * vx; dots[2] = kx * vx;
     fin = isfinite(kx) && isfinite(vx);
   }
-  block_sum4(dots, fin, dsc);      // also makes ks/vs/qs visible
+  block_sum4(dots, fin, dsc);      // also makes ks/vs/qs and the barrier init visible
+  const bool got = tc::mbar_wait(&sbar, 0, LPOLLS_SD);
+  if (__syncthreads_or(!got)) {
+    // the copy may still land: wait for it (bounded) before the CTA releases its memory
+    if (tid == 0) {
+      atomicOr(&g_decode_status, 2u);
+      tc::mbar_wait(&sbar, 0, LPOLLS_SD);
+    }
+    return;
+  }
+  auto row_of = [&](int m) -> float4 {   // row w + 8m, this thread's 4 columns
+    return m < SD_NREG ? ps[m] : srow[(w + 8 * m - 8 * SD_NREG) * (HD / 4) + lane];
+  };
   float4 ak = make_float4(0.f, 0.f, 0.f, 0.f), av = ak;
 #pragma unroll
   for (int m = 0; m < NR; ++m) {
+    const float4 x = row_of(m);
     const float kr = ks[w + 8 * m], vr = vs[w + 8 * m];
-    ak.x = fmaf(kr, ps[m].x, ak.x); ak.y = fmaf(kr, ps[m].y, ak.y);
-    ak.z = fmaf(kr, ps[m].z, ak.z); ak.w = fmaf(kr, ps[m].w, ak.w);
-    av.x = fmaf(vr, ps[m].x, av.x); av.y = fmaf(vr, ps[m].y, av.y);
-    av.z = fmaf(vr, ps[m].z, av.z); av.w = fmaf(vr, ps[m].w, av.w);
+    ak.x = fmaf(kr, x.x, ak.x); ak.y = fmaf(kr, x.y, ak.y);
+    ak.z = fmaf(kr, x.z, ak.z); ak.w = fmaf(kr, x.w, ak.w);
+    av.x = fmaf(vr, x.x, av.x); av.y = fmaf(vr, x.y, av.y);
+    av.z = fmaf(vr, x.z, av.z); av.w = fmaf(vr, x.w, av.w);
   }
   red[w][lane][0] = ak;
   red[w][lane][1] = av;
@@ -278,7 +304,7 @@ __global__ void __launch_bounds__(DT, 2) sssd_decode128_kernel(DecodeArgs A) {
 #pragma unroll
   for (int m = 0; m < NR; ++m) {
     const int r = w + 8 * m;
-    float4 x = ps[m];
+    float4 x = row_of(m);
     if (ok) {
       const float kr = ks[r], vr = vs[r];
       x.x += fmaf(kr, al.x, vr * be.x); x.y += fmaf(kr, al.y, vr * be.y);
@@ -1028,9 +1054,10 @@ int launch_typed(const DecodeArgs& A, cudaStream_t st) {
   const int ncham = (A.D > 0) ? A.b * (A.D / CWD) : 0;
   const int grid = A.ns + ncham;
   const bool fo = A.mode == VERACE_DECODE_FIRST_ORDER;
-  if (A.D == 0 && A.d == 128)
-    sssd_decode128_kernel<T><<<grid, DT, 0, st>>>(A);
-  else if (A.D == 0)
+  if (A.D == 0 && A.d == 128) {
+    VERACE_CUDA(cudaFuncSetAttribute(sssd_decode128_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, SD_SMEM));
+    sssd_decode128_kernel<T><<<grid, DT, SD_SMEM, st>>>(A);
+  } else if (A.D == 0)
     decode_step_kernel<T, false, false><<<grid, DT, 0, st>>>(A);
   else if (fo)
     decode_step_kernel<T, true, true><<<grid, DT, 0, st>>>(A);
