@@ -566,13 +566,15 @@ struct LazyArgs {
 
 // The dot products between this step's k, v, q and the pending factors: one CTA per
 // (item, factor slot) (slots past the item's count return at once), each thread a few
-// rows of the six contiguous vectors, then a block reduction.
+// rows of the six contiguous vectors, then a block reduction.  The slot-0 CTA of each item
+// also zeroes the item's stripe counter for the lazy_cham_kernel launch that follows.
 template <typename T>
 __global__ void __launch_bounds__(DT) lazy_pre_kernel(LazyArgs A) {
   __shared__ float red[DT / 32][6];
   const int D = A.D, P = A.P;
   const int item = blockIdx.x / P, j = blockIdx.x % P;
   const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
+  if (j == 0 && tid == 0) A.cnt[item] = 0u;
   const int p = A.pcount[item];
   if (p >= P || j >= p) return;       // a folding step needs none of them
   const size_t voff = (size_t)item * D;
@@ -1241,8 +1243,7 @@ extern "C" int verace_decode_cham_lazy(const void* cham_q, const void* cham_k, c
   A.cqp = (float*)(base + L.cqp);
   A.cnt = (unsigned int*)(base + L.cnt);
   A.b = b; A.D = D; A.P = P;
-  VERACE_CUDA(cudaMemsetAsync(A.cnt, 0, (size_t)b * sizeof(unsigned int), st));
-  const unsigned grid = (unsigned)(b * (D / CWD));
+  const unsigned grid = (unsigned)(b * (D / CWD));   // (lazy_pre_kernel zeroes A.cnt)
   CUtensorMap mr, mi;
   if (int rc = make_plane_map(&mr, h_re, b, D)) return rc;
   if (int rc = make_plane_map(&mi, h_im, b, D)) return rc;
