@@ -7,6 +7,7 @@ states), <= 2e-2 on bf16 outputs, orthogonality of the state <= 1e-3.
 """
 import os
 
+import numpy as np
 import pytest
 import torch
 
@@ -76,3 +77,30 @@ def test_tc_sssd_nonfinite_token_is_identity():
     _status_ok()
     torch.testing.assert_close(st_b, st_i)
     torch.testing.assert_close(out_b, out_i)
+
+
+def test_tc_sssd_bf16_split_launch_chunk_ranges():
+    """bf16 with few chains and many chunks takes the split launch (the prep of chunk range
+    p + 1 beside the scan of range p, the state passed on through psi_out): 10 chunks in
+    uneven ranges, a partial last chunk, a carried state, halted tokens across a range
+    boundary and a non-finite token; then the same call again (shared side-stream
+    resources)."""
+    b, s, h = 1, 613, 8
+    q, k, v, delta = random_sssd_inputs(b, s, h, 128, seed=905, dtype=torch.bfloat16)
+    delta[:, 120:200] = 0.0
+    k[0, 333, 5, 11] = float("nan")
+    gen = torch.Generator().manual_seed(906)
+    psi0 = torch.linalg.qr(torch.randn(b, h, 128, 128, generator=gen))[0].cuda()
+    out, st = V.launch_sssd_scan(q, k, v, delta, psi0)
+    _status_ok()
+    d_ref = to_np(delta).copy()
+    d_ref[0, 333, 5] = 0.0
+    k_ref = to_np(k).copy()
+    k_ref[0, 333, 5, 11] = 0.0
+    o_ref, st_ref = oracle.sssd_scan(to_np(q), k_ref, to_np(v), d_ref, to_np(psi0))
+    assert np.isfinite(to_np(out)).all()
+    assert rel_fro(to_np(out), o_ref) <= 2e-2
+    assert rel_fro(to_np(st), st_ref) <= 1e-4
+    out2, st2 = V.launch_sssd_scan(q, k, v, delta, psi0)
+    torch.testing.assert_close(out2, out, rtol=0, atol=0)
+    torch.testing.assert_close(st2, st, rtol=0, atol=0)

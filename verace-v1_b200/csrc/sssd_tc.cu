@@ -10,6 +10,8 @@
 // products take hi*hi + hi*lo + lo*hi.  The state update accumulates straight into
 // the TMEM copy of S, which is read back to global memory only after the last chunk.
 // T for every chunk comes from sssd_tc_prep (all chunks in parallel, fp32 SIMT).
+#include <mutex>
+
 #include "common.cuh"
 #include "tc.cuh"
 #include "tmap.cuh"
@@ -72,7 +74,8 @@ constexpr int prep_ctas() { return sizeof(T) == 2 ? 3 : 1; }
 template <typename T>
 __global__ void __launch_bounds__(THR3, prep_ctas<T>())
 sssd_tc_prep(const T* __restrict__ k, const T* __restrict__ v, const float* __restrict__ delta,
-             unsigned char* __restrict__ Tws, unsigned long long* __restrict__ badws, int S, int H, int nch) {
+             unsigned char* __restrict__ Tws, unsigned long long* __restrict__ badws, int S, int H, int nch,
+             int c_base) {
   extern __shared__ __align__(16) float sm3[];
   constexpr int PW = R3 + 1, P = 132;
   constexpr bool BF = sizeof(T) == 2;   // bf16 inputs: G on the tensor cores (W is exact in bf16)
@@ -83,7 +86,7 @@ sssd_tc_prep(const T* __restrict__ k, const T* __restrict__ v, const float* __re
   __shared__ unsigned long long bad_bits;
   __shared__ __align__(8) uint64_t gbar;
   __shared__ uint32_t gslot;
-  const int c = blockIdx.x, chain = blockIdx.y, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int c = c_base + blockIdx.x, chain = blockIdx.y, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int bi = chain / H, hi = chain % H;
   const int t0 = c * C3, nt = min(C3, S - t0);
   if (BF && warp == 0) tc::tmem_alloc(&gslot, 128);
@@ -542,7 +545,7 @@ sssd_tc_scan_bf16(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
                   const __grid_constant__ CUtensorMap tm_v, const float* __restrict__ psi0,
                   __nv_bfloat16* __restrict__ out, float* __restrict__ psi_out,
                   const unsigned char* __restrict__ Tws, const unsigned long long* __restrict__ badws,
-                  int S, int H, int nch) {
+                  int S, int H, int nch, int c_begin, int c_end) {
   extern __shared__ __align__(1024) unsigned char sx[];
   auto sW = [&](int s) { return sx + Y_W + s * TILE3; };
   auto sQ = [&](int s) { return sx + Y_Q + s * Q_TILE; };
@@ -569,25 +572,28 @@ sssd_tc_scan_bf16(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
   const uint32_t lb = (uint32_t)(32 * (warp & 3)) << 16;
   const int row = 32 * (warp & 3) + lane, half = warp >> 2;
 
+  // The launch runs chunks [c_begin, c_end) (the state enters as psi0 and leaves as
+  // psi_out); j below counts chunks from c_begin, which sets the slots and barrier phases.
   // chunk j's W and Q into slot j & 1; chunk j's T into the T buffer (thread 0)
+  const int ncl = c_end - c_begin;
   auto issue_wq = [&](int j) {
-    const int s = j & 1;
+    const int s = j & 1, cg = c_begin + j;
     tc::mbar_expect_tx(&bar[1 + s], TILE3 + Q_TILE);
 #pragma unroll
     for (int kb = 0; kb < 2; ++kb) {
-      tc::tma_load_4d(sW(s) + kb * 16384, &tm_k, 64 * kb, hi, j * C3, bi, &bar[1 + s]);
-      tc::tma_load_4d(sW(s) + kb * 16384 + 8192, &tm_v, 64 * kb, hi, j * C3, bi, &bar[1 + s]);
-      tc::tma_load_4d(sQ(s) + kb * 8192, &tm_q, 64 * kb, hi, j * C3, bi, &bar[1 + s]);
+      tc::tma_load_4d(sW(s) + kb * 16384, &tm_k, 64 * kb, hi, cg * C3, bi, &bar[1 + s]);
+      tc::tma_load_4d(sW(s) + kb * 16384 + 8192, &tm_v, 64 * kb, hi, cg * C3, bi, &bar[1 + s]);
+      tc::tma_load_4d(sQ(s) + kb * 8192, &tm_q, 64 * kb, hi, cg * C3, bi, &bar[1 + s]);
     }
   };
   auto issue_t = [&](int j) {
     tc::mbar_expect_tx(&bar[3], 2 * TILE3);
-    tc::bulk_load(sT, Tws + ((size_t)chain * nch + j) * 2 * TILE3, 2 * TILE3, &bar[3]);
+    tc::bulk_load(sT, Tws + ((size_t)chain * nch + c_begin + j) * 2 * TILE3, 2 * TILE3, &bar[3]);
   };
-  int wq_issued = min(nch, 2), wq_done = 0, t_issued = nch > 0 ? 1 : 0, t_done = 0;
-  if (tid == 0 && nch > 0) {
+  int wq_issued = min(ncl, 2), wq_done = 0, t_issued = ncl > 0 ? 1 : 0, t_done = 0;
+  if (tid == 0 && ncl > 0) {
     issue_wq(0);
-    if (nch > 1) issue_wq(1);
+    if (ncl > 1) issue_wq(1);
     issue_t(0);
   }
 
@@ -649,12 +655,13 @@ sssd_tc_scan_bf16(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
   constexpr uint32_t ID_S = tc::idesc_bf16(128, 128, true, true);
   constexpr uint32_t ID_O = tc::idesc_bf16(128, 64, true, true);
 
-  for (int c = 0; c < nch; ++c) {
-    const int s = c & 1, t0 = c * C3, nt = min(C3, S - t0);
+  for (int j = 0; j < ncl; ++j) {
+    const int c = c_begin + j;
+    const int s = j & 1, t0 = c * C3, nt = min(C3, S - t0);
     const unsigned long long bad = badws[(size_t)chain * nch + c];
     tmem_to_x(tS);
-    if (!wait_all(&bar[1 + s], (c >> 1) & 1)) { failed = true; break; }
-    wq_done = c + 1;
+    if (!wait_all(&bar[1 + s], (j >> 1) & 1)) { failed = true; break; }
+    wq_done = j + 1;
     if (bad) {   // zero the k and v rows of non-finite tokens (both K blocks)
       for (int e = tid; e < C3 * 32; e += THR3) {
         const int tau = e >> 5, kv = (e >> 4) & 1, kb = (e >> 3) & 1, ch = e & 7;
@@ -683,8 +690,8 @@ sssd_tc_scan_bf16(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
     // ---- Cm = T Z
     tmem_to_x(tZ);
     sync_for_mma();
-    if (!wait_all(&bar[3], c & 1)) { failed = true; break; }
-    t_done = c + 1;
+    if (!wait_all(&bar[3], j & 1)) { failed = true; break; }
+    t_done = j + 1;
     if (tid == 0) {
       const uint32_t th = tc::smem_addr(sT), tl = th + TILE3;
       const uint32_t xh = tc::smem_addr(sXh), xl = tc::smem_addr(sXl);
@@ -701,9 +708,9 @@ sssd_tc_scan_bf16(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
       tc::commit(&bar[0]);
     }
     if (!wait_mma()) { failed = true; break; }
-    if (c + 1 < nch) {   // T(c) has been read
-      if (tid == 0) issue_t(c + 1);
-      t_issued = c + 2;
+    if (j + 1 < ncl) {   // T(c) has been read
+      if (tid == 0) issue_t(j + 1);
+      t_issued = j + 2;
     }
     // ---- E = Cm Q ; S += W Cm
     tmem_to_x(tC);
@@ -778,9 +785,9 @@ sssd_tc_scan_bf16(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
     // the slot is free again: chunk c + 2's W and Q go there
     tc::fence_proxy_async();
     __syncthreads();
-    if (c + 2 < nch) {
-      if (tid == 0) issue_wq(c + 2);
-      wq_issued = c + 3;
+    if (j + 2 < ncl) {
+      if (tid == 0) issue_wq(j + 2);
+      wq_issued = j + 3;
     }
   }
   if (failed) {
@@ -824,6 +831,44 @@ int make_head_map(CUtensorMap* m, const void* base, int b, int S, int H) {
 template <typename T>
 size_t sssd_tc_prep_smem() { return sizeof(float) * ((sizeof(T) == 2 ? 0 : HD * (R3 + 1)) + R3 * 132); }
 
+// Split launch (bf16): the scan runs one chain per CTA, so b*h chains busy at most b*h SMs
+// and the prep of every chunk (many short CTAs) runs first on the whole GPU.  When the
+// chains fill no more than half of the SMs, the call is cut into SSSD_PARTS chunk ranges:
+// the prep of range p + 1 runs on a side stream while the scan of range p runs on the
+// caller's stream (events order them; no kernel waits on another), and the state passes
+// from one range to the next through psi_out.  Streams and events are created once per
+// device; a capturing caller stream takes the single-launch path.
+constexpr int SSSD_PARTS = 4;
+struct SplitRes {
+  cudaStream_t side = nullptr;
+  cudaEvent_t ev[1 + SSSD_PARTS] = {};
+  bool ready = false;
+};
+constexpr int SPLIT_MAX_DEVICES = 64;
+SplitRes g_split[SPLIT_MAX_DEVICES];
+std::mutex g_split_mutex;
+
+int split_resources(int dev, SplitRes** out) {
+  SplitRes& r = g_split[dev];
+  if (!r.ready) {
+    VERACE_CUDA(cudaStreamCreateWithFlags(&r.side, cudaStreamNonBlocking));
+    for (auto& e : r.ev) VERACE_CUDA(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
+    r.ready = true;
+  }
+  *out = &r;
+  return VERACE_OK;
+}
+
+template <typename T>
+int launch_prep(const void* k, const void* v, const float* delta, unsigned char* Tws, unsigned long long* badws,
+                int s, int h, int chains, int nch, int c0, int c1, cudaStream_t st) {
+  const size_t ps = sssd_tc_prep_smem<T>();
+  VERACE_CUDA(cudaFuncSetAttribute(sssd_tc_prep<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ps));
+  sssd_tc_prep<T><<<dim3(c1 - c0, chains), THR3, ps, st>>>((const T*)k, (const T*)v, delta, Tws, badws, s, h, nch,
+                                                           c0);
+  return check_launch("sssd_tc_prep");
+}
+
 template <typename T>
 int launch_sssd_tc(const void* q, const void* k, const void* v, const float* delta, const float* psi0,
                    void* out, float* psi_out, int b, int s, int h, unsigned char* Tws,
@@ -831,12 +876,6 @@ int launch_sssd_tc(const void* q, const void* k, const void* v, const float* del
   const int chains = b * h;
   const int nch = (s + C3 - 1) / C3;
   int rc;
-  if (nch > 0) {
-    const size_t ps = sssd_tc_prep_smem<T>();
-    VERACE_CUDA(cudaFuncSetAttribute(sssd_tc_prep<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ps));
-    sssd_tc_prep<T><<<dim3(nch, chains), THR3, ps, st>>>((const T*)k, (const T*)v, delta, Tws, badws, s, h, nch);
-    if ((rc = check_launch("sssd_tc_prep"))) return rc;
-  }
   if constexpr (sizeof(T) == 2) {
     // (an empty sequence issues no copies; its maps only need valid extents)
     const int sm = s > 0 ? s : 1;
@@ -845,10 +884,39 @@ int launch_sssd_tc(const void* q, const void* k, const void* v, const float* del
         (rc = make_head_map(&mv, v, b, sm, h)))
       return rc;
     VERACE_CUDA(cudaFuncSetAttribute(sssd_tc_scan_bf16, cudaFuncAttributeMaxDynamicSharedMemorySize, SSSD_TC2_SMEM));
+    int dev = 0, sms = 0;
+    VERACE_CUDA(cudaGetDevice(&dev));
+    VERACE_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+    cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+    VERACE_CUDA(cudaStreamIsCapturing(st, &cap));
+    if (nch >= 2 * SSSD_PARTS && 2 * chains <= sms && cap == cudaStreamCaptureStatusNone &&
+        dev < SPLIT_MAX_DEVICES) {
+      std::lock_guard<std::mutex> lock(g_split_mutex);
+      SplitRes* r = nullptr;
+      if ((rc = split_resources(dev, &r))) return rc;
+      VERACE_CUDA(cudaEventRecord(r->ev[0], st));             // the inputs are ready
+      VERACE_CUDA(cudaStreamWaitEvent(r->side, r->ev[0], 0));
+      for (int p = 0; p < SSSD_PARTS; ++p) {
+        const int c0 = p * nch / SSSD_PARTS, c1 = (p + 1) * nch / SSSD_PARTS;
+        if ((rc = launch_prep<T>(k, v, delta, Tws, badws, s, h, chains, nch, c0, c1, r->side))) return rc;
+        VERACE_CUDA(cudaEventRecord(r->ev[1 + p], r->side));
+      }
+      for (int p = 0; p < SSSD_PARTS; ++p) {
+        const int c0 = p * nch / SSSD_PARTS, c1 = (p + 1) * nch / SSSD_PARTS;
+        VERACE_CUDA(cudaStreamWaitEvent(st, r->ev[1 + p], 0));
+        sssd_tc_scan_bf16<<<chains, THR3, SSSD_TC2_SMEM, st>>>(mq, mk, mv, p == 0 ? psi0 : psi_out,
+                                                              (__nv_bfloat16*)out, psi_out, Tws, badws, s, h, nch,
+                                                              c0, c1);
+        if ((rc = check_launch("sssd_tc_scan_bf16"))) return rc;
+      }
+      return VERACE_OK;
+    }
+    if (nch > 0 && (rc = launch_prep<T>(k, v, delta, Tws, badws, s, h, chains, nch, 0, nch, st))) return rc;
     sssd_tc_scan_bf16<<<chains, THR3, SSSD_TC2_SMEM, st>>>(mq, mk, mv, psi0, (__nv_bfloat16*)out, psi_out, Tws, badws,
-                                                          s, h, nch);
+                                                          s, h, nch, 0, nch);
     return check_launch("sssd_tc_scan_bf16");
   } else {
+    if (nch > 0 && (rc = launch_prep<T>(k, v, delta, Tws, badws, s, h, chains, nch, 0, nch, st))) return rc;
     VERACE_CUDA(cudaFuncSetAttribute(sssd_tc_scan<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, SSSD_TC_SMEM));
     sssd_tc_scan<T><<<chains, THR3, SSSD_TC_SMEM, st>>>((const T*)q, (const T*)k, (const T*)v, psi0, (T*)out,
                                                        psi_out, Tws, badws, s, h, nch);
