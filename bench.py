@@ -268,7 +268,7 @@ def run_ours(args):
                    "global_batch": b * world, "seq_len": s, "layers": c["layers"],
                    "parallelism": f"dp{world} (batch shards, no collective)",
                    "l2": "no flush: per-step working set (weights 190 MB + activations) > 126 MB L2"},
-        "roofline": {"kernel": "verace_cham_scan (cham_tc_prep_ws, then per group of 8 chunks one cham_tc_colpass2 "
+        "roofline": {"kernel": "verace_cham_scan (cham_tc_prep_ws, then per group of 12 chunks one cham_tc_colpass2 "
                                "and one cham_tc_readout_batch)",
                      "bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
                      "frac": achieved / hbm, "traffic": traffic,

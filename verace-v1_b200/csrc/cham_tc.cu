@@ -49,7 +49,7 @@ constexpr int Z_TILE = R2 * N2 * 2;        // 16 KB: 128 x 64 bf16
 constexpr int CA_TILE = R2 * NB2 * 2;      //  8 KB: 128 x 32 bf16
 constexpr int Y_TILE = C2 * NB2 * 2;       //  4 KB: 64 tokens x 32 columns bf16
 
-constexpr int RING = 8;          // chunks per column-pass group; the ring keeps two groups' end states
+constexpr int RING = 12;         // chunks per column-pass group; the ring keeps two groups' end states
 
 struct TcWs {
   unsigned char* T;          // [b][nch][4][T_TILE]: Tr_hi, Tr_lo, Ti_hi, Ti_lo
@@ -57,7 +57,7 @@ struct TcWs {
   unsigned long long* bad;   // [b][nch]
   float* Hre;
   float* Him;
-  float* ring;               // [min(nch, RING)][b][D][D]: real parts of chunk end states
+  float* ring;               // [min(nch, 2 RING)][b][D][D]: real parts of chunk end states
   int nring;
   unsigned char* cm;         // [2][b][D/64][64 KB]: fused schedule, Cm operands between launches
 };
