@@ -838,7 +838,7 @@ size_t sssd_tc_prep_smem() { return sizeof(float) * ((sizeof(T) == 2 ? 0 : HD * 
 // caller's stream (events order them; no kernel waits on another), and the state passes
 // from one range to the next through psi_out.  Streams and events are created once per
 // device; a capturing caller stream takes the single-launch path.
-constexpr int SSSD_PARTS = 4;
+constexpr int SSSD_PARTS = 3;
 struct SplitRes {
   cudaStream_t side = nullptr;
   cudaEvent_t ev[1 + SSSD_PARTS] = {};
