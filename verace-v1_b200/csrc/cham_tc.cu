@@ -1324,7 +1324,9 @@ readout_ws_body(const CUtensorMap& tm_k, const CUtensorMap& tm_v, const CUtensor
 
 // ---------------------------------------------------------------------------------
 // Readout for the batched schedule, two CTAs per SM: readout_ws_body with the fp32
-// state rows split in place (no separate split buffers).
+// state rows split in place (no separate split buffers), or, given `pre`, the rows
+// already split by the column pass: per K tile one 32 KB image (bf16 hi 16K | lo 16K,
+// K-major core matrices, rows i0 .. i0+127) taken by one bulk copy, with no split step.
 // smem: stage s at s*40K = state rows [128][64] fp32 (2 boxes, 32K; split in place into
 //       bf16 hi 16K | lo 16K) | Y [64 tok][64] (8K); phase 2: W (32K) at 0, E split at 40K
 // TMEM: O [0,64)
@@ -1335,7 +1337,7 @@ __device__ __forceinline__ void
 readout2_body(const CUtensorMap& tm_k, const CUtensorMap& tm_v, const CUtensorMap& tm_q,
                 const CUtensorMap& tm_sr, const float* __restrict__ Ews,
                 const unsigned long long* __restrict__ badws, __nv_bfloat16* __restrict__ out,
-                int S, int D, int nch, int c, int bx, int item, int srow) {
+                int S, int D, int nch, int c, int bx, int item, int srow, const unsigned char* __restrict__ pre) {
   extern __shared__ __align__(1024) unsigned char smw[];
   uint64_t* bars = reinterpret_cast<uint64_t*>(smw + RW2_BAR);
   uint32_t* tslot = reinterpret_cast<uint32_t*>(smw + RW2_BAR + 8 * N_BARS);
@@ -1376,8 +1378,12 @@ readout2_body(const CUtensorMap& tm_k, const CUtensorMap& tm_v, const CUtensorMa
       auto issue = [&](int kt) {
         const int s = kt & 1;
         tc::mbar_expect_tx(&bars[B_TFULL + s], 32 * 1024 + 8 * 1024);
-        tc::tma_load_2d(stA(s), &tm_sr, kt * RKT, srow + i0, &bars[B_TFULL + s]);
-        tc::tma_load_2d(stA(s) + 16 * 1024, &tm_sr, kt * RKT + 32, srow + i0, &bars[B_TFULL + s]);
+        if (pre != nullptr) {
+          tc::bulk_load(stA(s), pre + (size_t)(bx * NTR + kt) * (32 * 1024), 32 * 1024, &bars[B_TFULL + s]);
+        } else {
+          tc::tma_load_2d(stA(s), &tm_sr, kt * RKT, srow + i0, &bars[B_TFULL + s]);
+          tc::tma_load_2d(stA(s) + 16 * 1024, &tm_sr, kt * RKT + 32, srow + i0, &bars[B_TFULL + s]);
+        }
         tc::tma_load_3d(stY(s), &tm_q, kt * RKT, t0, item, &bars[B_TFULL + s]);
       };
       constexpr uint32_t ID_O = tc::idesc_bf16(128, C2, false, false);
@@ -1385,7 +1391,7 @@ readout2_body(const CUtensorMap& tm_k, const CUtensorMap& tm_v, const CUtensorMa
       if (NTR > 1) issue(1);
       for (int kt = 0; kt < NTR && ok; ++kt) {
         const int s = kt & 1;
-        if (!pwait(B_TFULL + s, (kt >> 1) & 1) || !pwait(B_SFULL + s, (kt >> 1) & 1)) break;
+        if (!pwait(B_TFULL + s, (kt >> 1) & 1) || (pre == nullptr && !pwait(B_SFULL + s, (kt >> 1) & 1))) break;
         tc::fence_after_sync();
         const uint32_t ah = tc::smem_addr(splitA(s)), al = ah + 16 * 1024;
         const uint32_t y = tc::smem_addr(stY(s));
@@ -1400,6 +1406,7 @@ readout2_body(const CUtensorMap& tm_k, const CUtensorMap& tm_v, const CUtensorMa
           if (!pwait(B_MDONE + s, (kt >> 1) & 1)) break;
           issue(kt + 2);
         }
+        if (kt == NTR - 1) tc::commit(&bars[B_EDONE]);   // every main-loop MMA done (phase 0)
       }
       // W rows [i0, i0+128) of the chunk (k block, v block), then O -= W mask(E)
       if (ok && pwait(B_MDONE + ((NTR - 1) & 1), ((NTR - 1) >> 1) & 1)) {
@@ -1433,7 +1440,7 @@ readout2_body(const CUtensorMap& tm_k, const CUtensorMap& tm_v, const CUtensorMa
       if (!all) { if (ok && tid == 0) record_timeout(); ok = false; *fail = 1; }
       return ok;
     };
-    for (int kt = 0; kt < NTR && ok; ++kt) {
+    for (int kt = 0; kt < NTR && ok && pre == nullptr; ++kt) {
       const int s = kt & 1;
       if (!cwait(B_TFULL + s, (kt >> 1) & 1)) break;
       unsigned char* ah = splitA(s);
@@ -1466,8 +1473,10 @@ readout2_body(const CUtensorMap& tm_k, const CUtensorMap& tm_v, const CUtensorMa
       tc::named_sync(1, CONS);
       if (tid == 0) tc::mbar_arrive(&bars[B_SFULL + s]);
     }
-    // the E operand goes into stage 1: wait until the last main-loop MMA has read it
-    if (ok && cwait(B_MDONE + ((NTR - 1) & 1), ((NTR - 1) >> 1) & 1)) {
+    // the E operand goes into stage 1: wait until the last main-loop MMA has read it (a
+    // barrier of its own: consumers that skip the split loop would otherwise meet the
+    // stage barriers at an ambiguous phase)
+    if (ok && cwait(B_EDONE, 0)) {
       // -mask(E): keep later tokens (tok(r) > t), zero tokens that are non-finite
       const float* Ein = Ews + chunk * R2 * C2;
 #pragma unroll
@@ -1724,7 +1733,7 @@ enum { B2_FULL = 0, B2_SPL = 3, B2_MD = 6, B2_TT = 9, B2_ZR = 10, B2_P1 = 11, B2
 
 __device__ __forceinline__ void
 colpass2_body(const CUtensorMap& tm_k, const CUtensorMap& tm_v, const CUtensorMap& tm_hr64, const CUtensorMap& tm_hi64,
-              const CUtensorMap& tm_hr128, const CUtensorMap& tm_hi128, const CUtensorMap& tm_ring64, int nring, int b,
+              const CUtensorMap& tm_hr128, const CUtensorMap& tm_hi128, unsigned char* __restrict__ ring, int nring, int b,
               const __nv_bfloat16* __restrict__ q, const unsigned char* __restrict__ Tws, float* __restrict__ Ews,
               const unsigned long long* __restrict__ badws, int S, int D, int nch, int c0, int c1, int item, int jb) {
   extern __shared__ __align__(1024) unsigned char smc[];
@@ -1764,13 +1773,15 @@ colpass2_body(const CUtensorMap& tm_k, const CUtensorMap& tm_v, const CUtensorMa
     const int src_identity = c == 0;
     // The state is updated in place in the output planes (phase A reads its column
     // block, phase B adds dH with TMA reductions); phase A also stores the real part it
-    // reads (the end state of chunk c-1) to that chunk's ring slot for the readout.
+    // reads (the end state of chunk c-1), split into bf16 hi / lo, to that chunk's ring
+    // slot as the readout's K-major operand images: row r, column j of an item's D x D
+    // real plane at ((r / 128) (D / 64) + j / 64) 32K + kmaj(r % 128, j % 64) (+ 16K for lo).
     const CUtensorMap* tm_sr = &tm_hr64;
     const CUtensorMap* tm_si = &tm_hi64;
     const CUtensorMap* tm_dr = &tm_hr128;
     const CUtensorMap* tm_di = &tm_hi128;
     const int src_row_re = 0, src_row_im = 0, dst_row_re = 0, dst_row_im = 0;
-    const int ring_row = c > 0 ? (((c - 1) % nring) * b + item) * D : -1;
+    unsigned char* ring_img = c > 0 ? ring + (((size_t)((c - 1) % nring) * b + item) * D) * D * sizeof(float) : nullptr;
 
     auto issue_a = [&](int h) {   // phase-A half tile h into slot h % 3
       const int s = h % 3;
@@ -1940,10 +1951,6 @@ colpass2_body(const CUtensorMap& tm_k, const CUtensorMap& tm_v, const CUtensorMa
         const int s = h % 3;
         if (!cwait(B2_FULL + s, (h / 3) & 1)) break;
         unsigned char* w = slot(s);
-        if (ring_row >= 0 && tid == 0) {   // the real half as read: chunk c-1's end state, for its readout
-          tc::tma_store_2d(&tm_ring64, j0, ring_row + h * KH, w + 16384);
-          tc::bulk_commit();
-        }
         if (patch_w) zero_bad_rows(w, 1);
         float x[2][8];
 #pragma unroll
@@ -1963,8 +1970,7 @@ colpass2_body(const CUtensorMap& tm_k, const CUtensorMap& tm_v, const CUtensorMa
             x[u][4] = b.x; x[u][5] = b.y; x[u][6] = b.z; x[u][7] = b.w;
           }
         }
-        if (ring_row >= 0 && tid == 0) tc::bulk_wait_read<0>();
-        tc::named_sync(1, CONS);   // every fp32 value (and the ring copy) read before the split overwrites it
+        tc::named_sync(1, CONS);   // every fp32 value read before the split overwrites it
 #pragma unroll
         for (int u = 0; u < 2; ++u) {
           const int e = tid + CONS * u;
@@ -1973,6 +1979,12 @@ colpass2_body(const CUtensorMap& tm_k, const CUtensorMap& tm_v, const CUtensorMa
           tc::split8(x[u], hv, lv);
           *reinterpret_cast<uint4*>(w + 16384 + mnmaj(i, gg * 8, NGW)) = hv;
           *reinterpret_cast<uint4*>(w + 16384 + mnmaj(i, N2 + gg * 8, NGW)) = lv;
+          if (gg < 4 && ring_img != nullptr) {   // the real half as read: chunk c-1's end state
+            const int r = h * KH + i, j = j0 + gg * 8;
+            unsigned char* img = ring_img + (size_t)((r >> 7) * (D / RKT) + (j >> 6)) * (32 * 1024) + kmaj(r & 127, j & 63, R2);
+            *reinterpret_cast<uint4*>(img) = hv;
+            *reinterpret_cast<uint4*>(img + 16 * 1024) = lv;
+          }
         }
         tc::fence_proxy_async();
         tc::named_sync(1, CONS);
@@ -2138,19 +2150,21 @@ __global__ void __launch_bounds__(CP2_THREADS, 2)
 cham_tc_colpass2(const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
                  const __grid_constant__ CUtensorMap tm_hr64, const __grid_constant__ CUtensorMap tm_hi64,
                  const __grid_constant__ CUtensorMap tm_hr128, const __grid_constant__ CUtensorMap tm_hi128,
-                 const __grid_constant__ CUtensorMap tm_ring64, const __grid_constant__ CUtensorMap tm_q,
-                 const __grid_constant__ CUtensorMap tm_ring128, int nring, int b, const __nv_bfloat16* __restrict__ q,
+                 const __grid_constant__ CUtensorMap tm_q, unsigned char* __restrict__ ring, int nring, int b,
+                 const __nv_bfloat16* __restrict__ q,
                  const unsigned char* __restrict__ Tws, float* __restrict__ Ews,
                  const unsigned long long* __restrict__ badws, __nv_bfloat16* __restrict__ out, int S, int D, int nch,
                  int c0, int c1, int r0, int nr) {
   const int ncol = D / NB2, nrb = D / R2;
   const int bid = blockIdx.x;
   if (bid < ncol * b) {
-    colpass2_body(tm_k, tm_v, tm_hr64, tm_hi64, tm_hr128, tm_hi128, tm_ring64, nring, b, q, Tws, Ews, badws, S, D, nch,
+    colpass2_body(tm_k, tm_v, tm_hr64, tm_hi64, tm_hr128, tm_hi128, ring, nring, b, q, Tws, Ews, badws, S, D, nch,
                   c0, c1, bid / ncol, bid % ncol);
   } else {
     const int r = bid - ncol * b, item = r / (nrb * nr), c = r0 + (r % (nrb * nr)) / nrb, bx = r % nrb;
-    readout2_body(tm_k, tm_v, tm_q, tm_ring128, Ews, badws, out, S, D, nch, c, bx, item, ((c % nring) * b + item) * D);
+    // (the fp32 state map is not read: the ring slot holds the pre-split images)
+    readout2_body(tm_k, tm_v, tm_q, tm_hr128, Ews, badws, out, S, D, nch, c, bx, item, 0,
+                  ring + (((size_t)(c % nring) * b + item) * D) * D * sizeof(float));
   }
 }
 
@@ -2549,14 +2563,17 @@ cham_tc_readout_batch(const __grid_constant__ CUtensorMap tm_k, const __grid_con
                       const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_ring,
                       const __grid_constant__ CUtensorMap tm_last, const float* __restrict__ Ews,
                       const unsigned long long* __restrict__ badws, __nv_bfloat16* __restrict__ out, int S, int D,
-                      int nch, int c0, int ring, int b, int c_last) {
+                      int nch, int c0, int ring, int b, int c_last, const unsigned char* __restrict__ pre_ring) {
   const int nrb = D / R2;
   const int c = c0 + (int)blockIdx.x / nrb, bx = (int)blockIdx.x % nrb;
   const int item = blockIdx.y;
-  // chunk c's end state: its ring slot, or for chunk c_last (if any) tm_last, a [b*D] plane
+  // chunk c's end state: its ring slot (fp32 rows, or with pre_ring the pre-split images),
+  // or for chunk c_last (if any) tm_last, a [b*D] fp32 plane
   const bool last = c == c_last;
+  const unsigned char* pre =
+      (last || pre_ring == nullptr) ? nullptr : pre_ring + (((size_t)(c % ring) * b + item) * D) * D * sizeof(float);
   readout2_body(tm_k, tm_v, tm_q, last ? tm_last : tm_ring, Ews, badws, out, S, D, nch, c, bx, item,
-                last ? item * D : ((c % ring) * b + item) * D);
+                last ? item * D : ((c % ring) * b + item) * D, pre);
 }
 
 // k or v as a [b][S][D] bf16 tensor, boxes of 64 elements x 64 tokens with 128-byte swizzle
@@ -2672,7 +2689,7 @@ int launch_cham_tc(const void* q, const void* k, const void* v, const float* gam
       if (c >= 1 && (c % w.nring == 0 || c == nch)) {
         const int cb = ((c - 1) / w.nring) * w.nring;
         cham_tc_readout_batch<<<dim3((D / R2) * (c - cb), b), WS_THREADS, RW2_SMEM, st>>>(
-            mk, mv, mq, m_ring, m_ring, w.E, w.bad, (__nv_bfloat16*)out, s, D, nch, cb, w.nring, b, -1);
+            mk, mv, mq, m_ring, m_ring, w.E, w.bad, (__nv_bfloat16*)out, s, D, nch, cb, w.nring, b, -1, nullptr);
         if ((rc = check_launch("cham_tc_readout_batch"))) return rc;
       }
     }
@@ -2686,9 +2703,11 @@ int launch_cham_tc(const void* q, const void* k, const void* v, const float* gam
     // (the last chunk's is hr), so group g's launch also runs the readouts of the chunks
     // group g-1 completed, in the SM slots its column pass leaves free; one readout
     // launch finishes the sequence.  The ring holds two groups, so the two never meet.
-    CUtensorMap mq, m_ring, m_ring64, m_hr64, m_hi64, m_hr128, m_hi128;
-    if ((rc = make_kv_map(&mq, q, b, s, D)) || (rc = make_state_map(&m_ring, w.ring, w.nring * b, D)) ||
-        (rc = make_state_map(&m_ring64, w.ring, w.nring * b, D, KH)) ||
+    // The ring slots hold the end states' real parts as the readout's pre-split bf16
+    // hi / lo operand images (the same bytes as fp32), written by phase A.
+    CUtensorMap mq, m_hr64, m_hi64, m_hr128, m_hi128;
+    unsigned char* ring = reinterpret_cast<unsigned char*>(w.ring);
+    if ((rc = make_kv_map(&mq, q, b, s, D)) ||
         (rc = make_state_map(&m_hr64, hr, b, D, KH)) || (rc = make_state_map(&m_hi64, hi, b, D, KH)) ||
         (rc = make_state_map(&m_hr128, hr, b, D)) || (rc = make_state_map(&m_hi128, hi, b, D)))
       return rc;
@@ -2699,13 +2718,13 @@ int launch_cham_tc(const void* q, const void* k, const void* v, const float* gam
       const int ce = std::min(nch, cb + RING);
       const int nr = std::max(cb - 1, 0) - r0;   // chunks [r0, cb - 1) have their end states in the ring
       cham_tc_colpass2<<<(D / NB2) * b + (D / R2) * nr * b, CP2_THREADS, CP2_SMEM, st>>>(
-          mk, mv, m_hr64, m_hi64, m_hr128, m_hi128, m_ring64, mq, m_ring, w.nring, b, (const __nv_bfloat16*)q, w.T,
-          w.E, w.bad, (__nv_bfloat16*)out, s, D, nch, cb, ce, r0, nr);
+          mk, mv, m_hr64, m_hi64, m_hr128, m_hi128, mq, ring, w.nring, b, (const __nv_bfloat16*)q, w.T, w.E, w.bad,
+          (__nv_bfloat16*)out, s, D, nch, cb, ce, r0, nr);
       if ((rc = check_launch("cham_tc_colpass2"))) return rc;
       r0 += nr;
     }
     cham_tc_readout_batch<<<dim3((D / R2) * (nch - r0), b), WS_THREADS, RW2_SMEM, st>>>(
-        mk, mv, mq, m_ring, m_hr128, w.E, w.bad, (__nv_bfloat16*)out, s, D, nch, r0, w.nring, b, nch - 1);
+        mk, mv, mq, m_hr128, m_hr128, w.E, w.bad, (__nv_bfloat16*)out, s, D, nch, r0, w.nring, b, nch - 1, ring);
     if ((rc = check_launch("cham_tc_readout_batch"))) return rc;
     return VERACE_OK;
   }
