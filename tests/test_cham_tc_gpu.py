@@ -56,11 +56,14 @@ def test_tc_scan_bf16_matches_fp64_oracle(b, s, D):
 
 
 @pytest.mark.parametrize("sched", ["batched", "fused"])
-@pytest.mark.parametrize("b,s,D", [(2, 700, 256), (1, 64, 128), (3, 65, 128)])
+@pytest.mark.parametrize("b,s,D", [(2, 700, 256), (1, 64, 128), (3, 65, 128), (2, 1733, 128)])
 def test_tc_scan_bf16_schedules_match_fp64_oracle(sched, b, s, D):
     """The column-pass schedules chosen at larger batches (state in place with TMA
     reductions and ring copies for the readout; one fused pass per chunk), forced at sizes
-    the oracle runs in seconds, across ring groups (s = 700: 11 chunks, groups of 8)."""
+    the oracle runs in seconds.  s = 700 is 11 chunks, one group of the batched schedule;
+    s = 1733 is 28 chunks: groups of 12, 12 and 4, the second and third group launches
+    running the previous group's readouts from the pre-split ring, whose 24 slots are
+    reused by chunks 24-26."""
     q, k, v, g = random_cham_inputs(b, s, D, seed=550 + s, dtype=torch.bfloat16)
     os.environ["VERACE_CHAM_SCHEDULE"] = sched
     try:
@@ -103,7 +106,8 @@ def test_tc_scan_zero_gamma_and_nonfinite_tokens():
     torch.testing.assert_close(out_b, out_i)
 
 
-@pytest.mark.parametrize("b,s,D", [(3, 600, 256), (2, 130, 1024), (1, 64, 128), (2, 10, 128)])
+@pytest.mark.parametrize("b,s,D", [(3, 600, 256), (2, 130, 1024), (1, 64, 128), (2, 10, 128), (2, 1733, 128),
+                                   (1, 900, 1024)])
 def test_schedules_agree(b, s, D):
     """The three bf16 schedules (merged per-chunk launches; column passes two CTAs per SM
     with batched readouts; one fused pass per chunk) run the same arithmetic, so the
