@@ -57,7 +57,8 @@ struct TcWs {
   unsigned long long* bad;   // [b][nch]
   float* Hre;
   float* Him;
-  float* ring;               // [min(nch, 2 RING)][b][D][D]: real parts of chunk end states
+  float* ring;               // [min(nch, 2 RING)][b][D][D]: real parts of chunk end states (fp32 rows,
+                             // or in the batched schedule the readout's bf16 hi / lo operand images)
   int nring;
   unsigned char* cm;         // [2][b][D/64][64 KB]: fused schedule, Cm operands between launches
 };
