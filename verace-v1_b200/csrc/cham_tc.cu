@@ -2724,6 +2724,7 @@ int launch_cham_tc(const void* q, const void* k, const void* v, const float* gam
       if ((rc = check_launch("cham_tc_colpass2"))) return rc;
       r0 += nr;
     }
+    // (chunks before the last read their pre-split ring images; the fp32 map serves the last)
     cham_tc_readout_batch<<<dim3((D / R2) * (nch - r0), b), WS_THREADS, RW2_SMEM, st>>>(
         mk, mv, mq, m_hr128, m_hr128, w.E, w.bad, (__nv_bfloat16*)out, s, D, nch, r0, w.nring, b, nch - 1, ring);
     if ((rc = check_launch("cham_tc_readout_batch"))) return rc;
