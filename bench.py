@@ -254,10 +254,10 @@ def run_ours(args):
     achieved = cham_bytes / (cham_ms * 1e-3) / 1e9
     cham_flop = 18.0 * D * D * b * s              # 9 D² MAC per token (8 state update + 1 readout)
     # DRAM bytes per (item, chunk) measured by ncu at b=16, s=256 (batched schedule, 64
-    # item-chunks per launch: profiles/cham_tc_colpass2_b16_s256.md 884.2 MB per column-pass
-    # launch; cham_tc_readout_batch_b16_s256.md 304.6 MB per readout launch;
+    # item-chunks per launch: profiles/cham_tc_colpass2_b16_s256.md 887.6 MB per column-pass
+    # launch; cham_tc_readout_batch_b16_s256.md 304.1 MB per readout launch;
     # cham_tc_prep_ws_b16_s256.md 16.8 MB per prep launch), scaled to this call
-    traffic = (884.2e6 + 304.6e6 + 16.8e6) / 64 * b * nch
+    traffic = (887.6e6 + 304.1e6 + 16.8e6) / 64 * b * nch
     result = {
         "metric": METRIC, "value": world * tokens_per_step / (ms * 1e-3), "unit": UNIT,
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
