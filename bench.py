@@ -69,6 +69,46 @@ def _peaks():
 
 
 # ------------------------------------------------------------------------------ clocks
+def rank_shard_ids(rank, batch, seq, vocab):
+    """The rank's shard of the synthetic prefill batch: `batch` sequences of `seq` token
+    ids from a generator seeded by the rank (weak scaling: every rank has the same amount
+    of work on items of its own; no data crosses ranks)."""
+    import torch
+    gen = torch.Generator().manual_seed(0 + rank)
+    return torch.randint(0, vocab, (batch, seq), generator=gen)
+
+
+def make_rank_sync(world, device):
+    """(barrier, max_over_ranks) for the current process group.  On a CUDA device both
+    synchronise the device around the collective, so the timed region is bracketed on
+    every rank; max_over_ranks reduces one float (a time in ms) to its maximum."""
+    import torch
+    import torch.distributed as dist
+    cuda = device.type == "cuda"
+
+    def barrier():
+        if cuda:
+            torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        if cuda:
+            torch.cuda.synchronize()
+
+    def max_over_ranks(ms):
+        if world == 1:
+            return ms
+        t = torch.tensor([ms], device=device, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    return barrier, max_over_ranks
+
+
+def whole_job_rate(world, units_per_rank_step, ms_per_step):
+    """Units all ranks processed per second, over the slowest rank's time per step."""
+    return world * units_per_rank_step / (ms_per_step * 1e-3)
+
+
 class ClockSampler:
     FIELDS = ["index", "clocks.sm", "clocks.max.sm", "power.draw", "clocks_event_reasons.active",
               "clocks_event_reasons.hw_slowdown", "clocks_event_reasons.hw_thermal_slowdown",
@@ -138,8 +178,7 @@ def run_ours(args):
             cham_norm=torch.nn.RMSNorm(c["hidden"], eps=1e-6),
             cham=V.ContinuousHolographicMemory(c["hidden"], c["holo"]))).to(dev, dt).eval())
     embed = torch.nn.Embedding(c["vocab"], c["hidden"]).to(dev, dt)
-    gen = torch.Generator().manual_seed(0 + rank)
-    ids = torch.randint(0, c["vocab"], (c["batch"], c["seq"]), generator=gen).to(dev)
+    ids = rank_shard_ids(rank, c["batch"], c["seq"], c["vocab"]).to(dev)
     with torch.no_grad():
         x = embed(ids).contiguous()
 
@@ -168,18 +207,7 @@ def run_ours(args):
             n = V.add_rmsnorm(h, cm.w_out(rec), y_norm=cm.norm, out_norm=nxt)
         return h
 
-    def barrier():
-        torch.cuda.synchronize()
-        if world > 1:
-            dist.barrier()
-        torch.cuda.synchronize()
-
-    def max_over_ranks(ms):
-        if world == 1:
-            return ms
-        t = torch.tensor([ms], device=dev, dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        return float(t.item())
+    barrier, max_over_ranks = make_rank_sync(world, dev)
 
     tokens_per_step = c["batch"] * c["seq"] * c["layers"]
     with torch.no_grad():
@@ -259,7 +287,7 @@ def run_ours(args):
     # cham_tc_prep_ws_b16_s256.md 16.8 MB per prep launch), scaled to this call
     traffic = (887.6e6 + 304.1e6 + 16.8e6) / 64 * b * nch
     result = {
-        "metric": METRIC, "value": world * tokens_per_step / (ms * 1e-3), "unit": UNIT,
+        "metric": METRIC, "value": whole_job_rate(world, tokens_per_step, ms), "unit": UNIT,
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
         "dtype": "bf16 (fp32 recurrent state)", "data": "synthetic",
@@ -276,7 +304,7 @@ def run_ours(args):
                      "peak_source": f"{peak_kind} HBM copy bandwidth (MEASURED_PEAKS.json)",
                      "tensor_tflops": cham_flop / (cham_ms * 1e-3) / 1e12,
                      "tensor_frac": cham_flop / (cham_ms * 1e-3) / 1e12 / bf16_sus},
-        "e2e": {"value": world * tokens_per_step / (e2e_ms * 1e-3), "unit": UNIT,
+        "e2e": {"value": whole_job_rate(world, tokens_per_step, e2e_ms), "unit": UNIT,
                 "h2d_bytes_per_step": x.numel() * x.element_size(),
                 "d2h_bytes_per_step": x.numel() * x.element_size()},
         "clocks": clocks,
