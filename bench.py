@@ -68,7 +68,7 @@ def _peaks():
     return 6650.0, 1590.0, 1400.0, "fallback"
 
 
-# ------------------------------------------------------------------------------ clocks
+# ------------------------------------------------------------------------------ ranks
 def rank_shard_ids(rank, batch, seq, vocab):
     """The rank's shard of the synthetic prefill batch: `batch` sequences of `seq` token
     ids from a generator seeded by the rank (weak scaling: every rank has the same amount
@@ -109,6 +109,7 @@ def whole_job_rate(world, units_per_rank_step, ms_per_step):
     return world * units_per_rank_step / (ms_per_step * 1e-3)
 
 
+# ------------------------------------------------------------------------------ clocks
 class ClockSampler:
     FIELDS = ["index", "clocks.sm", "clocks.max.sm", "power.draw", "clocks_event_reasons.active",
               "clocks_event_reasons.hw_slowdown", "clocks_event_reasons.hw_thermal_slowdown",
