@@ -2564,7 +2564,7 @@ cham_tc_readout_batch(const __grid_constant__ CUtensorMap tm_k, const __grid_con
                       const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_ring,
                       const __grid_constant__ CUtensorMap tm_last, const float* __restrict__ Ews,
                       const unsigned long long* __restrict__ badws, __nv_bfloat16* __restrict__ out, int S, int D,
-                      int nch, int c0, int ring, int b, int c_last, const unsigned char* __restrict__ pre_ring) {
+                      int nch, int c0, int nring, int b, int c_last, const unsigned char* __restrict__ pre_ring) {
   const int nrb = D / R2;
   const int c = c0 + (int)blockIdx.x / nrb, bx = (int)blockIdx.x % nrb;
   const int item = blockIdx.y;
@@ -2572,9 +2572,9 @@ cham_tc_readout_batch(const __grid_constant__ CUtensorMap tm_k, const __grid_con
   // or for chunk c_last (if any) tm_last, a [b*D] fp32 plane
   const bool last = c == c_last;
   const unsigned char* pre =
-      (last || pre_ring == nullptr) ? nullptr : pre_ring + (((size_t)(c % ring) * b + item) * D) * D * sizeof(float);
+      (last || pre_ring == nullptr) ? nullptr : pre_ring + (((size_t)(c % nring) * b + item) * D) * D * sizeof(float);
   readout2_body(tm_k, tm_v, tm_q, last ? tm_last : tm_ring, Ews, badws, out, S, D, nch, c, bx, item,
-                last ? item * D : ((c % ring) * b + item) * D, pre);
+                last ? item * D : ((c % nring) * b + item) * D, pre);
 }
 
 // k or v as a [b][S][D] bf16 tensor, boxes of 64 elements x 64 tokens with 128-byte swizzle
