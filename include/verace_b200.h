@@ -86,12 +86,18 @@ VERACE_API int verace_sssd_scan(const void* q, const void* k, const void* v, con
  * that cannot allocate device memory on the path that runs the scan (plugin or FFI
  * runtimes that own all device memory and pass only inputs and outputs; serving
  * loops with a fixed memory budget, where an allocation may synchronise the device).
- * Same arguments and results as verace_sssd_scan without the workspace: the scratch
- * is a fixed 16 MiB device array inside this library, which every GPU that loads the
- * library holds until the process exits.  Sizes whose scratch exceeds 16 MiB
- * (verace_sssd_scan_workspace(b, s, h, d) > 16 MiB) return VERACE_ERR_UNSUPPORTED.
+ * Same arguments as verace_sssd_scan without the workspace: the scratch is a fixed
+ * 16 MiB device array inside this library, which every GPU that loads the library holds
+ * until the process exits.  It always runs the fp32 SIMT scan kernels (32-token chunk
+ * transforms), whatever the head size, so its results equal verace_sssd_scan's to the
+ * fp32 parity tolerance (1e-4 relative), not bit for bit where verace_sssd_scan takes
+ * the tensor-core path (head_dim 128).  Limit: the scratch holds b*h*ceil(s/32) chunk
+ * transforms of 16 KiB each plus one 8-byte mask word per transform (each part rounded
+ * up to 256 bytes); sizes beyond 16 MiB return VERACE_ERR_UNSUPPORTED before any pointer
+ * is looked at (b*h*ceil(s/32) <= 1023, e.g. b = 2, h = 8, s = 2016).
  * The first call on a device looks the array's device address up (once per device,
- * with that device current); make that first call before any stream capture.
+ * with that device current); it returns VERACE_ERR_INVALID if `stream` is being
+ * captured at that moment, so make that first call before any stream capture.
  * All calls in a process share the one array per device: calls that overlap on the
  * GPU (issued on concurrent streams, or from several host threads) race on it and
  * give undefined results, so serialise them (one stream, or an event between calls).

@@ -12,8 +12,6 @@ checks that a size whose scratch would not fit is refused with a clear error.
 The file name sorts last so that a run that stops at the first failure has already
 run every other test; it passes alone in a fresh process as well.
 """
-import ctypes
-
 import pytest
 import torch
 
@@ -66,10 +64,17 @@ def test_noalloc_sssd_scan_matches_regular_entry_point_on_two_calls():
 
 
 def test_noalloc_sssd_scan_refuses_sizes_beyond_its_scratch():
+    # Every pointer is NULL: the size limit is checked before the pointers, so the call is
+    # refused with VERACE_ERR_UNSUPPORTED (2).  Should that check ever stop catching this
+    # size, the NULL-pointer check returns VERACE_ERR_INVALID (1) instead and the test fails
+    # without any kernel being launched.
     L = _lib.lib()
-    b, s, h, d = 8, 2048, 8, 128          # needs ~64 MiB of scratch
+    b, s, h, d = 8, 2048, 8, 128          # b*h*ceil(s/32) = 4096 transforms: ~64 MiB of scratch
     assert L.verace_sssd_scan_workspace(b, s, h, d) > (16 << 20)
-    fake = ctypes.c_void_p(256)
-    rc = L.verace_sssd_scan_noalloc(fake, fake, fake, fake, None, fake, fake, b, s, h, d, 0, None)
+    rc = L.verace_sssd_scan_noalloc(None, None, None, None, None, None, None, b, s, h, d, 0, None)
     assert rc == 2
     assert "fixed" in L.verace_last_error().decode()
+    # the largest size that fits (1023 transforms) passes the size check and then stops at
+    # the NULL pointers
+    rc = L.verace_sssd_scan_noalloc(None, None, None, None, None, None, None, 1, 1023 * 32, 1, 128, 0, None)
+    assert rc == 1

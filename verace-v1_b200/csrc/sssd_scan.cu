@@ -345,13 +345,19 @@ constexpr int MAX_DEVICES = 64;
 std::mutex g_noalloc_mutex;
 void* g_noalloc_ptr[MAX_DEVICES] = {};
 
-int noalloc_scratch(void** out) {
+int noalloc_scratch(void** out, cudaStream_t stream) {
   int dev = 0;
   VERACE_CUDA(cudaGetDevice(&dev));
   VERACE_REQUIRE(dev >= 0 && dev < MAX_DEVICES, VERACE_ERR_UNSUPPORTED,
                  "verace_sssd_scan_noalloc: device ordinal %d out of range", dev);
   std::lock_guard<std::mutex> lock(g_noalloc_mutex);
   if (g_noalloc_ptr[dev] == nullptr) {
+    // the address lookup is a runtime call that must not be recorded into a graph
+    cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+    VERACE_CUDA(cudaStreamIsCapturing(stream, &cap));
+    VERACE_REQUIRE(cap == cudaStreamCaptureStatusNone, VERACE_ERR_INVALID,
+                   "verace_sssd_scan_noalloc: the first call on device %d came while its stream is "
+                   "being captured; make one call on this device before any capture", dev);
     void* p = nullptr;
     VERACE_CUDA(cudaGetSymbolAddress(&p, g_sssd_noalloc_scratch));
     g_noalloc_ptr[dev] = p;
@@ -374,16 +380,17 @@ extern "C" int verace_sssd_scan_noalloc(const void* q, const void* k, const void
   VERACE_REQUIRE(dtype == VERACE_F32 || dtype == VERACE_BF16 || dtype == VERACE_F16,
                  VERACE_ERR_INVALID, "verace_sssd_scan_noalloc: unknown dtype %d", dtype);
   if (b == 0) return VERACE_OK;
-  VERACE_REQUIRE(psi_out != nullptr, VERACE_ERR_INVALID, "verace_sssd_scan_noalloc: psi_out is NULL");
-  VERACE_REQUIRE(s == 0 || (q && k && v && delta && out), VERACE_ERR_INVALID,
-                 "verace_sssd_scan_noalloc: NULL input/output pointer");
+  // the size limit first: a size that does not fit is refused before any pointer is looked at
   const size_t need = s > 0 ? simt_workspace(b, s, h) : 0;
   VERACE_REQUIRE(need <= SSSD_NOALLOC_SCRATCH_BYTES, VERACE_ERR_UNSUPPORTED,
                  "verace_sssd_scan_noalloc: this size needs %zu bytes of scratch, more than the "
                  "fixed %zu-byte device array; use verace_sssd_scan with a workspace",
                  need, SSSD_NOALLOC_SCRATCH_BYTES);
+  VERACE_REQUIRE(psi_out != nullptr, VERACE_ERR_INVALID, "verace_sssd_scan_noalloc: psi_out is NULL");
+  VERACE_REQUIRE(s == 0 || (q && k && v && delta && out), VERACE_ERR_INVALID,
+                 "verace_sssd_scan_noalloc: NULL input/output pointer");
   void* scratch = nullptr;
-  const int rc = noalloc_scratch(&scratch);
+  const int rc = noalloc_scratch(&scratch, (cudaStream_t)stream);
   if (rc != VERACE_OK) return rc;
   const size_t chains = (size_t)b * h;
   const size_t nch = ((size_t)s + SC - 1) / SC;
