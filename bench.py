@@ -275,17 +275,26 @@ def run_ours(args):
     hbm, bf16_burst, bf16_sus, peak_kind = _peaks()
     D, b, s = c["holo"], c["batch"], c["seq"]
     nch = (s + 63) // 64
-    # Algorithmic bytes of one verace_cham_scan call (chunked scan, 64-token chunks): the
-    # D x D complex fp32 state read (except the identity start) and written once per chunk,
-    # q/k/v in and the readout out (bf16), and the per-chunk T coefficients (128 KB per
-    # item and chunk) written by the prep and read by the column pass.
-    cham_bytes = (2 * nch - 1) * b * 2 * D * D * 4 + 4 * b * s * D * 2 + 2 * nch * b * 131072
-    achieved = cham_bytes / (cham_ms * 1e-3) / 1e9
-    cham_flop = 18.0 * D * D * b * s              # 9 D² MAC per token (8 state update + 1 readout)
-    # DRAM bytes per (item, chunk) measured by ncu at b=16, s=256 (batched schedule, 64
-    # item-chunks per launch: profiles/cham_tc_colpass2_b16_s256.md 887.6 MB per column-pass
-    # launch; cham_tc_readout_batch_b16_s256.md 304.1 MB per readout launch;
-    # cham_tc_prep_ws_b16_s256.md 16.8 MB per prep launch), scaled to this call
+    # Roofline of one verace_cham_scan call on the algorithmic basis of the path's work
+    # unit: FLOP = the necessary 18 D^2 per token (9 D^2 MAC: the rank-2 state update 8 D^2
+    # and the readout D^2; the reference formulation's 228 D^2 includes a per-position
+    # Newton-Schulz polynomial that is the identity for the fresh hologram and is not
+    # counted), bytes = the state read and written once per call (2 planes x D^2 x 4 B,
+    # each way) plus q, k, v in and the readout out in bf16 and gamma in fp32 per token.
+    # T_roof = max(bytes / HBM peak, FLOP / sustained bf16 peak); the call is tensor-bound.
+    cham_flop = 18.0 * D * D * b * s
+    cham_bytes_algo = b * 2 * (2 * D * D * 4) + b * s * (4 * D * 2 + 4)
+    t_meas = cham_ms * 1e-3
+    t_roof = max(cham_bytes_algo / (hbm * 1e9), cham_flop / (bf16_sus * 1e12))
+    tflops = cham_flop / t_meas / 1e12
+    # This design's own traffic: the chunked scan reads and writes the D x D complex state
+    # once per 64-token chunk (the identity start is not read), and moves q/k/v/readout and
+    # the per-chunk T coefficients (128 KB per item and chunk, written by the prep, read by
+    # the column pass).  DRAM bytes per (item, chunk) measured by ncu at b=16, s=256
+    # (profiles/cham_tc_colpass2_b16_s256.md 887.6 MB per column-pass launch;
+    # cham_tc_readout_batch_b16_s256.md 304.1 MB per readout launch; cham_tc_prep_ws_b16_s256.md
+    # 16.8 MB per prep launch, 64 item-chunks each), scaled to this call.
+    chunk_bytes = (2 * nch - 1) * b * 2 * D * D * 4 + 4 * b * s * D * 2 + 2 * nch * b * 131072
     traffic = (887.6e6 + 304.1e6 + 16.8e6) / 64 * b * nch
     result = {
         "metric": METRIC, "value": whole_job_rate(world, tokens_per_step, ms), "unit": UNIT,
@@ -300,12 +309,22 @@ def run_ours(args):
                    "l2": "no flush: per-step working set (weights 190 MB + activations) > 126 MB L2"},
         "roofline": {"kernel": "verace_cham_scan (cham_tc_prep_ws, then per group of 12 chunks one cham_tc_colpass2 "
                                "and one cham_tc_readout_batch)",
-                     "bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
-                     "frac": achieved / hbm, "traffic": traffic,
-                     "bytes_per_launch": cham_bytes, "ms_per_launch": cham_ms,
-                     "peak_source": f"{peak_kind} HBM copy bandwidth (MEASURED_PEAKS.json)",
-                     "tensor_tflops": cham_flop / (cham_ms * 1e-3) / 1e12,
-                     "tensor_frac": cham_flop / (cham_ms * 1e-3) / 1e12 / bf16_sus},
+                     "bound": "tensor", "achieved": tflops, "peak": bf16_sus, "unit": "TFLOP/s",
+                     "frac": t_roof / t_meas, "traffic": traffic,
+                     "basis": "18 D^2 FLOP per token-layer (necessary: rank-2 update + readout); bytes = state "
+                              "read+written once per call + (4 D + 1) elements per token; "
+                              "frac = max(bytes/HBM, FLOP/bf16 sustained) / measured",
+                     "flop_per_launch": cham_flop, "bytes_per_launch": cham_bytes_algo,
+                     "t_roof_ms": t_roof * 1e3, "ms_per_launch": cham_ms,
+                     "peak_source": f"{peak_kind} cuBLAS bf16 GEMM, sustained (MEASURED_PEAKS.json); "
+                                    f"HBM {hbm} GB/s {peak_kind} copy",
+                     "frac_of_bf16_burst": tflops / bf16_burst,
+                     "reference_formulation_flop": 228.0 * D * D * b * s,
+                     "chunked_design": {"bytes_per_launch": chunk_bytes, "unit": "GB/s",
+                                        "achieved": chunk_bytes / t_meas / 1e9, "peak": hbm,
+                                        "frac": chunk_bytes / t_meas / 1e9 / hbm,
+                                        "note": "this design's own bytes: the state read and written once per "
+                                                "64-token chunk"}},
         "e2e": {"value": whole_job_rate(world, tokens_per_step, e2e_ms), "unit": UNIT,
                 "h2d_bytes_per_step": x.numel() * x.element_size(),
                 "d2h_bytes_per_step": x.numel() * x.element_size()},

@@ -18,6 +18,8 @@ with, and the one its tests treat as ground truth), not its Triton kernels:
     prefix product P_t = U_t ... U_1               :222     (``parallel_complex_prefix_scan`` :246-293)
     H_t = P_t H_0 (H_0 on the right)               :229-230
     per-position Newton-Schulz x3                  :236     (``parallel_newton_schulz_retraction`` :296-315)
+    (``cham_scan_rank2``: the same scan in O(D^2) per token by the reference Triton
+    kernel's Woodbury form, triton_kernels.py:152-306, for long sequences at D = 1024)
     rec_t = Re(NS(H_t)) q_t, y = RMSNorm(w_out rec):239-241
     exported state = raw H_s (never retracted)     :243
 * ``newton_schulz_unitary_retraction``             cham_memory.py:21-51
@@ -46,7 +48,7 @@ import numpy as np
 __all__ = [
     "l2_normalize", "sigmoid", "silu", "rms_norm",
     "sssd_cayley_factors", "sssd_scan", "sssd_forward",
-    "cham_cayley_factors", "cham_scan", "cham_forward",
+    "cham_cayley_factors", "cham_scan", "cham_forward", "cham_scan_rank2", "cham_scan_rank2_c", "ns_polynomial",
     "newton_schulz_unitary_retraction", "sssd_projections", "cham_projections",
     "situ_glu", "mcmoe_route", "mcmoe_projection", "mcmoe_forward",
 ]
@@ -135,14 +137,16 @@ def sssd_scan(q, k, v, delta, initial_state=None, dtype=np.float64):
 
 
 def sssd_forward(p, x, num_heads, head_dim, initial_state=None, return_state=False,
-                 active_mask=None, dtype=np.float64):
-    """``SSSDAttention.forward`` (sssd_attention.py:103-182), eager path."""
+                 active_mask=None, dtype=np.float64, norm_eps=None):
+    """``SSSDAttention.forward`` (sssd_attention.py:103-182), eager path.  ``norm_eps``: the
+    head RMSNorm's eps (None: the machine epsilon of ``dtype``, as torch.nn.RMSNorm(eps=None)
+    does for its input's dtype; a model run in bf16 uses bf16's)."""
     x = np.asarray(x, dtype=dtype)
     p = {n: np.asarray(w, dtype=dtype) for n, w in p.items()}
     b, s, _ = x.shape
     q, k, v, delta = sssd_projections(p, x, num_heads, head_dim, active_mask)
     o, psi = sssd_scan(q, k, v, delta, initial_state, dtype=dtype)
-    o_norm = rms_norm(o, p["head_rmsnorm.weight"]).reshape(b, s, num_heads * head_dim)
+    o_norm = rms_norm(o, p["head_rmsnorm.weight"], norm_eps).reshape(b, s, num_heads * head_dim)
     out = _linear(o_norm, p["w_out.weight"])
     return out, (psi if return_state else None)
 
@@ -217,13 +221,127 @@ def cham_scan(q, k, v, gamma, initial_hologram=None, dtype=np.float64, ns_steps=
     return rec, (Hraw.real.astype(dtype), Hraw.imag.astype(dtype))
 
 
-def cham_forward(p, x, initial_hologram=None, active_mask=None, dtype=np.float64):
+def ns_polynomial(H0, steps=3):
+    """p(A) with A = H0ᴴ H0 such that NS^steps(H) = H p(A) for every H with Hᴴ H = A.
+
+    One Newton-Schulz step (cham_memory.py:21-51) maps H to H g(A), g(X) = (3I - X)/2, and
+    then (H g(A))ᴴ (H g(A)) = A g(A)^2 (g(A) commutes with A), so three steps give
+    H g(A0) g(A1) g(A2) with A_{j+1} = A_j g(A_j)^2."""
+    D = H0.shape[-1]
+    eye = np.eye(D, dtype=H0.dtype)
+    A = np.conj(np.swapaxes(H0, -1, -2)) @ H0
+    poly = np.broadcast_to(eye, A.shape).copy()
+    for _ in range(steps):
+        g = 0.5 * (3.0 * eye - A)
+        poly = poly @ g
+        A = A @ g @ g
+    return poly
+
+
+def cham_scan_rank2(q, k, v, gamma, initial_hologram=None, dtype=np.float64, ns_steps=3, dense_ns_at=()):
+    """The CHAM scan of ``cham_scan`` in O(D^2) per token, for long sequences at D = 1024.
+
+    State update: the reference's own Woodbury form of the exact Cayley factor
+    (triton_kernels.py:152-306, the per-token comment there): U_t = (I - iG/2)^-1 (I + iG/2)
+    with G = γ W J Wᵀ, W = [k v], J = [[0, 1], [1, 0]], so with B = (iγ/2) J and
+    K = (I2 - B WᵀW)^-1 B (Sherman-Morrison-Woodbury, no 1/γ):
+        Y = H + W (B (Wᵀ H)),   U_t H = Y + W (K (Wᵀ Y)).
+    H_t = U_t H_{t-1} from H_0 (the same product as P_t H_0 of cham_memory.py:222-230, in
+    sequential order).  A non-finite factor leaves the state unchanged (the identity
+    substitution of cham_memory.py:76-96).
+
+    Readout: rec_t = Re(NS^3(H_t) q_t) (cham_memory.py:236-239) evaluated as
+    Re(H_t p(A) q_t) with p = ``ns_polynomial`` of A = H_0ᴴ H_0: every U_t is unitary, so
+    H_tᴴ H_t = A for all t and NS^3(H_t) = H_t p(A) exactly in exact arithmetic.  For the
+    positions in ``dense_ns_at`` the readout is also formed by the dense retraction of H_t
+    (``newton_schulz_unitary_retraction``) and returned in a dict, so a caller can check
+    the identity on its own inputs.
+
+    Returns (rec [b,s,D], (Hr, Hi) [b,D,D], {t: dense rec_t [b,D]})."""
+    q, k, v, gamma = (np.asarray(a, dtype=dtype) for a in (q, k, v, gamma))
+    b, s, D = q.shape
+    cd = _cdtype(dtype)
+    if initial_hologram is None:
+        H = np.broadcast_to(np.eye(D, dtype=cd), (b, D, D)).copy()
+    else:
+        H = (np.asarray(initial_hologram[0], dtype=dtype)
+             + 1j * np.asarray(initial_hologram[1], dtype=dtype)).astype(cd)
+    poly = ns_polynomial(H, ns_steps)
+    J = np.array([[0.0, 1.0], [1.0, 0.0]], dtype=cd)
+    I2 = np.eye(2, dtype=cd)
+    rec = np.zeros((b, s, D), dtype=dtype)
+    dense = {}
+    want = set(int(t) for t in dense_ns_at)
+    for t in range(s):
+        for i in range(b):
+            W = np.stack([k[i, t], v[i, t]], axis=1).astype(cd)          # [D, 2]
+            B = 0.5j * gamma[i, t] * J
+            with np.errstate(all="ignore"):
+                K = np.linalg.solve(I2 - B @ (W.T @ W), B)
+                Y = H[i] + W @ (B @ (W.T @ H[i]))
+                Hn = Y + W @ (K @ (W.T @ Y))
+            if np.isfinite(Hn).all():
+                H[i] = Hn
+        rec[:, t] = np.real(H @ (poly @ q[:, t, :, None].astype(cd)))[..., 0]
+        if t in want:
+            Hr, _ = newton_schulz_unitary_retraction(H.real, H.imag, ns_steps)
+            dense[t] = (Hr @ q[:, t, :, None])[..., 0]
+    return rec, (H.real.astype(dtype), H.imag.astype(dtype)), dense
+
+
+_CLIB = None
+
+
+def _clib():
+    """oracle/_liboracle.so (``cham_rank2.c``), built on first use."""
+    global _CLIB
+    if _CLIB is None:
+        import ctypes
+        import importlib.util
+        import os
+        here = os.path.dirname(os.path.abspath(__file__))
+        spec = importlib.util.spec_from_file_location("oracle_build", os.path.join(here, "build.py"))
+        mod = importlib.util.module_from_spec(spec)
+        spec.loader.exec_module(mod)
+        L = ctypes.CDLL(mod.build())
+        dp = ctypes.c_void_p
+        L.cham_rank2_scan.restype = None
+        L.cham_rank2_scan.argtypes = [ctypes.c_int] * 3 + [dp] * 9
+        _CLIB = L
+    return _CLIB
+
+
+def cham_scan_rank2_c(q, k, v, gamma, initial_hologram=None, ns_steps=3):
+    """``cham_scan_rank2`` (fp64) computed by ``cham_rank2.c``: same arguments and results,
+    without the dense check.  Returns (rec [b,s,D], (Hr, Hi) [b,D,D])."""
+    q, k, v, gamma = (np.ascontiguousarray(a, dtype=np.float64) for a in (q, k, v, gamma))
+    b, s, D = q.shape
+    if initial_hologram is None:
+        Hr = np.ascontiguousarray(np.broadcast_to(np.eye(D), (b, D, D)))
+        Hi = np.zeros((b, D, D))
+        pr = pi = None
+    else:
+        Hr = np.array(initial_hologram[0], dtype=np.float64, order="C")
+        Hi = np.array(initial_hologram[1], dtype=np.float64, order="C")
+        poly = ns_polynomial(Hr + 1j * Hi, ns_steps)
+        pr, pi = np.ascontiguousarray(poly.real), np.ascontiguousarray(poly.imag)
+    rec = np.zeros((b, s, D))
+    ptr = lambda a: None if a is None else a.ctypes.data
+    _clib().cham_rank2_scan(b, s, D, ptr(q), ptr(k), ptr(v), ptr(gamma), ptr(Hr), ptr(Hi), ptr(pr), ptr(pi),
+                            ptr(rec))
+    return rec, (Hr, Hi)
+
+
+def cham_forward(p, x, initial_hologram=None, active_mask=None, dtype=np.float64, norm_eps=None, rank2=False):
     """``ContinuousHolographicMemory.forward`` (cham_memory.py:117-243), eager path."""
     x = np.asarray(x, dtype=dtype)
     p = {n: np.asarray(w, dtype=dtype) for n, w in p.items()}
     q, k, v, gamma = cham_projections(p, x, active_mask)
-    rec, H = cham_scan(q, k, v, gamma, initial_hologram, dtype=dtype)
-    y = rms_norm(_linear(rec, p["w_out.weight"]), p["norm.weight"])
+    if rank2:   # the same scan in O(D^2) per token (fp64, cham_rank2.c)
+        rec, H = cham_scan_rank2_c(q, k, v, gamma, initial_hologram)
+    else:
+        rec, H = cham_scan(q, k, v, gamma, initial_hologram, dtype=dtype)
+    y = rms_norm(_linear(rec, p["w_out.weight"]), p["norm.weight"], norm_eps)
     return y, H
 
 

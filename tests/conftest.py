@@ -69,3 +69,34 @@ def mcmoe_weights(g):
         mine = np.concatenate([[f.sum(), (f * f).sum()], f[:16]])
         np.testing.assert_allclose(mine, fps[k], rtol=1e-6, atol=1e-6, err_msg=f"weights of {k} differ")
     return sd
+
+
+def config1_case():
+    """BASELINE config 1 (one SSSD + CHAM layer, fp32, hidden 1024, 8 heads x 128, D = 1024,
+    x = randn(2, 512, 1024) under seed 0, weights default-initialised under seed 0, SSSD
+    first): (sssd module, cham module, x, golden dict) on the CPU.  The modules and x are
+    re-created from the seeds, as tests/golden/make_golden.py built the reference's, and
+    checked against the fingerprints the reference left in config1_golden.npz."""
+    import torch
+    import verace_v1_b200 as V
+    z = np.load(os.path.join(GOLDEN, "config1_golden.npz"))
+    g = {k: z[k] for k in z.files}
+    torch.manual_seed(0)
+    sssd = V.SSSDAttention(1024, 8, 128, 256)
+    cham = V.ContinuousHolographicMemory(1024, 1024)
+    torch.manual_seed(0)
+    x = torch.randn(2, 512, 1024)
+
+    def fp(t):
+        f = t.detach().double().reshape(-1)
+        return torch.cat([torch.stack([f.sum(), (f * f).sum()]), f[:16]]).numpy()
+
+    np.testing.assert_allclose(fp(x), g["x/fp"], rtol=1e-9, atol=1e-9, err_msg="config-1 input differs")
+    for prefix, m in (("sssd", sssd), ("cham", cham)):
+        sd = m.state_dict()
+        names = sorted(k[len(prefix) + 4:] for k in g if k.startswith(prefix + "/fp/"))
+        assert names == sorted(sd), f"{prefix} parameter names differ from the reference's"
+        for k, v in sd.items():
+            np.testing.assert_allclose(fp(v), g[f"{prefix}/fp/{k}"], rtol=1e-9, atol=1e-9,
+                                       err_msg=f"{prefix} weights of {k} differ")
+    return sssd, cham, x, g

@@ -45,7 +45,7 @@ def _put(store, prefix, **arrays):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", default=os.environ.get("VERACE_REFERENCE", ""))
-    ap.add_argument("--only", action="append", choices=["sssd", "cham", "ns", "mcmoe", "layer"],
+    ap.add_argument("--only", action="append", choices=["sssd", "cham", "ns", "mcmoe", "layer", "config1"],
                     help="regenerate only these files (default: all)")
     args = ap.parse_args()
 
@@ -60,7 +60,8 @@ def main():
                                                 newton_schulz_unitary_retraction)
     # one thread: torch 2.11's MKL complex batched solve was seen to spin forever with an
     # explicit multi-thread setting on this host (CLASWP parameter errors).
-    torch.set_num_threads(1)
+    if args.only != ["config1"]:
+        torch.set_num_threads(1)
 
     if want("sssd"):
         # ------------------------------------------------------------------ SSSD
@@ -284,8 +285,64 @@ def main():
             f = v.astype(np.float64).ravel()
             ly[f"layers/fp/{k}"] = np.concatenate([[f.sum(), (f * f).sum()], f[:16]])
         np.savez_compressed(os.path.join(HERE, "layer_golden.npz"), **ly)
-    for f in ("sssd_golden.npz", "cham_golden.npz", "ns_golden.npz", "mcmoe_golden.npz", "layer_golden.npz"):
-        print(f, os.path.getsize(os.path.join(HERE, f)), "bytes")
+    if want("config1"):
+        # ------------------------------------------------------------------ config 1, full size
+        # One SSSD + CHAM layer in fp32 at the BASELINE configuration: hidden 1024, 8 heads x
+        # 128, D = 1024, x = randn(2, 512, 1024) under seed 0, weights default-initialised
+        # under seed 0 (SSSDAttention first, then ContinuousHolographicMemory, both fed x).
+        # The reference's eager CHAM needs ~16 GB per 64 tokens at D = 1024, so it runs in
+        # 64-token chunks through initial_hologram (the state composes exactly on the right,
+        # cham_memory.py:222-230).  Outputs and states are stored as sketches (products with
+        # fixed random matrices stored here) plus full rows at a few positions; weights and
+        # x as fingerprints (the tests rebuild them from the same seeds).
+        import time
+        c1 = {}   # run alone (--only config1): torch's default thread count
+        torch.manual_seed(0)
+        sssd_m = SSSDAttention(1024, 8, 128, 256)
+        cham_m = ContinuousHolographicMemory(1024, 1024)
+        torch.manual_seed(0)
+        x = torch.randn(2, 512, 1024)
+        g = torch.Generator().manual_seed(21)
+        r_out = torch.randn(1024, 8, generator=g)
+        r_d = torch.randn(128, 4, generator=g)
+        r_D = torch.randn(1024, 4, generator=g)
+        rows = torch.tensor([0, 1, 63, 64, 127, 200, 255, 256, 383, 511])
+        c1["sketch/r_out"] = r_out.numpy()
+        c1["sketch/r_d"] = r_d.numpy()
+        c1["sketch/r_D"] = r_D.numpy()
+        c1["sketch/rows"] = rows.numpy()
+
+        def fp(t):
+            f = t.detach().double().reshape(-1)
+            return torch.cat([torch.stack([f.sum(), (f * f).sum()]), f[:16]]).numpy()
+
+        c1["x/fp"] = fp(x)
+        for k, v in sssd_m.state_dict().items():
+            c1[f"sssd/fp/{k}"] = fp(v)
+        for k, v in cham_m.state_dict().items():
+            c1[f"cham/fp/{k}"] = fp(v)
+        with torch.no_grad():
+            t0 = time.time()
+            out, psi = sssd_m(x, return_state=True)
+            print("config1 sssd", time.time() - t0, "s", flush=True)
+            _put(c1, "sssd", out_sk=out @ r_out, out_rows=out[:, rows], psi_sk=psi @ r_d,
+                 psi_diag=torch.diagonal(psi, dim1=-2, dim2=-1))
+            H = None
+            ys = []
+            for c0 in range(0, 512, 64):
+                t0 = time.time()
+                y, H = cham_m(x[:, c0:c0 + 64], initial_hologram=H)
+                ys.append(y)
+                print("config1 cham chunk", c0, time.time() - t0, "s", flush=True)
+            y = torch.cat(ys, dim=1)
+            Hr, Hi = H
+            _put(c1, "cham", out_sk=y @ r_out, out_rows=y[:, rows], hr_sk=Hr @ r_D, hi_sk=Hi @ r_D,
+                 hr_diag=torch.diagonal(Hr, dim1=-2, dim2=-1), hi_diag=torch.diagonal(Hi, dim1=-2, dim2=-1))
+        np.savez_compressed(os.path.join(HERE, "config1_golden.npz"), **c1)
+    for f in ("sssd_golden.npz", "cham_golden.npz", "ns_golden.npz", "mcmoe_golden.npz", "layer_golden.npz",
+              "config1_golden.npz"):
+        if os.path.exists(os.path.join(HERE, f)):
+            print(f, os.path.getsize(os.path.join(HERE, f)), "bytes")
 
 
 if __name__ == "__main__":
