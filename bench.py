@@ -338,6 +338,9 @@ def run_ours(args):
     if not args.no_mcmoe:
         torch.cuda.empty_cache()
         result["mcmoe"] = run_mcmoe(args, V, dev, barrier, max_over_ranks)
+    if world == 1 and not args.no_decode and not args.no_triton_bar:
+        torch.cuda.empty_cache()
+        result["decode"]["reference_triton"] = run_triton_bar(dev)
     if world == 1 and not args.no_cpu_baseline:
         result["cpu_baseline"] = cpu_sample(tokens=args.cpu_tokens)
     if rank == 0:
@@ -527,14 +530,51 @@ def run_decode(args, layers, embed, V, dev, rank, barrier, max_over_ranks):
 
 
 # ------------------------------------------------------------------------------ CPU arm
+REF_DIR = os.path.join(ROOT, "baseline", "_ref")
+
+
+def _reference_modules():
+    """The reference package from its offline install under baseline/_ref (its own
+    modules, unmodified), or None when it is not installed."""
+    if not os.path.isdir(os.path.join(REF_DIR, "verace_v1")):
+        return None
+    if REF_DIR not in sys.path:
+        sys.path.append(REF_DIR)
+    from verace_v1.modules.sssd_attention import SSSDAttention
+    from verace_v1.modules.cham_memory import ContinuousHolographicMemory
+    return SSSDAttention, ContinuousHolographicMemory
+
+
 def cpu_sample(tokens=16):
-    """Time the reference's eager algorithm (numpy restatement, fp32 as the reference's
-    eager path) for one item x `tokens` tokens through one layer's SSSD and CHAM."""
+    """Time the reference's CPU path for one item x `tokens` tokens through one layer's
+    SSSD and CHAM (config-1 modules: hidden 1024, 8 heads x 128, D = 1024, fp32, seed 0).
+
+    With the reference installed (baseline/_ref) this runs the reference's own eager
+    modules (SSSDAttention.forward sssd_attention.py:103-182, ContinuousHolographicMemory
+    .forward cham_memory.py:117-243) on CPU tensors with torch's default thread count
+    ("kind": "reference"); otherwise the numpy restatement of the same algorithm in
+    oracle/ ("kind": "port")."""
     import numpy as np
-    import oracle
     c = CFG
-    rng = np.random.default_rng(0)
     hid, h, d, D = c["hidden"], c["heads"], c["head_dim"], c["holo"]
+    ref = _reference_modules()
+    if ref is not None:
+        import torch
+        SSSD, CHAM = ref
+        torch.manual_seed(0)
+        sssd, cham = SSSD(hid, h, d, 256).eval(), CHAM(hid, D).eval()
+        x = torch.randn(1, tokens, hid, generator=torch.Generator().manual_seed(0))
+        with torch.no_grad():
+            t0 = time.perf_counter()
+            sssd(x, return_state=True)
+            cham(x)
+            dt = time.perf_counter() - t0
+        return {"value": tokens / dt, "unit": UNIT, "cores": torch.get_num_threads(), "kind": "reference",
+                "sample": f"1 sequence x {tokens} tokens x 1 layer: the reference's eager SSSDAttention + "
+                          f"ContinuousHolographicMemory (config-1 modules, D=1024, fp32, CPU, "
+                          f"{torch.get_num_threads()} torch threads), {dt:.1f} s"}
+    import oracle
+    rng = np.random.default_rng(0)
     bound = 1.0 / np.sqrt(hid)
     u = lambda *shape: rng.uniform(-bound, bound, size=shape).astype(np.float32)
     ps = {"w_q.weight": u(h * d, hid), "w_k.weight": u(h * d, hid), "w_v.weight": u(h * d, hid),
@@ -553,6 +593,58 @@ def cpu_sample(tokens=16):
                       f"eager restatement), {dt:.1f} s"}
 
 
+def run_triton_bar(dev, steps=2):
+    """The reference's own GPU decode path, timed on this GPU: its Triton launchers
+    (launch_sssd_triton_scan, triton_kernels.py:603-636; launch_cham_triton_update, which at
+    D = 1024 takes the host-looped tiled path launch_cham_triton_tiled, :552-597), unmodified
+    from the offline install under baseline/_ref, for ONE layer of a config-3 decode step:
+    b = 64 items, one token each, carried states (8 heads x 128, D = 1024), bf16 inputs.
+    One warm-up step (Triton JIT), then `steps` timed steps with CUDA events; the full
+    12-layer step is 12 x this (the projections and glue around the mixers not counted)."""
+    import torch
+    if not os.path.isdir(os.path.join(REF_DIR, "verace_v1")):
+        return {"unavailable": "the reference is not installed under baseline/_ref"}
+    if REF_DIR not in sys.path:
+        sys.path.append(REF_DIR)
+    try:
+        from verace_v1.serving import triton_kernels as TK
+    except Exception as e:        # noqa: BLE001 -- report why the bar could not be taken
+        return {"unavailable": f"reference Triton kernels not importable: {e!r}"[:300]}
+    b, h, d, D = DEC["batch"], CFG["heads"], CFG["head_dim"], CFG["holo"]
+    g = torch.Generator(device=dev).manual_seed(11)
+    nrm = torch.nn.functional.normalize
+    rn = lambda *sh: torch.randn(*sh, generator=g, device=dev)
+    sq, sk, sv = (nrm(rn(b, 1, h, d), dim=-1).to(torch.bfloat16) for _ in range(3))
+    dl = 0.1 * torch.sigmoid(rn(b, 1, h))
+    cq, ck, cv = (nrm(rn(b, 1, D), dim=-1).to(torch.bfloat16) for _ in range(3))
+    gm = 0.1 * torch.sigmoid(rn(b, 1))
+    psi = torch.eye(d, device=dev).expand(b, h, d, d).contiguous()
+    holo = (torch.eye(D, device=dev).expand(b, D, D).contiguous(), torch.zeros(b, D, D, device=dev))
+
+    def step(psi, holo):
+        _, psi = TK.launch_sssd_triton_scan(sq, sk, sv, dl, psi)
+        _, holo = TK.launch_cham_triton_update(cq, ck, cv, gm, holo)
+        return psi, holo
+
+    with torch.no_grad():
+        psi, holo = step(psi, holo)
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        t0 = time.perf_counter()
+        e0.record()
+        for _ in range(steps):
+            psi, holo = step(psi, holo)
+        e1.record()
+        torch.cuda.synchronize()
+        wall = time.perf_counter() - t0
+    us = e0.elapsed_time(e1) * 1e3 / steps
+    return {"workload": f"reference Triton decode, one layer: b={b}, 1 token per item, carried states, "
+                        f"{h}x{d} heads, D={D}, bf16 inputs (baseline/_ref, unmodified)",
+            "us_per_layer_step": us, "us_per_step_12_layers_extrapolated": 12 * us,
+            "us_per_token_12_layers_extrapolated": 12 * us / b, "steps_timed": steps,
+            "host_wall_s": wall}
+
+
 def run_reference(args):
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -565,16 +657,15 @@ def run_reference(args):
     wall = time.perf_counter() - t0
     value = args.ref_tokens * args.steps / wall
     ms = wall * 1e3 / args.steps
-    c = CFG
     print(json.dumps({
         "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "fp32", "data": "synthetic",
-        "config": {"workload": "config 2 (bounded CPU sample: 1 sequence x "
-                               f"{args.ref_tokens} tokens x 1 layer per step)",
+        "config": {"workload": "config 2's per-layer mixers (hidden 1024, 8x128 heads, D=1024) on a bounded CPU "
+                               f"sample: 1 sequence x {args.ref_tokens} tokens x 1 layer per step",
                    "global_batch": 1, "seq_len": args.ref_tokens, "layers": 1,
                    "parallelism": "host cores"},
-        "cpu_baseline": {"value": value, "unit": UNIT, "cores": vals[-1]["cores"], "kind": "port",
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": vals[-1]["cores"], "kind": vals[-1]["kind"],
                          "sample": vals[-1]["sample"]},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }), flush=True)
@@ -643,6 +734,8 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-decode", action="store_true", help="skip the config-3 decode measurement")
     ap.add_argument("--no-mcmoe", action="store_true", help="skip the M-CMoE sub-layer measurement")
+    ap.add_argument("--no-triton-bar", action="store_true",
+                    help="skip timing the reference's Triton decode path (one layer, config 3)")
     ap.add_argument("--only", choices=["cham", "sssd", "decode", "mcmoe"], default=None,
                     help="time one scan entry point alone (kernel-level case for profiling)")
     ap.add_argument("--batch", type=int, default=None)
