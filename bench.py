@@ -109,6 +109,26 @@ def whole_job_rate(world, units_per_rank_step, ms_per_step):
     return world * units_per_rank_step / (ms_per_step * 1e-3)
 
 
+def gather_outputs(world, t):
+    """Every rank's output shard, concatenated along dim 0 on every rank (one NCCL
+    all_gather over NVLink; the only data-path collective: the items are independent)."""
+    if world == 1:
+        return t
+    import torch
+    import torch.distributed as dist
+    out = torch.empty((world * t.shape[0],) + tuple(t.shape[1:]), dtype=t.dtype, device=t.device)
+    dist.all_gather_into_tensor(out, t.contiguous())
+    return out
+
+
+def strong_shard(rank, world, global_batch):
+    """The contiguous range [lo, hi) of a fixed global batch's items that a rank runs
+    (strong scaling: the total work is fixed, each rank takes a share)."""
+    per = (global_batch + world - 1) // world
+    lo = min(rank * per, global_batch)
+    return lo, min(lo + per, global_batch)
+
+
 # ------------------------------------------------------------------------------ clocks
 class ClockSampler:
     FIELDS = ["index", "clocks.sm", "clocks.max.sm", "power.draw", "clocks_event_reasons.active",
@@ -206,6 +226,7 @@ def run_ours(args):
                 cham_events.append((e0, e1))
             nxt = layers[li + 1]["sssd_norm"] if li + 1 < len(layers) else None
             n = V.add_rmsnorm(h, cm.w_out(rec), y_norm=cm.norm, out_norm=nxt)
+        gather_outputs(world, h)     # every rank receives all ranks' outputs (NCCL all_gather)
         return h
 
     barrier, max_over_ranks = make_rank_sync(world, dev)
@@ -305,7 +326,7 @@ def run_ours(args):
         "config": {"workload": "config 2: 12-layer SSSD+CHAM prefill, b=8 x s=2048 per GPU, "
                                "hidden 1024, 8x128 heads, D=1024",
                    "global_batch": b * world, "seq_len": s, "layers": c["layers"],
-                   "parallelism": f"dp{world} (batch shards, no collective)",
+                   "parallelism": f"dp{world} (batch shards; outputs all-gathered over NCCL each step)",
                    "l2": "no flush: per-step working set (weights 190 MB + activations) > 126 MB L2"},
         "roofline": {"kernel": "verace_cham_scan (cham_tc_prep_ws, then per group of 12 chunks one cham_tc_colpass2 "
                                "and one cham_tc_readout_batch)",
@@ -338,6 +359,9 @@ def run_ours(args):
     if not args.no_mcmoe:
         torch.cuda.empty_cache()
         result["mcmoe"] = run_mcmoe(args, V, dev, barrier, max_over_ranks)
+    if not args.no_strong:
+        torch.cuda.empty_cache()
+        result["strong"] = run_strong(args, V, dev, rank, world, barrier, max_over_ranks)
     if world == 1 and not args.no_decode and not args.no_triton_bar:
         torch.cuda.empty_cache()
         result["decode"]["reference_triton"] = run_triton_bar(dev)
@@ -347,6 +371,60 @@ def run_ours(args):
         print(json.dumps(result), flush=True)
     if world > 1:
         dist.destroy_process_group()
+
+
+C5 = dict(batch=256, seq=4096, hidden=4096, heads=32, head_dim=128, holo=1024, vocab=32000, micro=8)
+
+
+def run_strong(args, V, dev, rank, world, barrier, max_over_ranks):
+    """Config 5, one decoder layer, strong scaling: a fixed global batch of 256 sequences x
+    4096 uniform-random token ids (seed 0) through one VeraceV1Layer (SSSD 32 heads x 128,
+    CHAM D = 1024, M-CMoE rank 32 / 64 components / top-8; hidden 4096; random init, seed 0;
+    bf16 activations, fp32 recurrent states), the items split across the ranks (256/N each),
+    run in micro-batches of 8 items.  Each step ends with the NCCL all_gather of every
+    item's last-position hidden state (the outputs a generation step reads).  Time: the
+    max over ranks of the CUDA-event time per step.  The 32-layer model is 32 x this work
+    per forward (ACDE halting at random init keeps every token for all layers)."""
+    import torch
+    c = C5
+    cfg = V.VeraceV1Config(vocab_size=c["vocab"], hidden_dim=c["hidden"], num_layers=1, num_heads=c["heads"],
+                           head_dim=c["head_dim"], chams_holographic_dim=c["holo"])
+    torch.manual_seed(0)
+    layer = V.VeraceV1Layer(1, cfg).to(dev, torch.bfloat16).eval()   # layer_idx 1: no snapshot commit
+    embed = torch.nn.Embedding(c["vocab"], c["hidden"]).to(dev, torch.bfloat16)
+    ids = torch.randint(0, c["vocab"], (c["batch"], c["seq"]), generator=torch.Generator().manual_seed(0))
+    lo, hi = strong_shard(rank, world, c["batch"])
+    ids = ids[lo:hi].to(dev)
+    last = torch.empty(hi - lo, c["hidden"], device=dev, dtype=torch.bfloat16)
+
+    def step():
+        for m0 in range(0, hi - lo, c["micro"]):
+            x = embed(ids[m0:m0 + c["micro"]])
+            h, _, _, _ = layer(x)
+            last[m0:m0 + c["micro"]].copy_(h[:, -1])
+        return gather_outputs(world, last)
+
+    with torch.no_grad():
+        for _ in range(max(1, min(args.warmup, 2))):
+            step()
+        barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        reps = 2
+        e0.record()
+        for _ in range(reps):
+            out = step()
+        e1.record()
+        barrier()
+        ms = max_over_ranks(e0.elapsed_time(e1) / reps)
+    assert out.shape[0] == c["batch"]
+    del layer, embed
+    tokens = c["batch"] * c["seq"]
+    return {"workload": "config 5, one VeraceV1Layer (SSSD 32x128 + CHAM D=1024 + M-CMoE top-8/64), hidden 4096, "
+                        "global batch 256 x 4096 tokens split over the ranks (strong scaling), bf16, micro-batches "
+                        "of 8 items, last-position hidden states all-gathered each step",
+            "scaling": "strong", "n_gpus": world, "items_per_rank": hi - lo, "ms_per_step": ms,
+            "token_layers_per_s": tokens / (ms * 1e-3),
+            "model_tokens_per_s_32_layers": tokens / (32 * ms * 1e-3)}
 
 
 def run_mcmoe(args, V, dev, barrier, max_over_ranks):
@@ -734,6 +812,8 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-decode", action="store_true", help="skip the config-3 decode measurement")
     ap.add_argument("--no-mcmoe", action="store_true", help="skip the M-CMoE sub-layer measurement")
+    ap.add_argument("--no-strong", action="store_true",
+                    help="skip the config-5 one-layer strong-scaling measurement")
     ap.add_argument("--no-triton-bar", action="store_true",
                     help="skip timing the reference's Triton decode path (one layer, config 3)")
     ap.add_argument("--only", choices=["cham", "sssd", "decode", "mcmoe"], default=None,

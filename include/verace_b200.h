@@ -128,6 +128,32 @@ VERACE_API int verace_cham_scan(const void* q, const void* k, const void* v, con
                      void* workspace, size_t workspace_bytes, void* stream);
 
 /* ------------------------------------------------------------------------------
+ * Continuing a CHAM scan from a carried hologram H0 (initial_hologram of
+ * ContinuousHolographicMemory.forward, cham_memory.py:117-122 and :229-239; the
+ * launchers' initial_hologram argument, triton_kernels.py:639-685, :552-597).
+ * Every U_t is unitary, so NS3(H_t) = H_t p(A) with A = H0^H H0 for the Newton-Schulz
+ * polynomial p, and p(I + E) = I - E/2 + O(E^2).
+ * verace_cham_unitarity: eps [b] fp32 (device) = max over 4 fixed +-1 probe vectors r of
+ *   |(H^H H - I) r| / |r| per item, in fp64 (three launches; workspace
+ *   verace_cham_unitarity_workspace(b, D) bytes).  It estimates the RMS action of E; for a
+ *   worst-case (rank-one) E the readout error of the unitary scan is up to sqrt(D) eps / 2.
+ * verace_cham_scan_unitary: verace_cham_scan with the readout Re(H_t q_t), i.e. p(A) = I,
+ *   exact when H0 is unitary and within |E q_t| / 2 + O(|E|^2) of the Newton-Schulz
+ *   readout otherwise; runs on the tensor cores for D % 128 == 0 (bf16 / fp32), else on
+ *   the SIMT scan without the readout polynomial.  Workspace as verace_cham_scan with
+ *   has_h0 = 1.  A caller picks it over verace_cham_scan when eps shows H0 unitary to
+ *   within its tolerance (the Python launcher does: tensor-core speed for holograms grown
+ *   by these scans, the exact polynomial readout for any other).
+ * ---------------------------------------------------------------------------- */
+VERACE_API size_t verace_cham_unitarity_workspace(int b, int D);
+VERACE_API int verace_cham_unitarity(const float* h_re, const float* h_im, int b, int D, float* eps,
+                                     void* workspace, size_t workspace_bytes, void* stream);
+VERACE_API int verace_cham_scan_unitary(const void* q, const void* k, const void* v, const float* gamma,
+                                        const float* h0_re, const float* h0_im, void* out, float* h_re,
+                                        float* h_im, int b, int s, int D, int dtype, void* workspace,
+                                        size_t workspace_bytes, void* stream);
+
+/* ------------------------------------------------------------------------------
  * Dense Newton-Schulz unitary retraction, `steps` iterations of H <- H (3I - H^H H) / 2.
  * Replaces newton_schulz_unitary_retraction (verace_v1/modules/cham_memory.py:21-51).
  * h_re, h_im, out_re, out_im : [b, D, D] fp32 (out may not alias the input).

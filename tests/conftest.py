@@ -100,3 +100,44 @@ def config1_case():
             np.testing.assert_allclose(fp(v), g[f"{prefix}/fp/{k}"], rtol=1e-9, atol=1e-9,
                                        err_msg=f"{prefix} weights of {k} differ")
     return sssd, cham, x, g
+
+
+MODEL_OUT_OF_PATH = ("vision_encoder.", "energy_critic.")
+
+
+def model_reinit(model, seed=0):
+    """Deterministic re-initialisation of a VeraceV1Model's in-path parameters (the
+    reference's or the drop-in's: same names), so that a reference model and the drop-in
+    hold the same weights without storing them: parameters in sorted-name order from one
+    generator; RMSNorm weights 1 + 0.1 N(0,1), the M-CMoE bases 0.02 N(0,1), the ACDE
+    halting unit N(0, 0.2^2) with bias 3 (tokens halt at different layers), every other
+    matrix N(0,1)/sqrt(fan_in)."""
+    import torch
+    g = torch.Generator().manual_seed(seed)
+    params = dict(model.named_parameters())
+    with torch.no_grad():
+        for name in sorted(params):
+            if name.startswith(MODEL_OUT_OF_PATH):
+                continue
+            p = params[name]
+            if name.endswith("norm.weight"):
+                p.copy_(1.0 + 0.1 * torch.randn(p.shape, generator=g))
+            elif name.endswith(("u_basis", "v_basis")):
+                p.copy_(0.02 * torch.randn(p.shape, generator=g))
+            elif name == "acd_engine.w_halting.weight":
+                p.copy_(0.2 * torch.randn(p.shape, generator=g))
+            elif name == "acd_engine.w_halting.bias":
+                p.fill_(3.0)
+            else:
+                p.copy_(torch.randn(p.shape, generator=g) / p.shape[-1] ** 0.5)
+
+
+def model_fingerprints(model):
+    """{name: [sum, sum of squares, first 16 values]} of the in-path parameters."""
+    out = {}
+    for k, v in model.state_dict().items():
+        if k.startswith(MODEL_OUT_OF_PATH):
+            continue
+        f = v.detach().double().reshape(-1).cpu().numpy()
+        out[k] = np.concatenate([[f.sum(), (f * f).sum()], f[:16]])
+    return out

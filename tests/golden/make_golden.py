@@ -45,7 +45,7 @@ def _put(store, prefix, **arrays):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", default=os.environ.get("VERACE_REFERENCE", ""))
-    ap.add_argument("--only", action="append", choices=["sssd", "cham", "ns", "mcmoe", "layer", "config1"],
+    ap.add_argument("--only", action="append", choices=["sssd", "cham", "ns", "mcmoe", "layer", "config1", "model"],
                     help="regenerate only these files (default: all)")
     args = ap.parse_args()
 
@@ -60,7 +60,7 @@ def main():
                                                 newton_schulz_unitary_retraction)
     # one thread: torch 2.11's MKL complex batched solve was seen to spin forever with an
     # explicit multi-thread setting on this host (CLASWP parameter errors).
-    if args.only != ["config1"]:
+    if args.only not in (["config1"], ["model"]):
         torch.set_num_threads(1)
 
     if want("sssd"):
@@ -339,8 +339,53 @@ def main():
             _put(c1, "cham", out_sk=y @ r_out, out_rows=y[:, rows], hr_sk=Hr @ r_D, hi_sk=Hi @ r_D,
                  hr_diag=torch.diagonal(Hr, dim1=-2, dim2=-1), hi_diag=torch.diagonal(Hi, dim1=-2, dim2=-1))
         np.savez_compressed(os.path.join(HERE, "config1_golden.npz"), **c1)
+    if want("model"):
+        # ------------------------------------------------------------------ the model
+        # VeraceV1Model.forward (backbone.py:144-210) at a small configuration (head_dim 128,
+        # D = 128: the tensor-core widths): ACDE prefill of 2 x 12 tokens, then two
+        # single-token steps through layer_states (the decode convention of
+        # serving/hyper_generate.py:58-77).  The in-path weights are re-initialised by
+        # tests/conftest.py:model_reinit (the tests re-create them the same way) and pinned
+        # by fingerprints; the vision encoder is built small and never used.
+        sys.path.insert(0, os.path.dirname(HERE))
+        from conftest import model_fingerprints, model_reinit
+        from verace_v1.config import VeraceV1Config
+        from verace_v1.modules.backbone import VeraceV1Model
+
+        @__import__("dataclasses").dataclass
+        class TinyVision:
+            embed_dim: int = 32
+            num_layers: int = 1
+            num_heads: int = 2
+            patch_size: int = 14
+
+        cfg = VeraceV1Config(vocab_size=64, hidden_dim=128, num_layers=4, num_heads=1, head_dim=128,
+                             spectral_dim=64, chams_holographic_dim=128, mcmoe_rank=8, mcmoe_num_components=8,
+                             vision_config=TinyVision())
+        torch.manual_seed(0)
+        model = VeraceV1Model(cfg).eval()
+        model_reinit(model, seed=0)
+        md = {}
+        for k, v in model_fingerprints(model).items():
+            md[f"fp/{k}"] = v
+        ids = torch.randint(0, 64, (2, 12), generator=torch.Generator().manual_seed(1))
+        nxt = torch.randint(0, 64, (2, 2), generator=torch.Generator().manual_seed(2))
+        with torch.no_grad():
+            logits, depth, hidden, st = model(ids, return_hidden=True, return_layer_states=True)
+            md["prefill/ids"] = ids.numpy()
+            md["prefill/logits"] = logits.numpy()
+            md["prefill/depth"] = depth.numpy()
+            md["prefill/hidden"] = hidden.numpy()
+            for i in range(2):
+                lg, dp, st = model(nxt[:, i:i + 1], layer_states=st, return_layer_states=True)
+                md[f"step{i}/ids"] = nxt[:, i:i + 1].numpy()
+                md[f"step{i}/logits"] = lg.numpy()
+                md[f"step{i}/depth"] = dp.numpy()
+            lg, dp = model(ids, use_adaptive_depth=False)
+            md["static/logits"] = lg.numpy()
+        np.savez_compressed(os.path.join(HERE, "model_golden.npz"), **md)
     for f in ("sssd_golden.npz", "cham_golden.npz", "ns_golden.npz", "mcmoe_golden.npz", "layer_golden.npz",
-              "config1_golden.npz"):
+              "config1_golden.npz", "model_golden.npz"):
         if os.path.exists(os.path.join(HERE, f)):
             print(f, os.path.getsize(os.path.join(HERE, f)), "bytes")
 

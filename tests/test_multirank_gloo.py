@@ -1,9 +1,10 @@
 """The multi-GPU host logic of bench.py, on CPU: two gloo ranks (world_size 2) run the
 helpers the NCCL ranks run on B200s.  Each rank takes its own shard of the batch (weak
-scaling: the same amount of work, different items, no collective on the data path); the
-timed region is bracketed by the barrier and reduced to the slowest rank's time; the
-reported value is the units all ranks processed over that time.  The reference arm runs
-on rank 0 alone.
+scaling: the same amount of work, different items); the only data-path collective is the
+all_gather of the ranks' outputs; the timed region is bracketed by the barrier and reduced
+to the slowest rank's time; the reported value is the units all ranks processed over that
+time.  The strong-scaling leg splits one fixed global batch into contiguous ranges.  The
+reference arm runs on rank 0 alone.
 """
 import argparse
 import datetime
@@ -47,6 +48,16 @@ def _rank_worker(rank, world, port):
         assert slowest == 17.5
         rate = bench.whole_job_rate(world, batch * seq * layers, slowest)
         assert abs(rate - world * batch * seq * layers / 17.5e-3) <= 1e-9 * rate
+        # the data-path collective: every rank receives all ranks' outputs, in rank order
+        out = torch.full((batch, 3), float(rank))
+        got = bench.gather_outputs(world, out)
+        assert tuple(got.shape) == (world * batch, 3)
+        assert torch.equal(got, torch.cat([torch.full((batch, 3), float(r)) for r in range(world)]))
+        # strong scaling: a fixed global batch split into contiguous, disjoint, covering ranges
+        lo, hi = bench.strong_shard(rank, world, 256)
+        ranges = [torch.tensor([lo, hi]) for _ in range(world)]
+        dist.all_gather(ranges, torch.tensor([lo, hi]))
+        assert [tuple(r.tolist()) for r in ranges] == [(0, 128), (128, 256)]
         barrier()
     finally:
         dist.destroy_process_group()
@@ -60,6 +71,10 @@ def test_single_rank_needs_no_process_group():
     barrier, max_over_ranks = bench.make_rank_sync(1, torch.device("cpu"))
     barrier()
     assert max_over_ranks(3.25) == 3.25
+    t = torch.arange(6.0).view(2, 3)
+    assert bench.gather_outputs(1, t) is t
+    assert bench.strong_shard(0, 1, 256) == (0, 256)
+    assert [bench.strong_shard(r, 8, 256) for r in (0, 7)] == [(0, 32), (224, 256)]
     assert bench.whole_job_rate(1, 1000, 2.0) == 500000.0
     assert torch.equal(bench.rank_shard_ids(0, 3, 5, 50), bench.rank_shard_ids(0, 3, 5, 50))
 

@@ -13,6 +13,9 @@ Public surface (mirrors the reference package verace_v1 for this path):
     launch_mcmoe_route, situ_glu                     (M-CMoE sub-layer)
     VeraceV1Layer, AdaptiveCognitiveDepthEngine, VeraceV1Config (a decoder layer; the
                                                      ACDE loop batched over items)
+    VeraceV1Model                                    (embedding, ACDE over the layers, final
+                                                     norm, LM head; incremental decode
+                                                     through layer_states)
 The kernels live in libverace_b200.so (C ABI: include/verace_b200.h), built by
 build.py; nothing here falls back to CPU or Python arithmetic.
 """
@@ -26,6 +29,7 @@ from .mcmoe import (ManifoldContinuousMoE, SiTUGLU, launch_mcmoe_projection, lau
                     launch_mcmoe_triton_projection, situ_glu)
 from .config import VeraceV1Config
 from .layer import AdaptiveCognitiveDepthEngine, VeraceV1Layer
+from .model import VeraceV1Model
 
 __all__ = [
     "SSSDAttention", "ContinuousHolographicMemory", "newton_schulz_unitary_retraction",
@@ -34,4 +38,5 @@ __all__ = [
     "device_status", "rmsnorm", "add_rmsnorm", "launch_decode_cham_lazy", "flush_pending", "pending_storage",
     "ManifoldContinuousMoE", "SiTUGLU", "launch_mcmoe_projection", "launch_mcmoe_triton_projection",
     "launch_mcmoe_route", "situ_glu", "VeraceV1Config", "VeraceV1Layer", "AdaptiveCognitiveDepthEngine",
+    "VeraceV1Model",
 ]

@@ -29,6 +29,9 @@ _SIGNATURES = {
     "verace_sssd_scan_noalloc": (_i, [_p, _p, _p, _p, _p, _p, _p, _i, _i, _i, _i, _i, _p]),
     "verace_cham_scan_workspace": (_c_size, [_i, _i, _i, _i]),
     "verace_cham_scan": (_i, [_p, _p, _p, _p, _p, _p, _p, _p, _p, _i, _i, _i, _i, _p, _c_size, _p]),
+    "verace_cham_unitarity_workspace": (_c_size, [_i, _i]),
+    "verace_cham_unitarity": (_i, [_p, _p, _i, _i, _p, _p, _c_size, _p]),
+    "verace_cham_scan_unitary": (_i, [_p, _p, _p, _p, _p, _p, _p, _p, _p, _i, _i, _i, _i, _p, _c_size, _p]),
     "verace_cham_retract_workspace": (_c_size, [_i, _i]),
     "verace_cham_retract": (_i, [_p, _p, _p, _p, _i, _i, _i, _p, _c_size, _p]),
     "verace_decode_workspace": (_c_size, [_i, _i]),

@@ -37,9 +37,11 @@ namespace verace {
 
 // tcgen05 path (cham_tc.cu)
 bool cham_tc_supported(int D, int dtype, bool has_h0);
+bool cham_tc_supported_unitary(int D, int dtype);
 size_t cham_tc_workspace(int b, int s, int D);
-int cham_tc_scan(const void* q, const void* k, const void* v, const float* gamma, void* out,
-                 float* hr, float* hi, int b, int s, int D, int dtype, void* workspace, cudaStream_t st);
+int cham_tc_scan(const void* q, const void* k, const void* v, const float* gamma, const float* h0r,
+                 const float* h0i, void* out, float* hr, float* hi, int b, int s, int D, int dtype, void* workspace,
+                 cudaStream_t st);
 int tc_read_status(cudaStream_t st, int* status);
 int sssd_tc_read_status(int* status);
 int decode_read_status(unsigned int* status);
@@ -455,7 +457,7 @@ int readout_polynomial(const float* h0r, const float* h0i, int b, int s, int D, 
 template <typename T>
 int launch_cham(const void* q, const void* k, const void* v, const float* gamma,
                 const float* h0r, const float* h0i, void* out, float* hr, float* hi,
-                int b, int s, int D, const ChamWs& w, cudaStream_t st) {
+                int b, int s, int D, const ChamWs& w, cudaStream_t st, bool exact_readout = true) {
   const int nch = (s + CC - 1) / CC;
   int rc;
   const size_t ps = prep_smem(), cs = colpass_smem(), rs = readout_smem();
@@ -463,7 +465,7 @@ int launch_cham(const void* q, const void* k, const void* v, const float* gamma,
   cham_prep_kernel<T><<<dim3(nch, b), THREADS, ps, st>>>((const T*)k, (const T*)v, gamma, w.T, w.E, w.bad, s, D, nch);
   if ((rc = check_launch("cham_prep_kernel"))) return rc;
 
-  const bool yc = h0r != nullptr;
+  const bool yc = h0r != nullptr && exact_readout;   // readout vectors p(H0ᴴH0) q
   const float* yr = nullptr;
   const float* yi = nullptr;
   if (yc) {
@@ -506,7 +508,7 @@ using namespace verace;
 extern "C" size_t verace_cham_scan_workspace(int b, int s, int D, int has_h0) {
   if (b <= 0 || s <= 0 || D <= 0) return 256;
   size_t n = ws_layout(b, s, D, has_h0 ? 1 : 0, nullptr, nullptr);
-  if (!has_h0 && D % 128 == 0) {
+  if (D % 128 == 0) {   // (with has_h0: the tensor-core continuation of verace_cham_scan_unitary)
     const size_t t = cham_tc_workspace(b, s, D);
     if (t > n) n = t;
   }
@@ -544,7 +546,7 @@ extern "C" int verace_cham_scan(const void* q, const void* k, const void* v, con
                  "verace_cham_scan: workspace of %zu bytes required, %zu given", need,
                  workspace ? workspace_bytes : (size_t)0);
   if (cham_tc_supported(D, dtype, has_h0 != 0) && !force_simt())
-    return cham_tc_scan(q, k, v, gamma, out, h_re, h_im, b, s, D, dtype, workspace, st);
+    return cham_tc_scan(q, k, v, gamma, nullptr, nullptr, out, h_re, h_im, b, s, D, dtype, workspace, st);
   ChamWs w;
   char* base = (char*)align_up((size_t)workspace, 256);
   ws_layout(b, s, D, has_h0, &w, base);
@@ -552,6 +554,171 @@ extern "C" int verace_cham_scan(const void* q, const void* k, const void* v, con
     case VERACE_F32: return launch_cham<float>(q, k, v, gamma, h0_re, h0_im, out, h_re, h_im, b, s, D, w, st);
     case VERACE_BF16: return launch_cham<__nv_bfloat16>(q, k, v, gamma, h0_re, h0_im, out, h_re, h_im, b, s, D, w, st);
     default: return launch_cham<__half>(q, k, v, gamma, h0_re, h0_im, out, h_re, h_im, b, s, D, w, st);
+  }
+}
+
+// ---------------------------------------------------------------------------------
+// Continuation from a unitary hologram.  The Newton-Schulz readout of the scan is
+// Re(NS3(H_t) q_t) = Re(H_t p(A) q_t) with A = H0ᴴ H0 (every U_t is unitary), and
+// p(I + E) = I - E/2 + O(E^2): for a unitary H0, p(A) = I and the readout is Re(H_t q_t),
+// which the tensor-core scan computes.  verace_cham_unitarity measures how far H0 is from
+// unitary, so that a caller can choose between that scan and the exact one.
+namespace verace {
+namespace {
+constexpr int PROBES = 4;
+
+__device__ __forceinline__ double probe_sign(int j, int c) {
+  const unsigned int h = ((unsigned int)c * 2654435761u) ^ ((unsigned int)(j + 1) * 0x9E3779B9u);
+  return ((h >> 15) & 1u) ? 1.0 : -1.0;
+}
+
+// u_j = H r_j for PROBES fixed +-1 vectors r_j: one warp per row, fp64 sums; u [b][J][D] (re, im)
+__global__ void unitarity_rows_kernel(const float* __restrict__ hr, const float* __restrict__ hi,
+                                      double2* __restrict__ u, int b, int D) {
+  const long long row = (long long)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
+  const int lane = threadIdx.x & 31;
+  if (row >= (long long)b * D) return;
+  const float* pr = hr + row * D;
+  const float* pi = hi + row * D;
+  double ar[PROBES], ai[PROBES];
+#pragma unroll
+  for (int j = 0; j < PROBES; ++j) ar[j] = ai[j] = 0.0;
+  for (int c = lane; c < D; c += 32) {
+    const double xr = pr[c], xi = pi[c];
+#pragma unroll
+    for (int j = 0; j < PROBES; ++j) {
+      const double sg = probe_sign(j, c);
+      ar[j] += sg * xr;
+      ai[j] += sg * xi;
+    }
+  }
+#pragma unroll
+  for (int j = 0; j < PROBES; ++j) {
+    for (int o = 16; o > 0; o >>= 1) {
+      ar[j] += __shfl_xor_sync(0xffffffffu, ar[j], o);
+      ai[j] += __shfl_xor_sync(0xffffffffu, ai[j], o);
+    }
+  }
+  if (lane == 0) {
+    const long long item = row / D, r = row % D;
+#pragma unroll
+    for (int j = 0; j < PROBES; ++j) u[(item * PROBES + j) * D + r] = make_double2(ar[j], ai[j]);
+  }
+}
+
+// w_j = Hᴴ u_j for a stripe of 32 columns (8 warps over the rows), then the stripe's
+// sum of |w_j - r_j|^2, added into err [b][J]
+__global__ void unitarity_cols_kernel(const float* __restrict__ hr, const float* __restrict__ hi,
+                                      const double2* __restrict__ u, double* __restrict__ err, int D) {
+  __shared__ double sr[8][PROBES][32], si[8][PROBES][32];
+  const int item = blockIdx.y, c = blockIdx.x * 32 + (threadIdx.x & 31), wv = threadIdx.x / 32;
+  double ar[PROBES], ai[PROBES];
+#pragma unroll
+  for (int j = 0; j < PROBES; ++j) ar[j] = ai[j] = 0.0;
+  const float* pr = hr + (size_t)item * D * D;
+  const float* pi = hi + (size_t)item * D * D;
+  const double2* uu = u + (size_t)item * PROBES * D;
+  if (c < D) {
+    for (int r = wv; r < D; r += 8) {
+      const double xr = pr[(size_t)r * D + c], xi = pi[(size_t)r * D + c];
+#pragma unroll
+      for (int j = 0; j < PROBES; ++j) {
+        const double2 q = uu[j * D + r];   // conj(H[r][c]) u[r]
+        ar[j] += xr * q.x + xi * q.y;
+        ai[j] += xr * q.y - xi * q.x;
+      }
+    }
+  }
+#pragma unroll
+  for (int j = 0; j < PROBES; ++j) { sr[wv][j][threadIdx.x & 31] = ar[j]; si[wv][j][threadIdx.x & 31] = ai[j]; }
+  __syncthreads();
+  if (wv < PROBES) {
+    const int j = wv, l = threadIdx.x & 31;
+    double wr = 0.0, wi = 0.0;
+    for (int k = 0; k < 8; ++k) { wr += sr[k][j][l]; wi += si[k][j][l]; }
+    double e = 0.0;
+    if (blockIdx.x * 32 + l < D) {
+      const double d = wr - probe_sign(j, blockIdx.x * 32 + l);
+      e = d * d + wi * wi;
+    }
+    for (int o = 16; o > 0; o >>= 1) e += __shfl_xor_sync(0xffffffffu, e, o);
+    if (l == 0) atomicAdd(&err[item * PROBES + j], e);
+  }
+}
+
+__global__ void unitarity_final_kernel(const double* __restrict__ err, float* __restrict__ eps, int b, int D) {
+  const int item = blockIdx.x * blockDim.x + threadIdx.x;
+  if (item >= b) return;
+  double m = 0.0;
+  for (int j = 0; j < PROBES; ++j) m = fmax(m, err[item * PROBES + j]);
+  eps[item] = (float)sqrt(m / (double)D);   // |E r| / |r|, |r|^2 = D
+}
+}  // namespace
+}  // namespace verace
+
+extern "C" size_t verace_cham_unitarity_workspace(int b, int D) {
+  if (b <= 0 || D <= 0) return 256;
+  return align_up((size_t)b * PROBES * D * sizeof(double2), 256) + align_up((size_t)b * PROBES * sizeof(double), 256) +
+         256;
+}
+
+extern "C" int verace_cham_unitarity(const float* h_re, const float* h_im, int b, int D, float* eps,
+                                     void* workspace, size_t workspace_bytes, void* stream) {
+  VERACE_REQUIRE(b >= 0 && D >= 1, VERACE_ERR_INVALID, "verace_cham_unitarity: invalid sizes b=%d D=%d", b, D);
+  if (b == 0) return VERACE_OK;
+  VERACE_REQUIRE(h_re && h_im && eps, VERACE_ERR_INVALID, "verace_cham_unitarity: NULL pointer");
+  const size_t need = verace_cham_unitarity_workspace(b, D);
+  VERACE_REQUIRE(workspace != nullptr && workspace_bytes >= need, VERACE_ERR_WORKSPACE,
+                 "verace_cham_unitarity: workspace of %zu bytes required, %zu given", need,
+                 workspace ? workspace_bytes : (size_t)0);
+  cudaStream_t st = (cudaStream_t)stream;
+  char* base = (char*)align_up((size_t)workspace, 256);
+  double2* u = (double2*)base;
+  double* err = (double*)(base + align_up((size_t)b * PROBES * D * sizeof(double2), 256));
+  VERACE_CUDA(cudaMemsetAsync(err, 0, (size_t)b * PROBES * sizeof(double), st));
+  const long long rows = (long long)b * D;
+  unitarity_rows_kernel<<<(unsigned)((rows + 7) / 8), 256, 0, st>>>(h_re, h_im, u, b, D);
+  int rc = check_launch("unitarity_rows_kernel");
+  if (rc) return rc;
+  unitarity_cols_kernel<<<dim3((D + 31) / 32, b), 256, 0, st>>>(h_re, h_im, u, err, D);
+  if ((rc = check_launch("unitarity_cols_kernel"))) return rc;
+  unitarity_final_kernel<<<(b + 127) / 128, 128, 0, st>>>(err, eps, b, D);
+  return check_launch("unitarity_final_kernel");
+}
+
+extern "C" int verace_cham_scan_unitary(const void* q, const void* k, const void* v, const float* gamma,
+                                        const float* h0_re, const float* h0_im, void* out, float* h_re,
+                                        float* h_im, int b, int s, int D, int dtype, void* workspace,
+                                        size_t workspace_bytes, void* stream) {
+  VERACE_REQUIRE(b >= 0 && s >= 0 && D >= 1, VERACE_ERR_INVALID,
+                 "verace_cham_scan_unitary: invalid sizes b=%d s=%d D=%d", b, s, D);
+  VERACE_REQUIRE(dtype == VERACE_F32 || dtype == VERACE_BF16 || dtype == VERACE_F16,
+                 VERACE_ERR_INVALID, "verace_cham_scan_unitary: unknown dtype %d", dtype);
+  VERACE_REQUIRE((h0_re == nullptr) == (h0_im == nullptr), VERACE_ERR_INVALID,
+                 "verace_cham_scan_unitary: h0_re and h0_im must both be given or both be NULL");
+  if (h0_re == nullptr || b == 0 || s == 0)   // nothing to assume: the exact scan
+    return verace_cham_scan(q, k, v, gamma, h0_re, h0_im, out, h_re, h_im, b, s, D, dtype, workspace,
+                            workspace_bytes, stream);
+  VERACE_REQUIRE(h_re && h_im, VERACE_ERR_INVALID, "verace_cham_scan_unitary: NULL state output");
+  VERACE_REQUIRE(q && k && v && gamma && out, VERACE_ERR_INVALID,
+                 "verace_cham_scan_unitary: NULL input/output pointer");
+  const size_t need = verace_cham_scan_workspace(b, s, D, 1);
+  VERACE_REQUIRE(workspace != nullptr && workspace_bytes >= need, VERACE_ERR_WORKSPACE,
+                 "verace_cham_scan_unitary: workspace of %zu bytes required, %zu given", need,
+                 workspace ? workspace_bytes : (size_t)0);
+  cudaStream_t st = (cudaStream_t)stream;
+  if (cham_tc_supported_unitary(D, dtype) && !force_simt())
+    return cham_tc_scan(q, k, v, gamma, h0_re, h0_im, out, h_re, h_im, b, s, D, dtype, workspace, st);
+  ChamWs w;
+  char* base = (char*)align_up((size_t)workspace, 256);
+  ws_layout(b, s, D, 0, &w, base);
+  switch (dtype) {
+    case VERACE_F32:
+      return launch_cham<float>(q, k, v, gamma, h0_re, h0_im, out, h_re, h_im, b, s, D, w, st, false);
+    case VERACE_BF16:
+      return launch_cham<__nv_bfloat16>(q, k, v, gamma, h0_re, h0_im, out, h_re, h_im, b, s, D, w, st, false);
+    default:
+      return launch_cham<__half>(q, k, v, gamma, h0_re, h0_im, out, h_re, h_im, b, s, D, w, st, false);
   }
 }
 

@@ -1736,7 +1736,8 @@ __device__ __forceinline__ void
 colpass2_body(const CUtensorMap& tm_k, const CUtensorMap& tm_v, const CUtensorMap& tm_hr64, const CUtensorMap& tm_hi64,
               const CUtensorMap& tm_hr128, const CUtensorMap& tm_hi128, unsigned char* __restrict__ ring, int nring, int b,
               const __nv_bfloat16* __restrict__ q, const unsigned char* __restrict__ Tws, float* __restrict__ Ews,
-              const unsigned long long* __restrict__ badws, int S, int D, int nch, int c0, int c1, int item, int jb) {
+              const unsigned long long* __restrict__ badws, int S, int D, int nch, int c0, int c1, int item, int jb,
+              int h0) {
   extern __shared__ __align__(1024) unsigned char smc[];
   uint64_t* bars = reinterpret_cast<uint64_t*>(smc + CP2_BAR);
   uint32_t* tslot = reinterpret_cast<uint32_t*>(smc + CP2_BAR + 8 * N_BARS2);
@@ -1771,7 +1772,7 @@ colpass2_body(const CUtensorMap& tm_k, const CUtensorMap& tm_v, const CUtensorMa
     const size_t chunk = (size_t)item * nch + c;
     const unsigned long long bad = badws[chunk];
     const bool patch_w = bad != 0ull;       // padded rows come back zero from the TMA bounds
-    const int src_identity = c == 0;
+    const int src_identity = c == 0 && !h0;   // with a carried hologram the planes start as H0
     // The state is updated in place in the output planes (phase A reads its column
     // block, phase B adds dH with TMA reductions); phase A also stores the real part it
     // reads (the end state of chunk c-1), split into bf16 hi / lo, to that chunk's ring
@@ -2155,12 +2156,12 @@ cham_tc_colpass2(const __grid_constant__ CUtensorMap tm_k, const __grid_constant
                  const __nv_bfloat16* __restrict__ q,
                  const unsigned char* __restrict__ Tws, float* __restrict__ Ews,
                  const unsigned long long* __restrict__ badws, __nv_bfloat16* __restrict__ out, int S, int D, int nch,
-                 int c0, int c1, int r0, int nr) {
+                 int c0, int c1, int r0, int nr, int h0) {
   const int ncol = D / NB2, nrb = D / R2;
   const int bid = blockIdx.x;
   if (bid < ncol * b) {
     colpass2_body(tm_k, tm_v, tm_hr64, tm_hi64, tm_hr128, tm_hi128, ring, nring, b, q, Tws, Ews, badws, S, D, nch,
-                  c0, c1, bid / ncol, bid % ncol);
+                  c0, c1, bid / ncol, bid % ncol, h0);
   } else {
     const int r = bid - ncol * b, item = r / (nrb * nr), c = r0 + (r % (nrb * nr)) / nrb, bx = r % nrb;
     // (the fp32 state map is not read: the ring slot holds the pre-split images)
@@ -2630,8 +2631,9 @@ Schedule cham_schedule(int b, int D) {
 size_t tc_prep_smem() { return sizeof(float) * (PREP_DT * (R2 + 1) + 3 * R2 * (R2 + 1)); }
 
 template <typename T>
-int launch_cham_tc(const void* q, const void* k, const void* v, const float* gamma,
-                   void* out, float* hr, float* hi, int b, int s, int D, const TcWs& w, cudaStream_t st) {
+int launch_cham_tc(const void* q, const void* k, const void* v, const float* gamma, const float* h0r,
+                   const float* h0i, void* out, float* hr, float* hi, int b, int s, int D, const TcWs& w,
+                   cudaStream_t st) {
   const int nch = (s + C2 - 1) / C2;
   int rc;
   const size_t ps = tc_prep_smem();
@@ -2651,8 +2653,8 @@ int launch_cham_tc(const void* q, const void* k, const void* v, const float* gam
     if ((rc = check_launch("cham_tc_prep"))) return rc;
   }
   const dim3 gc(D / NB2, b), gr(D / R2, b);
-  const float* cur_r = nullptr;
-  const float* cur_i = nullptr;
+  const float* cur_r = h0r;   // state at the start of the chunk: nullptr = the identity
+  const float* cur_i = h0i;
   constexpr bool WS = sizeof(T) == 2;   // bf16: warp-specialised TMA colpass
   CUtensorMap mk, mv, m_out_r, m_out_i, m_ping_r, m_ping_i;
   if (WS) {
@@ -2663,7 +2665,8 @@ int launch_cham_tc(const void* q, const void* k, const void* v, const float* gam
       return rc;
     if (nch < 2) { m_ping_r = m_out_r; m_ping_i = m_out_i; }
   }
-  const Schedule sched = WS ? cham_schedule(b, D) : SCHED_MERGED;
+  Schedule sched = WS ? cham_schedule(b, D) : SCHED_MERGED;
+  if (h0r != nullptr && sched == SCHED_FUSED) sched = SCHED_BATCHED;   // the fused schedule starts from I
   if (sched == SCHED_FUSED) {
     CUtensorMap mq, m_ring, m_ring64, m_him64, m_hi64;
     const size_t plane = (size_t)b * D * D;
@@ -2714,13 +2717,18 @@ int launch_cham_tc(const void* q, const void* k, const void* v, const float* gam
       return rc;
     VERACE_CUDA(cudaFuncSetAttribute(cham_tc_colpass2, cudaFuncAttributeMaxDynamicSharedMemorySize, CP2_SMEM));
     VERACE_CUDA(cudaFuncSetAttribute(cham_tc_readout_batch, cudaFuncAttributeMaxDynamicSharedMemorySize, RW2_SMEM));
+    if (h0r != nullptr) {   // the planes are updated in place: start them as H0
+      const size_t plane = (size_t)b * D * D * sizeof(float);
+      VERACE_CUDA(cudaMemcpyAsync(hr, h0r, plane, cudaMemcpyDeviceToDevice, st));
+      VERACE_CUDA(cudaMemcpyAsync(hi, h0i, plane, cudaMemcpyDeviceToDevice, st));
+    }
     int r0 = 0;   // first chunk not read out yet
     for (int cb = 0; cb < nch; cb += RING) {
       const int ce = std::min(nch, cb + RING);
       const int nr = std::max(cb - 1, 0) - r0;   // chunks [r0, cb - 1) have their end states in the ring
       cham_tc_colpass2<<<(D / NB2) * b + (D / R2) * nr * b, CP2_THREADS, CP2_SMEM, st>>>(
           mk, mv, m_hr64, m_hi64, m_hr128, m_hi128, mq, ring, w.nring, b, (const __nv_bfloat16*)q, w.T, w.E, w.bad,
-          (__nv_bfloat16*)out, s, D, nch, cb, ce, r0, nr);
+          (__nv_bfloat16*)out, s, D, nch, cb, ce, r0, nr, h0r != nullptr ? 1 : 0);
       if ((rc = check_launch("cham_tc_colpass2"))) return rc;
       r0 += nr;
     }
@@ -2731,8 +2739,10 @@ int launch_cham_tc(const void* q, const void* k, const void* v, const float* gam
     return VERACE_OK;
   }
   if (WS) {
-    CUtensorMap mq;
+    CUtensorMap mq, m_h0r, m_h0i;
     if ((rc = make_kv_map(&mq, q, b, s, D))) return rc;
+    if (h0r != nullptr && ((rc = make_state_map(&m_h0r, h0r, b, D)) || (rc = make_state_map(&m_h0i, h0i, b, D))))
+      return rc;
     VERACE_CUDA(cudaFuncSetAttribute(cham_tc_step_ws, cudaFuncAttributeMaxDynamicSharedMemorySize, WS_SMEM));
     for (int c = 0; c <= nch; ++c) {
       const bool to_out = ((nch - 1 - c) % 2) == 0;
@@ -2742,10 +2752,11 @@ int launch_cham_tc(const void* q, const void* k, const void* v, const float* gam
       const bool src_out = c > 0 && ((nch - c) % 2) == 0;
       const int ncol = c < nch ? D / NB2 : 0;
       const int nread = c > 0 ? D / R2 : 0;
+      const bool from_h0 = c == 0 && h0r != nullptr;   // chunk 0 reads the carried hologram
       cham_tc_step_ws<<<dim3(ncol + nread, b), WS_THREADS, WS_SMEM, st>>>(
-          mk, mv, mq, src_out ? m_out_r : m_ping_r, src_out ? m_out_i : m_ping_i, to_out ? m_out_r : m_ping_r,
-          to_out ? m_out_i : m_ping_i, (const __nv_bfloat16*)q, w.T,
-          w.E, w.bad, c == 0 ? 1 : 0, dr, di, (__nv_bfloat16*)out, s, D, nch, c, ncol);
+          mk, mv, mq, from_h0 ? m_h0r : (src_out ? m_out_r : m_ping_r), from_h0 ? m_h0i : (src_out ? m_out_i : m_ping_i),
+          to_out ? m_out_r : m_ping_r, to_out ? m_out_i : m_ping_i, (const __nv_bfloat16*)q, w.T,
+          w.E, w.bad, (c == 0 && h0r == nullptr) ? 1 : 0, dr, di, (__nv_bfloat16*)out, s, D, nch, c, ncol);
       if ((rc = check_launch("cham_tc_step_ws"))) return rc;
     }
     return VERACE_OK;
@@ -2770,20 +2781,27 @@ int launch_cham_tc(const void* q, const void* k, const void* v, const float* gam
 
 }  // namespace
 
+// The tensor-core scan reads out Re(H_t q_t): the exact Newton-Schulz readout for a fresh
+// hologram, and for a carried one only where the caller has established that H0 is unitary
+// (verace_cham_scan_unitary).  Exact readouts of a carried hologram take the SIMT path.
 bool cham_tc_supported(int D, int dtype, bool has_h0) {
   return !has_h0 && D >= 128 && D % 128 == 0 && (dtype == VERACE_BF16 || dtype == VERACE_F32);
+}
+bool cham_tc_supported_unitary(int D, int dtype) {
+  return D >= 128 && D % 128 == 0 && (dtype == VERACE_BF16 || dtype == VERACE_F32);
 }
 
 size_t cham_tc_workspace(int b, int s, int D) { return tc_ws_layout(b, s, D, nullptr, nullptr); }
 
-int cham_tc_scan(const void* q, const void* k, const void* v, const float* gamma, void* out,
-                 float* hr, float* hi, int b, int s, int D, int dtype, void* workspace, cudaStream_t st) {
+int cham_tc_scan(const void* q, const void* k, const void* v, const float* gamma, const float* h0r,
+                 const float* h0i, void* out, float* hr, float* hi, int b, int s, int D, int dtype, void* workspace,
+                 cudaStream_t st) {
   TcWs w;
   char* base = (char*)align_up((size_t)workspace, 256);
   tc_ws_layout(b, s, D, &w, base);
   if (dtype == VERACE_BF16)
-    return launch_cham_tc<__nv_bfloat16>(q, k, v, gamma, out, hr, hi, b, s, D, w, st);
-  return launch_cham_tc<float>(q, k, v, gamma, out, hr, hi, b, s, D, w, st);
+    return launch_cham_tc<__nv_bfloat16>(q, k, v, gamma, h0r, h0i, out, hr, hi, b, s, D, w, st);
+  return launch_cham_tc<float>(q, k, v, gamma, h0r, h0i, out, hr, hi, b, s, D, w, st);
 }
 
 int tc_read_status(cudaStream_t st, int* status) {
