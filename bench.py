@@ -362,6 +362,9 @@ def run_ours(args):
     if not args.no_strong:
         torch.cuda.empty_cache()
         result["strong"] = run_strong(args, V, dev, rank, world, barrier, max_over_ranks)
+    if not args.no_long:
+        torch.cuda.empty_cache()
+        result["long"] = run_long(args, V, dev, rank, world, barrier, max_over_ranks)
     if world == 1 and not args.no_decode and not args.no_triton_bar:
         torch.cuda.empty_cache()
         result["decode"]["reference_triton"] = run_triton_bar(dev)
@@ -425,6 +428,92 @@ def run_strong(args, V, dev, rank, world, barrier, max_over_ranks):
             "scaling": "strong", "n_gpus": world, "items_per_rank": hi - lo, "ms_per_step": ms,
             "token_layers_per_s": tokens / (ms * 1e-3),
             "model_tokens_per_s_32_layers": tokens / (32 * ms * 1e-3)}
+
+
+C4 = dict(seq=65536, hidden=2048, heads=16, head_dim=128, holo=1024)
+
+
+def run_long(args, V, dev, rank, world, barrier, max_over_ranks):
+    """Config 4: one long sequence through one layer's SSSD and CHAM sub-layers (hidden
+    2048, 16 heads x 128, D = 1024; random init, seed 0; x ~ N(0, 1) of [1, 65536, 2048]
+    from seed 1; bf16, fp32 states): h <- h + SSSD(RMSNorm(h)); h <- h + CHAM(RMSNorm(h)).
+    One sequence leaves 16 SSSD chains and one hologram: both scans run as parallel
+    sequence ranges (ranges.py).  With N ranks each takes one contiguous segment of the
+    sequence (strong scaling); the segment products cross the ranks in one NCCL all_gather
+    per mixer and the outputs in one more.  Also times the scans alone, ranges against one
+    chain (N = 1)."""
+    import torch
+    from verace_v1_b200.kernels import launch_cham_update, launch_sssd_scan
+    from verace_v1_b200.ranges import cham_scan_ranges, pick_ranges, sssd_scan_ranges
+    c = C4
+    torch.manual_seed(0)
+    sssd_norm = torch.nn.RMSNorm(c["hidden"], eps=1e-6)
+    sssd = V.SSSDAttention(c["hidden"], c["heads"], c["head_dim"], 256)
+    cham_norm = torch.nn.RMSNorm(c["hidden"], eps=1e-6)
+    cham = V.ContinuousHolographicMemory(c["hidden"], c["holo"])
+    mods = torch.nn.ModuleList([sssd_norm, sssd, cham_norm, cham]).to(dev, torch.bfloat16).eval()
+    seg = c["seq"] // world
+    x = torch.randn(1, c["seq"], c["hidden"], generator=torch.Generator().manual_seed(1))
+    xs = x[:, rank * seg:(rank + 1) * seg].to(dev, torch.bfloat16)
+    del x
+    group = None
+    if world > 1:
+        import torch.distributed as dist
+        group = dist.group.WORLD
+    Rs = pick_ranges(c["heads"], seg, dev, per_sm=1)
+    Rc = pick_ranges(c["holo"] // 32, seg, dev, per_sm=2)
+
+    def step():
+        h = xs.clone()
+        n = V.rmsnorm(h, sssd_norm)
+        q, k, v, dl = sssd.project(n)
+        if group is None:
+            o, _ = launch_sssd_scan(q, k, v, dl)
+        else:
+            o, _ = sssd_scan_ranges(q, k, v, dl, None, Rs, group)
+        n = V.add_rmsnorm(h, sssd.finish(o), out_norm=cham_norm)
+        q, k, v, g = cham.project(n)
+        if group is None:
+            rec, _ = launch_cham_update(q, k, v, g)
+        else:
+            rec, _ = cham_scan_ranges(q, k, v, g, None, Rc, group)
+        V.add_rmsnorm(h, cham.w_out(rec), y_norm=cham.norm)
+        return gather_outputs(world, h)
+
+    def timed(fn, reps):
+        fn()
+        barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(reps):
+            fn()
+        e1.record()
+        barrier()
+        return max_over_ranks(e0.elapsed_time(e1) / reps)
+
+    with torch.no_grad():
+        ms = timed(step, 3)
+        res = {"workload": "config 4: one SSSD + CHAM layer, b=1 x s=65536, hidden 2048, 16x128 heads, D=1024, "
+                           "bf16; the scans as parallel sequence ranges"
+                           + (f"; the sequence split over {world} ranks (strong scaling)" if world > 1 else ""),
+               "scaling": "strong", "n_gpus": world, "ms_per_step": ms,
+               "token_layers_per_s": c["seq"] / (ms * 1e-3), "ranges": {"sssd": Rs, "cham": Rc}}
+        if world == 1:
+            n = V.rmsnorm(xs, sssd_norm)
+            qs, ks, vs, dl = sssd.project(n)
+            qc, kc, vc, g = cham.project(n)
+            res["sssd_scan_ms"] = timed(lambda: launch_sssd_scan(qs, ks, vs, dl), 3)
+            res["sssd_scan_one_chain_ms"] = timed(lambda: launch_sssd_scan(qs, ks, vs, dl, _ranges=False), 2)
+            res["cham_scan_ms"] = timed(lambda: launch_cham_update(qc, kc, vc, g), 3)
+            res["cham_scan_one_chain_ms"] = timed(lambda: launch_cham_update(qc, kc, vc, g, _ranges=False), 1)
+            _, _, bf16_sus, _ = _peaks()
+            flop = c["seq"] * (18.0 * c["heads"] * c["head_dim"] ** 2 + 18.0 * c["holo"] ** 2)
+            t = (res["sssd_scan_ms"] + res["cham_scan_ms"]) * 1e-3
+            res["scan_roofline"] = {"bound": "tensor", "flop": flop, "achieved": flop / t / 1e12, "peak": bf16_sus,
+                                    "unit": "TFLOP/s", "frac": flop / t / 1e12 / bf16_sus,
+                                    "basis": "18 h d^2 + 18 D^2 FLOP per token (necessary), both scans"}
+    del mods, xs
+    return res
 
 
 def run_mcmoe(args, V, dev, barrier, max_over_ranks):
@@ -812,6 +901,7 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-decode", action="store_true", help="skip the config-3 decode measurement")
     ap.add_argument("--no-mcmoe", action="store_true", help="skip the M-CMoE sub-layer measurement")
+    ap.add_argument("--no-long", action="store_true", help="skip the config-4 long-sequence measurement")
     ap.add_argument("--no-strong", action="store_true",
                     help="skip the config-5 one-layer strong-scaling measurement")
     ap.add_argument("--no-triton-bar", action="store_true",

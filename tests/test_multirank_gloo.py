@@ -63,6 +63,38 @@ def _rank_worker(rank, world, port):
         dist.destroy_process_group()
 
 
+def _segment_worker(rank, world, port):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60))
+    try:
+        bench._load_package()      # registers the package in this spawned process
+        from verace_v1_b200 import ranges
+        g = torch.Generator().manual_seed(7)
+        Ts = [torch.randn(2, 3, 5, 5, generator=g, dtype=torch.float64) for _ in range(world)]
+        Tc = [torch.randn(2, 5, 5, generator=g, dtype=torch.complex128) for _ in range(world)]
+        S0 = torch.randn(2, 3, 5, 5, generator=g, dtype=torch.float64)
+        S0c = torch.randn(2, 5, 5, generator=g, dtype=torch.complex128)
+        # the state entering this rank's segment: the earlier segments' products, in order
+        S = ranges._prior_product(Ts[rank], S0, dist.group.WORLD)
+        Sc = ranges._prior_product(Tc[rank], S0c, dist.group.WORLD)
+        want, wantc = S0, S0c
+        for j in range(rank):
+            want, wantc = Ts[j] @ want, Tc[j] @ wantc
+        assert torch.allclose(S, want, rtol=1e-12, atol=1e-12)
+        assert torch.allclose(Sc, wantc, rtol=1e-12, atol=1e-12)
+        # a segment's product of its ranges, newest on the left
+        P = torch.randn(2, 4, 3, 3, generator=g, dtype=torch.float64)
+        T = ranges._segment_product(P)
+        assert torch.allclose(T, P[:, 3] @ P[:, 2] @ P[:, 1] @ P[:, 0])
+    finally:
+        dist.destroy_process_group()
+
+
+def test_sequence_segments_carry_state_across_two_gloo_ranks():
+    mp.start_processes(_segment_worker, args=(2, _free_port()), nprocs=2, start_method="spawn", join=True)
+
+
 def test_two_gloo_ranks_shard_and_time_like_the_nccl_ranks():
     mp.start_processes(_rank_worker, args=(2, _free_port()), nprocs=2, start_method="spawn", join=True)
 

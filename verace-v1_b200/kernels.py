@@ -42,13 +42,19 @@ def _ptr(t: Optional[torch.Tensor]):
 
 
 def launch_sssd_scan(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, delta: torch.Tensor,
-                     initial_state: Optional[torch.Tensor] = None
+                     initial_state: Optional[torch.Tensor] = None, *, _ranges: bool = True
                      ) -> Tuple[torch.Tensor, torch.Tensor]:
     """q, k, v: [b, s, h, d] (L2-normalised); delta: [b, s, h]; initial_state:
     optional [b, h, d, d] (identity when None).
-    Returns (out [b, s, h, d] in q's dtype, final_state [b, h, d, d] fp32)."""
+    Returns (out [b, s, h, d] in q's dtype, final_state [b, h, d, d] fp32).
+    Long sequences on few chains run as parallel sequence ranges (ranges.py)."""
     assert q.is_cuda, "This kernel requires CUDA tensors"
     b, s, h, d = q.shape
+    if _ranges and b * h > 0 and not torch.cuda.is_current_stream_capturing():
+        from .ranges import pick_ranges, sssd_scan_ranges
+        R = pick_ranges(b * h, s, q.device, per_sm=1)
+        if R > 1:
+            return sssd_scan_ranges(q, k, v, delta, initial_state, R)
     q_c = _prep(q)
     dt = q_c.dtype
     k_c = k.to(dt).contiguous()
@@ -112,7 +118,8 @@ def _carried_path(h0r: torch.Tensor, h0i: torch.Tensor, s: int, D: int, dt: torc
 
 
 def launch_cham_update(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, gamma: torch.Tensor,
-                       initial_hologram: Optional[Tuple[torch.Tensor, torch.Tensor]] = None
+                       initial_hologram: Optional[Tuple[torch.Tensor, torch.Tensor]] = None, *,
+                       _ranges: bool = True
                        ) -> Tuple[torch.Tensor, Tuple[torch.Tensor, torch.Tensor]]:
     """q, k, v: [b, s, D]; gamma: [b, s]; initial_hologram: optional (H_real, H_imag)
     [b, D, D] ((I, 0) when None).
@@ -120,10 +127,16 @@ def launch_cham_update(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, gamma:
 
     A carried hologram is checked for unitarity first (one host read): a unitary one
     continues on the tensor-core scan (one token: the fused decode kernel), any other on
-    the exact Newton-Schulz readout polynomial; see UNITARY_TOL."""
+    the exact Newton-Schulz readout polynomial; see UNITARY_TOL.  Long sequences on few
+    holograms run as parallel sequence ranges (ranges.py)."""
     global last_carried_path
     assert q.is_cuda, "This kernel requires CUDA tensors"
     b, s, D = q.shape
+    if _ranges and b > 0 and D % 32 == 0 and not torch.cuda.is_current_stream_capturing():
+        from .ranges import cham_scan_ranges, pick_ranges
+        R = pick_ranges(b * (D // 32), s, q.device, per_sm=2)
+        if R > 1:
+            return cham_scan_ranges(q, k, v, gamma, initial_hologram, R)
     q_c = _prep(q)
     dt = q_c.dtype
     k_c = k.to(dt).contiguous()
