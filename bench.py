@@ -866,6 +866,12 @@ def run_only(args):
         q, k, v = (nrm(torch.randn(b, D, generator=g), dim=-1).to(dev, torch.bfloat16) for _ in range(3))
         gam = (0.1 * torch.sigmoid(torch.randn(b, generator=g))).to(dev)
         fn = lambda: st.step_cham(0, q, k, v, gam)
+    elif args.only == "retract":
+        V = sys.modules["verace_v1_b200"]
+        D = c["holo"]
+        Hr = (torch.eye(D).expand(b, D, D) + 0.01 * torch.randn(b, D, D, generator=g)).to(dev)
+        Hi = (0.01 * torch.randn(b, D, D, generator=g)).to(dev)
+        fn = lambda: V.newton_schulz_unitary_retraction(Hr, Hi, 3)
     elif args.only == "cham":
         D = c["holo"]
         q, k, v = (nrm(torch.randn(b, s, D, generator=g), dim=-1).to(dev, torch.bfloat16) for _ in range(3))
@@ -906,7 +912,7 @@ def main():
                     help="skip the config-5 one-layer strong-scaling measurement")
     ap.add_argument("--no-triton-bar", action="store_true",
                     help="skip timing the reference's Triton decode path (one layer, config 3)")
-    ap.add_argument("--only", choices=["cham", "sssd", "decode", "mcmoe"], default=None,
+    ap.add_argument("--only", choices=["cham", "sssd", "decode", "mcmoe", "retract"], default=None,
                     help="time one scan entry point alone (kernel-level case for profiling)")
     ap.add_argument("--batch", type=int, default=None)
     ap.add_argument("--seq", type=int, default=None)

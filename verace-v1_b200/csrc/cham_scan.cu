@@ -71,6 +71,8 @@ struct ChamWs {
   float* Hre;                // [b][D][D]  ping-pong partner of the output state
   float* Him;
   float* Y;                  // [6][2][b][s][D]  readout polynomial vectors (has_h0 only)
+  void* pack;                // the tensor-core complex GEMM's operand scratch (has_h0 only)
+  size_t pack_bytes;
 };
 
 size_t ws_layout(int b, int s, int D, int has_h0, ChamWs* w, char* base) {
@@ -85,6 +87,8 @@ size_t ws_layout(int b, int s, int D, int has_h0, ChamWs* w, char* base) {
   t.Hre = (float*)take(need_ping ? (size_t)b * D * D * sizeof(float) : 0);
   t.Him = (float*)take(need_ping ? (size_t)b * D * D * sizeof(float) : 0);
   t.Y = (float*)take(has_h0 ? (size_t)12 * b * s * D * sizeof(float) : 0);
+  t.pack_bytes = has_h0 ? cgemm_tc_scratch(s, D, D, b) : 0;
+  t.pack = take(t.pack_bytes);
   if (w) *w = t;
   return off + 256;
 }
@@ -422,7 +426,7 @@ size_t readout_smem() {
 // y = p(A) q with A = H0ᴴ H0 (see the file comment).  All vector sets are [b][s][D]
 // planar complex in the workspace; returns the index of the set holding y.
 int readout_polynomial(const float* h0r, const float* h0i, int b, int s, int D, float* Y,
-                       int* y_index, cudaStream_t st) {
+                       void* pack, size_t pack_bytes, int* y_index, cudaStream_t st) {
   const size_t set = (size_t)2 * b * s * D;
   auto re = [&](int i) { return Y + i * set; };
   auto im = [&](int i) { return Y + i * set + set / 2; };
@@ -430,13 +434,13 @@ int readout_polynomial(const float* h0r, const float* h0i, int b, int s, int D, 
   const int TMP = 5;
   // out = alpha * A in + beta * comb   (A in = H0ᴴ (H0 in))
   auto applyA = [&](int in, int outi, float alpha, float beta, int comb) -> int {
-    int rc = cgemm(s, D, D, b, 1.f, CMat{re(in), im(in), D, vs}, false, false,
-                   CMat{h0r, h0i, D, hs}, true, false, 0.f, CMat{nullptr, nullptr, 0, 0},
-                   re(TMP), im(TMP), D, vs, st);
+    int rc = cgemm_tc(s, D, D, b, 1.f, CMat{re(in), im(in), D, vs}, false, false,
+                      CMat{h0r, h0i, D, hs}, true, false, 0.f, CMat{nullptr, nullptr, 0, 0},
+                      re(TMP), im(TMP), D, vs, pack, pack_bytes, st);
     if (rc) return rc;
-    return cgemm(s, D, D, b, alpha, CMat{re(TMP), im(TMP), D, vs}, false, false,
-                 CMat{h0r, h0i, D, hs}, false, true, beta, CMat{re(comb), im(comb), D, vs},
-                 re(outi), im(outi), D, vs, st);
+    return cgemm_tc(s, D, D, b, alpha, CMat{re(TMP), im(TMP), D, vs}, false, false,
+                    CMat{h0r, h0i, D, hs}, false, true, beta, CMat{re(comb), im(comb), D, vs},
+                    re(outi), im(outi), D, vs, pack, pack_bytes, st);
   };
   auto g0 = [&](int in, int outi) { return applyA(in, outi, -0.5f, 1.5f, in); };
   int rc = 0;
@@ -473,7 +477,7 @@ int launch_cham(const void* q, const void* k, const void* v, const float* gamma,
     to_complex_kernel<T><<<1024, 256, 0, st>>>((const T*)q, w.Y, w.Y + set / 2, set / 2);
     if ((rc = check_launch("to_complex_kernel"))) return rc;
     int yidx = 0;
-    if ((rc = readout_polynomial(h0r, h0i, b, s, D, w.Y, &yidx, st))) return rc;
+    if ((rc = readout_polynomial(h0r, h0i, b, s, D, w.Y, w.pack, w.pack_bytes, &yidx, st))) return rc;
     yr = w.Y + yidx * set;
     yi = yr + set / 2;
   }
@@ -724,7 +728,7 @@ extern "C" int verace_cham_scan_unitary(const void* q, const void* k, const void
 
 extern "C" size_t verace_cham_retract_workspace(int b, int D) {
   if (b <= 0 || D <= 0) return 256;
-  return align_up((size_t)4 * b * D * D * sizeof(float), 256) + 256;
+  return align_up((size_t)4 * b * D * D * sizeof(float), 256) + cgemm_tc_scratch(D, D, D, b) + 256;
 }
 
 extern "C" int verace_cham_retract(const float* h_re, const float* h_im, float* out_re, float* out_im,
@@ -750,6 +754,8 @@ extern "C" int verace_cham_retract(const float* h_re, const float* h_im, float* 
   float* HHi = base + n;
   float* Pr = base + 2 * n;
   float* Pi = base + 3 * n;
+  void* pack = base + 4 * n;
+  const size_t pack_bytes = need - 256 - align_up((size_t)4 * n * sizeof(float), 256);
   const long long hs = (long long)D * D;
   const float* cr = h_re;
   const float* ci = h_im;
@@ -758,12 +764,12 @@ extern "C" int verace_cham_retract(const float* h_re, const float* h_im, float* 
     float* nr = to_out ? out_re : Pr;
     float* ni = to_out ? out_im : Pi;
     // HH = curᴴ cur
-    int rc = cgemm(D, D, D, b, 1.f, CMat{cr, ci, D, hs}, true, true, CMat{cr, ci, D, hs}, false, false,
-                   0.f, CMat{nullptr, nullptr, 0, 0}, HHr, HHi, D, hs, st);
+    int rc = cgemm_tc(D, D, D, b, 1.f, CMat{cr, ci, D, hs}, true, true, CMat{cr, ci, D, hs}, false, false,
+                      0.f, CMat{nullptr, nullptr, 0, 0}, HHr, HHi, D, hs, pack, pack_bytes, st);
     if (rc) return rc;
     // next = 1.5 cur - 0.5 cur HH
-    rc = cgemm(D, D, D, b, -0.5f, CMat{cr, ci, D, hs}, false, false, CMat{HHr, HHi, D, hs}, false, false,
-               1.5f, CMat{cr, ci, D, hs}, nr, ni, D, hs, st);
+    rc = cgemm_tc(D, D, D, b, -0.5f, CMat{cr, ci, D, hs}, false, false, CMat{HHr, HHi, D, hs}, false, false,
+                  1.5f, CMat{cr, ci, D, hs}, nr, ni, D, hs, pack, pack_bytes, st);
     if (rc) return rc;
     cr = nr;
     ci = ni;
@@ -779,6 +785,9 @@ extern "C" int verace_device_status(void* stream) {
   if (rc) return rc;
   status |= status2;
   rc = mcmoe_read_status(&status2);
+  if (rc) return rc;
+  status |= status2;
+  rc = cgemm_tc_read_status(&status2);
   if (rc) return rc;
   status |= status2;
   unsigned int dstat = 0;   // bit 0: a hologram far from unitary; bit 1: a decode wait gave up
