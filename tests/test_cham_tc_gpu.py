@@ -55,11 +55,11 @@ def test_tc_scan_bf16_matches_fp64_oracle(b, s, D):
     assert np.abs(to_np(Hi) - Hi_ref).max() <= 1e-4
 
 
-@pytest.mark.parametrize("sched", ["batched", "fused", "wide"])
+@pytest.mark.parametrize("sched", ["batched", "fused"])
 @pytest.mark.parametrize("b,s,D", [(2, 700, 256), (1, 64, 128), (3, 65, 128), (2, 1733, 128)])
 def test_tc_scan_bf16_schedules_match_fp64_oracle(sched, b, s, D):
-    """The column-pass schedules (state in place with TMA reductions and ring copies for the
-    readout, 32 or 64 columns per CTA; one fused pass per chunk), forced at sizes
+    """The column-pass schedules chosen at larger batches (state in place with TMA
+    reductions and ring copies for the readout; one fused pass per chunk), forced at sizes
     the oracle runs in seconds.  s = 700 is 11 chunks, one group of the batched schedule;
     s = 1733 is 28 chunks: groups of 12, 12 and 4, the second and third group launches
     running the previous group's readouts from the pre-split ring, whose 24 slots are
@@ -109,22 +109,21 @@ def test_tc_scan_zero_gamma_and_nonfinite_tokens():
 @pytest.mark.parametrize("b,s,D", [(3, 600, 256), (2, 130, 1024), (1, 64, 128), (2, 10, 128), (2, 1733, 128),
                                    (1, 900, 1024)])
 def test_schedules_agree(b, s, D):
-    """The four bf16 schedules (merged per-chunk launches; column passes two CTAs per SM
-    with batched readouts; the same with 64 columns and one CTA per SM; one fused pass per
-    chunk) run the same arithmetic, so the results agree to fp32 accumulation order (the E
-    partials are summed atomically)."""
+    """The three bf16 schedules (merged per-chunk launches; column passes two CTAs per SM
+    with batched readouts; one fused pass per chunk) run the same arithmetic, so the
+    results agree to fp32 accumulation order (the E partials are summed atomically)."""
     q, k, v, g = random_cham_inputs(b, s, D, seed=800 + s, dtype=torch.bfloat16)
     k[0, min(5, s - 1), 3] = float("nan")
     res = {}
     try:
-        for sched in ("merged", "batched", "fused", "wide"):
+        for sched in ("merged", "batched", "fused"):
             os.environ["VERACE_CHAM_SCHEDULE"] = sched
             res[sched] = V.launch_cham_update(q, k, v, g)
     finally:
         del os.environ["VERACE_CHAM_SCHEDULE"]
     _status_ok()
     out_m, (Hr_m, Hi_m) = res["merged"]
-    for sched in ("batched", "fused", "wide"):
+    for sched in ("batched", "fused"):
         out, (Hr, Hi) = res[sched]
         # the complex state against its own norm (its imaginary part is ~50x smaller, and the
         # schedules sum the hi- and lo-operand products in different orders)

@@ -2171,459 +2171,6 @@ cham_tc_colpass2(const __grid_constant__ CUtensorMap tm_k, const __grid_constant
 }
 
 // ---------------------------------------------------------------------------------
-// Column pass with 64 complex columns per CTA and one CTA per SM ("wide" schedule, used
-// while the launch's column CTAs fit one wave: b * D / 64 <= #SMs).  The arithmetic of
-// colpass2_body; the CTA count halves (at b = 8, D = 1024: 128 CTAs, one per SM, instead
-// of 256 sharing SMs two by two), each chunk's W tiles are streamed once per 64 columns
-// instead of once per 32, and the whole shared memory serves one chain of phases: phase T
-// takes all four T tiles in one round, phase B stages dH beside the next W tile.
-//
-// smem (208 KB + barriers):
-//   phase A: slots [0,48K) [48K,96K) [96K,144K); slot = W half tile (k box 8K | v box 8K)
-//            | state half tile (re 2 boxes 16K | im 2 boxes 16K, fp32 SW128), split in
-//            place into one bf16 MN-major operand [64 rows][hi 128 | lo 128] (32K)
-//   phase T: Tr hi | Tr lo | Ti hi | Ti lo at [0,128K)
-//   phase E: Re(Cm) K-major hi 16K | lo 16K at [0,32K), Y (64 tok x 64 cols) at [32K,40K)
-//   phase B: slots [0,64K) [64K,128K): W tile (32K), then dH (re 2 boxes | im 2 boxes, 64K)
-//   ZC [144K,208K): Z as [128][hi 128 | lo 128] bf16 MN-major, then Cm the same way
-// TMEM (512 columns): Z [0,256); P1 [0,256) P2 [256,512); E [0,64); dH[2] at 0 and 256.
-constexpr int NB4 = 64, N4 = 2 * NB4, NGW4 = 2 * N4 / 8;
-constexpr int CP4_SLOT = 48 * 1024, CP4_BSLOT = 64 * 1024, CP4_ZC = 144 * 1024, CP4_BAR = 208 * 1024;
-constexpr int CP4_SMEM = CP4_BAR + 256;
-
-__device__ __forceinline__ void
-colpass4_body(const CUtensorMap& tm_k, const CUtensorMap& tm_v, const CUtensorMap& tm_hr64, const CUtensorMap& tm_hi64,
-              const CUtensorMap& tm_hr128, const CUtensorMap& tm_hi128, unsigned char* __restrict__ ring, int nring, int b,
-              const __nv_bfloat16* __restrict__ q, const unsigned char* __restrict__ Tws, float* __restrict__ Ews,
-              const unsigned long long* __restrict__ badws, int S, int D, int nch, int c0, int c1, int item, int jb,
-              int h0) {
-  extern __shared__ __align__(1024) unsigned char smc[];
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smc + CP4_BAR);
-  uint32_t* tslot = reinterpret_cast<uint32_t*>(smc + CP4_BAR + 8 * N_BARS2);
-  volatile int* fail = reinterpret_cast<volatile int*>(smc + CP4_BAR + 8 * N_BARS2 + 16);
-  auto aslot = [&](int s) { return smc + s * CP4_SLOT; };    // phase A
-  auto bslot = [&](int s) { return smc + s * CP4_BSLOT; };   // phase B
-  unsigned char* sZ = smc + CP4_ZC;       // Z, then Cm: [128][hi 128 | lo 128] bf16 MN-major (64K)
-  unsigned char* sAh = smc;               // phase E: Re(Cm) K-major hi/lo, Y
-  unsigned char* sAl = smc + 16 * 1024;
-  unsigned char* sY = smc + 32 * 1024;
-
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int j0 = jb * NB4;
-  const int NH = D / KH, NT = D / KT;
-
-  if (warp == 0) tc::tmem_alloc(tslot, 512);
-  if (tid == 0) {
-    for (int i = 0; i < N_BARS2; ++i) tc::mbar_init(&bars[i], 1);
-    *fail = 0;
-    tc::fence_mbar_init();
-  }
-  tc::fence_before_sync();
-  __syncthreads();
-  tc::fence_after_sync();
-  const uint32_t tbase = *tslot;
-  const uint32_t tZ = tbase, tP1 = tbase, tP2 = tbase + 256, tE = tbase, tDH = tbase;
-
-  for (int c = c0; c < c1; ++c) {
-    const int t0 = c * C2, nt = min(C2, S - t0);
-    const size_t chunk = (size_t)item * nch + c;
-    const unsigned long long bad = badws[chunk];
-    const bool patch_w = bad != 0ull;       // padded rows come back zero from the TMA bounds
-    const int src_identity = c == 0 && !h0;
-    unsigned char* ring_img = c > 0 ? ring + (((size_t)((c - 1) % nring) * b + item) * D) * D * sizeof(float) : nullptr;
-
-    auto issue_a = [&](int h) {   // phase-A half tile h into slot h % 3
-      const int s = h % 3;
-      unsigned char* w = aslot(s);
-      tc::mbar_expect_tx(&bars[B2_FULL + s], 16 * 1024 + (src_identity ? 0 : 32 * 1024));
-      tc::tma_load_3d(w, &tm_k, h * KH, t0, item, &bars[B2_FULL + s]);
-      tc::tma_load_3d(w + 8192, &tm_v, h * KH, t0, item, &bars[B2_FULL + s]);
-      if (!src_identity) {
-#pragma unroll
-        for (int bx = 0; bx < 2; ++bx) {
-          tc::tma_load_2d(w + 16384 + bx * 8192, &tm_hr64, j0 + 32 * bx, item * D + h * KH, &bars[B2_FULL + s]);
-          tc::tma_load_2d(w + 32768 + bx * 8192, &tm_hi64, j0 + 32 * bx, item * D + h * KH, &bars[B2_FULL + s]);
-        }
-      }
-    };
-    if (warp == 9) {
-      // ============ phase-A loader (one thread): refill each slot once its MMAs are done ============
-      if (lane == 0) {
-        for (int h = 0; h + 3 < NH; ++h) {
-          if (*fail || !tc::mbar_wait(&bars[B2_MD + h % 3], (h / 3) & 1, MAX_POLLS)) {
-            *fail = 1;
-            record_timeout();
-            break;
-          }
-          issue_a(h + 3);
-        }
-      }
-    } else if (warp == 8) {
-      // ======================= producer (one thread) =======================
-      if (lane == 0) {
-        bool ok = true;
-        auto pwait = [&](int bb, uint32_t par) {
-          if (!ok) return false;
-          if (*fail || !tc::mbar_wait(&bars[bb], par, MAX_POLLS)) { ok = false; *fail = 1; record_timeout(); }
-          return ok;
-        };
-        auto issue_b = [&](int kt) {  // phase-B W tile kt into slot (kt + 1) & 1
-          const int s = (kt + 1) & 1;
-          unsigned char* w = bslot(s);
-          tc::mbar_expect_tx(&bars[B2_FULL + s], W_TILE);
-#pragma unroll
-          for (int kb = 0; kb < KT / 64; ++kb) {
-            tc::tma_load_3d(w + kb * 16384, &tm_k, kt * KT + kb * 64, t0, item, &bars[B2_FULL + s]);
-            tc::tma_load_3d(w + kb * 16384 + 8192, &tm_v, kt * KT + kb * 64, t0, item, &bars[B2_FULL + s]);
-          }
-        };
-        constexpr uint32_t ID_Z = tc::idesc_bf16(128, 2 * N4, false, true);
-        constexpr uint32_t ID_H = tc::idesc_bf16(128, 2 * N4, true, true);
-        // ---- phase A: Z = Wᵀ S over 64-row half tiles (the loader warp refills the slots)
-        for (int h = 0; h < 3 && h < NH; ++h) issue_a(h);
-        for (int h = 0; h < NH && ok; ++h) {
-          const int s = h % 3;
-          if (!pwait(B2_FULL + s, (h / 3) & 1) || !pwait(B2_SPL + s, (h / 3) & 1)) break;
-          tc::fence_after_sync();
-          const uint32_t aw = tc::smem_addr(aslot(s));
-          const uint32_t bb = aw + 16384;
-#pragma unroll 1
-          for (int ks = 0; ks < KH / 16; ++ks) {
-            const uint64_t a = tc::sdesc_sw128(aw + ks * 32, 16, 1024);
-            tc::mma_bf16(tZ, a, tc::sdesc(bb + ks * 2 * NGW4 * 128, NGW4 * 128, 128), ID_Z, (h > 0 || ks > 0) ? 1u : 0u);
-          }
-          tc::commit(&bars[B2_MD + s]);
-        }
-        // ---- phase T: all four T tiles in one round; P1 = Tr Z, P2 = Ti Z
-        const int sl = (NH - 1) % 3;
-        const unsigned char* tsrc = Tws + chunk * 4 * T_TILE;
-        constexpr uint32_t ID_T = tc::idesc_bf16(128, 2 * N4, false, true);
-        constexpr uint32_t ID_TH = tc::idesc_bf16(128, N4, false, true);
-        if (ok && pwait(B2_MD + sl, ((NH - 1) / 3) & 1)) {   // every phase-A MMA done: slots free
-          tc::mbar_expect_tx(&bars[B2_TT], 4 * T_TILE);
-#pragma unroll
-          for (int i = 0; i < 4; ++i) tc::bulk_load(smc + i * T_TILE, tsrc + i * T_TILE, T_TILE, &bars[B2_TT]);
-          if (pwait(B2_ZR, 0) && pwait(B2_TT, 0)) {
-            tc::fence_after_sync();
-            const uint32_t z = tc::smem_addr(sZ);
-#pragma unroll 1
-            for (int p = 0; p < 2; ++p) {
-              const uint32_t th = tc::smem_addr(smc + 2 * p * T_TILE), tl = th + T_TILE;
-              const uint32_t td = p == 0 ? tP1 : tP2;
-#pragma unroll 1
-              for (int ks = 0; ks < R2 / 16; ++ks) {
-                const uint64_t ah = tc::sdesc(th + ks * 2 * R2 * 16, R2 * 16, 128);
-                const uint64_t al = tc::sdesc(tl + ks * 2 * R2 * 16, R2 * 16, 128);
-                const uint64_t bz = tc::sdesc(z + ks * 2 * NGW4 * 128, NGW4 * 128, 128);   // [Z_hi | Z_lo]
-                tc::mma_bf16(td, ah, bz, ID_T, ks > 0 ? 1u : 0u);
-                tc::mma_bf16(td, al, bz, ID_TH, 1u);                                       // T_lo Z_hi
-              }
-            }
-            tc::commit(&bars[B2_MT]);
-          }
-        }
-        // ---- phase E: E = Re(Cm) Y; the first phase-B W tile goes to slot 1
-        if (ok && pwait(B2_MT, 0)) {
-          issue_b(0);
-          if (pwait(B2_CR, 0)) {
-            tc::fence_after_sync();
-            constexpr uint32_t ID_E = tc::idesc_bf16(128, C2, false, false);
-            const uint32_t ah = tc::smem_addr(sAh), al = tc::smem_addr(sAl), yh = tc::smem_addr(sY);
-#pragma unroll 1
-            for (int ks = 0; ks < NB4 / 16; ++ks) {
-              const uint64_t b_h = tc::sdesc(yh + ks * 2 * C2 * 16, C2 * 16, 128);
-              tc::mma_bf16(tE, tc::sdesc(ah + ks * 2 * R2 * 16, R2 * 16, 128), b_h, ID_E, ks > 0 ? 1u : 0u);
-              tc::mma_bf16(tE, tc::sdesc(al + ks * 2 * R2 * 16, R2 * 16, 128), b_h, ID_E, 1u);
-            }
-            tc::commit(&bars[B2_ME]);
-          }
-        }
-        // ---- phase B: per 128-row tile: W tile -> dH = W Cm (TMEM, double-buffered) ->
-        // dH staged into the same slot -> TMA reduce-add onto the state -> slot free
-        if (ok && pwait(B2_ME, 0)) {
-          if (NT > 1) issue_b(1);
-          for (int kt = 0; kt < NT && ok; ++kt) {
-            const int s = (kt + 1) & 1, d = kt & 1;
-            const uint32_t use = (uint32_t)((NH + 2 - s) / 3 + (kt >> 1));   // use of barrier FULL+s
-            if (!pwait(B2_FULL + s, use & 1)) break;
-            if (patch_w && !pwait(B2_SPL + s, use & 1)) break;
-            if (kt == 0 && !pwait(B2_ER, 0)) break;   // dH[0] overlaps E: the consumers have read it
-            if (kt >= 2 && !pwait(B2_DF + d, ((kt - 2) >> 1) & 1)) break;
-            tc::fence_after_sync();
-            const uint32_t aw = tc::smem_addr(bslot(s));
-            const uint32_t cm = tc::smem_addr(sZ);
-#pragma unroll 1
-            for (int ks = 0; ks < R2 / 16; ++ks) {
-              const uint64_t a = tc::sdesc_sw128(aw + ks * 2048, 16384, 1024);
-              tc::mma_bf16(tDH + 256 * d, a, tc::sdesc(cm + ks * 2 * NGW4 * 128, NGW4 * 128, 128), ID_H,
-                           ks > 0 ? 1u : 0u);
-            }
-            tc::commit(&bars[B2_DH + d]);
-            // tile kt-1's slot, once its store has read it, takes W tile kt+1
-            if (kt >= 1 && kt + 1 < NT) {
-              const int sp = kt & 1;
-              if (!pwait(B2_SR + sp, ((kt - 1) >> 1) & 1)) break;
-              issue_b(kt + 1);
-            }
-          }
-        }
-      }
-    } else {
-      // ======================= consumers (warps 0-7) =======================
-      const uint32_t lane_base = (uint32_t)(32 * (warp & 3)) << 16;
-      const int row = 32 * (warp & 3) + lane, half = warp >> 2;
-      bool ok = true;
-      auto cwait = [&](int bb, uint32_t par) {
-        bool mine = ok && !*fail && tc::mbar_wait(&bars[bb], par, MAX_POLLS);
-        const bool all = consumers_all(mine);
-        if (!all) { if (ok && tid == 0) record_timeout(); ok = false; *fail = 1; }
-        return ok;
-      };
-      auto zero_bad_rows = [&](unsigned char* w, int nblk) {   // swizzled W (half) tile, nblk blocks of 16K
-        for (int e = tid; e < R2 * 8 * nblk; e += CONS) {
-          const int r = e % R2, cc = e / R2;                    // 16-byte chunk cc of row r
-          if ((bad >> tok(r)) & 1ull)
-            *reinterpret_cast<uint4*>(w + (cc >> 3) * 16384 + r * 128 + (((cc & 7) ^ (r & 7)) << 4)) =
-                make_uint4(0, 0, 0, 0);
-        }
-      };
-      // ---- phase A: split each state half tile in place
-      for (int h = 0; h < NH && ok; ++h) {
-        const int s = h % 3;
-        if (!cwait(B2_FULL + s, (h / 3) & 1)) break;
-        unsigned char* w = aslot(s);
-        if (patch_w) zero_bad_rows(w, 1);
-        float x[4][8];
-#pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          const int e = tid + CONS * u;
-          const int i = e % KH, gg = e / KH;          // row i, 8-column group gg (0-7 re, 8-15 im)
-          const int plane = gg >> 3, cg = gg & 7;
-          if (src_identity) {
-            const int gi = h * KH + i, col = j0 + cg * 8;
-#pragma unroll
-            for (int jj = 0; jj < 8; ++jj) x[u][jj] = (plane == 0 && gi == col + jj) ? 1.f : 0.f;
-          } else {
-            const unsigned char* box = w + 16384 + plane * 16384 + (cg >> 2) * 8192;
-            const int cc0 = 2 * (cg & 3);
-            const float4 a = *reinterpret_cast<const float4*>(box + i * 128 + ((cc0 ^ (i & 7)) << 4));
-            const float4 bq = *reinterpret_cast<const float4*>(box + i * 128 + (((cc0 + 1) ^ (i & 7)) << 4));
-            x[u][0] = a.x; x[u][1] = a.y; x[u][2] = a.z; x[u][3] = a.w;
-            x[u][4] = bq.x; x[u][5] = bq.y; x[u][6] = bq.z; x[u][7] = bq.w;
-          }
-        }
-        tc::named_sync(1, CONS);   // every fp32 value read before the split overwrites it
-#pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          const int e = tid + CONS * u;
-          const int i = e % KH, gg = e / KH;
-          const int plane = gg >> 3, cg = gg & 7;
-          uint4 hv, lv;
-          tc::split8(x[u], hv, lv);
-          *reinterpret_cast<uint4*>(w + 16384 + mnmaj(i, plane * NB4 + cg * 8, NGW4)) = hv;
-          *reinterpret_cast<uint4*>(w + 16384 + mnmaj(i, N4 + plane * NB4 + cg * 8, NGW4)) = lv;
-          if (plane == 0 && ring_img != nullptr) {   // the real half as read: chunk c-1's end state
-            const int r = h * KH + i, j = j0 + cg * 8;
-            unsigned char* img = ring_img + (size_t)((r >> 7) * (D / RKT) + (j >> 6)) * (32 * 1024) + kmaj(r & 127, j & 63, R2);
-            *reinterpret_cast<uint4*>(img) = hv;
-            *reinterpret_cast<uint4*>(img + 16 * 1024) = lv;
-          }
-        }
-        tc::fence_proxy_async();
-        tc::named_sync(1, CONS);
-        if (tid == 0) tc::mbar_arrive(&bars[B2_SPL + s]);
-      }
-      // ---- phase T: Z -> operand (MD of the last half tile: every phase-A MMA done)
-      const int sl = (NH - 1) % 3;
-      if (ok && cwait(B2_MD + sl, ((NH - 1) / 3) & 1)) {
-        tc::fence_after_sync();
-#pragma unroll 1
-        for (int p = 0; p < 2; ++p) {
-          const int cb = NB4 * half + 32 * p;   // 32 of the 128 real columns (re 0-63 | im 64-127)
-          float z[32], zl[32];
-          tc::tmem_ld16(tZ + lane_base + cb, z);
-          tc::tmem_ld16(tZ + lane_base + cb + 16, z + 16);
-          tc::tmem_ld16(tZ + lane_base + N4 + cb, zl);
-          tc::tmem_ld16(tZ + lane_base + N4 + cb + 16, zl + 16);
-#pragma unroll
-          for (int j = 0; j < 32; ++j) z[j] += zl[j];
-#pragma unroll
-          for (int g4 = 0; g4 < 4; ++g4) {
-            uint4 hv, lv;
-            tc::split8(z + 8 * g4, hv, lv);
-            *reinterpret_cast<uint4*>(sZ + mnmaj(row, cb + 8 * g4, NGW4)) = hv;
-            *reinterpret_cast<uint4*>(sZ + mnmaj(row, N4 + cb + 8 * g4, NGW4)) = lv;
-          }
-        }
-        tc::fence_proxy_async();
-        tc::fence_before_sync();
-        tc::named_sync(1, CONS);
-        if (tid == 0) tc::mbar_arrive(&bars[B2_ZR]);
-      }
-      // ---- phase E: Cm -> operands (ZC: MN-major re | im; Re(Cm) K-major and Y at the bottom)
-      if (ok && cwait(B2_MT, 0)) {
-        tc::fence_after_sync();
-        // Cm = P1 - i P2 term by term (Re = P1r - P2i, Im = P1i + P2r), each product's two
-        // accumulator halves (hi-operand and lo-operand parts) summed; real part first
-#pragma unroll 1
-        for (int part = 0; part < 2; ++part) {
-          const int cr1 = part == 0 ? 0 : NB4, cr2 = part == 0 ? NB4 : 0;
-          const float sg = part == 0 ? -1.f : 1.f;
-#pragma unroll 1
-          for (int p = 0; p < 2; ++p) {
-            const int jc = 32 * half + 16 * p;   // 16 of the 64 columns of this part
-            float cv[16], a[16], b2[16];
-            tc::tmem_ld16(tP1 + lane_base + cr1 + jc, a);
-            tc::tmem_ld16(tP1 + lane_base + N4 + cr1 + jc, b2);
-#pragma unroll
-            for (int j = 0; j < 16; ++j) cv[j] = a[j] + b2[j];
-            tc::tmem_ld16(tP2 + lane_base + cr2 + jc, a);
-            tc::tmem_ld16(tP2 + lane_base + N4 + cr2 + jc, b2);
-#pragma unroll
-            for (int j = 0; j < 16; ++j) cv[j] += sg * (a[j] + b2[j]);
-#pragma unroll
-            for (int g2 = 0; g2 < 2; ++g2) {
-              uint4 hv, lv;
-              tc::split8(cv + 8 * g2, hv, lv);
-              *reinterpret_cast<uint4*>(sZ + mnmaj(row, cr1 + jc + 8 * g2, NGW4)) = hv;
-              *reinterpret_cast<uint4*>(sZ + mnmaj(row, N4 + cr1 + jc + 8 * g2, NGW4)) = lv;
-              if (part == 0) {
-                *reinterpret_cast<uint4*>(sAh + kmaj(row, jc + 8 * g2, R2)) = hv;
-                *reinterpret_cast<uint4*>(sAl + kmaj(row, jc + 8 * g2, R2)) = lv;
-              }
-            }
-          }
-        }
-#pragma unroll
-        for (int u = 0; u < 2; ++u) {
-          const int e = tid + CONS * u;
-          const int t = e % C2, gq = e / C2;   // 64 tokens x 8 groups of 8 columns
-          uint4 qv = make_uint4(0, 0, 0, 0);
-          if (t < nt) qv = *reinterpret_cast<const uint4*>(q + ((size_t)item * S + t0 + t) * D + j0 + gq * 8);
-          *reinterpret_cast<uint4*>(sY + kmaj(t, gq * 8, C2)) = qv;
-        }
-        tc::fence_proxy_async();
-        tc::fence_before_sync();
-        tc::named_sync(1, CONS);
-        if (tid == 0) tc::mbar_arrive(&bars[B2_CR]);
-      }
-      if (ok && cwait(B2_ME, 0)) {
-        tc::fence_after_sync();
-        float e[32];
-        tc::tmem_ld16(tE + lane_base + 32 * half, e);
-        tc::tmem_ld16(tE + lane_base + 32 * half + 16, e + 16);
-        tc::fence_before_sync();
-        tc::named_sync(1, CONS);
-        if (tid == 0) tc::mbar_arrive(&bars[B2_ER]);   // E read: the first dH may overwrite it
-        float4* Eo = reinterpret_cast<float4*>(Ews + chunk * R2 * C2 + (size_t)row * C2 + 32 * half);
-#pragma unroll
-        for (int t = 0; t < 8; ++t) atomicAdd(Eo + t, make_float4(e[4 * t], e[4 * t + 1], e[4 * t + 2], e[4 * t + 3]));
-      }
-      // ---- phase B: S_next = S + dH (thread: one row of one plane, 64 columns), TMA reduce
-      for (int kt = 0; kt < NT && ok; ++kt) {
-        const int s = (kt + 1) & 1, d = kt & 1;
-        unsigned char* w = bslot(s);
-        if (patch_w) {
-          if (!cwait(B2_FULL + s, ((NH + 2 - s) / 3 + (kt >> 1)) & 1)) break;
-          zero_bad_rows(w, 2);
-          tc::fence_proxy_async();
-          tc::named_sync(1, CONS);
-          if (tid == 0) tc::mbar_arrive(&bars[B2_SPL + s]);
-        }
-        if (!cwait(B2_DH + d, (kt >> 1) & 1)) break;
-        tc::fence_after_sync();
-        const int gi = kt * KT + row;
-#pragma unroll 1
-        for (int p = 0; p < 2; ++p) {
-          const int cb = NB4 * half + 32 * p;   // this plane's columns 32p .. 32p + 31
-          float dh[32], dl[32];
-          tc::tmem_ld16(tDH + 256 * d + lane_base + cb, dh);
-          tc::tmem_ld16(tDH + 256 * d + lane_base + cb + 16, dh + 16);
-          tc::tmem_ld16(tDH + 256 * d + lane_base + N4 + cb, dl);
-          tc::tmem_ld16(tDH + 256 * d + lane_base + N4 + cb + 16, dl + 16);
-          // the slot's W tile was read by the MMA that produced dH: the slot takes dH, as
-          // two boxes per plane (the first chunk stores I + dH instead of adding dH)
-          unsigned char* box = w + half * 32768 + p * 16384;
-#pragma unroll
-          for (int cc = 0; cc < 8; ++cc) {
-            float v4[4];
-#pragma unroll
-            for (int jj = 0; jj < 4; ++jj)
-              v4[jj] = dh[4 * cc + jj] + dl[4 * cc + jj] +
-                       ((src_identity && !half && gi == j0 + 32 * p + 4 * cc + jj) ? 1.f : 0.f);
-            *reinterpret_cast<float4*>(box + row * 128 + ((cc ^ (row & 7)) << 4)) =
-                make_float4(v4[0], v4[1], v4[2], v4[3]);
-          }
-        }
-        tc::fence_proxy_async();
-        tc::fence_before_sync();
-        tc::named_sync(1, CONS);
-        if (tid == 0) {
-          tc::mbar_arrive(&bars[B2_DF + d]);   // dH[d] may be overwritten
-#pragma unroll
-          for (int pl = 0; pl < 2; ++pl)
-#pragma unroll
-            for (int p = 0; p < 2; ++p) {
-              const CUtensorMap* tm = pl ? &tm_hi128 : &tm_hr128;
-              unsigned char* src = w + pl * 32768 + p * 16384;
-              if (src_identity) tc::tma_store_2d(tm, j0 + 32 * p, item * D + kt * KT, src);
-              else tc::tma_reduce_add_2d(tm, j0 + 32 * p, item * D + kt * KT, src);
-            }
-          tc::bulk_commit();
-          tc::bulk_wait_read<0>();                 // the store has read the slot
-          tc::mbar_arrive(&bars[B2_SR + s]);
-        }
-      }
-      if (tid == 0) {
-        tc::bulk_wait<0>();                        // all state writes performed
-        tc::fence_proxy_async_global();            // before the next chunk's loads read them
-      }
-    }
-    // chunk done: every load consumed, every MMA waited for, every store performed
-    tc::fence_before_sync();
-    __syncthreads();
-    if (*fail) break;
-    if (c + 1 < c1) {
-      if (tid == 0) {
-        for (int i = 0; i < N_BARS2; ++i) {
-          tc::mbar_inval(&bars[i]);
-          tc::mbar_init(&bars[i], 1);
-        }
-        tc::fence_mbar_init();
-      }
-      __syncthreads();
-      tc::fence_after_sync();
-    }
-  }
-  tc::fence_before_sync();
-  __syncthreads();
-  if (warp == 0) tc::tmem_dealloc(tbase, 512);
-}
-
-// One launch per group of chunks, the wide column pass: CTAs [0, D/64 * b) run the column
-// pass of chunks [c0, c1); the rest run the readouts of chunks [r0, r0 + nr) from the ring.
-__global__ void __launch_bounds__(CP2_THREADS, 1)
-cham_tc_colpass4(const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
-                 const __grid_constant__ CUtensorMap tm_hr64, const __grid_constant__ CUtensorMap tm_hi64,
-                 const __grid_constant__ CUtensorMap tm_hr128, const __grid_constant__ CUtensorMap tm_hi128,
-                 const __grid_constant__ CUtensorMap tm_q, unsigned char* __restrict__ ring, int nring, int b,
-                 const __nv_bfloat16* __restrict__ q,
-                 const unsigned char* __restrict__ Tws, float* __restrict__ Ews,
-                 const unsigned long long* __restrict__ badws, __nv_bfloat16* __restrict__ out, int S, int D, int nch,
-                 int c0, int c1, int r0, int nr, int h0) {
-  const int ncol = D / NB4, nrb = D / R2;
-  const int bid = blockIdx.x;
-  if (bid < ncol * b) {
-    colpass4_body(tm_k, tm_v, tm_hr64, tm_hi64, tm_hr128, tm_hi128, ring, nring, b, q, Tws, Ews, badws, S, D, nch,
-                  c0, c1, bid / ncol, bid % ncol, h0);
-  } else {
-    const int r = bid - ncol * b, item = r / (nrb * nr), c = r0 + (r % (nrb * nr)) / nrb, bx = r % nrb;
-    readout2_body(tm_k, tm_v, tm_q, tm_hr128, Ews, badws, out, S, D, nch, c, bx, item, 0,
-                  ring + (((size_t)(c % nring) * b + item) * D) * D * sizeof(float));
-  }
-}
-
-// ---------------------------------------------------------------------------------
 // Fused column pass (bf16 inputs): launch c makes ONE pass over the state rows that
 // finishes chunk c-1 and starts chunk c,
 //     S_c = S_{c-1} + W_{c-1} Cm_{c-1}        (stored: re -> ring[c-1], im -> ping)
@@ -3067,21 +2614,18 @@ int make_state_map(CUtensorMap* m, const float* base, int b, int D, int rows = K
 //   batched: column passes two CTAs per SM, readouts batched over up to RING chunks.
 //   fused:   one pass over the state per chunk (finish chunk c-1, start chunk c), one CTA
 //            per 64 columns, readouts batched as above.
-//   wide:    the batched schedule with one CTA per 64 columns and per SM (colpass4), while
-//            those CTAs fit one wave (b * D / 64 <= #SMs).
-// VERACE_CHAM_SCHEDULE=merged|batched|fused|wide forces one; all are tested against each other.
-enum Schedule { SCHED_MERGED, SCHED_BATCHED, SCHED_FUSED, SCHED_WIDE };
+// VERACE_CHAM_SCHEDULE=merged|batched|fused forces one; all are tested against each other.
+enum Schedule { SCHED_MERGED, SCHED_BATCHED, SCHED_FUSED };
 Schedule cham_schedule(int b, int D) {
   const char* e = getenv("VERACE_CHAM_SCHEDULE");
   if (e != nullptr) {
     if (!strcmp(e, "merged")) return SCHED_MERGED;
     if (!strcmp(e, "batched")) return SCHED_BATCHED;
     if (!strcmp(e, "fused")) return SCHED_FUSED;
-    if (!strcmp(e, "wide")) return SCHED_WIDE;
   }
   int dev = 0, sms = 148;
   if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  return (long long)b * (D / NB4) <= sms ? SCHED_WIDE : SCHED_BATCHED;
+  return (long long)b * (D / NB2 + D / R2) <= sms ? SCHED_MERGED : SCHED_BATCHED;
 }
 
 size_t tc_prep_smem() { return sizeof(float) * (PREP_DT * (R2 + 1) + 3 * R2 * (R2 + 1)); }
@@ -3157,7 +2701,7 @@ int launch_cham_tc(const void* q, const void* k, const void* v, const float* gam
                                 cudaMemcpyDeviceToDevice, st));
     return VERACE_OK;
   }
-  if (sched == SCHED_BATCHED || sched == SCHED_WIDE) {
+  if (sched == SCHED_BATCHED) {
     // Column passes two CTAs per SM over groups of RING chunks, the state in place in
     // hr / hi.  Chunk c's end state is copied into the ring by chunk c+1's column pass
     // (the last chunk's is hr), so group g's launch also runs the readouts of the chunks
@@ -3171,9 +2715,7 @@ int launch_cham_tc(const void* q, const void* k, const void* v, const float* gam
         (rc = make_state_map(&m_hr64, hr, b, D, KH)) || (rc = make_state_map(&m_hi64, hi, b, D, KH)) ||
         (rc = make_state_map(&m_hr128, hr, b, D)) || (rc = make_state_map(&m_hi128, hi, b, D)))
       return rc;
-    const bool wide = sched == SCHED_WIDE;
     VERACE_CUDA(cudaFuncSetAttribute(cham_tc_colpass2, cudaFuncAttributeMaxDynamicSharedMemorySize, CP2_SMEM));
-    VERACE_CUDA(cudaFuncSetAttribute(cham_tc_colpass4, cudaFuncAttributeMaxDynamicSharedMemorySize, CP4_SMEM));
     VERACE_CUDA(cudaFuncSetAttribute(cham_tc_readout_batch, cudaFuncAttributeMaxDynamicSharedMemorySize, RW2_SMEM));
     if (h0r != nullptr) {   // the planes are updated in place: start them as H0
       const size_t plane = (size_t)b * D * D * sizeof(float);
@@ -3184,17 +2726,10 @@ int launch_cham_tc(const void* q, const void* k, const void* v, const float* gam
     for (int cb = 0; cb < nch; cb += RING) {
       const int ce = std::min(nch, cb + RING);
       const int nr = std::max(cb - 1, 0) - r0;   // chunks [r0, cb - 1) have their end states in the ring
-      if (wide) {
-        cham_tc_colpass4<<<(D / NB4) * b + (D / R2) * nr * b, CP2_THREADS, CP4_SMEM, st>>>(
-            mk, mv, m_hr64, m_hi64, m_hr128, m_hi128, mq, ring, w.nring, b, (const __nv_bfloat16*)q, w.T, w.E, w.bad,
-            (__nv_bfloat16*)out, s, D, nch, cb, ce, r0, nr, h0r != nullptr ? 1 : 0);
-        if ((rc = check_launch("cham_tc_colpass4"))) return rc;
-      } else {
-        cham_tc_colpass2<<<(D / NB2) * b + (D / R2) * nr * b, CP2_THREADS, CP2_SMEM, st>>>(
-            mk, mv, m_hr64, m_hi64, m_hr128, m_hi128, mq, ring, w.nring, b, (const __nv_bfloat16*)q, w.T, w.E, w.bad,
-            (__nv_bfloat16*)out, s, D, nch, cb, ce, r0, nr, h0r != nullptr ? 1 : 0);
-        if ((rc = check_launch("cham_tc_colpass2"))) return rc;
-      }
+      cham_tc_colpass2<<<(D / NB2) * b + (D / R2) * nr * b, CP2_THREADS, CP2_SMEM, st>>>(
+          mk, mv, m_hr64, m_hi64, m_hr128, m_hi128, mq, ring, w.nring, b, (const __nv_bfloat16*)q, w.T, w.E, w.bad,
+          (__nv_bfloat16*)out, s, D, nch, cb, ce, r0, nr, h0r != nullptr ? 1 : 0);
+      if ((rc = check_launch("cham_tc_colpass2"))) return rc;
       r0 += nr;
     }
     // (chunks before the last read their pre-split ring images; the fp32 map serves the last)
