@@ -359,6 +359,9 @@ def run_ours(args):
     if not args.no_mcmoe:
         torch.cuda.empty_cache()
         result["mcmoe"] = run_mcmoe(args, V, dev, barrier, max_over_ranks)
+    if not args.no_model:
+        torch.cuda.empty_cache()
+        result["model"] = run_model(args, V, dev, rank, world, barrier, max_over_ranks)
     if not args.no_strong:
         torch.cuda.empty_cache()
         result["strong"] = run_strong(args, V, dev, rank, world, barrier, max_over_ranks)
@@ -374,6 +377,40 @@ def run_ours(args):
         print(json.dumps(result), flush=True)
     if world > 1:
         dist.destroy_process_group()
+
+
+def run_model(args, V, dev, rank, world, barrier, max_over_ranks):
+    """BASELINE config 2 as the whole model: VeraceV1Model (12 layers of SSSD + CHAM +
+    M-CMoE, ACDE halting at the default configuration, the LM head) prefill of the rank's
+    8 x 2048 uniform-random ids, random init (seed 0), weights in bf16, through the drop-in
+    model's forward.  Tokens/s over all ranks; the headline line times the SSSD + CHAM
+    chain of the same layers alone."""
+    import torch
+    c = CFG
+    cfg = V.VeraceV1Config(vocab_size=c["vocab"], hidden_dim=c["hidden"], num_layers=c["layers"],
+                           num_heads=c["heads"], head_dim=c["head_dim"], chams_holographic_dim=c["holo"])
+    torch.manual_seed(0)
+    model = V.VeraceV1Model(cfg).to(dev, torch.bfloat16).eval()
+    ids = rank_shard_ids(rank, c["batch"], c["seq"], c["vocab"]).to(dev)
+    with torch.no_grad():
+        for _ in range(max(1, min(args.warmup, 2))):
+            logits, depth = model(ids)
+        barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        reps = 2
+        e0.record()
+        for _ in range(reps):
+            logits, depth = model(ids)
+        e1.record()
+        barrier()
+        ms = max_over_ranks(e0.elapsed_time(e1) / reps)
+        mean_depth = float(depth.float().mean())
+    del model, logits
+    tokens = world * c["batch"] * c["seq"]
+    return {"workload": "config 2 as VeraceV1Model: 12 layers (SSSD + CHAM + M-CMoE top-8/64), ACDE at the "
+                        "default config, LM head; b=8 x s=2048 per GPU, bf16 weights, random init",
+            "ms_per_forward": ms, "model_tokens_per_s": tokens / (ms * 1e-3),
+            "mean_ponder_cost": mean_depth}
 
 
 C5 = dict(batch=256, seq=4096, hidden=4096, heads=32, head_dim=128, holo=1024, vocab=32000, micro=8)
@@ -908,6 +945,7 @@ def main():
     ap.add_argument("--no-decode", action="store_true", help="skip the config-3 decode measurement")
     ap.add_argument("--no-mcmoe", action="store_true", help="skip the M-CMoE sub-layer measurement")
     ap.add_argument("--no-long", action="store_true", help="skip the config-4 long-sequence measurement")
+    ap.add_argument("--no-model", action="store_true", help="skip the whole-model config-2 prefill measurement")
     ap.add_argument("--no-strong", action="store_true",
                     help="skip the config-5 one-layer strong-scaling measurement")
     ap.add_argument("--no-triton-bar", action="store_true",
