@@ -1380,7 +1380,8 @@ readout2_body(const CUtensorMap& tm_k, const CUtensorMap& tm_v, const CUtensorMa
         const int s = kt & 1;
         tc::mbar_expect_tx(&bars[B_TFULL + s], 32 * 1024 + 8 * 1024);
         if (pre != nullptr) {
-          tc::bulk_load(stA(s), pre + (size_t)(bx * NTR + kt) * (32 * 1024), 32 * 1024, &bars[B_TFULL + s]);
+          tc::bulk_load_hint(stA(s), pre + (size_t)(bx * NTR + kt) * (32 * 1024), 32 * 1024, &bars[B_TFULL + s],
+                             tc::policy_evict_first());
         } else {
           tc::tma_load_2d(stA(s), &tm_sr, kt * RKT, srow + i0, &bars[B_TFULL + s]);
           tc::tma_load_2d(stA(s) + 16 * 1024, &tm_sr, kt * RKT + 32, srow + i0, &bars[B_TFULL + s]);
@@ -1791,9 +1792,10 @@ colpass2_body(const CUtensorMap& tm_k, const CUtensorMap& tm_v, const CUtensorMa
       tc::mbar_expect_tx(&bars[B2_FULL + s], 16 * 1024 + (src_identity ? 0 : 16 * 1024));
       tc::tma_load_3d(w, &tm_k, h * KH, t0, item, &bars[B2_FULL + s]);
       tc::tma_load_3d(w + 8192, &tm_v, h * KH, t0, item, &bars[B2_FULL + s]);
-      if (!src_identity) {
-        tc::tma_load_2d(w + 16384, tm_sr, j0, (src_row_re + item) * D + h * KH, &bars[B2_FULL + s]);
-        tc::tma_load_2d(w + 24576, tm_si, j0, (src_row_im + item) * D + h * KH, &bars[B2_FULL + s]);
+      if (!src_identity) {   // the state stays in L2 from chunk to chunk (b D^2 x 8 B)
+        const uint64_t keep = tc::policy_evict_last();
+        tc::tma_load_2d_hint(w + 16384, tm_sr, j0, (src_row_re + item) * D + h * KH, &bars[B2_FULL + s], keep);
+        tc::tma_load_2d_hint(w + 24576, tm_si, j0, (src_row_im + item) * D + h * KH, &bars[B2_FULL + s], keep);
       }
     };
     if (warp == 9) {
@@ -1949,6 +1951,7 @@ colpass2_body(const CUtensorMap& tm_k, const CUtensorMap& tm_v, const CUtensorMa
         }
       };
       // ---- phase A: split each state half tile in place
+      const uint64_t stream_once = tc::policy_evict_first();
       for (int h = 0; h < NH && ok; ++h) {
         const int s = h % 3;
         if (!cwait(B2_FULL + s, (h / 3) & 1)) break;
@@ -1984,8 +1987,8 @@ colpass2_body(const CUtensorMap& tm_k, const CUtensorMap& tm_v, const CUtensorMa
           if (gg < 4 && ring_img != nullptr) {   // the real half as read: chunk c-1's end state
             const int r = h * KH + i, j = j0 + gg * 8;
             unsigned char* img = ring_img + (size_t)((r >> 7) * (D / RKT) + (j >> 6)) * (32 * 1024) + kmaj(r & 127, j & 63, R2);
-            *reinterpret_cast<uint4*>(img) = hv;
-            *reinterpret_cast<uint4*>(img + 16 * 1024) = lv;
+            tc::st_global_hint(img, hv, stream_once);   // read once, by the readout
+            tc::st_global_hint(img + 16 * 1024, lv, stream_once);
           }
         }
         tc::fence_proxy_async();
@@ -2107,12 +2110,13 @@ colpass2_body(const CUtensorMap& tm_k, const CUtensorMap& tm_v, const CUtensorMa
         tc::fence_proxy_async();
         tc::named_sync(1, CONS);
         if (tid == 0) {
+          const uint64_t keep = tc::policy_evict_last();
           if (src_identity) {
-            tc::tma_store_2d(tm_dr, j0, (dst_row_re + item) * D + kt * KT, w);
-            tc::tma_store_2d(tm_di, j0, (dst_row_im + item) * D + kt * KT, w + 16384);
+            tc::tma_store_2d_hint(tm_dr, j0, (dst_row_re + item) * D + kt * KT, w, keep);
+            tc::tma_store_2d_hint(tm_di, j0, (dst_row_im + item) * D + kt * KT, w + 16384, keep);
           } else {
-            tc::tma_reduce_add_2d(tm_dr, j0, (dst_row_re + item) * D + kt * KT, w);
-            tc::tma_reduce_add_2d(tm_di, j0, (dst_row_im + item) * D + kt * KT, w + 16384);
+            tc::tma_reduce_add_2d_hint(tm_dr, j0, (dst_row_re + item) * D + kt * KT, w, keep);
+            tc::tma_reduce_add_2d_hint(tm_di, j0, (dst_row_im + item) * D + kt * KT, w + 16384, keep);
           }
           tc::bulk_commit();
           tc::bulk_wait_read<0>();                 // the store has read the slot

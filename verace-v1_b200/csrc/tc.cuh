@@ -219,6 +219,26 @@ __device__ __forceinline__ void tma_load_4d(void* smem, const void* tmap, int x,
       "l"(tmap), "r"(x), "r"(y), "r"(z), "r"(w), "r"(smem_addr(mbar))
       : "memory");
 }
+// L2 eviction-priority policies (for the cache-hinted copies below): evict_last for data
+// that is read again soon (a scan's resident state), evict_first for data streamed once.
+__device__ __forceinline__ uint64_t policy_evict_last() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+__device__ __forceinline__ uint64_t policy_evict_first() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+__device__ __forceinline__ void tma_load_2d_hint(void* smem, const void* tmap, int x, int y, uint64_t* mbar,
+                                                 uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
+      " [%0], [%1, {%2, %3}], [%4], %5;" ::"r"(smem_addr(smem)),
+      "l"(tmap), "r"(x), "r"(y), "r"(smem_addr(mbar)), "l"(policy)
+      : "memory");
+}
 // Prefetch a box of a tensor into L2 (no shared memory, no completion to wait for).
 __device__ __forceinline__ void tma_prefetch_2d(const void* tmap, int x, int y) {
   asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global [%0, {%1, %2}];" ::"l"(tmap), "r"(x), "r"(y) : "memory");
@@ -233,6 +253,24 @@ __device__ __forceinline__ void tma_store_2d(const void* tmap, int x, int y, con
 __device__ __forceinline__ void tma_reduce_add_2d(const void* tmap, int x, int y, const void* smem) {
   asm volatile("cp.reduce.async.bulk.tensor.2d.global.shared::cta.add.tile.bulk_group [%0, {%1, %2}], [%3];" ::"l"(tmap),
                "r"(x), "r"(y), "r"(smem_addr(smem))
+               : "memory");
+}
+__device__ __forceinline__ void tma_store_2d_hint(const void* tmap, int x, int y, const void* smem, uint64_t policy) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group.L2::cache_hint [%0, {%1, %2}], [%3], %4;" ::"l"(
+                   tmap), "r"(x), "r"(y), "r"(smem_addr(smem)), "l"(policy)
+               : "memory");
+}
+__device__ __forceinline__ void tma_reduce_add_2d_hint(const void* tmap, int x, int y, const void* smem,
+                                                       uint64_t policy) {
+  asm volatile(
+      "cp.reduce.async.bulk.tensor.2d.global.shared::cta.add.tile.bulk_group.L2::cache_hint [%0, {%1, %2}], [%3], %4;" ::"l"(
+          tmap), "r"(x), "r"(y), "r"(smem_addr(smem)), "l"(policy)
+      : "memory");
+}
+// 16-byte global store with an L2 eviction-priority policy.
+__device__ __forceinline__ void st_global_hint(void* gmem, uint4 v, uint64_t policy) {
+  asm volatile("st.global.L2::cache_hint.v4.b32 [%0], {%1, %2, %3, %4}, %5;" ::"l"(gmem), "r"(v.x), "r"(v.y), "r"(v.z),
+               "r"(v.w), "l"(policy)
                : "memory");
 }
 // Order this thread's completed bulk (async-proxy) global writes before later async-proxy reads.
@@ -255,6 +293,14 @@ __device__ __forceinline__ void bulk_load(void* smem, const void* gmem, uint32_t
       "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
           smem_addr(smem)),
       "l"(gmem), "r"(bytes), "r"(smem_addr(mbar))
+      : "memory");
+}
+__device__ __forceinline__ void bulk_load_hint(void* smem, const void* gmem, uint32_t bytes, uint64_t* mbar,
+                                               uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;" ::"r"(
+          smem_addr(smem)),
+      "l"(gmem), "r"(bytes), "r"(smem_addr(mbar)), "l"(policy)
       : "memory");
 }
 // Named barrier over `count` threads (id 1..15; id 0 is __syncthreads).
