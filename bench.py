@@ -47,6 +47,24 @@ CFG = dict(layers=12, batch=8, seq=2048, hidden=1024, heads=8, head_dim=128, hol
 DEC = dict(batch=64, prompt=1024, steps=256, pending=8)
 
 
+def build_chain(V, dev):
+    """The config-2/3 chain: per layer RMSNorm -> SSSD -> RMSNorm -> CHAM (bf16 weights,
+    random init from seed 0), and the token embedding."""
+    import torch
+    c = CFG
+    dt = torch.bfloat16
+    torch.manual_seed(0)
+    layers = []
+    for _ in range(c["layers"]):
+        layers.append(torch.nn.ModuleDict(dict(
+            sssd_norm=torch.nn.RMSNorm(c["hidden"], eps=1e-6),
+            sssd=V.SSSDAttention(c["hidden"], c["heads"], c["head_dim"], 256),
+            cham_norm=torch.nn.RMSNorm(c["hidden"], eps=1e-6),
+            cham=V.ContinuousHolographicMemory(c["hidden"], c["holo"]))).to(dev, dt).eval())
+    embed = torch.nn.Embedding(c["vocab"], c["hidden"]).to(dev, dt)
+    return layers, embed
+
+
 def _load_package():
     import importlib.util
     if "verace_v1_b200" in sys.modules:
@@ -189,16 +207,7 @@ def run_ours(args):
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
 
     c = CFG
-    dt = torch.bfloat16
-    torch.manual_seed(0)
-    layers = []
-    for _ in range(c["layers"]):
-        layers.append(torch.nn.ModuleDict(dict(
-            sssd_norm=torch.nn.RMSNorm(c["hidden"], eps=1e-6),
-            sssd=V.SSSDAttention(c["hidden"], c["heads"], c["head_dim"], 256),
-            cham_norm=torch.nn.RMSNorm(c["hidden"], eps=1e-6),
-            cham=V.ContinuousHolographicMemory(c["hidden"], c["holo"]))).to(dev, dt).eval())
-    embed = torch.nn.Embedding(c["vocab"], c["hidden"]).to(dev, dt)
+    layers, embed = build_chain(V, dev)
     ids = rank_shard_ids(rank, c["batch"], c["seq"], c["vocab"]).to(dev)
     with torch.no_grad():
         x = embed(ids).contiguous()
@@ -903,6 +912,12 @@ def run_only(args):
         q, k, v = (nrm(torch.randn(b, D, generator=g), dim=-1).to(dev, torch.bfloat16) for _ in range(3))
         gam = (0.1 * torch.sigmoid(torch.randn(b, generator=g))).to(dev)
         fn = lambda: st.step_cham(0, q, k, v, gam)
+    elif args.only == "decode_step":   # the whole config-3 decode leg (12 layers, CUDA graph per step)
+        V = sys.modules["verace_v1_b200"]
+        layers, embed = build_chain(V, dev)
+        res = run_decode(args, layers, embed, V, dev, 0, torch.cuda.synchronize, lambda x: x)
+        print(json.dumps({"only": args.only, **res}), flush=True)
+        return
     elif args.only == "retract":
         V = sys.modules["verace_v1_b200"]
         D = c["holo"]
@@ -950,7 +965,7 @@ def main():
                     help="skip the config-5 one-layer strong-scaling measurement")
     ap.add_argument("--no-triton-bar", action="store_true",
                     help="skip timing the reference's Triton decode path (one layer, config 3)")
-    ap.add_argument("--only", choices=["cham", "sssd", "decode", "mcmoe", "retract"], default=None,
+    ap.add_argument("--only", choices=["cham", "sssd", "decode", "decode_step", "mcmoe", "retract"], default=None,
                     help="time one scan entry point alone (kernel-level case for profiling)")
     ap.add_argument("--batch", type=int, default=None)
     ap.add_argument("--seq", type=int, default=None)

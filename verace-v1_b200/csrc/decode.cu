@@ -78,6 +78,21 @@ __device__ __forceinline__ float ld1(const void* p, size_t i) {
   return to_f32(static_cast<const T*>(p)[i]);
 }
 
+// Elements i .. i + 3 as floats in one 8-byte (16-bit types) or 16-byte (fp32) load: i a
+// multiple of 4 and the base aligned to four elements.
+template <typename T>
+__device__ __forceinline__ void ld4(const void* p, size_t i, float (&x)[4]) {
+  if constexpr (sizeof(T) == 4) {
+    const float4 v = *reinterpret_cast<const float4*>(static_cast<const float*>(p) + i);
+    x[0] = v.x; x[1] = v.y; x[2] = v.z; x[3] = v.w;
+  } else {
+    const uint2 v = *reinterpret_cast<const uint2*>(static_cast<const T*>(p) + i);
+    const T* e = reinterpret_cast<const T*>(&v);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) x[j] = to_f32(e[j]);
+  }
+}
+
 __device__ __forceinline__ float warp_sum(float x) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) x += __shfl_xor_sync(0xffffffffu, x, o);
@@ -560,22 +575,84 @@ struct LazyArgs {
   float* bq;                   // [b][LP_MAX][2]: Re(B_j0 q), Re(B_j1 q)
   float* part;                 // [b][D/32][D] readout partials
   float* cqp;                  // [b][D/32][4] per stripe: kᵀH q (re, im), vᵀH q (re, im)
-  unsigned int* cnt;           // [b]
-  int b, D, P;
+  int* pcold;                  // [b] the pending counts as this step found them
+  int b, D, P, nst;            // nst: column stripes of lazy_cham_kernel
 };
+
+// The 2x2 complex factor N of a CHAM Cayley step for gate g (c = g / 2) from the Gram
+// entries kk, vv, kv:  N = 2c / det [[-c vv, c kv + i], [c kv + i, -c kk]],
+// det = 1 + c² (kk vv - kv²) - 2 i c kv; `ok` is false when k, v, the gate or N is not
+// finite, and such a step is the identity (cham_memory.py:54-96).  The stripe kernel and
+// the readout kernel of a step both form N here, from the same Gram sums.
+struct ChamN {
+  float n00r, n00i, n01r, n01i, n11r, n11i;
+  bool ok;
+};
+__device__ __forceinline__ ChamN cham_factor(float kk, float vv, float kv, float g, bool fin) {
+  ChamN n;
+  const float cc = 0.5f * g;
+  const float dr = 1.f + cc * cc * (kk * vv - kv * kv);
+  const float di = -2.f * cc * kv;
+  const float m2 = dr * dr + di * di;
+  const float fr = 2.f * cc * dr / m2;
+  const float fi = -2.f * cc * di / m2;
+  n.n00r = fr * (-cc * vv); n.n00i = fi * (-cc * vv);
+  n.n11r = fr * (-cc * kk); n.n11i = fi * (-cc * kk);
+  n.n01r = fr * (cc * kv) - fi; n.n01i = fr + fi * (cc * kv);
+  n.ok = fin && isfinite(g) && isfinite(n.n00r) && isfinite(n.n00i) && isfinite(n.n01r) && isfinite(n.n01i) &&
+         isfinite(n.n11r) && isfinite(n.n11i);
+  return n;
+}
+
+// k, v (and the stripe's q columns when qs != nullptr) of one item into shared memory,
+// with the Gram sums kk, vv, kv, qq (per thread; block_sum4 finishes them) and the
+// finiteness of k, v.  Four elements per load when the bases allow it; every kernel that
+// forms a step's N calls this with the same thread count, so their sums agree bitwise.
+template <typename T>
+__device__ __forceinline__ void load_kvq(const LazyArgs& A, size_t voff, int D, float* ks, float* vs, float* qs,
+                                         int cs0, int W, float (&dots)[4], bool& fin) {
+  const int tid = threadIdx.x;
+  const bool vec4 = ((reinterpret_cast<uintptr_t>(A.ck) | reinterpret_cast<uintptr_t>(A.cv) |
+                      reinterpret_cast<uintptr_t>(A.cq)) & (4 * sizeof(T) - 1)) == 0;
+  if (vec4) {
+    for (int i = 4 * tid; i < D; i += 4 * DT) {
+      float kx[4], vx[4], qx[4];
+      ld4<T>(A.ck, voff + i, kx);
+      ld4<T>(A.cv, voff + i, vx);
+      ld4<T>(A.cq, voff + i, qx);
+      *reinterpret_cast<float4*>(ks + i) = make_float4(kx[0], kx[1], kx[2], kx[3]);
+      *reinterpret_cast<float4*>(vs + i) = make_float4(vx[0], vx[1], vx[2], vx[3]);
+      if (qs != nullptr && i >= cs0 && i < cs0 + W)
+        *reinterpret_cast<float4*>(qs + i - cs0) = make_float4(qx[0], qx[1], qx[2], qx[3]);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        dots[0] += kx[j] * kx[j]; dots[1] += vx[j] * vx[j]; dots[2] += kx[j] * vx[j]; dots[3] += qx[j] * qx[j];
+        fin = fin && isfinite(kx[j]) && isfinite(vx[j]);
+      }
+    }
+  } else {
+    for (int i = tid; i < D; i += DT) {
+      const float kx = ld1<T>(A.ck, voff + i), vx = ld1<T>(A.cv, voff + i), qx = ld1<T>(A.cq, voff + i);
+      ks[i] = kx; vs[i] = vx;
+      if (qs != nullptr && i >= cs0 && i < cs0 + W) qs[i - cs0] = qx;
+      dots[0] += kx * kx; dots[1] += vx * vx; dots[2] += kx * vx; dots[3] += qx * qx;
+      fin = fin && isfinite(kx) && isfinite(vx);
+    }
+  }
+}
 
 // The dot products between this step's k, v, q and the pending factors: one CTA per
 // (item, factor slot) (slots past the item's count return at once), each thread a few
 // rows of the six contiguous vectors, then a block reduction.  The slot-0 CTA of each item
-// also zeroes the item's stripe counter for the lazy_cham_kernel launch that follows.
+// also keeps the item's pending count for lazy_out_kernel (which rewrites the count).
 template <typename T>
 __global__ void __launch_bounds__(DT) lazy_pre_kernel(LazyArgs A) {
   __shared__ float red[DT / 32][6];
   const int D = A.D, P = A.P;
   const int item = blockIdx.x / P, j = blockIdx.x % P;
   const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
-  if (j == 0 && tid == 0) A.cnt[item] = 0u;
   const int p = A.pcount[item];
+  if (j == 0 && tid == 0) A.pcold[item] = p;
   if (p >= P || j >= p) return;       // a folding step needs none of them
   const size_t voff = (size_t)item * D;
   const float* a0 = A.pa + ((size_t)item * P + j) * 2 * D;
@@ -605,41 +682,53 @@ __global__ void __launch_bounds__(DT) lazy_pre_kernel(LazyArgs A) {
   }
 }
 
-// The stripe streams through NSTG shared-memory stages of 64 rows (re box 8 KB | im box
-// 8 KB, 128-byte rows, no swizzle), loaded by TMA: thread 0 keeps every stage in flight,
-// so the read pass is not limited by the loads a thread can hold in registers.  A
-// folding step updates each stage in place and TMA-stores it back.
-constexpr int LROWS = 64;                    // rows per stage
+// The stripe (W = 64 columns when D is a multiple of 64, else 32) streams through NSTG
+// shared-memory stages of 16 KB (ROWS rows: re box | im box, W floats a row, no swizzle),
+// loaded by TMA: thread 0 keeps every stage in flight, so the read pass is not limited by
+// the loads a thread can hold in registers.  Each thread takes two rows of four columns
+// per stage.  A folding step updates each stage in place and TMA-stores it back.  The
+// wider stripe halves the CTAs, and with them the per-CTA set-up (k, v, q and the pending
+// factors' columns) and reductions, for the same bytes streamed.
 constexpr int NSTG = 5;                      // stages
-constexpr int LSTAGE = 2 * LROWS * CWD * 4;  // 16 KB
-// dynamic smem: stages | A rows of the stage (fold steps) [LP_MAX][2][LROWS], two buffers of
-// [LP_MAX / 2][2][LROWS] when P <= LP_MAX / 2 | ks [D] | vs [D] | barriers
-constexpr int LAS_OFF = NSTG * LSTAGE;
-constexpr int LKS_OFF = LAS_OFF + LP_MAX * 2 * LROWS * 4;
-size_t lazy_smem(int D) { return LKS_OFF + 2 * (size_t)D * 4 + 8 * NSTG + 16; }
+template <int W>
+struct LazyGeom {
+  static constexpr int TPR = W / 4;                 // threads per row
+  static constexpr int RPG = DT / TPR;              // rows per row group
+  static constexpr int ROWS = 2 * RPG;              // rows per stage
+  static constexpr int STAGE = 2 * ROWS * W * 4;    // bytes per stage (16 KB)
+  // dynamic smem: stages | A rows of the stage (fold steps) [LP_MAX][2][ROWS], two buffers
+  // of [LP_MAX / 2][2][ROWS] when P <= LP_MAX / 2 | pending B over the stripe [P][4][W] |
+  // ks [D] | vs [D] | barriers
+  static constexpr int AS_OFF = NSTG * STAGE;
+  static constexpr int PBS_OFF = AS_OFF + LP_MAX * 2 * ROWS * 4;
+  __host__ __device__ static size_t ks_off(int P) { return PBS_OFF + (size_t)P * 4 * W * 4; }
+  static size_t smem(int D, int P) { return ks_off(P) + 2 * (size_t)D * 4 + 8 * NSTG + 16; }
+};
+static_assert(LazyGeom<32>::STAGE == 16384 && LazyGeom<64>::STAGE == 16384, "16 KB stages");
 constexpr uint32_t LPOLLS = 1u << 22;
 
-template <typename T>
+template <typename T, int W>
 __global__ void __launch_bounds__(DT, 2)
 lazy_cham_kernel(LazyArgs A, const __grid_constant__ CUtensorMap tm_r, const __grid_constant__ CUtensorMap tm_i) {
+  using G = LazyGeom<W>;
+  constexpr int TPR = G::TPR, RPG = G::RPG, LROWS = G::ROWS, LSTAGE = G::STAGE;
   extern __shared__ __align__(128) unsigned char lsm[];
-  float* as = reinterpret_cast<float*>(lsm + LAS_OFF);   // [j][kv][row of the stage]
-  float* ks = reinterpret_cast<float*>(lsm + LKS_OFF);
+  float* as = reinterpret_cast<float*>(lsm + G::AS_OFF);   // [j][kv][row of the stage]
+  float* pbs = reinterpret_cast<float*>(lsm + G::PBS_OFF);  // pending B_j over the stripe: [j][4][W]
+  float* ks = reinterpret_cast<float*>(lsm + G::ks_off(A.P));
   float* vs = ks + A.D;
   uint64_t* full = reinterpret_cast<uint64_t*>(vs + A.D);   // TMA landed (8-byte aligned: D % 32 == 0)
-  __shared__ float qs[CWD];
-  __shared__ float red[8][CWD][4];
-  __shared__ float pbs[LP_MAX][4][CWD];   // pending B_j over this stripe's columns
+  __shared__ __align__(16) float qs[W];
+  __shared__ float red[8][W][4];
   __shared__ float gs[LP_MAX][4];
   __shared__ float dsc[8][4];
   __shared__ float cq4[8][4];
-  __shared__ int last_flag;
   const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
   const int D = A.D, P = A.P;
-  const int nst = D / CWD;
+  const int nst = D / W;
   const int item = blockIdx.x / nst, stripe = blockIdx.x % nst;
   const int c8 = lane % TPR;
-  const int rp = threadIdx.x / TPR;       // rows rp and rp + 32 of each stage
+  const int rp = threadIdx.x / TPR;       // rows rp and rp + RPG of each stage
   const int p = A.pcount[item];
   const bool fold = p >= P;               // fold the P pending factors into S this step
   const int np = fold ? P : p;            // pending factors read by this step
@@ -649,8 +738,8 @@ lazy_cham_kernel(LazyArgs A, const __grid_constant__ CUtensorMap tm_r, const __g
   auto issue = [&](int rb) {
     const int s = rb % NSTG;
     tc::mbar_expect_tx(&full[s], LSTAGE);
-    tc::tma_load_2d(stage(s), &tm_r, stripe * CWD, item * D + rb * LROWS, &full[s]);
-    tc::tma_load_2d(stage(s) + LROWS * CWD, &tm_i, stripe * CWD, item * D + rb * LROWS, &full[s]);
+    tc::tma_load_2d(stage(s), &tm_r, stripe * W, item * D + rb * LROWS, &full[s]);
+    tc::tma_load_2d(stage(s) + LROWS * W, &tm_i, stripe * W, item * D + rb * LROWS, &full[s]);
   };
   if (tid == 0) {
     for (int s = 0; s < NSTG; ++s) tc::mbar_init(&full[s], 1);
@@ -663,19 +752,31 @@ lazy_cham_kernel(LazyArgs A, const __grid_constant__ CUtensorMap tm_r, const __g
   float* pb = A.pb + (size_t)item * P * 4 * D;
   float dots[4] = {0.f, 0.f, 0.f, 0.f};
   bool fin = true;
-  const int cs0 = stripe * CWD;
-  for (int i = tid; i < D; i += DT) {
-    const float kx = ld1<T>(A.ck, voff + i), vx = ld1<T>(A.cv, voff + i), qx = ld1<T>(A.cq, voff + i);
-    ks[i] = kx; vs[i] = vx;
-    if (i >= cs0 && i < cs0 + CWD) qs[i - cs0] = qx;
-    dots[0] += kx * kx; dots[1] += vx * vx; dots[2] += kx * vx; dots[3] += qx * qx;
-    fin = fin && isfinite(kx) && isfinite(vx);
+  const int cs0 = stripe * W;
+  // The small per-step inputs, all requested before any is used: the pending factors' B
+  // rows over this stripe (float4s) and their dot products with this step's k, v (gs),
+  // then k, v, q.
+  constexpr int PBV = (LP_MAX * W + DT - 1) / DT;   // float4s of B per thread, at most
+  float4 pbv[PBV];
+#pragma unroll
+  for (int u = 0; u < PBV; ++u) {
+    const int e = tid + DT * u;   // W float4s per factor: 4 rows x W / 4
+    if (e < np * W) {
+      const int j = e / W, rr = (e / (W / 4)) % 4, c4 = e % (W / 4);
+      pbv[u] = *reinterpret_cast<const float4*>(pb + ((size_t)j * 4 + rr) * D + cs0 + 4 * c4);
+    }
   }
-  for (int e = tid; e < np * 4 * CWD; e += DT) {
-    const int j = e / (4 * CWD), rr = (e / CWD) % 4, c = e % CWD;
-    pbs[j][rr][c] = pb[((size_t)j * 4 + rr) * D + cs0 + c];
+  const float gv = (!fold && tid < 4 * p) ? A.g[((size_t)item * LP_MAX + tid / 4) * 4 + tid % 4] : 0.f;
+  load_kvq<T>(A, voff, D, ks, vs, qs, cs0, W, dots, fin);
+#pragma unroll
+  for (int u = 0; u < PBV; ++u) {
+    const int e = tid + DT * u;
+    if (e < np * W) {
+      const int j = e / W, rr = (e / (W / 4)) % 4, c4 = e % (W / 4);
+      *reinterpret_cast<float4*>(pbs + (j * 4 + rr) * W + 4 * c4) = pbv[u];
+    }
   }
-  if (!fold && tid < 4 * p) gs[tid / 4][tid % 4] = A.g[((size_t)item * LP_MAX + tid / 4) * 4 + tid % 4];
+  if (!fold && tid < 4 * p) gs[tid / 4][tid % 4] = gv;
   // Fold steps with P <= LP_MAX / 2 double-buffer the A rows: stage rb + 1's rows are
   // loaded into registers during stage rb and stored to the other buffer after its
   // compute, so no stage waits for them.
@@ -703,6 +804,9 @@ lazy_cham_kernel(LazyArgs A, const __grid_constant__ CUtensorMap tm_r, const __g
     if (NRB > 1) a_fetch(1);
   }
   block_sum4(dots, fin, dsc);      // also makes ks/vs/qs/pbs/gs, stage 0's A rows and the barrier inits visible
+  // every read of the pending count is behind us: lazy_out_kernel may start (it waits for
+  // this grid's completion before it reads what the stripes write)
+  asm volatile("griddepcontrol.launch_dependents;");
 
   // ---- one pass: column sums kᵀS, vᵀS and the readout partials S_re q, folding first
   float acc[4][4];
@@ -718,13 +822,13 @@ lazy_cham_kernel(LazyArgs A, const __grid_constant__ CUtensorMap tm_r, const __g
     // (a wait that gives up still reaches this stage's barrier, which votes on it)
     const bool got = tc::mbar_wait(&full[s], (rb / NSTG) & 1, LPOLLS);
     float* sr = stage(s);
-    float* si = sr + LROWS * CWD;
+    float* si = sr + LROWS * W;
     float4 xr2[2], xi2[2];
 #pragma unroll
     for (int h = 0; h < 2; ++h) {
-      const int i = rp + 32 * h;
-      xr2[h] = *reinterpret_cast<const float4*>(sr + i * CWD + 4 * c8);
-      xi2[h] = *reinterpret_cast<const float4*>(si + i * CWD + 4 * c8);
+      const int i = rp + RPG * h;
+      xr2[h] = *reinterpret_cast<const float4*>(sr + i * W + 4 * c8);
+      xi2[h] = *reinterpret_cast<const float4*>(si + i * W + 4 * c8);
     }
     if (fold) {   // S += sum_j A_j B_j; each factor's four columns of B serve both rows
       const float* asb = as;
@@ -737,13 +841,13 @@ lazy_cham_kernel(LazyArgs A, const __grid_constant__ CUtensorMap tm_r, const __g
       }
 #pragma unroll 2
       for (int j = 0; j < P; ++j) {
-        const float4 b0r = *reinterpret_cast<const float4*>(&pbs[j][0][4 * c8]);
-        const float4 b0i = *reinterpret_cast<const float4*>(&pbs[j][1][4 * c8]);
-        const float4 b1r = *reinterpret_cast<const float4*>(&pbs[j][2][4 * c8]);
-        const float4 b1i = *reinterpret_cast<const float4*>(&pbs[j][3][4 * c8]);
+        const float4 b0r = *reinterpret_cast<const float4*>(pbs + (j * 4 + 0) * W + 4 * c8);
+        const float4 b0i = *reinterpret_cast<const float4*>(pbs + (j * 4 + 1) * W + 4 * c8);
+        const float4 b1r = *reinterpret_cast<const float4*>(pbs + (j * 4 + 2) * W + 4 * c8);
+        const float4 b1i = *reinterpret_cast<const float4*>(pbs + (j * 4 + 3) * W + 4 * c8);
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
-          const int i = rp + 32 * h;
+          const int i = rp + RPG * h;
           const float a0 = asb[(2 * j) * LROWS + i], a1 = asb[(2 * j + 1) * LROWS + i];
 #pragma unroll
           for (int jj = 0; jj < 4; ++jj) {
@@ -754,9 +858,9 @@ lazy_cham_kernel(LazyArgs A, const __grid_constant__ CUtensorMap tm_r, const __g
       }
 #pragma unroll
       for (int h = 0; h < 2; ++h) {
-        const int i = rp + 32 * h;
-        *reinterpret_cast<float4*>(sr + i * CWD + 4 * c8) = xr2[h];
-        *reinterpret_cast<float4*>(si + i * CWD + 4 * c8) = xi2[h];
+        const int i = rp + RPG * h;
+        *reinterpret_cast<float4*>(sr + i * W + 4 * c8) = xr2[h];
+        *reinterpret_cast<float4*>(si + i * W + 4 * c8) = xi2[h];
       }
       if (adbl && rb + 1 < NRB) {   // the other buffer was last read in stage rb - 1
         a_put(rb + 1);
@@ -765,7 +869,7 @@ lazy_cham_kernel(LazyArgs A, const __grid_constant__ CUtensorMap tm_r, const __g
     }
 #pragma unroll
     for (int h = 0; h < 2; ++h) {
-      const int i = rp + 32 * h, r = rb * LROWS + i;
+      const int i = rp + RPG * h, r = rb * LROWS + i;
       const float4 xr = xr2[h], xi = xi2[h];
       const float kr = ks[r], vr = vs[r];
       float o = 0.f;
@@ -789,8 +893,8 @@ lazy_cham_kernel(LazyArgs A, const __grid_constant__ CUtensorMap tm_r, const __g
       if (fold) {
         // stage rb leaves by TMA store; the stage stored one step earlier, whose store has
         // had a stage's compute to read it, takes the next load
-        tc::tma_store_2d(&tm_r, stripe * CWD, item * D + rb * LROWS, sr);
-        tc::tma_store_2d(&tm_i, stripe * CWD, item * D + rb * LROWS, si);
+        tc::tma_store_2d(&tm_r, stripe * W, item * D + rb * LROWS, sr);
+        tc::tma_store_2d(&tm_i, stripe * W, item * D + rb * LROWS, si);
         tc::bulk_commit();
         if (rb >= 1) {
           tc::bulk_wait_read<1>();
@@ -836,22 +940,9 @@ lazy_cham_kernel(LazyArgs A, const __grid_constant__ CUtensorMap tm_r, const __g
       for (int j = 0; j < 4; ++j) red[w][4 * lane + j][qn] = acc[qn][j];
   }
   __syncthreads();
-  const float kk = dots[0], vv = dots[1], kv = dots[2];
-  const float gm = A.gamma[item];
-  const float cc = 0.5f * gm;
-  const float dr = 1.f + cc * cc * (kk * vv - kv * kv);
-  const float di = -2.f * cc * kv;
-  const float m2 = dr * dr + di * di;
-  const float fr = 2.f * cc * dr / m2;
-  const float fi = -2.f * cc * di / m2;
-  const float n00r = fr * (-cc * vv), n00i = fi * (-cc * vv);
-  const float n11r = fr * (-cc * kk), n11i = fi * (-cc * kk);
-  const float n01r = fr * (cc * kv) - fi, n01i = fr + fi * (cc * kv);
-  // non-finite k, v, gate or factor: identity (cham_memory.py:54-96)
-  const bool ok = fin && isfinite(gm) && isfinite(n00r) && isfinite(n00i) && isfinite(n01r) && isfinite(n01i) &&
-                  isfinite(n11r) && isfinite(n11i);
+  const ChamN N = cham_factor(dots[0], dots[1], dots[2], A.gamma[item], fin);
   float cqv[4] = {0.f, 0.f, 0.f, 0.f};
-  if (tid < CWD) {
+  if (tid < W) {
     const int c = tid;
     float t[4];
 #pragma unroll
@@ -864,93 +955,125 @@ lazy_cham_kernel(LazyArgs A, const __grid_constant__ CUtensorMap tm_r, const __g
     // the pending factors' share of kᵀH and vᵀH (none after a fold)
     for (int j = 0; j < (fold ? 0 : p); ++j) {
       const float gkk = gs[j][0], gkv = gs[j][1], gvk = gs[j][2], gvv = gs[j][3];
-      t[0] += gkk * pbs[j][0][c] + gkv * pbs[j][2][c];
-      t[1] += gkk * pbs[j][1][c] + gkv * pbs[j][3][c];
-      t[2] += gvk * pbs[j][0][c] + gvv * pbs[j][2][c];
-      t[3] += gvk * pbs[j][1][c] + gvv * pbs[j][3][c];
+      const float* pj = pbs + j * 4 * W + c;
+      t[0] += gkk * pj[0] + gkv * pj[2 * W];
+      t[1] += gkk * pj[W] + gkv * pj[3 * W];
+      t[2] += gvk * pj[0] + gvv * pj[2 * W];
+      t[3] += gvk * pj[W] + gvv * pj[3 * W];
     }
     const float qc = qs[c];
     cqv[0] = t[0] * qc; cqv[1] = t[1] * qc; cqv[2] = t[2] * qc; cqv[3] = t[3] * qc;
     float b0r = 0.f, b0i = 0.f, b1r = 0.f, b1i = 0.f;
-    if (ok) {
-      b0r = n00r * t[0] - n00i * t[1] + n01r * t[2] - n01i * t[3];
-      b0i = n00r * t[1] + n00i * t[0] + n01r * t[3] + n01i * t[2];
-      b1r = n01r * t[0] - n01i * t[1] + n11r * t[2] - n11i * t[3];
-      b1i = n01r * t[1] + n01i * t[0] + n11r * t[3] + n11i * t[2];
+    if (N.ok) {
+      b0r = N.n00r * t[0] - N.n00i * t[1] + N.n01r * t[2] - N.n01i * t[3];
+      b0i = N.n00r * t[1] + N.n00i * t[0] + N.n01r * t[3] + N.n01i * t[2];
+      b1r = N.n01r * t[0] - N.n01i * t[1] + N.n11r * t[2] - N.n11i * t[3];
+      b1i = N.n01r * t[1] + N.n01i * t[0] + N.n11r * t[3] + N.n11i * t[2];
     }
     float* nb = pb + (size_t)snew * 4 * D + cs0 + c;
     nb[0] = b0r; nb[D] = b0i; nb[2 * D] = b1r; nb[3 * D] = b1i;
   }
-  if (w == 0) {   // this stripe's share of kᵀH q and vᵀH q
+  if (w < W / 32) {   // this stripe's share of kᵀH q and vᵀH q: one partial per column warp
 #pragma unroll
     for (int j = 0; j < 4; ++j) cqv[j] = warp_sum(cqv[j]);
     if (lane == 0) {
-      float* dst = A.cqp + ((size_t)item * nst + stripe) * 4;
-      dst[0] = cqv[0]; dst[1] = cqv[1]; dst[2] = cqv[2]; dst[3] = cqv[3];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) cq4[w][j] = cqv[j];
     }
   }
-  // publish: CTA barrier, one release fence and the stripe count
   __syncthreads();
   if (tid == 0) {
-    __threadfence();
-    const unsigned int prev = atomicAdd(&A.cnt[item], 1u);
-    last_flag = (prev == (unsigned int)(nst - 1));
-    if (last_flag) __threadfence();
-  }
-  __syncthreads();
-  if (!last_flag) return;
-  // ---- last CTA of the item: the readout and the new factor's A part
-  {
-    float x[4] = {0.f, 0.f, 0.f, 0.f};
-    for (int st = tid; st < nst; st += DT) {
-      const float* src = A.cqp + ((size_t)item * nst + st) * 4;
+    float* dst = A.cqp + ((size_t)item * nst + stripe) * 4;
 #pragma unroll
-      for (int j = 0; j < 4; ++j) x[j] += __ldcg(src + j);
-    }
-    bool dummy = true;
-    block_sum4(x, dummy, dsc);
-    if (tid == 0) {
-      // Re of the new factor times q: B0'q = N00 (kᵀHq) + N01 (vᵀHq), B1'q = N01 (kᵀHq) + N11 (vᵀHq)
-      cq4[0][0] = ok ? n00r * x[0] - n00i * x[1] + n01r * x[2] - n01i * x[3] : 0.f;
-      cq4[0][1] = ok ? n01r * x[0] - n01i * x[1] + n11r * x[2] - n11i * x[3] : 0.f;
-    }
-    __syncthreads();
-  }
-  const float u0 = cq4[0][0], u1 = cq4[0][1];
-  const float* pbq = A.bq + (size_t)item * LP_MAX * 2;
-  const float* pb0 = A.part + (size_t)item * nst * D;
-  T* y = static_cast<T*>(A.cout) + voff;
-  const int npend = fold ? 0 : p;
-  // rows i .. i + 3 per thread: one 16-byte load per stripe, 16 stripes in flight (the
-  // stripes summed in order)
-  for (int i = 4 * tid; i < D; i += 4 * DT) {
-    float sacc[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll 16
-    for (int st = 0; st < nst; ++st) {
-      const float4 x = __ldcg(reinterpret_cast<const float4*>(pb0 + (size_t)st * D + i));
-      sacc[0] += x.x; sacc[1] += x.y; sacc[2] += x.z; sacc[3] += x.w;
-    }
-    for (int j = 0; j < npend; ++j) {
-      const float4 a0 = *reinterpret_cast<const float4*>(pa + (size_t)j * 2 * D + i);
-      const float4 a1 = *reinterpret_cast<const float4*>(pa + ((size_t)j * 2 + 1) * D + i);
-      const float q0 = __ldcg(pbq + 2 * j), q1 = __ldcg(pbq + 2 * j + 1);
+    for (int j = 0; j < 4; ++j) {
+      float x = 0.f;
 #pragma unroll
-      for (int e = 0; e < 4; ++e) sacc[e] += compc(a0, e) * q0 + compc(a1, e) * q1;
+      for (int ww = 0; ww < W / 32; ++ww) x += cq4[ww][j];
+      dst[j] = x;
+    }
+  }
+}
+
+// The step's readout, one CTA per (item, 256 rows), launched as a programmatic dependent of
+// lazy_cham_kernel: the part that does not read the stripes' results (k, v and the step's
+// factor N) runs while the stripe kernel's last CTAs finish, then griddepcontrol.wait
+// (the stripe kernel complete and its writes visible) and
+//     y = sum over stripes of the S_re q partials (in stripe order)
+//       + sum_j (k_j Re(B_j0 q) + v_j Re(B_j1 q))          (pending factors)
+//       + k Re(B0' q) + v Re(B1' q)                          (this step's factor)
+// with Re(B' q) = Re(N [kᵀHq; vᵀHq]) from the stripes' shares; then this step's factor's
+// A part (k, v; zero for an identity step) over the CTA's rows, and the item's pending
+// count.  The pending count is read from the copy lazy_pre_kernel took (pcold), because
+// the count itself is rewritten here.
+template <typename T>
+__global__ void __launch_bounds__(DT) lazy_out_kernel(LazyArgs A) {
+  extern __shared__ __align__(16) float lso[];   // ks [D] | vs [D]
+  __shared__ float dsc[8][4], dsc2[8][4];
+  const int item = blockIdx.y, tid = threadIdx.x, r = blockIdx.x * DT + tid;
+  const int D = A.D, P = A.P, nst = A.nst;
+  float* ks = lso;
+  float* vs = lso + D;
+  const size_t voff = (size_t)item * D;
+  const int p = A.pcold[item];
+  const bool fold = p >= P;
+  const int npend = fold ? 0 : p, snew = fold ? 0 : p;
+  float dots[4] = {0.f, 0.f, 0.f, 0.f};
+  bool fin = true;
+  load_kvq<T>(A, voff, D, ks, vs, nullptr, 0, 0, dots, fin);
+  block_sum4(dots, fin, dsc);     // also makes ks, vs visible
+  const ChamN N = cham_factor(dots[0], dots[1], dots[2], A.gamma[item], fin);
+  float bq[LP_MAX][2];
+#pragma unroll
+  for (int j = 0; j < LP_MAX; ++j)   // (written by lazy_pre_kernel, complete before the stripe kernel began)
+    if (j < npend) {
+      bq[j][0] = __ldcg(A.bq + ((size_t)item * LP_MAX + j) * 2);
+      bq[j][1] = __ldcg(A.bq + ((size_t)item * LP_MAX + j) * 2 + 1);
+    }
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  float x[4] = {0.f, 0.f, 0.f, 0.f};
+  for (int st = tid; st < nst; st += DT) {
+    const float* src = A.cqp + ((size_t)item * nst + st) * 4;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) x[j] = __ldcg(src + j);
+  }
+  float sacc = 0.f;
+  const float* pa = A.pa + (size_t)item * P * 2 * D;
+  if (r < D) {   // the row's pending factor rows and stripe partials (in order), loads in flight together
+    float av[LP_MAX][2];
+#pragma unroll
+    for (int j = 0; j < LP_MAX; ++j)
+      if (j < npend) {
+        av[j][0] = pa[(size_t)j * 2 * D + r];
+        av[j][1] = pa[((size_t)j * 2 + 1) * D + r];
+      }
+    const float* pb0 = A.part + (size_t)item * nst * D + r;
+    for (int s0 = 0; s0 < nst; s0 += 16) {
+      float pv[16];
+#pragma unroll
+      for (int st = 0; st < 16; ++st)
+        if (s0 + st < nst) pv[st] = __ldcg(pb0 + (size_t)(s0 + st) * D);
+#pragma unroll
+      for (int st = 0; st < 16; ++st)
+        if (s0 + st < nst) sacc += pv[st];
     }
 #pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      if (ok) sacc[e] += ks[i + e] * u0 + vs[i + e] * u1;   // (an identity step adds nothing; k, v may be non-finite)
-      y[i + e] = from_f32<T>(sacc[e]);
-    }
+    for (int j = 0; j < LP_MAX; ++j)
+      if (j < npend) sacc += av[j][0] * bq[j][0] + av[j][1] * bq[j][1];
   }
-  // this step's A part (zero for an identity step, so that nothing non-finite is kept)
-  __syncthreads();
-  float* na = A.pa + ((size_t)item * P + snew) * 2 * D;
-  for (int i = tid; i < D; i += DT) {
-    na[i] = ok ? ks[i] : 0.f;
-    na[D + i] = ok ? vs[i] : 0.f;
+  bool dummy = true;
+  block_sum4(x, dummy, dsc2);
+  // Re of the new factor times q: B0'q = N00 (kᵀHq) + N01 (vᵀHq), B1'q = N01 (kᵀHq) + N11 (vᵀHq)
+  const float u0 = N.ok ? N.n00r * x[0] - N.n00i * x[1] + N.n01r * x[2] - N.n01i * x[3] : 0.f;
+  const float u1 = N.ok ? N.n01r * x[0] - N.n01i * x[1] + N.n11r * x[2] - N.n11i * x[3] : 0.f;
+  if (r < D) {
+    if (N.ok) sacc += ks[r] * u0 + vs[r] * u1;   // (an identity step adds nothing; k, v may be non-finite)
+    static_cast<T*>(A.cout)[voff + r] = from_f32<T>(sacc);
+    // this step's A part (slot snew is not among the pending rows read above)
+    float* na = A.pa + ((size_t)item * P + snew) * 2 * D;
+    na[r] = N.ok ? ks[r] : 0.f;
+    na[D + r] = N.ok ? vs[r] : 0.f;
   }
-  if (tid == 0) A.pcount[item] = snew + 1;
+  if (blockIdx.x == 0 && tid == 0) A.pcount[item] = snew + 1;
 }
 
 // Fold every pending factor into S and empty the list (one CTA per (item, stripe)).
@@ -1068,13 +1191,13 @@ int launch_typed(const DecodeArgs& A, cudaStream_t st) {
   return check_launch("decode_step_kernel");
 }
 
-// one hologram plane as a [b*D rows][D] fp32 tensor, boxes of 32 columns x 64 rows, no swizzle
-int make_plane_map(CUtensorMap* m, const float* base, int b, int D) {
+// one hologram plane as a [b*D rows][D] fp32 tensor, boxes of `cols` columns x `rows` rows, no swizzle
+int make_plane_map(CUtensorMap* m, const float* base, int b, int D, int cols, int rows) {
   auto enc = tmap_encoder();
   VERACE_REQUIRE(enc != nullptr, VERACE_ERR_CUDA, "cuTensorMapEncodeTiled is not available");
   const cuuint64_t dims[2] = {(cuuint64_t)D, (cuuint64_t)b * D};
   const cuuint64_t strides[1] = {(cuuint64_t)D * 4};
-  const cuuint32_t box[2] = {(cuuint32_t)CWD, (cuuint32_t)LROWS};
+  const cuuint32_t box[2] = {(cuuint32_t)cols, (cuuint32_t)rows};
   const cuuint32_t es[2] = {1, 1};
   CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(base), dims, strides, box, es,
                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
@@ -1093,7 +1216,7 @@ LazyWs lazy_ws_layout(int b, int D) {
   const int nst = D / CWD;
   L.part = off; off = align_up(off + (size_t)b * nst * D * sizeof(float), 256);
   L.cqp = off;  off = align_up(off + (size_t)b * nst * 4 * sizeof(float), 256);
-  L.cnt = off;  off = align_up(off + (size_t)b * sizeof(unsigned int), 256);
+  L.cnt = off;  off = align_up(off + (size_t)b * sizeof(int), 256);
   L.g = off;    off = align_up(off + (size_t)b * LP_MAX * 4 * sizeof(float), 256);
   L.bq = off;   off = align_up(off + (size_t)b * LP_MAX * 2 * sizeof(float), 256);
   L.total = off + 256;
@@ -1201,6 +1324,40 @@ extern "C" int verace_decode_step(const void* sssd_q, const void* sssd_k, const 
   }
 }
 
+// lazy_pre_kernel, lazy_cham_kernel over (item, stripe) CTAs with the widest stripe D
+// allows, then lazy_out_kernel over the items.
+template <typename T, int W>
+int launch_lazy_w(const LazyArgs& A, const float* h_re, const float* h_im, cudaStream_t st) {
+  using G = LazyGeom<W>;
+  CUtensorMap mr, mi;
+  if (int rc = make_plane_map(&mr, h_re, A.b, A.D, W, G::ROWS)) return rc;
+  if (int rc = make_plane_map(&mi, h_im, A.b, A.D, W, G::ROWS)) return rc;
+  lazy_pre_kernel<T><<<A.b * A.P, DT, 0, st>>>(A);   // (also keeps the pending counts)
+  if (int rc = check_launch("lazy_pre_kernel")) return rc;
+  const size_t smem = G::smem(A.D, A.P);
+  VERACE_CUDA(cudaFuncSetAttribute(lazy_cham_kernel<T, W>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  LazyArgs B = A;
+  B.nst = A.D / W;
+  lazy_cham_kernel<T, W><<<(unsigned)(A.b * B.nst), DT, smem, st>>>(B, mr, mi);
+  if (int rc = check_launch("lazy_cham_kernel")) return rc;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)((A.D + DT - 1) / DT), (unsigned)A.b);
+  cfg.blockDim = dim3(DT);
+  cfg.dynamicSmemBytes = 2 * (size_t)A.D * sizeof(float);
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  VERACE_CUDA(cudaLaunchKernelEx(&cfg, lazy_out_kernel<T>, B));
+  return check_launch("lazy_out_kernel");
+}
+template <typename T>
+int launch_lazy(const LazyArgs& A, const float* h_re, const float* h_im, cudaStream_t st) {
+  return A.D % 64 == 0 ? launch_lazy_w<T, 64>(A, h_re, h_im, st) : launch_lazy_w<T, 32>(A, h_re, h_im, st);
+}
+
 extern "C" size_t verace_decode_lazy_workspace(int b, int D) {
   if (b <= 0 || D <= 0 || D % CWD) return 256;
   return lazy_ws_layout(b, D).total;
@@ -1241,36 +1398,13 @@ extern "C" int verace_decode_cham_lazy(const void* cham_q, const void* cham_k, c
   A.bq = (float*)(base + L.bq);
   A.part = (float*)(base + L.part);
   A.cqp = (float*)(base + L.cqp);
-  A.cnt = (unsigned int*)(base + L.cnt);
+  A.pcold = (int*)(base + L.cnt);
   A.b = b; A.D = D; A.P = P;
-  const unsigned grid = (unsigned)(b * (D / CWD));   // (lazy_pre_kernel zeroes A.cnt)
-  CUtensorMap mr, mi;
-  if (int rc = make_plane_map(&mr, h_re, b, D)) return rc;
-  if (int rc = make_plane_map(&mi, h_im, b, D)) return rc;
   switch (dtype) {
-    case VERACE_F32:
-      lazy_pre_kernel<float><<<b * P, DT, 0, st>>>(A);
-      if (int rc = check_launch("lazy_pre_kernel")) return rc;
-      VERACE_CUDA(cudaFuncSetAttribute(lazy_cham_kernel<float>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       (int)lazy_smem(D)));
-      lazy_cham_kernel<float><<<grid, DT, lazy_smem(D), st>>>(A, mr, mi);
-      break;
-    case VERACE_BF16:
-      lazy_pre_kernel<__nv_bfloat16><<<b * P, DT, 0, st>>>(A);
-      if (int rc = check_launch("lazy_pre_kernel")) return rc;
-      VERACE_CUDA(cudaFuncSetAttribute(lazy_cham_kernel<__nv_bfloat16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       (int)lazy_smem(D)));
-      lazy_cham_kernel<__nv_bfloat16><<<grid, DT, lazy_smem(D), st>>>(A, mr, mi);
-      break;
-    default:
-      lazy_pre_kernel<__half><<<b * P, DT, 0, st>>>(A);
-      if (int rc = check_launch("lazy_pre_kernel")) return rc;
-      VERACE_CUDA(cudaFuncSetAttribute(lazy_cham_kernel<__half>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       (int)lazy_smem(D)));
-      lazy_cham_kernel<__half><<<grid, DT, lazy_smem(D), st>>>(A, mr, mi);
-      break;
+    case VERACE_F32: return launch_lazy<float>(A, h_re, h_im, st);
+    case VERACE_BF16: return launch_lazy<__nv_bfloat16>(A, h_re, h_im, st);
+    default: return launch_lazy<__half>(A, h_re, h_im, st);
   }
-  return check_launch("lazy_cham_kernel");
 }
 
 extern "C" int verace_decode_cham_flush(float* h_re, float* h_im, void* pending, int P, int b, int D, void* stream) {
