@@ -7,13 +7,18 @@
 // The reference runs these as separate projections and a dozen elementwise and reduction
 // kernels; here they are one GEMM (outside this file) and one pass over its output.
 //
-// Work split: each head vector is normalised by a group of lanes of one warp (16-byte
-// loads, fp32 norms, segmented shuffle reductions): several short vectors share a warp,
-// long ones take a whole warp.  A lane group takes UPT consecutive vectors (adjacent
-// heads of a row) and issues all of their loads before the first reduction, so short
-// vectors still keep several 16-byte loads per thread in flight.  The gates are a
-// grid-stride tail of the same launch.
+// Work split, 16-bit activations with h·d a multiple of 256 and head vectors that divide
+// or span whole 32-lane rounds of 16-byte chunks (the configs' 8 x 128 and 1 x 1024):
+// one row per warp, every lane issuing its 12 loads of a 1024-wide row before the first
+// reduction (mixer_prologue_rows; 53 us against 72 us for the general split at 16384
+// rows of 8 x 128 heads).  Otherwise each head vector is normalised by a group of lanes of
+// one warp (16-byte loads, fp32 norms, segmented shuffle reductions): several short
+// vectors share a warp, long ones take a whole warp, and the gates are a grid-stride tail
+// of the same launch.
 #include "common.cuh"
+
+#include <algorithm>
+#include <type_traits>
 
 namespace verace {
 namespace {
@@ -161,6 +166,121 @@ mixer_prologue_kernel(const T* __restrict__ y, long long ld, T* __restrict__ q, 
   gate[e] = val;
 }
 
+// Row-per-warp variant for 16-bit activations when h d is a multiple of 256 and each head
+// vector either divides a 32-lane round of 16-byte chunks (RV = 0: d / 8 a divisor of 32)
+// or is RV whole rounds (d / 8 = 32 RV, RV dividing NR): a lane issues NR of a row's
+// 16-byte loads (6 KB a warp at h d = 1024) before the first reduction, so the loads in
+// flight are not limited by the vectors a lane group holds.  Chunk c = lane + 32 i of the
+// row's q | k | v part lies in part c / (h d / 8), head (c mod (h d / 8)) / (d / 8).
+// Two 16-bit values in a 32-bit word <-> floats, by value (no address taken, so a row's
+// words stay in registers).
+template <typename T>
+__device__ __forceinline__ float2 unpack2(uint32_t w) {
+  if constexpr (std::is_same<T, __nv_bfloat16>::value) {
+    return make_float2(__uint_as_float(w << 16), __uint_as_float(w & 0xffff0000u));
+  } else {
+    return __half22float2(__halves2half2(__ushort_as_half((unsigned short)(w & 0xffffu)),
+                                         __ushort_as_half((unsigned short)(w >> 16))));
+  }
+}
+template <typename T>
+__device__ __forceinline__ uint32_t pack2(float a, float b) {
+  if constexpr (std::is_same<T, __nv_bfloat16>::value) {
+    return (uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(a)) |
+           ((uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(b)) << 16);
+  } else {
+    return (uint32_t)__half_as_ushort(__float2half_rn(a)) | ((uint32_t)__half_as_ushort(__float2half_rn(b)) << 16);
+  }
+}
+template <typename T>
+__device__ __forceinline__ uint32_t silu2(uint32_t w) {
+  const float2 f = unpack2<T>(w);
+  return pack2<T>(silu_f(f.x), silu_f(f.y));
+}
+template <typename T>
+__device__ __forceinline__ float ss2(uint32_t w) {
+  const float2 f = unpack2<T>(w);
+  return f.x * f.x + f.y * f.y;
+}
+
+// Normalise one row segment held as NR rounds of 16-byte words (round i = chunks
+// lane + 32 (r0 + i) of the row's q | k | v part) and store it; the gates are separate.
+template <typename T, int NR, int RV>
+__device__ __forceinline__ void rows_finish(uint4 (&raw)[NR], int r0, int rounds, int lane, int nc, int pc, int silu_v,
+                                            long long row, int hd, T* __restrict__ q, T* __restrict__ k,
+                                            T* __restrict__ v) {
+  float sc[NR];   // per round: this lane's sum of squares, then the vector's 1 / norm
+#pragma unroll
+  for (int i = 0; i < NR; ++i) {
+    if (silu_v && (lane + 32 * (r0 + i)) / pc == 2) {   // v through SiLU, kept in the input type (as
+      raw[i].x = silu2<T>(raw[i].x);                     // the reference's SiLU output is)
+      raw[i].y = silu2<T>(raw[i].y);
+      raw[i].z = silu2<T>(raw[i].z);
+      raw[i].w = silu2<T>(raw[i].w);
+    }
+    sc[i] = ss2<T>(raw[i].x) + ss2<T>(raw[i].y) + ss2<T>(raw[i].z) + ss2<T>(raw[i].w);
+  }
+  if constexpr (RV == 0) {   // 32 / nc vectors per round: segmented reduction over nc lanes
+#pragma unroll
+    for (int i = 0; i < NR; ++i) {
+      float ss = sc[i];
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1)
+        if (o < nc) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+      sc[i] = 1.f / fmaxf(sqrtf(ss), 1e-12f);
+    }
+  } else {                   // one vector per RV consecutive rounds
+#pragma unroll
+    for (int i0 = 0; i0 < NR; i0 += RV) {
+      float ss = 0.f;
+#pragma unroll
+      for (int i = i0; i < i0 + RV; ++i) ss += sc[i];
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+      const float r = 1.f / fmaxf(sqrtf(ss), 1e-12f);
+#pragma unroll
+      for (int i = i0; i < i0 + RV; ++i) sc[i] = r;
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < NR; ++i) {
+    if (r0 + i < rounds) {
+      const int c = lane + 32 * (r0 + i), part = c / pc, cc = c - part * pc;
+      const float r = sc[i];
+      const float2 a = unpack2<T>(raw[i].x), b = unpack2<T>(raw[i].y), c2 = unpack2<T>(raw[i].z),
+                   d2 = unpack2<T>(raw[i].w);
+      const uint4 o = make_uint4(pack2<T>(a.x * r, a.y * r), pack2<T>(b.x * r, b.y * r), pack2<T>(c2.x * r, c2.y * r),
+                                 pack2<T>(d2.x * r, d2.y * r));
+      *reinterpret_cast<uint4*>((part == 0 ? q : part == 1 ? k : v) + row * hd + 8LL * cc) = o;
+    }
+  }
+}
+
+// One row per warp, NR rounds of loads in flight per lane (a segment loop for rows of more
+// than NR rounds).
+template <typename T, int NR, int RV>
+__global__ void __launch_bounds__(PT, 3) mixer_prologue_rows(const T* __restrict__ y, long long ld, T* __restrict__ q,
+                                                            T* __restrict__ k, T* __restrict__ v,
+                                                            float* __restrict__ gate,
+                                                            const unsigned char* __restrict__ mask, long long n, int h,
+                                                            int d, int g, int silu_v) {
+  const int lane = threadIdx.x & 31;
+  const long long row = (long long)blockIdx.x * (PT / 32) + (threadIdx.x >> 5);
+  if (row >= n) return;
+  const int hd = h * d, nc = d / 8, pc = hd / 8;
+  const int rounds = 3 * pc / 32;
+  const T* src = y + row * ld;
+  const bool keep = mask == nullptr || mask[row];
+  for (int j = lane; j < g; j += 32) gate[row * g + j] = keep ? 0.1f * sigmoid_f(to_f32(src[3LL * hd + j])) : 0.f;
+  for (int r0 = 0; r0 < rounds; r0 += NR) {
+    uint4 raw[NR];
+#pragma unroll
+    for (int i = 0; i < NR; ++i)
+      if (r0 + i < rounds) raw[i] = *reinterpret_cast<const uint4*>(src + 8 * (lane + 32 * (r0 + i)));
+    rows_finish<T, NR, RV>(raw, r0, rounds, lane, nc, pc, silu_v, row, hd, q, k, v);
+  }
+}
+
 template <typename T>
 int launch_prologue(const void* y, long long ld, void* q, void* k, void* v, float* gate, const unsigned char* mask,
                     long long n, int h, int d, int g, int silu_v, cudaStream_t st) {
@@ -168,8 +288,10 @@ int launch_prologue(const void* y, long long ld, void* q, void* k, void* v, floa
   int L, cpl;
   if (nc <= 16 && (16 % nc) == 0) { L = nc; cpl = 1; }
   else { L = 32; cpl = (nc + 31) / 32; }
-  const int upt = 1;                  // vectors per lane group
+  constexpr int UPT = 1;   // vectors per lane group (2 and 4 measured slower)
+  const int upt = UPT;
   const long long units = n * 3 * h;
+  const int hd = h * d;
   const long long per_block = (long long)(PT / 32) * (32 / L) * upt;
   const long long nvec_blocks = (units + per_block - 1) / per_block;
   const long long ngate_blocks = (n * g + PT - 1) / PT;
@@ -177,19 +299,34 @@ int launch_prologue(const void* y, long long ld, void* q, void* k, void* v, floa
   VERACE_REQUIRE(grid < (1LL << 31), VERACE_ERR_UNSUPPORTED, "verace_mixer_prologue: too many rows");
   const T* yy = (const T*)y;
   T *qq = (T*)q, *kk = (T*)k, *vv = (T*)v;
+  if constexpr (sizeof(T) == 2) {
+    const bool fits = hd % 256 == 0 && (nc <= 32 ? 32 % nc == 0 : (nc == 64 || nc == 128));
+    const int rv = nc <= 32 ? 0 : nc / 32;
+    if (fits) {   // one row per warp, 12 rounds per segment
+      const unsigned gr = (unsigned)((n + PT / 32 - 1) / (PT / 32));
+      if (rv == 0)
+        mixer_prologue_rows<T, 12, 0><<<gr, PT, 0, st>>>(yy, ld, qq, kk, vv, gate, mask, n, h, d, g, silu_v);
+      else if (rv == 2)
+        mixer_prologue_rows<T, 12, 2><<<gr, PT, 0, st>>>(yy, ld, qq, kk, vv, gate, mask, n, h, d, g, silu_v);
+      else
+        mixer_prologue_rows<T, 12, 4><<<gr, PT, 0, st>>>(yy, ld, qq, kk, vv, gate, mask, n, h, d, g, silu_v);
+      return check_launch("mixer_prologue_rows");
+    }
+  }
   if (cpl == 1)
-    mixer_prologue_kernel<T, 1, 1><<<(unsigned)grid, PT, 0, st>>>(yy, ld, qq, kk, vv, gate, mask, n, h, d, g, silu_v,
+    mixer_prologue_kernel<T, 1, UPT><<<(unsigned)grid, PT, 0, st>>>(yy, ld, qq, kk, vv, gate, mask, n, h, d, g, silu_v,
                                                                    L, nvec_blocks);
   else if (cpl <= 4)
-    mixer_prologue_kernel<T, 4, 1><<<(unsigned)grid, PT, 0, st>>>(yy, ld, qq, kk, vv, gate, mask, n, h, d, g, silu_v,
+    mixer_prologue_kernel<T, 4, UPT><<<(unsigned)grid, PT, 0, st>>>(yy, ld, qq, kk, vv, gate, mask, n, h, d, g, silu_v,
                                                                    L, nvec_blocks);
   else
-    mixer_prologue_kernel<T, MAXV, 1><<<(unsigned)grid, PT, 0, st>>>(yy, ld, qq, kk, vv, gate, mask, n, h, d, g,
+    mixer_prologue_kernel<T, MAXV, UPT><<<(unsigned)grid, PT, 0, st>>>(yy, ld, qq, kk, vv, gate, mask, n, h, d, g,
                                                                       silu_v, L, nvec_blocks);
   return check_launch("mixer_prologue_kernel");
 }
 
 }  // namespace
+
 }  // namespace verace
 
 using namespace verace;
@@ -211,6 +348,8 @@ extern "C" int verace_mixer_prologue(const void* y, long long ld, void* q, void*
   if (n == 0) return VERACE_OK;
   VERACE_REQUIRE(y && q && k && v && (gate || gate_cols == 0), VERACE_ERR_INVALID,
                  "verace_mixer_prologue: NULL pointer");
+  VERACE_REQUIRE((((uintptr_t)y | (uintptr_t)q | (uintptr_t)k | (uintptr_t)v) & 15) == 0, VERACE_ERR_INVALID,
+                 "verace_mixer_prologue: y, q, k and v must be 16-byte aligned");
   cudaStream_t st = (cudaStream_t)stream;
   switch (dtype) {
     case VERACE_F32:
