@@ -34,10 +34,11 @@ def _reference(y, h, d, g, silu_v, mask):
 @pytest.mark.parametrize("h,d,g,silu_v", [(8, 128, 8, False), (1, 1024, 1, True), (3, 64, 3, False), (1, 160, 1, True),
                                           (16, 128, 16, False), (2, 1024, 2, True), (4, 512, 4, True)])
 def test_prologue_matches_reference_elementwise(dtype, h, d, g, silu_v):
-    """16-bit rows with h d a multiple of 256 take the row-per-warp kernel (one segment of
-    12 rounds at h d = 1024, two at 2048; head vectors of half a round, two rounds or four
-    rounds); the other cases the general split."""
-    n = 333
+    """16-bit activations at 4133 rows with h d a multiple of 256 take the row-per-warp kernel
+    (one segment of 12 rounds at h d = 1024, two at 2048; head vectors of half a round, two
+    rounds or four rounds); the other cases the general split (as does a decode step's
+    handful of rows, test_decode_gpu)."""
+    n = 4133 if dtype != torch.float32 else 333   # 16-bit rows from 4096 take the row-per-warp kernel
     ld = 3 * h * d + g + ((-(3 * h * d + g)) % 8)
     gen = torch.Generator().manual_seed(900 + d)
     y = torch.randn(n, ld, generator=gen).to("cuda", dtype)

@@ -7,14 +7,14 @@
 // The reference runs these as separate projections and a dozen elementwise and reduction
 // kernels; here they are one GEMM (outside this file) and one pass over its output.
 //
-// Work split, 16-bit activations with h·d a multiple of 256 and head vectors that divide
-// or span whole 32-lane rounds of 16-byte chunks (the configs' 8 x 128 and 1 x 1024):
-// one row per warp, every lane issuing its 12 loads of a 1024-wide row before the first
-// reduction (mixer_prologue_rows; 53 us against 72 us for the general split at 16384
-// rows of 8 x 128 heads).  Otherwise each head vector is normalised by a group of lanes of
-// one warp (16-byte loads, fp32 norms, segmented shuffle reductions): several short
-// vectors share a warp, long ones take a whole warp, and the gates are a grid-stride tail
-// of the same launch.
+// Work split, from 4096 rows of 16-bit activations with h·d a multiple of 256 and head
+// vectors that divide or span whole 32-lane rounds of 16-byte chunks (the configs' 8 x 128
+// and 1 x 1024): one row per warp, every lane issuing its 12 loads of a 1024-wide row
+// before the first reduction (mixer_prologue_rows; 53 us against 72 us for the general
+// split at 16384 rows of 8 x 128 heads).  Otherwise each head vector is normalised by a
+// group of lanes of one warp (16-byte loads, fp32 norms, segmented shuffle reductions):
+// several short vectors share a warp, long ones take a whole warp, and the gates are a
+// grid-stride tail of the same launch.
 #include "common.cuh"
 
 #include <algorithm>
@@ -300,7 +300,9 @@ int launch_prologue(const void* y, long long ld, void* q, void* k, void* v, floa
   const T* yy = (const T*)y;
   T *qq = (T*)q, *kk = (T*)k, *vv = (T*)v;
   if constexpr (sizeof(T) == 2) {
-    const bool fits = hd % 256 == 0 && (nc <= 32 ? 32 % nc == 0 : (nc == 64 || nc == 128));
+    // (for a few rows, e.g. a decode step's batch, one warp per row leaves most SMs idle and
+    // the general split's many small lane groups are faster)
+    const bool fits = n >= 4096 && hd % 256 == 0 && (nc <= 32 ? 32 % nc == 0 : (nc == 64 || nc == 128));
     const int rv = nc <= 32 ? 0 : nc / 32;
     if (fits) {   // one row per warp, 12 rounds per segment
       const unsigned gr = (unsigned)((n + PT / 32 - 1) / (PT / 32));
