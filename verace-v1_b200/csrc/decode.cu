@@ -651,6 +651,10 @@ __global__ void __launch_bounds__(DT) lazy_pre_kernel(LazyArgs A) {
   const int D = A.D, P = A.P;
   const int item = blockIdx.x / P, j = blockIdx.x % P;
   const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
+  // launched as a programmatic dependent of the projection epilogue (k, v, q); the stripe
+  // kernel that follows may start its hologram loads once every CTA here has started
+  asm volatile("griddepcontrol.launch_dependents;");
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   const int p = A.pcount[item];
   if (j == 0 && tid == 0) A.pcold[item] = p;
   if (p >= P || j >= p) return;       // a folding step needs none of them
@@ -729,10 +733,6 @@ lazy_cham_kernel(LazyArgs A, const __grid_constant__ CUtensorMap tm_r, const __g
   const int item = blockIdx.x / nst, stripe = blockIdx.x % nst;
   const int c8 = lane % TPR;
   const int rp = threadIdx.x / TPR;       // rows rp and rp + RPG of each stage
-  const int p = A.pcount[item];
-  const bool fold = p >= P;               // fold the P pending factors into S this step
-  const int np = fold ? P : p;            // pending factors read by this step
-  const int snew = fold ? 0 : p;          // slot of this step's factor
   const int NRB = D / LROWS;
   auto stage = [&](int s) { return reinterpret_cast<float*>(lsm + s * LSTAGE); };
   auto issue = [&](int rb) {
@@ -741,11 +741,20 @@ lazy_cham_kernel(LazyArgs A, const __grid_constant__ CUtensorMap tm_r, const __g
     tc::tma_load_2d(stage(s), &tm_r, stripe * W, item * D + rb * LROWS, &full[s]);
     tc::tma_load_2d(stage(s) + LROWS * W, &tm_i, stripe * W, item * D + rb * LROWS, &full[s]);
   };
+  // The hologram stages depend on no earlier kernel of this step: they are requested
+  // before griddepcontrol.wait, which (this kernel being launched as a programmatic
+  // dependent of lazy_pre_kernel) returns once lazy_pre_kernel and, through it, the
+  // projection epilogue are complete and their writes visible.
   if (tid == 0) {
     for (int s = 0; s < NSTG; ++s) tc::mbar_init(&full[s], 1);
     tc::fence_mbar_init();
     for (int rb = 0; rb < NSTG && rb < NRB; ++rb) issue(rb);
   }
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  const int p = A.pcount[item];
+  const bool fold = p >= P;               // fold the P pending factors into S this step
+  const int np = fold ? P : p;            // pending factors read by this step
+  const int snew = fold ? 0 : p;          // slot of this step's factor
 
   const size_t voff = (size_t)item * D;
   const float* pa = A.pa + (size_t)item * P * 2 * D;
@@ -1332,24 +1341,29 @@ int launch_lazy_w(const LazyArgs& A, const float* h_re, const float* h_im, cudaS
   CUtensorMap mr, mi;
   if (int rc = make_plane_map(&mr, h_re, A.b, A.D, W, G::ROWS)) return rc;
   if (int rc = make_plane_map(&mi, h_im, A.b, A.D, W, G::ROWS)) return rc;
-  lazy_pre_kernel<T><<<A.b * A.P, DT, 0, st>>>(A);   // (also keeps the pending counts)
+  // all three launched as programmatic dependents of the kernel before them
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.stream = st;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cfg.blockDim = dim3(DT);
+  cfg.gridDim = dim3((unsigned)(A.b * A.P));
+  cfg.dynamicSmemBytes = 0;
+  VERACE_CUDA(cudaLaunchKernelEx(&cfg, lazy_pre_kernel<T>, A));   // (also keeps the pending counts)
   if (int rc = check_launch("lazy_pre_kernel")) return rc;
   const size_t smem = G::smem(A.D, A.P);
   VERACE_CUDA(cudaFuncSetAttribute(lazy_cham_kernel<T, W>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
   LazyArgs B = A;
   B.nst = A.D / W;
-  lazy_cham_kernel<T, W><<<(unsigned)(A.b * B.nst), DT, smem, st>>>(B, mr, mi);
+  cfg.gridDim = dim3((unsigned)(A.b * B.nst));
+  cfg.dynamicSmemBytes = smem;
+  VERACE_CUDA(cudaLaunchKernelEx(&cfg, lazy_cham_kernel<T, W>, B, mr, mi));
   if (int rc = check_launch("lazy_cham_kernel")) return rc;
-  cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)((A.D + DT - 1) / DT), (unsigned)A.b);
-  cfg.blockDim = dim3(DT);
   cfg.dynamicSmemBytes = 2 * (size_t)A.D * sizeof(float);
-  cfg.stream = st;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
   VERACE_CUDA(cudaLaunchKernelEx(&cfg, lazy_out_kernel<T>, B));
   return check_launch("lazy_out_kernel");
 }

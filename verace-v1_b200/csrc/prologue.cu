@@ -85,6 +85,9 @@ mixer_prologue_kernel(const T* __restrict__ y, long long ld, T* __restrict__ q, 
                       long long n, int h, int d, int g, int silu_v, int L, long long nvec_blocks) {
   const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
   const int hd = h * d;
+  // a kernel launched after this one as a programmatic dependent (the deferred decode
+  // step's lazy_pre_kernel) may start; it waits for this grid's completion before reading
+  asm volatile("griddepcontrol.launch_dependents;");
   if ((long long)blockIdx.x < nvec_blocks) {
     const int upw = 32 / L;                                    // lane groups per warp
     const long long unit0 = (((long long)blockIdx.x * (PT / 32) + w) * upw + lane / L) * UPT;   // (row, part, head)
