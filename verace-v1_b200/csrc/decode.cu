@@ -262,6 +262,10 @@ __global__ void __launch_bounds__(DT, 4) sssd_decode128_kernel(DecodeArgs A) {
   float4 ps[SD_NREG];
 #pragma unroll
   for (int m = 0; m < SD_NREG; ++m) ps[m] = __ldcs(reinterpret_cast<const float4*>(P + (size_t)(w + 8 * m) * HD) + lane);
+  // The state depends on no earlier kernel of this step and is requested above; launched as
+  // a programmatic dependent of the projection epilogue, the kernel waits here for k, v, q
+  // and the gate.
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   float dots[4] = {0.f, 0.f, 0.f, 0.f};
   bool fin = true;
   if (tid < HD) {
@@ -1190,7 +1194,17 @@ int launch_typed(const DecodeArgs& A, cudaStream_t st) {
   const bool fo = A.mode == VERACE_DECODE_FIRST_ORDER;
   if (A.D == 0 && A.d == 128) {
     VERACE_CUDA(cudaFuncSetAttribute(sssd_decode128_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, SD_SMEM));
-    sssd_decode128_kernel<T><<<grid, DT, SD_SMEM, st>>>(A);
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)grid);
+    cfg.blockDim = dim3(DT);
+    cfg.dynamicSmemBytes = SD_SMEM;
+    cfg.stream = st;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    VERACE_CUDA(cudaLaunchKernelEx(&cfg, sssd_decode128_kernel<T>, A));
   } else if (A.D == 0)
     decode_step_kernel<T, false, false><<<grid, DT, 0, st>>>(A);
   else if (fo)
