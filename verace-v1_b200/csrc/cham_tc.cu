@@ -58,7 +58,7 @@ struct TcWs {
   float* Hre;
   float* Him;
   float* ring;               // [min(nch, 2 RING)][b][D][D]: real parts of chunk end states (fp32 rows,
-                             // or in the batched schedule the readout's bf16 hi / lo operand images)
+                             // or in the batched schedule the readout's bf16 operand images, half a slot)
   int nring;
   unsigned char* cm;         // [2][b][D/64][64 KB]: fused schedule, Cm operands between launches
 };
@@ -1378,9 +1378,9 @@ readout2_body(const CUtensorMap& tm_k, const CUtensorMap& tm_v, const CUtensorMa
       };
       auto issue = [&](int kt) {
         const int s = kt & 1;
-        tc::mbar_expect_tx(&bars[B_TFULL + s], 32 * 1024 + 8 * 1024);
-        if (pre != nullptr) {
-          tc::bulk_load_hint(stA(s), pre + (size_t)(bx * NTR + kt) * (32 * 1024), 32 * 1024, &bars[B_TFULL + s],
+        tc::mbar_expect_tx(&bars[B_TFULL + s], (pre != nullptr ? 16 : 32) * 1024 + 8 * 1024);
+        if (pre != nullptr) {   // the image's bf16 tile (the real part rounded once)
+          tc::bulk_load_hint(stA(s), pre + (size_t)(bx * NTR + kt) * (16 * 1024), 16 * 1024, &bars[B_TFULL + s],
                              tc::policy_evict_first());
         } else {
           tc::tma_load_2d(stA(s), &tm_sr, kt * RKT, srow + i0, &bars[B_TFULL + s]);
@@ -1401,7 +1401,7 @@ readout2_body(const CUtensorMap& tm_k, const CUtensorMap& tm_v, const CUtensorMa
         for (int ks = 0; ks < RKT / 16; ++ks) {
           const uint64_t b = tc::sdesc_sw128(y + ks * 32, 16, 1024);
           tc::mma_bf16(tO, tc::sdesc(ah + ks * 2 * R2 * 16, R2 * 16, 128), b, ID_O, (kt > 0 || ks > 0) ? 1u : 0u);
-          tc::mma_bf16(tO, tc::sdesc(al + ks * 2 * R2 * 16, R2 * 16, 128), b, ID_O, 1u);
+          if (pre == nullptr) tc::mma_bf16(tO, tc::sdesc(al + ks * 2 * R2 * 16, R2 * 16, 128), b, ID_O, 1u);
         }
         tc::commit(&bars[B_MDONE + s]);
         if (kt + 2 < NTR) {
@@ -1776,9 +1776,12 @@ colpass2_body(const CUtensorMap& tm_k, const CUtensorMap& tm_v, const CUtensorMa
     const int src_identity = c == 0 && !h0;   // with a carried hologram the planes start as H0
     // The state is updated in place in the output planes (phase A reads its column
     // block, phase B adds dH with TMA reductions); phase A also stores the real part it
-    // reads (the end state of chunk c-1), split into bf16 hi / lo, to that chunk's ring
-    // slot as the readout's K-major operand images: row r, column j of an item's D x D
-    // real plane at ((r / 128) (D / 64) + j / 64) 32K + kmaj(r % 128, j % 64) (+ 16K for lo).
+    // reads (the end state of chunk c-1), rounded to bf16, to that chunk's ring slot as
+    // the readout's K-major operand images: row r, column j of an item's D x D real plane
+    // at ((r / 128) (D / 64) + j / 64) 16K + kmaj(r % 128, j % 64).  (The readout's state
+    // operand is the one place the bf16 path rounds the state: Re(H) q with Re(H) to 2^-9
+    // relative, the readout itself rounded to bf16 after; the state and everything
+    // carried from chunk to chunk stay fp32-accurate.)
     const CUtensorMap* tm_sr = &tm_hr64;
     const CUtensorMap* tm_si = &tm_hi64;
     const CUtensorMap* tm_dr = &tm_hr128;
@@ -1986,9 +1989,8 @@ colpass2_body(const CUtensorMap& tm_k, const CUtensorMap& tm_v, const CUtensorMa
           *reinterpret_cast<uint4*>(w + 16384 + mnmaj(i, N2 + gg * 8, NGW)) = lv;
           if (gg < 4 && ring_img != nullptr) {   // the real half as read: chunk c-1's end state
             const int r = h * KH + i, j = j0 + gg * 8;
-            unsigned char* img = ring_img + (size_t)((r >> 7) * (D / RKT) + (j >> 6)) * (32 * 1024) + kmaj(r & 127, j & 63, R2);
+            unsigned char* img = ring_img + (size_t)((r >> 7) * (D / RKT) + (j >> 6)) * (16 * 1024) + kmaj(r & 127, j & 63, R2);
             tc::st_global_hint(img, hv, stream_once);   // read once, by the readout
-            tc::st_global_hint(img + 16 * 1024, lv, stream_once);
           }
         }
         tc::fence_proxy_async();
@@ -2711,8 +2713,8 @@ int launch_cham_tc(const void* q, const void* k, const void* v, const float* gam
     // (the last chunk's is hr), so group g's launch also runs the readouts of the chunks
     // group g-1 completed, in the SM slots its column pass leaves free; one readout
     // launch finishes the sequence.  The ring holds two groups, so the two never meet.
-    // The ring slots hold the end states' real parts as the readout's pre-split bf16
-    // hi / lo operand images (the same bytes as fp32), written by phase A.
+    // The ring slots hold the end states' real parts as the readout's bf16 operand images
+    // (half the bytes of fp32), written by phase A.
     CUtensorMap mq, m_hr64, m_hi64, m_hr128, m_hi128;
     unsigned char* ring = reinterpret_cast<unsigned char*>(w.ring);
     if ((rc = make_kv_map(&mq, q, b, s, D)) ||
