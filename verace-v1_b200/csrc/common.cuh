@@ -9,6 +9,8 @@
 #include <stdint.h>
 #include <stddef.h>
 
+#include <type_traits>
+
 #include "../../include/verace_b200.h"
 
 namespace verace {
@@ -45,6 +47,39 @@ template <typename T> __device__ __forceinline__ T from_f32(float x);
 template <> __device__ __forceinline__ float from_f32<float>(float x) { return x; }
 template <> __device__ __forceinline__ __nv_bfloat16 from_f32<__nv_bfloat16>(float x) { return __float2bfloat16_rn(x); }
 template <> __device__ __forceinline__ __half from_f32<__half>(float x) { return __float2half_rn(x); }
+
+// Two 16-bit values in a 32-bit word <-> floats, by value (no address taken, so arrays of
+// words stay in registers).  T is __nv_bfloat16 or __half.
+template <typename T>
+__device__ __forceinline__ float2 unpack2(uint32_t w) {
+  if constexpr (std::is_same<T, __nv_bfloat16>::value) {
+    return make_float2(__uint_as_float(w << 16), __uint_as_float(w & 0xffff0000u));
+  } else {
+    return __half22float2(__halves2half2(__ushort_as_half((unsigned short)(w & 0xffffu)),
+                                         __ushort_as_half((unsigned short)(w >> 16))));
+  }
+}
+template <typename T>
+__device__ __forceinline__ uint32_t pack2(float a, float b) {
+  if constexpr (std::is_same<T, __nv_bfloat16>::value) {
+    return (uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(a)) |
+           ((uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(b)) << 16);
+  } else {
+    return (uint32_t)__half_as_ushort(__float2half_rn(a)) | ((uint32_t)__half_as_ushort(__float2half_rn(b)) << 16);
+  }
+}
+// The 8 values of a 16-byte word of 16-bit elements, and back.
+template <typename T>
+__device__ __forceinline__ void unpack8(const uint4& u, float* x) {
+  float2 f = unpack2<T>(u.x); x[0] = f.x; x[1] = f.y;
+  f = unpack2<T>(u.y); x[2] = f.x; x[3] = f.y;
+  f = unpack2<T>(u.z); x[4] = f.x; x[5] = f.y;
+  f = unpack2<T>(u.w); x[6] = f.x; x[7] = f.y;
+}
+template <typename T>
+__device__ __forceinline__ uint4 pack8(const float* x) {
+  return make_uint4(pack2<T>(x[0], x[1]), pack2<T>(x[2], x[3]), pack2<T>(x[4], x[5]), pack2<T>(x[6], x[7]));
+}
 
 // ------------------------------------------------------------------ SMEM GEMM
 // C(m,n) (=|+=) alpha * sum_k A(m,k) B(k,n) over an M x N output with K terms, where

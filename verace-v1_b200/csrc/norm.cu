@@ -211,6 +211,94 @@ add_rmsnorm_kernel(T* __restrict__ h, const T* __restrict__ y, const T* __restri
   }
 }
 
+// add_rmsnorm for 16-bit activations and rows of at most 4 chunks per lane: the same
+// arithmetic in the same order, with the row's h and y chunks held as the loaded 16-byte
+// words (unpacked where used) instead of floats, so that a thread holds a quarter of the
+// registers and more rows' loads are in flight per SM.
+template <typename T, int L, int V>
+__global__ void __launch_bounds__(NT, 3)
+add_rmsnorm16_kernel(T* __restrict__ h, const T* __restrict__ y, const T* __restrict__ wy, float eps_y,
+                     const T* __restrict__ wn, float eps_n, T* __restrict__ n, long long rows, int cols, int norm_y) {
+  static_assert(sizeof(T) == 2 && prefetch_w<V>(), "16-bit rows of at most 4 chunks per lane");
+  const int lane = threadIdx.x & 31;
+  const long long row = ((long long)blockIdx.x * NT + threadIdx.x) / L;
+  const int sl = lane % L, nc = cols / 8;
+  const bool act = row < rows;
+  const long long off = (act ? row : 0) * cols;
+  Raw8<T> wyr[V], wnr[V];
+  load_w<T, L, V>(norm_y ? wy : nullptr, sl, nc, wyr);
+  load_w<T, L, V>(n ? wn : nullptr, sl, nc, wnr);
+  uint4 ar[V], br[V];
+#pragma unroll
+  for (int i = 0; i < V; ++i) {
+    const int cc = sl + L * i;
+    if (cc < nc) {
+      ar[i] = *reinterpret_cast<const uint4*>(h + off + 8 * cc);
+      br[i] = *reinterpret_cast<const uint4*>(y + off + 8 * cc);
+    } else {
+      ar[i] = br[i] = make_uint4(0, 0, 0, 0);
+    }
+  }
+  // sum of squares of a row held as words, in rms_apply's order; then 1 / rms
+  auto inv_rms = [&](const uint4 (&r)[V], float eps) {
+    float ss = 0.f;
+#pragma unroll
+    for (int i = 0; i < V; ++i)
+      if (sl + L * i < nc) {
+        float x[8];
+        unpack8<T>(r[i], x);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) ss = fmaf(x[j], x[j], ss);
+      }
+    ss = group_sum<L>(ss);
+    return rsqrtf(ss / (float)cols + eps);
+  };
+  const float rs_y = norm_y ? inv_rms(br, eps_y) : 0.f;
+#pragma unroll
+  for (int i = 0; i < V; ++i) {
+    float xa[8], xb[8];
+    unpack8<T>(ar[i], xa);
+    unpack8<T>(br[i], xb);
+    if (norm_y && sl + L * i < nc) {
+      float wv[8];
+      if (wy) unraw<T>(wyr[i], wv);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const float r = rnd<T>(xb[j] * rs_y);
+        xb[j] = wy ? rnd<T>(r * wv[j]) : r;
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < 8; ++j) xa[j] = rnd<T>(xa[j] + xb[j]);
+    ar[i] = pack8<T>(xa);   // (exact: every value is already rounded to T)
+  }
+  if (act) {
+#pragma unroll
+    for (int i = 0; i < V; ++i) {
+      const int cc = sl + L * i;
+      if (cc < nc) *reinterpret_cast<uint4*>(h + off + 8 * cc) = ar[i];
+    }
+  }
+  if (!n) return;
+  const float rs_n = inv_rms(ar, eps_n);
+  if (!act) return;
+#pragma unroll
+  for (int i = 0; i < V; ++i) {
+    const int cc = sl + L * i;
+    if (cc < nc) {
+      float x[8], wv[8];
+      unpack8<T>(ar[i], x);
+      if (wn) unraw<T>(wnr[i], wv);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const float r = rnd<T>(x[j] * rs_n);
+        x[j] = wn ? rnd<T>(r * wv[j]) : r;
+      }
+      *reinterpret_cast<uint4*>(n + off + 8 * cc) = pack8<T>(x);
+    }
+  }
+}
+
 // lanes per row and chunks per lane for a row of `cols`
 struct Shape {
   int L, V;
@@ -248,6 +336,21 @@ int launch_add_rmsnorm(void* h, const void* y, const void* wy, float eps_y, int 
   const T* a = (const T*)wy;
   const T* bw = (const T*)wn;
   T* nn = (T*)n;
+  if constexpr (sizeof(T) == 2) {
+    if (sh.L == 16) {
+      add_rmsnorm16_kernel<T, 16, 1><<<(unsigned)grid, NT, 0, st>>>(hh, yy, a, eps_y, bw, eps_n, nn, rows, cols, norm_y);
+      return check_launch("add_rmsnorm16_kernel");
+    }
+    if (sh.V <= 4) {
+      if (sh.V == 1)
+        add_rmsnorm16_kernel<T, 32, 1><<<(unsigned)grid, NT, 0, st>>>(hh, yy, a, eps_y, bw, eps_n, nn, rows, cols,
+                                                                      norm_y);
+      else
+        add_rmsnorm16_kernel<T, 32, 4><<<(unsigned)grid, NT, 0, st>>>(hh, yy, a, eps_y, bw, eps_n, nn, rows, cols,
+                                                                      norm_y);
+      return check_launch("add_rmsnorm16_kernel");
+    }
+  }
   if (sh.L == 16)
     add_rmsnorm_kernel<T, 16, 1><<<(unsigned)grid, NT, 0, st>>>(hh, yy, a, eps_y, bw, eps_n, nn, rows, cols, norm_y);
   else if (sh.V == 1)

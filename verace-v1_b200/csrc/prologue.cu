@@ -175,26 +175,6 @@ mixer_prologue_kernel(const T* __restrict__ y, long long ld, T* __restrict__ q, 
 // 16-byte loads (6 KB a warp at h d = 1024) before the first reduction, so the loads in
 // flight are not limited by the vectors a lane group holds.  Chunk c = lane + 32 i of the
 // row's q | k | v part lies in part c / (h d / 8), head (c mod (h d / 8)) / (d / 8).
-// Two 16-bit values in a 32-bit word <-> floats, by value (no address taken, so a row's
-// words stay in registers).
-template <typename T>
-__device__ __forceinline__ float2 unpack2(uint32_t w) {
-  if constexpr (std::is_same<T, __nv_bfloat16>::value) {
-    return make_float2(__uint_as_float(w << 16), __uint_as_float(w & 0xffff0000u));
-  } else {
-    return __half22float2(__halves2half2(__ushort_as_half((unsigned short)(w & 0xffffu)),
-                                         __ushort_as_half((unsigned short)(w >> 16))));
-  }
-}
-template <typename T>
-__device__ __forceinline__ uint32_t pack2(float a, float b) {
-  if constexpr (std::is_same<T, __nv_bfloat16>::value) {
-    return (uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(a)) |
-           ((uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(b)) << 16);
-  } else {
-    return (uint32_t)__half_as_ushort(__float2half_rn(a)) | ((uint32_t)__half_as_ushort(__float2half_rn(b)) << 16);
-  }
-}
 template <typename T>
 __device__ __forceinline__ uint32_t silu2(uint32_t w) {
   const float2 f = unpack2<T>(w);
