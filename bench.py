@@ -380,6 +380,8 @@ def run_ours(args):
     if world == 1 and not args.no_decode and not args.no_triton_bar:
         torch.cuda.empty_cache()
         result["decode"]["reference_triton"] = run_triton_bar(dev)
+        torch.cuda.empty_cache()
+        result["c1_scans"] = run_triton_c1(V, dev)
     if world == 1 and not args.no_cpu_baseline:
         result["cpu_baseline"] = cpu_sample(tokens=args.cpu_tokens)
     if rank == 0:
@@ -856,6 +858,55 @@ def run_triton_bar(dev, steps=2):
             "us_per_layer_step": us, "us_per_step_12_layers_extrapolated": 12 * us,
             "us_per_token_12_layers_extrapolated": 12 * us / b, "steps_timed": steps,
             "host_wall_s": wall}
+
+
+def run_triton_c1(V, dev):
+    """Config 1's two mixer scans (b = 2, s = 512, 8 x 128 heads, D = 1024, fp32) through the
+    reference's own Triton launchers (baseline/_ref, unmodified; at D = 1024 CHAM takes the
+    host-looped tiled path, triton_kernels.py:552-597) and through this package's launchers,
+    on the same inputs, one timed call each after a warm-up (the reference's on a 2-token
+    prefix, for its JIT); CUDA events on the current stream."""
+    import torch
+    if not os.path.isdir(os.path.join(REF_DIR, "verace_v1")):
+        return {"unavailable": "the reference is not installed under baseline/_ref"}
+    if REF_DIR not in sys.path:
+        sys.path.append(REF_DIR)
+    try:
+        from verace_v1.serving import triton_kernels as TK
+    except Exception as e:        # noqa: BLE001 -- report why the timing could not be taken
+        return {"unavailable": f"reference Triton kernels not importable: {e!r}"[:300]}
+    b, s, h, d, D = 2, 512, CFG["heads"], CFG["head_dim"], CFG["holo"]
+    g = torch.Generator(device=dev).manual_seed(12)
+    nrm = torch.nn.functional.normalize
+    rn = lambda *sh: torch.randn(*sh, generator=g, device=dev)
+    sq, sk, sv = (nrm(rn(b, s, h, d), dim=-1) for _ in range(3))
+    dl = 0.1 * torch.sigmoid(rn(b, s, h))
+    cq, ck, cv = (nrm(rn(b, s, D), dim=-1) for _ in range(3))
+    gm = 0.1 * torch.sigmoid(rn(b, s))
+
+    def timed(fn):
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        out = fn()
+        e1.record()
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1), out
+
+    with torch.no_grad():
+        TK.launch_sssd_triton_scan(sq[:, :2], sk[:, :2], sv[:, :2], dl[:, :2])
+        TK.launch_cham_triton_update(cq[:, :2], ck[:, :2], cv[:, :2], gm[:, :2])
+        ref_ms, (ro_s, ro_c) = timed(lambda: (TK.launch_sssd_triton_scan(sq, sk, sv, dl)[0],
+                                              TK.launch_cham_triton_update(cq, ck, cv, gm)[0]))
+        V.launch_sssd_scan(sq, sk, sv, dl)
+        V.launch_cham_update(cq, ck, cv, gm)
+        ours_ms, (oo_s, oo_c) = timed(lambda: (V.launch_sssd_scan(sq, sk, sv, dl)[0],
+                                               V.launch_cham_update(cq, ck, cv, gm)[0]))
+    rel = lambda a, r: float((a.float() - r.float()).norm() / r.float().norm())
+    return {"workload": f"config 1's mixer scans: SSSD ({h}x{d}) + CHAM (D={D}) over b={b} x s={s}, fp32 "
+                        "inputs, no initial state",
+            "reference_triton_ms": ref_ms, "ours_ms": ours_ms, "ratio": ref_ms / ours_ms,
+            "rel_diff_sssd_out": rel(oo_s, ro_s), "rel_diff_cham_out": rel(oo_c, ro_c)}
 
 
 def run_reference(args):
