@@ -3,7 +3,7 @@
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
-Workload: the SSSD and CHAM sublayers of a 12-layer Verace V1
+Workload (benchmark config 2): the SSSD and CHAM sublayers of a 12-layer Verace V1
 stack (hidden 1024, 8 heads x 128, holographic width 1024) over a prefill batch of
 8 sequences x 2048 tokens in bf16 (fp32 recurrent state), random-init weights
 (seed 0), synthetic token embeddings (uniform ids over [0, 32000), seed 0).  One
@@ -15,7 +15,7 @@ token before layer 12, so every token runs all 12 layers.
 
 Unit: token-layers/s (one token through SSSD + CHAM of one layer).
 
-Decode (reported under "decode"): the same 12 layers, 64 items per
+Decode (benchmark config 3, reported under "decode"): the same 12 layers, 64 items per
 GPU, a 1024-token prompt prefilled with the scans, then 256 single-token steps with
 teacher-forced random ids, each step one CUDA graph of the layer glue and the decode
 kernels that update the resident states in place (verace_decode_step for the SSSD heads;
@@ -391,7 +391,7 @@ def run_ours(args):
 
 
 def run_model(args, V, dev, rank, world, barrier, max_over_ranks):
-    """BASELINE config 2 as the whole model: VeraceV1Model (12 layers of SSSD + CHAM +
+    """benchmark config 2 as the whole model: VeraceV1Model (12 layers of SSSD + CHAM +
     M-CMoE, ACDE halting at the default configuration, the LM head) prefill of the rank's
     8 x 2048 uniform-random ids, random init (seed 0), weights in bf16, through the drop-in
     model's forward.  Tokens/s over all ranks; the headline line times the SSSD + CHAM

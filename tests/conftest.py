@@ -72,7 +72,7 @@ def mcmoe_weights(g):
 
 
 def config1_case():
-    """BASELINE config 1 (one SSSD + CHAM layer, fp32, hidden 1024, 8 heads x 128, D = 1024,
+    """benchmark config 1 (one SSSD + CHAM layer, fp32, hidden 1024, 8 heads x 128, D = 1024,
     x = randn(2, 512, 1024) under seed 0, weights default-initialised under seed 0, SSSD
     first): (sssd module, cham module, x, golden dict) on the CPU.  The modules and x are
     re-created from the seeds, as tests/golden/make_golden.py built the reference's, and

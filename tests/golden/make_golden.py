@@ -287,7 +287,7 @@ def main():
         np.savez_compressed(os.path.join(HERE, "layer_golden.npz"), **ly)
     if want("config1"):
         # ------------------------------------------------------------------ config 1, full size
-        # One SSSD + CHAM layer in fp32 at the BASELINE configuration: hidden 1024, 8 heads x
+        # One SSSD + CHAM layer in fp32 at the benchmark configuration: hidden 1024, 8 heads x
         # 128, D = 1024, x = randn(2, 512, 1024) under seed 0, weights default-initialised
         # under seed 0 (SSSDAttention first, then ContinuousHolographicMemory, both fed x).
         # The reference's eager CHAM needs ~16 GB per 64 tokens at D = 1024, so it runs in

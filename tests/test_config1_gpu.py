@@ -1,4 +1,4 @@
-"""BASELINE config 1 at its own size on the GPU: one SSSD + CHAM layer in fp32, hidden
+"""benchmark config 1 at its own size on the GPU: one SSSD + CHAM layer in fp32, hidden
 1024, 8 heads x 128, D = 1024, x = randn(2, 512, 1024) under seed 0, weights seeded as
 the reference built them (checked against the reference's fingerprints).
 

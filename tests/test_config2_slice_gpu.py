@@ -1,4 +1,4 @@
-"""A slice of BASELINE config 2 on the GPU against the fp64 oracle: the bench's 12-layer
+"""A slice of benchmark config 2 on the GPU against the fp64 oracle: the bench's 12-layer
 SSSD -> CHAM chain (hidden 1024, 8 heads x 128, D = 1024, weights seeded and cast to bf16,
 token embeddings of uniform random ids) on 1 item x 256 tokens, bf16 activations and fp32
 recurrent states through the drop-in modules.

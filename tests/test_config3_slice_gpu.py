@@ -1,4 +1,4 @@
-"""A slice of BASELINE config 3 on the GPU against the fp64 oracle: one layer's SSSD
+"""A slice of benchmark config 3 on the GPU against the fp64 oracle: one layer's SSSD
 (8 heads x 128) and CHAM (D = 1024) states for 2 items, a 1024-token prompt prefilled by
 the scans, then 256 single-token decode steps through DecodeState with the bench's
 settings (bf16 inputs, the "unitary" CHAM readout Re(H q), hologram updates deferred and

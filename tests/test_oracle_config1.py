@@ -1,4 +1,4 @@
-"""Pins the CPU oracle at BASELINE config 1 (one SSSD + CHAM layer in fp32, hidden 1024,
+"""Pins the CPU oracle at benchmark config 1 (one SSSD + CHAM layer in fp32, hidden 1024,
 8 heads x 128, D = 1024, b = 2, s = 512) to the reference's own output at that size
 (tests/golden/config1_golden.npz, made by tests/golden/make_golden.py --only config1 from
 the reference's eager modules, CHAM fed in 64-token chunks through initial_hologram).

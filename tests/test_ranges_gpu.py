@@ -1,4 +1,4 @@
-"""Sequence-parallel scans (ranges.py) for long sequences on few chains (BASELINE
+"""Sequence-parallel scans (ranges.py) for long sequences on few chains (benchmark
 config 4's shape, shortened): the sequence is cut into ranges scanned side by side from
 the identity, the range products are chained in fp32, and the ranges are scanned again
 from the carried states.  Checked against the fp64 oracle and against the one-chain scan

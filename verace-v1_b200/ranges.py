@@ -1,4 +1,4 @@
-"""Sequence-parallel SSSD and CHAM scans for long sequences on few chains (BASELINE
+"""Sequence-parallel SSSD and CHAM scans for long sequences on few chains (benchmark
 config 4: one sequence of 65536 tokens, 16 SSSD heads, one hologram).
 
 The reference scans in O(log S) depth with a Blelloch prefix over the per-token factors
