@@ -14,7 +14,9 @@ contiguous ranges that run side by side as R independent chains:
    library GEMMs, a few per call);
 3. each range scanned again from its carried state S_r, giving every token's readout and
    the final state (the carried holograms are products of unitary factors, so the CHAM
-   launcher continues them on the tensor cores after its unitarity probe).
+   launcher continues them on the tensor cores after its unitarity probe).  Range 0 of a
+   single sequence that starts from the identity already has its readouts from step 1, so
+   step 3 then runs ranges 1..R-1 only.
 
 Both passes fill the GPU (b*R chains), which is what turns config 4 from a walk along one
 chain into work for all SMs.  The same split runs across GPUs (``group``): each rank
@@ -113,7 +115,7 @@ def sssd_scan_ranges(q, k, v, delta, initial_state: Optional[torch.Tensor], R: i
     n = R * L
     qp, kp, vp = (_pad(x, n).view(b * R, L, h, d) for x in (q, k, v))
     dp = _pad(delta.reshape(b, s, h).float(), n).view(b * R, L, h)
-    _, P = launch_sssd_scan(qp, kp, vp, dp, _ranges=False)            # [b*R, h, d, d]
+    out1, P = launch_sssd_scan(qp, kp, vp, dp, _ranges=False)         # [b*R, h, d, d]
     P = P.view(b, R, h, d, d)
     if initial_state is None:
         S0 = torch.eye(d, device=q.device, dtype=torch.float32).expand(b, h, d, d)
@@ -122,6 +124,12 @@ def sssd_scan_ranges(q, k, v, delta, initial_state: Optional[torch.Tensor], R: i
     if group is not None:
         S0 = _prior_product(_segment_product(P), S0, group)
     starts = _carry(P, S0)
+    if b == 1 and initial_state is None and group is None and R > 1:   # range 0's readouts are final
+        out1 = out1.view(R, L, h, d)
+        out, psi = launch_sssd_scan(qp[1:], kp[1:], vp[1:], dp[1:], initial_state=starts[0, 1:].contiguous(),
+                                    _ranges=False)
+        full = torch.cat([out1[:1], out], dim=0).view(1, n, h, d)
+        return full[:, :s], psi[-1:].contiguous()
     out, psi = launch_sssd_scan(qp, kp, vp, dp, initial_state=starts.view(b * R, h, d, d), _ranges=False)
     return out.view(b, n, h, d)[:, :s], psi.view(b, R, h, d, d)[:, -1].contiguous()
 
@@ -136,7 +144,7 @@ def cham_scan_ranges(q, k, v, gamma, initial_hologram: Optional[Tuple[torch.Tens
     n = R * L
     qp, kp, vp = (_pad(x, n).view(b * R, L, D) for x in (q, k, v))
     gp = _pad(gamma.reshape(b, s).float(), n).view(b * R, L)
-    _, (Pr, Pi) = launch_cham_update(qp, kp, vp, gp, _ranges=False)    # range products from I
+    out1, (Pr, Pi) = launch_cham_update(qp, kp, vp, gp, _ranges=False)   # range products from I
     P = torch.complex(Pr, Pi).view(b, R, D, D)
     del Pr, Pi
     if initial_hologram is None:
@@ -147,6 +155,13 @@ def cham_scan_ranges(q, k, v, gamma, initial_hologram: Optional[Tuple[torch.Tens
         S0 = _prior_product(_segment_product(P), S0, group)
     starts = _carry(P, S0).view(b * R, D, D)
     del P
+    if b == 1 and initial_hologram is None and group is None and R > 1:   # range 0's readouts are final
+        st = starts[1:]
+        out, (Hr, Hi) = launch_cham_update(qp[1:], kp[1:], vp[1:], gp[1:], initial_hologram=(st.real, st.imag),
+                                           _ranges=False)
+        full = torch.cat([out1.view(R, L, D)[:1], out], dim=0).view(1, n, D)
+        return full[:, :s], (Hr[-1:].contiguous(), Hi[-1:].contiguous())
+    del out1
     out, (Hr, Hi) = launch_cham_update(qp, kp, vp, gp, initial_hologram=(starts.real, starts.imag), _ranges=False)
     Hr = Hr.view(b, R, D, D)[:, -1].contiguous()
     Hi = Hi.view(b, R, D, D)[:, -1].contiguous()
