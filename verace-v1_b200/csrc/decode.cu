@@ -691,37 +691,81 @@ __global__ void __launch_bounds__(DT) lazy_pre_kernel(LazyArgs A) {
 }
 
 // The stripe (W = 64 columns when D is a multiple of 64, else 32) streams through NSTG
-// shared-memory stages of 16 KB (ROWS rows: re box | im box, W floats a row, no swizzle),
-// loaded by TMA: thread 0 keeps every stage in flight, so the read pass is not limited by
+// shared-memory stages of 16 KB (ROWS rows: re box | im box, W floats a row; unswizzled,
+// or for the tensor-core fold two 32-column swizzled boxes per plane, see sw_off), loaded by
+// TMA: thread 0 keeps every stage in flight, so the read pass is not limited by
 // the loads a thread can hold in registers.  Each thread takes two rows of four columns
 // per stage.  A folding step updates each stage in place and TMA-stores it back.  The
 // wider stripe halves the CTAs, and with them the per-CTA set-up (k, v, q and the pending
 // factors' columns) and reductions, for the same bytes streamed.
 constexpr int NSTG = 5;                      // stages
-template <int W>
+template <int W, bool MF = false>
 struct LazyGeom {
   static constexpr int TPR = W / 4;                 // threads per row
   static constexpr int RPG = DT / TPR;              // rows per row group
   static constexpr int ROWS = 2 * RPG;              // rows per stage
   static constexpr int STAGE = 2 * ROWS * W * 4;    // bytes per stage (16 KB)
-  // dynamic smem: stages | A rows of the stage (fold steps) [LP_MAX][2][ROWS], two buffers
-  // of [LP_MAX / 2][2][ROWS] when P <= LP_MAX / 2 | pending B over the stripe [P][4][W] |
+  // dynamic smem: stages | A rows of the stage (fold steps): fp32 [LP_MAX][2][ROWS], two
+  // buffers of [LP_MAX / 2][2][ROWS] when P <= LP_MAX / 2; with the tensor-core fold (MF) two
+  // buffers of three bf16 pieces [ROWS][8 words] | pending B over the stripe [P][4][W] |
   // ks [D] | vs [D] | barriers
   static constexpr int AS_OFF = NSTG * STAGE;
-  static constexpr int PBS_OFF = AS_OFF + LP_MAX * 2 * ROWS * 4;
+  static constexpr int AS_BYTES = MF ? 2 * 3 * ROWS * 8 * 4 : LP_MAX * 2 * ROWS * 4;
+  static constexpr int PBS_OFF = AS_OFF + AS_BYTES;
   __host__ __device__ static size_t ks_off(int P) { return PBS_OFF + (size_t)P * 4 * W * 4; }
   static size_t smem(int D, int P) { return ks_off(P) + 2 * (size_t)D * 4 + 8 * NSTG + 16; }
 };
 static_assert(LazyGeom<32>::STAGE == 16384 && LazyGeom<64>::STAGE == 16384, "16 KB stages");
+static_assert(LazyGeom<64, true>::ROWS == 32, "the tensor-core fold tiles a stage as 2 x 16 rows");
+
+// The tensor-core fold's stage layout: each plane of a 64-column stage is two 32-column
+// boxes of 32 rows x 128 bytes, stored by TMA with the 128-byte swizzle (16-byte chunk
+// index XOR row mod 8), so that the m16n8 accumulator fragments (eight rows by two chunks
+// per warp) and the read pass's float4s both spread over all banks.  Float offset of
+// (row r, column c) within a plane:
+__device__ __forceinline__ int sw_off(int r, int c) {
+  return (c >> 5) * 1024 + r * 32 + ((((c & 31) >> 2) ^ (r & 7)) << 2) + (c & 3);
+}
+
+// D += A B for one m16n8k16 tile, bf16 operands, fp32 accumulators (PTX mma.sync; the
+// fragment layouts are the ISA's: A rows gid / gid + 8, k pairs 2 tig (+8); B k pairs
+// 2 tig (+8), column gid; D rows gid / gid + 8, columns 2 tig, 2 tig + 1).
+__device__ __forceinline__ void mma_m16n8k16_bf16(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+      "{%0, %1, %2, %3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+// x = hi + mid + lo as three bf16 values (each the round-to-nearest of what the previous
+// ones leave; the residuals are exact in fp32), 24 significant bits in all.
+__device__ __forceinline__ void split3_bf16(float x, uint16_t& h, uint16_t& m, uint16_t& l) {
+  const __nv_bfloat16 bh = __float2bfloat16_rn(x);
+  const float r1 = x - __bfloat162float(bh);
+  const __nv_bfloat16 bm = __float2bfloat16_rn(r1);
+  const __nv_bfloat16 bl = __float2bfloat16_rn(r1 - __bfloat162float(bm));
+  h = __bfloat16_as_ushort(bh); m = __bfloat16_as_ushort(bm); l = __bfloat16_as_ushort(bl);
+}
 constexpr uint32_t LPOLLS = 1u << 22;
 
-template <typename T, int W>
+//
+// MF (bf16 steps, W = 64, P <= 8): the stages are in the swizzled layout of sw_off and a
+// folding step runs S += sum_j A_j B_j on the tensor cores, as a 32 x 64 x 2P product per
+// plane and stage (mma.sync m16n8k16; each warp one plane, 16 rows, 32 columns).  A (the
+// pending factors' k, v rows) enters as bf16 pieces hi + mid + lo (a bf16 step's k, v are
+// exact in the first; the others are zero and their products skipped, warp by warp), B
+// (the factors' columns over the stripe, fp32) as three bf16 pieces held in registers for
+// the whole pass.  The update is accumulated from zero and added to the state in fp32, so
+// the tensor cores' rounding is relative to the update, not to the state.
+template <typename T, int W, bool MF>
 __global__ void __launch_bounds__(DT, 2)
 lazy_cham_kernel(LazyArgs A, const __grid_constant__ CUtensorMap tm_r, const __grid_constant__ CUtensorMap tm_i) {
-  using G = LazyGeom<W>;
+  static_assert(!MF || W == 64, "the tensor-core fold tiles 64-column stripes");
+  using G = LazyGeom<W, MF>;
   constexpr int TPR = G::TPR, RPG = G::RPG, LROWS = G::ROWS, LSTAGE = G::STAGE;
-  extern __shared__ __align__(128) unsigned char lsm[];
-  float* as = reinterpret_cast<float*>(lsm + G::AS_OFF);   // [j][kv][row of the stage]
+  extern __shared__ __align__(1024) unsigned char lsm[];
+  float* as = reinterpret_cast<float*>(lsm + G::AS_OFF);   // [j][kv][row of the stage] (MF: bf16 pieces)
   float* pbs = reinterpret_cast<float*>(lsm + G::PBS_OFF);  // pending B_j over the stripe: [j][4][W]
   float* ks = reinterpret_cast<float*>(lsm + G::ks_off(A.P));
   float* vs = ks + A.D;
@@ -741,10 +785,36 @@ lazy_cham_kernel(LazyArgs A, const __grid_constant__ CUtensorMap tm_r, const __g
   auto stage = [&](int s) { return reinterpret_cast<float*>(lsm + s * LSTAGE); };
   auto issue = [&](int rb) {
     const int s = rb % NSTG;
+    const int y = item * D + rb * LROWS;
     tc::mbar_expect_tx(&full[s], LSTAGE);
-    tc::tma_load_2d(stage(s), &tm_r, stripe * W, item * D + rb * LROWS, &full[s]);
-    tc::tma_load_2d(stage(s) + LROWS * W, &tm_i, stripe * W, item * D + rb * LROWS, &full[s]);
+    if constexpr (MF) {   // per plane two 32-column boxes (x stays a multiple of 32 floats)
+      tc::tma_load_2d(stage(s), &tm_r, stripe * W, y, &full[s]);
+      tc::tma_load_2d(stage(s) + 1024, &tm_r, stripe * W + 32, y, &full[s]);
+      tc::tma_load_2d(stage(s) + 2048, &tm_i, stripe * W, y, &full[s]);
+      tc::tma_load_2d(stage(s) + 3072, &tm_i, stripe * W + 32, y, &full[s]);
+    } else {
+      tc::tma_load_2d(stage(s), &tm_r, stripe * W, y, &full[s]);
+      tc::tma_load_2d(stage(s) + LROWS * W, &tm_i, stripe * W, y, &full[s]);
+    }
   };
+  auto store = [&](int rb, const float* sr, const float* si) {
+    const int y = item * D + rb * LROWS;
+    if constexpr (MF) {
+      tc::tma_store_2d(&tm_r, stripe * W, y, sr);
+      tc::tma_store_2d(&tm_r, stripe * W + 32, y, sr + 1024);
+      tc::tma_store_2d(&tm_i, stripe * W, y, si);
+      tc::tma_store_2d(&tm_i, stripe * W + 32, y, si + 1024);
+    } else {
+      tc::tma_store_2d(&tm_r, stripe * W, y, sr);
+      tc::tma_store_2d(&tm_i, stripe * W, y, si);
+    }
+  };
+  // float offset of a thread's float4 (row i, columns 4 c8 ..) within a stage plane
+  auto xoff = [&](int i) { return MF ? sw_off(i, 4 * c8) : i * W + 4 * c8; };
+  if (MF && (tc::smem_addr(lsm) & 1023u)) {   // the swizzle needs 1024-byte aligned stages
+    if (tid == 0) atomicOr(&g_decode_status, 2u);   // (reported as a pass that did not run)
+    return;
+  }
   // The hologram stages depend on no earlier kernel of this step: they are requested
   // before griddepcontrol.wait, which (this kernel being launched as a programmatic
   // dependent of lazy_pre_kernel) returns once lazy_pre_kernel and, through it, the
@@ -797,20 +867,58 @@ lazy_cham_kernel(LazyArgs A, const __grid_constant__ CUtensorMap tm_r, const __g
   const int an = P * 2 * LROWS;            // A values per stage
   float apre[LP_MAX / 2];
   auto a_fetch = [&](int rb) {
+    if constexpr (MF) {   // (k_j, v_j) of row e % LROWS for factor j = e / LROWS, one pair a thread
+      const int e = tid;
+      if (e < P * LROWS) {
+        const float* src = pa + (size_t)(2 * (e / LROWS)) * D + rb * LROWS + e % LROWS;
+        apre[0] = __ldg(src);
+        apre[1] = __ldg(src + D);
+      }
+    } else {
 #pragma unroll
-    for (int u = 0; u < LP_MAX / 2; ++u) {
-      const int e = tid + DT * u;
-      if (e < an) apre[u] = __ldg(pa + (size_t)(e / LROWS) * D + rb * LROWS + e % LROWS);
+      for (int u = 0; u < LP_MAX / 2; ++u) {
+        const int e = tid + DT * u;
+        if (e < an) apre[u] = __ldg(pa + (size_t)(e / LROWS) * D + rb * LROWS + e % LROWS);
+      }
     }
   };
+  // MF: the A buffer of a stage is three arrays (hi, mid, lo) of [row][8 words], each word a
+  // (k_j, v_j) bf16 pair; word c = 2 (j & 3) + (j >> 2) of a row sits at position
+  // c ^ ((row >> 2) & 7), so that the writes (a warp: one factor, 32 rows) and the fragment
+  // reads (8 rows x 4 factors) both reach 32 distinct banks.
+  constexpr int AWORDS = LROWS * 8;      // words per piece array
+  auto a_word = [](int row, int c) { return row * 8 + (c ^ ((row >> 2) & 7)); };
   auto a_put = [&](int rb) {
-    float* dst = as + (rb & 1) * (LP_MAX / 2) * 2 * LROWS;
+    if constexpr (MF) {
+      uint32_t* dst = reinterpret_cast<uint32_t*>(as) + (rb & 1) * 3 * AWORDS;
+      const int e = tid;
+      if (e < P * LROWS) {
+        const int j = e / LROWS, row = e % LROWS;
+        const int wd = a_word(row, 2 * (j & 3) + (j >> 2));
+        uint16_t hk, mk, lk, hv, mv, lv;
+        split3_bf16(apre[0], hk, mk, lk);
+        split3_bf16(apre[1], hv, mv, lv);
+        dst[wd] = hk | ((uint32_t)hv << 16);
+        dst[AWORDS + wd] = mk | ((uint32_t)mv << 16);
+        dst[2 * AWORDS + wd] = lk | ((uint32_t)lv << 16);
+      }
+    } else {
+      float* dst = as + (rb & 1) * (LP_MAX / 2) * 2 * LROWS;
 #pragma unroll
-    for (int u = 0; u < LP_MAX / 2; ++u) {
-      const int e = tid + DT * u;
-      if (e < an) dst[e] = apre[u];
+      for (int u = 0; u < LP_MAX / 2; ++u) {
+        const int e = tid + DT * u;
+        if (e < an) dst[e] = apre[u];
+      }
     }
   };
+  if (MF && fold) {   // the words of factors j >= P (never written by a_put) are zero
+    uint32_t* aw = reinterpret_cast<uint32_t*>(as);
+    for (int e = tid; e < 2 * 3 * AWORDS; e += DT) {
+      const int row = (e % AWORDS) >> 3;
+      const int c = (e & 7) ^ ((row >> 2) & 7);
+      if ((c >> 1) + 4 * (c & 1) >= P) aw[e] = 0u;
+    }
+  }
   if (adbl) {
     a_fetch(0);
     a_put(0);
@@ -820,6 +928,35 @@ lazy_cham_kernel(LazyArgs A, const __grid_constant__ CUtensorMap tm_r, const __g
   // every read of the pending count is behind us: lazy_out_kernel may start (it waits for
   // this grid's completion before it reads what the stripes write)
   asm volatile("griddepcontrol.launch_dependents;");
+
+  // MF fold: this warp's plane, 16-row half of the stage, 32-column box; its B fragments
+  // (factor j = tig, tig + 4; column gid of each 8-column tile) in three bf16 pieces
+  const int gid = lane >> 2, tig = lane & 3;
+  const int fpl = w >> 2, fmt = (w >> 1) & 1, fnh = w & 1;
+  uint32_t bfr[3][4][2];
+#pragma unroll
+  for (int t = 0; t < 3; ++t)
+#pragma unroll
+    for (int nt = 0; nt < 4; ++nt) bfr[t][nt][0] = bfr[t][nt][1] = 0u;
+  if (MF && fold) {
+#pragma unroll
+    for (int nt = 0; nt < 4; ++nt)
+#pragma unroll
+      for (int hf = 0; hf < 2; ++hf) {
+        const int j = tig + 4 * hf, n = fnh * 32 + nt * 8 + gid;
+        float x0 = 0.f, x1 = 0.f;    // rows k = 2j (with k_j) and 2j + 1 (with v_j) of B
+        if (j < P) {
+          x0 = pbs[(j * 4 + fpl) * W + n];
+          x1 = pbs[(j * 4 + 2 + fpl) * W + n];
+        }
+        uint16_t h0, m0, l0, h1, m1, l1;
+        split3_bf16(x0, h0, m0, l0);
+        split3_bf16(x1, h1, m1, l1);
+        bfr[0][nt][hf] = h0 | ((uint32_t)h1 << 16);
+        bfr[1][nt][hf] = m0 | ((uint32_t)m1 << 16);
+        bfr[2][nt][hf] = l0 | ((uint32_t)l1 << 16);
+      }
+  }
 
   // ---- one pass: column sums kᵀS, vᵀS and the readout partials S_re q, folding first
   float acc[4][4];
@@ -836,14 +973,54 @@ lazy_cham_kernel(LazyArgs A, const __grid_constant__ CUtensorMap tm_r, const __g
     const bool got = tc::mbar_wait(&full[s], (rb / NSTG) & 1, LPOLLS);
     float* sr = stage(s);
     float* si = sr + LROWS * W;
+    if (MF && fold) {   // S += sum_j A_j B_j on the tensor cores, in place in the stage
+      const uint32_t* ab = reinterpret_cast<const uint32_t*>(as) + (rb & 1) * 3 * AWORDS;
+      const int r0 = fmt * 16 + gid;
+      uint32_t af[3][4];
+#pragma unroll
+      for (int t = 0; t < 3; ++t) {   // rows r0, r0 + 8; factors tig (k 2 tig, 2 tig + 1) and tig + 4
+        af[t][0] = ab[t * AWORDS + a_word(r0, 2 * tig)];
+        af[t][1] = ab[t * AWORDS + a_word(r0 + 8, 2 * tig)];
+        af[t][2] = ab[t * AWORDS + a_word(r0, 2 * tig + 1)];
+        af[t][3] = ab[t * AWORDS + a_word(r0 + 8, 2 * tig + 1)];
+      }
+      const bool use_m = __any_sync(0xffffffffu, (af[1][0] | af[1][1] | af[1][2] | af[1][3]) != 0u);
+      const bool use_l = __any_sync(0xffffffffu, (af[2][0] | af[2][1] | af[2][2] | af[2][3]) != 0u);
+      float* tile = (fpl ? si : sr) + fnh * 1024;
+#pragma unroll
+      for (int nt = 0; nt < 4; ++nt) {
+        float d[4] = {0.f, 0.f, 0.f, 0.f};   // smallest products first
+        if (use_l) mma_m16n8k16_bf16(d, af[2], bfr[0][nt][0], bfr[0][nt][1]);
+        if (use_m) {
+          mma_m16n8k16_bf16(d, af[1], bfr[1][nt][0], bfr[1][nt][1]);
+          mma_m16n8k16_bf16(d, af[1], bfr[0][nt][0], bfr[0][nt][1]);
+        }
+        mma_m16n8k16_bf16(d, af[0], bfr[2][nt][0], bfr[2][nt][1]);
+        mma_m16n8k16_bf16(d, af[0], bfr[1][nt][0], bfr[1][nt][1]);
+        mma_m16n8k16_bf16(d, af[0], bfr[0][nt][0], bfr[0][nt][1]);
+        // rows r0 and r0 + 8 (same swizzle phase), columns 8 nt + 2 tig + {0, 1} of the box
+        const int o = r0 * 32 + (((2 * nt + (tig >> 1)) ^ (r0 & 7)) << 2) + (tig & 1) * 2;
+        float2* p0 = reinterpret_cast<float2*>(tile + o);
+        float2* p1 = reinterpret_cast<float2*>(tile + o + 8 * 32);
+        float2 c0 = *p0, c1 = *p1;
+        c0.x += d[0]; c0.y += d[1]; c1.x += d[2]; c1.y += d[3];
+        *p0 = c0;
+        *p1 = c1;
+      }
+      __syncthreads();   // the folded stage, before the pass below reads other warps' rows
+      if (rb + 1 < NRB) {   // the other A buffer was last read in stage rb - 1
+        a_put(rb + 1);
+        if (rb + 2 < NRB) a_fetch(rb + 2);
+      }
+    }
     float4 xr2[2], xi2[2];
 #pragma unroll
     for (int h = 0; h < 2; ++h) {
       const int i = rp + RPG * h;
-      xr2[h] = *reinterpret_cast<const float4*>(sr + i * W + 4 * c8);
-      xi2[h] = *reinterpret_cast<const float4*>(si + i * W + 4 * c8);
+      xr2[h] = *reinterpret_cast<const float4*>(sr + xoff(i));
+      xi2[h] = *reinterpret_cast<const float4*>(si + xoff(i));
     }
-    if (fold) {   // S += sum_j A_j B_j; each factor's four columns of B serve both rows
+    if (!MF && fold) {   // S += sum_j A_j B_j; each factor's four columns of B serve both rows
       const float* asb = as;
       if (adbl) {
         asb = as + (rb & 1) * (LP_MAX / 2) * 2 * LROWS;
@@ -906,8 +1083,7 @@ lazy_cham_kernel(LazyArgs A, const __grid_constant__ CUtensorMap tm_r, const __g
       if (fold) {
         // stage rb leaves by TMA store; the stage stored one step earlier, whose store has
         // had a stage's compute to read it, takes the next load
-        tc::tma_store_2d(&tm_r, stripe * W, item * D + rb * LROWS, sr);
-        tc::tma_store_2d(&tm_i, stripe * W, item * D + rb * LROWS, si);
+        store(rb, sr, si);
         tc::bulk_commit();
         if (rb >= 1) {
           tc::bulk_wait_read<1>();
@@ -1214,8 +1390,9 @@ int launch_typed(const DecodeArgs& A, cudaStream_t st) {
   return check_launch("decode_step_kernel");
 }
 
-// one hologram plane as a [b*D rows][D] fp32 tensor, boxes of `cols` columns x `rows` rows, no swizzle
-int make_plane_map(CUtensorMap* m, const float* base, int b, int D, int cols, int rows) {
+// one hologram plane as a [b*D rows][D] fp32 tensor, boxes of `cols` columns x `rows` rows,
+// unswizzled or with the 128-byte swizzle (cols = 32)
+int make_plane_map(CUtensorMap* m, const float* base, int b, int D, int cols, int rows, bool swizzle128) {
   auto enc = tmap_encoder();
   VERACE_REQUIRE(enc != nullptr, VERACE_ERR_CUDA, "cuTensorMapEncodeTiled is not available");
   const cuuint64_t dims[2] = {(cuuint64_t)D, (cuuint64_t)b * D};
@@ -1223,8 +1400,8 @@ int make_plane_map(CUtensorMap* m, const float* base, int b, int D, int cols, in
   const cuuint32_t box[2] = {(cuuint32_t)cols, (cuuint32_t)rows};
   const cuuint32_t es[2] = {1, 1};
   CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(base), dims, strides, box, es,
-                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
-                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   VERACE_REQUIRE(r == CUDA_SUCCESS, VERACE_ERR_CUDA, "cuTensorMapEncodeTiled (hologram plane) failed: %d", (int)r);
   return VERACE_OK;
 }
@@ -1348,13 +1525,14 @@ extern "C" int verace_decode_step(const void* sssd_q, const void* sssd_k, const 
 }
 
 // lazy_pre_kernel, lazy_cham_kernel over (item, stripe) CTAs with the widest stripe D
-// allows, then lazy_out_kernel over the items.
-template <typename T, int W>
+// allows (MF: the tensor-core fold and its swizzled stages), then lazy_out_kernel over the
+// items.
+template <typename T, int W, bool MF>
 int launch_lazy_w(const LazyArgs& A, const float* h_re, const float* h_im, cudaStream_t st) {
-  using G = LazyGeom<W>;
+  using G = LazyGeom<W, MF>;
   CUtensorMap mr, mi;
-  if (int rc = make_plane_map(&mr, h_re, A.b, A.D, W, G::ROWS)) return rc;
-  if (int rc = make_plane_map(&mi, h_im, A.b, A.D, W, G::ROWS)) return rc;
+  if (int rc = make_plane_map(&mr, h_re, A.b, A.D, MF ? 32 : W, G::ROWS, MF)) return rc;
+  if (int rc = make_plane_map(&mi, h_im, A.b, A.D, MF ? 32 : W, G::ROWS, MF)) return rc;
   // all three launched as programmatic dependents of the kernel before them
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -1369,12 +1547,13 @@ int launch_lazy_w(const LazyArgs& A, const float* h_re, const float* h_im, cudaS
   VERACE_CUDA(cudaLaunchKernelEx(&cfg, lazy_pre_kernel<T>, A));   // (also keeps the pending counts)
   if (int rc = check_launch("lazy_pre_kernel")) return rc;
   const size_t smem = G::smem(A.D, A.P);
-  VERACE_CUDA(cudaFuncSetAttribute(lazy_cham_kernel<T, W>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  VERACE_CUDA(cudaFuncSetAttribute(lazy_cham_kernel<T, W, MF>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                   (int)smem));
   LazyArgs B = A;
   B.nst = A.D / W;
   cfg.gridDim = dim3((unsigned)(A.b * B.nst));
   cfg.dynamicSmemBytes = smem;
-  VERACE_CUDA(cudaLaunchKernelEx(&cfg, lazy_cham_kernel<T, W>, B, mr, mi));
+  VERACE_CUDA(cudaLaunchKernelEx(&cfg, lazy_cham_kernel<T, W, MF>, B, mr, mi));
   if (int rc = check_launch("lazy_cham_kernel")) return rc;
   cfg.gridDim = dim3((unsigned)((A.D + DT - 1) / DT), (unsigned)A.b);
   cfg.dynamicSmemBytes = 2 * (size_t)A.D * sizeof(float);
@@ -1383,7 +1562,11 @@ int launch_lazy_w(const LazyArgs& A, const float* h_re, const float* h_im, cudaS
 }
 template <typename T>
 int launch_lazy(const LazyArgs& A, const float* h_re, const float* h_im, cudaStream_t st) {
-  return A.D % 64 == 0 ? launch_lazy_w<T, 64>(A, h_re, h_im, st) : launch_lazy_w<T, 32>(A, h_re, h_im, st);
+  if (A.D % 64 != 0) return launch_lazy_w<T, 32, false>(A, h_re, h_im, st);
+  if constexpr (std::is_same<T, __nv_bfloat16>::value) {
+    if (A.P <= LP_MAX / 2) return launch_lazy_w<T, 64, true>(A, h_re, h_im, st);
+  }
+  return launch_lazy_w<T, 64, false>(A, h_re, h_im, st);
 }
 
 extern "C" size_t verace_decode_lazy_workspace(int b, int D) {
