@@ -654,8 +654,8 @@ def run_decode(args, layers, embed, V, dev, rank, barrier, max_over_ranks):
                 q, k, v, dl = sm.project(nrm)
                 o = st.step_sssd(l, q, k, v, dl)
                 nrm = V.add_rmsnorm(hcur, sm.finish(o.view(b, 1, nh, d)), out_norm=L["cham_norm"])
-                q, k, v, g = cm.project(nrm)
-                rec = st.step_cham(l, q, k, v, g)
+                # the projection epilogue inside the deferred step's first kernel
+                rec = st.step_cham_projected(l, cm.projection(nrm))
                 nxt = layers[l + 1]["sssd_norm"] if l + 1 < nl else None
                 nrm = V.add_rmsnorm(hcur, cm.w_out(rec.view(b, 1, D)), y_norm=cm.norm, out_norm=nxt)
             return hcur

@@ -225,6 +225,15 @@ VERACE_API int verace_decode_cham_lazy(const void* cham_q, const void* cham_k, c
                                        size_t workspace_bytes, void* stream);
 VERACE_API int verace_decode_cham_flush(float* h_re, float* h_im, void* pending, int P, int b, int D,
                                         void* stream);
+/* The same step from the layer's raw projection rows, with the projection epilogue of
+ * ContinuousHolographicMemory.project (verace_v1/modules/cham_memory.py:129-153: SiLU on v,
+ * q, k, v L2-normalised, gamma = 0.1 * sigmoid) folded into the step's first kernel: one
+ * launch fewer than verace_mixer_prologue + verace_decode_cham_lazy, the same arithmetic
+ * (SiLU rounded to dtype as the reference's SiLU output is; normalised values rounded to
+ * dtype).  y: [b, ld] (dtype), row = q | k | v (D each) | gate; ld >= 3 D + 1. */
+VERACE_API int verace_decode_cham_lazy_projected(const void* y, long long ld, float* h_re, float* h_im,
+                                                 void* pending, int P, void* cham_out, int b, int D, int dtype,
+                                                 void* workspace, size_t workspace_bytes, void* stream);
 
 /* ------------------------------------------------------------------------------
  * Block glue: the RMSNorms and residual adds around the two mixers

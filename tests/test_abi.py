@@ -155,3 +155,23 @@ def test_mcmoe_rejects_bad_arguments_without_a_device():
     assert L.verace_mcmoe_workspace(4, 100, 64, 32, 1) == 256            # direct path: none
     assert L.verace_situ_glu(fake, fake, 4, fake, 2, 8, 4.0, 25.0, 1, None) == 1 and "ld" in _err()
     assert L.verace_situ_glu(fake, fake, 8, fake, 2, 8, 4.0, 25.0, 5, None) == 1 and "dtype" in _err()
+
+
+@host_only
+def test_projected_lazy_decode_rejects_bad_arguments_without_a_device():
+    L = _lib.lib()
+    fake = ctypes.c_void_p(256)
+    ws = L.verace_decode_lazy_workspace(4, 1024)
+    f = [fake, fake, fake]
+    assert L.verace_decode_cham_lazy_projected(fake, 3080, *f, 0, fake, 4, 1024, 1, fake, ws, None) == 1
+    assert "pending depth" in _err()
+    assert L.verace_decode_cham_lazy_projected(fake, 3072, *f, 8, fake, 4, 1024, 1, fake, ws, None) == 1
+    assert "row stride" in _err()
+    assert L.verace_decode_cham_lazy_projected(None, 3080, *f, 8, fake, 4, 1024, 1, fake, ws, None) == 1
+    assert L.verace_decode_cham_lazy_projected(fake, 3080, *f, 8, fake, 4, 1024, 7, fake, ws, None) == 1
+    assert "dtype" in _err()
+    assert L.verace_decode_cham_lazy_projected(fake, 3080, *f, 8, fake, 4, 80, 1, fake, ws, None) == 2
+    assert "holographic" in _err()
+    assert L.verace_decode_cham_lazy_projected(fake, 3080, *f, 8, fake, 4, 1024, 1, fake, 16, None) == 4
+    assert "workspace" in _err()
+    assert L.verace_decode_cham_lazy_projected(None, 0, None, None, None, 8, None, 0, 1024, 1, None, 0, None) == 0

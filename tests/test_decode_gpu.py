@@ -297,3 +297,33 @@ def test_decode_state_defers_unitary_steps_and_flushes_for_layer_states():
     o_l = lazy.step_cham(0, cq[:, 0].float(), ck[:, 0].float(), cv[:, 0].float(), g[:, 0], mode="first_order")
     o_e = eager.step_cham(0, cq[:, 0].float(), ck[:, 0].float(), cv[:, 0].float(), g[:, 0], mode="first_order")
     assert rel_fro(to_np(o_l), to_np(o_e)) <= 1e-5
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("b,D,P", [(3, 256, 4), (2, 1024, 8)])
+def test_projected_lazy_step_matches_prologue_then_lazy_step(dtype, b, D, P):
+    """verace_decode_cham_lazy_projected (the projection epilogue inside the step's first
+    kernel) against the mixer prologue followed by verace_decode_cham_lazy, over 19 steps
+    from a unitary hologram (folds included; one token's k non-finite): outputs, and the
+    planes after a flush."""
+    n = 19
+    ld = 3 * D + 1 + 7                         # q | k | v | gate, padded to a multiple of 8
+    g = torch.Generator().manual_seed(830 + D + P)
+    ys = (torch.randn(n, b, ld, generator=g) * 0.3).to("cuda", dtype)
+    ys[6, b - 1, D + 11] = float("nan")        # a k element of the last item at step 6
+    hr0, hi0 = _holo(_unitary(b, D, 831))
+    fr, fi = hr0.clone(), hi0.clone()
+    rr, ri = hr0.clone(), hi0.clone()
+    pf, pr = V.pending_storage(b, D, P), V.pending_storage(b, D, P)
+    tol_y = 1e-5 if dtype == torch.float32 else 1e-2
+    for t in range(n):
+        yf = V.launch_decode_cham_lazy_projected(ys[t], fr, fi, pf, P)
+        q, k, v, gm = V.kernels.mixer_prologue(ys[t], 1, D, 1, True)
+        yr = V.launch_decode_cham_lazy(q, k, v, gm, rr, ri, pr, P)
+        assert yf.dtype == dtype and tuple(yf.shape) == (b, D)
+        assert rel_fro(to_np(yf), to_np(yr)) <= tol_y, t
+    assert V.device_status() == 0
+    V.flush_pending(fr, fi, pf, P)
+    V.flush_pending(rr, ri, pr, P)
+    tol_h = 1e-6 if dtype == torch.float32 else 1e-3
+    assert rel_fro(to_np(fr) + 1j * to_np(fi), to_np(rr) + 1j * to_np(ri)) <= tol_h

@@ -41,6 +41,8 @@ _SIGNATURES = {
     "verace_decode_pending_bytes": (_c_size, [_i, _i, _i]),
     "verace_decode_cham_lazy": (_i, [_p] * 7 + [_i, _p, _i, _i, _i, _p, _c_size, _p]),
     "verace_decode_cham_flush": (_i, [_p, _p, _p, _i, _i, _i, _p]),
+    "verace_decode_cham_lazy_projected": (_i, [_p, ctypes.c_longlong, _p, _p, _p, _i, _p, _i, _i, _i, _p, _c_size,
+                                               _p]),
     "verace_rmsnorm": (_i, [_p, _p, _p, ctypes.c_longlong, _i, ctypes.c_float, _i, _p]),
     "verace_add_rmsnorm": (_i, [_p, _p, _i, _p, ctypes.c_float, _p, ctypes.c_float, _p, ctypes.c_longlong, _i, _i,
                                 _p]),

@@ -38,6 +38,13 @@ class ContinuousHolographicMemory(nn.Module):
         self.w_out = nn.Linear(holographic_dim, hidden_dim, bias=False)
         self.norm = nn.RMSNorm(hidden_dim)
 
+    def projection(self, x: torch.Tensor) -> torch.Tensor:
+        """The concatenated projection y = x [W_q; W_k; W_v; W_gamma]ᵀ, [b, s, ld] (rows
+        q | k | v | gate, zero-padded to a multiple of 8): the GEMM of :meth:`project`
+        without its epilogue, as the deferred decode step consumes it."""
+        W = concat_weights(self, [self.w_q.weight, self.w_k.weight, self.w_v.weight, self.w_gamma.weight])
+        return F.linear(x, W)
+
     def project(self, x: torch.Tensor, active_mask: Optional[torch.Tensor] = None):
         """q, k, v [b, s, D] and gamma [b, s] (cham_memory.py:129-153): one GEMM with the
         concatenated projection weights, then the fused normalisation/SiLU/gate pass."""

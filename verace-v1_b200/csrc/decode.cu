@@ -580,6 +580,8 @@ struct LazyArgs {
   float* part;                 // [b][D/32][D] readout partials
   float* cqp;                  // [b][D/32][4] per stripe: kᵀH q (re, im), vᵀH q (re, im)
   int* pcold;                  // [b] the pending counts as this step found them
+  const void* y; long long yld;   // projected steps: the raw projection rows (q | k | v | gate)
+  void* pq; void* pk; void* pv; float* pg;   // ... and where lazy_pre_kernel leaves q, k, v, gamma
   int b, D, P, nst;            // nst: column stripes of lazy_cham_kernel
 };
 
@@ -649,31 +651,92 @@ __device__ __forceinline__ void load_kvq(const LazyArgs& A, size_t voff, int D, 
 // (item, factor slot) (slots past the item's count return at once), each thread a few
 // rows of the six contiguous vectors, then a block reduction.  The slot-0 CTA of each item
 // also keeps the item's pending count for lazy_out_kernel (which rewrites the count).
-template <typename T>
+//
+// PROJ: the step starts from the layer's raw projection row y = q | k | v | gate and this
+// kernel is also its projection epilogue (the mixer prologue's CHAM row, one launch fewer):
+// v through SiLU rounded to the input type (as the reference's SiLU output is), q, k, v
+// L2-normalised (eps 1e-12) and rounded to the input type, gamma = 0.1 sigmoid(y_gate)
+// (cham_memory.py:129-153).  Every CTA of the item that has a dot product to form
+// normalises the row itself (the same threads and order, so bitwise alike) and the slot-0
+// CTA stores q, k, v and gamma for the two kernels after it.
+template <typename T, bool PROJ>
 __global__ void __launch_bounds__(DT) lazy_pre_kernel(LazyArgs A) {
   __shared__ float red[DT / 32][6];
+  __shared__ float nsc[DT / 32][4];
+  constexpr int NPT = MAXD / DT;   // row elements per thread (PROJ)
   const int D = A.D, P = A.P;
   const int item = blockIdx.x / P, j = blockIdx.x % P;
   const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
-  // launched as a programmatic dependent of the projection epilogue (k, v, q); the stripe
-  // kernel that follows may start its hologram loads once every CTA here has started
+  // launched as a programmatic dependent of the projection epilogue (k, v, q) or, PROJ, of
+  // the projection itself; the stripe kernel that follows may start its hologram loads
+  // once every CTA here has started
   asm volatile("griddepcontrol.launch_dependents;");
   asm volatile("griddepcontrol.wait;" ::: "memory");
   const int p = A.pcount[item];
   if (j == 0 && tid == 0) A.pcold[item] = p;
-  if (p >= P || j >= p) return;       // a folding step needs none of them
+  const bool dots = p < P && j < p;   // (a folding step needs none of them)
+  if (!dots && !(PROJ && j == 0)) return;
   const size_t voff = (size_t)item * D;
+  float nq[NPT], nk[NPT], nv[NPT];
+  if constexpr (PROJ) {
+    const size_t yr = (size_t)item * A.yld;
+    float ss[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int u = 0; u < NPT; ++u) {
+      const int i = tid + DT * u;
+      nq[u] = nk[u] = nv[u] = 0.f;
+      if (i < D) {
+        nq[u] = ld1<T>(A.y, yr + i);
+        nk[u] = ld1<T>(A.y, yr + D + i);
+        const float xv = ld1<T>(A.y, yr + 2 * (size_t)D + i);
+        nv[u] = to_f32(from_f32<T>(xv / (1.f + expf(-xv))));
+        ss[0] += nq[u] * nq[u]; ss[1] += nk[u] * nk[u]; ss[2] += nv[u] * nv[u];
+      }
+    }
+    bool all = true;
+    block_sum4(ss, all, nsc);
+    const float iq = 1.f / fmaxf(sqrtf(ss[0]), 1e-12f), ik = 1.f / fmaxf(sqrtf(ss[1]), 1e-12f),
+                iv = 1.f / fmaxf(sqrtf(ss[2]), 1e-12f);
+#pragma unroll
+    for (int u = 0; u < NPT; ++u) {
+      const int i = tid + DT * u;
+      if (i < D) {
+        const T tq = from_f32<T>(nq[u] * iq), tk = from_f32<T>(nk[u] * ik), tv = from_f32<T>(nv[u] * iv);
+        nq[u] = to_f32(tq); nk[u] = to_f32(tk); nv[u] = to_f32(tv);
+        if (j == 0) {
+          static_cast<T*>(A.pq)[voff + i] = tq;
+          static_cast<T*>(A.pk)[voff + i] = tk;
+          static_cast<T*>(A.pv)[voff + i] = tv;
+        }
+      }
+    }
+    if (j == 0 && tid == 0) A.pg[item] = 0.1f * (1.f / (1.f + expf(-ld1<T>(A.y, yr + 3 * (size_t)D))));
+    if (!dots) return;
+  }
   const float* a0 = A.pa + ((size_t)item * P + j) * 2 * D;
   const float* a1 = a0 + D;
   const float* b0 = A.pb + ((size_t)item * P + j) * 4 * D;   // Re(B_j0)
   const float* b1 = b0 + 2 * (size_t)D;                       // Re(B_j1)
   float x[6] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f};   // k.k_j, k.v_j, v.k_j, v.v_j, Re(B_j0) q, Re(B_j1) q
+  if constexpr (PROJ) {
+#pragma unroll
+    for (int u = 0; u < NPT; ++u) {
+      const int i = tid + DT * u;
+      if (i < D) {
+        const float kx = nk[u], vx = nv[u], qx = nq[u];
+        const float y0 = a0[i], y1 = a1[i];
+        x[0] += kx * y0; x[1] += kx * y1; x[2] += vx * y0; x[3] += vx * y1;
+        x[4] += b0[i] * qx; x[5] += b1[i] * qx;
+      }
+    }
+  } else {
 #pragma unroll 4
-  for (int i = tid; i < D; i += DT) {
-    const float kx = ld1<T>(A.ck, voff + i), vx = ld1<T>(A.cv, voff + i), qx = ld1<T>(A.cq, voff + i);
-    const float y0 = a0[i], y1 = a1[i];
-    x[0] += kx * y0; x[1] += kx * y1; x[2] += vx * y0; x[3] += vx * y1;
-    x[4] += b0[i] * qx; x[5] += b1[i] * qx;
+    for (int i = tid; i < D; i += DT) {
+      const float kx = ld1<T>(A.ck, voff + i), vx = ld1<T>(A.cv, voff + i), qx = ld1<T>(A.cq, voff + i);
+      const float y0 = a0[i], y1 = a1[i];
+      x[0] += kx * y0; x[1] += kx * y1; x[2] += vx * y0; x[3] += vx * y1;
+      x[4] += b0[i] * qx; x[5] += b1[i] * qx;
+    }
   }
 #pragma unroll
   for (int e = 0; e < 6; ++e) {
@@ -1407,7 +1470,7 @@ int make_plane_map(CUtensorMap* m, const float* base, int b, int D, int cols, in
 }
 
 struct LazyWs {
-  size_t part, cqp, cnt, g, bq, total;
+  size_t part, cqp, cnt, g, bq, pq, pk, pv, pg, total;
 };
 
 LazyWs lazy_ws_layout(int b, int D) {
@@ -1419,6 +1482,11 @@ LazyWs lazy_ws_layout(int b, int D) {
   L.cnt = off;  off = align_up(off + (size_t)b * sizeof(int), 256);
   L.g = off;    off = align_up(off + (size_t)b * LP_MAX * 4 * sizeof(float), 256);
   L.bq = off;   off = align_up(off + (size_t)b * LP_MAX * 2 * sizeof(float), 256);
+  // projected steps: q, k, v (at most fp32) and gamma as the pre-pass leaves them
+  L.pq = off;   off = align_up(off + (size_t)b * D * sizeof(float), 256);
+  L.pk = off;   off = align_up(off + (size_t)b * D * sizeof(float), 256);
+  L.pv = off;   off = align_up(off + (size_t)b * D * sizeof(float), 256);
+  L.pg = off;   off = align_up(off + (size_t)b * sizeof(float), 256);
   L.total = off + 256;
   return L;
 }
@@ -1544,7 +1612,10 @@ int launch_lazy_w(const LazyArgs& A, const float* h_re, const float* h_im, cudaS
   cfg.blockDim = dim3(DT);
   cfg.gridDim = dim3((unsigned)(A.b * A.P));
   cfg.dynamicSmemBytes = 0;
-  VERACE_CUDA(cudaLaunchKernelEx(&cfg, lazy_pre_kernel<T>, A));   // (also keeps the pending counts)
+  if (A.y != nullptr)
+    VERACE_CUDA(cudaLaunchKernelEx(&cfg, lazy_pre_kernel<T, true>, A));   // (also keeps the pending counts)
+  else
+    VERACE_CUDA(cudaLaunchKernelEx(&cfg, lazy_pre_kernel<T, false>, A));
   if (int rc = check_launch("lazy_pre_kernel")) return rc;
   const size_t smem = G::smem(A.D, A.P);
   VERACE_CUDA(cudaFuncSetAttribute(lazy_cham_kernel<T, W, MF>, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -1579,31 +1650,27 @@ extern "C" size_t verace_decode_pending_bytes(int b, int D, int P) {
   return pending_bytes(b, D, P);
 }
 
-extern "C" int verace_decode_cham_lazy(const void* cham_q, const void* cham_k, const void* cham_v, const float* gamma,
-                                       float* h_re, float* h_im, void* pending, int P, void* cham_out, int b, int D,
-                                       int dtype, void* workspace, size_t workspace_bytes, void* stream) {
-  VERACE_REQUIRE(b >= 0 && D >= 0, VERACE_ERR_INVALID, "verace_decode_cham_lazy: invalid sizes b=%d D=%d", b, D);
-  VERACE_REQUIRE(dtype == VERACE_F32 || dtype == VERACE_BF16 || dtype == VERACE_F16, VERACE_ERR_INVALID,
-                 "verace_decode_cham_lazy: unknown dtype %d", dtype);
-  VERACE_REQUIRE(P >= 1 && P <= LP_MAX, VERACE_ERR_INVALID,
-                 "verace_decode_cham_lazy: pending depth %d outside [1, %d]", P, LP_MAX);
-  if (b == 0 || D == 0) return VERACE_OK;
-  VERACE_REQUIRE(cham_q && cham_k && cham_v && gamma && h_re && h_im && pending && cham_out, VERACE_ERR_INVALID,
-                 "verace_decode_cham_lazy: NULL pointer");
+// The shared part of the two deferred-update entry points: A carries the step's inputs
+// (q, k, v, gamma, or the projection rows y).
+static int cham_lazy_run(const char* fn, LazyArgs A, float* h_re, float* h_im, void* pending, int P,
+                         void* cham_out, int b, int D, int dtype, void* workspace, size_t workspace_bytes,
+                         void* stream) {
+  VERACE_REQUIRE(h_re && h_im && pending && cham_out, VERACE_ERR_INVALID, "%s: NULL pointer", fn);
   VERACE_REQUIRE(D % CWD == 0 && D <= MAXD, VERACE_ERR_UNSUPPORTED,
-                 "verace_decode_cham_lazy: holographic dim %d unsupported (a multiple of %d, at most %d)", D, CWD,
-                 MAXD);
+                 "%s: holographic dim %d unsupported (a multiple of %d, at most %d)", fn, D, CWD, MAXD);
   VERACE_REQUIRE((((uintptr_t)h_re | (uintptr_t)h_im | (uintptr_t)pending) & 15) == 0, VERACE_ERR_INVALID,
-                 "verace_decode_cham_lazy: hologram and pending storage must be 16-byte aligned");
+                 "%s: hologram and pending storage must be 16-byte aligned", fn);
   const size_t need = verace_decode_lazy_workspace(b, D);
   VERACE_REQUIRE(workspace != nullptr && workspace_bytes >= need, VERACE_ERR_WORKSPACE,
-                 "verace_decode_cham_lazy: workspace of %zu bytes required, %zu given", need,
-                 workspace ? workspace_bytes : (size_t)0);
+                 "%s: workspace of %zu bytes required, %zu given", fn, need, workspace ? workspace_bytes : (size_t)0);
   cudaStream_t st = (cudaStream_t)stream;
   const LazyWs L = lazy_ws_layout(b, D);
   char* base = (char*)align_up((size_t)workspace, 256);
-  LazyArgs A{};
-  A.cq = cham_q; A.ck = cham_k; A.cv = cham_v; A.gamma = gamma; A.hr = h_re; A.hi = h_im; A.cout = cham_out;
+  if (A.y != nullptr) {   // the pre-pass leaves q, k, v, gamma in the workspace for the others
+    A.pq = base + L.pq; A.pk = base + L.pk; A.pv = base + L.pv; A.pg = (float*)(base + L.pg);
+    A.cq = A.pq; A.ck = A.pk; A.cv = A.pv; A.gamma = A.pg;
+  }
+  A.hr = h_re; A.hi = h_im; A.cout = cham_out;
   pending_ptrs(pending, b, D, P, &A.pcount, &A.pa, &A.pb);
   A.g = (float*)(base + L.g);
   A.bq = (float*)(base + L.bq);
@@ -1616,6 +1683,41 @@ extern "C" int verace_decode_cham_lazy(const void* cham_q, const void* cham_k, c
     case VERACE_BF16: return launch_lazy<__nv_bfloat16>(A, h_re, h_im, st);
     default: return launch_lazy<__half>(A, h_re, h_im, st);
   }
+}
+
+extern "C" int verace_decode_cham_lazy(const void* cham_q, const void* cham_k, const void* cham_v, const float* gamma,
+                                       float* h_re, float* h_im, void* pending, int P, void* cham_out, int b, int D,
+                                       int dtype, void* workspace, size_t workspace_bytes, void* stream) {
+  VERACE_REQUIRE(b >= 0 && D >= 0, VERACE_ERR_INVALID, "verace_decode_cham_lazy: invalid sizes b=%d D=%d", b, D);
+  VERACE_REQUIRE(dtype == VERACE_F32 || dtype == VERACE_BF16 || dtype == VERACE_F16, VERACE_ERR_INVALID,
+                 "verace_decode_cham_lazy: unknown dtype %d", dtype);
+  VERACE_REQUIRE(P >= 1 && P <= LP_MAX, VERACE_ERR_INVALID,
+                 "verace_decode_cham_lazy: pending depth %d outside [1, %d]", P, LP_MAX);
+  if (b == 0 || D == 0) return VERACE_OK;
+  VERACE_REQUIRE(cham_q && cham_k && cham_v && gamma, VERACE_ERR_INVALID, "verace_decode_cham_lazy: NULL pointer");
+  LazyArgs A{};
+  A.cq = cham_q; A.ck = cham_k; A.cv = cham_v; A.gamma = gamma;
+  return cham_lazy_run("verace_decode_cham_lazy", A, h_re, h_im, pending, P, cham_out, b, D, dtype, workspace,
+                       workspace_bytes, stream);
+}
+
+extern "C" int verace_decode_cham_lazy_projected(const void* y, long long ld, float* h_re, float* h_im,
+                                                 void* pending, int P, void* cham_out, int b, int D, int dtype,
+                                                 void* workspace, size_t workspace_bytes, void* stream) {
+  VERACE_REQUIRE(b >= 0 && D >= 0, VERACE_ERR_INVALID, "verace_decode_cham_lazy_projected: invalid sizes b=%d D=%d",
+                 b, D);
+  VERACE_REQUIRE(dtype == VERACE_F32 || dtype == VERACE_BF16 || dtype == VERACE_F16, VERACE_ERR_INVALID,
+                 "verace_decode_cham_lazy_projected: unknown dtype %d", dtype);
+  VERACE_REQUIRE(P >= 1 && P <= LP_MAX, VERACE_ERR_INVALID,
+                 "verace_decode_cham_lazy_projected: pending depth %d outside [1, %d]", P, LP_MAX);
+  if (b == 0 || D == 0) return VERACE_OK;
+  VERACE_REQUIRE(y != nullptr, VERACE_ERR_INVALID, "verace_decode_cham_lazy_projected: NULL pointer");
+  VERACE_REQUIRE(ld >= 3LL * D + 1, VERACE_ERR_INVALID,
+                 "verace_decode_cham_lazy_projected: row stride %lld shorter than q | k | v | gate", ld);
+  LazyArgs A{};
+  A.y = y; A.yld = ld;
+  return cham_lazy_run("verace_decode_cham_lazy_projected", A, h_re, h_im, pending, P, cham_out, b, D, dtype,
+                       workspace, workspace_bytes, stream);
 }
 
 extern "C" int verace_decode_cham_flush(float* h_re, float* h_im, void* pending, int P, int b, int D, void* stream) {

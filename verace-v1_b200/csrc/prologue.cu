@@ -131,7 +131,8 @@ mixer_prologue_kernel(const T* __restrict__ y, long long ld, T* __restrict__ q, 
         if (active && cc < nc) {
 #pragma unroll
           for (int j = 0; j < 8; ++j) {
-            if (act) x[u][i][j] = silu_f(x[u][i][j]);
+            if (act) x[u][i][j] = to_f32(from_f32<T>(silu_f(x[u][i][j])));   // in the input type, as the
+                                                                            // reference's SiLU output is
             ss += x[u][i][j] * x[u][i][j];
           }
         }

@@ -174,6 +174,34 @@ def launch_decode_cham_lazy(q, k, v, gamma, H_real, H_imag, pending: torch.Tenso
     return out
 
 
+def launch_decode_cham_lazy_projected(y: torch.Tensor, H_real, H_imag, pending: torch.Tensor, P: int,
+                                      workspace: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """:func:`launch_decode_cham_lazy` from the layer's raw projection rows y [b, ld] (or
+    [b, 1, ld]; row = q | k | v | gate of ContinuousHolographicMemory's concatenated
+    projection, :meth:`ContinuousHolographicMemory.projection`), the projection epilogue
+    (SiLU on v, L2 normalisation, the gate) run inside the step's first kernel."""
+    assert y.is_cuda, "This kernel requires CUDA tensors"
+    assert y.dtype in _DTYPE, f"unsupported dtype {y.dtype}"
+    b, D = H_real.shape[0], H_real.shape[-1]
+    for H in (H_real, H_imag):
+        assert H.dtype == torch.float32 and H.is_contiguous() and tuple(H.shape) == (b, D, D), \
+            "H_real / H_imag must be contiguous fp32 [b, D, D] tensors (updated in place)"
+    assert pending.dtype == torch.uint8 and pending.numel() >= lib().verace_decode_pending_bytes(b, D, P), \
+        "pending storage too small for (b, D, P)"
+    y2 = y.reshape(b, y.shape[-1])
+    assert y2.stride(-1) == 1, "projection rows must be contiguous"
+    out = torch.empty(b, D, device=y.device, dtype=y.dtype)
+    if workspace is None:
+        workspace = _lazy_workspace(b, D, y.device)
+    with torch.cuda.device(y.device):
+        rc = lib().verace_decode_cham_lazy_projected(y2.data_ptr(), y2.stride(0), H_real.data_ptr(),
+                                                     H_imag.data_ptr(), pending.data_ptr(), P, out.data_ptr(), b, D,
+                                                     _DTYPE[y.dtype], workspace.data_ptr(), workspace.numel(),
+                                                     torch.cuda.current_stream(y.device).cuda_stream)
+    check(rc, "verace_decode_cham_lazy_projected")
+    return out
+
+
 def flush_pending(H_real: torch.Tensor, H_imag: torch.Tensor, pending: torch.Tensor, P: int) -> None:
     """Fold the pending factors into the stored planes and empty the list."""
     b, D = H_real.shape[0], H_real.shape[-1]
@@ -247,6 +275,17 @@ class DecodeState:
         self.flush(layer)
         return launch_decode_step(None, (q, k, v, gamma, self.H_real[layer], self.H_imag[layer]),
                                   mode=mode, workspace=self.workspace)[1]
+
+    def step_cham_projected(self, layer: int, y: torch.Tensor, active_mask=None) -> torch.Tensor:
+        """CHAM half from the layer's raw projection rows (unitary readout): with deferred
+        updates the projection epilogue runs inside the step
+        (:func:`launch_decode_cham_lazy_projected`); otherwise through the mixer prologue."""
+        if self.P > 0 and active_mask is None:
+            return launch_decode_cham_lazy_projected(y, self.H_real[layer], self.H_imag[layer],
+                                                     self.pending[layer], self.P, workspace=self.lazy_workspace)
+        from .kernels import mixer_prologue
+        q, k, v, g = mixer_prologue(y.reshape(self.batch, -1), 1, self.D, 1, True, active_mask)
+        return self.step_cham(layer, q, k, v, g, mode="unitary")
 
     def flush(self, layer: Optional[int] = None) -> None:
         """Fold the pending hologram factors of one layer (or all) into H_real / H_imag."""
