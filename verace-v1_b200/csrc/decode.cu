@@ -264,7 +264,9 @@ __global__ void __launch_bounds__(DT, 4) sssd_decode128_kernel(DecodeArgs A) {
   for (int m = 0; m < SD_NREG; ++m) ps[m] = __ldcs(reinterpret_cast<const float4*>(P + (size_t)(w + 8 * m) * HD) + lane);
   // The state depends on no earlier kernel of this step and is requested above; launched as
   // a programmatic dependent of the projection epilogue, the kernel waits here for k, v, q
-  // and the gate.
+  // and the gate.  The kernel after it (the per-head norm of the readout, a programmatic
+  // dependent) may launch now; it waits for this grid's completion before reading.
+  asm volatile("griddepcontrol.launch_dependents;");
   asm volatile("griddepcontrol.wait;" ::: "memory");
   float dots[4] = {0.f, 0.f, 0.f, 0.f};
   bool fin = true;

@@ -146,6 +146,9 @@ rmsnorm_kernel(const T* __restrict__ x, const T* __restrict__ w, T* __restrict__
   const T* xr = x + (act ? row : 0) * cols;
   Raw8<T> wr[V];
   load_w<T, L, V>(w, sl, nc, wr);
+  // launched as a programmatic dependent of the kernel before it (the SSSD decode step ahead
+  // of its per-head norm triggers early): the weights above need nothing from it, x does
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   float v[V][8];
 #pragma unroll
   for (int i = 0; i < V; ++i) {
@@ -318,10 +321,19 @@ int launch_rmsnorm(const void* x, const void* w, void* y, long long rows, int co
   const T* xx = (const T*)x;
   const T* ww = (const T*)w;
   T* yy = (T*)y;
-  if (sh.L == 16) rmsnorm_kernel<T, 16, 1><<<(unsigned)grid, NT, 0, st>>>(xx, ww, yy, rows, cols, eps);
-  else if (sh.V == 1) rmsnorm_kernel<T, 32, 1><<<(unsigned)grid, NT, 0, st>>>(xx, ww, yy, rows, cols, eps);
-  else if (sh.V == 4) rmsnorm_kernel<T, 32, 4><<<(unsigned)grid, NT, 0, st>>>(xx, ww, yy, rows, cols, eps);
-  else rmsnorm_kernel<T, 32, MAXV><<<(unsigned)grid, NT, 0, st>>>(xx, ww, yy, rows, cols, eps);
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)grid);
+  cfg.blockDim = dim3(NT);
+  cfg.stream = st;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (sh.L == 16) VERACE_CUDA(cudaLaunchKernelEx(&cfg, rmsnorm_kernel<T, 16, 1>, xx, ww, yy, rows, cols, eps));
+  else if (sh.V == 1) VERACE_CUDA(cudaLaunchKernelEx(&cfg, rmsnorm_kernel<T, 32, 1>, xx, ww, yy, rows, cols, eps));
+  else if (sh.V == 4) VERACE_CUDA(cudaLaunchKernelEx(&cfg, rmsnorm_kernel<T, 32, 4>, xx, ww, yy, rows, cols, eps));
+  else VERACE_CUDA(cudaLaunchKernelEx(&cfg, rmsnorm_kernel<T, 32, MAXV>, xx, ww, yy, rows, cols, eps));
   return check_launch("rmsnorm_kernel");
 }
 
