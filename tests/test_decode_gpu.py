@@ -250,13 +250,13 @@ def test_unsupported_shapes_are_refused():
         V.launch_decode_step((sq[:, 0], sk[:, 0], sv[:, 0], dl[:, 0], psi), None, mode="exact")
 
 
-@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16, torch.float16])
 @pytest.mark.parametrize("b,D,P", [(3, 256, 4), (2, 1024, 8), (1, 128, 1), (1, 256, 16)])
 def test_lazy_cham_decode_matches_eager_unitary_steps(dtype, b, D, P):
     """21 steps from a unitary hologram (folds every P steps; one non-finite token):
     the deferred-update step's outputs and, after a flush, its planes equal the eager
     unitary step's to fp32 rounding order.  P <= 8 folds with double-buffered factor
-    rows, P = 16 with one buffer."""
+    rows, P = 16 with one buffer; bf16 with P <= 8 folds on the tensor cores."""
     n = 21
     q, k, v, g = random_cham_inputs(b, n, D, seed=790 + D + P, dtype=dtype)
     k[0, 5, 3] = float("nan")
@@ -327,3 +327,26 @@ def test_projected_lazy_step_matches_prologue_then_lazy_step(dtype, b, D, P):
     V.flush_pending(rr, ri, pr, P)
     tol_h = 1e-6 if dtype == torch.float32 else 1e-3
     assert rel_fro(to_np(fr) + 1j * to_np(fi), to_np(rr) + 1j * to_np(ri)) <= tol_h
+
+
+@pytest.mark.parametrize("P", [3, 5])   # folds at steps P, 2P, ...: the odd ones are bf16 steps
+def test_lazy_tensor_core_fold_of_fp32_factors(P):
+    """Alternating fp32 and bf16 deferred steps on one pending list: the bf16 steps' kernel
+    folds on the tensor cores factors whose k, v came from fp32 steps (not exact in bf16;
+    they enter as hi + mid + lo pieces).  Outputs and, after a flush, the planes against
+    eager unitary steps of the same dtypes."""
+    b, D, n = 2, 256, 17
+    q, k, v, g = random_cham_inputs(b, n, D, seed=840 + P)
+    hr0, hi0 = _holo(_unitary(b, D, 841))
+    er, ei = hr0.clone(), hi0.clone()
+    lr, li = hr0.clone(), hi0.clone()
+    pend = V.pending_storage(b, D, P)
+    for t in range(n):
+        dt = torch.float32 if t % 2 == 0 else torch.bfloat16
+        args = (q[:, t].to(dt), k[:, t].to(dt), v[:, t].to(dt), g[:, t])
+        _, ye = V.launch_decode_step(None, args + (er, ei), mode="unitary")
+        yl = V.launch_decode_cham_lazy(*args, lr, li, pend, P)
+        assert rel_fro(to_np(yl), to_np(ye)) <= (2e-6 if dt == torch.float32 else 1e-2), t
+    assert V.device_status() == 0
+    V.flush_pending(lr, li, pend, P)
+    assert rel_fro(to_np(lr) + 1j * to_np(li), to_np(er) + 1j * to_np(ei)) <= 2e-6
