@@ -138,6 +138,26 @@ __device__ __forceinline__ void sssd_factor(float kk, float vv, float kv, float 
   m10 = f * fmaf(-a, kv, -1.f); m11 = f * (a * kk);
 }
 
+// The warp's sums over its 32 lanes of 16 per-lane values (the readout partials of the
+// warp's 16 state rows), as a reduce-scatter: 16 shuffles instead of 5 per value.  Lane l
+// (and l ^ 1) ends with the total of value 8 b4 + 4 b3 + 2 b2 + b1, b_i = bit i of l.
+__device__ __forceinline__ float warp_sum16_scatter(const float (&o)[16]) {
+  const int lane = threadIdx.x & 31;
+  float a[8], c[4], e[2];
+  const bool h4 = (lane & 16) != 0, h3 = (lane & 8) != 0, h2 = (lane & 4) != 0, h1 = (lane & 2) != 0;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) a[i] = (h4 ? o[i + 8] : o[i]) + __shfl_xor_sync(0xffffffffu, h4 ? o[i] : o[i + 8], 16);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) c[i] = (h3 ? a[i + 4] : a[i]) + __shfl_xor_sync(0xffffffffu, h3 ? a[i] : a[i + 4], 8);
+#pragma unroll
+  for (int i = 0; i < 2; ++i) e[i] = (h2 ? c[i + 2] : c[i]) + __shfl_xor_sync(0xffffffffu, h2 ? c[i] : c[i + 2], 4);
+  const float f = (h1 ? e[1] : e[0]) + __shfl_xor_sync(0xffffffffu, h1 ? e[0] : e[1], 2);
+  return f + __shfl_xor_sync(0xffffffffu, f, 1);
+}
+__device__ __forceinline__ int warp_sum16_slot(int lane) {
+  return 8 * ((lane >> 4) & 1) + 4 * ((lane >> 3) & 1) + 2 * ((lane >> 2) & 1) + ((lane >> 1) & 1);
+}
+
 template <typename T>
 __device__ void sssd_part(const DecodeArgs& A, int chain) {
   __shared__ float ks[MAXHD], vs[MAXHD], qs[MAXHD];
@@ -213,11 +233,15 @@ __device__ void sssd_part(const DecodeArgs& A, int chain) {
   const float4 q4 = colok ? make_float4(qs[4 * lane], qs[4 * lane + 1], qs[4 * lane + 2], qs[4 * lane + 3])
                           : make_float4(0.f, 0.f, 0.f, 0.f);
   T* out = static_cast<T*>(A.sout) + vec;
-  // pass 2: update, readout, store (rows re-read from L2)
+  // pass 2: update, readout, store (rows re-read from L2); the readout partials of the
+  // warp's rows w + 8 m are summed over the lanes together afterwards
+  static_assert(MAXHD / 8 == 16, "16 rows per warp");
+  float ov[16];
 #pragma unroll 4
   for (int m = 0; m < MAXHD / 8; ++m) {
     const int r = w + 8 * m;
-    if (r >= d) break;               // warp-uniform
+    ov[m] = 0.f;
+    if (r >= d) continue;            // warp-uniform
     float4 x = colok ? *reinterpret_cast<const float4*>(P + (size_t)r * d + 4 * lane)
                      : make_float4(0.f, 0.f, 0.f, 0.f);
     if (ok) {
@@ -225,11 +249,12 @@ __device__ void sssd_part(const DecodeArgs& A, int chain) {
       x.x += fmaf(kr, al[0], vr * be[0]); x.y += fmaf(kr, al[1], vr * be[1]);
       x.z += fmaf(kr, al[2], vr * be[2]); x.w += fmaf(kr, al[3], vr * be[3]);
     }
-    float o = fmaf(x.w, q4.w, fmaf(x.z, q4.z, fmaf(x.y, q4.y, x.x * q4.x)));
-    o = warp_sum(o);
-    if (lane == 0) out[r] = from_f32<T>(o);
+    ov[m] = fmaf(x.w, q4.w, fmaf(x.z, q4.z, fmaf(x.y, q4.y, x.x * q4.x)));
     if (colok) __stcs(reinterpret_cast<float4*>(P + (size_t)r * d + 4 * lane), x);
   }
+  const float o = warp_sum16_scatter(ov);
+  const int r = w + 8 * warp_sum16_slot(lane);
+  if ((lane & 1) == 0 && r < d) out[r] = from_f32<T>(o);
 }
 
 // SSSD-only step for head_dim 128 (the step's SSSD half when the CHAM half runs deferred):
@@ -322,6 +347,8 @@ __global__ void __launch_bounds__(DT, 4) sssd_decode128_kernel(DecodeArgs A) {
                                 fmaf(m10, sa.z, m11 * sb.z), fmaf(m10, sa.w, m11 * sb.w));
   const float4 q4 = make_float4(qs[4 * lane], qs[4 * lane + 1], qs[4 * lane + 2], qs[4 * lane + 3]);
   T* out = static_cast<T*>(A.sout) + vec;
+  static_assert(NR == 16, "16 rows per warp");
+  float ov[NR];
 #pragma unroll
   for (int m = 0; m < NR; ++m) {
     const int r = w + 8 * m;
@@ -332,10 +359,10 @@ __global__ void __launch_bounds__(DT, 4) sssd_decode128_kernel(DecodeArgs A) {
       x.z += fmaf(kr, al.z, vr * be.z); x.w += fmaf(kr, al.w, vr * be.w);
     }
     __stcs(reinterpret_cast<float4*>(P + (size_t)r * HD) + lane, x);
-    float o = fmaf(x.w, q4.w, fmaf(x.z, q4.z, fmaf(x.y, q4.y, x.x * q4.x)));
-    o = warp_sum(o);
-    if (lane == 0) out[r] = from_f32<T>(o);
+    ov[m] = fmaf(x.w, q4.w, fmaf(x.z, q4.z, fmaf(x.y, q4.y, x.x * q4.x)));
   }
+  const float o = warp_sum16_scatter(ov);   // (the readout sums as sssd_part forms them)
+  if ((lane & 1) == 0) out[w + 8 * warp_sum16_slot(lane)] = from_f32<T>(o);
 }
 
 // ------------------------------------------------------------------------- CHAM
