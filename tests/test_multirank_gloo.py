@@ -1,4 +1,4 @@
-"""The multi-GPU host logic of bench.py, on CPU: two gloo ranks (world_size 2) run the
+"""The multi-GPU host logic of bench.py, on CPU: two and four gloo ranks run the
 helpers the NCCL ranks run on B200s.  Each rank takes its own shard of the batch (weak
 scaling: the same amount of work, different items); the only data-path collective is the
 all_gather of the ranks' outputs; the timed region is bracketed by the barrier and reduced
@@ -13,6 +13,7 @@ import os
 import socket
 import sys
 
+import pytest
 import torch
 import torch.distributed as dist
 import torch.multiprocessing as mp
@@ -43,7 +44,7 @@ def _rank_worker(rank, world, port):
         assert not torch.equal(shards[0], shards[1])                       # on items of its own
         assert torch.equal(ids, bench.rank_shard_ids(rank, batch, seq, vocab))   # a function of the rank
         barrier()
-        ms = 10.0 + 7.5 * rank                                             # rank 1 is the slow one
+        ms = 17.5 if rank == 1 else 10.0 + rank * 0.5                     # rank 1 is the slow one
         slowest = max_over_ranks(ms)
         assert slowest == 17.5
         rate = bench.whole_job_rate(world, batch * seq * layers, slowest)
@@ -57,7 +58,8 @@ def _rank_worker(rank, world, port):
         lo, hi = bench.strong_shard(rank, world, 256)
         ranges = [torch.tensor([lo, hi]) for _ in range(world)]
         dist.all_gather(ranges, torch.tensor([lo, hi]))
-        assert [tuple(r.tolist()) for r in ranges] == [(0, 128), (128, 256)]
+        assert [tuple(r.tolist()) for r in ranges] == [(i * 256 // world, (i + 1) * 256 // world)
+                                                       for i in range(world)]
         barrier()
     finally:
         dist.destroy_process_group()
@@ -91,12 +93,14 @@ def _segment_worker(rank, world, port):
         dist.destroy_process_group()
 
 
-def test_sequence_segments_carry_state_across_two_gloo_ranks():
-    mp.start_processes(_segment_worker, args=(2, _free_port()), nprocs=2, start_method="spawn", join=True)
+@pytest.mark.parametrize("world", [2, 4])
+def test_sequence_segments_carry_state_across_gloo_ranks(world):
+    mp.start_processes(_segment_worker, args=(world, _free_port()), nprocs=world, start_method="spawn", join=True)
 
 
-def test_two_gloo_ranks_shard_and_time_like_the_nccl_ranks():
-    mp.start_processes(_rank_worker, args=(2, _free_port()), nprocs=2, start_method="spawn", join=True)
+@pytest.mark.parametrize("world", [2, 4])
+def test_gloo_ranks_shard_and_time_like_the_nccl_ranks(world):
+    mp.start_processes(_rank_worker, args=(world, _free_port()), nprocs=world, start_method="spawn", join=True)
 
 
 def test_single_rank_needs_no_process_group():
