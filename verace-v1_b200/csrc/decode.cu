@@ -271,7 +271,10 @@ __global__ void __launch_bounds__(DT, 4) sssd_decode128_kernel(DecodeArgs A) {
   constexpr int HD = 128, NR = HD / 8;
   extern __shared__ __align__(128) float4 srow[];           // [SD_SROWS][HD / 4]
   __shared__ float ks[HD], vs[HD], qs[HD];
-  __shared__ float4 red[8][HD / 4][2];
+  // column partials of the warps, [warp][kᵀΨ x y z w, vᵀΨ x y z w][lane], and their sums
+  // over the warps (warp c forms sum c, adding the warps in order as sssd_part does)
+  __shared__ float red[8][8][HD / 4];
+  __shared__ float rsum[8][HD / 4];
   __shared__ float dsc[8][4];
   __shared__ __align__(8) uint64_t sbar;
   const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
@@ -324,8 +327,15 @@ __global__ void __launch_bounds__(DT, 4) sssd_decode128_kernel(DecodeArgs A) {
     av.x = fmaf(vr, x.x, av.x); av.y = fmaf(vr, x.y, av.y);
     av.z = fmaf(vr, x.z, av.z); av.w = fmaf(vr, x.w, av.w);
   }
-  red[w][lane][0] = ak;
-  red[w][lane][1] = av;
+  red[w][0][lane] = ak.x; red[w][1][lane] = ak.y; red[w][2][lane] = ak.z; red[w][3][lane] = ak.w;
+  red[w][4][lane] = av.x; red[w][5][lane] = av.y; red[w][6][lane] = av.z; red[w][7][lane] = av.w;
+  __syncthreads();
+  {
+    float t = 0.f;
+#pragma unroll
+    for (int ww = 0; ww < 8; ++ww) t += red[ww][w][lane];
+    rsum[w][lane] = t;
+  }
   __syncthreads();
   const float dl = A.delta[chain];
   float m00, m01, m10, m11;
@@ -333,13 +343,8 @@ __global__ void __launch_bounds__(DT, 4) sssd_decode128_kernel(DecodeArgs A) {
   // Non-finite k, v, gate or factor: identity, as the reference's _solve_cayley
   // substitution does (sssd_attention.py:52-71).
   const bool ok = fin && isfinite(dl) && isfinite(m00) && isfinite(m01) && isfinite(m10) && isfinite(m11);
-  float4 sa = make_float4(0.f, 0.f, 0.f, 0.f), sb = sa;
-#pragma unroll
-  for (int ww = 0; ww < 8; ++ww) {
-    const float4 x = red[ww][lane][0], y = red[ww][lane][1];
-    sa.x += x.x; sa.y += x.y; sa.z += x.z; sa.w += x.w;
-    sb.x += y.x; sb.y += y.y; sb.z += y.z; sb.w += y.w;
-  }
+  const float4 sa = make_float4(rsum[0][lane], rsum[1][lane], rsum[2][lane], rsum[3][lane]);
+  const float4 sb = make_float4(rsum[4][lane], rsum[5][lane], rsum[6][lane], rsum[7][lane]);
   // coefficients of k_r (al) and v_r (be) in each of the thread's columns
   const float4 al = make_float4(fmaf(m00, sa.x, m01 * sb.x), fmaf(m00, sa.y, m01 * sb.y),
                                 fmaf(m00, sa.z, m01 * sb.z), fmaf(m00, sa.w, m01 * sb.w));
